@@ -1,0 +1,458 @@
+#!/usr/bin/env python
+"""Benchmark: forward edges/s of WignerDBasis + EquivariantEdgewiseLinear
+on B200, with roofline, clocks, end-to-end and CPU baseline.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload: in/out Repr(lvals=[0..4], mult=64), N = 20000
+nodes uniform in a 60 A cube, 32-nearest-neighbour graph (src over the neighbours
+of dst), E = 640000, node features (N, 64, 25) ~ N(0, 1) gathered to edges by
+src, directions = dst - src, num_bins = 100 over [0, 10], float32, seed 1.
+Synthetic data (the reference benchmarks on random graphs too); module weights
+random-init with torch.manual_seed(1).
+
+One step = P, Q = WignerDBasis(directions); out = layer(P, Q, x[src], distances),
+inputs resident in HBM (4.1 GB of edge features per step >> 126 MB L2, so no
+flush is needed).  Under torchrun (N > 1) every rank runs its own independent
+graph (seed 1 + rank): data-parallel, no collective on the data path, weak scaling.
+
+--impl reference times the reference algorithm on the host cores: the CPU
+restatement in oracle/ (batched matrix_exp basis, bmm, block-diagonal mix, bmm;
+the reference has no CPU kernel of its own), on a bounded sample of the same
+workload per step.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "flash-eq_b200"))
+
+import torch  # noqa: E402
+
+LVALS = [0, 1, 2, 3, 4]
+MULT = 64
+N_NODES = 20000
+K_NN = 32
+BOX = 60.0
+NUM_BINS = 100
+MAX_DIST = 10.0
+SEED = 1
+
+
+# ---------------------------------------------------------------------------
+# Workload
+# ---------------------------------------------------------------------------
+def knn_graph(coords: torch.Tensor, k: int, chunk: int = 4096):
+    """src -> dst: src ranges over the k nearest neighbours (no self) of each dst."""
+    n = coords.shape[0]
+    nbrs = []
+    for s in range(0, n, chunk):
+        d = torch.cdist(coords[s:s + chunk], coords)
+        idx = torch.arange(s, min(n, s + chunk), device=coords.device)
+        d[torch.arange(len(idx), device=coords.device), idx] = float("inf")
+        nbrs.append(d.topk(k, dim=1, largest=False).indices)
+    nbr = torch.cat(nbrs)
+    dst = torch.arange(n, device=coords.device).repeat_interleave(k)
+    return nbr.reshape(-1), dst
+
+
+def make_workload(seed: int, device):
+    g = torch.Generator().manual_seed(seed)
+    coords = torch.rand(N_NODES, 3, generator=g) * BOX
+    x = torch.randn(N_NODES, MULT, sum(2 * l + 1 for l in LVALS), generator=g)
+    coords_d = coords.to(device)
+    src, dst = knn_graph(coords_d, K_NN)
+    return {"coords": coords, "x": x, "coords_d": coords_d, "x_d": x.to(device), "src": src, "dst": dst}
+
+
+def build_modules(device):
+    import flash_eq as fe
+
+    torch.manual_seed(SEED)
+    r = fe.Repr(LVALS, mult=MULT)
+    layer = fe.EquivariantEdgewiseLinear(r, r, num_bins=NUM_BINS, min_dist=0.0, max_dist=MAX_DIST).to(device)
+    layer.eval()
+    basis = fe.WignerDBasis([r, r]).to(device)
+    return layer, basis
+
+
+def per_edge_work():
+    """Algorithmic bytes and flops per edge (fp32 I/O) of the edgewise linear."""
+    d = sum(2 * l + 1 for l in LVALS)
+    byts = MULT * d * 4 * 2 + 16
+    mix = 0
+    for m in range(max(LVALS) + 1):
+        n = sum(1 for l in LVALS if l >= m)
+        mix += 2 * MULT * MULT * n * n * (1 if m == 0 else 4)
+    rot = 2 * 2 * MULT * sum((2 * l + 1) ** 2 for l in LVALS)
+    table_bytes = (NUM_BINS + 1) * MULT * MULT * sum(2 * min(a, b) + 1 for a in LVALS for b in LVALS) * 4
+    return byts, mix, rot, table_bytes
+
+
+# ---------------------------------------------------------------------------
+# Clocks sampler (nvidia-smi during the timed region)
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu_index = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", str(self.gpu_index)],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+        except (OSError, ValueError):
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        mhz, mx, reasons, power = [], None, set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                mhz.append(float(parts[1]))
+                mx = float(parts[2])
+                power.append(float(parts[3]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        mhz.sort()
+        return {"sm_mhz": mhz[len(mhz) // 2] if mhz else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(mhz), "power_w_max": max(power) if power else None}
+
+
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as fh:
+            pk = json.load(fh)
+        return float(pk["hbm_gbs"]), float(pk["bf16_tflops"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, 1590.0, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the reference algorithm on the host cores (oracle port)
+# ---------------------------------------------------------------------------
+def cpu_reference_setup(sample_edges: int):
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import feq_oracle as orc
+
+    wl = _cpu_workload()
+    layer, _ = build_modules("cpu")
+    with torch.no_grad():
+        table = layer.radial_weights()
+    p1, p2 = layer.radial_weights.binning_params()
+    src, dst = wl["src"], wl["dst"]
+    sel = torch.arange(min(sample_edges, src.numel()))
+    vec = wl["coords"][dst[sel]] - wl["coords"][src[sel]]
+    ef = wl["x"][src[sel]]
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+
+    def step():
+        dist = vec.norm(dim=-1)
+        P = orc.wigner_basis(vec, LVALS)
+        return orc.edgewise_fwd(P, P, ef, dist, table, LVALS, LVALS, layer.solid_harmonic_scale, p1, p2,
+                                NUM_BINS, False, nthreads=threads)
+
+    return step, int(sel.numel()), threads
+
+
+_CPU_WL = {}
+
+
+def _cpu_workload():
+    if "wl" not in _CPU_WL:
+        _CPU_WL["wl"] = make_workload(SEED, "cpu")
+    return _CPU_WL["wl"]
+
+
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as fh:
+            for ln in fh:
+                if ln.startswith("model name"):
+                    return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def time_cpu(step, n, reps):
+    step()
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        step()
+    return (time.perf_counter() - t0) / reps
+
+
+def pick_cpu_sample(target_s: float = 2.0):
+    """Size the per-step sample so one step takes about target_s seconds."""
+    step, n, threads = cpu_reference_setup(256)
+    t = time_cpu(step, n, 1)
+    per_edge = t / n
+    return max(256, min(640000, int(target_s / max(per_edge, 1e-9)))), threads
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    sample, threads = pick_cpu_sample(2.0)
+    step, n, threads = cpu_reference_setup(sample)
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = (time.perf_counter() - t0) / args.steps
+    value = n / dt
+    line = {
+        "metric": "edges/sec (fwd)", "impl": "reference", "value": value, "unit": "edges/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": config_block(args.gpus),
+        "cpu_baseline": {"value": value, "unit": "edges/s", "cores": threads, "kind": "port",
+                         "sample": f"{n} edges of the config-2 workload per step (CPU: {cpu_model()})"},
+        "e2e": {"value": value, "unit": "edges/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def config_block(n_gpus):
+    return {"workload": "config2: WignerDBasis + EquivariantEdgewiseLinear forward, Repr([0,1,2,3,4],64) -> same, "
+                        "N=20000 uniform 60A cube, 32-NN, E=640000 per GPU, 100 bins over [0,10]",
+            "edges_per_gpu": N_NODES * K_NN, "global_edges": N_NODES * K_NN * n_gpus,
+            "parallelism": f"dp{n_gpus} (independent graph per GPU)",
+            "l2": "no flush: 4.1 GB of edge features read per step >> 126 MB L2"}
+
+
+# ---------------------------------------------------------------------------
+# Our arm
+# ---------------------------------------------------------------------------
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    pg = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+        pg = dist
+    return world, rank, local, pg
+
+
+def barrier(pg):
+    if pg is not None:
+        pg.barrier()
+    torch.cuda.synchronize()
+
+
+def max_over_ranks(pg, v: float) -> float:
+    if pg is None:
+        return v
+    t = torch.tensor([v], device="cuda", dtype=torch.float64)
+    pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    return float(t.item())
+
+
+def gpu_index_for(local: int) -> int:
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        ids = [v.strip() for v in vis.split(",") if v.strip()]
+        if local < len(ids) and ids[local].isdigit():
+            return int(ids[local])
+    return local
+
+
+def run_ours(args):
+    world, rank, local, pg = dist_setup(args)
+    dev = torch.device("cuda", local)
+    from flash_eq.cuda import _lib, block_diagonal_cuda
+
+    lib = _lib.load()
+    wl = make_workload(SEED + rank, dev)
+    layer, basis = build_modules(dev)
+    src, dst, x, coords = wl["src"], wl["dst"], wl["x_d"], wl["coords_d"]
+    E = src.numel()
+    vec = coords[dst] - coords[src]
+    dist_e = vec.norm(dim=-1)
+
+    def step():
+        with torch.no_grad():
+            P, Q = basis(vec)
+            return layer(P, Q, x[src], dist_e)
+
+    for _ in range(args.warmup):
+        step()
+    barrier(pg)
+    clk = ClockSampler(gpu_index_for(local))
+    clk.start()
+    n0 = lib.feq_launch_count()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(pg)
+    t0.record()
+    for _ in range(args.steps):
+        step()
+    t1.record()
+    barrier(pg)
+    launches = lib.feq_launch_count() - n0
+    clocks = clk.stop()
+    ms = max_over_ranks(pg, t0.elapsed_time(t1) / args.steps)
+    value = E * world / (ms / 1e3)
+
+    # --- dominant stage: the block-diagonal radial mix, timed alone on the same shapes
+    byts, mix_flops, rot_flops, table_bytes = per_edge_work()
+    with torch.no_grad():
+        table = layer.radial_weights()
+        P, _ = basis(vec)
+        g_in = torch.bmm(x[src], P)                       # m-first input of the mix
+    p1, p2 = layer.radial_weights.binning_params()
+    pr = layer.product_repr
+    for _ in range(2):
+        block_diagonal_cuda(g_in, table, dist_e, pr, p1, p2, NUM_BINS, False, 0.1)
+    reps = 3
+    m0, m1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    m0.record()
+    for _ in range(reps):
+        block_diagonal_cuda(g_in, table, dist_e, pr, p1, p2, NUM_BINS, False, 0.1)
+    m1.record()
+    torch.cuda.synchronize()
+    mix_ms = m0.elapsed_time(m1) / reps
+    del g_in, P
+    hbm_peak, tc_peak, peak_kind = measured_peaks()
+    mix_bytes = E * (byts - 16 + 4) + table_bytes          # g in, h out, distance, table
+    achieved_gbs = mix_bytes / (mix_ms / 1e3) / 1e9
+    mix_tflops = E * mix_flops / (mix_ms / 1e3) / 1e12
+    sm_mhz = clocks.get("sm_max_mhz") or 1965.0
+    fp32_peak = 148 * 128 * 2 * sm_mhz * 1e6 / 1e12       # FMA lanes x 2 flop x clock (nominal)
+
+    # --- end to end through the public API from pinned host buffers
+    e2e = run_e2e(args, wl, layer, basis, dev, pg, world)
+
+    result = None
+    if rank == 0:
+        result = {
+            "metric": "edges/sec (fwd, device-timed)", "value": value, "unit": "edges/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": config_block(world),
+            "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": hbm_peak, "unit": "GB/s",
+                         "frac": achieved_gbs / hbm_peak, "traffic": None,
+                         "kernel": "block-diagonal radial mix (binning+sort+relayout+mix), timed alone",
+                         "peak_kind": peak_kind,
+                         "note": "fp32 mix on CUDA cores is FLOP-bound, see compute"},
+            "compute": {"achieved": mix_tflops, "unit": "TFLOP/s", "peak": fp32_peak,
+                        "peak_kind": "nominal fp32 FMA (148 SM x 128 lanes x 2 x max clock)",
+                        "frac": mix_tflops / fp32_peak, "mix_ms": mix_ms,
+                        "flop_per_edge": mix_flops, "bytes_per_edge": byts},
+            "clocks": clocks,
+            "e2e": e2e,
+            "gpu_launches": int(launches),
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            try:
+                sample, threads = pick_cpu_sample(3.0)
+                cstep, n, threads = cpu_reference_setup(sample)
+                dt = time_cpu(cstep, n, 3)
+                result["cpu_baseline"] = {"value": n / dt, "unit": "edges/s", "cores": threads, "kind": "port",
+                                          "sample": f"{n} edges of the same workload, 3 reps "
+                                                    f"(CPU: {cpu_model()})"}
+            except Exception as exc:  # the baseline must not hide the GPU number
+                result["cpu_baseline"] = {"value": None, "error": repr(exc)}
+        print(json.dumps(result), flush=True)
+    if pg is not None:
+        pg.barrier()
+        pg.destroy_process_group()
+    return 0
+
+
+def run_e2e(args, wl, layer, basis, dev, pg, world):
+    """Same step through the public API with host buffers: H2D of the step's
+    inputs from pinned memory and D2H of the full output, inside the timed region."""
+    x_h = wl["x"].pin_memory()
+    c_h = wl["coords"].pin_memory()
+    s_h, d_h = wl["src"].cpu().pin_memory(), wl["dst"].cpu().pin_memory()
+    E = s_h.numel()
+    d_out = sum(2 * l + 1 for l in LVALS)
+    out_h = torch.empty(E, MULT, d_out, pin_memory=True)
+
+    def step():
+        x = x_h.to(dev, non_blocking=True)
+        c = c_h.to(dev, non_blocking=True)
+        s, d = s_h.to(dev, non_blocking=True), d_h.to(dev, non_blocking=True)
+        with torch.no_grad():
+            v = c[d] - c[s]
+            P, Q = basis(v)
+            y = layer(P, Q, x[s], v.norm(dim=-1))
+        out_h.copy_(y, non_blocking=True)
+
+    steps = max(1, min(args.steps, 5))
+    step()
+    barrier(pg)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(steps):
+        step()
+    t1.record()
+    barrier(pg)
+    ms = max_over_ranks(pg, t0.elapsed_time(t1) / steps)
+    h2d = x_h.numel() * 4 + c_h.numel() * 4 + s_h.numel() * 8 + d_h.numel() * 8
+    return {"value": E * world / (ms / 1e3), "unit": "edges/s", "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": out_h.numel() * 4, "ms_per_step": ms, "steps": steps}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,399 @@
+// feq_abi.cu -- the extern "C" entry points of libflasheq_b200.so: argument
+// validation, host-side layout tables, workspace planning and kernel sequencing.
+// Declarations and the reference interface each one replaces: include/flasheq_b200.h.
+#include <cuda_runtime.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <algorithm>
+#include <atomic>
+#include <string>
+
+#include "feq_internal.cuh"
+
+namespace feq {
+
+// kernels (feq_rotate.cu, feq_mix.cu, feq_graph.cu)
+int launch_basis(const float *dirs, int64_t E, const ReprLayout &L, int layout, float *out, cudaStream_t s);
+int launch_rotate_in(const float *x, const int64_t *src, int64_t nsrc, const float *edge_add,
+                     const float *dirs, const float *P, int64_t E, int C, const ReprLayout &L,
+                     float *g, int32_t *status, cudaStream_t s);
+int launch_rotate_out(const float *h, const float *dirs, const float *Q, int64_t E, int C,
+                      const ReprLayout &L, float *out, cudaStream_t s);
+int64_t mix_max_tiles(int64_t E, int nb);
+int launch_relayout(const float *T, float *Wt, int nb1, int Cin, int Cout, const MixLayout &M, cudaStream_t s);
+int launch_build_tiles(const int64_t *offsets, int nb, int4 *tiles, int *num_tiles, cudaStream_t s);
+int launch_mix(const float *g, const float *Wt, const float *dist, const int64_t *perm, const int4 *tiles,
+               const int *num_tiles, int64_t max_tiles, int64_t E, int Cin, int Cout, int din, int dout,
+               const MixLayout &M, Binning bins, float sh_scale, float *h, cudaStream_t s);
+int launch_binning(const float *dist, int64_t E, Binning b, int32_t *lo, float *t, cudaStream_t s);
+size_t edge_sort_workspace(int64_t E, int32_t nk);
+template <typename K>
+int launch_edge_sort(const K *keys, int64_t E, int32_t nk, int64_t *perm, int64_t *offsets,
+                     int32_t *status, void *ws, size_t ws_bytes, cudaStream_t s);
+int launch_edge_logits(const float *Q, const float *K, int64_t E, int H, int D, float scale,
+                       const float *dist, float decay, float *logits, cudaStream_t s);
+int launch_segment_softmax(const float *logits, int64_t N, int H, const int64_t *perm,
+                           const int64_t *offsets, float *weights, cudaStream_t s);
+int launch_segment_pool(const float *rows, int64_t L, const float *w, int H, const int64_t *perm,
+                        const int64_t *offsets, int64_t N, int reduce, float *out, cudaStream_t s);
+int launch_attn_pool(const FeqAttnArgs &a, cudaStream_t s);
+
+static thread_local std::string g_last_error;
+static std::atomic<long long> g_launches{0};
+
+void count_launches(int n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+void record_cuda_error(cudaError_t err) {
+    g_last_error = std::string(cudaGetErrorName(err)) + ": " + cudaGetErrorString(err);
+}
+
+int build_repr_layout(const int32_t *lv, int32_t n, ReprLayout *L) {
+    if (!lv || n < 1) return FEQ_ERR_INVALID_ARGUMENT;
+    if (n > kMaxIrreps) return FEQ_ERR_UNSUPPORTED;
+    memset(L, 0, sizeof(*L));
+    int off = 0, lmax = 0;
+    bool present[kMaxL + 1] = {false};
+    for (int r = 0; r < n; r++) {
+        const int l = lv[r];
+        if (l < 0) return FEQ_ERR_INVALID_ARGUMENT;
+        if (l > kMaxL) return FEQ_ERR_UNSUPPORTED;
+        L->irrep_l[r] = (int8_t)l;
+        L->irrep_off[r] = (int16_t)off;
+        off += 2 * l + 1;
+        if (off > kMaxDim) return FEQ_ERR_UNSUPPORTED;
+        lmax = std::max(lmax, l);
+        present[l] = true;
+    }
+    L->n_irreps = n;
+    L->dim = off;
+    L->lmax = lmax;
+    int u = 0, doff = 0;
+    int slot_of[kMaxL + 1];
+    for (int l = 0; l <= kMaxL; l++) {
+        slot_of[l] = -1;
+        if (!present[l]) continue;
+        L->unique_l[u] = (int8_t)l;
+        L->unique_doff[u] = (int16_t)doff;
+        slot_of[l] = u;
+        doff += (2 * l + 1) * (2 * l + 1);
+        u++;
+    }
+    L->n_unique = u;
+    L->dblock_floats = doff;
+    for (int r = 0; r < n; r++) {
+        L->irrep_slot[r] = (int8_t)slot_of[L->irrep_l[r]];
+        for (int k = 0; k < 2 * L->irrep_l[r] + 1; k++) L->std_irrep[L->irrep_off[r] + k] = (int8_t)r;
+    }
+    // m-first order (wigner.py:243-272): all m = 0, then per m the (+m, -m) pairs.
+    int j = 0;
+    for (int r = 0; r < n; r++) L->perm[j++] = (int16_t)(L->irrep_off[r] + L->irrep_l[r]);
+    for (int m = 1; m <= lmax; m++)
+        for (int r = 0; r < n; r++)
+            if (L->irrep_l[r] >= m) {
+                L->perm[j++] = (int16_t)(L->irrep_off[r] + L->irrep_l[r] + m);
+                L->perm[j++] = (int16_t)(L->irrep_off[r] + L->irrep_l[r] - m);
+            }
+    for (int q = 0; q < off; q++) L->inv_perm[L->perm[q]] = (int16_t)q;
+    return FEQ_OK;
+}
+
+// Restates precompute_block_info (block_diagonal.cu:1191-1266) plus the re-laid
+// table geometry used by the mix kernel.
+int build_mix_layout(const int32_t *lin, int32_t nin, const int32_t *lout, int32_t nout, int c_in,
+                     int c_out, MixLayout *M) {
+    if (!lin || !lout || nin < 1 || nout < 1) return FEQ_ERR_INVALID_ARGUMENT;
+    if (nin > kMaxIrreps || nout > kMaxIrreps) return FEQ_ERR_UNSUPPORTED;
+    memset(M, 0, sizeof(*M));
+    int lmi = 0, lmo = 0;
+    for (int i = 0; i < nin; i++) {
+        if (lin[i] < 0) return FEQ_ERR_INVALID_ARGUMENT;
+        lmi = std::max<int>(lmi, lin[i]);
+    }
+    for (int i = 0; i < nout; i++) {
+        if (lout[i] < 0) return FEQ_ERR_INVALID_ARGUMENT;
+        lmo = std::max<int>(lmo, lout[i]);
+    }
+    const int mmax = std::max(lmi, lmo);
+    if (mmax > kMaxL) return FEQ_ERR_UNSUPPORTED;   // reference: mmax < MAX_LVALS (:1298)
+    M->n_blocks = mmax + 1;
+    M->lmax_in = lmi;
+    M->lmax_out = lmo;
+    int in_off = 0, out_off = 0, w_off = 0;
+    int64_t roff = 0;
+    for (int m = 0; m <= mmax; m++) {
+        MixBlock &B = M->blk[m];
+        B.m = m;
+        int ni = 0, no = 0;
+        for (int i = 0; i < nin; i++)
+            if (lin[i] >= m) B.l_in[ni++] = (int8_t)lin[i];
+        for (int i = 0; i < nout; i++)
+            if (lout[i] >= m) B.l_out[no++] = (int8_t)lout[i];
+        B.n_in = ni;
+        B.n_out = no;
+        B.in_off = in_off;
+        B.out_off = out_off;
+        B.w_off = w_off;
+        const int mult = m == 0 ? 1 : 2;
+        if (ni > 0 && no > 0) {
+            B.relaid_stride = ((c_out * no * mult) + 1) & ~1;
+            roff = (roff + 3) & ~int64_t(3);
+            B.relaid_off = (int)roff;
+            roff += (int64_t)c_in * ni * B.relaid_stride;
+            in_off += mult * ni;
+            out_off += mult * no;
+            w_off += mult * no * ni;
+        }
+    }
+    M->wdim = w_off;
+    M->relaid_row = (roff + 3) & ~int64_t(3);
+    if (M->relaid_row > 0x7fffffffll) return FEQ_ERR_UNSUPPORTED;
+    return FEQ_OK;
+}
+
+static int dims_of(const int32_t *lv, int32_t n) {
+    int d = 0;
+    for (int i = 0; i < n; i++) d += 2 * lv[i] + 1;
+    return d;
+}
+
+// Radial-mix plan shared by block_diagonal_fwd and edgewise_fwd.
+struct MixPlan {
+    float *Wt;
+    int32_t *keys;
+    int64_t *perm, *offsets;
+    int4 *tiles;
+    int *num_tiles;
+    void *sort_ws;
+    size_t sort_ws_bytes;
+    int64_t max_tiles;
+};
+
+static void carve_mix(WsCarver &w, int64_t E, int nb, const MixLayout &M, MixPlan &p) {
+    const int64_t E1 = std::max<int64_t>(E, 1);
+    p.Wt = (float *)w.take(sizeof(float) * ((size_t)M.relaid_row * (nb + 1) + 16));
+    p.keys = (int32_t *)w.take(sizeof(int32_t) * E1);
+    p.perm = (int64_t *)w.take(sizeof(int64_t) * E1);
+    p.offsets = (int64_t *)w.take(sizeof(int64_t) * (nb + 1));
+    p.max_tiles = mix_max_tiles(E, nb);
+    p.tiles = (int4 *)w.take(sizeof(int4) * p.max_tiles);
+    p.num_tiles = (int *)w.take(sizeof(int) * 4);
+    p.sort_ws_bytes = edge_sort_workspace(E, nb);
+    p.sort_ws = w.take(p.sort_ws_bytes);
+}
+
+static int run_mix(const MixPlan &p, const float *g, const float *table, const float *dist, int64_t E,
+                   int Cin, int Cout, int din, int dout, const MixLayout &M, Binning bins, float sh_scale,
+                   float *h, cudaStream_t s) {
+    int rc;
+    if ((rc = launch_binning(dist, E, bins, p.keys, nullptr, s)) != FEQ_OK) return rc;
+    if ((rc = launch_edge_sort<int32_t>(p.keys, E, bins.num_bins, p.perm, p.offsets, nullptr, p.sort_ws,
+                                        p.sort_ws_bytes, s)) != FEQ_OK)
+        return rc;
+    if ((rc = launch_build_tiles(p.offsets, bins.num_bins, p.tiles, p.num_tiles, s)) != FEQ_OK) return rc;
+    if ((rc = launch_relayout(table, p.Wt, bins.num_bins + 1, Cin, Cout, M, s)) != FEQ_OK) return rc;
+    return launch_mix(g, p.Wt, dist, p.perm, p.tiles, p.num_tiles, p.max_tiles, E, Cin, Cout, din, dout, M,
+                      bins, sh_scale, h, s);
+}
+
+static bool mix_args_ok(int64_t E, int Cin, int Cout, int nb) {
+    return E >= 0 && E < 0x7fffffffll && Cin >= 1 && Cout >= 1 && nb >= 1 && nb < (1 << 24);
+}
+
+}  // namespace feq
+
+using namespace feq;
+
+extern "C" {
+
+const char *feq_status_string(int status) {
+    switch (status) {
+        case FEQ_OK: return "ok";
+        case FEQ_ERR_INVALID_ARGUMENT: return "invalid argument";
+        case FEQ_ERR_UNSUPPORTED: return "unsupported by this build (limits: l <= 16, <= 64 irreps, dim <= 512)";
+        case FEQ_ERR_WORKSPACE: return "workspace missing or too small";
+        case FEQ_ERR_CUDA: return "CUDA error";
+        case FEQ_ERR_NO_DEVICE: return "no usable CUDA device";
+        default: return "unknown status";
+    }
+}
+
+int feq_abi_version(void) { return 1; }
+
+const char *feq_last_error(void) { return g_last_error.c_str(); }
+
+int64_t feq_launch_count(void) { return (int64_t)g_launches.load(); }
+
+int feq_wigner_basis(const float *directions, int64_t num_edges, const int32_t *lvals, int32_t num_lvals,
+                     int32_t layout, float *out, feq_stream_t stream) {
+    if (num_edges < 0 || (layout != FEQ_BASIS_MFIRST && layout != FEQ_BASIS_ROT_TO_EZ))
+        return FEQ_ERR_INVALID_ARGUMENT;
+    ReprLayout L;
+    int rc = build_repr_layout(lvals, num_lvals, &L);
+    if (rc != FEQ_OK) return rc;
+    if (num_edges == 0) return FEQ_OK;
+    if (!directions || !out) return FEQ_ERR_INVALID_ARGUMENT;
+    if (num_edges > 0x7fffffffll * 8) return FEQ_ERR_UNSUPPORTED;
+    return launch_basis(directions, num_edges, L, layout, out, (cudaStream_t)stream);
+}
+
+int feq_edge_binning(const float *distances, int64_t num_edges, float bin_param1, float bin_param2,
+                     int32_t num_bins, int32_t log_bins, int32_t *bin_lo, float *t, feq_stream_t stream) {
+    if (num_edges < 0 || num_bins < 1) return FEQ_ERR_INVALID_ARGUMENT;
+    if (num_edges == 0) return FEQ_OK;
+    if (!distances || (!bin_lo && !t)) return FEQ_ERR_INVALID_ARGUMENT;
+    Binning b{bin_param1, bin_param2, num_bins, log_bins ? 1 : 0};
+    return launch_binning(distances, num_edges, b, bin_lo, t, (cudaStream_t)stream);
+}
+
+size_t feq_edge_sort_workspace_bytes(int64_t num_edges, int32_t num_keys) {
+    if (num_edges < 0 || num_keys < 1) return 0;
+    return edge_sort_workspace(num_edges, num_keys);
+}
+
+int feq_edge_sort(const int32_t *keys, int64_t num_edges, int32_t num_keys, int64_t *perm, int64_t *offsets,
+                  int32_t *status, void *workspace, size_t workspace_bytes, feq_stream_t stream) {
+    if (num_edges < 0 || num_keys < 1 || !offsets || (num_edges > 0 && (!keys || !perm)))
+        return FEQ_ERR_INVALID_ARGUMENT;
+    return launch_edge_sort<int32_t>(keys, num_edges, num_keys, perm, offsets, status, workspace,
+                                     workspace_bytes, (cudaStream_t)stream);
+}
+
+int feq_edge_sort_i64(const int64_t *keys, int64_t num_edges, int32_t num_keys, int64_t *perm,
+                      int64_t *offsets, int32_t *status, void *workspace, size_t workspace_bytes,
+                      feq_stream_t stream) {
+    if (num_edges < 0 || num_keys < 1 || !offsets || (num_edges > 0 && (!keys || !perm)))
+        return FEQ_ERR_INVALID_ARGUMENT;
+    return launch_edge_sort<int64_t>(keys, num_edges, num_keys, perm, offsets, status, workspace,
+                                     workspace_bytes, (cudaStream_t)stream);
+}
+
+size_t feq_block_diagonal_workspace_bytes(int64_t num_edges, int32_t c_in, int32_t c_out,
+                                          const int32_t *lvals_in, int32_t n_lvals_in,
+                                          const int32_t *lvals_out, int32_t n_lvals_out, int32_t num_bins) {
+    MixLayout M;
+    if (!mix_args_ok(num_edges, c_in, c_out, num_bins)) return 0;
+    if (build_mix_layout(lvals_in, n_lvals_in, lvals_out, n_lvals_out, c_in, c_out, &M) != FEQ_OK) return 0;
+    WsCarver w{nullptr, 0, 0};
+    MixPlan p;
+    carve_mix(w, num_edges, num_bins, M, p);
+    return w.used + 256;
+}
+
+int feq_block_diagonal_fwd(const float *features, const float *radial_table, const float *distances,
+                           int64_t num_edges, int32_t c_in, int32_t c_out, const int32_t *lvals_in,
+                           int32_t n_lvals_in, const int32_t *lvals_out, int32_t n_lvals_out, float sh_scale,
+                           float bin_param1, float bin_param2, int32_t num_bins, int32_t log_bins,
+                           float *output, void *workspace, size_t workspace_bytes, feq_stream_t stream) {
+    if (!mix_args_ok(num_edges, c_in, c_out, num_bins)) return FEQ_ERR_INVALID_ARGUMENT;
+    MixLayout M;
+    int rc = build_mix_layout(lvals_in, n_lvals_in, lvals_out, n_lvals_out, c_in, c_out, &M);
+    if (rc != FEQ_OK) return rc;
+    if (num_edges == 0) return FEQ_OK;
+    if (!features || !radial_table || !distances || !output) return FEQ_ERR_INVALID_ARGUMENT;
+    WsCarver w{(char *)workspace, 0, workspace_bytes};
+    MixPlan p;
+    carve_mix(w, num_edges, num_bins, M, p);
+    if (!workspace || w.used > workspace_bytes) return FEQ_ERR_WORKSPACE;
+    const int din = dims_of(lvals_in, n_lvals_in), dout = dims_of(lvals_out, n_lvals_out);
+    Binning b{bin_param1, bin_param2, num_bins, log_bins ? 1 : 0};
+    return run_mix(p, features, radial_table, distances, num_edges, c_in, c_out, din, dout, M, b, sh_scale,
+                   output, (cudaStream_t)stream);
+}
+
+size_t feq_edgewise_workspace_bytes(const FeqEdgewiseArgs *a) {
+    if (!a || !mix_args_ok(a->num_edges, a->c_in, a->c_out, a->num_bins)) return 0;
+    MixLayout M;
+    ReprLayout Li, Lo;
+    if (build_mix_layout(a->lvals_in, a->n_lvals_in, a->lvals_out, a->n_lvals_out, a->c_in, a->c_out, &M) !=
+        FEQ_OK)
+        return 0;
+    if (build_repr_layout(a->lvals_in, a->n_lvals_in, &Li) != FEQ_OK) return 0;
+    if (build_repr_layout(a->lvals_out, a->n_lvals_out, &Lo) != FEQ_OK) return 0;
+    const int64_t E1 = std::max<int64_t>(a->num_edges, 1);
+    WsCarver w{nullptr, 0, 0};
+    w.take(sizeof(float) * (size_t)E1 * a->c_in * Li.dim);
+    w.take(sizeof(float) * (size_t)E1 * a->c_out * Lo.dim);
+    MixPlan p;
+    carve_mix(w, a->num_edges, a->num_bins, M, p);
+    return w.used + 256;
+}
+
+int feq_edgewise_fwd(const FeqEdgewiseArgs *a, void *workspace, size_t workspace_bytes, feq_stream_t stream) {
+    if (!a || !mix_args_ok(a->num_edges, a->c_in, a->c_out, a->num_bins)) return FEQ_ERR_INVALID_ARGUMENT;
+    MixLayout M;
+    ReprLayout Li, Lo;
+    int rc = build_mix_layout(a->lvals_in, a->n_lvals_in, a->lvals_out, a->n_lvals_out, a->c_in, a->c_out, &M);
+    if (rc != FEQ_OK) return rc;
+    if ((rc = build_repr_layout(a->lvals_in, a->n_lvals_in, &Li)) != FEQ_OK) return rc;
+    if ((rc = build_repr_layout(a->lvals_out, a->n_lvals_out, &Lo)) != FEQ_OK) return rc;
+    const int64_t E = a->num_edges;
+    if (E == 0) return FEQ_OK;
+    if (!a->x || !a->distances || !a->radial_table || !a->out) return FEQ_ERR_INVALID_ARGUMENT;
+    if (!a->directions && (!a->P_in || !a->Q_out)) return FEQ_ERR_INVALID_ARGUMENT;
+    if (a->src && a->num_src_rows < 1) return FEQ_ERR_INVALID_ARGUMENT;
+    cudaStream_t s = (cudaStream_t)stream;
+    WsCarver w{(char *)workspace, 0, workspace_bytes};
+    float *g = (float *)w.take(sizeof(float) * (size_t)E * a->c_in * Li.dim);
+    float *h = (float *)w.take(sizeof(float) * (size_t)E * a->c_out * Lo.dim);
+    MixPlan p;
+    carve_mix(w, E, a->num_bins, M, p);
+    if (!workspace || w.used > workspace_bytes) return FEQ_ERR_WORKSPACE;
+    Binning b{a->bin_param1, a->bin_param2, a->num_bins, a->log_bins ? 1 : 0};
+    if ((rc = launch_rotate_in(a->x, a->src, a->num_src_rows, a->edge_add, a->directions, a->P_in, E, a->c_in,
+                               Li, g, a->status, s)) != FEQ_OK)
+        return rc;
+    if ((rc = run_mix(p, g, a->radial_table, a->distances, E, a->c_in, a->c_out, Li.dim, Lo.dim, M, b,
+                      a->sh_scale, h, s)) != FEQ_OK)
+        return rc;
+    return launch_rotate_out(h, a->directions, a->Q_out, E, a->c_out, Lo, a->out, s);
+}
+
+int feq_segment_softmax(const float *logits, int64_t num_edges, int32_t num_heads, const int64_t *perm,
+                        const int64_t *offsets, int64_t num_nodes, float *weights, feq_stream_t stream) {
+    if (num_edges < 0 || num_nodes < 0 || num_heads < 1) return FEQ_ERR_INVALID_ARGUMENT;
+    if (num_edges == 0 || num_nodes == 0) return FEQ_OK;
+    if (!logits || !perm || !offsets || !weights) return FEQ_ERR_INVALID_ARGUMENT;
+    return launch_segment_softmax(logits, num_nodes, num_heads, perm, offsets, weights, (cudaStream_t)stream);
+}
+
+int feq_edge_attention_weights(const float *Q, const float *K, int64_t num_edges, int32_t num_heads,
+                               int32_t qk_dim, float scale, const float *distances, float decay_scale,
+                               const int64_t *perm, const int64_t *offsets, int64_t num_nodes, float *weights,
+                               feq_stream_t stream) {
+    if (num_edges < 0 || num_nodes < 0 || num_heads < 1 || qk_dim < 1) return FEQ_ERR_INVALID_ARGUMENT;
+    if (num_edges == 0) return FEQ_OK;
+    if (!Q || !K || !perm || !offsets || !weights || (decay_scale > 0.0f && !distances))
+        return FEQ_ERR_INVALID_ARGUMENT;
+    cudaStream_t s = (cudaStream_t)stream;
+    int rc = launch_edge_logits(Q, K, num_edges, num_heads, qk_dim, scale, distances, decay_scale, weights, s);
+    if (rc != FEQ_OK) return rc;
+    return launch_segment_softmax(weights, num_nodes, num_heads, perm, offsets, weights, s);
+}
+
+int feq_segment_pool(const float *edge_rows, int64_t row_len, const float *weights, int32_t num_heads,
+                     const int64_t *perm, const int64_t *offsets, int64_t num_nodes, int32_t reduce, float *out,
+                     feq_stream_t stream) {
+    if (row_len < 0 || num_nodes < 0 || reduce < FEQ_REDUCE_SUM || reduce > FEQ_REDUCE_MAX)
+        return FEQ_ERR_INVALID_ARGUMENT;
+    if (weights && (num_heads < 1 || row_len % num_heads)) return FEQ_ERR_INVALID_ARGUMENT;
+    if (num_nodes == 0 || row_len == 0) return FEQ_OK;
+    if (!perm || !offsets || !out) return FEQ_ERR_INVALID_ARGUMENT;
+    return launch_segment_pool(edge_rows, row_len, weights, weights ? num_heads : 0, perm, offsets, num_nodes,
+                               reduce, out, (cudaStream_t)stream);
+}
+
+int feq_attn_pool_fwd(const FeqAttnArgs *a, feq_stream_t stream) {
+    if (!a || a->num_nodes < 0 || a->num_edges < 0 || a->num_heads < 1 || a->c_qk < 1 || a->d_qk < 1 ||
+        a->c_v < 1 || a->d_v < 1)
+        return FEQ_ERR_INVALID_ARGUMENT;
+    if (a->c_qk % a->num_heads || a->c_v % a->num_heads) return FEQ_ERR_INVALID_ARGUMENT;
+    if (a->reduce != FEQ_REDUCE_SUM && a->reduce != FEQ_REDUCE_MEAN) return FEQ_ERR_UNSUPPORTED;
+    if (a->num_nodes == 0) return FEQ_OK;
+    if (!a->qk || !a->perm || !a->offsets || !a->out || (a->num_edges > 0 && (!a->v || !a->src)))
+        return FEQ_ERR_INVALID_ARGUMENT;
+    if (a->decay_scale > 0.0f && !a->distances) return FEQ_ERR_INVALID_ARGUMENT;
+    return launch_attn_pool(*a, (cudaStream_t)stream);
+}
+
+}  // extern "C"

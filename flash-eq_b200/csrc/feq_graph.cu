@@ -1,0 +1,358 @@
+// feq_graph.cu -- edge bookkeeping and the dst-segment operators.
+//
+// Reference behaviour replaced:
+//   compute_binning                    flash_eq/cuda/csrc/block_diagonal.cu:82-115
+//   torch.argsort(distances)           flash_eq/cuda/block_diagonal.py:102-103
+//   _neighbor_softmax (scatter amax / exp / scatter_add / divide)
+//                                      flash_eq/layers/attention.py:108-141
+//   logits (Q*K).sum(-1)*scale - d/decay
+//                                      flash_eq/layers/attention.py:92-99
+//   _apply_attention + GraphPooling    flash_eq/layers/attention.py:143-167,
+//                                      flash_eq/layers/pooling.py:21-57
+//
+// Everything that reduces over a destination works on dst-sorted segments
+// (perm/offsets from a stable radix sort), one CTA or warp per segment, in a
+// fixed order: results are deterministic run to run, unlike scatter_add_.
+#include <cub/device/device_radix_sort.cuh>
+#include <cuda_runtime.h>
+#include <math.h>
+
+#include "feq_internal.cuh"
+
+namespace feq {
+
+// ---------------------------------------------------------------------------
+// Binning
+// ---------------------------------------------------------------------------
+__global__ void binning_kernel(const float *__restrict__ dist, int64_t E, Binning b,
+                               int32_t *__restrict__ lo_out, float *__restrict__ t_out) {
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < E;
+         e += (int64_t)gridDim.x * blockDim.x) {
+        int lo;
+        float t;
+        bin_of(dist[e], b, lo, t);
+        if (lo_out) lo_out[e] = lo;
+        if (t_out) t_out[e] = t;
+    }
+}
+
+int launch_binning(const float *dist, int64_t E, Binning b, int32_t *lo, float *t, cudaStream_t s) {
+    if (E == 0) return FEQ_OK;
+    const int64_t grid = min64((E + 255) / 256, 148 * 32);
+    binning_kernel<<<(unsigned)grid, 256, 0, s>>>(dist, E, b, lo, t);
+    FEQ_LAUNCH_CHECK();
+    return FEQ_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Stable sort by key with segment offsets
+// ---------------------------------------------------------------------------
+template <typename K>
+__global__ void prep_keys_kernel(const K *__restrict__ keys, int64_t E, int32_t nk,
+                                 int32_t *__restrict__ kout, int64_t *__restrict__ ids,
+                                 int32_t *status) {
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < E;
+         e += (int64_t)gridDim.x * blockDim.x) {
+        K k = keys[e];
+        if (k < 0 || k >= (K)nk) {
+            set_status(status, 1);
+            k = (K)(nk - 1);
+        }
+        kout[e] = (int32_t)k;
+        ids[e] = e;
+    }
+}
+
+// offsets[k] = first sorted position whose key is >= k; offsets[nk] = E.
+__global__ void offsets_kernel(const int32_t *__restrict__ sk, int64_t E, int32_t nk,
+                               int64_t *__restrict__ offsets) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i <= E;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int32_t prev = i > 0 ? sk[i - 1] : -1;
+        const int32_t cur = i < E ? sk[i] : nk;
+        for (int32_t k = prev + 1; k <= cur; k++) offsets[k] = i;
+    }
+}
+
+static int key_bits(int32_t nk) {
+    int bits = 1;
+    while (bits < 31 && (1ll << bits) < (long long)nk) bits++;
+    return bits;
+}
+
+static size_t cub_sort_bytes(int64_t E, int32_t nk) {
+    size_t bytes = 0;
+    cub::DeviceRadixSort::SortPairs(nullptr, bytes, (const int32_t *)nullptr, (int32_t *)nullptr,
+                                    (const int64_t *)nullptr, (int64_t *)nullptr, E, 0, key_bits(nk),
+                                    (cudaStream_t)0);
+    return bytes;
+}
+
+size_t edge_sort_workspace(int64_t E, int32_t nk) {
+    WsCarver w{nullptr, 0, 0};
+    w.take(sizeof(int32_t) * max64(E, 1));   // keys in
+    w.take(sizeof(int32_t) * max64(E, 1));   // keys out
+    w.take(sizeof(int64_t) * max64(E, 1));   // ids in
+    w.take(std::max<size_t>(cub_sort_bytes(E, nk), 16));
+    return w.used + 256;
+}
+
+template <typename K>
+int launch_edge_sort(const K *keys, int64_t E, int32_t nk, int64_t *perm, int64_t *offsets,
+                     int32_t *status, void *ws, size_t ws_bytes, cudaStream_t s) {
+    if (nk <= 0) return FEQ_ERR_INVALID_ARGUMENT;
+    if (E == 0) {
+        FEQ_CUDA_TRY(cudaMemsetAsync(offsets, 0, sizeof(int64_t) * (nk + 1), s));
+        return FEQ_OK;
+    }
+    if (ws_bytes < edge_sort_workspace(E, nk) || ws == nullptr) return FEQ_ERR_WORKSPACE;
+    WsCarver w{(char *)ws, 0, ws_bytes};
+    int32_t *kin = (int32_t *)w.take(sizeof(int32_t) * E);
+    int32_t *kout = (int32_t *)w.take(sizeof(int32_t) * E);
+    int64_t *ids = (int64_t *)w.take(sizeof(int64_t) * E);
+    size_t tmp_bytes = std::max<size_t>(cub_sort_bytes(E, nk), 16);
+    void *tmp = w.take(tmp_bytes);
+    const int64_t grid = min64((E + 255) / 256, 148 * 32);
+    prep_keys_kernel<K><<<(unsigned)grid, 256, 0, s>>>(keys, E, nk, kin, ids, status);
+    FEQ_LAUNCH_CHECK();
+    FEQ_CUDA_TRY(cub::DeviceRadixSort::SortPairs(tmp, tmp_bytes, kin, kout, ids, perm, E, 0,
+                                                 key_bits(nk), s));
+    count_launches(3);
+    const int64_t grid2 = min64((E + 256) / 256, 148 * 32);
+    offsets_kernel<<<(unsigned)grid2, 256, 0, s>>>(kout, E, nk, offsets);
+    FEQ_LAUNCH_CHECK();
+    return FEQ_OK;
+}
+
+template int launch_edge_sort<int32_t>(const int32_t *, int64_t, int32_t, int64_t *, int64_t *,
+                                       int32_t *, void *, size_t, cudaStream_t);
+template int launch_edge_sort<int64_t>(const int64_t *, int64_t, int32_t, int64_t *, int64_t *,
+                                       int32_t *, void *, size_t, cudaStream_t);
+
+// ---------------------------------------------------------------------------
+// Edge logits (edge-level Q, K) and segment softmax
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// One warp per (edge, head): logits[e, h] = scale * <Q[e,h,:], K[e,h,:]> - dist/decay.
+__global__ void edge_logits_kernel(const float *__restrict__ Q, const float *__restrict__ K, int64_t E,
+                                   int H, int D, float scale, const float *__restrict__ dist,
+                                   float decay, float *__restrict__ logits) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    for (int64_t w = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); w < E * H; w += warps) {
+        const float *q = Q + w * D, *k = K + w * D;
+        float acc = 0.0f;
+        for (int i = lane; i < D; i += 32) acc = fmaf(__ldg(q + i), __ldg(k + i), acc);
+        acc = warp_sum(acc);
+        if (lane == 0) {
+            float v = acc * scale;
+            if (decay > 0.0f && dist) v -= dist[w / H] / decay;
+            logits[w] = v;
+        }
+    }
+}
+
+// One warp per destination node; heads looped.  In place (logits == weights) is fine.
+__global__ void segment_softmax_kernel(const float *logits, int64_t N, int H,
+                                       const int64_t *__restrict__ perm,
+                                       const int64_t *__restrict__ offsets, float *weights) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    for (int64_t n = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); n < N; n += warps) {
+        const int64_t s0 = offsets[n], s1 = offsets[n + 1];
+        for (int h = 0; h < H; h++) {
+            float mx = -INFINITY;
+            for (int64_t p = s0 + lane; p < s1; p += 32) mx = fmaxf(mx, logits[perm[p] * H + h]);
+            mx = warp_max(mx);
+            float sm = 0.0f;
+            for (int64_t p = s0 + lane; p < s1; p += 32) sm += expf(logits[perm[p] * H + h] - mx);
+            sm = warp_sum(sm);
+            const float inv = 1.0f / (sm + 1e-8f);
+            for (int64_t p = s0 + lane; p < s1; p += 32) {
+                const int64_t e = perm[p];
+                weights[e * H + h] = expf(logits[e * H + h] - mx) * inv;
+            }
+        }
+    }
+}
+
+int launch_edge_logits(const float *Q, const float *K, int64_t E, int H, int D, float scale,
+                       const float *dist, float decay, float *logits, cudaStream_t s) {
+    if (E == 0) return FEQ_OK;
+    const int64_t grid = min64((E * H + 7) / 8, 148 * 32);
+    edge_logits_kernel<<<(unsigned)grid, 256, 0, s>>>(Q, K, E, H, D, scale, dist, decay, logits);
+    FEQ_LAUNCH_CHECK();
+    return FEQ_OK;
+}
+
+int launch_segment_softmax(const float *logits, int64_t N, int H, const int64_t *perm,
+                           const int64_t *offsets, float *weights, cudaStream_t s) {
+    if (N == 0) return FEQ_OK;
+    const int64_t grid = min64((N + 7) / 8, 148 * 64);
+    segment_softmax_kernel<<<(unsigned)grid, 256, 0, s>>>(logits, N, H, perm, offsets, weights);
+    FEQ_LAUNCH_CHECK();
+    return FEQ_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Segmented pooling: one CTA per node, threads over row elements.
+// ---------------------------------------------------------------------------
+__global__ void segment_pool_kernel(const float *__restrict__ rows, int64_t L,
+                                    const float *__restrict__ w, int H,
+                                    const int64_t *__restrict__ perm,
+                                    const int64_t *__restrict__ offsets, int reduce,
+                                    float *__restrict__ out) {
+    const int64_t n = blockIdx.x;
+    const int64_t s0 = offsets[n], s1 = offsets[n + 1];
+    const int64_t hd = H > 0 ? L / H : L;
+    for (int64_t j = threadIdx.x; j < L; j += blockDim.x) {
+        const int h = (w && H > 0) ? (int)(j / hd) : 0;
+        float acc = reduce == FEQ_REDUCE_MAX ? -INFINITY : 0.0f;
+        for (int64_t p = s0; p < s1; p++) {
+            const int64_t e = perm[p];
+            float v = __ldg(rows + e * L + j);
+            if (w) v *= __ldg(w + e * H + h);
+            acc = reduce == FEQ_REDUCE_MAX ? fmaxf(acc, v) : acc + v;
+        }
+        if (reduce == FEQ_REDUCE_MAX) {
+            if (s1 == s0) acc = 0.0f;   // empty segment: -inf -> 0 (pooling.py:57)
+        } else if (reduce == FEQ_REDUCE_MEAN) {
+            acc = acc / (float)max64(s1 - s0, 1);
+        }
+        out[n * L + j] = acc;
+    }
+}
+
+int launch_segment_pool(const float *rows, int64_t L, const float *w, int H, const int64_t *perm,
+                        const int64_t *offsets, int64_t N, int reduce, float *out, cudaStream_t s) {
+    if (N == 0 || L == 0) return FEQ_OK;
+    if (N > 0x7fffffffll) return FEQ_ERR_UNSUPPORTED;
+    const int threads = (int)min64(256, ((L + 31) / 32) * 32);
+    segment_pool_kernel<<<(unsigned)N, threads, 0, s>>>(rows, L, w, H, perm, offsets, reduce, out);
+    FEQ_LAUNCH_CHECK();
+    return FEQ_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Fused attention + pooling (EquivariantAttention without the V projection).
+// One CTA per destination node, online softmax over chunks of the segment.
+// ---------------------------------------------------------------------------
+constexpr int kAttnThreads = 128;
+constexpr int kAttnChunk = 32;
+constexpr int kAttnMaxHeads = 64;
+
+__global__ void __launch_bounds__(kAttnThreads)
+attn_pool_kernel(const __grid_constant__ FeqAttnArgs a) {
+    extern __shared__ float smem[];
+    const int64_t n = blockIdx.x;
+    const int C = a.c_qk, d = a.d_qk, H = a.num_heads;
+    const int qrow = C * d;                 // one of Q / K
+    const int vrow = a.c_v * a.d_v;
+    const int hd = qrow / H;                // Q/K floats per head
+    const int vhd = vrow / H;               // V floats per head
+    float *q_s = smem;                      // qrow
+    float *acc_s = q_s + qrow;              // vrow
+    __shared__ float lg_s[kAttnChunk][kAttnMaxHeads];
+    __shared__ float corr_s[kAttnMaxHeads], m_s[kAttnMaxHeads], sum_s[kAttnMaxHeads];
+    __shared__ int64_t eid_s[kAttnChunk], sid_s[kAttnChunk];
+
+    const float *qn = a.qk + n * (int64_t)(2 * qrow);
+    for (int j = threadIdx.x; j < qrow; j += kAttnThreads) q_s[j] = __ldg(qn + j);
+    for (int j = threadIdx.x; j < vrow; j += kAttnThreads) acc_s[j] = 0.0f;
+    if (threadIdx.x < H) {
+        m_s[threadIdx.x] = -INFINITY;
+        sum_s[threadIdx.x] = 0.0f;
+    }
+    const int64_t s0 = a.offsets[n], s1 = a.offsets[n + 1];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = kAttnThreads / 32;
+    for (int64_t c0 = s0; c0 < s1; c0 += kAttnChunk) {
+        const int cn = (int)min64(kAttnChunk, s1 - c0);
+        __syncthreads();
+        if (threadIdx.x < cn) {
+            const int64_t e = a.perm[c0 + threadIdx.x];
+            int64_t sidx = a.src[e];
+            if (sidx < 0 || sidx >= a.num_nodes) {
+                set_status(a.status, 1);
+                sidx = -1;
+            }
+            eid_s[threadIdx.x] = e;
+            sid_s[threadIdx.x] = sidx;
+        }
+        __syncthreads();
+        // logits: one warp per (edge, head) pair
+        for (int pr = warp; pr < cn * H; pr += nwarps) {
+            const int k = pr / H, h = pr - k * H;
+            const int64_t sidx = sid_s[k];
+            float acc = 0.0f;
+            if (sidx >= 0) {
+                const float *kr = a.qk + sidx * (int64_t)(2 * qrow) + qrow + h * hd;
+                const float *qr = q_s + h * hd;
+                for (int i = lane; i < hd; i += 32) acc = fmaf(qr[i], __ldg(kr + i), acc);
+            }
+            acc = warp_sum(acc);
+            if (lane == 0) {
+                float v = acc * a.scale;
+                if (a.decay_scale > 0.0f && a.distances) v -= a.distances[eid_s[k]] / a.decay_scale;
+                lg_s[k][h] = v;
+            }
+        }
+        __syncthreads();
+        // online softmax update per head
+        if (threadIdx.x < H) {
+            const int h = threadIdx.x;
+            float mc = -INFINITY;
+            for (int k = 0; k < cn; k++) mc = fmaxf(mc, lg_s[k][h]);
+            const float mold = m_s[h], mnew = fmaxf(mold, mc);
+            const float corr = (mold == -INFINITY) ? 0.0f : expf(mold - mnew);
+            float sm = sum_s[h] * corr;
+            for (int k = 0; k < cn; k++) {
+                const float p = expf(lg_s[k][h] - mnew);
+                lg_s[k][h] = p;
+                sm += p;
+            }
+            sum_s[h] = sm;
+            m_s[h] = mnew;
+            corr_s[h] = corr;
+        }
+        __syncthreads();
+        // weighted V accumulation
+        for (int j = threadIdx.x; j < vrow; j += kAttnThreads) {
+            const int h = j / vhd;
+            float acc = acc_s[j] * corr_s[h];
+            for (int k = 0; k < cn; k++) acc = fmaf(lg_s[k][h], __ldg(a.v + eid_s[k] * (int64_t)vrow + j), acc);
+            acc_s[j] = acc;
+        }
+    }
+    __syncthreads();
+    const float cnt = (float)max64(s1 - s0, 1);
+    for (int j = threadIdx.x; j < vrow; j += kAttnThreads) {
+        const int h = j / vhd;
+        float v = acc_s[j] / (sum_s[h] + 1e-8f);
+        if (a.reduce == FEQ_REDUCE_MEAN) v /= cnt;
+        a.out[n * (int64_t)vrow + j] = v;
+    }
+}
+
+int launch_attn_pool(const FeqAttnArgs &a, cudaStream_t s) {
+    if (a.num_nodes == 0) return FEQ_OK;
+    if (a.num_heads < 1 || a.num_heads > kAttnMaxHeads) return FEQ_ERR_UNSUPPORTED;
+    if (a.num_nodes > 0x7fffffffll) return FEQ_ERR_UNSUPPORTED;
+    const size_t smem = sizeof(float) * ((size_t)a.c_qk * a.d_qk + (size_t)a.c_v * a.d_v);
+    if (smem > 160 * 1024) return FEQ_ERR_UNSUPPORTED;
+    FEQ_CUDA_TRY(cudaFuncSetAttribute(attn_pool_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    attn_pool_kernel<<<(unsigned)a.num_nodes, kAttnThreads, smem, s>>>(a);
+    FEQ_LAUNCH_CHECK();
+    return FEQ_OK;
+}
+
+}  // namespace feq

@@ -1,0 +1,280 @@
+"""Torch-facing wrappers of the native ops.
+
+Every op: checks that inputs are CUDA float32 tensors, makes them contiguous,
+allocates outputs and workspace through torch's caching allocator, and enqueues
+the kernels on the current CUDA stream.  There is no CPU path: on a machine
+without a GPU the ops raise ``CUDANotAvailableError`` (the reference's error,
+flash_eq/cuda/block_diagonal.py:34-55).
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+
+
+class CUDANotAvailableError(RuntimeError):
+    """Raised when CUDA is required but not available (flash_eq/cuda/block_diagonal.py:34-36)."""
+
+
+def _require_cuda(*tensors):
+    if not torch.cuda.is_available():
+        raise CUDANotAvailableError(
+            "flash-eq requires a CUDA-capable GPU. No CUDA device was detected."
+        )
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("flash-eq ops need CUDA tensors; got a tensor on " + str(t.device))
+    return _lib.load()
+
+
+def _f32(t: torch.Tensor, name: str) -> torch.Tensor:
+    if t.dtype != torch.float32:
+        raise TypeError(f"{name}: flash-eq B200 kernels compute in float32; got {t.dtype}")
+    return t.contiguous()
+
+
+def _p(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def _stream(device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _workspace(nbytes: int, device) -> torch.Tensor:
+    return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+
+
+def dim_of(lvals) -> int:
+    return sum(2 * int(l) + 1 for l in lvals)
+
+
+# ---------------------------------------------------------------------------
+def wigner_basis(directions: torch.Tensor, lvals, layout: int = _lib.FEQ_BASIS_MFIRST) -> torch.Tensor:
+    lib = _require_cuda(directions)
+    directions = _f32(directions, "directions")
+    if directions.dim() != 2 or directions.shape[-1] != 3:
+        raise ValueError(f"directions must be (E, 3); got {tuple(directions.shape)}")
+    E = directions.shape[0]
+    d = dim_of(lvals)
+    out = torch.empty(E, d, d, device=directions.device, dtype=torch.float32)
+    arr, n = _lib.i32_array(lvals)
+    rc = lib.feq_wigner_basis(_p(directions), E, arr, n, layout, _p(out), _stream(directions.device))
+    _lib.check(rc, "feq_wigner_basis")
+    return out
+
+
+def edge_binning(distances: torch.Tensor, p1: float, p2: float, num_bins: int, log_bins: bool):
+    lib = _require_cuda(distances)
+    distances = _f32(distances, "distances")
+    E = distances.numel()
+    lo = torch.empty(E, dtype=torch.int32, device=distances.device)
+    t = torch.empty(E, dtype=torch.float32, device=distances.device)
+    rc = lib.feq_edge_binning(_p(distances), E, float(p1), float(p2), int(num_bins), int(bool(log_bins)),
+                              _p(lo), _p(t), _stream(distances.device))
+    _lib.check(rc, "feq_edge_binning")
+    return lo, t
+
+
+def edge_sort(keys: torch.Tensor, num_keys: int):
+    """Stable sort of edge ids by key -> (perm int64 (E,), offsets int64 (num_keys+1,), status int32 (1,))."""
+    lib = _require_cuda(keys)
+    keys = keys.contiguous()
+    E = keys.numel()
+    dev = keys.device
+    perm = torch.empty(E, dtype=torch.int64, device=dev)
+    offsets = torch.empty(num_keys + 1, dtype=torch.int64, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    ws_bytes = lib.feq_edge_sort_workspace_bytes(E, num_keys)
+    ws = _workspace(ws_bytes, dev)
+    if keys.dtype == torch.int64:
+        fn = lib.feq_edge_sort_i64
+    elif keys.dtype == torch.int32:
+        fn = lib.feq_edge_sort
+    else:
+        raise TypeError("edge_sort keys must be int32 or int64")
+    rc = fn(_p(keys), E, int(num_keys), _p(perm), _p(offsets), _p(status), _p(ws), ws.numel(), _stream(dev))
+    _lib.check(rc, "feq_edge_sort")
+    return perm, offsets, status
+
+
+def block_diagonal_fwd(features, radial_table, distances, lvals_in, lvals_out, sh_scale, p1, p2,
+                       num_bins, log_bins):
+    lib = _require_cuda(features, radial_table, distances)
+    features = _f32(features, "features")
+    radial_table = _f32(radial_table, "radial_table")
+    distances = _f32(distances, "distances")
+    E, c_in, d_in = features.shape
+    c_out = radial_table.shape[1]
+    d_out = dim_of(lvals_out)
+    if d_in != dim_of(lvals_in):
+        raise ValueError(f"features dim {d_in} does not match lvals_in {list(lvals_in)}")
+    if radial_table.shape[0] != num_bins + 1 or radial_table.shape[2] != c_in:
+        raise ValueError(f"radial_table shape {tuple(radial_table.shape)} does not match "
+                         f"(num_bins+1={num_bins + 1}, Cout, Cin={c_in}, W)")
+    out = torch.empty(E, c_out, d_out, dtype=torch.float32, device=features.device)
+    if E == 0:
+        return out
+    ai, ni = _lib.i32_array(lvals_in)
+    ao, no = _lib.i32_array(lvals_out)
+    ws_bytes = lib.feq_block_diagonal_workspace_bytes(E, c_in, c_out, ai, ni, ao, no, int(num_bins))
+    if ws_bytes == 0:
+        raise RuntimeError("block-diagonal: unsupported layout (l <= 16, <= 64 irreps)")
+    ws = _workspace(ws_bytes, features.device)
+    rc = lib.feq_block_diagonal_fwd(_p(features), _p(radial_table), _p(distances), E, c_in, c_out, ai, ni, ao,
+                                    no, float(sh_scale), float(p1), float(p2), int(num_bins),
+                                    int(bool(log_bins)), _p(out), _p(ws), ws.numel(),
+                                    _stream(features.device))
+    _lib.check(rc, "feq_block_diagonal_fwd")
+    return out
+
+
+def edgewise_fwd(x, distances, radial_table, lvals_in, lvals_out, c_out, sh_scale, p1, p2, num_bins,
+                 log_bins, *, src=None, edge_add=None, directions=None, P=None, Q=None, status=None):
+    """Fused Q . Lambda(r) . P^T . f.  Rows f[e] = x[src[e]] (+ edge_add[e]) or x[e].
+
+    Basis from ``directions`` (E, 3) when given, else from the dense P (E, d_in, d_in)
+    and Q (E, d_out, d_out).
+    """
+    lib = _require_cuda(x, distances, radial_table, src, edge_add, directions, P, Q)
+    x = _f32(x, "x")
+    distances = _f32(distances, "distances")
+    radial_table = _f32(radial_table, "radial_table")
+    E = distances.numel()
+    c_in = x.shape[1]
+    d_in, d_out = dim_of(lvals_in), dim_of(lvals_out)
+    if x.shape[2] != d_in:
+        raise ValueError(f"feature dim {x.shape[2]} does not match lvals_in {list(lvals_in)}")
+    if radial_table.shape[0] != num_bins + 1 or radial_table.shape[1] != c_out or radial_table.shape[2] != c_in:
+        raise ValueError(f"radial_table shape {tuple(radial_table.shape)} does not match "
+                         f"({num_bins + 1}, {c_out}, {c_in}, W)")
+    dev = x.device
+    out = torch.empty(E, c_out, d_out, dtype=torch.float32, device=dev)
+    if E == 0:
+        return out
+    args = _lib.FeqEdgewiseArgs()
+    args.x = x.data_ptr()
+    if src is not None:
+        src = src.contiguous()
+        if src.dtype != torch.int64:
+            src = src.to(torch.int64)
+        args.src = src.data_ptr()
+        args.num_src_rows = x.shape[0]
+    elif x.shape[0] != E:
+        raise ValueError("edge features must have one row per edge")
+    if edge_add is not None:
+        edge_add = _f32(edge_add, "edge_features")
+        args.edge_add = edge_add.data_ptr()
+    if directions is not None:
+        directions = _f32(directions, "directions")
+        args.directions = directions.data_ptr()
+    else:
+        P = _f32(P, "P")
+        Q = _f32(Q, "Q")
+        if tuple(P.shape) != (E, d_in, d_in) or tuple(Q.shape) != (E, d_out, d_out):
+            raise ValueError(f"P {tuple(P.shape)} / Q {tuple(Q.shape)} do not match E={E}, "
+                             f"d_in={d_in}, d_out={d_out}")
+        args.P_in = P.data_ptr()
+        args.Q_out = Q.data_ptr()
+    args.distances = distances.data_ptr()
+    args.radial_table = radial_table.data_ptr()
+    args.num_edges = E
+    args.c_in, args.c_out = c_in, c_out
+    ai, ni = _lib.i32_array(lvals_in)
+    ao, no = _lib.i32_array(lvals_out)
+    args.lvals_in, args.n_lvals_in = ai, ni
+    args.lvals_out, args.n_lvals_out = ao, no
+    args.sh_scale, args.bin_param1, args.bin_param2 = float(sh_scale), float(p1), float(p2)
+    args.num_bins, args.log_bins = int(num_bins), int(bool(log_bins))
+    args.out = out.data_ptr()
+    if status is not None:
+        args.status = status.data_ptr()
+    ws_bytes = lib.feq_edgewise_workspace_bytes(ctypes.byref(args))
+    if ws_bytes == 0:
+        raise RuntimeError("edgewise: unsupported layout (l <= 16, <= 64 irreps, dim <= 512)")
+    ws = _workspace(ws_bytes, dev)
+    rc = lib.feq_edgewise_fwd(ctypes.byref(args), _p(ws), ws.numel(), _stream(dev))
+    _lib.check(rc, "feq_edgewise_fwd")
+    return out
+
+
+def segment_softmax(logits, perm, offsets, num_nodes):
+    lib = _require_cuda(logits, perm, offsets)
+    logits = _f32(logits, "logits")
+    E, H = logits.shape
+    w = torch.empty_like(logits)
+    if E == 0:
+        return w
+    rc = lib.feq_segment_softmax(_p(logits), E, H, _p(perm), _p(offsets), int(num_nodes), _p(w),
+                                 _stream(logits.device))
+    _lib.check(rc, "feq_segment_softmax")
+    return w
+
+
+def edge_attention_weights(Q, K, scale, distances, decay, perm, offsets, num_nodes):
+    lib = _require_cuda(Q, K, perm, offsets)
+    Q, K = _f32(Q, "Q"), _f32(K, "K")
+    E, H, D = Q.shape
+    w = torch.empty(E, H, dtype=torch.float32, device=Q.device)
+    if E == 0:
+        return w
+    dptr = None
+    if decay is not None and distances is not None:
+        distances = _f32(distances, "distances")
+        dptr = _p(distances)
+    rc = lib.feq_edge_attention_weights(_p(Q), _p(K), E, H, D, float(scale), dptr,
+                                        float(decay) if dptr is not None else 0.0, _p(perm), _p(offsets),
+                                        int(num_nodes), _p(w), _stream(Q.device))
+    _lib.check(rc, "feq_edge_attention_weights")
+    return w
+
+
+def segment_pool(rows, perm, offsets, num_nodes, reduce="sum", weights=None):
+    """rows (E, C, d) -> (N, C, d); optional per-head weights (E, H)."""
+    lib = _require_cuda(rows, perm, offsets, weights)
+    rows = _f32(rows, "edge_features")
+    E = rows.shape[0]
+    L = rows[0].numel() if E > 0 else int(torch.tensor(rows.shape[1:]).prod())
+    out = torch.empty((num_nodes,) + tuple(rows.shape[1:]), dtype=torch.float32, device=rows.device)
+    H = 0
+    wptr = None
+    if weights is not None:
+        weights = _f32(weights, "weights")
+        H = weights.shape[1]
+        wptr = _p(weights)
+    rc = lib.feq_segment_pool(_p(rows), L, wptr, H, _p(perm), _p(offsets), int(num_nodes),
+                              _lib.FEQ_REDUCE[reduce], _p(out), _stream(rows.device))
+    _lib.check(rc, "feq_segment_pool")
+    return out
+
+
+def attn_pool(qk, v, src, distances, perm, offsets, num_nodes, num_heads, scale, decay, reduce="sum",
+              status=None):
+    """Fused softmax-attention pooling: QK (N, 2C, d) node rows, V (E, Cv, dv) edge rows."""
+    lib = _require_cuda(qk, v, src, perm, offsets)
+    qk, v = _f32(qk, "QK"), _f32(v, "V")
+    N, c2, d = qk.shape
+    E, c_v, d_v = v.shape
+    out = torch.empty(num_nodes, c_v, d_v, dtype=torch.float32, device=qk.device)
+    a = _lib.FeqAttnArgs()
+    a.qk, a.v = qk.data_ptr(), v.data_ptr()
+    src = src.contiguous()
+    a.src = src.data_ptr()
+    if decay is not None:
+        distances = _f32(distances, "distances")
+        a.distances = distances.data_ptr()
+        a.decay_scale = float(decay)
+    a.perm, a.offsets = perm.data_ptr(), offsets.data_ptr()
+    a.num_nodes, a.num_edges = int(num_nodes), E
+    a.c_qk, a.d_qk, a.c_v, a.d_v, a.num_heads = c2 // 2, d, c_v, d_v, int(num_heads)
+    a.scale = float(scale)
+    a.reduce = _lib.FEQ_REDUCE[reduce]
+    a.out = out.data_ptr()
+    if status is not None:
+        a.status = status.data_ptr()
+    rc = lib.feq_attn_pool_fwd(ctypes.byref(a), _stream(qk.device))
+    _lib.check(rc, "feq_attn_pool_fwd")
+    return out

@@ -1,0 +1,115 @@
+"""SO(3)-equivariant linear layers (flash_eq/layers/linear.py in the reference).
+
+``EquivariantEdgewiseLinear`` computes out = Q . Lambda(r) . P^T . f per edge in
+one native call (rotate into the edge frame, distance-interpolated block-diagonal
+mix, rotate back).  The reference does bmm -> block_diagonal_cuda -> bmm with
+argsort/gather copies around the kernel (linear.py:100-160).
+
+When P and Q are the unmodified outputs of ``WignerDBasis`` (or ``LazyBasis``
+handles) for the same directions, the kernel rebuilds their blocks from the
+directions and never reads the dense matrices; any other P / Q is applied as a
+dense matrix exactly like the reference's bmm.
+
+``EquivariantLinear`` is node-level and stays in PyTorch (linear.py:172-268).
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn as nn
+
+from ..cuda import ops
+from ..cuda.block_diagonal import forward_only
+from ..representations import ProductRepr, Repr
+from ..representations.wigner import LazyBasis, basis_source
+from .radial import SeparableRadialNet
+
+
+def _dense(M):
+    return M.dense() if isinstance(M, LazyBasis) else M
+
+
+class EquivariantEdgewiseLinear(nn.Module):
+    """Edgewise equivariant linear map with distance-binned radial weights."""
+
+    radial_weights: SeparableRadialNet
+
+    def __init__(self, in_repr: Repr, out_repr: Repr, num_bins: int = 100, rank: int = 4, hidden_dim: int = 64,
+                 min_dist: float = 0.0, max_dist: float = 10.0, log_bins: bool = False,
+                 solid_harmonic_scale: float = 0.1) -> None:
+        super().__init__()
+        self.in_repr, self.out_repr = in_repr, out_repr
+        self.rank = rank
+        self.solid_harmonic_scale = solid_harmonic_scale
+        self.product_repr = ProductRepr(in_repr, out_repr)
+        self.weight_dim = self.product_repr.nreps()
+        self.channels_in, self.channels_out = in_repr.mult, out_repr.mult
+        self.radial_weights = SeparableRadialNet(num_bins=num_bins, out_mult=self.channels_out,
+                                                 in_mult=self.channels_in, weight_dim=self.weight_dim, rank=rank,
+                                                 hidden_dim=hidden_dim, min_val=min_dist, max_val=max_dist,
+                                                 log=log_bins)
+        self._lin = tuple(in_repr.lvals.tolist())
+        self._lout = tuple(out_repr.lvals.tolist())
+
+    def forward(self, P, Q, edge_features: torch.Tensor, distances: torch.Tensor) -> torch.Tensor:
+        """(E, Cin, d_in) edge features -> (E, Cout, d_out), standard SH order."""
+        return self._run(P, Q, edge_features, distances)
+
+    def _run(self, P, Q, x, distances, src=None, edge_add=None):
+        rw = self.radial_weights
+        E = distances.shape[0]
+        if E == 0:
+            return torch.zeros(0, self.channels_out, self.out_repr.dim(), device=x.device, dtype=x.dtype)
+        p1, p2 = rw.binning_params()
+        table = rw()
+        dist = distances.to(torch.float32)
+        dP, dQ = basis_source(P, self._lin), basis_source(Q, self._lout)
+        fused = dP is not None and dQ is not None and dP is dQ
+        Pd = Qd = None
+        if not fused:
+            Pd, Qd = _dense(P), _dense(Q)
+
+        def run(xx, tab, dd, ea, pp, qq):
+            return ops.edgewise_fwd(
+                xx.detach(), dd.detach(), tab.detach(), self._lin, self._lout, self.channels_out,
+                self.solid_harmonic_scale, p1, p2, rw.num_bins, rw.log, src=src,
+                edge_add=None if ea is None else ea.detach(), directions=dP if fused else None,
+                P=None if pp is None else pp.detach(), Q=None if qq is None else qq.detach())
+
+        return forward_only(run, x, table, dist, edge_add, Pd, Qd)
+
+    def extra_repr(self) -> str:
+        rw = self.radial_weights
+        return (f"in_repr={self.in_repr}, out_repr={self.out_repr}, num_bins={rw.num_bins}, "
+                f"dist=[{rw.min_val}, {rw.max_val}], spacing={'log' if rw.log else 'linear'}, rank={self.rank}")
+
+
+class EquivariantLinear(nn.Module):
+    """Per-degree channel mixing; bias (and activation) on l = 0 components only."""
+
+    def __init__(self, in_repr: Repr, out_repr: Repr, bias: bool = True, activation: nn.Module | None = None) -> None:
+        super().__init__()
+        if not torch.equal(in_repr.lvals, out_repr.lvals):
+            raise ValueError(
+                "EquivariantLinear cannot modify the degrees of a representation. "
+                f"Got input lvals={in_repr.lvals.tolist()}, output lvals={out_repr.lvals.tolist()}"
+            )
+        self.in_repr, self.out_repr = in_repr, out_repr
+        self.weight = nn.Parameter(torch.empty(in_repr.nreps() * out_repr.mult, in_repr.mult))
+        nn.init.xavier_uniform_(self.weight)
+        self.register_buffer("indices", torch.tensor(in_repr.indices(), dtype=torch.long))
+        self.expanddims = (1, out_repr.mult, in_repr.dim())
+        self.outdims = (in_repr.nreps(), out_repr.mult, in_repr.dim())
+        nscalar, self.scalar_locs = in_repr.find_scalar()
+        self.bias: nn.Parameter | None
+        self.bias = nn.Parameter(torch.zeros(out_repr.mult, nscalar)) if (nscalar > 0 and bias) else None
+        self.activation = activation if activation is not None else nn.Identity()
+
+    def forward(self, f: torch.Tensor) -> torch.Tensor:
+        *b, _, _ = f.shape
+        out = (self.weight @ f).view(*b, *self.outdims)
+        ix = self.indices.expand(*b, *self.expanddims)
+        out = out.gather(dim=-3, index=ix).squeeze(-3)
+        if self.bias is not None:
+            out = out.clone()
+            out[..., self.scalar_locs] = self.activation(out[..., self.scalar_locs] + self.bias).to(out.dtype)
+        return out

@@ -1,0 +1,224 @@
+/*
+ * flasheq_b200.h -- C ABI of libflasheq_b200.so, the B200 (sm_100a) kernels behind
+ * the drop-in ``flash_eq`` Python package.
+ *
+ * Conventions (all entry points):
+ *   - Plain device pointers and sizes; no framework types.  The caller owns every
+ *     buffer, including the workspace (size from the matching *_workspace_bytes).
+ *   - Work is enqueued on ``stream`` (a cudaStream_t passed as void*); nothing
+ *     synchronises the host, nothing allocates device memory.
+ *   - Return FEQ_OK or an FEQ_ERR_* code; never abort or trap.  feq_status_string
+ *     turns a code into text.  Problems only a kernel can see (an index out of
+ *     range) are written to the caller's int32 ``status`` word, which the caller
+ *     may read after the stream completes (0 == fine).
+ *   - Tensors are row-major and contiguous, float32 unless stated.
+ *   - Layouts follow hmblair/flash-eq: features (E, C, dim) in the standard
+ *     (l, m = -l..l) order; "m-first" order as built by
+ *     flash_eq/representations/wigner.py:243-272; radial table
+ *     (num_bins + 1, C_out, C_in, W) with W = ProductRepr(in, out).nreps().
+ *
+ * Each entry point names the reference interface it replaces.
+ */
+#ifndef FLASHEQ_B200_H
+#define FLASHEQ_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef void *feq_stream_t; /* cudaStream_t */
+
+enum feq_status_code {
+    FEQ_OK = 0,
+    FEQ_ERR_INVALID_ARGUMENT = 1,   /* bad pointer / size / layout */
+    FEQ_ERR_UNSUPPORTED = 2,        /* valid request outside this build's limits */
+    FEQ_ERR_WORKSPACE = 3,          /* workspace missing or too small */
+    FEQ_ERR_CUDA = 4,               /* a CUDA runtime call or launch failed */
+    FEQ_ERR_NO_DEVICE = 5           /* no usable CUDA device */
+};
+
+/* Limits.  FEQ_MAX_L matches the reference's MAX_LVALS = 17 (l <= 16,
+ * flash_eq/cuda/csrc/block_diagonal.cu:172, :1298-1300). */
+#define FEQ_MAX_L 16
+#define FEQ_MAX_IRREPS 64
+#define FEQ_MAX_DIM 512
+
+/* Basis output layouts for feq_wigner_basis. */
+#define FEQ_BASIS_MFIRST 0     /* WignerDBasis.forward: rot_to_ez(d).mT[..., perm] */
+#define FEQ_BASIS_ROT_TO_EZ 1  /* WignerD.rot_to_ez: rot(axis, angle).mT, standard order */
+
+/* Pooling / reduction modes (flash_eq/layers/pooling.py:21-57). */
+#define FEQ_REDUCE_SUM 0
+#define FEQ_REDUCE_MEAN 1
+#define FEQ_REDUCE_MAX 2
+
+/* ---------------------------------------------------------------------------
+ * Library
+ * ------------------------------------------------------------------------ */
+const char *feq_status_string(int status);
+int feq_abi_version(void);
+/* Human-readable last CUDA error seen by this thread (empty when none). */
+const char *feq_last_error(void);
+/* Kernels this library has enqueued since load (its own kernels; each CUB radix
+ * sort call is counted once per kernel it launches: 3).  No counterpart in the
+ * reference; used by benchmarks to report how many native kernels ran. */
+int64_t feq_launch_count(void);
+
+/* ---------------------------------------------------------------------------
+ * Wigner-D basis.
+ * Replaces WignerDBasis.forward / WignerD.rot_to_ez
+ * (flash_eq/representations/wigner.py:198-240, :341-370), which build the
+ * matrices with a batched torch.linalg.matrix_exp.  Here each (edge, l) block is
+ * a closed form in (theta, phi) evaluated per edge.
+ *   directions (E, 3) need not be normalised; out (E, dim, dim).
+ * ------------------------------------------------------------------------ */
+int feq_wigner_basis(const float *directions, int64_t num_edges, const int32_t *lvals,
+                     int32_t num_lvals, int32_t layout, float *out, feq_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Distance binning (block_diagonal.cu:82-115 compute_binning): per edge the bin
+ * index lo (int32, bit-exact) and interpolation weight t (unclamped in linear mode).
+ * ------------------------------------------------------------------------ */
+int feq_edge_binning(const float *distances, int64_t num_edges, float bin_param1,
+                     float bin_param2, int32_t num_bins, int32_t log_bins, int32_t *bin_lo,
+                     float *t, feq_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Stable sort of edges by an int32 key in [0, num_keys): perm[i] = id of the i-th
+ * edge in (key, id) order, offsets[k] = first position of key k (num_keys + 1
+ * entries).  Keys outside the range set *status and are treated as num_keys - 1.
+ * Used for the bin grouping of the radial mix and for dst-sorted (CSR) segments.
+ * The reference sorts with torch.argsort (flash_eq/cuda/block_diagonal.py:102-103)
+ * and pools with scatter_add_ (flash_eq/layers/pooling.py:21-30).
+ * ------------------------------------------------------------------------ */
+size_t feq_edge_sort_workspace_bytes(int64_t num_edges, int32_t num_keys);
+int feq_edge_sort(const int32_t *keys, int64_t num_edges, int32_t num_keys, int64_t *perm,
+                  int64_t *offsets, int32_t *status, void *workspace, size_t workspace_bytes,
+                  feq_stream_t stream);
+/* Same, reading int64 keys (e.g. Graph.dst). */
+int feq_edge_sort_i64(const int64_t *keys, int64_t num_edges, int32_t num_keys, int64_t *perm,
+                      int64_t *offsets, int32_t *status, void *workspace, size_t workspace_bytes,
+                      feq_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Block-diagonal radial mix in the m-first basis.
+ * Replaces _block_diagonal_cuda.forward (flash_eq/cuda/csrc/block_diagonal.cu:
+ * 1268-1540) called through block_diagonal_cuda (flash_eq/cuda/block_diagonal.py:
+ * 206-274): features (E, Cin, Din) m-first, radial_table (num_bins+1, Cout, Cin, W),
+ * distances (E,) -> output (E, Cout, Dout) m-first.  No host sync, no sort/unsort
+ * copies: edges are grouped by bin internally and results land in input order.
+ * ------------------------------------------------------------------------ */
+size_t feq_block_diagonal_workspace_bytes(int64_t num_edges, int32_t c_in, int32_t c_out,
+                                          const int32_t *lvals_in, int32_t n_lvals_in,
+                                          const int32_t *lvals_out, int32_t n_lvals_out,
+                                          int32_t num_bins);
+int feq_block_diagonal_fwd(const float *features, const float *radial_table,
+                           const float *distances, int64_t num_edges, int32_t c_in,
+                           int32_t c_out, const int32_t *lvals_in, int32_t n_lvals_in,
+                           const int32_t *lvals_out, int32_t n_lvals_out, float sh_scale,
+                           float bin_param1, float bin_param2, int32_t num_bins,
+                           int32_t log_bins, float *output, void *workspace,
+                           size_t workspace_bytes, feq_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Fused edgewise linear: out = Q . Lambda(r) . P^T . f.
+ * Replaces EquivariantEdgewiseLinear.forward (flash_eq/layers/linear.py:100-160):
+ * bmm(f, P) -> block_diagonal_cuda -> bmm(out, Q^T).
+ *
+ * Input rows: f[e] = x[src[e]] (+ edge_add[e]) when src != NULL (the gather of
+ * EquivariantAttention, flash_eq/layers/attention.py:307-310), else x[e].
+ * Basis: when directions != NULL, P and Q blocks are built per edge from the edge
+ * direction (never materialised); otherwise the dense (E, d, d) matrices P_in and
+ * Q_out are read as given, exactly like the reference's bmm.
+ * ------------------------------------------------------------------------ */
+typedef struct FeqEdgewiseArgs {
+    const float *x;            /* (E or N, c_in, d_in) */
+    const int64_t *src;        /* optional (E,) gather index into x */
+    int64_t num_src_rows;      /* rows of x when src != NULL (bounds check) */
+    const float *edge_add;     /* optional (E, c_in, d_in) added after the gather */
+    const float *directions;   /* optional (E, 3): fused basis */
+    const float *P_in;         /* (E, d_in, d_in) when directions == NULL */
+    const float *Q_out;        /* (E, d_out, d_out) when directions == NULL */
+    const float *distances;    /* (E,) */
+    const float *radial_table; /* (num_bins + 1, c_out, c_in, W) */
+    int64_t num_edges;
+    int32_t c_in, c_out;
+    const int32_t *lvals_in;   /* host array */
+    int32_t n_lvals_in;
+    const int32_t *lvals_out;  /* host array */
+    int32_t n_lvals_out;
+    float sh_scale, bin_param1, bin_param2;
+    int32_t num_bins, log_bins;
+    float *out;                /* (E, c_out, d_out) standard order */
+    int32_t *status;           /* optional device int32: 1 = a src index was out of range */
+} FeqEdgewiseArgs;
+
+size_t feq_edgewise_workspace_bytes(const FeqEdgewiseArgs *args);
+int feq_edgewise_fwd(const FeqEdgewiseArgs *args, void *workspace, size_t workspace_bytes,
+                     feq_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Segment softmax over edges that share a destination
+ * (EquivariantEdgeAttention._neighbor_softmax, flash_eq/layers/attention.py:108-141):
+ *   w[e, h] = exp(l[e,h] - max_seg) / (sum_seg exp(. - max_seg) + 1e-8)
+ * with perm/offsets from feq_edge_sort on dst.  Deterministic (no atomics).
+ * ------------------------------------------------------------------------ */
+int feq_segment_softmax(const float *logits, int64_t num_edges, int32_t num_heads,
+                        const int64_t *perm, const int64_t *offsets, int64_t num_nodes,
+                        float *weights, feq_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Edge attention logits and weights for edge-level Q, K
+ * (EquivariantEdgeAttention.forward, attention.py:92-103):
+ *   logits[e,h] = scale * sum_i Q[e,h,i] K[e,h,i] - (decay > 0 ? dist[e]/decay : 0)
+ *   weights = segment softmax of logits.
+ * ------------------------------------------------------------------------ */
+int feq_edge_attention_weights(const float *Q, const float *K, int64_t num_edges,
+                               int32_t num_heads, int32_t qk_dim, float scale,
+                               const float *distances, float decay_scale, const int64_t *perm,
+                               const int64_t *offsets, int64_t num_nodes, float *weights,
+                               feq_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Segmented pooling of edge rows onto destination nodes
+ * (GraphPooling, flash_eq/layers/pooling.py:21-57; scatter_add_ / scatter_reduce_):
+ *   out[n, :] = reduce_{e : dst[e] = n} (w[e, head(j)] *) X[e, :]
+ * row_len = C * dim.  When weights != NULL each row is first multiplied per head:
+ * element j of a row belongs to head j / (row_len / num_heads)
+ * (EquivariantEdgeAttention._apply_attention, attention.py:143-167).
+ * Nodes without edges get 0 (sum, mean, max).  Deterministic.
+ * ------------------------------------------------------------------------ */
+int feq_segment_pool(const float *edge_rows, int64_t row_len, const float *weights,
+                     int32_t num_heads, const int64_t *perm, const int64_t *offsets,
+                     int64_t num_nodes, int32_t reduce, float *out, feq_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Fused attention + pooling for EquivariantAttention (attention.py:271-314):
+ *   Q = QK[dst, :C], K = QK[src, C:], logits per head as above (online softmax
+ *   over the dst segment), out[n] = reduce_e w[e, head] * V[e]   (sum or mean).
+ * QK (N, 2C, d) node rows; V (E, Cv, dv) edge rows.
+ * ------------------------------------------------------------------------ */
+typedef struct FeqAttnArgs {
+    const float *qk;          /* (N, 2*c_qk, d_qk) */
+    const float *v;           /* (E, c_v, d_v) */
+    const int64_t *src;       /* (E,) */
+    const float *distances;   /* (E,), may be NULL when decay_scale <= 0 */
+    const int64_t *perm;      /* dst-sorted edge ids (E,) */
+    const int64_t *offsets;   /* (N + 1,) */
+    int64_t num_nodes, num_edges;
+    int32_t c_qk, d_qk, c_v, d_v, num_heads;
+    float scale, decay_scale;
+    int32_t reduce;           /* FEQ_REDUCE_SUM or FEQ_REDUCE_MEAN */
+    float *out;               /* (N, c_v, d_v) */
+    int32_t *status;          /* optional: 1 = a src index was out of range */
+} FeqAttnArgs;
+
+int feq_attn_pool_fwd(const FeqAttnArgs *args, feq_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* FLASHEQ_B200_H */
