@@ -64,10 +64,11 @@ def knn_graph(coords: torch.Tensor, k: int, chunk: int = 4096):
     return nbr.reshape(-1), dst
 
 
-def make_workload(seed: int, device):
+def make_workload(seed: int, device, n_nodes: int = N_NODES):
+    """Nodes uniform in a cube of side BOX * (n_nodes / N_NODES)^(1/3) (constant density)."""
     g = torch.Generator().manual_seed(seed)
-    coords = torch.rand(N_NODES, 3, generator=g) * BOX
-    x = torch.randn(N_NODES, MULT, sum(2 * l + 1 for l in LVALS), generator=g)
+    coords = torch.rand(n_nodes, 3, generator=g) * (BOX * (n_nodes / N_NODES) ** (1.0 / 3.0))
+    x = torch.randn(n_nodes, MULT, sum(2 * l + 1 for l in LVALS), generator=g)
     coords_d = coords.to(device)
     src, dst = knn_graph(coords_d, K_NN)
     return {"coords": coords, "x": x, "coords_d": coords_d, "x_d": x.to(device), "src": src, "dst": dst}
@@ -252,7 +253,10 @@ def run_reference(args):
     return 0
 
 
-def config_block(n_gpus):
+def config_block(n_gpus, n_nodes=N_NODES):
+    if n_nodes != N_NODES:
+        return {"workload": f"profiling case: config-2 shapes with N={n_nodes} nodes, E={n_nodes * K_NN}",
+                "edges_per_gpu": n_nodes * K_NN, "global_edges": n_nodes * K_NN * n_gpus}
     return {"workload": "config2: WignerDBasis + EquivariantEdgewiseLinear forward, Repr([0,1,2,3,4],64) -> same, "
                         "N=20000 uniform 60A cube, 32-NN, E=640000 per GPU, 100 bins over [0,10]",
             "edges_per_gpu": N_NODES * K_NN, "global_edges": N_NODES * K_NN * n_gpus,
@@ -309,7 +313,7 @@ def run_ours(args):
     from flash_eq.cuda import _lib, block_diagonal_cuda
 
     lib = _lib.load()
-    wl = make_workload(SEED + rank, dev)
+    wl = make_workload(SEED + rank, dev, args.nodes)
     layer, basis = build_modules(dev)
     src, dst, x, coords = wl["src"], wl["dst"], wl["x_d"], wl["coords_d"]
     E = src.numel()
@@ -367,7 +371,7 @@ def run_ours(args):
     fp32_peak = 148 * 128 * 2 * sm_mhz * 1e6 / 1e12       # FMA lanes x 2 flop x clock (nominal)
 
     # --- end to end through the public API from pinned host buffers
-    e2e = run_e2e(args, wl, layer, basis, dev, pg, world)
+    e2e = run_e2e(args, wl, layer, basis, dev, pg, world) if args.e2e_steps > 0 else None
 
     result = None
     if rank == 0:
@@ -375,7 +379,7 @@ def run_ours(args):
             "metric": "edges/sec (fwd, device-timed)", "value": value, "unit": "edges/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": config_block(world),
+            "config": config_block(world, args.nodes),
             "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": hbm_peak, "unit": "GB/s",
                          "frac": achieved_gbs / hbm_peak, "traffic": None,
                          "kernel": "block-diagonal radial mix (binning+sort+relayout+mix), timed alone",
@@ -389,7 +393,7 @@ def run_ours(args):
             "e2e": e2e,
             "gpu_launches": int(launches),
         }
-        if world == 1 and not args.no_cpu_baseline:
+        if world == 1 and not args.no_cpu_baseline and args.nodes == N_NODES:
             try:
                 sample, threads = pick_cpu_sample(3.0)
                 cstep, n, threads = cpu_reference_setup(sample)
@@ -426,7 +430,7 @@ def run_e2e(args, wl, layer, basis, dev, pg, world):
             y = layer(P, Q, x[s], v.norm(dim=-1))
         out_h.copy_(y, non_blocking=True)
 
-    steps = max(1, min(args.steps, 5))
+    steps = args.e2e_steps
     step()
     barrier(pg)
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -448,6 +452,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--nodes", type=int, default=N_NODES,
+                    help="graph size (default: the config-2 size); smaller values only for profiling captures")
+    ap.add_argument("--e2e-steps", type=int, default=3)
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)

@@ -238,6 +238,8 @@ def segment_pool(rows, perm, offsets, num_nodes, reduce="sum", weights=None):
     rows = _f32(rows, "edge_features")
     E = rows.shape[0]
     L = rows[0].numel() if E > 0 else int(torch.tensor(rows.shape[1:]).prod())
+    if E == 0:   # every segment empty: sum, mean and max all give 0 (pooling.py:21-57)
+        return torch.zeros((num_nodes,) + tuple(rows.shape[1:]), dtype=torch.float32, device=rows.device)
     out = torch.empty((num_nodes,) + tuple(rows.shape[1:]), dtype=torch.float32, device=rows.device)
     H = 0
     wptr = None
@@ -258,6 +260,8 @@ def attn_pool(qk, v, src, distances, perm, offsets, num_nodes, num_heads, scale,
     qk, v = _f32(qk, "QK"), _f32(v, "V")
     N, c2, d = qk.shape
     E, c_v, d_v = v.shape
+    if E == 0:
+        return torch.zeros(num_nodes, c_v, d_v, dtype=torch.float32, device=qk.device)
     out = torch.empty(num_nodes, c_v, d_v, dtype=torch.float32, device=qk.device)
     a = _lib.FeqAttnArgs()
     a.qk, a.v = qk.data_ptr(), v.data_ptr()
