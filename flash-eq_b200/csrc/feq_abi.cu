@@ -48,6 +48,8 @@ void record_cuda_error(cudaError_t err) {
     g_last_error = std::string(cudaGetErrorName(err)) + ": " + cudaGetErrorString(err);
 }
 
+void record_error_text(const char *msg) { g_last_error = msg; }
+
 int build_repr_layout(const int32_t *lv, int32_t n, ReprLayout *L) {
     if (!lv || n < 1) return FEQ_ERR_INVALID_ARGUMENT;
     if (n > kMaxIrreps) return FEQ_ERR_UNSUPPORTED;

@@ -123,6 +123,30 @@ int feq_block_diagonal_fwd(const float *features, const float *radial_table,
                            int32_t log_bins, float *output, void *workspace,
                            size_t workspace_bytes, feq_stream_t stream);
 
+/* Same operation as feq_block_diagonal_fwd for callers that cannot allocate device
+ * memory: code running where cudaMalloc is unavailable or not allowed (a host
+ * framework that owns every allocation, a plugin without an allocator handle), or
+ * that must not allocate while it runs.  No counterpart in the reference.
+ *   - The scratch is a fixed array of FEQ_NOALLOC_SCRATCH_BYTES in the library's
+ *     device memory (every GPU that loads the library holds it until exit); inputs
+ *     and the output are still the caller's.  A problem whose scratch would exceed
+ *     it returns FEQ_ERR_WORKSPACE and feq_last_error() gives the sizes.
+ *   - The first call on a device looks up the array's device address on that device
+ *     (with that device current); make that first call before any stream capture.
+ *   - All calls share the one array and it keeps the previous call's contents (no
+ *     part needs to start at zero: each call writes every region before reading it).
+ *     Calls whose GPU work overlaps in time race on it: serialise them (one stream,
+ *     or events between streams).
+ *   - Allocates nothing: no cudaMalloc / cudaFree and no allocating library call. */
+#define FEQ_NOALLOC_SCRATCH_BYTES ((size_t)32 << 20)
+int feq_block_diagonal_fwd_noalloc(const float *features, const float *radial_table,
+                                   const float *distances, int64_t num_edges, int32_t c_in,
+                                   int32_t c_out, const int32_t *lvals_in, int32_t n_lvals_in,
+                                   const int32_t *lvals_out, int32_t n_lvals_out,
+                                   float sh_scale, float bin_param1, float bin_param2,
+                                   int32_t num_bins, int32_t log_bins, float *output,
+                                   feq_stream_t stream);
+
 /* ---------------------------------------------------------------------------
  * Fused edgewise linear: out = Q . Lambda(r) . P^T . f.
  * Replaces EquivariantEdgewiseLinear.forward (flash_eq/layers/linear.py:100-160):
