@@ -315,6 +315,7 @@ def run_ours(args):
     lib = _lib.load()
     wl = make_workload(SEED + rank, dev, args.nodes)
     layer, basis = build_modules(dev)
+    layer.mix_precision = args.mix
     src, dst, x, coords = wl["src"], wl["dst"], wl["x_d"], wl["coords_d"]
     E = src.numel()
     vec = coords[dst] - coords[src]
@@ -455,6 +456,8 @@ def main():
     ap.add_argument("--nodes", type=int, default=N_NODES,
                     help="graph size (default: the config-2 size); smaller values only for profiling captures")
     ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--mix", choices=["fp32", "bf16x3", "bf16"], default="fp32",
+                    help="radial-mix arithmetic: fp32 CUDA cores, bf16x3 / bf16 tensor cores")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)

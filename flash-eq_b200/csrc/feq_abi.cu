@@ -9,6 +9,8 @@
 #include <atomic>
 #include <string>
 
+#include <cuda_bf16.h>
+
 #include "feq_internal.cuh"
 
 namespace feq {
@@ -20,9 +22,9 @@ int launch_rotate_in(const float *x, const int64_t *src, int64_t nsrc, const flo
                      float *g, int32_t *status, cudaStream_t s);
 int launch_rotate_out(const float *h, const float *dirs, const float *Q, int64_t E, int C,
                       const ReprLayout &L, float *out, cudaStream_t s);
-int64_t mix_max_tiles(int64_t E, int nb);
+int64_t mix_max_tiles(int64_t E, int nb, int te);
 int launch_relayout(const float *T, float *Wt, int nb1, int Cin, int Cout, const MixLayout &M, cudaStream_t s);
-int launch_build_tiles(const int64_t *offsets, int nb, int4 *tiles, int *num_tiles, cudaStream_t s);
+int launch_build_tiles(const int64_t *offsets, int nb, int te, int4 *tiles, int *num_tiles, cudaStream_t s);
 int launch_mix(const float *g, const float *Wt, const float *dist, const int64_t *perm, const int4 *tiles,
                const int *num_tiles, int64_t max_tiles, int64_t E, int Cin, int Cout, int din, int dout,
                const MixLayout &M, Binning bins, float sh_scale, float *h, cudaStream_t s);
@@ -38,6 +40,22 @@ int launch_segment_softmax(const float *logits, int64_t N, int H, const int64_t 
 int launch_segment_pool(const float *rows, int64_t L, const float *w, int H, const int64_t *perm,
                         const int64_t *offsets, int64_t N, int reduce, float *out, cudaStream_t s);
 int launch_attn_pool(const FeqAttnArgs &a, cudaStream_t s);
+
+// tensor-core path (feq_tcmix.cu, feq_rotate.cu)
+int launch_tc_relayout_b(const float *T, __nv_bfloat16 *Bhi, __nv_bfloat16 *Blo, int nb1, int Cin, int Cout,
+                         int wdim, const TcGeom &G, int64_t total, cudaStream_t s);
+int launch_tc_mix(int split, const __nv_bfloat16 *A, const __nv_bfloat16 *A2, int64_t a_rows, int a_cols,
+                  const __nv_bfloat16 *Bm, const __nv_bfloat16 *Bm2, int64_t b_rows, const TcBlockGeom &B,
+                  int a_col0, int n_valid, int h_ld, int h_col0, const int4 *tiles, const int *num_tiles,
+                  int64_t max_tiles, const float *tval, float *H, int32_t *status, cudaStream_t s);
+int launch_rotate_in_tc(const float *x, const int64_t *src, int64_t nsrc, const float *edge_add, const float *dirs,
+                        const float *P, const float *dist, const int64_t *perm, int64_t E, int C,
+                        const ReprLayout &L, const TcPosMap &M, int k_total, Binning bins, float sh_scale,
+                        bool split, __nv_bfloat16 *A_hi, __nv_bfloat16 *A_lo, float *tval, int32_t *status,
+                        cudaStream_t s);
+int launch_rotate_out_tc(const float *H, int h_ld, const float *dirs, const float *Q, const float *dist,
+                         const int64_t *perm, int64_t E, int C, const ReprLayout &L, const TcPosMap &M,
+                         float sh_scale, float *out, cudaStream_t s);
 
 static thread_local std::string g_last_error;
 static std::atomic<long long> g_launches{0};
@@ -177,7 +195,7 @@ static void carve_mix(WsCarver &w, int64_t E, int nb, const MixLayout &M, MixPla
     p.keys = (int32_t *)w.take(sizeof(int32_t) * E1);
     p.perm = (int64_t *)w.take(sizeof(int64_t) * E1);
     p.offsets = (int64_t *)w.take(sizeof(int64_t) * (nb + 1));
-    p.max_tiles = mix_max_tiles(E, nb);
+    p.max_tiles = mix_max_tiles(E, nb, 0);
     p.tiles = (int4 *)w.take(sizeof(int4) * p.max_tiles);
     p.num_tiles = (int *)w.take(sizeof(int) * 4);
     p.sort_ws_bytes = edge_sort_workspace(E, nb);
@@ -192,7 +210,7 @@ static int run_mix(const MixPlan &p, const float *g, const float *table, const f
     if ((rc = launch_edge_sort<int32_t>(p.keys, E, bins.num_bins, p.perm, p.offsets, nullptr, p.sort_ws,
                                         p.sort_ws_bytes, s)) != FEQ_OK)
         return rc;
-    if ((rc = launch_build_tiles(p.offsets, bins.num_bins, p.tiles, p.num_tiles, s)) != FEQ_OK) return rc;
+    if ((rc = launch_build_tiles(p.offsets, bins.num_bins, 0, p.tiles, p.num_tiles, s)) != FEQ_OK) return rc;
     if ((rc = launch_relayout(table, p.Wt, bins.num_bins + 1, Cin, Cout, M, s)) != FEQ_OK) return rc;
     return launch_mix(g, p.Wt, dist, p.perm, p.tiles, p.num_tiles, p.max_tiles, E, Cin, Cout, din, dout, M,
                       bins, sh_scale, h, s);
@@ -200,6 +218,149 @@ static int run_mix(const MixPlan &p, const float *g, const float *table, const f
 
 static bool mix_args_ok(int64_t E, int Cin, int Cout, int nb) {
     return E >= 0 && E < 0x7fffffffll && Cin >= 1 && Cout >= 1 && nb >= 1 && nb < (1 << 24);
+}
+
+// ---------------------------------------------------------------------------
+// Tensor-core plan: GEMM geometry per m-block and the row maps of A and H.
+// ---------------------------------------------------------------------------
+struct TcPlan {
+    TcGeom G;
+    int koff[kMaxBlocks], noff[kMaxBlocks], nvalid[kMaxBlocks];
+    int k_total, n_total;
+    int64_t b_total;
+    TcPosMap in_map, out_map;
+};
+
+// Offset of block m in m-first order when every irrep with l >= m contributes
+// (wigner.py:243-272), independent of whether the block takes part in the mix.
+static void mfirst_offsets(const ReprLayout &L, int *off) {
+    int o = 0;
+    for (int m = 0; m <= kMaxL; m++) {
+        off[m] = o;
+        int n = 0;
+        for (int r = 0; r < L.n_irreps; r++) n += L.irrep_l[r] >= m;
+        o += (m == 0 ? 1 : 2) * n;
+    }
+}
+
+static void fill_posmap(const ReprLayout &L, const TcPlan &T, const MixLayout &M, bool input, TcPosMap *map) {
+    int off[kMaxL + 1];
+    mfirst_offsets(L, off);
+    memset(map, 0, sizeof(*map));
+    for (int j = 0; j < L.dim; j++) {
+        const int ps = L.perm[j], ir = L.std_irrep[ps], l = L.irrep_l[ir];
+        const int col = ps - L.irrep_off[ir];
+        const int m = col >= l ? col - l : l - col;
+        map->l[j] = (int8_t)l;
+        map->base[j] = -1;
+        if (m < T.G.n_blocks) {
+            const MixBlock &B = M.blk[m];
+            const int mult = m == 0 ? 1 : 2;
+            if (input) {
+                map->base[j] = T.koff[m] + (j - off[m]);
+                map->stride[j] = (int16_t)(mult * B.n_in);
+            } else {
+                map->base[j] = T.noff[m] + (j - off[m]);
+                map->stride[j] = (int16_t)(mult * B.n_out);
+            }
+        }
+    }
+}
+
+static int build_tc_plan(const MixLayout &M, const ReprLayout &Li, const ReprLayout &Lo, int Cin, int Cout, int nb,
+                         TcPlan *T) {
+    memset(T, 0, sizeof(*T));
+    int kt = 0, nt = 0, nblk = 0;
+    int64_t boff = 0;
+    for (int m = 0; m < M.n_blocks; m++) {
+        const MixBlock &B = M.blk[m];
+        if (B.n_in == 0 || B.n_out == 0) break;   // emptiness is monotone in m
+        const int mult = m == 0 ? 1 : 2;
+        TcBlockGeom &g = T->G.g[m];
+        g.mult = mult;
+        g.n_in = B.n_in;
+        g.n_out = B.n_out;
+        g.w_off = B.w_off;
+        const int K = Cin * mult * B.n_in, N = Cout * mult * B.n_out;
+        g.kpad = (K + 63) / 64 * 64;
+        g.npad = (N + 127) / 128 * 128;
+        g.boff = boff;
+        T->koff[m] = kt;
+        T->noff[m] = nt;
+        T->nvalid[m] = N;
+        kt += g.kpad;
+        nt += N;
+        boff += (int64_t)(nb + 1) * g.npad * g.kpad;
+        nblk++;
+    }
+    T->G.n_blocks = nblk;
+    T->k_total = kt;
+    T->n_total = nt;
+    T->b_total = boff;
+    if ((int64_t)kt > 65535 || (int64_t)nt > (1 << 20)) return FEQ_ERR_UNSUPPORTED;
+    fill_posmap(Li, *T, M, true, &T->in_map);
+    fill_posmap(Lo, *T, M, false, &T->out_map);
+    return FEQ_OK;
+}
+
+struct TcBuffers {
+    __nv_bfloat16 *A_hi, *A_lo, *B_hi, *B_lo;
+    float *H, *tval;
+    int32_t *keys;
+    int64_t *perm, *offsets;
+    int4 *tiles;
+    int *num_tiles;
+    void *sort_ws;
+    size_t sort_ws_bytes;
+    int64_t max_tiles;
+};
+
+static void carve_tc(WsCarver &w, int64_t E, int nb, const TcPlan &T, bool split, TcBuffers &b) {
+    const int64_t E1 = std::max<int64_t>(E, 1);
+    b.A_hi = (__nv_bfloat16 *)w.take(2 * (size_t)E1 * T.k_total);
+    b.A_lo = split ? (__nv_bfloat16 *)w.take(2 * (size_t)E1 * T.k_total) : nullptr;
+    b.B_hi = (__nv_bfloat16 *)w.take(2 * (size_t)T.b_total);
+    b.B_lo = split ? (__nv_bfloat16 *)w.take(2 * (size_t)T.b_total) : nullptr;
+    b.H = (float *)w.take(4 * (size_t)E1 * T.n_total);
+    b.tval = (float *)w.take(4 * (size_t)E1);
+    b.keys = (int32_t *)w.take(4 * (size_t)E1);
+    b.perm = (int64_t *)w.take(8 * (size_t)E1);
+    b.offsets = (int64_t *)w.take(8 * (size_t)(nb + 1));
+    b.max_tiles = mix_max_tiles(E, nb, 128);
+    b.tiles = (int4 *)w.take(sizeof(int4) * b.max_tiles);
+    b.num_tiles = (int *)w.take(16);
+    b.sort_ws_bytes = edge_sort_workspace(E, nb);
+    b.sort_ws = w.take(b.sort_ws_bytes);
+}
+
+static int run_edgewise_tc(const FeqEdgewiseArgs *a, const MixLayout &M, const ReprLayout &Li,
+                           const ReprLayout &Lo, const TcPlan &T, const TcBuffers &b, cudaStream_t s) {
+    const int64_t E = a->num_edges;
+    const bool split = a->mix_mode == FEQ_MIX_BF16X3;
+    Binning bins{a->bin_param1, a->bin_param2, a->num_bins, a->log_bins ? 1 : 0};
+    int rc;
+    if ((rc = launch_binning(a->distances, E, bins, b.keys, nullptr, s)) != FEQ_OK) return rc;
+    if ((rc = launch_edge_sort<int32_t>(b.keys, E, a->num_bins, b.perm, b.offsets, nullptr, b.sort_ws,
+                                        b.sort_ws_bytes, s)) != FEQ_OK)
+        return rc;
+    if ((rc = launch_build_tiles(b.offsets, a->num_bins, 128, b.tiles, b.num_tiles, s)) != FEQ_OK) return rc;
+    if ((rc = launch_tc_relayout_b(a->radial_table, b.B_hi, b.B_lo, a->num_bins + 1, a->c_in, a->c_out, M.wdim, T.G,
+                                   T.b_total, s)) != FEQ_OK)
+        return rc;
+    if ((rc = launch_rotate_in_tc(a->x, a->src, a->num_src_rows, a->edge_add, a->directions, a->P_in, a->distances,
+                                  b.perm, E, a->c_in, Li, T.in_map, T.k_total, bins, a->sh_scale, split, b.A_hi,
+                                  b.A_lo, b.tval, a->status, s)) != FEQ_OK)
+        return rc;
+    for (int m = 0; m < T.G.n_blocks; m++) {
+        const TcBlockGeom &g = T.G.g[m];
+        const int64_t b_rows = (int64_t)(a->num_bins + 1) * g.npad;
+        if ((rc = launch_tc_mix(split ? 3 : 1, b.A_hi, b.A_lo, E, T.k_total, b.B_hi + g.boff,
+                                split ? b.B_lo + g.boff : nullptr, b_rows, g, T.koff[m], T.nvalid[m], T.n_total,
+                                T.noff[m], b.tiles, b.num_tiles, b.max_tiles, b.tval, b.H, a->status, s)) != FEQ_OK)
+            return rc;
+    }
+    return launch_rotate_out_tc(b.H, T.n_total, a->directions, a->Q_out, a->distances, b.perm, E, a->c_out, Lo,
+                                T.out_map, a->sh_scale, a->out, s);
 }
 
 }  // namespace feq
@@ -312,6 +473,14 @@ size_t feq_edgewise_workspace_bytes(const FeqEdgewiseArgs *a) {
         return 0;
     if (build_repr_layout(a->lvals_in, a->n_lvals_in, &Li) != FEQ_OK) return 0;
     if (build_repr_layout(a->lvals_out, a->n_lvals_out, &Lo) != FEQ_OK) return 0;
+    if (a->mix_mode == FEQ_MIX_BF16 || a->mix_mode == FEQ_MIX_BF16X3) {
+        static thread_local TcPlan T;
+        if (build_tc_plan(M, Li, Lo, a->c_in, a->c_out, a->num_bins, &T) != FEQ_OK) return 0;
+        WsCarver w{nullptr, 0, 0};
+        TcBuffers b;
+        carve_tc(w, a->num_edges, a->num_bins, T, a->mix_mode == FEQ_MIX_BF16X3, b);
+        return w.used + 256;
+    }
     const int64_t E1 = std::max<int64_t>(a->num_edges, 1);
     WsCarver w{nullptr, 0, 0};
     w.take(sizeof(float) * (size_t)E1 * a->c_in * Li.dim);
@@ -334,7 +503,17 @@ int feq_edgewise_fwd(const FeqEdgewiseArgs *a, void *workspace, size_t workspace
     if (!a->x || !a->distances || !a->radial_table || !a->out) return FEQ_ERR_INVALID_ARGUMENT;
     if (!a->directions && (!a->P_in || !a->Q_out)) return FEQ_ERR_INVALID_ARGUMENT;
     if (a->src && a->num_src_rows < 1) return FEQ_ERR_INVALID_ARGUMENT;
+    if (a->mix_mode < FEQ_MIX_FP32 || a->mix_mode > FEQ_MIX_BF16X3) return FEQ_ERR_INVALID_ARGUMENT;
     cudaStream_t s = (cudaStream_t)stream;
+    if (a->mix_mode != FEQ_MIX_FP32) {
+        static thread_local TcPlan T;
+        if ((rc = build_tc_plan(M, Li, Lo, a->c_in, a->c_out, a->num_bins, &T)) != FEQ_OK) return rc;
+        WsCarver w{(char *)workspace, 0, workspace_bytes};
+        TcBuffers b;
+        carve_tc(w, E, a->num_bins, T, a->mix_mode == FEQ_MIX_BF16X3, b);
+        if (!workspace || w.used > workspace_bytes) return FEQ_ERR_WORKSPACE;
+        return run_edgewise_tc(a, M, Li, Lo, T, b, s);
+    }
     WsCarver w{(char *)workspace, 0, workspace_bytes};
     float *g = (float *)w.take(sizeof(float) * (size_t)E * a->c_in * Li.dim);
     float *h = (float *)w.take(sizeof(float) * (size_t)E * a->c_out * Lo.dim);

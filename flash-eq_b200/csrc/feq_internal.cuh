@@ -57,6 +57,27 @@ struct MixLayout {
     MixBlock blk[kMaxBlocks];
 };
 
+// Tensor-core path: where component j (m-first order) of channel c lives in a GEMM
+// row (A for the input repr, H for the output repr): base[j] + c * stride[j], or
+// base[j] = -1 when j belongs to a block that does not take part in the mix; l[j] is
+// the degree of j (solid-harmonic scaling).
+struct TcPosMap {
+    int32_t base[kMaxDim];
+    int16_t stride[kMaxDim];
+    int8_t l[kMaxDim];
+};
+
+// Tensor-core radial mix: per m-block GEMM geometry.  B (the re-laid table) holds, per
+// block, (num_bins + 1) matrices of npad x kpad bf16 (K-major) starting at element boff.
+struct TcBlockGeom {
+    int mult, n_in, n_out, w_off, kpad, npad;
+    int64_t boff;
+};
+struct TcGeom {
+    int n_blocks;                    // non-empty blocks (a prefix of m = 0..mmax)
+    TcBlockGeom g[kMaxBlocks];
+};
+
 struct Binning {
     float p1, p2;
     int num_bins;

@@ -86,7 +86,12 @@ mix_kernel(const float *__restrict__ g, const float *__restrict__ Wt, const floa
     __shared__ float t_s[kTileE];
     __shared__ float sp_s[kTileE][kMaxL + 1];
     __shared__ int64_t eid_s[kTileE];
+    __shared__ int8_t lin_s[kMaxIrreps], lout_s[kMaxIrreps];   // degrees, staged off the param bank
     float *g_s = smem;   // [ci_chunk * n_in][kTileE][mult]
+    if (threadIdx.x < kMaxIrreps) {
+        lin_s[threadIdx.x] = B.l_in[threadIdx.x];
+        lout_s[threadIdx.x] = B.l_out[threadIdx.x];
+    }
 
     const int lmax = max(M.lmax_in, M.lmax_out);
     if (threadIdx.x < kTileE) {
@@ -131,7 +136,7 @@ mix_kernel(const float *__restrict__ g, const float *__restrict__ Wt, const floa
             const int64_t e = eid_s[k];
             if (e >= 0) {
                 v = __ldg(g + (e * Cin + c0 + cl) * (int64_t)din + B.in_off + mult * i + comp);
-                v *= sp_s[k][B.l_in[i]];
+                v *= sp_s[k][lin_s[i]];
             }
             g_s[idx] = v;
         }
@@ -158,10 +163,17 @@ mix_kernel(const float *__restrict__ g, const float *__restrict__ Wt, const floa
                 __syncthreads();
             }
             if (active) {
-                for (int row = 0; row < cn * n_in; row++) {
-                    const int64_t woff = (int64_t)((c0 * n_in) + row) * wstride + 2 * u;
-                    const float2 w0 = __ldg(reinterpret_cast<const float2 *>(W0 + woff));
-                    const float2 w1 = __ldg(reinterpret_cast<const float2 *>(W1 + woff));
+                const int rows = cn * n_in;
+                const float2 *wp0 = reinterpret_cast<const float2 *>(W0 + (int64_t)(c0 * n_in) * wstride + 2 * u);
+                const float2 *wp1 = reinterpret_cast<const float2 *>(W1 + (int64_t)(c0 * n_in) * wstride + 2 * u);
+                const int wstep = wstride / 2;   // float2 per (ci, i) row
+                float2 nw0 = __ldg(wp0), nw1 = __ldg(wp1);
+                for (int row = 0; row < rows; row++) {
+                    const float2 w0 = nw0, w1 = nw1;
+                    if (row + 1 < rows) {   // prefetch the next row's weights (hides L2 latency)
+                        nw0 = __ldg(wp0 + (int64_t)(row + 1) * wstep);
+                        nw1 = __ldg(wp1 + (int64_t)(row + 1) * wstep);
+                    }
                     const float dx = w1.x - w0.x, dy = w1.y - w0.y;
                     if (kCplx) {
                         const float4 *gr = reinterpret_cast<const float4 *>(g_s + row * kTileE * 2);
@@ -201,7 +213,7 @@ mix_kernel(const float *__restrict__ g, const float *__restrict__ Wt, const floa
         if (active) {
             if (kCplx) {
                 const int co = u / n_out, o = u - co * n_out;
-                const int lo_ = B.l_out[o];
+                const int lo_ = lout_s[o];
 #pragma unroll
                 for (int k = 0; k < kTileE; k++) {
                     if (k < len) {
@@ -217,7 +229,7 @@ mix_kernel(const float *__restrict__ g, const float *__restrict__ Wt, const floa
                 const int co0 = q0 / n_out, o0 = q0 - co0 * n_out;
                 const int co1 = q1 / n_out, o1 = q1 - co1 * n_out;
                 const bool has1 = q1 < Cout * n_out;
-                const int l0 = B.l_out[o0], l1 = has1 ? B.l_out[o1] : 0;
+                const int l0 = lout_s[o0], l1 = has1 ? lout_s[o1] : 0;
 #pragma unroll
                 for (int k = 0; k < kTileE; k++) {
                     if (k < len) {
@@ -246,7 +258,7 @@ __global__ void zero_blocks_kernel(float *__restrict__ h, int64_t E, int Cout, i
 }
 
 // Tile list: for each bin, ceil(count / kTileE) tiles (start, len, bin).
-__global__ void build_tiles_kernel(const int64_t *__restrict__ offsets, int nb, int4 *__restrict__ tiles,
+__global__ void build_tiles_kernel(const int64_t *__restrict__ offsets, int nb, int te, int4 *__restrict__ tiles,
                                    int *__restrict__ num_tiles) {
     __shared__ int partial[1024];
     const int T = blockDim.x;
@@ -255,7 +267,7 @@ __global__ void build_tiles_kernel(const int64_t *__restrict__ offsets, int nb, 
     int cnt = 0;
     for (int b = b0; b < b1; b++) {
         const int64_t c = offsets[b + 1] - offsets[b];
-        cnt += (int)((c + kTileE - 1) / kTileE);
+        cnt += (int)((c + te - 1) / te);
     }
     partial[threadIdx.x] = cnt;
     __syncthreads();
@@ -268,8 +280,8 @@ __global__ void build_tiles_kernel(const int64_t *__restrict__ offsets, int nb, 
     int t = partial[threadIdx.x] - cnt;
     for (int b = b0; b < b1; b++) {
         const int64_t s = offsets[b], c = offsets[b + 1] - s;
-        for (int64_t k = 0; k < c; k += kTileE) {
-            tiles[t++] = make_int4((int)(s + k), (int)min64(kTileE, c - k), b, 0);
+        for (int64_t k = 0; k < c; k += te) {
+            tiles[t++] = make_int4((int)(s + k), (int)min64(te, c - k), b, 0);
         }
     }
     if (threadIdx.x == T - 1) *num_tiles = partial[T - 1];
@@ -278,7 +290,7 @@ __global__ void build_tiles_kernel(const int64_t *__restrict__ offsets, int nb, 
 // ---------------------------------------------------------------------------
 // Host
 // ---------------------------------------------------------------------------
-int64_t mix_max_tiles(int64_t E, int nb) { return E / kTileE + nb + 1; }
+int64_t mix_max_tiles(int64_t E, int nb, int te) { return E / (te > 0 ? te : kTileE) + nb + 1; }
 
 int launch_relayout(const float *T, float *Wt, int nb1, int Cin, int Cout, const MixLayout &M,
                     cudaStream_t s) {
@@ -290,8 +302,8 @@ int launch_relayout(const float *T, float *Wt, int nb1, int Cin, int Cout, const
     return FEQ_OK;
 }
 
-int launch_build_tiles(const int64_t *offsets, int nb, int4 *tiles, int *num_tiles, cudaStream_t s) {
-    build_tiles_kernel<<<1, 1024, 0, s>>>(offsets, nb, tiles, num_tiles);
+int launch_build_tiles(const int64_t *offsets, int nb, int te, int4 *tiles, int *num_tiles, cudaStream_t s) {
+    build_tiles_kernel<<<1, 1024, 0, s>>>(offsets, nb, te > 0 ? te : kTileE, tiles, num_tiles);
     FEQ_LAUNCH_CHECK();
     return FEQ_OK;
 }

@@ -15,6 +15,7 @@
 // steps (normalise with +eps, axis (-d_y, d_x) / (|.| + eps), theta = acos of the
 // clamped d_z) so degenerate inputs land where the reference does: d = 0 and
 // d = -e_z give the identity, as matrix_exp of a zero generator does.
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
 #include "feq_internal.cuh"
@@ -103,12 +104,25 @@ __device__ void build_dblocks(const ReprLayout &L, int nedges, const EdgeTrig *t
     __syncthreads();
 }
 
+// Kernel parameters live in the constant bank: indexing them with a per-thread index
+// serialises a warp's reads.  Each kernel therefore copies its layout struct into
+// shared memory once and reads it from there.
+static_assert(sizeof(ReprLayout) % 4 == 0, "ReprLayout is copied as 32-bit words");
+__device__ __forceinline__ void stage_layout(const ReprLayout &src, ReprLayout &dst) {
+    const int *s = reinterpret_cast<const int *>(&src);
+    int *d = reinterpret_cast<int *>(&dst);
+    for (int i = threadIdx.x; i < (int)(sizeof(ReprLayout) / 4); i += blockDim.x) d[i] = s[i];
+    __syncthreads();
+}
+
 // ---------------------------------------------------------------------------
 // Dense basis output (API compatibility with WignerDBasis / rot_to_ez).
 // ---------------------------------------------------------------------------
-__global__ void basis_kernel(const float *__restrict__ dirs, int64_t E, const __grid_constant__ ReprLayout L,
+__global__ void basis_kernel(const float *__restrict__ dirs, int64_t E, const __grid_constant__ ReprLayout Lp,
                              int layout, int epb, float *__restrict__ out) {
     extern __shared__ float smem[];
+    __shared__ ReprLayout L;
+    stage_layout(Lp, L);
     EdgeTrig *trig_s = reinterpret_cast<EdgeTrig *>(smem);
     float *m_s = reinterpret_cast<float *>(trig_s + epb);
     float *d_s = m_s + epb * L.dblock_floats;
@@ -151,9 +165,11 @@ template <bool kDense, bool kGather>
 __global__ void rotate_in_kernel(const float *__restrict__ x, const int64_t *__restrict__ src,
                                  int64_t nsrc, const float *__restrict__ edge_add,
                                  const float *__restrict__ dirs, const float *__restrict__ P,
-                                 int64_t E, int C, const __grid_constant__ ReprLayout L, int epb,
+                                 int64_t E, int C, const __grid_constant__ ReprLayout Lp, int epb,
                                  float *__restrict__ g, int32_t *status) {
     extern __shared__ float smem[];
+    __shared__ ReprLayout L;
+    stage_layout(Lp, L);
     const int d = L.dim, row = C * d;
     float *f_s = smem;                                   // epb * row
     float *b_s = f_s + epb * row;                        // basis area
@@ -225,8 +241,10 @@ __global__ void rotate_in_kernel(const float *__restrict__ x, const int64_t *__r
 template <bool kDense>
 __global__ void rotate_out_kernel(const float *__restrict__ h, const float *__restrict__ dirs,
                                   const float *__restrict__ Q, int64_t E, int C,
-                                  const __grid_constant__ ReprLayout L, int epb, float *__restrict__ out) {
+                                  const __grid_constant__ ReprLayout Lp, int epb, float *__restrict__ out) {
     extern __shared__ float smem[];
+    __shared__ ReprLayout L;
+    stage_layout(Lp, L);
     const int d = L.dim, row = C * d;
     float *h_s = smem;
     float *b_s = h_s + epb * row;
@@ -342,6 +360,275 @@ int launch_rotate_out(const float *h, const float *dirs, const float *Q, int64_t
     } else {
         FEQ_CUDA_TRY(cudaFuncSetAttribute(rotate_out_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
         rotate_out_kernel<false><<<(unsigned)grid, 256, smem, s>>>(h, dirs, Q, E, C, L, epb, out);
+    }
+    FEQ_LAUNCH_CHECK();
+    return FEQ_OK;
+}
+
+}  // namespace feq
+
+// ===========================================================================
+// Tensor-core path: producer of the GEMM's A rows and consumer of its output rows.
+// Rows are in bin-sorted order p; edge e = perm[p].
+// ===========================================================================
+namespace feq {
+
+static_assert(sizeof(TcPosMap) % 4 == 0, "TcPosMap is copied as 32-bit words");
+
+__device__ __forceinline__ void stage_posmap(const TcPosMap &src, TcPosMap &dst) {
+    const int *s = reinterpret_cast<const int *>(&src);
+    int *d = reinterpret_cast<int *>(&dst);
+    for (int i = threadIdx.x; i < (int)(sizeof(TcPosMap) / 4); i += blockDim.x) d[i] = s[i];
+}
+
+// A[p][map.base[j] + c * map.stride[j]] = (g[e][c][j]) * s_e^l(j), as bf16 (hi [, lo]).
+// g = f . P with f = x[src[e]] (+ edge_add[e]) or x[e].  Also tval[p] = t_e.
+template <bool kDense, bool kGather, bool kSplit>
+__global__ void rotate_in_tc_kernel(const float *__restrict__ x, const int64_t *__restrict__ src, int64_t nsrc,
+                                    const float *__restrict__ edge_add, const float *__restrict__ dirs,
+                                    const float *__restrict__ P, const float *__restrict__ dist,
+                                    const int64_t *__restrict__ perm, int64_t E, int C,
+                                    const __grid_constant__ ReprLayout Lp, const __grid_constant__ TcPosMap Mp,
+                                    int k_total, Binning bins, float sh_scale, int epb,
+                                    __nv_bfloat16 *__restrict__ A_hi, __nv_bfloat16 *__restrict__ A_lo,
+                                    float *__restrict__ tval, int32_t *status) {
+    extern __shared__ float smem[];
+    __shared__ ReprLayout L;
+    __shared__ TcPosMap Mm;
+    __shared__ float sp_s[16][kMaxL + 1];
+    __shared__ int64_t eid_s[16];
+    stage_posmap(Mp, Mm);
+    stage_layout(Lp, L);
+    const int d = L.dim, row = C * d;
+    const int64_t p0 = (int64_t)blockIdx.x * epb;
+    const int ne = (int)min64(epb, E - p0);
+    float *f_s = smem;                          // epb * row
+    float *a_s = f_s + epb * row;               // epb * k_total (fp32 staging of the A rows)
+    float *b_s = a_s + epb * k_total;           // basis area
+    if (threadIdx.x < ne) {
+        const int64_t e = perm[p0 + threadIdx.x];
+        eid_s[threadIdx.x] = e;
+        const float dd = dist[e];
+        int lo;
+        float t;
+        bin_of(dd, bins, lo, t);
+        tval[p0 + threadIdx.x] = t;
+        const float s = dd / (dd + sh_scale);
+        for (int l = 0; l <= L.lmax; l++) sp_s[threadIdx.x][l] = ipowf(s, l);
+    }
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < ne * row; idx += blockDim.x) {
+        const int k = idx / row, r = idx - k * row;
+        const int64_t e = eid_s[k];
+        float v;
+        if (kGather) {
+            const int64_t s = src[e];
+            if (s < 0 || s >= nsrc) {
+                set_status(status, 1);
+                v = 0.0f;
+            } else {
+                v = __ldg(x + s * row + r);
+            }
+        } else {
+            v = __ldg(x + e * row + r);
+        }
+        if (edge_add) v += __ldg(edge_add + e * row + r);
+        f_s[idx] = v;
+    }
+    for (int idx = threadIdx.x; idx < ne * k_total; idx += blockDim.x) a_s[idx] = 0.0f;   // K padding
+    const float *D_s;
+    if (kDense) {
+        const int dd2 = d * d;
+        for (int idx = threadIdx.x; idx < ne * dd2; idx += blockDim.x) {
+            const int k = idx / dd2;
+            b_s[idx] = __ldg(P + eid_s[k] * dd2 + (idx - k * dd2));
+        }
+        __syncthreads();
+        D_s = b_s;
+    } else {
+        EdgeTrig *trig_s = reinterpret_cast<EdgeTrig *>(b_s);
+        float *m_s = reinterpret_cast<float *>(trig_s + epb);
+        float *d_s = m_s + epb * L.dblock_floats;
+        if (threadIdx.x < ne) {
+            const float *v = dirs + eid_s[threadIdx.x] * 3;
+            edge_trig(v[0], v[1], v[2], L.lmax, trig_s[threadIdx.x]);
+        }
+        __syncthreads();
+        build_dblocks(L, ne, trig_s, m_s, d_s);
+        D_s = d_s;
+    }
+    for (int idx = threadIdx.x; idx < ne * row; idx += blockDim.x) {
+        const int k = idx / row, r = idx - k * row;
+        const int c = r / d, j = r - c * d;
+        const int base = Mm.base[j];
+        if (base < 0) continue;                 // component not used by any non-empty block
+        const float *fr = f_s + k * row + c * d;
+        float acc = 0.0f;
+        if (kDense) {
+            const float *Pe = D_s + k * d * d;
+            for (int q = 0; q < d; q++) acc = fmaf(fr[q], Pe[q * d + j], acc);
+        } else {
+            const int ps = L.perm[j];
+            const int ir = L.std_irrep[ps];
+            const int l = L.irrep_l[ir], n = 2 * l + 1, off = L.irrep_off[ir];
+            const int col = ps - off;
+            const float *De = D_s + k * L.dblock_floats + L.unique_doff[L.irrep_slot[ir]];
+            for (int q = 0; q < n; q++) acc = fmaf(fr[off + q], De[q * n + col], acc);
+        }
+        a_s[k * k_total + base + c * Mm.stride[j]] = acc * sp_s[k][Mm.l[j]];
+    }
+    __syncthreads();
+    // rows out: 8 bf16 (16 B) per store; k_total is a multiple of 64
+    const int per = k_total / 8;
+    for (int idx = threadIdx.x; idx < ne * per; idx += blockDim.x) {
+        const int k = idx / per, q = idx - k * per;
+        const float *v = a_s + k * k_total + q * 8;
+        __align__(16) __nv_bfloat16 hi[8], lo[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            hi[u] = __float2bfloat16_rn(v[u]);
+            lo[u] = __float2bfloat16_rn(v[u] - __bfloat162float(hi[u]));
+        }
+        const int64_t off = (p0 + k) * (int64_t)k_total + q * 8;
+        *reinterpret_cast<uint4 *>(A_hi + off) = *reinterpret_cast<const uint4 *>(hi);
+        if (kSplit) *reinterpret_cast<uint4 *>(A_lo + off) = *reinterpret_cast<const uint4 *>(lo);
+    }
+}
+
+// out[e][c][k] = sum_j h[c][j] Q[e][k][j] with h[c][j] = H[p][map.base[j] + c * map.stride[j]] * s_e^l(j)
+// (0 for components of blocks without input).
+template <bool kDense>
+__global__ void rotate_out_tc_kernel(const float *__restrict__ H, int h_ld, const float *__restrict__ dirs,
+                                     const float *__restrict__ Q, const float *__restrict__ dist,
+                                     const int64_t *__restrict__ perm, int64_t E, int C,
+                                     const __grid_constant__ ReprLayout Lp, const __grid_constant__ TcPosMap Mp,
+                                     float sh_scale, int epb, float *__restrict__ out) {
+    extern __shared__ float smem[];
+    __shared__ ReprLayout L;
+    __shared__ TcPosMap Mm;
+    __shared__ float sp_s[16][kMaxL + 1];
+    __shared__ int64_t eid_s[16];
+    stage_posmap(Mp, Mm);
+    stage_layout(Lp, L);
+    const int d = L.dim, row = C * d;
+    const int64_t p0 = (int64_t)blockIdx.x * epb;
+    const int ne = (int)min64(epb, E - p0);
+    float *h_s = smem;
+    float *b_s = h_s + epb * row;
+    if (threadIdx.x < ne) {
+        const int64_t e = perm[p0 + threadIdx.x];
+        eid_s[threadIdx.x] = e;
+        const float dd = dist[e];
+        const float s = dd / (dd + sh_scale);
+        for (int l = 0; l <= L.lmax; l++) sp_s[threadIdx.x][l] = ipowf(s, l);
+    }
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < ne * row; idx += blockDim.x) {
+        const int k = idx / row, r = idx - k * row;
+        const int c = r / d, j = r - c * d;
+        const int base = Mm.base[j];
+        h_s[idx] = base < 0 ? 0.0f : __ldg(H + (p0 + k) * (int64_t)h_ld + base + c * Mm.stride[j]) * sp_s[k][Mm.l[j]];
+    }
+    const float *D_s;
+    if (kDense) {
+        const int dd2 = d * d;
+        for (int idx = threadIdx.x; idx < ne * dd2; idx += blockDim.x) {
+            const int k = idx / dd2;
+            b_s[idx] = __ldg(Q + eid_s[k] * dd2 + (idx - k * dd2));
+        }
+        __syncthreads();
+        D_s = b_s;
+    } else {
+        EdgeTrig *trig_s = reinterpret_cast<EdgeTrig *>(b_s);
+        float *m_s = reinterpret_cast<float *>(trig_s + epb);
+        float *d_s = m_s + epb * L.dblock_floats;
+        if (threadIdx.x < ne) {
+            const float *v = dirs + eid_s[threadIdx.x] * 3;
+            edge_trig(v[0], v[1], v[2], L.lmax, trig_s[threadIdx.x]);
+        }
+        __syncthreads();
+        build_dblocks(L, ne, trig_s, m_s, d_s);
+        D_s = d_s;
+    }
+    for (int idx = threadIdx.x; idx < ne * row; idx += blockDim.x) {
+        const int k = idx / row, r = idx - k * row;
+        const int c = r / d, kk = r - c * d;
+        const float *hr = h_s + k * row + c * d;
+        float acc = 0.0f;
+        if (kDense) {
+            const float *Qe = D_s + k * d * d + kk * d;
+            for (int j = 0; j < d; j++) acc = fmaf(hr[j], Qe[j], acc);
+        } else {
+            const int ir = L.std_irrep[kk];
+            const int l = L.irrep_l[ir], n = 2 * l + 1, off = L.irrep_off[ir];
+            const float *De = D_s + k * L.dblock_floats + L.unique_doff[L.irrep_slot[ir]] + (kk - off) * n;
+            for (int col = 0; col < n; col++) acc = fmaf(hr[L.inv_perm[off + col]], De[col], acc);
+        }
+        out[eid_s[k] * row + r] = acc;
+    }
+}
+
+constexpr size_t kTcRotSmemBudget = 160 * 1024;
+
+int launch_rotate_in_tc(const float *x, const int64_t *src, int64_t nsrc, const float *edge_add, const float *dirs,
+                        const float *P, const float *dist, const int64_t *perm, int64_t E, int C,
+                        const ReprLayout &L, const TcPosMap &M, int k_total, Binning bins, float sh_scale,
+                        bool split, __nv_bfloat16 *A_hi, __nv_bfloat16 *A_lo, float *tval, int32_t *status,
+                        cudaStream_t s) {
+    if (E == 0) return FEQ_OK;
+    const bool dense = dirs == nullptr;
+    const size_t row = (size_t)C * L.dim;
+    const size_t per = row + k_total + basis_area_floats(L, 1, dense);
+    if (per * 4 > kTcRotSmemBudget) return FEQ_ERR_UNSUPPORTED;
+    const int epb = pick_epb(per, 0, kTcRotSmemBudget, 8);
+    const size_t smem = per * epb * 4;
+    const int64_t grid = (E + epb - 1) / epb;
+#define FEQ_ROT_IN_TC(D, G, S)                                                                              \
+    do {                                                                                                    \
+        FEQ_CUDA_TRY(cudaFuncSetAttribute(rotate_in_tc_kernel<D, G, S>,                                     \
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));         \
+        rotate_in_tc_kernel<D, G, S><<<(unsigned)grid, 256, smem, s>>>(x, src, nsrc, edge_add, dirs, P, dist, \
+                                                                       perm, E, C, L, M, k_total, bins,     \
+                                                                       sh_scale, epb, A_hi, A_lo, tval,     \
+                                                                       status);                             \
+    } while (0)
+    if (dense) {
+        if (src) {
+            if (split) FEQ_ROT_IN_TC(true, true, true); else FEQ_ROT_IN_TC(true, true, false);
+        } else {
+            if (split) FEQ_ROT_IN_TC(true, false, true); else FEQ_ROT_IN_TC(true, false, false);
+        }
+    } else {
+        if (src) {
+            if (split) FEQ_ROT_IN_TC(false, true, true); else FEQ_ROT_IN_TC(false, true, false);
+        } else {
+            if (split) FEQ_ROT_IN_TC(false, false, true); else FEQ_ROT_IN_TC(false, false, false);
+        }
+    }
+#undef FEQ_ROT_IN_TC
+    FEQ_LAUNCH_CHECK();
+    return FEQ_OK;
+}
+
+int launch_rotate_out_tc(const float *H, int h_ld, const float *dirs, const float *Q, const float *dist,
+                         const int64_t *perm, int64_t E, int C, const ReprLayout &L, const TcPosMap &M,
+                         float sh_scale, float *out, cudaStream_t s) {
+    if (E == 0) return FEQ_OK;
+    const bool dense = dirs == nullptr;
+    const size_t row = (size_t)C * L.dim;
+    const size_t per = row + basis_area_floats(L, 1, dense);
+    if (per * 4 > kSmemBudget) return FEQ_ERR_UNSUPPORTED;
+    const int epb = pick_epb(per, 0, kSmemBudget, 8);
+    const size_t smem = per * epb * 4;
+    const int64_t grid = (E + epb - 1) / epb;
+    if (dense) {
+        FEQ_CUDA_TRY(cudaFuncSetAttribute(rotate_out_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        rotate_out_tc_kernel<true><<<(unsigned)grid, 256, smem, s>>>(H, h_ld, dirs, Q, dist, perm, E, C, L, M,
+                                                                     sh_scale, epb, out);
+    } else {
+        FEQ_CUDA_TRY(cudaFuncSetAttribute(rotate_out_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        rotate_out_tc_kernel<false><<<(unsigned)grid, 256, smem, s>>>(H, h_ld, dirs, Q, dist, perm, E, C, L, M,
+                                                                      sh_scale, epb, out);
     }
     FEQ_LAUNCH_CHECK();
     return FEQ_OK;

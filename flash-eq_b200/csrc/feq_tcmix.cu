@@ -1,0 +1,355 @@
+// feq_tcmix.cu -- the distance-binned block-diagonal radial mix on the 5th-gen tensor
+// cores (tcgen05 + TMEM, TMA-fed).  Same mathematics as feq_mix.cu / the reference
+// forward kernels (flash_eq/cuda/csrc/block_diagonal.cu:558-733).
+//
+// Formulation.  Edges are sorted by distance bin; a tile is 128 consecutive sorted
+// rows of one bin b.  For m-block m the mix is a GEMM over K = (ci, i, re/im) with the
+// m > 0 2x2 blocks [[a, b], [-b, a]] embedded as real 2x2 sub-matrices:
+//     D_lo = A . B_m(b)^T,   D_hi = A . B_m(b+1)^T      (two TMEM accumulators)
+//     out  = D_lo + t_e (D_hi - D_lo)                     (per-row lerp, epilogue)
+// A = rotated input rows scaled by s^l_in (bf16), B = re-laid radial table (bf16).
+// For float32-level accuracy every operand is split x = hi + lo into two bf16 values
+// and D accumulates hi.hi + hi.lo + lo.hi (kSplit = 3): ~16 mantissa bits per product.
+//
+// Kernel roles (192 threads, persistent, one CTA per SM):
+//   warp 0      TMA producer: A tile + B(b) tile + B(b+1) tile per 64-wide K step
+//   warp 1      TMEM allocator; one elected thread issues tcgen05.mma
+//   warps 2..5  epilogue: tcgen05.ld of both accumulators, lerp, store fp32 rows
+// TMEM holds two accumulator pairs (2 x (128 + 128) columns) so the epilogue of one
+// work item overlaps the MMAs of the next.  All TMA loads are plain (no multicast).
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include "feq_internal.cuh"
+#include "feq_sm100.cuh"
+
+namespace feq {
+
+using namespace sm100;
+
+constexpr int kTcRows = 128;     // UMMA M (rows = edges)
+constexpr int kTcN = 128;        // UMMA N per work item (output columns)
+constexpr int kTcK = 64;         // K per stage (one 128-byte swizzle row of bf16)
+constexpr int kTcThreads = 192;
+constexpr uint32_t kTcTileBytes = kTcRows * kTcK * 2;   // 16 KB (A tile and B tile alike)
+
+struct TcGemmParams {
+    int n_tiles_n;          // N_pad(m) / 128
+    int k_steps;            // K_pad(m) / 64
+    int a_col0;             // first A column of block m
+    int npad;               // padded rows of one (bin, block) B matrix
+    int n_valid;            // unpadded output columns of block m
+    int h_ld;               // row stride of H (all blocks)
+    int h_col0;             // first H column of block m
+    const int4 *tiles;      // (start, len, bin, -) row tiles of <= 128 sorted rows
+    const int *num_tiles;
+    const float *tval;      // per sorted row: interpolation weight t
+    float *H;               // (E, h_ld) sorted rows
+    int32_t *status;        // set to 2 when a wait timed out
+};
+
+template <int kSplit>
+__global__ void __launch_bounds__(kTcThreads, 1)
+tc_mix_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapA2,
+              const __grid_constant__ CUtensorMap mapB, const __grid_constant__ CUtensorMap mapB2,
+              const __grid_constant__ TcGemmParams P) {
+    constexpr int kTiles = kSplit == 1 ? 3 : 6;      // A, B(b), B(b+1) [, A.lo, B(b).lo, B(b+1).lo]
+    constexpr int kStages = kSplit == 1 ? 4 : 2;
+    constexpr uint32_t kStageBytes = kTiles * kTcTileBytes;
+    constexpr uint32_t kIdesc = idesc_bf16_f32(kTcRows, kTcN);
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    __shared__ uint64_t full_bar[kStages], empty_bar[kStages], tfull_bar[2], tempty_bar[2], drain_bar;
+    __shared__ uint32_t tmem_base_s;
+    __shared__ int abort_s;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; s++) {
+            mbar_init(&full_bar[s], 1);
+            mbar_init(&empty_bar[s], 1);
+        }
+        for (int b = 0; b < 2; b++) {
+            mbar_init(&tfull_bar[b], 1);
+            mbar_init(&tempty_bar[b], 128);
+        }
+        mbar_init(&drain_bar, 1);
+        abort_s = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0 && lane == 0) {
+        prefetch_tmap(&mapA);
+        prefetch_tmap(&mapB);
+        if (kSplit == 3) {
+            prefetch_tmap(&mapA2);
+            prefetch_tmap(&mapB2);
+        }
+    }
+    if (warp == 1) {
+        tmem_alloc(&tmem_base_s, 512);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_base_s;
+    const int n_items = *P.num_tiles * P.n_tiles_n;
+    volatile int *abort_flag = &abort_s;
+
+    if (warp == 0 && lane == 0) {
+        // ---------------- TMA producer ----------------
+        int it = 0;
+        for (int item = blockIdx.x; item < n_items && !*abort_flag; item += gridDim.x) {
+            const int tile = item / P.n_tiles_n, nt = item - tile * P.n_tiles_n;
+            const int4 T = P.tiles[tile];
+            const int rb0 = T.z * P.npad + nt * kTcN, rb1 = rb0 + P.npad;
+            for (int ks = 0; ks < P.k_steps; ks++, it++) {
+                const int s = it % kStages, r = it / kStages;
+                if (r > 0 && !mbar_wait(&empty_bar[s], (r - 1) & 1, abort_flag)) break;
+                uint8_t *base = smem + (size_t)s * kStageBytes;
+                mbar_arrive_expect_tx(&full_bar[s], kStageBytes);
+                const int ax = P.a_col0 + ks * kTcK, bx = ks * kTcK;
+                tma_load_2d(base, &mapA, ax, T.x, &full_bar[s]);
+                tma_load_2d(base + kTcTileBytes, &mapB, bx, rb0, &full_bar[s]);
+                tma_load_2d(base + 2 * kTcTileBytes, &mapB, bx, rb1, &full_bar[s]);
+                if (kSplit == 3) {
+                    tma_load_2d(base + 3 * kTcTileBytes, &mapA2, ax, T.x, &full_bar[s]);
+                    tma_load_2d(base + 4 * kTcTileBytes, &mapB2, bx, rb0, &full_bar[s]);
+                    tma_load_2d(base + 5 * kTcTileBytes, &mapB2, bx, rb1, &full_bar[s]);
+                }
+            }
+        }
+        // drain: the last loads of every stage must have landed before the CTA exits
+        for (int k = max(0, it - kStages); k < it; k++) mbar_wait_drain(&full_bar[k % kStages], (k / kStages) & 1);
+    } else if (warp == 1 && lane == 0) {
+        // ---------------- MMA issuer ----------------
+        int it = 0, j = 0;
+        for (int item = blockIdx.x; item < n_items && !*abort_flag; item += gridDim.x, j++) {
+            const int buf = j & 1, rr = j >> 1;
+            if (rr > 0 && !mbar_wait(&tempty_bar[buf], (rr - 1) & 1, abort_flag)) break;
+            tc_fence_after();
+            const uint32_t d_lo = tmem + buf * 2 * kTcN, d_hi = d_lo + kTcN;
+            bool ok = true;
+            for (int ks = 0; ks < P.k_steps; ks++, it++) {
+                const int s = it % kStages, r = it / kStages;
+                if (!mbar_wait(&full_bar[s], r & 1, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t base = smem_u32(smem + (size_t)s * kStageBytes);
+#pragma unroll
+                for (int kk = 0; kk < kTcK / 16; kk++) {
+                    const uint32_t koff = kk * 32;   // 16 bf16 = 32 bytes along K
+                    const uint64_t a = smem_desc_sw128(base + koff);
+                    const uint64_t b0 = smem_desc_sw128(base + kTcTileBytes + koff);
+                    const uint64_t b1 = smem_desc_sw128(base + 2 * kTcTileBytes + koff);
+                    const uint32_t acc = (ks > 0 || kk > 0) ? 1u : 0u;
+                    umma_f16(d_lo, a, b0, kIdesc, acc);
+                    umma_f16(d_hi, a, b1, kIdesc, acc);
+                    if (kSplit == 3) {
+                        const uint64_t a2 = smem_desc_sw128(base + 3 * kTcTileBytes + koff);
+                        const uint64_t b02 = smem_desc_sw128(base + 4 * kTcTileBytes + koff);
+                        const uint64_t b12 = smem_desc_sw128(base + 5 * kTcTileBytes + koff);
+                        umma_f16(d_lo, a, b02, kIdesc, 1u);
+                        umma_f16(d_hi, a, b12, kIdesc, 1u);
+                        umma_f16(d_lo, a2, b0, kIdesc, 1u);
+                        umma_f16(d_hi, a2, b1, kIdesc, 1u);
+                    }
+                }
+                umma_commit(&empty_bar[s]);   // stage s is free once these MMAs finish
+            }
+            if (!ok) break;
+            umma_commit(&tfull_bar[buf]);
+        }
+        // drain: every MMA issued above must complete before TMEM is released
+        umma_commit(&drain_bar);
+        mbar_wait_drain(&drain_bar, 0);
+    } else if (warp >= 2) {
+        // ---------------- epilogue ----------------
+        const int q = warp & 3;                 // TMEM lane quadrant this warp may access
+        const int row = q * 32 + lane;
+        const bool vec4 = ((P.h_ld | P.h_col0 | P.n_valid) & 3) == 0;
+        int j = 0;
+        for (int item = blockIdx.x; item < n_items; item += gridDim.x, j++) {
+            const int buf = j & 1, rr = j >> 1;
+            if (!mbar_wait(&tfull_bar[buf], rr & 1, abort_flag)) break;
+            tc_fence_after();
+            const int tile = item / P.n_tiles_n, nt = item - tile * P.n_tiles_n;
+            const int4 T = P.tiles[tile];
+            const bool valid = row < T.y;
+            const int64_t p = (int64_t)T.x + row;
+            const float t = valid ? P.tval[p] : 0.0f;
+            const uint32_t t_lo = tmem + ((uint32_t)(q * 32) << 16) + buf * 2 * kTcN, t_hi = t_lo + kTcN;
+            float *hrow = P.H + p * P.h_ld + P.h_col0;
+#pragma unroll 1
+            for (int c0 = 0; c0 < kTcN; c0 += 32) {
+                uint32_t lo[32], hi[32];
+                tmem_ld32(t_lo + c0, lo);
+                tmem_ld32(t_hi + c0, hi);
+                tmem_wait_ld();
+                const int n0 = nt * kTcN + c0;
+                if (valid) {
+                    if (vec4 && n0 + 32 <= P.n_valid) {
+#pragma unroll
+                        for (int c = 0; c < 32; c += 4) {
+                            float4 v;
+                            v.x = fmaf(t, __uint_as_float(hi[c]) - __uint_as_float(lo[c]), __uint_as_float(lo[c]));
+                            v.y = fmaf(t, __uint_as_float(hi[c + 1]) - __uint_as_float(lo[c + 1]), __uint_as_float(lo[c + 1]));
+                            v.z = fmaf(t, __uint_as_float(hi[c + 2]) - __uint_as_float(lo[c + 2]), __uint_as_float(lo[c + 2]));
+                            v.w = fmaf(t, __uint_as_float(hi[c + 3]) - __uint_as_float(lo[c + 3]), __uint_as_float(lo[c + 3]));
+                            *reinterpret_cast<float4 *>(hrow + n0 + c) = v;
+                        }
+                    } else {
+#pragma unroll
+                        for (int c = 0; c < 32; c++) {
+                            if (n0 + c < P.n_valid) {
+                                const float l = __uint_as_float(lo[c]), h = __uint_as_float(hi[c]);
+                                hrow[n0 + c] = fmaf(t, h - l, l);
+                            }
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&tempty_bar[buf]);
+        }
+    }
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+    if (threadIdx.x == 0 && abort_s && P.status) atomicMax(P.status, 2);
+}
+
+// B operand: per block m and bin b a (npad x kpad) K-major bf16 matrix (rows = output
+// columns n = (co, o, re/im), cols = k = (ci, i, re/im)), zero padded; the m > 0 2x2
+// blocks are written as [[a, b], [-b, a]].  With a second buffer the float32 weight is
+// split hi + lo.
+__global__ void tc_relayout_b_kernel(const float *__restrict__ T, __nv_bfloat16 *__restrict__ Bhi,
+                                     __nv_bfloat16 *__restrict__ Blo, int nb1, int Cin, int Cout, int wdim,
+                                     const __grid_constant__ TcGeom G, int64_t total) {
+    for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+         idx += (int64_t)gridDim.x * blockDim.x) {
+        int q = 0;
+        while (q + 1 < G.n_blocks && G.g[q + 1].boff <= idx) q++;
+        const TcBlockGeom &B = G.g[q];
+        const int64_t r = idx - B.boff;
+        const int64_t rowi = r / B.kpad;
+        const int k = (int)(r - rowi * B.kpad);
+        const int b = (int)(rowi / B.npad);
+        const int n = (int)(rowi - (int64_t)b * B.npad);
+        float v = 0.0f;
+        const int kin = B.mult * B.n_in, kout = B.mult * B.n_out;
+        if (B.n_in > 0 && B.n_out > 0 && b < nb1 && n < Cout * kout && k < Cin * kin) {
+            const int co = n / kout, rn = n - co * kout, o = rn / B.mult, oc = rn - o * B.mult;
+            const int ci = k / kin, rk = k - ci * kin, i = rk / B.mult, ic = rk - i * B.mult;
+            const float *w = T + ((int64_t)(b * Cout + co) * Cin + ci) * wdim + B.w_off;
+            if (B.mult == 1) {
+                v = __ldg(w + o * B.n_in + i);
+            } else {
+                const float a = __ldg(w + 2 * (o * B.n_in + i)), bb = __ldg(w + 2 * (o * B.n_in + i) + 1);
+                v = (oc == ic) ? a : (oc == 0 ? bb : -bb);   // (re,im) -> b, (im,re) -> -b
+            }
+        }
+        const __nv_bfloat16 hi = __float2bfloat16_rn(v);
+        Bhi[idx] = hi;
+        if (Blo) Blo[idx] = __float2bfloat16_rn(v - __bfloat162float(hi));
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Host
+// ---------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *,
+                                  CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                  CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+
+// 2D bf16 K-major tensor (inner = cols), box 64 x 128, 128-byte swizzle, zero OOB fill.
+static int make_map(CUtensorMap *m, const void *base, int64_t cols, int64_t rows) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return FEQ_ERR_CUDA;
+    if ((reinterpret_cast<uintptr_t>(base) & 15) || (cols * 2) % 16) return FEQ_ERR_INVALID_ARGUMENT;
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)(cols * 2)};
+    cuuint32_t box[2] = {(cuuint32_t)kTcK, (cuuint32_t)kTcRows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? FEQ_OK : FEQ_ERR_INVALID_ARGUMENT;
+}
+
+int launch_tc_relayout_b(const float *T, __nv_bfloat16 *Bhi, __nv_bfloat16 *Blo, int nb1, int Cin, int Cout,
+                         int wdim, const TcGeom &G, int64_t total, cudaStream_t s) {
+    if (total == 0) return FEQ_OK;
+    const int64_t grid = min64((total + 255) / 256, 148 * 32);
+    tc_relayout_b_kernel<<<(unsigned)grid, 256, 0, s>>>(T, Bhi, Blo, nb1, Cin, Cout, wdim, G, total);
+    FEQ_LAUNCH_CHECK();
+    return FEQ_OK;
+}
+
+// One persistent launch per m-block.
+int launch_tc_mix(int split, const __nv_bfloat16 *A, const __nv_bfloat16 *A2, int64_t a_rows, int a_cols,
+                  const __nv_bfloat16 *Bm, const __nv_bfloat16 *Bm2, int64_t b_rows, const TcBlockGeom &B,
+                  int a_col0, int n_valid, int h_ld, int h_col0, const int4 *tiles, const int *num_tiles,
+                  int64_t max_tiles, const float *tval, float *H, int32_t *status, cudaStream_t s) {
+    CUtensorMap mA, mA2, mB, mB2;
+    int rc;
+    if ((rc = make_map(&mA, A, a_cols, a_rows)) != FEQ_OK) return rc;
+    if ((rc = make_map(&mB, Bm, B.kpad, b_rows)) != FEQ_OK) return rc;
+    if (split == 3) {
+        if ((rc = make_map(&mA2, A2, a_cols, a_rows)) != FEQ_OK) return rc;
+        if ((rc = make_map(&mB2, Bm2, B.kpad, b_rows)) != FEQ_OK) return rc;
+    } else {
+        mA2 = mA;
+        mB2 = mB;
+    }
+    TcGemmParams P;
+    P.n_tiles_n = B.npad / kTcN;
+    P.k_steps = B.kpad / kTcK;
+    P.a_col0 = a_col0;
+    P.npad = B.npad;
+    P.n_valid = n_valid;
+    P.h_ld = h_ld;
+    P.h_col0 = h_col0;
+    P.tiles = tiles;
+    P.num_tiles = num_tiles;
+    P.tval = tval;
+    P.H = H;
+    P.status = status;
+    int dev = 0, sms = 148;
+    FEQ_CUDA_TRY(cudaGetDevice(&dev));
+    FEQ_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    const int64_t items = max_tiles * P.n_tiles_n;
+    const int grid = (int)min64(sms, max64(items, 1));
+    const size_t smem = (size_t)(split == 1 ? 4 * 3 : 2 * 6) * kTcTileBytes + 1024;
+    if (split == 1) {
+        FEQ_CUDA_TRY(cudaFuncSetAttribute(tc_mix_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        tc_mix_kernel<1><<<grid, kTcThreads, smem, s>>>(mA, mA2, mB, mB2, P);
+    } else {
+        FEQ_CUDA_TRY(cudaFuncSetAttribute(tc_mix_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        tc_mix_kernel<3><<<grid, kTcThreads, smem, s>>>(mA, mA2, mB, mB2, P);
+    }
+    FEQ_LAUNCH_CHECK();
+    return FEQ_OK;
+}
+
+}  // namespace feq

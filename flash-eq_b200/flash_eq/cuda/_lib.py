@@ -17,6 +17,7 @@ FEQ_OK = 0
 FEQ_BASIS_MFIRST = 0
 FEQ_BASIS_ROT_TO_EZ = 1
 FEQ_REDUCE = {"sum": 0, "mean": 1, "max": 2}
+FEQ_MIX = {"fp32": 0, "bf16": 1, "bf16x3": 2}
 MAX_L = 16
 
 c_i32p = ctypes.POINTER(ctypes.c_int32)
@@ -31,7 +32,7 @@ class FeqEdgewiseArgs(ctypes.Structure):
         ("c_out", ctypes.c_int32), ("lvals_in", c_i32p), ("n_lvals_in", ctypes.c_int32),
         ("lvals_out", c_i32p), ("n_lvals_out", ctypes.c_int32), ("sh_scale", ctypes.c_float),
         ("bin_param1", ctypes.c_float), ("bin_param2", ctypes.c_float), ("num_bins", ctypes.c_int32),
-        ("log_bins", ctypes.c_int32), ("out", c_vp), ("status", c_vp),
+        ("log_bins", ctypes.c_int32), ("out", c_vp), ("status", c_vp), ("mix_mode", ctypes.c_int32),
     ]
 
 

@@ -133,12 +133,15 @@ def block_diagonal_fwd(features, radial_table, distances, lvals_in, lvals_out, s
 
 
 def edgewise_fwd(x, distances, radial_table, lvals_in, lvals_out, c_out, sh_scale, p1, p2, num_bins,
-                 log_bins, *, src=None, edge_add=None, directions=None, P=None, Q=None, status=None):
+                 log_bins, *, src=None, edge_add=None, directions=None, P=None, Q=None, status=None, mix="fp32"):
     """Fused Q . Lambda(r) . P^T . f.  Rows f[e] = x[src[e]] (+ edge_add[e]) or x[e].
 
     Basis from ``directions`` (E, 3) when given, else from the dense P (E, d_in, d_in)
-    and Q (E, d_out, d_out).
+    and Q (E, d_out, d_out).  ``mix``: "fp32" (CUDA cores), "bf16" (tensor cores,
+    bf16 operands) or "bf16x3" (tensor cores, float32-level accuracy).
     """
+    if mix not in _lib.FEQ_MIX:
+        raise ValueError(f"mix must be one of {list(_lib.FEQ_MIX)}, got {mix!r}")
     lib = _require_cuda(x, distances, radial_table, src, edge_add, directions, P, Q)
     x = _f32(x, "x")
     distances = _f32(distances, "distances")
@@ -192,6 +195,7 @@ def edgewise_fwd(x, distances, radial_table, lvals_in, lvals_out, c_out, sh_scal
     args.out = out.data_ptr()
     if status is not None:
         args.status = status.data_ptr()
+    args.mix_mode = _lib.FEQ_MIX[mix]
     ws_bytes = lib.feq_edgewise_workspace_bytes(ctypes.byref(args))
     if ws_bytes == 0:
         raise RuntimeError("edgewise: unsupported layout (l <= 16, <= 64 irreps, dim <= 512)")

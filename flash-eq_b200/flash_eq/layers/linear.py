@@ -24,6 +24,9 @@ from ..representations.wigner import LazyBasis, basis_source
 from .radial import SeparableRadialNet
 
 
+DEFAULT_MIX_PRECISION = "fp32"
+
+
 def _dense(M):
     return M.dense() if isinstance(M, LazyBasis) else M
 
@@ -49,6 +52,10 @@ class EquivariantEdgewiseLinear(nn.Module):
                                                  log=log_bins)
         self._lin = tuple(in_repr.lvals.tolist())
         self._lout = tuple(out_repr.lvals.tolist())
+        # Arithmetic of the radial mix (not a reference kwarg, so not in __init__):
+        # "fp32" CUDA-core float32, "bf16x3" tensor cores at float32-level accuracy,
+        # "bf16" tensor cores with bf16 operands (the bf16-mix mode).
+        self.mix_precision = DEFAULT_MIX_PRECISION
 
     def forward(self, P, Q, edge_features: torch.Tensor, distances: torch.Tensor) -> torch.Tensor:
         """(E, Cin, d_in) edge features -> (E, Cout, d_out), standard SH order."""
@@ -73,7 +80,8 @@ class EquivariantEdgewiseLinear(nn.Module):
                 xx.detach(), dd.detach(), tab.detach(), self._lin, self._lout, self.channels_out,
                 self.solid_harmonic_scale, p1, p2, rw.num_bins, rw.log, src=src,
                 edge_add=None if ea is None else ea.detach(), directions=dP if fused else None,
-                P=None if pp is None else pp.detach(), Q=None if qq is None else qq.detach())
+                P=None if pp is None else pp.detach(), Q=None if qq is None else qq.detach(),
+                mix=self.mix_precision)
 
         return forward_only(run, x, table, dist, edge_add, Pd, Qd)
 

@@ -177,8 +177,20 @@ typedef struct FeqEdgewiseArgs {
     float sh_scale, bin_param1, bin_param2;
     int32_t num_bins, log_bins;
     float *out;                /* (E, c_out, d_out) standard order */
-    int32_t *status;           /* optional device int32: 1 = a src index was out of range */
+    int32_t *status;           /* optional device int32: 1 = a src index was out of range,
+                                  2 = a tensor-core wait timed out (result invalid) */
+    int32_t mix_mode;          /* FEQ_MIX_* below */
 } FeqEdgewiseArgs;
+
+/* Radial-mix arithmetic for feq_edgewise_fwd.
+ *   FEQ_MIX_FP32       float32 FMA on CUDA cores (the reference's arithmetic)
+ *   FEQ_MIX_BF16       tcgen05 tensor cores, bf16 operands, fp32 accumulation
+ *                      (the "bf16-mix" mode: ~1e-3 relative error)
+ *   FEQ_MIX_BF16X3     tcgen05 tensor cores with every operand split into two bf16
+ *                      terms (hi.hi + hi.lo + lo.hi): float32-level accuracy */
+#define FEQ_MIX_FP32 0
+#define FEQ_MIX_BF16 1
+#define FEQ_MIX_BF16X3 2
 
 size_t feq_edgewise_workspace_bytes(const FeqEdgewiseArgs *args);
 int feq_edgewise_fwd(const FeqEdgewiseArgs *args, void *workspace, size_t workspace_bytes,
