@@ -227,6 +227,7 @@ struct TcPlan {
     TcGeom G;
     int koff[kMaxBlocks], noff[kMaxBlocks], nvalid[kMaxBlocks];
     int k_total, n_total;
+    int c_in, c_out;
     int64_t b_total;
     TcPosMap in_map, out_map;
 };
@@ -256,12 +257,26 @@ static void fill_posmap(const ReprLayout &L, const TcPlan &T, const MixLayout &M
         if (m < T.G.n_blocks) {
             const MixBlock &B = M.blk[m];
             const int mult = m == 0 ? 1 : 2;
+            // columns are (member, re/im, channel) with the channel fastest
             if (input) {
-                map->base[j] = T.koff[m] + (j - off[m]);
-                map->stride[j] = (int16_t)(mult * B.n_in);
+                map->base[j] = T.koff[m] + (j - off[m]) * T.c_in;
             } else {
-                map->base[j] = T.noff[m] + (j - off[m]);
-                map->stride[j] = (int16_t)(mult * B.n_out);
+                map->base[j] = T.noff[m] + (j - off[m]) * T.c_out;
+            }
+            map->stride[j] = 1;
+            (void)mult;
+            (void)B;
+        }
+    }
+    for (int j = 0; j < L.dim; j++) map->base_std[L.perm[j]] = map->base[j];
+    map->n_pad = 0;
+    if (input) {
+        for (int m = 0; m < T.G.n_blocks; m++) {
+            const int K = T.c_in * T.G.g[m].mult * T.G.g[m].n_in;
+            if (K < T.G.g[m].kpad) {
+                map->pad_lo[map->n_pad] = T.koff[m] + K;
+                map->pad_hi[map->n_pad] = T.koff[m] + T.G.g[m].kpad;
+                map->n_pad++;
             }
         }
     }
@@ -270,6 +285,8 @@ static void fill_posmap(const ReprLayout &L, const TcPlan &T, const MixLayout &M
 static int build_tc_plan(const MixLayout &M, const ReprLayout &Li, const ReprLayout &Lo, int Cin, int Cout, int nb,
                          TcPlan *T) {
     memset(T, 0, sizeof(*T));
+    T->c_in = Cin;
+    T->c_out = Cout;
     int kt = 0, nt = 0, nblk = 0;
     int64_t boff = 0;
     for (int m = 0; m < M.n_blocks; m++) {

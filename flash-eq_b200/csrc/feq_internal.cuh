@@ -58,13 +58,17 @@ struct MixLayout {
 };
 
 // Tensor-core path: where component j (m-first order) of channel c lives in a GEMM
-// row (A for the input repr, H for the output repr): base[j] + c * stride[j], or
+// row (A for the input repr, H for the output repr): base[j] + c * stride[j] (stride 1:
+// the channel is the fastest column index), or
 // base[j] = -1 when j belongs to a block that does not take part in the mix; l[j] is
 // the degree of j (solid-harmonic scaling).
 struct TcPosMap {
     int32_t base[kMaxDim];
+    int32_t base_std[kMaxDim];       // base of the component at standard position k
     int16_t stride[kMaxDim];
     int8_t l[kMaxDim];
+    int n_pad;                       // zero-padding column ranges of the A row
+    int pad_lo[kMaxBlocks], pad_hi[kMaxBlocks];
 };
 
 // Tensor-core radial mix: per m-block GEMM geometry.  B (the re-laid table) holds, per

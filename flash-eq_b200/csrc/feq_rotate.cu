@@ -369,11 +369,13 @@ int launch_rotate_out(const float *h, const float *dirs, const float *Q, int64_t
 
 // ===========================================================================
 // Tensor-core path: producer of the GEMM's A rows and consumer of its output rows.
-// Rows are in bin-sorted order p; edge e = perm[p].
+// One warp per edge; rows are in bin-sorted order p, edge e = perm[p].  A and H
+// columns put the channel fastest, so lane = channel touches consecutive addresses.
 // ===========================================================================
 namespace feq {
 
 static_assert(sizeof(TcPosMap) % 4 == 0, "TcPosMap is copied as 32-bit words");
+constexpr int kTcWarps = 8;
 
 __device__ __forceinline__ void stage_posmap(const TcPosMap &src, TcPosMap &dst) {
     const int *s = reinterpret_cast<const int *>(&src);
@@ -381,194 +383,255 @@ __device__ __forceinline__ void stage_posmap(const TcPosMap &src, TcPosMap &dst)
     for (int i = threadIdx.x; i < (int)(sizeof(TcPosMap) / 4); i += blockDim.x) d[i] = s[i];
 }
 
-// A[p][map.base[j] + c * map.stride[j]] = (g[e][c][j]) * s_e^l(j), as bf16 (hi [, lo]).
-// g = f . P with f = x[src[e]] (+ edge_add[e]) or x[e].  Also tval[p] = t_e.
-template <bool kDense, bool kGather, bool kSplit>
-__global__ void rotate_in_tc_kernel(const float *__restrict__ x, const int64_t *__restrict__ src, int64_t nsrc,
-                                    const float *__restrict__ edge_add, const float *__restrict__ dirs,
-                                    const float *__restrict__ P, const float *__restrict__ dist,
-                                    const int64_t *__restrict__ perm, int64_t E, int C,
-                                    const __grid_constant__ ReprLayout Lp, const __grid_constant__ TcPosMap Mp,
-                                    int k_total, Binning bins, float sh_scale, int epb,
-                                    __nv_bfloat16 *__restrict__ A_hi, __nv_bfloat16 *__restrict__ A_lo,
-                                    float *__restrict__ tval, int32_t *status) {
-    extern __shared__ float smem[];
-    __shared__ ReprLayout L;
-    __shared__ TcPosMap Mm;
-    __shared__ float sp_s[16][kMaxL + 1];
-    __shared__ int64_t eid_s[16];
-    stage_posmap(Mp, Mm);
-    stage_layout(Lp, L);
-    const int d = L.dim, row = C * d;
-    const int64_t p0 = (int64_t)blockIdx.x * epb;
-    const int ne = (int)min64(epb, E - p0);
-    float *f_s = smem;                          // epb * row
-    float *a_s = f_s + epb * row;               // epb * k_total (fp32 staging of the A rows)
-    float *b_s = a_s + epb * k_total;           // basis area
-    if (threadIdx.x < ne) {
-        const int64_t e = perm[p0 + threadIdx.x];
-        eid_s[threadIdx.x] = e;
-        const float dd = dist[e];
-        int lo;
-        float t;
-        bin_of(dd, bins, lo, t);
-        tval[p0 + threadIdx.x] = t;
-        const float s = dd / (dd + sh_scale);
-        for (int l = 0; l <= L.lmax; l++) sp_s[threadIdx.x][l] = ipowf(s, l);
-    }
-    __syncthreads();
-    for (int idx = threadIdx.x; idx < ne * row; idx += blockDim.x) {
-        const int k = idx / row, r = idx - k * row;
-        const int64_t e = eid_s[k];
-        float v;
-        if (kGather) {
-            const int64_t s = src[e];
-            if (s < 0 || s >= nsrc) {
-                set_status(status, 1);
-                v = 0.0f;
-            } else {
-                v = __ldg(x + s * row + r);
-            }
-        } else {
-            v = __ldg(x + e * row + r);
+// Warp-cooperative version of build_dblocks for one edge.
+__device__ void build_dblocks_warp(const ReprLayout &L, const EdgeTrig &tr, float *m_s, float *d_s, int lane) {
+    const int per = L.dblock_floats;
+    for (int r = lane; r < per; r += 32) {
+        int u = 0;
+        while (u + 1 < L.n_unique && L.unique_doff[u + 1] <= r) u++;
+        const int l = L.unique_l[u], n = 2 * l + 1;
+        const float *t = feq_wt_data + feq_wt_offset[l] + (r - L.unique_doff[u]) * n;
+        float acc = __ldg(t);
+        for (int m = 1; m <= l; m++) {
+            acc = fmaf(__ldg(t + 2 * m - 1), tr.ct[m], acc);
+            acc = fmaf(__ldg(t + 2 * m), tr.st[m], acc);
         }
-        if (edge_add) v += __ldg(edge_add + e * row + r);
-        f_s[idx] = v;
+        m_s[r] = acc;
     }
-    for (int idx = threadIdx.x; idx < ne * k_total; idx += blockDim.x) a_s[idx] = 0.0f;   // K padding
-    const float *D_s;
-    if (kDense) {
-        const int dd2 = d * d;
-        for (int idx = threadIdx.x; idx < ne * dd2; idx += blockDim.x) {
-            const int k = idx / dd2;
-            b_s[idx] = __ldg(P + eid_s[k] * dd2 + (idx - k * dd2));
-        }
-        __syncthreads();
-        D_s = b_s;
-    } else {
-        EdgeTrig *trig_s = reinterpret_cast<EdgeTrig *>(b_s);
-        float *m_s = reinterpret_cast<float *>(trig_s + epb);
-        float *d_s = m_s + epb * L.dblock_floats;
-        if (threadIdx.x < ne) {
-            const float *v = dirs + eid_s[threadIdx.x] * 3;
-            edge_trig(v[0], v[1], v[2], L.lmax, trig_s[threadIdx.x]);
-        }
-        __syncthreads();
-        build_dblocks(L, ne, trig_s, m_s, d_s);
-        D_s = d_s;
+    __syncwarp();
+    for (int r = lane; r < per; r += 32) {
+        int u = 0;
+        while (u + 1 < L.n_unique && L.unique_doff[u + 1] <= r) u++;
+        const int l = L.unique_l[u], n = 2 * l + 1;
+        const int pq = r - L.unique_doff[u];
+        const int a = pq / n, b = pq - a * n;
+        const int ma = a < l ? l - a : a - l, mb = b < l ? l - b : b - l;
+        const float ca = tr.cp[ma], cb = tr.cp[mb];
+        const float sa = a < l ? tr.sp[ma] : -tr.sp[ma];
+        const float sb = b < l ? tr.sp[mb] : -tr.sp[mb];
+        const float *M = m_s + L.unique_doff[u];
+        float v = ca * cb * M[a * n + b];
+        if (mb) v = fmaf(ca * sb, M[a * n + (2 * l - b)], v);
+        if (ma) v = fmaf(sa * cb, M[(2 * l - a) * n + b], v);
+        if (ma && mb) v = fmaf(sa * sb, M[(2 * l - a) * n + (2 * l - b)], v);
+        d_s[r] = v;
     }
-    for (int idx = threadIdx.x; idx < ne * row; idx += blockDim.x) {
-        const int k = idx / row, r = idx - k * row;
-        const int c = r / d, j = r - c * d;
-        const int base = Mm.base[j];
-        if (base < 0) continue;                 // component not used by any non-empty block
-        const float *fr = f_s + k * row + c * d;
-        float acc = 0.0f;
-        if (kDense) {
-            const float *Pe = D_s + k * d * d;
-            for (int q = 0; q < d; q++) acc = fmaf(fr[q], Pe[q * d + j], acc);
-        } else {
-            const int ps = L.perm[j];
-            const int ir = L.std_irrep[ps];
-            const int l = L.irrep_l[ir], n = 2 * l + 1, off = L.irrep_off[ir];
-            const int col = ps - off;
-            const float *De = D_s + k * L.dblock_floats + L.unique_doff[L.irrep_slot[ir]];
-            for (int q = 0; q < n; q++) acc = fmaf(fr[off + q], De[q * n + col], acc);
-        }
-        a_s[k * k_total + base + c * Mm.stride[j]] = acc * sp_s[k][Mm.l[j]];
-    }
-    __syncthreads();
-    // rows out: 8 bf16 (16 B) per store; k_total is a multiple of 64
-    const int per = k_total / 8;
-    for (int idx = threadIdx.x; idx < ne * per; idx += blockDim.x) {
-        const int k = idx / per, q = idx - k * per;
-        const float *v = a_s + k * k_total + q * 8;
-        __align__(16) __nv_bfloat16 hi[8], lo[8];
+    __syncwarp();
+}
+
+// Floats of the per-warp basis area (trig + M + D blocks, or a dense d x d matrix).
+__host__ __device__ inline int tc_warp_basis_floats(const ReprLayout &L, bool dense) {
+    return dense ? L.dim * L.dim : (int)(sizeof(EdgeTrig) / sizeof(float)) + 2 * L.dblock_floats;
+}
+
+// y[col] = sum_q f[q] D[q*N + col] (kIn: rotate into the edge frame, D^T applied) or
+// y[kk] = sum_col f[col] D[kk*N + col] (rotate back).  f in registers, D broadcast.
+template <int N, bool kIn, typename Emit>
+__device__ __forceinline__ void rotate_block(const float *__restrict__ fsrc, const float *__restrict__ D, Emit emit) {
+    float f[N];
 #pragma unroll
-        for (int u = 0; u < 8; u++) {
-            hi[u] = __float2bfloat16_rn(v[u]);
-            lo[u] = __float2bfloat16_rn(v[u] - __bfloat162float(hi[u]));
-        }
-        const int64_t off = (p0 + k) * (int64_t)k_total + q * 8;
-        *reinterpret_cast<uint4 *>(A_hi + off) = *reinterpret_cast<const uint4 *>(hi);
-        if (kSplit) *reinterpret_cast<uint4 *>(A_lo + off) = *reinterpret_cast<const uint4 *>(lo);
+    for (int q = 0; q < N; q++) f[q] = fsrc[q];
+#pragma unroll
+    for (int o = 0; o < N; o++) {
+        float acc = 0.0f;
+#pragma unroll
+        for (int q = 0; q < N; q++) acc = fmaf(f[q], kIn ? D[q * N + o] : D[o * N + q], acc);
+        emit(o, acc);
     }
 }
 
-// out[e][c][k] = sum_j h[c][j] Q[e][k][j] with h[c][j] = H[p][map.base[j] + c * map.stride[j]] * s_e^l(j)
-// (0 for components of blocks without input).
-template <bool kDense>
-__global__ void rotate_out_tc_kernel(const float *__restrict__ H, int h_ld, const float *__restrict__ dirs,
-                                     const float *__restrict__ Q, const float *__restrict__ dist,
-                                     const int64_t *__restrict__ perm, int64_t E, int C,
-                                     const __grid_constant__ ReprLayout Lp, const __grid_constant__ TcPosMap Mp,
-                                     float sh_scale, int epb, float *__restrict__ out) {
+template <bool kIn, typename Emit>
+__device__ __forceinline__ void rotate_block_any(int l, const float *__restrict__ fsrc, const float *__restrict__ D,
+                                                 Emit emit) {
+    switch (l) {
+        case 0: rotate_block<1, kIn>(fsrc, D, emit); break;
+        case 1: rotate_block<3, kIn>(fsrc, D, emit); break;
+        case 2: rotate_block<5, kIn>(fsrc, D, emit); break;
+        case 3: rotate_block<7, kIn>(fsrc, D, emit); break;
+        case 4: rotate_block<9, kIn>(fsrc, D, emit); break;
+        default: {
+            const int n = 2 * l + 1;
+            for (int o = 0; o < n; o++) {
+                float acc = 0.0f;
+                for (int q = 0; q < n; q++) acc = fmaf(fsrc[q], kIn ? D[q * n + o] : D[o * n + q], acc);
+                emit(o, acc);
+            }
+        }
+    }
+}
+
+// A[p][base(k) + c] = (f[e][c] . P)[k] * s_e^l(k) as bf16 (hi [, lo]); tval[p] = t_e.
+// Lane = channel: each column store of the warp covers 32 consecutive bf16.
+template <bool kDense, bool kGather, bool kSplit>
+__global__ void __launch_bounds__(kTcWarps * 32)
+rotate_in_tc_kernel(const float *__restrict__ x, const int64_t *__restrict__ src, int64_t nsrc,
+                    const float *__restrict__ edge_add, const float *__restrict__ dirs, const float *__restrict__ P,
+                    const float *__restrict__ dist, const int64_t *__restrict__ perm, int64_t E, int C,
+                    const __grid_constant__ ReprLayout Lp, const __grid_constant__ TcPosMap Mp, int k_total,
+                    Binning bins, float sh_scale, int per_warp, __nv_bfloat16 *__restrict__ A_hi,
+                    __nv_bfloat16 *__restrict__ A_lo, float *__restrict__ tval, int32_t *status) {
     extern __shared__ float smem[];
     __shared__ ReprLayout L;
     __shared__ TcPosMap Mm;
-    __shared__ float sp_s[16][kMaxL + 1];
-    __shared__ int64_t eid_s[16];
     stage_posmap(Mp, Mm);
     stage_layout(Lp, L);
-    const int d = L.dim, row = C * d;
-    const int64_t p0 = (int64_t)blockIdx.x * epb;
-    const int ne = (int)min64(epb, E - p0);
-    float *h_s = smem;
-    float *b_s = h_s + epb * row;
-    if (threadIdx.x < ne) {
-        const int64_t e = perm[p0 + threadIdx.x];
-        eid_s[threadIdx.x] = e;
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int d = L.dim, ds = d | 1, row = C * d;
+    float *ws = smem + (size_t)w * per_warp;
+    float *fs = ws + tc_warp_basis_floats(L, kDense);        // 32 x ds
+    EdgeTrig *trig = reinterpret_cast<EdgeTrig *>(ws);
+    float *m_s = ws + sizeof(EdgeTrig) / sizeof(float);
+    float *d_s = m_s + L.dblock_floats;
+    for (int64_t p = (int64_t)blockIdx.x * kTcWarps + w; p < E; p += (int64_t)gridDim.x * kTcWarps) {
+        const int64_t e = perm[p];
         const float dd = dist[e];
         const float s = dd / (dd + sh_scale);
-        for (int l = 0; l <= L.lmax; l++) sp_s[threadIdx.x][l] = ipowf(s, l);
-    }
-    __syncthreads();
-    for (int idx = threadIdx.x; idx < ne * row; idx += blockDim.x) {
-        const int k = idx / row, r = idx - k * row;
-        const int c = r / d, j = r - c * d;
-        const int base = Mm.base[j];
-        h_s[idx] = base < 0 ? 0.0f : __ldg(H + (p0 + k) * (int64_t)h_ld + base + c * Mm.stride[j]) * sp_s[k][Mm.l[j]];
-    }
-    const float *D_s;
-    if (kDense) {
-        const int dd2 = d * d;
-        for (int idx = threadIdx.x; idx < ne * dd2; idx += blockDim.x) {
-            const int k = idx / dd2;
-            b_s[idx] = __ldg(Q + eid_s[k] * dd2 + (idx - k * dd2));
+        int64_t xrow = e;
+        if (kGather) {
+            xrow = src[e];
+            if (xrow < 0 || xrow >= nsrc) {
+                if (lane == 0) set_status(status, 1);
+                xrow = -1;
+            }
         }
-        __syncthreads();
-        D_s = b_s;
-    } else {
-        EdgeTrig *trig_s = reinterpret_cast<EdgeTrig *>(b_s);
-        float *m_s = reinterpret_cast<float *>(trig_s + epb);
-        float *d_s = m_s + epb * L.dblock_floats;
-        if (threadIdx.x < ne) {
-            const float *v = dirs + eid_s[threadIdx.x] * 3;
-            edge_trig(v[0], v[1], v[2], L.lmax, trig_s[threadIdx.x]);
+        if (lane == 0) {
+            int lo;
+            float t;
+            bin_of(dd, bins, lo, t);
+            tval[p] = t;
+            if (!kDense) edge_trig(dirs[e * 3], dirs[e * 3 + 1], dirs[e * 3 + 2], L.lmax, *trig);
         }
-        __syncthreads();
-        build_dblocks(L, ne, trig_s, m_s, d_s);
-        D_s = d_s;
-    }
-    for (int idx = threadIdx.x; idx < ne * row; idx += blockDim.x) {
-        const int k = idx / row, r = idx - k * row;
-        const int c = r / d, kk = r - c * d;
-        const float *hr = h_s + k * row + c * d;
-        float acc = 0.0f;
         if (kDense) {
-            const float *Qe = D_s + k * d * d + kk * d;
-            for (int j = 0; j < d; j++) acc = fmaf(hr[j], Qe[j], acc);
-        } else {
-            const int ir = L.std_irrep[kk];
-            const int l = L.irrep_l[ir], n = 2 * l + 1, off = L.irrep_off[ir];
-            const float *De = D_s + k * L.dblock_floats + L.unique_doff[L.irrep_slot[ir]] + (kk - off) * n;
-            for (int col = 0; col < n; col++) acc = fmaf(hr[L.inv_perm[off + col]], De[col], acc);
+            for (int i = lane; i < d * d; i += 32) ws[i] = __ldg(P + e * d * d + i);
         }
-        out[eid_s[k] * row + r] = acc;
+        __nv_bfloat16 *ah = A_hi + p * (int64_t)k_total;
+        __nv_bfloat16 *al = kSplit ? A_lo + p * (int64_t)k_total : nullptr;
+        for (int r = 0; r < Mm.n_pad; r++)
+            for (int i = Mm.pad_lo[r] + lane; i < Mm.pad_hi[r]; i += 32) {
+                ah[i] = __float2bfloat16_rn(0.0f);
+                if (kSplit) al[i] = __float2bfloat16_rn(0.0f);
+            }
+        __syncwarp();
+        if (!kDense) build_dblocks_warp(L, *trig, m_s, d_s, lane);
+        for (int c0 = 0; c0 < C; c0 += 32) {
+            const int nch = min(32, C - c0);
+            for (int i = lane; i < nch * d; i += 32) {
+                const int c = i / d, q = i - c * d;
+                float v = xrow >= 0 ? __ldg(x + xrow * row + (c0 + c) * d + q) : 0.0f;
+                if (edge_add) v += __ldg(edge_add + e * row + (c0 + c) * d + q);
+                fs[c * ds + q] = v;
+            }
+            __syncwarp();
+            if (lane < nch) {
+                const float *fr = fs + lane * ds;
+                const int c = c0 + lane;
+                auto put = [&](int b, float v) {
+                    const __nv_bfloat16 hi = __float2bfloat16_rn(v);
+                    ah[b + c] = hi;
+                    if (kSplit) al[b + c] = __float2bfloat16_rn(v - __bfloat162float(hi));
+                };
+                if (kDense) {
+                    for (int j = 0; j < d; j++) {
+                        const int b = Mm.base[j];
+                        if (b < 0) continue;
+                        float acc = 0.0f;
+                        for (int q = 0; q < d; q++) acc = fmaf(fr[q], ws[q * d + j], acc);
+                        put(b, acc * ipowf(s, Mm.l[j]));
+                    }
+                } else {
+                    for (int r = 0; r < L.n_irreps; r++) {
+                        const int l = L.irrep_l[r], off = L.irrep_off[r];
+                        const float *D = d_s + L.unique_doff[L.irrep_slot[r]];
+                        const float sl = ipowf(s, l);
+                        const int32_t *bstd = Mm.base_std + off;
+                        rotate_block_any<true>(l, fr + off, D, [&](int col, float v) {
+                            const int b = bstd[col];
+                            if (b >= 0) put(b, v * sl);
+                        });
+                    }
+                }
+            }
+            __syncwarp();
+        }
     }
 }
 
-constexpr size_t kTcRotSmemBudget = 160 * 1024;
+// out[e][c][k] = sum_j h[c][j] Q[e][k][j], h[c][j] = H[p][base(j) + c] * s_e^l(j)
+// (0 where base < 0: output blocks that receive no input).  Output rows are staged
+// per 32-channel chunk and written contiguously.
+template <bool kDense>
+__global__ void __launch_bounds__(kTcWarps * 32)
+rotate_out_tc_kernel(const float *__restrict__ H, int h_ld, const float *__restrict__ dirs,
+                     const float *__restrict__ Q, const float *__restrict__ dist, const int64_t *__restrict__ perm,
+                     int64_t E, int C, const __grid_constant__ ReprLayout Lp, const __grid_constant__ TcPosMap Mp,
+                     float sh_scale, int per_warp, float *__restrict__ out) {
+    extern __shared__ float smem[];
+    __shared__ ReprLayout L;
+    __shared__ TcPosMap Mm;
+    stage_posmap(Mp, Mm);
+    stage_layout(Lp, L);
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int d = L.dim, ds = d | 1, row = C * d;
+    float *ws = smem + (size_t)w * per_warp;
+    float *hs = ws + tc_warp_basis_floats(L, kDense);        // 32 x ds (standard order)
+    float *os = hs + 32 * ds;                                 // 32 x ds
+    EdgeTrig *trig = reinterpret_cast<EdgeTrig *>(ws);
+    float *m_s = ws + sizeof(EdgeTrig) / sizeof(float);
+    float *d_s = m_s + L.dblock_floats;
+    for (int64_t p = (int64_t)blockIdx.x * kTcWarps + w; p < E; p += (int64_t)gridDim.x * kTcWarps) {
+        const int64_t e = perm[p];
+        const float dd = dist[e];
+        const float s = dd / (dd + sh_scale);
+        if (kDense) {
+            for (int i = lane; i < d * d; i += 32) ws[i] = __ldg(Q + e * d * d + i);
+        } else if (lane == 0) {
+            edge_trig(dirs[e * 3], dirs[e * 3 + 1], dirs[e * 3 + 2], L.lmax, *trig);
+        }
+        __syncwarp();
+        if (!kDense) build_dblocks_warp(L, *trig, m_s, d_s, lane);
+        const float *hp = H + p * (int64_t)h_ld;
+        float *op = out + e * (int64_t)row;
+        for (int c0 = 0; c0 < C; c0 += 32) {
+            const int nch = min(32, C - c0);
+            if (lane < nch) {
+                for (int k = 0; k < d; k++) {
+                    const int b = Mm.base_std[k];
+                    hs[lane * ds + k] = b < 0 ? 0.0f : __ldg(hp + b + c0 + lane) * ipowf(s, L.irrep_l[L.std_irrep[k]]);
+                }
+                const float *hr = hs + lane * ds;
+                float *orow = os + lane * ds;
+                if (kDense) {
+                    // dense Q is indexed by m-first columns: h in m-first order is hr[perm[j]]
+                    for (int k = 0; k < d; k++) {
+                        float acc = 0.0f;
+                        for (int j = 0; j < d; j++) acc = fmaf(hr[L.perm[j]], ws[k * d + j], acc);
+                        orow[k] = acc;
+                    }
+                } else {
+                    for (int r = 0; r < L.n_irreps; r++) {
+                        const int l = L.irrep_l[r], off = L.irrep_off[r];
+                        const float *D = d_s + L.unique_doff[L.irrep_slot[r]];
+                        rotate_block_any<false>(l, hr + off, D, [&](int kk, float v) { orow[off + kk] = v; });
+                    }
+                }
+            }
+            __syncwarp();
+            for (int i = lane; i < nch * d; i += 32) {
+                const int c = i / d, k = i - c * d;
+                op[c0 * d + i] = os[c * ds + k];
+            }
+            __syncwarp();
+        }
+    }
+}
+
+static int tc_grid(int64_t E, size_t smem) {
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int per_sm = (int)std::max<size_t>(1, std::min<size_t>(4, (200 * 1024) / (smem + 12 * 1024)));
+    return (int)min64((E + kTcWarps - 1) / kTcWarps, (int64_t)sms * per_sm * 8);
+}
 
 int launch_rotate_in_tc(const float *x, const int64_t *src, int64_t nsrc, const float *edge_add, const float *dirs,
                         const float *P, const float *dist, const int64_t *perm, int64_t E, int C,
@@ -577,20 +640,17 @@ int launch_rotate_in_tc(const float *x, const int64_t *src, int64_t nsrc, const 
                         cudaStream_t s) {
     if (E == 0) return FEQ_OK;
     const bool dense = dirs == nullptr;
-    const size_t row = (size_t)C * L.dim;
-    const size_t per = row + k_total + basis_area_floats(L, 1, dense);
-    if (per * 4 > kTcRotSmemBudget) return FEQ_ERR_UNSUPPORTED;
-    const int epb = pick_epb(per, 0, kTcRotSmemBudget, 8);
-    const size_t smem = per * epb * 4;
-    const int64_t grid = (E + epb - 1) / epb;
+    const int per_warp = (tc_warp_basis_floats(L, dense) + 32 * (L.dim | 1) + 3) & ~3;
+    const size_t smem = (size_t)per_warp * kTcWarps * 4;
+    if (smem > 200 * 1024) return FEQ_ERR_UNSUPPORTED;
+    const int grid = tc_grid(E, smem);
 #define FEQ_ROT_IN_TC(D, G, S)                                                                              \
     do {                                                                                                    \
         FEQ_CUDA_TRY(cudaFuncSetAttribute(rotate_in_tc_kernel<D, G, S>,                                     \
                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));         \
-        rotate_in_tc_kernel<D, G, S><<<(unsigned)grid, 256, smem, s>>>(x, src, nsrc, edge_add, dirs, P, dist, \
-                                                                       perm, E, C, L, M, k_total, bins,     \
-                                                                       sh_scale, epb, A_hi, A_lo, tval,     \
-                                                                       status);                             \
+        rotate_in_tc_kernel<D, G, S><<<(unsigned)grid, kTcWarps * 32, smem, s>>>(                           \
+            x, src, nsrc, edge_add, dirs, P, dist, perm, E, C, L, M, k_total, bins, sh_scale, per_warp, A_hi, \
+            A_lo, tval, status);                                                                            \
     } while (0)
     if (dense) {
         if (src) {
@@ -615,20 +675,18 @@ int launch_rotate_out_tc(const float *H, int h_ld, const float *dirs, const floa
                          float sh_scale, float *out, cudaStream_t s) {
     if (E == 0) return FEQ_OK;
     const bool dense = dirs == nullptr;
-    const size_t row = (size_t)C * L.dim;
-    const size_t per = row + basis_area_floats(L, 1, dense);
-    if (per * 4 > kSmemBudget) return FEQ_ERR_UNSUPPORTED;
-    const int epb = pick_epb(per, 0, kSmemBudget, 8);
-    const size_t smem = per * epb * 4;
-    const int64_t grid = (E + epb - 1) / epb;
+    const int per_warp = (tc_warp_basis_floats(L, dense) + 64 * (L.dim | 1) + 3) & ~3;
+    const size_t smem = (size_t)per_warp * kTcWarps * 4;
+    if (smem > 200 * 1024) return FEQ_ERR_UNSUPPORTED;
+    const int grid = tc_grid(E, smem);
     if (dense) {
         FEQ_CUDA_TRY(cudaFuncSetAttribute(rotate_out_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        rotate_out_tc_kernel<true><<<(unsigned)grid, 256, smem, s>>>(H, h_ld, dirs, Q, dist, perm, E, C, L, M,
-                                                                     sh_scale, epb, out);
+        rotate_out_tc_kernel<true><<<(unsigned)grid, kTcWarps * 32, smem, s>>>(H, h_ld, dirs, Q, dist, perm, E, C, L,
+                                                                               M, sh_scale, per_warp, out);
     } else {
         FEQ_CUDA_TRY(cudaFuncSetAttribute(rotate_out_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        rotate_out_tc_kernel<false><<<(unsigned)grid, 256, smem, s>>>(H, h_ld, dirs, Q, dist, perm, E, C, L, M,
-                                                                      sh_scale, epb, out);
+        rotate_out_tc_kernel<false><<<(unsigned)grid, kTcWarps * 32, smem, s>>>(H, h_ld, dirs, Q, dist, perm, E, C,
+                                                                                L, M, sh_scale, per_warp, out);
     }
     FEQ_LAUNCH_CHECK();
     return FEQ_OK;

@@ -3,7 +3,7 @@
 // forward kernels (flash_eq/cuda/csrc/block_diagonal.cu:558-733).
 //
 // Formulation.  Edges are sorted by distance bin; a tile is 128 consecutive sorted
-// rows of one bin b.  For m-block m the mix is a GEMM over K = (ci, i, re/im) with the
+// rows of one bin b.  For m-block m the mix is a GEMM over K = (i, re/im, ci) with the
 // m > 0 2x2 blocks [[a, b], [-b, a]] embedded as real 2x2 sub-matrices:
 //     D_lo = A . B_m(b)^T,   D_hi = A . B_m(b+1)^T      (two TMEM accumulators)
 //     out  = D_lo + t_e (D_hi - D_lo)                     (per-row lerp, epilogue)
@@ -226,7 +226,7 @@ tc_mix_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ 
 }
 
 // B operand: per block m and bin b a (npad x kpad) K-major bf16 matrix (rows = output
-// columns n = (co, o, re/im), cols = k = (ci, i, re/im)), zero padded; the m > 0 2x2
+// columns n = (o, re/im, co), cols = k = (i, re/im, ci); channel fastest), zero padded; the m > 0 2x2
 // blocks are written as [[a, b], [-b, a]].  With a second buffer the float32 weight is
 // split hi + lo.
 __global__ void tc_relayout_b_kernel(const float *__restrict__ T, __nv_bfloat16 *__restrict__ Bhi,
@@ -245,8 +245,9 @@ __global__ void tc_relayout_b_kernel(const float *__restrict__ T, __nv_bfloat16 
         float v = 0.0f;
         const int kin = B.mult * B.n_in, kout = B.mult * B.n_out;
         if (B.n_in > 0 && B.n_out > 0 && b < nb1 && n < Cout * kout && k < Cin * kin) {
-            const int co = n / kout, rn = n - co * kout, o = rn / B.mult, oc = rn - o * B.mult;
-            const int ci = k / kin, rk = k - ci * kin, i = rk / B.mult, ic = rk - i * B.mult;
+            // channel fastest: n = (o * mult + oc) * Cout + co, k = (i * mult + ic) * Cin + ci
+            const int co = n % Cout, rn = n / Cout, o = rn / B.mult, oc = rn - o * B.mult;
+            const int ci = k % Cin, rk = k / Cin, i = rk / B.mult, ic = rk - i * B.mult;
             const float *w = T + ((int64_t)(b * Cout + co) * Cin + ci) * wdim + B.w_off;
             if (B.mult == 1) {
                 v = __ldg(w + o * B.n_in + i);
