@@ -334,11 +334,13 @@ def run_ours(args):
     n0 = lib.feq_launch_count()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier(pg)
+    torch.cuda.profiler.start()      # lets `ncu --profile-from-start off` capture just the timed steps
     t0.record()
     for _ in range(args.steps):
         step()
     t1.record()
     barrier(pg)
+    torch.cuda.profiler.stop()
     launches = lib.feq_launch_count() - n0
     clocks = clk.stop()
     ms = max_over_ranks(pg, t0.elapsed_time(t1) / args.steps)
