@@ -56,6 +56,13 @@ int launch_rotate_in_tc(const float *x, const int64_t *src, int64_t nsrc, const 
 int launch_rotate_out_tc(const float *H, int h_ld, const float *dirs, const float *Q, const float *dist,
                          const int64_t *perm, int64_t E, int C, const ReprLayout &L, const TcPosMap &M,
                          float sh_scale, float *out, cudaStream_t s);
+int launch_rot_in_stream(const float *x, const int64_t *src, int64_t nsrc, const float *edge_add, const float *dirs,
+                         const float *dist, const int64_t *perm, int64_t E, int C, const ReprLayout &L,
+                         const TcPosMap &M, int k_total, Binning bins, float sh_scale, bool split,
+                         __nv_bfloat16 *A_hi, __nv_bfloat16 *A_lo, float *tval, int32_t *status, cudaStream_t s);
+int launch_rot_out_stream(const float *H, int h_ld, const float *dirs, const float *dist, const int64_t *perm,
+                          int64_t E, int C, const ReprLayout &L, const TcPosMap &M, float sh_scale, float *out,
+                          int32_t *status, cudaStream_t s);
 
 static thread_local std::string g_last_error;
 static std::atomic<long long> g_launches{0};
@@ -364,10 +371,15 @@ static int run_edgewise_tc(const FeqEdgewiseArgs *a, const MixLayout &M, const R
     if ((rc = launch_tc_relayout_b(a->radial_table, b.B_hi, b.B_lo, a->num_bins + 1, a->c_in, a->c_out, M.wdim, T.G,
                                    T.b_total, s)) != FEQ_OK)
         return rc;
-    if ((rc = launch_rotate_in_tc(a->x, a->src, a->num_src_rows, a->edge_add, a->directions, a->P_in, a->distances,
-                                  b.perm, E, a->c_in, Li, T.in_map, T.k_total, bins, a->sh_scale, split, b.A_hi,
-                                  b.A_lo, b.tval, a->status, s)) != FEQ_OK)
-        return rc;
+    // directions given: streaming bulk-copy kernels; dense bases or unaligned rows: general kernels
+    rc = launch_rot_in_stream(a->x, a->src, a->num_src_rows, a->edge_add, a->directions, a->distances, b.perm, E,
+                              a->c_in, Li, T.in_map, T.k_total, bins, a->sh_scale, split, b.A_hi, b.A_lo, b.tval,
+                              a->status, s);
+    if (rc == FEQ_ERR_UNSUPPORTED)
+        rc = launch_rotate_in_tc(a->x, a->src, a->num_src_rows, a->edge_add, a->directions, a->P_in, a->distances,
+                                 b.perm, E, a->c_in, Li, T.in_map, T.k_total, bins, a->sh_scale, split, b.A_hi,
+                                 b.A_lo, b.tval, a->status, s);
+    if (rc != FEQ_OK) return rc;
     for (int m = 0; m < T.G.n_blocks; m++) {
         const TcBlockGeom &g = T.G.g[m];
         const int64_t b_rows = (int64_t)(a->num_bins + 1) * g.npad;
@@ -376,8 +388,12 @@ static int run_edgewise_tc(const FeqEdgewiseArgs *a, const MixLayout &M, const R
                                 T.noff[m], b.tiles, b.num_tiles, b.max_tiles, b.tval, b.H, a->status, s)) != FEQ_OK)
             return rc;
     }
-    return launch_rotate_out_tc(b.H, T.n_total, a->directions, a->Q_out, a->distances, b.perm, E, a->c_out, Lo,
-                                T.out_map, a->sh_scale, a->out, s);
+    rc = launch_rot_out_stream(b.H, T.n_total, a->directions, a->distances, b.perm, E, a->c_out, Lo, T.out_map,
+                               a->sh_scale, a->out, a->status, s);
+    if (rc == FEQ_ERR_UNSUPPORTED)
+        rc = launch_rotate_out_tc(b.H, T.n_total, a->directions, a->Q_out, a->distances, b.perm, E, a->c_out, Lo,
+                                  T.out_map, a->sh_scale, a->out, s);
+    return rc;
 }
 
 }  // namespace feq

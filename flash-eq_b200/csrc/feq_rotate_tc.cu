@@ -1,0 +1,610 @@
+// feq_rotate_tc.cu -- the rotations into and out of the edge frame that feed and
+// drain the tensor-core radial mix, for bases given by edge directions.
+//
+// Reference behaviour replaced:
+//   torch.bmm(edge_features, P) and the solid-harmonic factor   flash_eq/layers/linear.py:135-140
+//   torch.bmm(out_diag, Q.mT)                                    flash_eq/layers/linear.py:160
+//
+// One warp streams edges in sorted-bin order.  Every edge row moves as a single
+// bulk copy (cp.async.bulk, completion on an mbarrier, no multicast): the next
+// edge's input row is in flight while the current one is rotated, and the result
+// row is written back by a bulk store from shared memory.  Per edge the warp builds
+// each degree's rotation block once, with the solid-harmonic factor s^l folded in,
+// and every lane then rotates two channels with the block rows read as float4
+// broadcasts.  Rows of the block are padded to a multiple of 4 floats.
+//
+//   rotate_in : A[p][base(j) + c] = s^l (f[e][c] . D)[j]          (bf16, or bf16 hi + lo)
+//   rotate_out: out[e][c][k]      = sum_q D[k][q] s^l h[p][base(q) + c]
+//
+// The closed form of the blocks and the direction reduction are those of the basis
+// kernel (feq_rotate.cu), so the fused path and a materialised basis agree.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include "feq_internal.cuh"
+#include "feq_sm100.cuh"
+#include "_build/feq_wigner_tables.inc"
+
+namespace feq {
+namespace {
+
+constexpr float kEpsR = 1e-8f;   // get_epsilon(float32), flash_eq/utils.py:19-27
+constexpr int kRotWarps = 4;     // warps per block
+constexpr int kGroup = 32;       // edges whose per-edge scalars are computed together
+
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+        ::"r"(sm100::smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(sm100::smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void bulk_store(void *dst, const void *src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;"
+                 ::"l"(reinterpret_cast<uint64_t>(dst)), "r"(sm100::smem_u32(src)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// Per-edge trig, compact: tv = [1, cos t, sin t, cos 2t, sin 2t, ...] (2 lmax + 1 floats)
+// followed by cos(m phi), sin(m phi) for m = 0..lmax.  Same float32 steps as the basis
+// kernel's edge_trig.
+__host__ __device__ constexpr int trig_floats(int lmax) { return 2 * lmax + 1 + 2 * (lmax + 1); }
+
+__device__ __forceinline__ void edge_trig_compact(float vx, float vy, float vz, int lmax, float *tr) {
+    float nv = sqrtf(vx * vx + vy * vy + vz * vz);
+    float den = nv + kEpsR;
+    float dx = vx / den, dy = vy / den, dz = vz / den;
+    float n = sqrtf(dy * dy + dx * dx);
+    float ax0 = -dy / (n + kEpsR), ax1 = dx / (n + kEpsR);
+    float theta = acosf(fminf(fmaxf(dz, -1.0f + kEpsR), 1.0f - kEpsR));
+    float rho = sqrtf(ax0 * ax0 + ax1 * ax1);
+    float th = theta * rho;
+    float c1p = 1.0f, s1p = 0.0f;
+    if (rho > 0.0f) {
+        c1p = ax0 / rho;
+        s1p = ax1 / rho;
+    }
+    float c1t, s1t;
+    sincosf(th, &s1t, &c1t);
+    float *tv = tr, *cp = tr + 2 * lmax + 1, *sp = cp + lmax + 1;
+    tv[0] = 1.0f;
+    cp[0] = 1.0f;
+    sp[0] = 0.0f;
+    float ct = 1.0f, st = 0.0f, c = 1.0f, s = 0.0f;
+    for (int m = 1; m <= lmax; m++) {
+        float nct = ct * c1t - st * s1t, nst = st * c1t + ct * s1t;
+        float nc = c * c1p - s * s1p, ns = s * c1p + c * s1p;
+        ct = nct; st = nst; c = nc; s = ns;
+        tv[2 * m - 1] = ct;
+        tv[2 * m] = st;
+        cp[m] = c;
+        sp[m] = s;
+    }
+}
+
+__host__ __device__ constexpr int pad4(int n) { return (n + 3) & ~3; }
+
+// Float offset of degree-slot u's padded block (N rows of pad4(N) floats).
+__host__ __device__ inline int rblock_floats(const ReprLayout &L) {
+    int t = 0;
+    for (int u = 0; u < L.n_unique; u++) {
+        const int n = 2 * L.unique_l[u] + 1;
+        t += n * pad4(n);
+    }
+    return t;
+}
+
+// M_l(theta') = sum_q T_l[:, :, q] tv[q] for one degree, then the padded rotation block
+//   kIn : R[q][o] = s^l D[q][o]      (input side: y[o] = sum_q f[q] R[q][o])
+//   !kIn: R[q][o] = s^l D[o][q]      (output side: y[o] = sum_q h[q] R[q][o])
+// D = R(phi) M R(phi)^T as in the basis kernel.  Whole warp; ends with __syncwarp.
+template <int N, bool kIn>
+__device__ __forceinline__ void build_rblock(const float *__restrict__ tr, int lmax, float sl, float *__restrict__ m_s,
+                                             float *__restrict__ r_s, int lane) {
+    constexpr int l = (N - 1) / 2, P = pad4(N);
+    const float *tv = tr, *cp = tr + 2 * lmax + 1, *sp = cp + lmax + 1;
+    const float *tab = feq_wt_data + feq_wt_offset[l];
+    for (int idx = lane; idx < N * N; idx += 32) {
+        const float *t = tab + idx * N;
+        float acc = 0.0f;
+#pragma unroll
+        for (int q = 0; q < N; q++) acc = fmaf(__ldg(t + q), tv[q], acc);
+        m_s[idx] = acc;
+    }
+    __syncwarp();
+    for (int idx = lane; idx < N * N; idx += 32) {
+        const int a = idx / N, b = idx - a * N;
+        const int ma = a < l ? l - a : a - l, mb = b < l ? l - b : b - l;
+        const float ca = cp[ma], cb = cp[mb];
+        const float sa = a < l ? sp[ma] : -sp[ma];
+        const float sb = b < l ? sp[mb] : -sp[mb];
+        float v = ca * cb * m_s[a * N + b];
+        if (mb) v = fmaf(ca * sb, m_s[a * N + (2 * l - b)], v);
+        if (ma) v = fmaf(sa * cb, m_s[(2 * l - a) * N + b], v);
+        if (ma && mb) v = fmaf(sa * sb, m_s[(2 * l - a) * N + (2 * l - b)], v);
+        if (kIn) r_s[a * P + b] = v * sl;
+        else r_s[b * P + a] = v * sl;
+    }
+    __syncwarp();
+}
+
+// Runtime-degree variant of build_rblock (degrees above 4).
+template <bool kIn>
+__device__ void build_rblock_any(int l, const float *__restrict__ tr, int lmax, float sl, float *__restrict__ m_s,
+                                 float *__restrict__ r_s, int lane) {
+    const int N = 2 * l + 1, P = pad4(N);
+    const float *tv = tr, *cp = tr + 2 * lmax + 1, *sp = cp + lmax + 1;
+    const float *tab = feq_wt_data + feq_wt_offset[l];
+    for (int idx = lane; idx < N * N; idx += 32) {
+        const float *t = tab + idx * N;
+        float acc = 0.0f;
+        for (int q = 0; q < N; q++) acc = fmaf(__ldg(t + q), tv[q], acc);
+        m_s[idx] = acc;
+    }
+    __syncwarp();
+    for (int idx = lane; idx < N * N; idx += 32) {
+        const int a = idx / N, b = idx - a * N;
+        const int ma = a < l ? l - a : a - l, mb = b < l ? l - b : b - l;
+        const float ca = cp[ma], cb = cp[mb];
+        const float sa = a < l ? sp[ma] : -sp[ma];
+        const float sb = b < l ? sp[mb] : -sp[mb];
+        float v = ca * cb * m_s[a * N + b];
+        if (mb) v = fmaf(ca * sb, m_s[a * N + (2 * l - b)], v);
+        if (ma) v = fmaf(sa * cb, m_s[(2 * l - a) * N + b], v);
+        if (ma && mb) v = fmaf(sa * sb, m_s[(2 * l - a) * N + (2 * l - b)], v);
+        if (kIn) r_s[a * P + b] = v * sl;
+        else r_s[b * P + a] = v * sl;
+    }
+    __syncwarp();
+}
+
+// All degree blocks of one edge.  rdoff[u] = float offset of slot u's padded block.
+template <bool kIn>
+__device__ __forceinline__ void build_all_rblocks(const ReprLayout &L, const int16_t *rdoff, const float *tr, float s,
+                                                  float *m_s, float *r_s, int lane) {
+    for (int u = 0; u < L.n_unique; u++) {
+        const int l = L.unique_l[u];
+        const float sl = ipowf(s, l);
+        float *R = r_s + rdoff[u];
+        switch (l) {
+            case 0: build_rblock<1, kIn>(tr, L.lmax, sl, m_s, R, lane); break;
+            case 1: build_rblock<3, kIn>(tr, L.lmax, sl, m_s, R, lane); break;
+            case 2: build_rblock<5, kIn>(tr, L.lmax, sl, m_s, R, lane); break;
+            case 3: build_rblock<7, kIn>(tr, L.lmax, sl, m_s, R, lane); break;
+            case 4: build_rblock<9, kIn>(tr, L.lmax, sl, m_s, R, lane); break;
+            default: build_rblock_any<kIn>(l, tr, L.lmax, sl, m_s, R, lane);
+        }
+    }
+}
+
+// y[o] = sum_q x[q] R[q][o] for two channels at once; x from get(q) -> float2, rows of R
+// read as float4 broadcasts, every output emitted as emit(o, y_ch0, y_ch1).
+template <int N, typename Get, typename Emit>
+__device__ __forceinline__ void rotate_pair(const float *__restrict__ R, Get get, Emit emit) {
+    constexpr int P = pad4(N);
+    float2 x[N];
+#pragma unroll
+    for (int q = 0; q < N; q++) x[q] = get(q);
+    float a0[P], a1[P];
+#pragma unroll
+    for (int o = 0; o < P; o++) a0[o] = a1[o] = 0.0f;
+#pragma unroll
+    for (int q = 0; q < N; q++) {
+        const float4 *row = reinterpret_cast<const float4 *>(R + q * P);
+#pragma unroll
+        for (int o4 = 0; o4 < P / 4; o4++) {
+            const float4 r = row[o4];
+            a0[4 * o4 + 0] = fmaf(x[q].x, r.x, a0[4 * o4 + 0]);
+            a1[4 * o4 + 0] = fmaf(x[q].y, r.x, a1[4 * o4 + 0]);
+            a0[4 * o4 + 1] = fmaf(x[q].x, r.y, a0[4 * o4 + 1]);
+            a1[4 * o4 + 1] = fmaf(x[q].y, r.y, a1[4 * o4 + 1]);
+            a0[4 * o4 + 2] = fmaf(x[q].x, r.z, a0[4 * o4 + 2]);
+            a1[4 * o4 + 2] = fmaf(x[q].y, r.z, a1[4 * o4 + 2]);
+            a0[4 * o4 + 3] = fmaf(x[q].x, r.w, a0[4 * o4 + 3]);
+            a1[4 * o4 + 3] = fmaf(x[q].y, r.w, a1[4 * o4 + 3]);
+        }
+    }
+#pragma unroll
+    for (int o = 0; o < N; o++) emit(o, a0[o], a1[o]);
+}
+
+template <typename Get, typename Emit>
+__device__ __forceinline__ void rotate_pair_any(int l, const float *__restrict__ R, Get get, Emit emit) {
+    switch (l) {
+        case 0: rotate_pair<1>(R, get, emit); break;
+        case 1: rotate_pair<3>(R, get, emit); break;
+        case 2: rotate_pair<5>(R, get, emit); break;
+        case 3: rotate_pair<7>(R, get, emit); break;
+        case 4: rotate_pair<9>(R, get, emit); break;
+        default: {
+            const int N = 2 * l + 1, P = pad4(N);
+            for (int o = 0; o < N; o++) {
+                float y0 = 0.0f, y1 = 0.0f;
+                for (int q = 0; q < N; q++) {
+                    const float2 v = get(q);
+                    const float r = R[q * P + o];
+                    y0 = fmaf(v.x, r, y0);
+                    y1 = fmaf(v.y, r, y1);
+                }
+                emit(o, y0, y1);
+            }
+        }
+    }
+}
+
+// Shared per-warp scratch, in floats: the group's trig, one M block, the rotation blocks.
+struct RotScratch {
+    int trig, mblk, rblk;      // float counts
+    __host__ __device__ int total() const { return trig + mblk + rblk; }
+};
+__host__ __device__ inline RotScratch rot_scratch(const ReprLayout &L) {
+    RotScratch s;
+    s.trig = pad4(kGroup * trig_floats(L.lmax));
+    s.mblk = pad4((2 * L.lmax + 1) * (2 * L.lmax + 1));
+    s.rblk = pad4(rblock_floats(L));
+    return s;
+}
+
+__device__ __forceinline__ void rblock_offsets(const ReprLayout &L, int16_t *rdoff) {
+    int t = 0;
+    for (int u = 0; u < L.n_unique; u++) {
+        rdoff[u] = (int16_t)t;
+        const int n = 2 * L.unique_l[u] + 1;
+        t += n * pad4(n);
+    }
+}
+
+__device__ __forceinline__ void copy_layout(const ReprLayout &src, ReprLayout &dst) {
+    const int *s = reinterpret_cast<const int *>(&src);
+    int *d = reinterpret_cast<int *>(&dst);
+    for (int i = threadIdx.x; i < (int)(sizeof(ReprLayout) / 4); i += blockDim.x) d[i] = s[i];
+}
+
+// Per-block shared state in front of the per-warp areas.
+struct RotShared {
+    ReprLayout L;
+    int16_t rdoff[kMaxL + 1];
+    uint64_t bar[kRotWarps][2];
+    int abort_flag;
+};
+
+// Per-warp dynamic shared memory (floats): in[2] rows, the out row, scratch.
+struct RotWarpLayout {
+    int in_row, out_row, scratch;   // floats, each a multiple of 4
+    __host__ __device__ int total() const { return 2 * in_row + out_row + scratch; }
+};
+
+// Bounded wait for row buffer `b`; false on time-out (status 2, the CTA aborts).
+__device__ __forceinline__ bool wait_row(RotShared &S, int w, int b, uint32_t &phase_bits, int32_t *status) {
+    const bool ok = sm100::mbar_wait(&S.bar[w][b], (phase_bits >> b) & 1u, &S.abort_flag);
+    if (ok) phase_bits ^= 1u << b;
+    else set_status(status, 2);
+    return ok;
+}
+
+// A[p][base_std(k) + c] = s_e^l(k) (f[e][c] . D_e)[k] as bf16 (hi, and lo = f - hi when kSplit);
+// f[e] = x[src[e]] (kGather) or x[e], plus edge_add[e] when given; tval[p] = t_e.
+template <bool kGather, bool kSplit>
+__global__ void __launch_bounds__(kRotWarps * 32)
+rot_in_kernel(const float *__restrict__ x, const int64_t *__restrict__ src, int64_t nsrc,
+              const float *__restrict__ edge_add, const float *__restrict__ dirs, const float *__restrict__ dist,
+              const int64_t *__restrict__ perm, int64_t E, int C, const __grid_constant__ ReprLayout Lp,
+              const __grid_constant__ TcPosMap Mp, int k_total, Binning bins, float sh_scale, RotWarpLayout WL,
+              __nv_bfloat16 *__restrict__ A_hi, __nv_bfloat16 *__restrict__ A_lo, float *__restrict__ tval,
+              int32_t *status) {
+    extern __shared__ __align__(128) float dsm[];
+    __shared__ RotShared S;
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    copy_layout(Lp, S.L);
+    if (threadIdx.x == 0) {
+        S.abort_flag = 0;
+        for (int i = 0; i < kRotWarps; i++) {
+            sm100::mbar_init(&S.bar[i][0], 1);
+            sm100::mbar_init(&S.bar[i][1], 1);
+        }
+        sm100::fence_mbar_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) rblock_offsets(S.L, S.rdoff);
+    const ReprLayout &L = S.L;
+    const int d = L.dim, row = C * d;
+    int32_t *bstd = reinterpret_cast<int32_t *>(dsm);
+    for (int i = threadIdx.x; i < d; i += blockDim.x) bstd[i] = Mp.base_std[i];
+    __syncthreads();
+
+    float *ws = dsm + pad4(d) + (size_t)w * WL.total();
+    __nv_bfloat16 *ahi = reinterpret_cast<__nv_bfloat16 *>(ws + 2 * WL.in_row);
+    __nv_bfloat16 *alo = ahi + k_total;
+    const RotScratch SC = rot_scratch(L);
+    float *trig = ws + 2 * WL.in_row + WL.out_row;
+    float *m_s = trig + SC.trig, *r_s = m_s + SC.mblk;
+    const int TF = trig_floats(L.lmax);
+    const uint32_t row_bytes = (uint32_t)row * 4u, a_bytes = (uint32_t)k_total * 2u;
+    uint32_t phase_bits = 0;
+    int pending = 0;   // bit b: a bulk load into buffer b is in flight
+    bool alive = true;
+    // padding columns of the A row are never written by the rotation: zero them once
+    for (int i = lane; i < (kSplit ? 2 : 1) * k_total / 2; i += 32) reinterpret_cast<uint32_t *>(ahi)[i] = 0u;
+
+    for (int64_t g0 = ((int64_t)blockIdx.x * kRotWarps + w) * kGroup; alive && g0 < E;
+         g0 += (int64_t)gridDim.x * kRotWarps * kGroup) {
+        const int ng = (int)min64(kGroup, E - g0);
+        int64_t e_l = 0, xr_l = -1;
+        float s_l = 0.0f;
+        if (lane < ng) {
+            const int64_t p = g0 + lane;
+            e_l = perm[p];
+            const float dd = dist[e_l];
+            s_l = dd / (dd + sh_scale);
+            int lo;
+            float t;
+            bin_of(dd, bins, lo, t);
+            tval[p] = t;
+            edge_trig_compact(dirs[e_l * 3], dirs[e_l * 3 + 1], dirs[e_l * 3 + 2], L.lmax, trig + lane * TF);
+            xr_l = e_l;
+            if (kGather) {
+                xr_l = src[e_l];
+                if (xr_l < 0 || xr_l >= nsrc) {
+                    set_status(status, 1);
+                    xr_l = -1;
+                }
+            }
+        }
+        __syncwarp();
+        auto issue = [&](int j) {
+            const int64_t xr = __shfl_sync(0xffffffffu, xr_l, j);
+            const int b = j & 1;
+            if (xr >= 0 && lane == 0) {
+                fence_async_smem();
+                sm100::mbar_arrive_expect_tx(&S.bar[w][b], row_bytes);
+                bulk_load(ws + b * WL.in_row, x + xr * (int64_t)row, row_bytes, &S.bar[w][b]);
+            }
+            if (xr >= 0) pending |= 1 << b;
+        };
+        issue(0);
+        for (int j = 0; j < ng; j++) {
+            const int64_t e = __shfl_sync(0xffffffffu, e_l, j);
+            const int64_t xr = __shfl_sync(0xffffffffu, xr_l, j);
+            const float s = __shfl_sync(0xffffffffu, s_l, j);
+            const int64_t p = g0 + j;
+            const int b = j & 1;
+            if (j + 1 < ng) issue(j + 1);
+            build_all_rblocks<true>(L, S.rdoff, trig + j * TF, s, m_s, r_s, lane);
+            float *fb = ws + b * WL.in_row;
+            if (xr >= 0) {
+                if (!wait_row(S, w, b, phase_bits, status)) {
+                    alive = false;
+                    break;
+                }
+                pending &= ~(1 << b);
+            } else {
+                for (int i = lane; i < row; i += 32) fb[i] = 0.0f;
+            }
+            if (edge_add) {
+                const float4 *ea = reinterpret_cast<const float4 *>(edge_add + e * (int64_t)row);
+                float4 *f4 = reinterpret_cast<float4 *>(fb);
+                for (int i = lane; i < row / 4; i += 32) {
+                    const float4 a = __ldg(ea + i);
+                    float4 v = f4[i];
+                    v.x += a.x; v.y += a.y; v.z += a.z; v.w += a.w;
+                    f4[i] = v;
+                }
+            }
+            if (lane == 0) bulk_wait_read0();   // the previous A row has left shared memory
+            __syncwarp();
+            for (int c = 2 * lane; c < C; c += 64) {
+                const float *f0 = fb + c * d, *f1 = f0 + d;
+                for (int r = 0; r < L.n_irreps; r++) {
+                    const int l = L.irrep_l[r], off = L.irrep_off[r];
+                    const float *R = r_s + S.rdoff[L.irrep_slot[r]];
+                    const int32_t *bo = bstd + off;
+                    rotate_pair_any(
+                        l, R, [&](int q) { return make_float2(f0[off + q], f1[off + q]); },
+                        [&](int o, float y0, float y1) {
+                            const int bcol = bo[o];
+                            if (bcol < 0) return;
+                            const __nv_bfloat162 hi = __floats2bfloat162_rn(y0, y1);
+                            *reinterpret_cast<__nv_bfloat162 *>(ahi + bcol + c) = hi;
+                            if (kSplit) {
+                                const float2 hf = __bfloat1622float2(hi);
+                                *reinterpret_cast<__nv_bfloat162 *>(alo + bcol + c) =
+                                    __floats2bfloat162_rn(y0 - hf.x, y1 - hf.y);
+                            }
+                        });
+                }
+            }
+            fence_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                bulk_store(A_hi + p * (int64_t)k_total, ahi, a_bytes);
+                if (kSplit) bulk_store(A_lo + p * (int64_t)k_total, alo, a_bytes);
+                bulk_commit();
+            }
+        }
+    }
+    // drain: loads still in flight (only after an abort) and the last stores
+    for (int b = 0; b < 2; b++)
+        if (pending & (1 << b)) sm100::mbar_wait_drain(&S.bar[w][b], (phase_bits >> b) & 1u);
+    if (lane == 0) bulk_wait0();
+}
+
+// out[e][c][k] = sum_q D_e[k][q] s_e^l h[q][c], h[q][c] = H[p][base_std(q) + c] (0 where
+// base_std < 0: output blocks that receive no input).
+__global__ void __launch_bounds__(kRotWarps * 32)
+rot_out_kernel(const float *__restrict__ H, int h_ld, const float *__restrict__ dirs, const float *__restrict__ dist,
+               const int64_t *__restrict__ perm, int64_t E, int C, const __grid_constant__ ReprLayout Lp,
+               const __grid_constant__ TcPosMap Mp, float sh_scale, RotWarpLayout WL, float *__restrict__ out,
+               int32_t *status) {
+    extern __shared__ __align__(128) float dsm[];
+    __shared__ RotShared S;
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    copy_layout(Lp, S.L);
+    if (threadIdx.x == 0) {
+        S.abort_flag = 0;
+        for (int i = 0; i < kRotWarps; i++) {
+            sm100::mbar_init(&S.bar[i][0], 1);
+            sm100::mbar_init(&S.bar[i][1], 1);
+        }
+        sm100::fence_mbar_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) rblock_offsets(S.L, S.rdoff);
+    const ReprLayout &L = S.L;
+    const int d = L.dim, row = C * d;
+    int32_t *bstd = reinterpret_cast<int32_t *>(dsm);
+    for (int i = threadIdx.x; i < d; i += blockDim.x) bstd[i] = Mp.base_std[i];
+    __syncthreads();
+
+    float *ws = dsm + pad4(d) + (size_t)w * WL.total();
+    float *ob = ws + 2 * WL.in_row;
+    const RotScratch SC = rot_scratch(L);
+    float *trig = ob + WL.out_row;
+    float *m_s = trig + SC.trig, *r_s = m_s + SC.mblk;
+    const int TF = trig_floats(L.lmax);
+    const uint32_t h_bytes = (uint32_t)h_ld * 4u, o_bytes = (uint32_t)row * 4u;
+    uint32_t phase_bits = 0;
+    int pending = 0;
+    bool alive = true;
+
+    for (int64_t g0 = ((int64_t)blockIdx.x * kRotWarps + w) * kGroup; alive && g0 < E;
+         g0 += (int64_t)gridDim.x * kRotWarps * kGroup) {
+        const int ng = (int)min64(kGroup, E - g0);
+        int64_t e_l = 0;
+        float s_l = 0.0f;
+        if (lane < ng) {
+            e_l = perm[g0 + lane];
+            const float dd = dist[e_l];
+            s_l = dd / (dd + sh_scale);
+            edge_trig_compact(dirs[e_l * 3], dirs[e_l * 3 + 1], dirs[e_l * 3 + 2], L.lmax, trig + lane * TF);
+        }
+        __syncwarp();
+        auto issue = [&](int j) {
+            const int b = j & 1;
+            if (lane == 0) {
+                fence_async_smem();
+                sm100::mbar_arrive_expect_tx(&S.bar[w][b], h_bytes);
+                bulk_load(ws + b * WL.in_row, H + (g0 + j) * (int64_t)h_ld, h_bytes, &S.bar[w][b]);
+            }
+            pending |= 1 << b;
+        };
+        issue(0);
+        for (int j = 0; j < ng; j++) {
+            const int64_t e = __shfl_sync(0xffffffffu, e_l, j);
+            const float s = __shfl_sync(0xffffffffu, s_l, j);
+            const int b = j & 1;
+            if (j + 1 < ng) issue(j + 1);
+            build_all_rblocks<false>(L, S.rdoff, trig + j * TF, s, m_s, r_s, lane);
+            if (!wait_row(S, w, b, phase_bits, status)) {
+                alive = false;
+                break;
+            }
+            pending &= ~(1 << b);
+            const float *hb = ws + b * WL.in_row;
+            if (lane == 0) bulk_wait_read0();   // the previous output row has left shared memory
+            __syncwarp();
+            for (int c = 2 * lane; c < C; c += 64) {
+                float *o0 = ob + c * d, *o1 = o0 + d;
+                for (int r = 0; r < L.n_irreps; r++) {
+                    const int l = L.irrep_l[r], off = L.irrep_off[r];
+                    const float *R = r_s + S.rdoff[L.irrep_slot[r]];
+                    const int32_t *bi = bstd + off;
+                    rotate_pair_any(
+                        l, R,
+                        [&](int q) {
+                            const int bcol = bi[q];
+                            return bcol < 0 ? make_float2(0.0f, 0.0f)
+                                            : *reinterpret_cast<const float2 *>(hb + bcol + c);
+                        },
+                        [&](int o, float y0, float y1) {
+                            o0[off + o] = y0;
+                            o1[off + o] = y1;
+                        });
+                }
+            }
+            fence_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                bulk_store(out + e * (int64_t)row, ob, o_bytes);
+                bulk_commit();
+            }
+        }
+    }
+    for (int b = 0; b < 2; b++)
+        if (pending & (1 << b)) sm100::mbar_wait_drain(&S.bar[w][b], (phase_bits >> b) & 1u);
+    if (lane == 0) bulk_wait0();
+}
+
+}  // namespace
+
+static bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+static int rot_grid(const void *kernel, size_t smem, int64_t E) {
+    int dev = 0, sms = 148, per_sm = 1;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kRotWarps * 32, smem) != cudaSuccess ||
+        per_sm < 1)
+        per_sm = 1;
+    const int64_t want = (E + kRotWarps * kGroup - 1) / (kRotWarps * kGroup);
+    return (int)std::max<int64_t>(1, min64(want, (int64_t)sms * per_sm));
+}
+
+// Streaming rotation into the A matrix of the tensor-core mix.  Returns
+// FEQ_ERR_UNSUPPORTED (nothing launched) when the shapes or alignments do not allow
+// whole-row bulk copies; the caller then uses the general kernels.
+int launch_rot_in_stream(const float *x, const int64_t *src, int64_t nsrc, const float *edge_add, const float *dirs,
+                         const float *dist, const int64_t *perm, int64_t E, int C, const ReprLayout &L,
+                         const TcPosMap &M, int k_total, Binning bins, float sh_scale, bool split,
+                         __nv_bfloat16 *A_hi, __nv_bfloat16 *A_lo, float *tval, int32_t *status, cudaStream_t s) {
+    if (E == 0) return FEQ_OK;
+    if (!dirs || (C & 1) || ((int64_t)C * L.dim) % 4 || k_total % 8 || !aligned16(x) ||
+        (edge_add && !aligned16(edge_add)) || !aligned16(A_hi) || (split && !aligned16(A_lo)))
+        return FEQ_ERR_UNSUPPORTED;
+    RotWarpLayout WL;
+    WL.in_row = pad4(C * L.dim);
+    WL.out_row = (split ? 2 : 1) * k_total / 2;
+    WL.scratch = rot_scratch(L).total();
+    const size_t smem = ((size_t)pad4(L.dim) + (size_t)kRotWarps * WL.total()) * 4;
+    if (smem + sizeof(RotShared) > 200 * 1024) return FEQ_ERR_UNSUPPORTED;
+#define FEQ_ROT_IN(G, S)                                                                                        \
+    do {                                                                                                        \
+        auto k = rot_in_kernel<G, S>;                                                                           \
+        FEQ_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));          \
+        const int grid = rot_grid((const void *)k, smem, E);                                                    \
+        k<<<grid, kRotWarps * 32, smem, s>>>(x, src, nsrc, edge_add, dirs, dist, perm, E, C, L, M, k_total, bins, \
+                                             sh_scale, WL, A_hi, A_lo, tval, status);                           \
+    } while (0)
+    if (src) {
+        if (split) FEQ_ROT_IN(true, true); else FEQ_ROT_IN(true, false);
+    } else {
+        if (split) FEQ_ROT_IN(false, true); else FEQ_ROT_IN(false, false);
+    }
+#undef FEQ_ROT_IN
+    FEQ_LAUNCH_CHECK();
+    return FEQ_OK;
+}
+
+// Streaming rotation of the mix result back out of the edge frame.
+int launch_rot_out_stream(const float *H, int h_ld, const float *dirs, const float *dist, const int64_t *perm,
+                          int64_t E, int C, const ReprLayout &L, const TcPosMap &M, float sh_scale, float *out,
+                          int32_t *status, cudaStream_t s) {
+    if (E == 0) return FEQ_OK;
+    if (!dirs || (C & 1) || ((int64_t)C * L.dim) % 4 || h_ld % 4 || !aligned16(H) || !aligned16(out))
+        return FEQ_ERR_UNSUPPORTED;
+    RotWarpLayout WL;
+    WL.in_row = pad4(h_ld);
+    WL.out_row = pad4(C * L.dim);
+    WL.scratch = rot_scratch(L).total();
+    const size_t smem = ((size_t)pad4(L.dim) + (size_t)kRotWarps * WL.total()) * 4;
+    if (smem + sizeof(RotShared) > 200 * 1024) return FEQ_ERR_UNSUPPORTED;
+    FEQ_CUDA_TRY(cudaFuncSetAttribute(rot_out_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    const int grid = rot_grid((const void *)rot_out_kernel, smem, E);
+    rot_out_kernel<<<grid, kRotWarps * 32, smem, s>>>(H, h_ld, dirs, dist, perm, E, C, L, M, sh_scale, WL, out,
+                                                      status);
+    FEQ_LAUNCH_CHECK();
+    return FEQ_OK;
+}
+
+}  // namespace feq
