@@ -5,10 +5,12 @@
 //   torch.bmm(edge_features, P) and the solid-harmonic factor   flash_eq/layers/linear.py:135-140
 //   torch.bmm(out_diag, Q.mT)                                    flash_eq/layers/linear.py:160
 //
-// One warp streams edges in sorted-bin order.  Every edge row moves as a single
+// One warp streams edges in sorted-bin order.  Every input row moves as a single
 // bulk copy (cp.async.bulk, completion on an mbarrier, no multicast): the next
-// edge's input row is in flight while the current one is rotated, and the result
-// row is written back by a bulk store from shared memory.  Per edge the warp builds
+// edge's row is in flight while the current one is rotated.  rotate_in writes its
+// bf16 columns straight to HBM (lanes hold consecutive channel pairs, so each store
+// covers 128 contiguous bytes); rotate_out stages the output row in shared memory
+// and writes it back with one bulk store.  Per edge the warp builds
 // each degree's rotation block once, with the solid-harmonic factor s^l folded in,
 // and every lane then rotates two channels with the block rows read as float4
 // broadcasts.  Rows of the block are padded to a multiple of 4 floats.
@@ -31,6 +33,7 @@ namespace {
 constexpr float kEpsR = 1e-8f;   // get_epsilon(float32), flash_eq/utils.py:19-27
 constexpr int kRotWarps = 4;     // warps per block
 constexpr int kGroup = 32;       // edges whose per-edge scalars are computed together
+constexpr int kWtcKUpTo4[5] = FEQ_WTC_K_UPTO4;   // terms per M entry, degrees 0..4
 
 __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
     asm volatile(
@@ -103,18 +106,26 @@ __host__ __device__ inline int rblock_floats(const ReprLayout &L) {
 template <int N, bool kIn>
 __device__ __forceinline__ void build_rblock(const float *__restrict__ tr, int lmax, float sl, float *__restrict__ m_s,
                                              float *__restrict__ r_s, int lane) {
-    constexpr int l = (N - 1) / 2, P = pad4(N);
+    constexpr int l = (N - 1) / 2, P = pad4(N), K = l / 2 + 1, kRounds = (N * N + 31) / 32;
+    static_assert(kWtcKUpTo4[l] == K, "compressed Wigner table layout");
     const float *tv = tr, *cp = tr + 2 * lmax + 1, *sp = cp + lmax + 1;
-    const float *tab = feq_wt_data + feq_wt_offset[l];
-    for (int idx = lane; idx < N * N; idx += 32) {
-        const float *t = tab + idx * N;
-        float acc = 0.0f;
+    const float *coef = feq_wtc_coef + feq_wtc_offset[l];
+    const unsigned char *term = feq_wtc_term + feq_wtc_offset[l];
 #pragma unroll
-        for (int q = 0; q < N; q++) acc = fmaf(__ldg(t + q), tv[q], acc);
-        m_s[idx] = acc;
+    for (int rd = 0; rd < kRounds; rd++) {
+        const int idx = lane + 32 * rd;
+        if (idx < N * N) {
+            float acc = 0.0f;
+#pragma unroll
+            for (int k = 0; k < K; k++) acc = fmaf(__ldg(coef + idx * K + k), tv[__ldg(term + idx * K + k)], acc);
+            m_s[idx] = acc;
+        }
     }
     __syncwarp();
-    for (int idx = lane; idx < N * N; idx += 32) {
+#pragma unroll
+    for (int rd = 0; rd < kRounds; rd++) {
+        const int idx = lane + 32 * rd;
+        if (idx >= N * N) break;
         const int a = idx / N, b = idx - a * N;
         const int ma = a < l ? l - a : a - l, mb = b < l ? l - b : b - l;
         const float ca = cp[ma], cb = cp[mb];
@@ -134,13 +145,13 @@ __device__ __forceinline__ void build_rblock(const float *__restrict__ tr, int l
 template <bool kIn>
 __device__ void build_rblock_any(int l, const float *__restrict__ tr, int lmax, float sl, float *__restrict__ m_s,
                                  float *__restrict__ r_s, int lane) {
-    const int N = 2 * l + 1, P = pad4(N);
+    const int N = 2 * l + 1, P = pad4(N), K = feq_wtc_k[l];
     const float *tv = tr, *cp = tr + 2 * lmax + 1, *sp = cp + lmax + 1;
-    const float *tab = feq_wt_data + feq_wt_offset[l];
+    const float *coef = feq_wtc_coef + feq_wtc_offset[l];
+    const unsigned char *term = feq_wtc_term + feq_wtc_offset[l];
     for (int idx = lane; idx < N * N; idx += 32) {
-        const float *t = tab + idx * N;
         float acc = 0.0f;
-        for (int q = 0; q < N; q++) acc = fmaf(__ldg(t + q), tv[q], acc);
+        for (int k = 0; k < K; k++) acc = fmaf(__ldg(coef + idx * K + k), tv[__ldg(term + idx * K + k)], acc);
         m_s[idx] = acc;
     }
     __syncwarp();
@@ -196,14 +207,14 @@ __device__ __forceinline__ void rotate_pair(const float *__restrict__ R, Get get
 #pragma unroll
         for (int o4 = 0; o4 < P / 4; o4++) {
             const float4 r = row[o4];
-            a0[4 * o4 + 0] = fmaf(x[q].x, r.x, a0[4 * o4 + 0]);
-            a1[4 * o4 + 0] = fmaf(x[q].y, r.x, a1[4 * o4 + 0]);
-            a0[4 * o4 + 1] = fmaf(x[q].x, r.y, a0[4 * o4 + 1]);
-            a1[4 * o4 + 1] = fmaf(x[q].y, r.y, a1[4 * o4 + 1]);
-            a0[4 * o4 + 2] = fmaf(x[q].x, r.z, a0[4 * o4 + 2]);
-            a1[4 * o4 + 2] = fmaf(x[q].y, r.z, a1[4 * o4 + 2]);
-            a0[4 * o4 + 3] = fmaf(x[q].x, r.w, a0[4 * o4 + 3]);
-            a1[4 * o4 + 3] = fmaf(x[q].y, r.w, a1[4 * o4 + 3]);
+            const float rv[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                if (4 * o4 + i < N) {   // padding columns are never read back
+                    a0[4 * o4 + i] = fmaf(x[q].x, rv[i], a0[4 * o4 + i]);
+                    a1[4 * o4 + i] = fmaf(x[q].y, rv[i], a1[4 * o4 + i]);
+                }
+            }
         }
     }
 #pragma unroll
@@ -315,18 +326,14 @@ rot_in_kernel(const float *__restrict__ x, const int64_t *__restrict__ src, int6
     __syncthreads();
 
     float *ws = dsm + pad4(d) + (size_t)w * WL.total();
-    __nv_bfloat16 *ahi = reinterpret_cast<__nv_bfloat16 *>(ws + 2 * WL.in_row);
-    __nv_bfloat16 *alo = ahi + k_total;
     const RotScratch SC = rot_scratch(L);
     float *trig = ws + 2 * WL.in_row + WL.out_row;
     float *m_s = trig + SC.trig, *r_s = m_s + SC.mblk;
     const int TF = trig_floats(L.lmax);
-    const uint32_t row_bytes = (uint32_t)row * 4u, a_bytes = (uint32_t)k_total * 2u;
+    const uint32_t row_bytes = (uint32_t)row * 4u;
     uint32_t phase_bits = 0;
     int pending = 0;   // bit b: a bulk load into buffer b is in flight
     bool alive = true;
-    // padding columns of the A row are never written by the rotation: zero them once
-    for (int i = lane; i < (kSplit ? 2 : 1) * k_total / 2; i += 32) reinterpret_cast<uint32_t *>(ahi)[i] = 0u;
 
     for (int64_t g0 = ((int64_t)blockIdx.x * kRotWarps + w) * kGroup; alive && g0 < E;
          g0 += (int64_t)gridDim.x * kRotWarps * kGroup) {
@@ -392,8 +399,15 @@ rot_in_kernel(const float *__restrict__ x, const int64_t *__restrict__ src, int6
                     f4[i] = v;
                 }
             }
-            if (lane == 0) bulk_wait_read0();   // the previous A row has left shared memory
             __syncwarp();
+            __nv_bfloat16 *ah = A_hi + p * (int64_t)k_total;
+            __nv_bfloat16 *al = kSplit ? A_lo + p * (int64_t)k_total : nullptr;
+            for (int r = 0; r < Mp.n_pad; r++)      // K padding of the m-blocks (zero columns)
+                for (int i = Mp.pad_lo[r] + 2 * lane; i < Mp.pad_hi[r]; i += 64) {
+                    *reinterpret_cast<uint32_t *>(ah + i) = 0u;
+                    if (kSplit) *reinterpret_cast<uint32_t *>(al + i) = 0u;
+                }
+            // lanes hold consecutive channel pairs: every column store is 128 contiguous bytes
             for (int c = 2 * lane; c < C; c += 64) {
                 const float *f0 = fb + c * d, *f1 = f0 + d;
                 for (int r = 0; r < L.n_irreps; r++) {
@@ -406,22 +420,16 @@ rot_in_kernel(const float *__restrict__ x, const int64_t *__restrict__ src, int6
                             const int bcol = bo[o];
                             if (bcol < 0) return;
                             const __nv_bfloat162 hi = __floats2bfloat162_rn(y0, y1);
-                            *reinterpret_cast<__nv_bfloat162 *>(ahi + bcol + c) = hi;
+                            *reinterpret_cast<__nv_bfloat162 *>(ah + bcol + c) = hi;
                             if (kSplit) {
                                 const float2 hf = __bfloat1622float2(hi);
-                                *reinterpret_cast<__nv_bfloat162 *>(alo + bcol + c) =
+                                *reinterpret_cast<__nv_bfloat162 *>(al + bcol + c) =
                                     __floats2bfloat162_rn(y0 - hf.x, y1 - hf.y);
                             }
                         });
                 }
             }
-            fence_async_smem();
             __syncwarp();
-            if (lane == 0) {
-                bulk_store(A_hi + p * (int64_t)k_total, ahi, a_bytes);
-                if (kSplit) bulk_store(A_lo + p * (int64_t)k_total, alo, a_bytes);
-                bulk_commit();
-            }
         }
     }
     // drain: loads still in flight (only after an abort) and the last stores
@@ -564,7 +572,7 @@ int launch_rot_in_stream(const float *x, const int64_t *src, int64_t nsrc, const
         return FEQ_ERR_UNSUPPORTED;
     RotWarpLayout WL;
     WL.in_row = pad4(C * L.dim);
-    WL.out_row = (split ? 2 : 1) * k_total / 2;
+    WL.out_row = 0;
     WL.scratch = rot_scratch(L).total();
     const size_t smem = ((size_t)pad4(L.dim) + (size_t)kRotWarps * WL.total()) * 4;
     if (smem + sizeof(RotShared) > 200 * 1024) return FEQ_ERR_UNSUPPORTED;

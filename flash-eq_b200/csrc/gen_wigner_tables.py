@@ -139,6 +139,39 @@ def main() -> int:
         for i in range(0, total, 8):
             fh.write("  " + ", ".join("%.9ef" % v for v in data[i:i + 8]) + ",\n")
         fh.write("};\n")
+        # Compressed form: each M entry is a short sum over the few trig terms whose
+        # coefficient is not zero (float32 round-off of exact zeros is dropped); every
+        # entry of degree l carries exactly K_l (coefficient, term) slots, unused ones 0.
+        coefs, qs, coffs, ks, ctotal = [], [], [], [], 0
+        for l in range(args.lmax + 1):
+            n = 2 * l + 1
+            t = tables_for(l).reshape(n * n, n)
+            keep = np.abs(t) > 1e-7
+            k = max(1, int(keep.sum(axis=1).max()))
+            c = np.zeros((n * n, k), dtype=np.float32)
+            q = np.zeros((n * n, k), dtype=np.int64)
+            for i in range(n * n):
+                idx = np.nonzero(keep[i])[0]
+                c[i, :len(idx)] = t[i, idx]
+                q[i, :len(idx)] = idx
+            coffs.append(ctotal)
+            ks.append(k)
+            coefs.append(c.reshape(-1))
+            qs.append(q.reshape(-1))
+            ctotal += n * n * k
+        cdata, qdata = np.concatenate(coefs), np.concatenate(qs)
+        fh.write(f"#define FEQ_WTC_SIZE {ctotal}\n")
+        fh.write("__device__ const int feq_wtc_offset[%d] = {%s};\n" % (len(coffs), ", ".join(map(str, coffs))))
+        fh.write("__device__ const int feq_wtc_k[%d] = {%s};\n" % (len(ks), ", ".join(map(str, ks))))
+        fh.write("#define FEQ_WTC_K_UPTO4 {%s}\n" % ", ".join(map(str, ks[:5])))
+        fh.write("__device__ const float feq_wtc_coef[FEQ_WTC_SIZE] = {\n")
+        for i in range(0, ctotal, 8):
+            fh.write("  " + ", ".join("%.9ef" % v for v in cdata[i:i + 8]) + ",\n")
+        fh.write("};\n")
+        fh.write("__device__ const unsigned char feq_wtc_term[FEQ_WTC_SIZE] = {\n")
+        for i in range(0, ctotal, 32):
+            fh.write("  " + ", ".join(str(int(v)) for v in qdata[i:i + 32]) + ",\n")
+        fh.write("};\n")
     return 0
 
 
