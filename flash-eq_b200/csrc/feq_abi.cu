@@ -17,6 +17,7 @@ namespace feq {
 
 // kernels (feq_rotate.cu, feq_mix.cu, feq_graph.cu)
 int launch_basis(const float *dirs, int64_t E, const ReprLayout &L, int layout, float *out, cudaStream_t s);
+int launch_basis_stream(const float *dirs, int64_t E, const ReprLayout &L, int mfirst, float *out, cudaStream_t s);
 int launch_rotate_in(const float *x, const int64_t *src, int64_t nsrc, const float *edge_add,
                      const float *dirs, const float *P, int64_t E, int C, const ReprLayout &L,
                      float *g, int32_t *status, cudaStream_t s);
@@ -430,7 +431,9 @@ int feq_wigner_basis(const float *directions, int64_t num_edges, const int32_t *
     if (num_edges == 0) return FEQ_OK;
     if (!directions || !out) return FEQ_ERR_INVALID_ARGUMENT;
     if (num_edges > 0x7fffffffll * 8) return FEQ_ERR_UNSUPPORTED;
-    return launch_basis(directions, num_edges, L, layout, out, (cudaStream_t)stream);
+    rc = launch_basis_stream(directions, num_edges, L, layout == FEQ_BASIS_MFIRST ? 1 : 0, out, (cudaStream_t)stream);
+    if (rc == FEQ_ERR_UNSUPPORTED) rc = launch_basis(directions, num_edges, L, layout, out, (cudaStream_t)stream);
+    return rc;
 }
 
 int feq_edge_binning(const float *distances, int64_t num_edges, float bin_param1, float bin_param2,

@@ -544,6 +544,54 @@ rot_out_kernel(const float *__restrict__ H, int h_ld, const float *__restrict__ 
     if (lane == 0) bulk_wait0();
 }
 
+// Dense per-edge basis: MFIRST  out[e][k][j] = D_e[k][perm[j]]  (same irrep, else 0)
+//                      ROT_TO_EZ out[e][k][j] = D_e[j][k]       (std order, D^T)
+// One warp per edge; lanes own columns, so every row is written with contiguous stores.
+__global__ void __launch_bounds__(kRotWarps * 32)
+basis_warp_kernel(const float *__restrict__ dirs, int64_t E, const __grid_constant__ ReprLayout Lp, int mfirst,
+                  int scratch_floats, float *__restrict__ out) {
+    extern __shared__ __align__(128) float dsm[];
+    __shared__ RotShared S;
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    copy_layout(Lp, S.L);
+    __syncthreads();
+    if (threadIdx.x == 0) rblock_offsets(S.L, S.rdoff);
+    __syncthreads();
+    const ReprLayout &L = S.L;
+    const int d = L.dim;
+    const int64_t dd = (int64_t)d * d;
+    const RotScratch SC = rot_scratch(L);
+    float *trig = dsm + (size_t)w * scratch_floats;
+    float *m_s = trig + SC.trig, *r_s = m_s + SC.mblk;
+    const int TF = trig_floats(L.lmax);
+    for (int64_t g0 = ((int64_t)blockIdx.x * kRotWarps + w) * kGroup; g0 < E;
+         g0 += (int64_t)gridDim.x * kRotWarps * kGroup) {
+        const int ng = (int)min64(kGroup, E - g0);
+        if (lane < ng) {
+            const float *v = dirs + (g0 + lane) * 3;
+            edge_trig_compact(v[0], v[1], v[2], L.lmax, trig + lane * TF);
+        }
+        __syncwarp();
+        for (int j0 = 0; j0 < ng; j0++) {
+            build_all_rblocks<true>(L, S.rdoff, trig + j0 * TF, 1.0f, m_s, r_s, lane);
+            float *o = out + (g0 + j0) * dd;
+            for (int jc = lane; jc < d; jc += 32) {
+                const int a = mfirst ? L.perm[jc] : jc;           // std index carried by this column
+                const int ir = L.std_irrep[a], off = L.irrep_off[ir], n = 2 * L.irrep_l[ir] + 1;
+                const float *R = r_s + S.rdoff[L.irrep_slot[ir]];
+                const int P = pad4(n);
+                for (int k = 0; k < d; k++) {
+                    const int rel = k - off;
+                    float v = 0.0f;
+                    if (rel >= 0 && rel < n) v = mfirst ? R[rel * P + (a - off)] : R[(a - off) * P + rel];
+                    o[(int64_t)k * d + jc] = v;
+                }
+            }
+            __syncwarp();
+        }
+    }
+}
+
 }  // namespace
 
 static bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -611,6 +659,19 @@ int launch_rot_out_stream(const float *H, int h_ld, const float *dirs, const flo
     const int grid = rot_grid((const void *)rot_out_kernel, smem, E);
     rot_out_kernel<<<grid, kRotWarps * 32, smem, s>>>(H, h_ld, dirs, dist, perm, E, C, L, M, sh_scale, WL, out,
                                                       status);
+    FEQ_LAUNCH_CHECK();
+    return FEQ_OK;
+}
+
+// Dense basis matrices, warp per edge.  FEQ_ERR_UNSUPPORTED when the layout does not fit.
+int launch_basis_stream(const float *dirs, int64_t E, const ReprLayout &L, int mfirst, float *out, cudaStream_t s) {
+    if (E == 0) return FEQ_OK;
+    const int scratch = rot_scratch(L).total();
+    const size_t smem = (size_t)kRotWarps * scratch * 4;
+    if (smem + sizeof(RotShared) > 200 * 1024) return FEQ_ERR_UNSUPPORTED;
+    FEQ_CUDA_TRY(cudaFuncSetAttribute(basis_warp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    const int grid = rot_grid((const void *)basis_warp_kernel, smem, E);
+    basis_warp_kernel<<<grid, kRotWarps * 32, smem, s>>>(dirs, E, L, mfirst, scratch, out);
     FEQ_LAUNCH_CHECK();
     return FEQ_OK;
 }

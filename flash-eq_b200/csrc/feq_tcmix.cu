@@ -262,6 +262,53 @@ __global__ void tc_relayout_b_kernel(const float *__restrict__ T, __nv_bfloat16 
     }
 }
 
+// Same layout, one block per (output channel co, bin b): the block's weights
+// T[b][co][:][:] (Cin x wdim floats, contiguous) are staged in shared memory with
+// coalesced loads, then every B row of that channel is written with consecutive
+// threads on consecutive k (input channel fastest).  Blocks with co = 0 also zero the
+// N-padding rows of their bin.
+__global__ void tc_relayout_b_rows_kernel(const float *__restrict__ T, __nv_bfloat16 *__restrict__ Bhi,
+                                          __nv_bfloat16 *__restrict__ Blo, int Cin, int Cout, int wdim,
+                                          const __grid_constant__ TcGeom G) {
+    extern __shared__ float tw[];
+    const int co = blockIdx.x, b = blockIdx.y;
+    const int64_t slice = (int64_t)Cin * wdim;
+    const float *src = T + ((int64_t)b * Cout + co) * slice;
+    for (int64_t i = threadIdx.x; i < slice; i += blockDim.x) tw[i] = __ldg(src + i);
+    __syncthreads();
+    for (int q = 0; q < G.n_blocks; q++) {
+        const TcBlockGeom &B = G.g[q];
+        const int kin = B.mult * B.n_in, kout = B.mult * B.n_out;
+        const int kvalid = (B.n_in > 0 && B.n_out > 0) ? Cin * kin : 0;
+        const int nreal = Cout * kout;
+        // rows owned by this block: rn * Cout + co, and the padding rows when co == 0
+        const int nrows = kout + (co == 0 ? B.npad - nreal : 0);
+        for (int rr = 0; rr < nrows; rr++) {
+            const bool real = rr < kout;
+            const int n = real ? rr * Cout + co : nreal + (rr - kout);
+            const int o = real ? rr / B.mult : 0, oc = real ? rr - o * B.mult : 0;
+            __nv_bfloat16 *rh = Bhi + B.boff + ((int64_t)b * B.npad + n) * B.kpad;
+            __nv_bfloat16 *rl = Blo ? Blo + B.boff + ((int64_t)b * B.npad + n) * B.kpad : nullptr;
+            for (int k = threadIdx.x; k < B.kpad; k += blockDim.x) {
+                float v = 0.0f;
+                if (real && k < kvalid) {
+                    const int ci = k % Cin, rk = k / Cin, i = rk / B.mult, ic = rk - i * B.mult;
+                    const float *w = tw + ci * wdim + B.w_off;
+                    if (B.mult == 1) {
+                        v = w[o * B.n_in + i];
+                    } else {
+                        const float a = w[2 * (o * B.n_in + i)], bb = w[2 * (o * B.n_in + i) + 1];
+                        v = (oc == ic) ? a : (oc == 0 ? bb : -bb);   // (re,im) -> b, (im,re) -> -b
+                    }
+                }
+                const __nv_bfloat16 hi = __float2bfloat16_rn(v);
+                rh[k] = hi;
+                if (rl) rl[k] = __float2bfloat16_rn(v - __bfloat162float(hi));
+            }
+        }
+    }
+}
+
 // ---------------------------------------------------------------------------
 // Host
 // ---------------------------------------------------------------------------
@@ -301,6 +348,16 @@ static int make_map(CUtensorMap *m, const void *base, int64_t cols, int64_t rows
 int launch_tc_relayout_b(const float *T, __nv_bfloat16 *Bhi, __nv_bfloat16 *Blo, int nb1, int Cin, int Cout,
                          int wdim, const TcGeom &G, int64_t total, cudaStream_t s) {
     if (total == 0) return FEQ_OK;
+    const size_t smem = (size_t)Cin * wdim * 4;
+    if (smem <= 96 * 1024 && Cout <= 65535 && nb1 <= 65535) {
+        if (smem > 48 * 1024)
+            FEQ_CUDA_TRY(cudaFuncSetAttribute(tc_relayout_b_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              (int)smem));
+        tc_relayout_b_rows_kernel<<<dim3((unsigned)Cout, (unsigned)nb1), 256, smem, s>>>(T, Bhi, Blo, Cin, Cout,
+                                                                                       wdim, G);
+        FEQ_LAUNCH_CHECK();
+        return FEQ_OK;
+    }
     const int64_t grid = min64((total + 255) / 256, 148 * 32);
     tc_relayout_b_kernel<<<(unsigned)grid, 256, 0, s>>>(T, Bhi, Blo, nb1, Cin, Cout, wdim, G, total);
     FEQ_LAUNCH_CHECK();
