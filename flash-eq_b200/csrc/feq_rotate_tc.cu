@@ -26,6 +26,7 @@
 #include "feq_internal.cuh"
 #include "feq_sm100.cuh"
 #include "_build/feq_wigner_tables.inc"
+#include "_build/feq_wigner_apply.inc"
 
 namespace feq {
 namespace {
@@ -245,6 +246,90 @@ __device__ __forceinline__ void rotate_pair_any(int l, const float *__restrict__
     }
 }
 
+// Compile-time access to the generated per-degree code.
+template <int L> struct WA;
+#define FEQ_DEF_WA(LL)                                                                                    \
+    template <> struct WA<LL> {                                                                           \
+        static constexpr int kNnz = FEQ_WM_NNZ_##LL;                                                      \
+        __device__ __forceinline__ static void wm(const float *tv, float sl, float (&m)[kNnz]) {          \
+            feq_wm_l##LL(tv, sl, m);                                                                      \
+        }                                                                                                 \
+        template <bool kT>                                                                                \
+        __device__ __forceinline__ static void wa(const float (&m)[kNnz], const float (&g)[2 * LL + 1],   \
+                                                  float (&h)[2 * LL + 1]) {                               \
+            feq_wa_l##LL<kT>(m, g, h);                                                                    \
+        }                                                                                                 \
+    };
+FEQ_DEF_WA(1)
+FEQ_DEF_WA(2)
+FEQ_DEF_WA(3)
+FEQ_DEF_WA(4)
+FEQ_DEF_WA(5)
+FEQ_DEF_WA(6)
+#undef FEQ_DEF_WA
+static_assert(FEQ_WA_LMAX == 6, "generated per-degree code covers degrees 1..6");
+constexpr int kFactoredLmax = 6;
+
+// One irrep of degree Lg for two channels, entirely in registers, through the factored
+// block D = R(phi) M R(phi)^T:
+//   kT = false: y = x D   = ((x R) M) R^T      (rotate_in:  y[o] = sum_q x[q] D[q][o])
+//   kT = true : y = x D^T = ((x R) M^T) R^T    (rotate_out: y[o] = sum_q x[q] D[o][q])
+// scaled by sl (folded into M).  tr: the edge's compact trig (tv, cos m phi, sin m phi).
+template <int Lg, bool kT, typename Get, typename Emit>
+__device__ __forceinline__ void rot_irrep2(const float *__restrict__ tr, int lmax, float sl, Get get, Emit emit) {
+    constexpr int N = 2 * Lg + 1;
+    const float *tv = tr, *cp = tr + 2 * lmax + 1, *sp = cp + lmax + 1;
+    float m[WA<Lg>::kNnz];
+    WA<Lg>::wm(tv, sl, m);
+    float g0[N], g1[N];
+#pragma unroll
+    for (int q = 0; q < N; q++) {
+        const float2 v = get(q);
+        g0[q] = v.x;
+        g1[q] = v.y;
+    }
+#pragma unroll
+    for (int mm = 1; mm <= Lg; mm++) {      // g <- g R(phi)
+        const int a = Lg - mm, b = Lg + mm;
+        const float c = cp[mm], s = sp[mm];
+        float t0 = g0[a] * c - g0[b] * s, t1 = g0[a] * s + g0[b] * c;
+        g0[a] = t0; g0[b] = t1;
+        t0 = g1[a] * c - g1[b] * s; t1 = g1[a] * s + g1[b] * c;
+        g1[a] = t0; g1[b] = t1;
+    }
+    float h0[N], h1[N];
+    WA<Lg>::template wa<kT>(m, g0, h0);
+    WA<Lg>::template wa<kT>(m, g1, h1);
+#pragma unroll
+    for (int mm = 1; mm <= Lg; mm++) {      // h <- h R(phi)^T
+        const int a = Lg - mm, b = Lg + mm;
+        const float c = cp[mm], s = sp[mm];
+        float t0 = h0[a] * c + h0[b] * s, t1 = h0[b] * c - h0[a] * s;
+        h0[a] = t0; h0[b] = t1;
+        t0 = h1[a] * c + h1[b] * s; t1 = h1[b] * c - h1[a] * s;
+        h1[a] = t0; h1[b] = t1;
+    }
+#pragma unroll
+    for (int o = 0; o < N; o++) emit(o, h0[o], h1[o]);
+}
+
+template <bool kT, typename Get, typename Emit>
+__device__ __forceinline__ void rot_irrep2_any(int l, const float *tr, int lmax, float sl, Get get, Emit emit) {
+    switch (l) {
+        case 0: {
+            const float2 v = get(0);
+            emit(0, v.x * sl, v.y * sl);
+            break;
+        }
+        case 1: rot_irrep2<1, kT>(tr, lmax, sl, get, emit); break;
+        case 2: rot_irrep2<2, kT>(tr, lmax, sl, get, emit); break;
+        case 3: rot_irrep2<3, kT>(tr, lmax, sl, get, emit); break;
+        case 4: rot_irrep2<4, kT>(tr, lmax, sl, get, emit); break;
+        case 5: rot_irrep2<5, kT>(tr, lmax, sl, get, emit); break;
+        default: rot_irrep2<6, kT>(tr, lmax, sl, get, emit); break;
+    }
+}
+
 // Shared per-warp scratch, in floats: the group's trig, one M block, the rotation blocks.
 struct RotScratch {
     int trig, mblk, rblk;      // float counts
@@ -297,7 +382,7 @@ __device__ __forceinline__ bool wait_row(RotShared &S, int w, int b, uint32_t &p
 
 // A[p][base_std(k) + c] = s_e^l(k) (f[e][c] . D_e)[k] as bf16 (hi, and lo = f - hi when kSplit);
 // f[e] = x[src[e]] (kGather) or x[e], plus edge_add[e] when given; tval[p] = t_e.
-template <bool kGather, bool kSplit>
+template <bool kGather, bool kSplit, bool kFactored>
 __global__ void __launch_bounds__(kRotWarps * 32)
 rot_in_kernel(const float *__restrict__ x, const int64_t *__restrict__ src, int64_t nsrc,
               const float *__restrict__ edge_add, const float *__restrict__ dirs, const float *__restrict__ dist,
@@ -378,7 +463,8 @@ rot_in_kernel(const float *__restrict__ x, const int64_t *__restrict__ src, int6
             const int64_t p = g0 + j;
             const int b = j & 1;
             if (j + 1 < ng) issue(j + 1);
-            build_all_rblocks<true>(L, S.rdoff, trig + j * TF, s, m_s, r_s, lane);
+            if constexpr (!kFactored) build_all_rblocks<true>(L, S.rdoff, trig + j * TF, s, m_s, r_s, lane);
+            const float *trj = trig + j * TF;
             float *fb = ws + b * WL.in_row;
             if (xr >= 0) {
                 if (!wait_row(S, w, b, phase_bits, status)) {
@@ -412,21 +498,23 @@ rot_in_kernel(const float *__restrict__ x, const int64_t *__restrict__ src, int6
                 const float *f0 = fb + c * d, *f1 = f0 + d;
                 for (int r = 0; r < L.n_irreps; r++) {
                     const int l = L.irrep_l[r], off = L.irrep_off[r];
-                    const float *R = r_s + S.rdoff[L.irrep_slot[r]];
                     const int32_t *bo = bstd + off;
-                    rotate_pair_any(
-                        l, R, [&](int q) { return make_float2(f0[off + q], f1[off + q]); },
-                        [&](int o, float y0, float y1) {
-                            const int bcol = bo[o];
-                            if (bcol < 0) return;
-                            const __nv_bfloat162 hi = __floats2bfloat162_rn(y0, y1);
-                            *reinterpret_cast<__nv_bfloat162 *>(ah + bcol + c) = hi;
-                            if (kSplit) {
-                                const float2 hf = __bfloat1622float2(hi);
-                                *reinterpret_cast<__nv_bfloat162 *>(al + bcol + c) =
-                                    __floats2bfloat162_rn(y0 - hf.x, y1 - hf.y);
-                            }
-                        });
+                    auto get = [&](int q) { return make_float2(f0[off + q], f1[off + q]); };
+                    auto emit = [&](int o, float y0, float y1) {
+                        const int bcol = bo[o];
+                        if (bcol < 0) return;
+                        const __nv_bfloat162 hi = __floats2bfloat162_rn(y0, y1);
+                        *reinterpret_cast<__nv_bfloat162 *>(ah + bcol + c) = hi;
+                        if (kSplit) {
+                            const float2 hf = __bfloat1622float2(hi);
+                            *reinterpret_cast<__nv_bfloat162 *>(al + bcol + c) =
+                                __floats2bfloat162_rn(y0 - hf.x, y1 - hf.y);
+                        }
+                    };
+                    if constexpr (kFactored)
+                        rot_irrep2_any<false>(l, trj, L.lmax, ipowf(s, l), get, emit);
+                    else
+                        rotate_pair_any(l, r_s + S.rdoff[L.irrep_slot[r]], get, emit);
                 }
             }
             __syncwarp();
@@ -440,6 +528,7 @@ rot_in_kernel(const float *__restrict__ x, const int64_t *__restrict__ src, int6
 
 // out[e][c][k] = sum_q D_e[k][q] s_e^l h[q][c], h[q][c] = H[p][base_std(q) + c] (0 where
 // base_std < 0: output blocks that receive no input).
+template <bool kFactored>
 __global__ void __launch_bounds__(kRotWarps * 32)
 rot_out_kernel(const float *__restrict__ H, int h_ld, const float *__restrict__ dirs, const float *__restrict__ dist,
                const int64_t *__restrict__ perm, int64_t E, int C, const __grid_constant__ ReprLayout Lp,
@@ -503,7 +592,8 @@ rot_out_kernel(const float *__restrict__ H, int h_ld, const float *__restrict__ 
             const float s = __shfl_sync(0xffffffffu, s_l, j);
             const int b = j & 1;
             if (j + 1 < ng) issue(j + 1);
-            build_all_rblocks<false>(L, S.rdoff, trig + j * TF, s, m_s, r_s, lane);
+            if constexpr (!kFactored) build_all_rblocks<false>(L, S.rdoff, trig + j * TF, s, m_s, r_s, lane);
+            const float *trj = trig + j * TF;
             if (!wait_row(S, w, b, phase_bits, status)) {
                 alive = false;
                 break;
@@ -516,19 +606,19 @@ rot_out_kernel(const float *__restrict__ H, int h_ld, const float *__restrict__ 
                 float *o0 = ob + c * d, *o1 = o0 + d;
                 for (int r = 0; r < L.n_irreps; r++) {
                     const int l = L.irrep_l[r], off = L.irrep_off[r];
-                    const float *R = r_s + S.rdoff[L.irrep_slot[r]];
                     const int32_t *bi = bstd + off;
-                    rotate_pair_any(
-                        l, R,
-                        [&](int q) {
-                            const int bcol = bi[q];
-                            return bcol < 0 ? make_float2(0.0f, 0.0f)
-                                            : *reinterpret_cast<const float2 *>(hb + bcol + c);
-                        },
-                        [&](int o, float y0, float y1) {
-                            o0[off + o] = y0;
-                            o1[off + o] = y1;
-                        });
+                    auto get = [&](int q) {
+                        const int bcol = bi[q];
+                        return bcol < 0 ? make_float2(0.0f, 0.0f) : *reinterpret_cast<const float2 *>(hb + bcol + c);
+                    };
+                    auto emit = [&](int o, float y0, float y1) {
+                        o0[off + o] = y0;
+                        o1[off + o] = y1;
+                    };
+                    if constexpr (kFactored)
+                        rot_irrep2_any<true>(l, trj, L.lmax, ipowf(s, l), get, emit);
+                    else
+                        rotate_pair_any(l, r_s + S.rdoff[L.irrep_slot[r]], get, emit);
                 }
             }
             fence_async_smem();
@@ -621,12 +711,13 @@ int launch_rot_in_stream(const float *x, const int64_t *src, int64_t nsrc, const
     RotWarpLayout WL;
     WL.in_row = pad4(C * L.dim);
     WL.out_row = 0;
-    WL.scratch = rot_scratch(L).total();
+    const bool factored = L.lmax <= kFactoredLmax;
+    WL.scratch = factored ? rot_scratch(L).trig : rot_scratch(L).total();
     const size_t smem = ((size_t)pad4(L.dim) + (size_t)kRotWarps * WL.total()) * 4;
     if (smem + sizeof(RotShared) > 200 * 1024) return FEQ_ERR_UNSUPPORTED;
 #define FEQ_ROT_IN(G, S)                                                                                        \
     do {                                                                                                        \
-        auto k = rot_in_kernel<G, S>;                                                                           \
+        auto k = factored ? rot_in_kernel<G, S, true> : rot_in_kernel<G, S, false>;                                                                         \
         FEQ_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));          \
         const int grid = rot_grid((const void *)k, smem, E);                                                    \
         k<<<grid, kRotWarps * 32, smem, s>>>(x, src, nsrc, edge_add, dirs, dist, perm, E, C, L, M, k_total, bins, \
@@ -652,13 +743,14 @@ int launch_rot_out_stream(const float *H, int h_ld, const float *dirs, const flo
     RotWarpLayout WL;
     WL.in_row = pad4(h_ld);
     WL.out_row = pad4(C * L.dim);
-    WL.scratch = rot_scratch(L).total();
+    const bool factored = L.lmax <= kFactoredLmax;
+    WL.scratch = factored ? rot_scratch(L).trig : rot_scratch(L).total();
     const size_t smem = ((size_t)pad4(L.dim) + (size_t)kRotWarps * WL.total()) * 4;
     if (smem + sizeof(RotShared) > 200 * 1024) return FEQ_ERR_UNSUPPORTED;
-    FEQ_CUDA_TRY(cudaFuncSetAttribute(rot_out_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    const int grid = rot_grid((const void *)rot_out_kernel, smem, E);
-    rot_out_kernel<<<grid, kRotWarps * 32, smem, s>>>(H, h_ld, dirs, dist, perm, E, C, L, M, sh_scale, WL, out,
-                                                      status);
+    auto k = factored ? rot_out_kernel<true> : rot_out_kernel<false>;
+    FEQ_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    const int grid = rot_grid((const void *)k, smem, E);
+    k<<<grid, kRotWarps * 32, smem, s>>>(H, h_ld, dirs, dist, perm, E, C, L, M, sh_scale, WL, out, status);
     FEQ_LAUNCH_CHECK();
     return FEQ_OK;
 }

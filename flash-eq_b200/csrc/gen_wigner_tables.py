@@ -121,6 +121,7 @@ def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("out")
     ap.add_argument("--lmax", type=int, default=16)
+    ap.add_argument("--apply-out", default=None, help="also write the unrolled sparse M_l products here")
     args = ap.parse_args()
     offs, chunks, total = [], [], 0
     for l in range(args.lmax + 1):
@@ -172,7 +173,47 @@ def main() -> int:
         for i in range(0, ctotal, 32):
             fh.write("  " + ", ".join(str(int(v)) for v in qdata[i:i + 32]) + ",\n")
         fh.write("};\n")
+    if args.apply_out:
+        write_apply(args.apply_out, min(args.lmax, 6))
     return 0
+
+
+def write_apply(path: str, lgen: int) -> None:
+    """Unrolled per-degree code for the factored rotation D_l = R(phi) M_l R(phi)^T.
+
+    feq_wm_l<l>(tv, sl, m):  the nonzero entries of s^l M_l(theta'), each a short sum of
+                              the trig terms tv[k] with constant coefficients;
+    feq_wa_l<l><kT>(m, g, h): h = g M_l (kT = false) or h = g M_l^T (kT = true), row
+                              vectors, only the nonzero entries of M_l.
+    """
+    out = ["/* generated by gen_wigner_tables.py -- unrolled sparse M_l products */",
+           f"#define FEQ_WA_LMAX {lgen}"]
+    for l in range(1, lgen + 1):
+        n = 2 * l + 1
+        t = tables_for(l).astype(np.float32).astype(np.float64).reshape(n * n, n)
+        ents = [i for i in range(n * n) if (np.abs(t[i]) > 1e-7).any()]
+        slot = {e: k for k, e in enumerate(ents)}
+        out.append(f"#define FEQ_WM_NNZ_{l} {len(ents)}")
+        out.append(f"__device__ __forceinline__ void feq_wm_l{l}(const float *tv, float sl, float (&m)[{len(ents)}]) {{")
+        for k, e in enumerate(ents):
+            terms = [f"{t[e, q]:.9e}f * tv[{q}]" for q in range(n) if abs(t[e, q]) > 1e-7]
+            out.append(f"    m[{k}] = sl * ({' + '.join(terms)});")
+        out.append("}")
+        out.append(f"template <bool kT> __device__ __forceinline__ void feq_wa_l{l}("
+                   f"const float (&m)[{len(ents)}], const float (&g)[{n}], float (&h)[{n}]) {{")
+        for tr in (False, True):
+            out.append("    if (%skT) {" % ("" if tr else "!"))
+            for o in range(n):
+                terms = []
+                for q in range(n):
+                    e = (o * n + q) if tr else (q * n + o)   # g M: h[o] = sum_q g[q] M[q][o]
+                    if e in slot:
+                        terms.append(f"g[{q}] * m[{slot[e]}]")
+                out.append(f"        h[{o}] = {' + '.join(terms) if terms else '0.0f'};")
+            out.append("    }")
+        out.append("}")
+    with open(path, "w") as fh:
+        fh.write("\n".join(out) + "\n")
 
 
 if __name__ == "__main__":
