@@ -57,7 +57,7 @@ tc_mix_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ 
     constexpr int kTiles = kSplit == 1 ? 3 : 6;      // A, B(b), B(b+1) [, A.lo, B(b).lo, B(b+1).lo]
     constexpr int kStages = kSplit == 1 ? 4 : 2;
     constexpr uint32_t kStageBytes = kTiles * kTcTileBytes;
-    constexpr uint32_t kIdesc = idesc_bf16_f32(kTcRows, kTcN);
+    constexpr uint32_t kIdesc = idesc_bf16_f32(kTcRows, 2 * kTcN);   // D_lo | D_hi
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -130,7 +130,7 @@ tc_mix_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ 
             const int buf = j & 1, rr = j >> 1;
             if (rr > 0 && !mbar_wait(&tempty_bar[buf], (rr - 1) & 1, abort_flag)) break;
             tc_fence_after();
-            const uint32_t d_lo = tmem + buf * 2 * kTcN, d_hi = d_lo + kTcN;
+            const uint32_t d_lo = tmem + buf * 2 * kTcN;
             bool ok = true;
             for (int ks = 0; ks < P.k_steps; ks++, it++) {
                 const int s = it % kStages, r = it / kStages;
@@ -142,21 +142,18 @@ tc_mix_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ 
                 const uint32_t base = smem_u32(smem + (size_t)s * kStageBytes);
 #pragma unroll
                 for (int kk = 0; kk < kTcK / 16; kk++) {
+                    // B(b) and B(b+1) tiles are adjacent in shared memory: one N = 256 MMA
+                    // writes D_lo (columns 0..127) and D_hi (columns 128..255) together.
                     const uint32_t koff = kk * 32;   // 16 bf16 = 32 bytes along K
                     const uint64_t a = smem_desc_sw128(base + koff);
-                    const uint64_t b0 = smem_desc_sw128(base + kTcTileBytes + koff);
-                    const uint64_t b1 = smem_desc_sw128(base + 2 * kTcTileBytes + koff);
+                    const uint64_t b = smem_desc_sw128(base + kTcTileBytes + koff);
                     const uint32_t acc = (ks > 0 || kk > 0) ? 1u : 0u;
-                    umma_f16(d_lo, a, b0, kIdesc, acc);
-                    umma_f16(d_hi, a, b1, kIdesc, acc);
+                    umma_f16(d_lo, a, b, kIdesc, acc);
                     if (kSplit == 3) {
                         const uint64_t a2 = smem_desc_sw128(base + 3 * kTcTileBytes + koff);
-                        const uint64_t b02 = smem_desc_sw128(base + 4 * kTcTileBytes + koff);
-                        const uint64_t b12 = smem_desc_sw128(base + 5 * kTcTileBytes + koff);
-                        umma_f16(d_lo, a, b02, kIdesc, 1u);
-                        umma_f16(d_hi, a, b12, kIdesc, 1u);
-                        umma_f16(d_lo, a2, b0, kIdesc, 1u);
-                        umma_f16(d_hi, a2, b1, kIdesc, 1u);
+                        const uint64_t b2 = smem_desc_sw128(base + 4 * kTcTileBytes + koff);
+                        umma_f16(d_lo, a, b2, kIdesc, 1u);
+                        umma_f16(d_lo, a2, b, kIdesc, 1u);
                     }
                 }
                 umma_commit(&empty_bar[s]);   // stage s is free once these MMAs finish
