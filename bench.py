@@ -12,7 +12,9 @@ Synthetic data (the reference benchmarks on random graphs too); module weights
 random-init with torch.manual_seed(1).
 
 One step = P, Q = WignerDBasis(directions); out = layer(P, Q, x[src], distances),
-inputs resident in HBM (4.1 GB of edge features per step >> 126 MB L2, so no
+with the layer's radial mix on the tensor cores (--mix bf16x3, the default: every
+operand split into two bf16 terms, float32-level accuracy; --mix bf16: the bf16-mix
+path; --mix fp32: CUDA-core float32), inputs resident in HBM (4.1 GB of edge features per step >> 126 MB L2, so no
 flush is needed).  Under torchrun (N > 1) every rank runs its own independent
 graph (seed 1 + rank): data-parallel, no collective on the data path, weak scaling.
 
@@ -151,6 +153,28 @@ class ClockSampler:
         mhz.sort()
         return {"sm_mhz": mhz[len(mhz) // 2] if mhz else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
                 "samples": len(mhz), "power_w_max": max(power) if power else None}
+
+
+def measured_sustained():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as fh:
+            return float(json.load(fh)["bf16_tflops_sustained"])
+    except (OSError, KeyError, ValueError):
+        return None
+
+
+def profiled_traffic(stage: str, E: int):
+    """DRAM bytes (read + write) of one step's launches of `stage`, from the committed ncu
+    summary profiles/<stage>_config2.md ("dram_bytes_per_edge: X"), scaled to E edges."""
+    path = os.path.join(ROOT, "profiles", f"{stage}_config2.md")
+    try:
+        with open(path) as fh:
+            for ln in fh:
+                if ln.strip().startswith("dram_bytes_per_edge:"):
+                    return float(ln.split(":", 1)[1]) * E
+    except (OSError, ValueError):
+        pass
+    return None
 
 
 def measured_peaks():
@@ -310,7 +334,7 @@ def gpu_index_for(local: int) -> int:
 def run_ours(args):
     world, rank, local, pg = dist_setup(args)
     dev = torch.device("cuda", local)
-    from flash_eq.cuda import _lib, block_diagonal_cuda
+    from flash_eq.cuda import _lib
 
     lib = _lib.load()
     wl = make_workload(SEED + rank, dev, args.nodes)
@@ -346,32 +370,60 @@ def run_ours(args):
     ms = max_over_ranks(pg, t0.elapsed_time(t1) / args.steps)
     value = E * world / (ms / 1e3)
 
-    # --- dominant stage: the block-diagonal radial mix, timed alone on the same shapes
+    # --- per-stage device times: CUDA events the library records on the stream each
+    # stage is launched on, over a few extra steps after the timed region
+    from flash_eq.cuda import ops as feq_ops
+
+    prof_steps = 3
+    feq_ops.profile_enable(True)
+    for _ in range(prof_steps):
+        step()
+    torch.cuda.synchronize()
+    stages = feq_ops.profile_read()
+    feq_ops.profile_enable(False)
     byts, mix_flops, rot_flops, table_bytes = per_edge_work()
-    with torch.no_grad():
-        table = layer.radial_weights()
-        P, _ = basis(vec)
-        g_in = torch.bmm(x[src], P)                       # m-first input of the mix
-    p1, p2 = layer.radial_weights.binning_params()
-    pr = layer.product_repr
-    for _ in range(2):
-        block_diagonal_cuda(g_in, table, dist_e, pr, p1, p2, NUM_BINS, False, 0.1)
-    reps = 3
-    m0, m1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
-    m0.record()
-    for _ in range(reps):
-        block_diagonal_cuda(g_in, table, dist_e, pr, p1, p2, NUM_BINS, False, 0.1)
-    m1.record()
-    torch.cuda.synchronize()
-    mix_ms = m0.elapsed_time(m1) / reps
-    del g_in, P
+    d = sum(2 * l + 1 for l in LVALS)
+    nsplit = 2 if args.mix == "bf16x3" else 1
+    tensor_mult = {"bf16x3": 6, "bf16": 2}.get(args.mix, 0)     # bf16 MMAs per algorithmic MAC
+    stage_bytes = {                                                # algorithmic bytes per edge
+        "basis": d * d * 4 + 12,
+        "rotate_in": MULT * d * 4 + 28 + 4 + MULT * d * 2 * nsplit,
+        "rotate_out": MULT * d * 4 * 2 + 24,
+        "tc_mix": MULT * d * 2 * nsplit + MULT * d * 4 + 4,
+    }
     hbm_peak, tc_peak, peak_kind = measured_peaks()
-    mix_bytes = E * (byts - 16 + 4) + table_bytes          # g in, h out, distance, table
-    achieved_gbs = mix_bytes / (mix_ms / 1e3) / 1e9
-    mix_tflops = E * mix_flops / (mix_ms / 1e3) / 1e12
-    sm_mhz = clocks.get("sm_max_mhz") or 1965.0
-    fp32_peak = 148 * 128 * 2 * sm_mhz * 1e6 / 1e12       # FMA lanes x 2 flop x clock (nominal)
+    tc_sustained = measured_sustained() or tc_peak
+    per_step = {k: {"ms": v[0] / prof_steps, "launches": v[1] // prof_steps} for k, v in stages.items()}
+    dom = max(per_step, key=lambda k: per_step[k]["ms"]) if per_step else None
+    roofline = None
+    if dom == "tc_mix":
+        t = per_step[dom]["ms"] / 1e3
+        alg = E * mix_flops / t / 1e12
+        exe = alg * tensor_mult
+        roofline = {"bound": "tensor", "achieved": alg, "peak": tc_sustained, "unit": "TFLOP/s",
+                    "frac": alg / tc_sustained, "traffic": profiled_traffic("tc_mix", E),
+                    "kernel": f"tc_mix ({per_step[dom]['launches']} launches per step, one per m-block), "
+                              f"CUDA events on its stream, {prof_steps} steps",
+                    "peak_kind": "measured bf16 sustained (MEASURED_PEAKS.json)",
+                    "executed_tflops": exe, "executed_frac": exe / tc_sustained,
+                    "note": f"achieved counts the algorithmic mix FLOPs; the {args.mix} formulation executes "
+                            f"{tensor_mult} bf16 MMA FLOPs per algorithmic FLOP (two neighbouring bins"
+                            + (", 3-term hi/lo split" if args.mix == "bf16x3" else "") + ")"}
+    elif dom is not None:
+        t = per_step[dom]["ms"] / 1e3
+        gbs = E * stage_bytes.get(dom, 0) / t / 1e9
+        roofline = {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak,
+                    "traffic": profiled_traffic(dom, E), "kernel": dom, "peak_kind": peak_kind}
+    for k, v in per_step.items():
+        if k in stage_bytes and k != "tc_mix":
+            v["hbm_gbs"] = E * stage_bytes[k] / (v["ms"] / 1e3) / 1e9
+    if "tc_mix" in per_step:
+        per_step["tc_mix"]["alg_tflops"] = E * mix_flops / (per_step["tc_mix"]["ms"] / 1e3) / 1e12
+    step_gbs = value / world * byts / 1e9
+    step_roofline = {"bound": "hbm", "achieved": step_gbs, "peak": hbm_peak, "unit": "GB/s",
+                     "frac": step_gbs / hbm_peak, "bytes_per_edge": byts,
+                     "note": "whole step against the fused-path algorithmic bytes per edge "
+                             "(input row + output row + 16 B, fp32)"}
 
     # --- end to end through the public API from pinned host buffers
     e2e = run_e2e(args, wl, layer, basis, dev, pg, world) if args.e2e_steps > 0 else None
@@ -381,17 +433,12 @@ def run_ours(args):
         result = {
             "metric": "edges/sec (fwd, device-timed)", "value": value, "unit": "edges/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": config_block(world, args.nodes),
-            "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": hbm_peak, "unit": "GB/s",
-                         "frac": achieved_gbs / hbm_peak, "traffic": None,
-                         "kernel": "block-diagonal radial mix (binning+sort+relayout+mix), timed alone",
-                         "peak_kind": peak_kind,
-                         "note": "fp32 mix on CUDA cores is FLOP-bound, see compute"},
-            "compute": {"achieved": mix_tflops, "unit": "TFLOP/s", "peak": fp32_peak,
-                        "peak_kind": "nominal fp32 FMA (148 SM x 128 lanes x 2 x max clock)",
-                        "frac": mix_tflops / fp32_peak, "mix_ms": mix_ms,
-                        "flop_per_edge": mix_flops, "bytes_per_edge": byts},
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16" if args.mix == "bf16" else "f32",
+            "data": "synthetic", "config": config_block(world, args.nodes),
+            "roofline": roofline,
+            "step_roofline": step_roofline,
+            "stages_ms_per_step": per_step,
+            "mix": args.mix,
             "clocks": clocks,
             "e2e": e2e,
             "gpu_launches": int(launches),
@@ -451,14 +498,14 @@ def run_e2e(args, wl, layer, basis, dev, pg, world):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--nodes", type=int, default=N_NODES,
                     help="graph size (default: the config-2 size); smaller values only for profiling captures")
     ap.add_argument("--e2e-steps", type=int, default=3)
-    ap.add_argument("--mix", choices=["fp32", "bf16x3", "bf16"], default="fp32",
+    ap.add_argument("--mix", choices=["fp32", "bf16x3", "bf16"], default="bf16x3",
                     help="radial-mix arithmetic: fp32 CUDA cores, bf16x3 / bf16 tensor cores")
     args = ap.parse_args()
     if args.impl == "reference":

@@ -7,7 +7,9 @@
 
 #include <algorithm>
 #include <atomic>
+#include <mutex>
 #include <string>
+#include <vector>
 
 #include <cuda_bf16.h>
 
@@ -69,6 +71,42 @@ static thread_local std::string g_last_error;
 static std::atomic<long long> g_launches{0};
 
 void count_launches(int n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+struct ProfRec {
+    std::string name;
+    cudaEvent_t a = nullptr, b = nullptr;
+};
+static std::mutex g_prof_mu;
+static bool g_prof_on = false;
+static std::vector<ProfRec> g_prof;
+
+static void prof_clear_locked() {
+    for (ProfRec &r : g_prof) {
+        if (r.a) cudaEventDestroy(r.a);
+        if (r.b) cudaEventDestroy(r.b);
+    }
+    g_prof.clear();
+}
+
+void prof_begin(const char *name, cudaStream_t s) {
+    std::lock_guard<std::mutex> lk(g_prof_mu);
+    if (!g_prof_on) return;
+    ProfRec r;
+    r.name = name;
+    if (cudaEventCreate(&r.a) != cudaSuccess || cudaEventCreate(&r.b) != cudaSuccess ||
+        cudaEventRecord(r.a, s) != cudaSuccess) {
+        if (r.a) cudaEventDestroy(r.a);
+        if (r.b) cudaEventDestroy(r.b);
+        return;
+    }
+    g_prof.push_back(r);
+}
+
+void prof_end(cudaStream_t s) {
+    std::lock_guard<std::mutex> lk(g_prof_mu);
+    if (!g_prof_on || g_prof.empty()) return;
+    cudaEventRecord(g_prof.back().b, s);
+}
 
 void record_cuda_error(cudaError_t err) {
     g_last_error = std::string(cudaGetErrorName(err)) + ": " + cudaGetErrorString(err);
@@ -364,15 +402,23 @@ static int run_edgewise_tc(const FeqEdgewiseArgs *a, const MixLayout &M, const R
     const bool split = a->mix_mode == FEQ_MIX_BF16X3;
     Binning bins{a->bin_param1, a->bin_param2, a->num_bins, a->log_bins ? 1 : 0};
     int rc;
-    if ((rc = launch_binning(a->distances, E, bins, b.keys, nullptr, s)) != FEQ_OK) return rc;
-    if ((rc = launch_edge_sort<int32_t>(b.keys, E, a->num_bins, b.perm, b.offsets, nullptr, b.sort_ws,
-                                        b.sort_ws_bytes, s)) != FEQ_OK)
-        return rc;
-    if ((rc = launch_build_tiles(b.offsets, a->num_bins, 128, b.tiles, b.num_tiles, s)) != FEQ_OK) return rc;
-    if ((rc = launch_tc_relayout_b(a->radial_table, b.B_hi, b.B_lo, a->num_bins + 1, a->c_in, a->c_out, M.wdim, T.G,
-                                   T.b_total, s)) != FEQ_OK)
-        return rc;
+    {
+        ProfScope ps("bin_sort_tiles", s);
+        if ((rc = launch_binning(a->distances, E, bins, b.keys, nullptr, s)) != FEQ_OK) return rc;
+        if ((rc = launch_edge_sort<int32_t>(b.keys, E, a->num_bins, b.perm, b.offsets, nullptr, b.sort_ws,
+                                            b.sort_ws_bytes, s)) != FEQ_OK)
+            return rc;
+        if ((rc = launch_build_tiles(b.offsets, a->num_bins, 128, b.tiles, b.num_tiles, s)) != FEQ_OK) return rc;
+    }
+    {
+        ProfScope ps("relayout_table", s);
+        if ((rc = launch_tc_relayout_b(a->radial_table, b.B_hi, b.B_lo, a->num_bins + 1, a->c_in, a->c_out, M.wdim,
+                                       T.G, T.b_total, s)) != FEQ_OK)
+            return rc;
+    }
     // directions given: streaming bulk-copy kernels; dense bases or unaligned rows: general kernels
+    {
+    ProfScope ps("rotate_in", s);
     rc = launch_rot_in_stream(a->x, a->src, a->num_src_rows, a->edge_add, a->directions, a->distances, b.perm, E,
                               a->c_in, Li, T.in_map, T.k_total, bins, a->sh_scale, split, b.A_hi, b.A_lo, b.tval,
                               a->status, s);
@@ -380,15 +426,18 @@ static int run_edgewise_tc(const FeqEdgewiseArgs *a, const MixLayout &M, const R
         rc = launch_rotate_in_tc(a->x, a->src, a->num_src_rows, a->edge_add, a->directions, a->P_in, a->distances,
                                  b.perm, E, a->c_in, Li, T.in_map, T.k_total, bins, a->sh_scale, split, b.A_hi,
                                  b.A_lo, b.tval, a->status, s);
+    }
     if (rc != FEQ_OK) return rc;
     for (int m = 0; m < T.G.n_blocks; m++) {
         const TcBlockGeom &g = T.G.g[m];
         const int64_t b_rows = (int64_t)(a->num_bins + 1) * g.npad;
+        ProfScope ps("tc_mix", s);
         if ((rc = launch_tc_mix(split ? 3 : 1, b.A_hi, b.A_lo, E, T.k_total, b.B_hi + g.boff,
                                 split ? b.B_lo + g.boff : nullptr, b_rows, g, T.koff[m], T.nvalid[m], T.n_total,
                                 T.noff[m], b.tiles, b.num_tiles, b.max_tiles, b.tval, b.H, a->status, s)) != FEQ_OK)
             return rc;
     }
+    ProfScope ps("rotate_out", s);
     rc = launch_rot_out_stream(b.H, T.n_total, a->directions, a->distances, b.perm, E, a->c_out, Lo, T.out_map,
                                a->sh_scale, a->out, a->status, s);
     if (rc == FEQ_ERR_UNSUPPORTED)
@@ -421,6 +470,50 @@ const char *feq_last_error(void) { return g_last_error.c_str(); }
 
 int64_t feq_launch_count(void) { return (int64_t)g_launches.load(); }
 
+int feq_profile_enable(int32_t on) {
+    std::lock_guard<std::mutex> lk(g_prof_mu);
+    if (on) {
+        for (ProfRec &r : g_prof) cudaEventSynchronize(r.b);
+        prof_clear_locked();
+    }
+    g_prof_on = on != 0;
+    return FEQ_OK;
+}
+
+int feq_profile_read(int32_t index, char *name, int32_t name_capacity, double *total_ms, int64_t *launches) {
+    std::lock_guard<std::mutex> lk(g_prof_mu);
+    std::vector<std::string> names;
+    std::vector<double> ms;
+    std::vector<int64_t> cnt;
+    for (ProfRec &r : g_prof) {
+        float t = 0.0f;
+        cudaError_t e = cudaEventSynchronize(r.b);
+        if (e == cudaSuccess) e = cudaEventElapsedTime(&t, r.a, r.b);
+        if (e != cudaSuccess) {
+            record_cuda_error(e);
+            return -FEQ_ERR_CUDA;
+        }
+        size_t k = 0;
+        while (k < names.size() && names[k] != r.name) k++;
+        if (k == names.size()) {
+            names.push_back(r.name);
+            ms.push_back(0.0);
+            cnt.push_back(0);
+        }
+        ms[k] += t;
+        cnt[k] += 1;
+    }
+    if (index >= 0 && index < (int32_t)names.size()) {
+        if (name && name_capacity > 0) {
+            strncpy(name, names[index].c_str(), (size_t)name_capacity - 1);
+            name[name_capacity - 1] = 0;
+        }
+        if (total_ms) *total_ms = ms[index];
+        if (launches) *launches = cnt[index];
+    }
+    return (int)names.size();
+}
+
 int feq_wigner_basis(const float *directions, int64_t num_edges, const int32_t *lvals, int32_t num_lvals,
                      int32_t layout, float *out, feq_stream_t stream) {
     if (num_edges < 0 || (layout != FEQ_BASIS_MFIRST && layout != FEQ_BASIS_ROT_TO_EZ))
@@ -431,6 +524,7 @@ int feq_wigner_basis(const float *directions, int64_t num_edges, const int32_t *
     if (num_edges == 0) return FEQ_OK;
     if (!directions || !out) return FEQ_ERR_INVALID_ARGUMENT;
     if (num_edges > 0x7fffffffll * 8) return FEQ_ERR_UNSUPPORTED;
+    ProfScope ps("basis", (cudaStream_t)stream);
     rc = launch_basis_stream(directions, num_edges, L, layout == FEQ_BASIS_MFIRST ? 1 : 0, out, (cudaStream_t)stream);
     if (rc == FEQ_ERR_UNSUPPORTED) rc = launch_basis(directions, num_edges, L, layout, out, (cudaStream_t)stream);
     return rc;

@@ -145,6 +145,16 @@ void record_cuda_error(cudaError_t err);
 void record_error_text(const char *msg);
 void count_launches(int n);
 
+// Stage timing: while profiling is enabled, ProfScope records an event pair around
+// the work enqueued during its lifetime on stream s.
+void prof_begin(const char *name, cudaStream_t s);
+void prof_end(cudaStream_t s);
+struct ProfScope {
+    cudaStream_t s;
+    ProfScope(const char *name, cudaStream_t st) : s(st) { prof_begin(name, s); }
+    ~ProfScope() { prof_end(s); }
+};
+
 // Workspace carving: every region 256-byte aligned.
 struct WsCarver {
     char *base;

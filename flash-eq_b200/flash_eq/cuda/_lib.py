@@ -52,6 +52,9 @@ SIGNATURES = {
     "feq_abi_version": (ctypes.c_int, []),
     "feq_last_error": (ctypes.c_char_p, []),
     "feq_launch_count": (ctypes.c_int64, []),
+    "feq_profile_enable": (ctypes.c_int, [ctypes.c_int32]),
+    "feq_profile_read": (ctypes.c_int, [ctypes.c_int32, ctypes.c_char_p, ctypes.c_int32,
+                                        ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int64)]),
     "feq_wigner_basis": (ctypes.c_int, [c_vp, ctypes.c_int64, c_i32p, ctypes.c_int32, ctypes.c_int32, c_vp, c_vp]),
     "feq_edge_binning": (ctypes.c_int, [c_vp, ctypes.c_int64, ctypes.c_float, ctypes.c_float, ctypes.c_int32,
                                         ctypes.c_int32, c_vp, c_vp, c_vp]),

@@ -286,3 +286,23 @@ def attn_pool(qk, v, src, distances, perm, offsets, num_nodes, num_heads, scale,
     rc = lib.feq_attn_pool_fwd(ctypes.byref(a), _stream(qk.device))
     _lib.check(rc, "feq_attn_pool_fwd")
     return out
+
+
+def profile_enable(on: bool = True) -> None:
+    """Start (or stop) recording CUDA-event stage timings inside the native library."""
+    _lib.load().feq_profile_enable(1 if on else 0)
+
+
+def profile_read() -> dict:
+    """{stage: (total_ms, launches)} of the stages recorded since profile_enable(True)."""
+    lib = _lib.load()
+    n = lib.feq_profile_read(-1, None, 0, None, None)
+    if n < 0:
+        _lib.check(-n, "feq_profile_read")
+    out = {}
+    for i in range(n):
+        buf = ctypes.create_string_buffer(64)
+        ms, cnt = ctypes.c_double(), ctypes.c_int64()
+        lib.feq_profile_read(i, buf, 64, ctypes.byref(ms), ctypes.byref(cnt))
+        out[buf.value.decode()] = (ms.value, cnt.value)
+    return out

@@ -24,7 +24,7 @@ from ..representations.wigner import LazyBasis, basis_source
 from .radial import SeparableRadialNet
 
 
-DEFAULT_MIX_PRECISION = "fp32"
+DEFAULT_MIX_PRECISION = "bf16x3"
 
 
 def _dense(M):

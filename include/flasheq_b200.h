@@ -66,6 +66,15 @@ const char *feq_last_error(void);
  * sort call is counted once per kernel it launches: 3).  No counterpart in the
  * reference; used by benchmarks to report how many native kernels ran. */
 int64_t feq_launch_count(void);
+/* Stage timing (no counterpart in the reference).  While enabled, each kernel stage
+ * of the Wigner basis and of the edgewise path is bracketed by two CUDA events
+ * recorded on the stream the stage is launched on.  feq_profile_enable(1) starts a
+ * new record set (0 stops recording).  feq_profile_read synchronises the events and
+ * returns the number of distinct stages; for 0 <= index < that number it also fills
+ * the stage name, the summed event time in milliseconds and the number of launches.
+ * Returns a negative status on error. */
+int feq_profile_enable(int32_t on);
+int feq_profile_read(int32_t index, char *name, int32_t name_capacity, double *total_ms, int64_t *launches);
 
 /* ---------------------------------------------------------------------------
  * Wigner-D basis.
