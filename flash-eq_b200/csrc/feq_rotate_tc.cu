@@ -254,6 +254,9 @@ template <int L> struct WA;
         __device__ __forceinline__ static void wm(const float *tv, float sl, float (&m)[kNnz]) {          \
             feq_wm_l##LL(tv, sl, m);                                                                      \
         }                                                                                                 \
+        __device__ __forceinline__ static void wmd(const float *tv, float (&M)[(2 * LL + 1) * (2 * LL + 1)]) { \
+            feq_wmd_l##LL(tv, M);                                                                         \
+        }                                                                                                 \
         template <bool kT>                                                                                \
         __device__ __forceinline__ static void wa(const float (&m)[kNnz], const float (&g)[2 * LL + 1],   \
                                                   float (&h)[2 * LL + 1]) {                               \
@@ -682,6 +685,132 @@ basis_warp_kernel(const float *__restrict__ dirs, int64_t E, const __grid_consta
     }
 }
 
+// Dense basis, one lane per edge.  For each irrep (uniform over the warp) every lane
+// builds its edge's M_l in registers and forms the block row by row:
+//   row a of D   (kT = false):  u = R[a] M,    v = R u
+//   row a of D^T (kT = true):   u = M R[a]^T,  v = R u
+// (R = R(phi): R[x][x] = cos m phi, R[l-m][l+m] = sin m phi, R[l+m][l-m] = -sin m phi),
+// which equals D = R M R^T entry by entry.  Up to kBasisRows consecutive output rows
+// of the 32 edges of the group are staged in shared memory (zeros outside the block)
+// and written per edge as one contiguous run of rows.
+constexpr int kBasisRows = 5;
+
+template <int Lg, bool kT>
+__device__ __forceinline__ void basis_irrep(const float *__restrict__ tr, int lmax, int off, const int16_t *colpos,
+                                            float *stage, int S, int lane, int ng, float *__restrict__ out,
+                                            int d, int64_t g0) {
+    constexpr int N = 2 * Lg + 1;
+    const float *tv = tr, *cp = tr + 2 * lmax + 1, *sp = cp + lmax + 1;
+    float M[N * N];
+    WA<Lg>::wmd(tv, M);
+    float c[Lg + 1], sn[Lg + 1];
+#pragma unroll
+    for (int m = 0; m <= Lg; m++) {
+        c[m] = cp[m];
+        sn[m] = sp[m];
+    }
+    auto rdiag = [&](int x) { return x == Lg ? 1.0f : c[x < Lg ? Lg - x : x - Lg]; };
+    auto roff = [&](int x) { return x < Lg ? sn[Lg - x] : (x > Lg ? -sn[x - Lg] : 0.0f); };
+    const int64_t dd = (int64_t)d * d;
+    float *mine = stage + lane * S;
+#pragma unroll
+    for (int a0 = 0; a0 < N; a0 += kBasisRows) {
+        constexpr int kR = kBasisRows;
+        const int rows = N - a0 < kR ? N - a0 : kR;
+#pragma unroll
+        for (int ar = 0; ar < kR; ar++) {
+            const int a = a0 + ar;
+            if (a >= N) break;
+            const int pa = 2 * Lg - a;
+            float u[N];
+#pragma unroll
+            for (int q = 0; q < N; q++) {
+                const float mq = kT ? M[q * N + a] : M[a * N + q];
+                const float mp = kT ? M[q * N + pa] : M[pa * N + q];
+                u[q] = a == Lg ? mq : rdiag(a) * mq + roff(a) * mp;
+            }
+#pragma unroll
+            for (int b = 0; b < N; b++) {
+                const int pb = 2 * Lg - b;
+                mine[ar * d + colpos[off + b]] = b == Lg ? u[b] : rdiag(b) * u[b] + roff(b) * u[pb];
+            }
+        }
+        __syncwarp();
+        const int run = rows * d;
+        for (int e = 0; e < ng; e++) {
+            float *dst = out + (g0 + e) * dd + (int64_t)(off + a0) * d;
+            const float *srow = stage + e * S;
+            for (int i = lane; i < run; i += 32) dst[i] = srow[i];
+        }
+        __syncwarp();
+#pragma unroll
+        for (int ar = 0; ar < kR; ar++) {
+            if (a0 + ar >= N) break;
+#pragma unroll
+            for (int b = 0; b < N; b++) mine[ar * d + colpos[off + b]] = 0.0f;
+        }
+        __syncwarp();
+    }
+}
+
+__global__ void __launch_bounds__(kRotWarps * 32)
+basis_lane_kernel(const float *__restrict__ dirs, int64_t E, const __grid_constant__ ReprLayout Lp, int mfirst,
+                  int per_warp, float *__restrict__ out) {
+    extern __shared__ __align__(128) float dsm[];
+    __shared__ ReprLayout L;
+    __shared__ int16_t colpos[kMaxDim];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    copy_layout(Lp, L);
+    __syncthreads();
+    // std position of a D column -> output column (m-first position, or itself)
+    for (int i = threadIdx.x; i < L.dim; i += blockDim.x) colpos[i] = mfirst ? L.inv_perm[i] : (int16_t)i;
+    __syncthreads();
+    const int d = L.dim, S = (kBasisRows * d) | 1, TF = trig_floats(L.lmax);
+    float *trig = dsm + (size_t)w * per_warp;
+    float *stage = trig + pad4(kGroup * TF);
+    for (int i = lane; i < kGroup * S; i += 32) stage[i] = 0.0f;
+    __syncwarp();
+    const float *tr = trig + lane * TF;
+    for (int64_t g0 = ((int64_t)blockIdx.x * kRotWarps + w) * kGroup; g0 < E;
+         g0 += (int64_t)gridDim.x * kRotWarps * kGroup) {
+        const int ng = (int)min64(kGroup, E - g0);
+        {
+            const int64_t e = g0 + min(lane, ng - 1);
+            edge_trig_compact(dirs[e * 3], dirs[e * 3 + 1], dirs[e * 3 + 2], L.lmax, trig + lane * TF);
+        }
+        __syncwarp();
+        for (int r = 0; r < L.n_irreps; r++) {
+            const int l = L.irrep_l[r], off = L.irrep_off[r];
+#define FEQ_BASIS_CASE(LL)                                                                                   \
+    case LL:                                                                                                 \
+        if (mfirst) basis_irrep<LL, false>(tr, L.lmax, off, colpos, stage, S, lane, ng, out, d, g0);           \
+        else basis_irrep<LL, true>(tr, L.lmax, off, colpos, stage, S, lane, ng, out, d, g0);                   \
+        break;
+            switch (l) {
+                case 0: {
+                    stage[lane * S + colpos[off]] = 1.0f;
+                    __syncwarp();
+                    for (int e = 0; e < ng; e++)
+                        for (int j = lane; j < d; j += 32)
+                            out[(g0 + e) * (int64_t)d * d + (int64_t)off * d + j] = stage[e * S + j];
+                    __syncwarp();
+                    stage[lane * S + colpos[off]] = 0.0f;
+                    __syncwarp();
+                    break;
+                }
+                FEQ_BASIS_CASE(1)
+                FEQ_BASIS_CASE(2)
+                FEQ_BASIS_CASE(3)
+                FEQ_BASIS_CASE(4)
+                FEQ_BASIS_CASE(5)
+                FEQ_BASIS_CASE(6)
+            }
+#undef FEQ_BASIS_CASE
+        }
+        __syncwarp();
+    }
+}
+
 }  // namespace
 
 static bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -758,6 +887,18 @@ int launch_rot_out_stream(const float *H, int h_ld, const float *dirs, const flo
 // Dense basis matrices, warp per edge.  FEQ_ERR_UNSUPPORTED when the layout does not fit.
 int launch_basis_stream(const float *dirs, int64_t E, const ReprLayout &L, int mfirst, float *out, cudaStream_t s) {
     if (E == 0) return FEQ_OK;
+    if (L.lmax <= kFactoredLmax) {
+        const int per_warp = pad4(kGroup * trig_floats(L.lmax)) + pad4(kGroup * ((kBasisRows * L.dim) | 1));
+        const size_t smem = (size_t)kRotWarps * per_warp * 4;
+        if (smem <= 160 * 1024) {
+            FEQ_CUDA_TRY(cudaFuncSetAttribute(basis_lane_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              (int)smem));
+            const int grid = rot_grid((const void *)basis_lane_kernel, smem, E);
+            basis_lane_kernel<<<grid, kRotWarps * 32, smem, s>>>(dirs, E, L, mfirst, per_warp, out);
+            FEQ_LAUNCH_CHECK();
+            return FEQ_OK;
+        }
+    }
     const int scratch = rot_scratch(L).total();
     const size_t smem = (size_t)kRotWarps * scratch * 4;
     if (smem + sizeof(RotShared) > 200 * 1024) return FEQ_ERR_UNSUPPORTED;

@@ -271,37 +271,80 @@ __global__ void tc_relayout_b_rows_kernel(const float *__restrict__ T, __nv_bflo
     const int co = blockIdx.x, b = blockIdx.y;
     const int64_t slice = (int64_t)Cin * wdim;
     const float *src = T + ((int64_t)b * Cout + co) * slice;
-    for (int64_t i = threadIdx.x; i < slice; i += blockDim.x) tw[i] = __ldg(src + i);
+    if ((slice & 3) == 0 && (reinterpret_cast<uintptr_t>(T) & 15) == 0) {
+        const float4 *s4 = reinterpret_cast<const float4 *>(src);
+        for (int64_t i = threadIdx.x; i < slice / 4; i += blockDim.x) reinterpret_cast<float4 *>(tw)[i] = __ldg(s4 + i);
+    } else {
+        for (int64_t i = threadIdx.x; i < slice; i += blockDim.x) tw[i] = __ldg(src + i);
+    }
     __syncthreads();
     for (int q = 0; q < G.n_blocks; q++) {
         const TcBlockGeom &B = G.g[q];
         const int kin = B.mult * B.n_in, kout = B.mult * B.n_out;
         const int kvalid = (B.n_in > 0 && B.n_out > 0) ? Cin * kin : 0;
         const int nreal = Cout * kout;
-        // rows owned by this block: rn * Cout + co, and the padding rows when co == 0
-        const int nrows = kout + (co == 0 ? B.npad - nreal : 0);
-        for (int rr = 0; rr < nrows; rr++) {
-            const bool real = rr < kout;
-            const int n = real ? rr * Cout + co : nreal + (rr - kout);
-            const int o = real ? rr / B.mult : 0, oc = real ? rr - o * B.mult : 0;
-            __nv_bfloat16 *rh = Bhi + B.boff + ((int64_t)b * B.npad + n) * B.kpad;
-            __nv_bfloat16 *rl = Blo ? Blo + B.boff + ((int64_t)b * B.npad + n) * B.kpad : nullptr;
-            for (int k = threadIdx.x; k < B.kpad; k += blockDim.x) {
-                float v = 0.0f;
-                if (real && k < kvalid) {
-                    const int ci = k % Cin, rk = k / Cin, i = rk / B.mult, ic = rk - i * B.mult;
-                    const float *w = tw + ci * wdim + B.w_off;
+        const int nq = Cin >> 2;
+        auto row_ptrs = [&](int n, __nv_bfloat16 *&rh, __nv_bfloat16 *&rl) {
+            rh = Bhi + B.boff + ((int64_t)b * B.npad + n) * B.kpad;
+            rl = Blo ? Blo + B.boff + ((int64_t)b * B.npad + n) * B.kpad : nullptr;
+        };
+        auto put4 = [&](__nv_bfloat16 *rh, __nv_bfloat16 *rl, int k0, const float (&v)[4]) {
+            const __nv_bfloat162 h01 = __floats2bfloat162_rn(v[0], v[1]), h23 = __floats2bfloat162_rn(v[2], v[3]);
+            uint2 hv;
+            hv.x = *reinterpret_cast<const uint32_t *>(&h01);
+            hv.y = *reinterpret_cast<const uint32_t *>(&h23);
+            *reinterpret_cast<uint2 *>(rh + k0) = hv;
+            if (rl) {
+                const float2 f01 = __bfloat1622float2(h01), f23 = __bfloat1622float2(h23);
+                const __nv_bfloat162 l01 = __floats2bfloat162_rn(v[0] - f01.x, v[1] - f01.y);
+                const __nv_bfloat162 l23 = __floats2bfloat162_rn(v[2] - f23.x, v[3] - f23.y);
+                uint2 lv;
+                lv.x = *reinterpret_cast<const uint32_t *>(&l01);
+                lv.y = *reinterpret_cast<const uint32_t *>(&l23);
+                *reinterpret_cast<uint2 *>(rl + k0) = lv;
+            }
+        };
+        // real rows rr * Cout + co: items (rr, rk, cq) = 4 input channels 4cq..4cq+3 of K row rk
+        if (kvalid > 0) {
+            const int items = kout * kin * nq;
+            for (int it = threadIdx.x; it < items; it += blockDim.x) {
+                const int cq = it % nq, t = it / nq, rk = t % kin, rr = t / kin;
+                const int o = rr / B.mult, oc = rr - o * B.mult, i = rk / B.mult, ic = rk - i * B.mult;
+                float v[4];
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    const float *w = tw + (4 * cq + u) * wdim + B.w_off;
                     if (B.mult == 1) {
-                        v = w[o * B.n_in + i];
+                        v[u] = w[o * B.n_in + i];
                     } else {
                         const float a = w[2 * (o * B.n_in + i)], bb = w[2 * (o * B.n_in + i) + 1];
-                        v = (oc == ic) ? a : (oc == 0 ? bb : -bb);   // (re,im) -> b, (im,re) -> -b
+                        v[u] = (oc == ic) ? a : (oc == 0 ? bb : -bb);   // (re,im) -> b, (im,re) -> -b
                     }
                 }
-                const __nv_bfloat16 hi = __float2bfloat16_rn(v);
-                rh[k] = hi;
-                if (rl) rl[k] = __float2bfloat16_rn(v - __bfloat162float(hi));
+                __nv_bfloat16 *rh, *rl;
+                row_ptrs(rr * Cout + co, rh, rl);
+                put4(rh, rl, rk * Cin + 4 * cq, v);
             }
+        }
+        // zeros: K padding of the real rows, and (co == 0) the N padding rows
+        const float z4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        const int kz = B.kpad - kvalid;           // multiple of 4
+        if (kvalid > 0 && kz > 0) {
+            const int zq = kz >> 2;
+            for (int it = threadIdx.x; it < kout * zq; it += blockDim.x) {
+                const int rr = it / zq, k0 = kvalid + 4 * (it - rr * zq);
+                __nv_bfloat16 *rh, *rl;
+                row_ptrs(rr * Cout + co, rh, rl);
+                put4(rh, rl, k0, z4);
+            }
+        }
+        const int zrows = (kvalid > 0 ? 0 : kout) + (co == 0 ? B.npad - nreal : 0);
+        for (int it = threadIdx.x; it < zrows * (B.kpad >> 2); it += blockDim.x) {
+            const int zr = it / (B.kpad >> 2), k0 = 4 * (it - zr * (B.kpad >> 2));
+            const int n = (kvalid > 0 || zr >= kout) ? nreal + (zr - (kvalid > 0 ? 0 : kout)) : zr * Cout + co;
+            __nv_bfloat16 *rh, *rl;
+            row_ptrs(n, rh, rl);
+            put4(rh, rl, k0, z4);
         }
     }
 }
@@ -346,7 +389,7 @@ int launch_tc_relayout_b(const float *T, __nv_bfloat16 *Bhi, __nv_bfloat16 *Blo,
                          int wdim, const TcGeom &G, int64_t total, cudaStream_t s) {
     if (total == 0) return FEQ_OK;
     const size_t smem = (size_t)Cin * wdim * 4;
-    if (smem <= 96 * 1024 && Cout <= 65535 && nb1 <= 65535) {
+    if (smem <= 96 * 1024 && Cout <= 65535 && nb1 <= 65535 && Cin % 4 == 0 && Cin / 4 <= 256) {
         if (smem > 48 * 1024)
             FEQ_CUDA_TRY(cudaFuncSetAttribute(tc_relayout_b_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                               (int)smem));

@@ -183,6 +183,7 @@ def write_apply(path: str, lgen: int) -> None:
 
     feq_wm_l<l>(tv, sl, m):  the nonzero entries of s^l M_l(theta'), each a short sum of
                               the trig terms tv[k] with constant coefficients;
+    feq_wmd_l<l>(tv, M):      all (2l+1)^2 entries of M_l(theta'), row-major (dense);
     feq_wa_l<l><kT>(m, g, h): h = g M_l (kT = false) or h = g M_l^T (kT = true), row
                               vectors, only the nonzero entries of M_l.
     """
@@ -198,6 +199,11 @@ def write_apply(path: str, lgen: int) -> None:
         for k, e in enumerate(ents):
             terms = [f"{t[e, q]:.9e}f * tv[{q}]" for q in range(n) if abs(t[e, q]) > 1e-7]
             out.append(f"    m[{k}] = sl * ({' + '.join(terms)});")
+        out.append("}")
+        out.append(f"__device__ __forceinline__ void feq_wmd_l{l}(const float *tv, float (&M)[{n * n}]) {{")
+        for e in range(n * n):
+            terms = [f"{t[e, q]:.9e}f * tv[{q}]" for q in range(n) if abs(t[e, q]) > 1e-7]
+            out.append(f"    M[{e}] = {' + '.join(terms) if terms else '0.0f'};")
         out.append("}")
         out.append(f"template <bool kT> __device__ __forceinline__ void feq_wa_l{l}("
                    f"const float (&m)[{len(ents)}], const float (&g)[{n}], float (&h)[{n}]) {{")
