@@ -464,7 +464,7 @@ const char *feq_status_string(int status) {
     }
 }
 
-int feq_abi_version(void) { return 1; }
+int feq_abi_version(void) { return 2; }
 
 const char *feq_last_error(void) { return g_last_error.c_str(); }
 
@@ -704,6 +704,7 @@ int feq_attn_pool_fwd(const FeqAttnArgs *a, feq_stream_t stream) {
     if (!a->qk || !a->perm || !a->offsets || !a->out || (a->num_edges > 0 && (!a->v || !a->src)))
         return FEQ_ERR_INVALID_ARGUMENT;
     if (a->decay_scale > 0.0f && !a->distances) return FEQ_ERR_INVALID_ARGUMENT;
+    if (a->k && a->num_src_nodes < 0) return FEQ_ERR_INVALID_ARGUMENT;
     return launch_attn_pool(*a, (cudaStream_t)stream);
 }
 

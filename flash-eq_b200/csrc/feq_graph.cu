@@ -266,7 +266,9 @@ attn_pool_kernel(const __grid_constant__ FeqAttnArgs a) {
     __shared__ float corr_s[kAttnMaxHeads], m_s[kAttnMaxHeads], sum_s[kAttnMaxHeads];
     __shared__ int64_t eid_s[kAttnChunk], sid_s[kAttnChunk];
 
-    const float *qn = a.qk + n * (int64_t)(2 * qrow);
+    const bool split_k = a.k != nullptr;   // Q rows in qk, K rows in k (partitioned graphs)
+    const int64_t nsrc = split_k ? a.num_src_nodes : a.num_nodes;
+    const float *qn = a.qk + n * (int64_t)(split_k ? qrow : 2 * qrow);
     for (int j = threadIdx.x; j < qrow; j += kAttnThreads) q_s[j] = __ldg(qn + j);
     for (int j = threadIdx.x; j < vrow; j += kAttnThreads) acc_s[j] = 0.0f;
     if (threadIdx.x < H) {
@@ -281,7 +283,7 @@ attn_pool_kernel(const __grid_constant__ FeqAttnArgs a) {
         if (threadIdx.x < cn) {
             const int64_t e = a.perm[c0 + threadIdx.x];
             int64_t sidx = a.src[e];
-            if (sidx < 0 || sidx >= a.num_nodes) {
+            if (sidx < 0 || sidx >= nsrc) {
                 set_status(a.status, 1);
                 sidx = -1;
             }
@@ -295,7 +297,8 @@ attn_pool_kernel(const __grid_constant__ FeqAttnArgs a) {
             const int64_t sidx = sid_s[k];
             float acc = 0.0f;
             if (sidx >= 0) {
-                const float *kr = a.qk + sidx * (int64_t)(2 * qrow) + qrow + h * hd;
+                const float *kr = split_k ? a.k + sidx * (int64_t)qrow + h * hd
+                                          : a.qk + sidx * (int64_t)(2 * qrow) + qrow + h * hd;
                 const float *qr = q_s + h * hd;
                 for (int i = lane; i < hd; i += 32) acc = fmaf(qr[i], __ldg(kr + i), acc);
             }

@@ -42,9 +42,12 @@ class FeqAttnArgs(ctypes.Structure):
         ("num_nodes", ctypes.c_int64), ("num_edges", ctypes.c_int64), ("c_qk", ctypes.c_int32),
         ("d_qk", ctypes.c_int32), ("c_v", ctypes.c_int32), ("d_v", ctypes.c_int32),
         ("num_heads", ctypes.c_int32), ("scale", ctypes.c_float), ("decay_scale", ctypes.c_float),
-        ("reduce", ctypes.c_int32), ("out", c_vp), ("status", c_vp),
+        ("reduce", ctypes.c_int32), ("out", c_vp), ("status", c_vp), ("k", c_vp),
+        ("num_src_nodes", ctypes.c_int64),
     ]
 
+
+FEQ_ABI_VERSION = 2   # must equal feq_abi_version() of the loaded library
 
 # name -> (restype, argtypes)
 SIGNATURES = {
@@ -108,6 +111,9 @@ def load() -> ctypes.CDLL:
             fn = getattr(lib, name)
             fn.restype = res
             fn.argtypes = args
+        if lib.feq_abi_version() != FEQ_ABI_VERSION:
+            raise ImportError(f"{LIB_PATH} has ABI version {lib.feq_abi_version()}, this package needs "
+                              f"{FEQ_ABI_VERSION}: rebuild it with  make -C flash-eq_b200/csrc -j4")
         _lib = lib
     return _lib
 

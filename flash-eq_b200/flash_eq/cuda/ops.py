@@ -258,11 +258,23 @@ def segment_pool(rows, perm, offsets, num_nodes, reduce="sum", weights=None):
 
 
 def attn_pool(qk, v, src, distances, perm, offsets, num_nodes, num_heads, scale, decay, reduce="sum",
-              status=None):
-    """Fused softmax-attention pooling: QK (N, 2C, d) node rows, V (E, Cv, dv) edge rows."""
+              status=None, k=None):
+    """Fused softmax-attention pooling: QK (N, 2C, d) node rows, V (E, Cv, dv) edge rows.
+
+    With ``k`` given (partitioned graphs): ``qk`` holds only the destinations' Q rows
+    (num_nodes, C, d) and ``k`` the K rows of every source node (N_src, C, d); src indexes k.
+    """
     lib = _require_cuda(qk, v, src, perm, offsets)
     qk, v = _f32(qk, "QK"), _f32(v, "V")
+    if k is not None:
+        k = _f32(k, "K")
+        if k.shape[1:] != qk.shape[1:]:
+            raise ValueError(f"K rows {tuple(k.shape[1:])} do not match Q rows {tuple(qk.shape[1:])}")
+        qk_rows = qk.shape[0]
+        qk = qk.reshape(qk_rows, -1, qk.shape[-1])
     N, c2, d = qk.shape
+    if k is not None:
+        c2 = 2 * c2
     E, c_v, d_v = v.shape
     if E == 0:
         return torch.zeros(num_nodes, c_v, d_v, dtype=torch.float32, device=qk.device)
@@ -283,6 +295,9 @@ def attn_pool(qk, v, src, distances, perm, offsets, num_nodes, num_heads, scale,
     a.out = out.data_ptr()
     if status is not None:
         a.status = status.data_ptr()
+    if k is not None:
+        a.k = k.data_ptr()
+        a.num_src_nodes = int(k.shape[0])
     rc = lib.feq_attn_pool_fwd(ctypes.byref(a), _stream(qk.device))
     _lib.check(rc, "feq_attn_pool_fwd")
     return out

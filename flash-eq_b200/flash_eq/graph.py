@@ -56,6 +56,10 @@ class Graph:
         return Graph(src=src, dst=dst, num_nodes=num_nodes)
 
     # -- dst-sorted view ----------------------------------------------------
+    def _check_src(self):
+        """Device bool: some src index lies outside [0, num_nodes) (None without edges)."""
+        return ((self.src < 0) | (self.src >= self.num_nodes)).any() if self.num_edges else None
+
     def _key(self):
         return (self.src.data_ptr(), self.src._version, self.dst.data_ptr(), self.dst._version,
                 self.num_nodes, self.src.shape[0])
@@ -68,7 +72,7 @@ class Graph:
         from .cuda import ops
 
         perm, offsets, status = ops.edge_sort(self.dst, self.num_nodes)
-        bad_src = ((self.src < 0) | (self.src >= self.num_nodes)).any() if self.num_edges else None
+        bad_src = self._check_src()
         if int(status.item()) != 0:
             raise ValueError("graph.dst has indices outside [0, num_nodes)")
         if bad_src is not None and bool(bad_src):

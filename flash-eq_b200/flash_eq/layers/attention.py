@@ -20,6 +20,7 @@ import torch.nn as nn
 from ..cuda import ops
 from ..cuda.block_diagonal import forward_only
 from ..graph import Graph
+from ..partition import PartitionedGraph
 from ..representations import Repr
 from .linear import EquivariantEdgewiseLinear, EquivariantLinear
 from .norm import EquivariantLayerNorm
@@ -120,12 +121,25 @@ class EquivariantAttention(nn.Module):
         mult = self.in_repr.mult
         qk = self.linear_qk(self.norm_qk(node_features))        # (N, 2C, d) node level
         perm, offsets = graph.dst_segments()
-        V = self.linear_v._run(P, Q_basis, node_features, distances, src=graph.src, edge_add=edge_features)
+        k_src = None
+        x_src = node_features
+        if isinstance(graph, PartitionedGraph):
+            # src rows live on other ranks: one all-gather of the inputs and one of K per layer
+            x_src = graph.gather_nodes(node_features)
+            k_src = graph.gather_nodes(qk[:, mult:].contiguous())
+        V = self.linear_v._run(P, Q_basis, x_src, distances, src=graph.src, edge_add=edge_features)
         att = self.attention
         dropping = self.training and isinstance(att.dropout, nn.Dropout)
         if self.pool.reduce in ("sum", "mean") and not dropping:
             decay = att.distance_decay_scale
             scale = att._scale_value()
+            if k_src is not None:
+                def run_k(q, v, d, k):
+                    return ops.attn_pool(q.detach(), v.detach(), graph.src, None if d is None else d.detach(), perm,
+                                         offsets, graph.num_nodes, self.num_heads, scale, decay, self.pool.reduce,
+                                         k=k.detach())
+                return forward_only(run_k, qk[:, :mult].contiguous(), V, distances if decay is not None else None,
+                                    k_src)
 
             def run(q, v, d):
                 return ops.attn_pool(q.detach(), v.detach(), graph.src, None if d is None else d.detach(), perm,
@@ -135,7 +149,7 @@ class EquivariantAttention(nn.Module):
         # max pooling or attention dropout: materialise per-edge weights
         E = graph.num_edges
         Qe = qk[:, :mult][graph.dst].reshape(E, self.num_heads, -1)
-        Ke = qk[:, mult:][graph.src].reshape(E, self.num_heads, -1)
+        Ke = (qk[:, mult:] if k_src is None else k_src)[graph.src].reshape(E, self.num_heads, -1)
         w = att.dropout(att.attention_weights(Qe, Ke, graph, distances))
         return pool_edges(V, graph, self.pool.reduce, weights=w)
 

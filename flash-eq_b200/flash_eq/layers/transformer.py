@@ -13,6 +13,7 @@ import torch
 import torch.nn as nn
 
 from ..graph import Graph
+from ..partition import PartitionedGraph
 from ..representations import Repr, WignerDBasis
 from .attention import EquivariantAttention
 from .gating import EquivariantGating
@@ -119,7 +120,10 @@ class EquivariantTransformer(nn.Module):
         self.final_norm = SeparableEquivariantLayerNorm(out_repr)
 
     def forward(self, coordinates: torch.Tensor, node_features: torch.Tensor, graph: Graph) -> torch.Tensor:
-        edge_vectors = coordinates[graph.src] - coordinates[graph.dst]    # src - dst (transformer.py:406)
+        if isinstance(graph, PartitionedGraph):      # src / dst are not global node ids there
+            edge_vectors = graph.edge_vectors(coordinates)
+        else:
+            edge_vectors = coordinates[graph.src] - coordinates[graph.dst]    # src - dst (transformer.py:406)
         distances = edge_vectors.norm(dim=-1)
         m_in, m_hidden, m_out = self.basis.lazy(edge_vectors)
         x = node_features

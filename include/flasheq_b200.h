@@ -59,6 +59,7 @@ enum feq_status_code {
  * Library
  * ------------------------------------------------------------------------ */
 const char *feq_status_string(int status);
+/* 2: FeqAttnArgs gained k / num_src_nodes (partitioned graphs). */
 int feq_abi_version(void);
 /* Human-readable last CUDA error seen by this thread (empty when none). */
 const char *feq_last_error(void);
@@ -259,6 +260,11 @@ typedef struct FeqAttnArgs {
     int32_t reduce;           /* FEQ_REDUCE_SUM or FEQ_REDUCE_MEAN */
     float *out;               /* (N, c_v, d_v) */
     int32_t *status;          /* optional: 1 = a src index was out of range */
+    /* Partitioned graphs (no counterpart in the reference): when k is not NULL, qk holds
+     * only the destinations' Q rows (num_nodes, c_qk, d_qk), k holds the K rows of every
+     * source node (num_src_nodes, c_qk, d_qk) and src indexes k. */
+    const float *k;
+    int64_t num_src_nodes;
 } FeqAttnArgs;
 
 int feq_attn_pool_fwd(const FeqAttnArgs *args, feq_stream_t stream);

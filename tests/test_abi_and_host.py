@@ -38,7 +38,7 @@ def test_library_exports_every_declared_symbol():
     for n in names:
         assert hasattr(lib, n), n
     assert set(names) == set(_lib.SIGNATURES), "ctypes signatures and header diverge"
-    assert lib.feq_abi_version() == 1
+    assert lib.feq_abi_version() == _lib.FEQ_ABI_VERSION
     assert lib.feq_status_string(0) == b"ok"
 
 

@@ -1,0 +1,95 @@
+"""Host logic of the dst-range partition (no GPU): boundaries, edge ownership, the
+padded src numbering and the row exchange, with two gloo ranks on CPU."""
+from __future__ import annotations
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from flash_eq import Graph
+from flash_eq.partition import dst_range_bounds, partition_graph
+
+
+def _graph(n=500, k=7, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    dst = torch.arange(n).repeat_interleave(k)
+    src = torch.randint(0, n, (n * k,), generator=g)
+    # uneven in-degrees: drop a random third of the edges
+    keep = torch.rand(n * k, generator=g) > 0.33
+    return Graph(src=src[keep], dst=dst[keep], num_nodes=n)
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 8])
+def test_partition_covers_every_edge_once_and_balances(world):
+    gr = _graph()
+    parts = [partition_graph(gr, world, r) for r in range(world)]
+    ids = torch.cat([p.edge_ids for p in parts])
+    assert torch.equal(torch.sort(ids).values, torch.arange(gr.num_edges))
+    starts = [p.node_start for p in parts] + [parts[-1].node_end]
+    assert starts[0] == 0 and starts[-1] == gr.num_nodes
+    assert all(parts[r].node_end == parts[r + 1].node_start for r in range(world - 1))
+    E = gr.num_edges
+    max_deg = int(torch.bincount(gr.dst, minlength=gr.num_nodes).max())
+    for p in parts:
+        assert abs(p.num_edges - E / world) <= max_deg + 1
+        assert torch.equal(p.dst + p.node_start, gr.dst[p.edge_ids])
+        assert torch.equal(p.src_global, gr.src[p.edge_ids])
+        assert int(p.dst.min()) >= 0 and int(p.dst.max()) < p.num_nodes
+
+
+def test_padded_src_numbering_matches_gathered_rows():
+    gr = _graph(n=301)
+    world = 4
+    parts = [partition_graph(gr, world, r) for r in range(world)]
+    x = torch.randn(gr.num_nodes, 3, 2)
+    rows = parts[0].rows_per_rank
+    gathered = torch.zeros(world * rows, 3, 2)
+    for r, p in enumerate(parts):
+        gathered[r * rows: r * rows + p.num_nodes] = x[p.node_start:p.node_end]
+    for p in parts:
+        assert torch.equal(gathered[p.src], x[p.src_global])
+
+
+def test_bounds_empty_and_single():
+    b = dst_range_bounds(torch.zeros(0, dtype=torch.long), 5, 3)
+    assert b.tolist()[0] == 0 and b.tolist()[-1] == 5 and torch.all(b[1:] >= b[:-1])
+    b = dst_range_bounds(torch.tensor([2, 2, 2]), 4, 2)
+    assert b.tolist()[0] == 0 and b.tolist()[-1] == 4
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        gr = _graph(n=257, seed=3)
+        x = torch.randn(gr.num_nodes, 4, 9, generator=torch.Generator().manual_seed(5))
+        p = partition_graph(gr, world, rank)
+        full = p.gather_nodes(x[p.node_start:p.node_end].contiguous())
+        q.put((rank, bool(torch.equal(full[p.src], x[p.src_global])), full.shape[0] == world * p.rows_per_rank))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gather_nodes_two_gloo_ranks():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for pr in procs:
+        pr.start()
+    res = [q.get(timeout=120) for _ in procs]
+    for pr in procs:
+        pr.join(timeout=60)
+        assert pr.exitcode == 0
+    assert all(ok and shape for _, ok, shape in res)
