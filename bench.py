@@ -278,6 +278,9 @@ def run_reference(args):
 
 
 def config_block(n_gpus, n_nodes=N_NODES):
+    if LVALS != [0, 1, 2, 3, 4]:
+        return {"workload": f"variant: config-2 graph (N={n_nodes}) with Repr({LVALS}, {MULT}) in and out",
+                "edges_per_gpu": n_nodes * K_NN, "global_edges": n_nodes * K_NN * n_gpus}
     if n_nodes != N_NODES:
         return {"workload": f"profiling case: config-2 shapes with N={n_nodes} nodes, E={n_nodes * K_NN}",
                 "edges_per_gpu": n_nodes * K_NN, "global_edges": n_nodes * K_NN * n_gpus}
@@ -505,9 +508,13 @@ def main():
     ap.add_argument("--nodes", type=int, default=N_NODES,
                     help="graph size (default: the config-2 size); smaller values only for profiling captures")
     ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--lmax", type=int, default=4,
+                    help="degrees 0..lmax in and out (default 4 = config 2); other values are variants, not the metric")
     ap.add_argument("--mix", choices=["fp32", "bf16x3", "bf16"], default="bf16x3",
                     help="radial-mix arithmetic: fp32 CUDA cores, bf16x3 / bf16 tensor cores")
     args = ap.parse_args()
+    global LVALS
+    LVALS = list(range(args.lmax + 1))
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)
