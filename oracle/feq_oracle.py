@@ -46,8 +46,16 @@ MAX_L = 17  # block_diagonal.cu:172
 # C restatement loader
 # ----------------------------------------------------------------------------
 @lru_cache(maxsize=1)
-def _lib() -> ctypes.CDLL:
+def _stale() -> bool:
     if not os.path.isfile(_LIB_PATH):
+        return True
+    built = os.path.getmtime(_LIB_PATH)
+    return any(os.path.getmtime(os.path.join(_HERE, f)) > built
+               for f in ("block_diagonal_ref.c", "block_diagonal_bwd_ref.c"))
+
+
+def _lib() -> ctypes.CDLL:
+    if _stale():
         import subprocess
 
         subprocess.check_call(["make", "-s", "-C", _HERE], stdout=subprocess.DEVNULL)
@@ -66,6 +74,12 @@ def _lib() -> ctypes.CDLL:
     lib.oracle_binning_f32.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_float, ctypes.c_float,
                                        ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]
     lib.oracle_num_cpus.restype = ctypes.c_int
+    vp = ctypes.c_void_p
+    lib.oracle_bd_bwd_f64.restype = ctypes.c_int
+    lib.oracle_bd_bwd_f64.argtypes = [vp, vp, vp, vp, ctypes.c_int64, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                      ctypes.c_int, ctypes.c_int, i32p, ctypes.c_int, i32p, ctypes.c_int,
+                                      ctypes.c_float, ctypes.c_float, ctypes.c_float, ctypes.c_int, ctypes.c_int,
+                                      vp, vp, vp]
     return lib
 
 
@@ -250,6 +264,28 @@ def block_diagonal_fwd(features, table, dist, lvals_in, lvals_out, sh_scale, p1,
         if rc < 0:
             raise RuntimeError("oracle block-diagonal: unsupported layout")
     return torch.from_numpy(out) if as_torch else out
+
+
+def block_diagonal_bwd(grad_out, features, table, dist, lvals_in, lvals_out, sh_scale, p1, p2, num_bins,
+                       log_bins):
+    """block_diagonal_cuda backward on CPU in float64 (block_diagonal.cu:747-1161):
+    (grad_features, grad_table, grad_distances) as float64 torch tensors."""
+    c = lambda x: np.ascontiguousarray((x.detach().cpu().numpy() if isinstance(x, torch.Tensor) else x),
+                                       dtype=np.float64)
+    go, f, tb, ds = c(grad_out), c(features), c(table), c(dist)
+    E, Cin, Din = f.shape
+    Cout, Wdim = tb.shape[1], tb.shape[3]
+    Dout = go.shape[2]
+    gf = np.empty_like(f)
+    gt = np.empty_like(tb)
+    gd = np.empty(E, dtype=np.float64)
+    rc = _lib().oracle_bd_bwd_f64(go.ctypes.data, f.ctypes.data, tb.ctypes.data, ds.ctypes.data, E, Cin, Cout,
+                                  Din, Dout, Wdim, _i32arr(lvals_in), len(lvals_in), _i32arr(lvals_out),
+                                  len(lvals_out), float(sh_scale), float(p1), float(p2), int(num_bins),
+                                  int(bool(log_bins)), gf.ctypes.data, gt.ctypes.data, gd.ctypes.data)
+    if rc < 0:
+        raise RuntimeError("oracle block-diagonal backward: unsupported layout")
+    return torch.from_numpy(gf), torch.from_numpy(gt), torch.from_numpy(gd)
 
 
 def edgewise_fwd(P, Q, edge_features, distances, table, lvals_in, lvals_out, sh_scale,
