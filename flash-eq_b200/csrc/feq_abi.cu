@@ -50,7 +50,8 @@ int launch_tc_relayout_b(const float *T, __nv_bfloat16 *Bhi, __nv_bfloat16 *Blo,
 int launch_tc_mix(int split, const __nv_bfloat16 *A, const __nv_bfloat16 *A2, int64_t a_rows, int a_cols,
                   const __nv_bfloat16 *Bm, const __nv_bfloat16 *Bm2, int64_t b_rows, const TcBlockGeom &B,
                   int a_col0, int n_valid, int h_ld, int h_col0, const int4 *tiles, const int *num_tiles,
-                  int64_t max_tiles, const float *tval, float *H, int32_t *status, cudaStream_t s);
+                  int64_t max_tiles, const float *tval, float *H, int32_t *status, cudaStream_t s,
+                  float *Hd = nullptr);
 int launch_rotate_in_tc(const float *x, const int64_t *src, int64_t nsrc, const float *edge_add, const float *dirs,
                         const float *P, const float *dist, const int64_t *perm, int64_t E, int C,
                         const ReprLayout &L, const TcPosMap &M, int k_total, Binning bins, float sh_scale,
@@ -66,6 +67,22 @@ int launch_rot_in_stream(const float *x, const int64_t *src, int64_t nsrc, const
 int launch_rot_out_stream(const float *H, int h_ld, const float *dirs, const float *dist, const int64_t *perm,
                           int64_t E, int C, const ReprLayout &L, const TcPosMap &M, float sh_scale, float *out,
                           int32_t *status, cudaStream_t s);
+
+int launch_bwd_prep_rows(const float *X, const float *dist, const int64_t *perm, int64_t E, int C, int D,
+                         const TcPosMap &Mp, int ld, Binning bins, float sh_scale, __nv_bfloat16 *Mhi,
+                         __nv_bfloat16 *Mlo, float *tval, cudaStream_t s);
+int launch_bwd_transpose_table(const float *T, float *Tt, int nb1, int Cout, int Cin, int W, const MixLayout &M,
+                               cudaStream_t s);
+int launch_bwd_rows(const float *gA, const float *gAd, int ld_g, const __nv_bfloat16 *Ahi, const __nv_bfloat16 *Alo,
+                    int ld_a, const __nv_bfloat16 *Ghi, const __nv_bfloat16 *Glo, int ld_gg, const float *H, int ld_h,
+                    const float *dist, const int64_t *perm, int64_t E, int Cin, int Din, int Cout, int Dout,
+                    const TcPosMap &in1, const TcPosMap &out1, const TcPosMap &in2, const TcPosMap &out2,
+                    Binning bins, float sh_scale, int any_l, float *grad_f, float *grad_d, cudaStream_t s);
+int launch_bwd_table_gemm(const __nv_bfloat16 *Ghi, const __nv_bfloat16 *Glo, int ld_g, int g_col0, int N,
+                          const __nv_bfloat16 *Ahi, const __nv_bfloat16 *Alo, int ld_a, int a_col0, int K,
+                          const int64_t *offsets, const float *tval, int nb, float *dB, cudaStream_t s);
+int launch_bwd_table_convert(const float *dB, const DbOff &dboff, int nb1, int Cout, int Cin, int W,
+                             const MixLayout &M, float *grad_table, cudaStream_t s);
 
 static thread_local std::string g_last_error;
 static std::atomic<long long> g_launches{0};
@@ -446,6 +463,125 @@ static int run_edgewise_tc(const FeqEdgewiseArgs *a, const MixLayout &M, const R
     return rc;
 }
 
+
+// ---------------------------------------------------------------------------
+// Backward of the block-diagonal mix (see feq_backward.cu for the formulation).
+// ---------------------------------------------------------------------------
+struct BwdPlan {
+    MixLayout M, M2;          // forward layout and the in/out-swapped one
+    ReprLayout Li, Lo;
+    TcPlan T, T2;             // tensor-core plans: W_t A (T) and G W_t^T (T2)
+    DbOff dboff;
+    int64_t db_total;
+    int64_t table_floats;
+};
+
+static int build_bwd_plan(const int32_t *lin, int nin, const int32_t *lout, int nout, int Cin, int Cout, int nb,
+                          BwdPlan *P) {
+    int rc;
+    if ((rc = build_mix_layout(lin, nin, lout, nout, Cin, Cout, &P->M)) != FEQ_OK) return rc;
+    if ((rc = build_mix_layout(lout, nout, lin, nin, Cout, Cin, &P->M2)) != FEQ_OK) return rc;
+    if ((rc = build_repr_layout(lin, nin, &P->Li)) != FEQ_OK) return rc;
+    if ((rc = build_repr_layout(lout, nout, &P->Lo)) != FEQ_OK) return rc;
+    if ((rc = build_tc_plan(P->M, P->Li, P->Lo, Cin, Cout, nb, &P->T)) != FEQ_OK) return rc;
+    if ((rc = build_tc_plan(P->M2, P->Lo, P->Li, Cout, Cin, nb, &P->T2)) != FEQ_OK) return rc;
+    if (P->T.G.n_blocks != P->T2.G.n_blocks) return FEQ_ERR_UNSUPPORTED;
+    int64_t off = 0;
+    memset(&P->dboff, 0, sizeof(P->dboff));
+    for (int m = 0; m < P->T.G.n_blocks; m++) {
+        const TcBlockGeom &g = P->T.G.g[m];
+        P->dboff.off[m] = off;
+        off += (int64_t)(nb + 1) * (Cout * g.mult * g.n_out) * (Cin * g.mult * g.n_in);
+    }
+    P->db_total = off;
+    P->table_floats = (int64_t)(nb + 1) * Cout * Cin * P->M.wdim;
+    return FEQ_OK;
+}
+
+struct BwdBuffers {
+    TcBuffers f;                     // A, B, H, tval, keys, perm, offsets, tiles, sort scratch
+    __nv_bfloat16 *G_hi, *G_lo, *Bt_hi, *Bt_lo;
+    float *Tt, *gA, *gAd, *dB;
+};
+
+static void carve_bwd(WsCarver &w, int64_t E, int nb, const BwdPlan &P, bool split, BwdBuffers &b) {
+    carve_tc(w, E, nb, P.T, split, b.f);
+    const int64_t E1 = std::max<int64_t>(E, 1);
+    b.G_hi = (__nv_bfloat16 *)w.take(2 * (size_t)E1 * P.T2.k_total);
+    b.G_lo = split ? (__nv_bfloat16 *)w.take(2 * (size_t)E1 * P.T2.k_total) : nullptr;
+    b.Bt_hi = (__nv_bfloat16 *)w.take(2 * (size_t)P.T2.b_total);
+    b.Bt_lo = split ? (__nv_bfloat16 *)w.take(2 * (size_t)P.T2.b_total) : nullptr;
+    b.Tt = (float *)w.take(4 * (size_t)P.table_floats);
+    b.gA = (float *)w.take(4 * (size_t)E1 * P.T2.n_total);
+    b.gAd = (float *)w.take(4 * (size_t)E1 * P.T2.n_total);
+    b.dB = (float *)w.take(4 * (size_t)std::max<int64_t>(P.db_total, 1));
+}
+
+static int run_bwd(const BwdPlan &P, const BwdBuffers &b, const float *go, const float *f, const float *table,
+                   const float *dist, int64_t E, int Cin, int Cout, int nb, Binning bins, float sh_scale, bool split,
+                   float *grad_f, float *grad_table, float *grad_d, int32_t *status, cudaStream_t s) {
+    const TcBuffers &t = b.f;
+    const TcPlan &T = P.T, &T2 = P.T2;
+    int rc;
+    {
+        ProfScope ps("bwd_sort", s);
+        if ((rc = launch_binning(dist, E, bins, t.keys, nullptr, s)) != FEQ_OK) return rc;
+        if ((rc = launch_edge_sort<int32_t>(t.keys, E, nb, t.perm, t.offsets, nullptr, t.sort_ws, t.sort_ws_bytes,
+                                            s)) != FEQ_OK)
+            return rc;
+        if ((rc = launch_build_tiles(t.offsets, nb, 128, t.tiles, t.num_tiles, s)) != FEQ_OK) return rc;
+    }
+    {
+        ProfScope ps("bwd_prep", s);
+        if ((rc = launch_bwd_prep_rows(f, dist, t.perm, E, Cin, P.Li.dim, T.in_map, T.k_total, bins, sh_scale, t.A_hi,
+                                       t.A_lo, t.tval, s)) != FEQ_OK)
+            return rc;
+        if ((rc = launch_bwd_prep_rows(go, dist, t.perm, E, Cout, P.Lo.dim, T2.in_map, T2.k_total, bins, sh_scale,
+                                       b.G_hi, b.G_lo, nullptr, s)) != FEQ_OK)
+            return rc;
+        if ((rc = launch_tc_relayout_b(table, t.B_hi, t.B_lo, nb + 1, Cin, Cout, P.M.wdim, T.G, T.b_total, s)) !=
+            FEQ_OK)
+            return rc;
+        if ((rc = launch_bwd_transpose_table(table, b.Tt, nb + 1, Cout, Cin, P.M.wdim, P.M, s)) != FEQ_OK) return rc;
+        if ((rc = launch_tc_relayout_b(b.Tt, b.Bt_hi, b.Bt_lo, nb + 1, Cout, Cin, P.M2.wdim, T2.G, T2.b_total, s)) !=
+            FEQ_OK)
+            return rc;
+    }
+    {
+        ProfScope ps("bwd_mix", s);
+        for (int m = 0; m < T.G.n_blocks; m++) {
+            const TcBlockGeom &g = T.G.g[m], &g2 = T2.G.g[m];
+            if ((rc = launch_tc_mix(split ? 3 : 1, t.A_hi, t.A_lo, E, T.k_total, t.B_hi + g.boff,
+                                    split ? t.B_lo + g.boff : nullptr, (int64_t)(nb + 1) * g.npad, g, T.koff[m],
+                                    T.nvalid[m], T.n_total, T.noff[m], t.tiles, t.num_tiles, t.max_tiles, t.tval, t.H,
+                                    status, s)) != FEQ_OK)
+                return rc;
+            if ((rc = launch_tc_mix(split ? 3 : 1, b.G_hi, b.G_lo, E, T2.k_total, b.Bt_hi + g2.boff,
+                                    split ? b.Bt_lo + g2.boff : nullptr, (int64_t)(nb + 1) * g2.npad, g2, T2.koff[m],
+                                    T2.nvalid[m], T2.n_total, T2.noff[m], t.tiles, t.num_tiles, t.max_tiles, t.tval,
+                                    b.gA, status, s, b.gAd)) != FEQ_OK)
+                return rc;
+        }
+    }
+    {
+        ProfScope ps("bwd_rows", s);
+        const int any_l = (P.Li.lmax > 0 || P.Lo.lmax > 0) ? 1 : 0;
+        if ((rc = launch_bwd_rows(b.gA, b.gAd, T2.n_total, t.A_hi, t.A_lo, T.k_total, b.G_hi, b.G_lo, T2.k_total, t.H,
+                                  T.n_total, dist, t.perm, E, Cin, P.Li.dim, Cout, P.Lo.dim, T.in_map, T.out_map,
+                                  T2.in_map, T2.out_map, bins, sh_scale, any_l, grad_f, grad_d, s)) != FEQ_OK)
+            return rc;
+    }
+    ProfScope ps("bwd_table", s);
+    for (int m = 0; m < T.G.n_blocks; m++) {
+        const TcBlockGeom &g = T.G.g[m];
+        const int N = Cout * g.mult * g.n_out, K = Cin * g.mult * g.n_in;
+        if ((rc = launch_bwd_table_gemm(b.G_hi, b.G_lo, T2.k_total, T2.koff[m], N, t.A_hi, t.A_lo, T.k_total,
+                                        T.koff[m], K, t.offsets, t.tval, nb, b.dB + P.dboff.off[m], s)) != FEQ_OK)
+            return rc;
+    }
+    return launch_bwd_table_convert(b.dB, P.dboff, nb + 1, Cout, Cin, P.M.wdim, P.M, grad_table, s);
+}
+
 }  // namespace feq
 
 using namespace feq;
@@ -592,6 +728,49 @@ int feq_block_diagonal_fwd(const float *features, const float *radial_table, con
     Binning b{bin_param1, bin_param2, num_bins, log_bins ? 1 : 0};
     return run_mix(p, features, radial_table, distances, num_edges, c_in, c_out, din, dout, M, b, sh_scale,
                    output, (cudaStream_t)stream);
+}
+
+size_t feq_block_diagonal_bwd_workspace_bytes(int64_t num_edges, int32_t c_in, int32_t c_out,
+                                              const int32_t *lvals_in, int32_t n_lvals_in,
+                                              const int32_t *lvals_out, int32_t n_lvals_out, int32_t num_bins,
+                                              int32_t mix_mode) {
+    if (!mix_args_ok(num_edges, c_in, c_out, num_bins)) return 0;
+    if (mix_mode != FEQ_MIX_BF16 && mix_mode != FEQ_MIX_BF16X3) return 0;
+    static thread_local BwdPlan P;
+    if (build_bwd_plan(lvals_in, n_lvals_in, lvals_out, n_lvals_out, c_in, c_out, num_bins, &P) != FEQ_OK) return 0;
+    WsCarver w{nullptr, 0, 0};
+    BwdBuffers b;
+    carve_bwd(w, num_edges, num_bins, P, mix_mode == FEQ_MIX_BF16X3, b);
+    return w.used + 256;
+}
+
+int feq_block_diagonal_bwd(const float *grad_output, const float *features, const float *radial_table,
+                           const float *distances, int64_t num_edges, int32_t c_in, int32_t c_out,
+                           const int32_t *lvals_in, int32_t n_lvals_in, const int32_t *lvals_out,
+                           int32_t n_lvals_out, float sh_scale, float bin_param1, float bin_param2,
+                           int32_t num_bins, int32_t log_bins, int32_t mix_mode, float *grad_features,
+                           float *grad_table, float *grad_distances, void *workspace, size_t workspace_bytes,
+                           feq_stream_t stream) {
+    if (!mix_args_ok(num_edges, c_in, c_out, num_bins)) return FEQ_ERR_INVALID_ARGUMENT;
+    if (mix_mode != FEQ_MIX_BF16 && mix_mode != FEQ_MIX_BF16X3) return FEQ_ERR_UNSUPPORTED;
+    static thread_local BwdPlan P;
+    int rc = build_bwd_plan(lvals_in, n_lvals_in, lvals_out, n_lvals_out, c_in, c_out, num_bins, &P);
+    if (rc != FEQ_OK) return rc;
+    if (!radial_table || !grad_table) return FEQ_ERR_INVALID_ARGUMENT;
+    cudaStream_t s = (cudaStream_t)stream;
+    if (num_edges == 0) {
+        FEQ_CUDA_TRY(cudaMemsetAsync(grad_table, 0, sizeof(float) * (size_t)P.table_floats, s));
+        return FEQ_OK;
+    }
+    if (!grad_output || !features || !distances || !grad_features || !grad_distances) return FEQ_ERR_INVALID_ARGUMENT;
+    WsCarver w{(char *)workspace, 0, workspace_bytes};
+    BwdBuffers b;
+    const bool split = mix_mode == FEQ_MIX_BF16X3;
+    carve_bwd(w, num_edges, num_bins, P, split, b);
+    if (!workspace || w.used > workspace_bytes) return FEQ_ERR_WORKSPACE;
+    Binning bins{bin_param1, bin_param2, num_bins, log_bins ? 1 : 0};
+    return run_bwd(P, b, grad_output, features, radial_table, distances, num_edges, c_in, c_out, num_bins, bins,
+                   sh_scale, split, grad_features, grad_table, grad_distances, nullptr, s);
 }
 
 size_t feq_edgewise_workspace_bytes(const FeqEdgewiseArgs *a) {

@@ -156,6 +156,11 @@ struct ProfScope {
 };
 
 // Workspace carving: every region 256-byte aligned.
+// Per-block float offsets of the backward's per-bin reduction buffer.
+struct DbOff {
+    int64_t off[kMaxBlocks];
+};
+
 struct WsCarver {
     char *base;
     size_t used, cap;

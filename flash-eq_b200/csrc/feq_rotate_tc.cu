@@ -10,10 +10,11 @@
 // edge's row is in flight while the current one is rotated.  rotate_in writes its
 // bf16 columns straight to HBM (lanes hold consecutive channel pairs, so each store
 // covers 128 contiguous bytes); rotate_out stages the output row in shared memory
-// and writes it back with one bulk store.  Per edge the warp builds
-// each degree's rotation block once, with the solid-harmonic factor s^l folded in,
-// and every lane then rotates two channels with the block rows read as float4
-// broadcasts.  Rows of the block are padded to a multiple of 4 floats.
+// and writes it back with one bulk store.  Every lane rotates two channels of each
+// irrep in registers through the factored block D_l = R(phi) M_l R(phi)^T: two
+// z-rotations by the edge azimuth around the sparse M_l, whose entries are generated
+// code (gen_wigner_tables.py) with s^l folded in.  Degrees above 6 fall back to
+// per-edge blocks built in shared memory (rows padded to 4 floats, float4 reads).
 //
 //   rotate_in : A[p][base(j) + c] = s^l (f[e][c] . D)[j]          (bf16, or bf16 hi + lo)
 //   rotate_out: out[e][c][k]      = sum_q D[k][q] s^l h[p][base(q) + c]

@@ -46,6 +46,7 @@ struct TcGemmParams {
     const int *num_tiles;
     const float *tval;      // per sorted row: interpolation weight t
     float *H;               // (E, h_ld) sorted rows
+    float *Hd;              // optional, same layout: D_hi - D_lo (the t-derivative of H)
     int32_t *status;        // set to 2 when a wait timed out
 };
 
@@ -198,6 +199,14 @@ tc_mix_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ 
                             v.z = fmaf(t, __uint_as_float(hi[c + 2]) - __uint_as_float(lo[c + 2]), __uint_as_float(lo[c + 2]));
                             v.w = fmaf(t, __uint_as_float(hi[c + 3]) - __uint_as_float(lo[c + 3]), __uint_as_float(lo[c + 3]));
                             *reinterpret_cast<float4 *>(hrow + n0 + c) = v;
+                            if (P.Hd) {
+                                float4 dv;
+                                dv.x = __uint_as_float(hi[c]) - __uint_as_float(lo[c]);
+                                dv.y = __uint_as_float(hi[c + 1]) - __uint_as_float(lo[c + 1]);
+                                dv.z = __uint_as_float(hi[c + 2]) - __uint_as_float(lo[c + 2]);
+                                dv.w = __uint_as_float(hi[c + 3]) - __uint_as_float(lo[c + 3]);
+                                *reinterpret_cast<float4 *>(P.Hd + p * P.h_ld + P.h_col0 + n0 + c) = dv;
+                            }
                         }
                     } else {
 #pragma unroll
@@ -205,6 +214,7 @@ tc_mix_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ 
                             if (n0 + c < P.n_valid) {
                                 const float l = __uint_as_float(lo[c]), h = __uint_as_float(hi[c]);
                                 hrow[n0 + c] = fmaf(t, h - l, l);
+                                if (P.Hd) P.Hd[p * P.h_ld + P.h_col0 + n0 + c] = h - l;
                             }
                         }
                     }
@@ -408,7 +418,7 @@ int launch_tc_relayout_b(const float *T, __nv_bfloat16 *Bhi, __nv_bfloat16 *Blo,
 int launch_tc_mix(int split, const __nv_bfloat16 *A, const __nv_bfloat16 *A2, int64_t a_rows, int a_cols,
                   const __nv_bfloat16 *Bm, const __nv_bfloat16 *Bm2, int64_t b_rows, const TcBlockGeom &B,
                   int a_col0, int n_valid, int h_ld, int h_col0, const int4 *tiles, const int *num_tiles,
-                  int64_t max_tiles, const float *tval, float *H, int32_t *status, cudaStream_t s) {
+                  int64_t max_tiles, const float *tval, float *H, int32_t *status, cudaStream_t s, float *Hd) {
     CUtensorMap mA, mA2, mB, mB2;
     int rc;
     if ((rc = make_map(&mA, A, a_cols, a_rows)) != FEQ_OK) return rc;
@@ -432,6 +442,7 @@ int launch_tc_mix(int split, const __nv_bfloat16 *A, const __nv_bfloat16 *A2, in
     P.num_tiles = num_tiles;
     P.tval = tval;
     P.H = H;
+    P.Hd = Hd;
     P.status = status;
     int dev = 0, sms = 148;
     FEQ_CUDA_TRY(cudaGetDevice(&dev));

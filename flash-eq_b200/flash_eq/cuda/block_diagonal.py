@@ -6,8 +6,11 @@ m-first basis, radial table (num_bins + 1, Cout, Cin, W), distances (E,).
 
 Differences in mechanism (not in results): no argsort/gather/unsort copies
 (edges are grouped by bin inside the native op), no host synchronisation, work
-is enqueued on the current stream.  Forward only: the backward pass is not part
-of this build and raises ``NotImplementedError`` if autograd reaches it.
+is enqueued on the current stream.  The backward (``_BlockDiagonalFunction``,
+block_diagonal.py:100-174 in the reference) runs the native
+``feq_block_diagonal_bwd``: grad_features, grad_table and grad_distances,
+deterministic (no atomics).  Other native ops of this package are forward only and
+raise ``NotImplementedError`` if autograd reaches them.
 """
 from __future__ import annotations
 
@@ -77,9 +80,30 @@ def block_diagonal_cuda(
     if max(max(lvals_in), max(lvals_out)) >= 17:
         raise RuntimeError("Maximum l-value exceeds supported limit (16).")
     dist = distances.to(features.dtype)
+    cfg = (tuple(lvals_in), tuple(lvals_out), float(sh_scale), float(bin_param1), float(bin_param2), int(num_bins),
+           bool(log_bins))
+    if torch.is_grad_enabled() and any(t.requires_grad for t in (features, radial_table, dist)):
+        return _BlockDiagonalFunction.apply(features, radial_table, dist, cfg)
+    return ops.block_diagonal_fwd(features.detach(), radial_table.detach(), dist.detach(), lvals_in, lvals_out,
+                                  sh_scale, bin_param1, bin_param2, num_bins, log_bins)
 
-    def run(f, tab, d):
-        return ops.block_diagonal_fwd(f.detach(), tab.detach(), d.detach(), lvals_in, lvals_out, sh_scale,
-                                      bin_param1, bin_param2, num_bins, log_bins)
 
-    return forward_only(run, features, radial_table, dist)
+class _BlockDiagonalFunction(torch.autograd.Function):
+    """Autograd of block_diagonal_cuda (flash_eq/cuda/block_diagonal.py:100-174)."""
+
+    @staticmethod
+    def forward(ctx, features, radial_table, dist, cfg):
+        lin, lout, sh, p1, p2, nb, log = cfg
+        ctx.cfg = cfg
+        ctx.save_for_backward(features, radial_table, dist)
+        return ops.block_diagonal_fwd(features.detach(), radial_table.detach(), dist.detach(), list(lin), list(lout),
+                                      sh, p1, p2, nb, log)
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        lin, lout, sh, p1, p2, nb, log = ctx.cfg
+        features, radial_table, dist = ctx.saved_tensors
+        gf, gt, gd = ops.block_diagonal_bwd(grad_out.contiguous(), features.detach(), radial_table.detach(),
+                                            dist.detach(), list(lin), list(lout), sh, p1, p2, nb, log)
+        return (gf if ctx.needs_input_grad[0] else None, gt if ctx.needs_input_grad[1] else None,
+                gd if ctx.needs_input_grad[2] else None, None)

@@ -132,6 +132,36 @@ def block_diagonal_fwd(features, radial_table, distances, lvals_in, lvals_out, s
     return out
 
 
+def block_diagonal_bwd(grad_out, features, radial_table, distances, lvals_in, lvals_out, sh_scale, p1, p2,
+                       num_bins, log_bins, mix="bf16x3"):
+    """(grad_features, grad_table, grad_distances) of block_diagonal_fwd (tensor-core mixes in ``mix``)."""
+    lib = _require_cuda(grad_out, features, radial_table, distances)
+    grad_out = _f32(grad_out, "grad_output")
+    features = _f32(features, "features")
+    radial_table = _f32(radial_table, "radial_table")
+    distances = _f32(distances, "distances")
+    E, c_in, d_in = features.shape
+    c_out = radial_table.shape[1]
+    if grad_out.shape != (E, c_out, dim_of(lvals_out)):
+        raise ValueError(f"grad_output shape {tuple(grad_out.shape)} does not match (E, Cout, d_out)")
+    gf = torch.empty_like(features)
+    gt = torch.empty_like(radial_table)
+    gd = torch.empty(E, dtype=torch.float32, device=features.device)
+    ai, ni = _lib.i32_array(lvals_in)
+    ao, no = _lib.i32_array(lvals_out)
+    mode = _lib.FEQ_MIX[mix]
+    ws_bytes = lib.feq_block_diagonal_bwd_workspace_bytes(E, c_in, c_out, ai, ni, ao, no, int(num_bins), mode)
+    if ws_bytes == 0:
+        raise RuntimeError(f"block-diagonal backward: unsupported layout or mix {mix!r}")
+    ws = _workspace(ws_bytes, features.device)
+    rc = lib.feq_block_diagonal_bwd(_p(grad_out), _p(features), _p(radial_table), _p(distances), E, c_in, c_out, ai,
+                                    ni, ao, no, float(sh_scale), float(p1), float(p2), int(num_bins),
+                                    int(bool(log_bins)), mode, _p(gf), _p(gt), _p(gd), _p(ws), ws.numel(),
+                                    _stream(features.device))
+    _lib.check(rc, "feq_block_diagonal_bwd")
+    return gf, gt, gd
+
+
 def edgewise_fwd(x, distances, radial_table, lvals_in, lvals_out, c_out, sh_scale, p1, p2, num_bins,
                  log_bins, *, src=None, edge_add=None, directions=None, P=None, Q=None, status=None, mix="fp32"):
     """Fused Q . Lambda(r) . P^T . f.  Rows f[e] = x[src[e]] (+ edge_add[e]) or x[e].

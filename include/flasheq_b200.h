@@ -133,6 +133,28 @@ int feq_block_diagonal_fwd(const float *features, const float *radial_table,
                            int32_t log_bins, float *output, void *workspace,
                            size_t workspace_bytes, feq_stream_t stream);
 
+/* Backward of feq_block_diagonal_fwd.
+ * Replaces _block_diagonal_cuda.backward (flash_eq/cuda/csrc/block_diagonal.cu:1543-1758,
+ * kernels :747-1161; wrapper _BlockDiagonalFunction.backward, block_diagonal.py:140-174):
+ * grad_output (E, c_out, d_out) and features (E, c_in, d_in) m-first, radial_table as in the
+ * forward; writes grad_features (E, c_in, d_in), grad_table (num_bins+1, c_out, c_in, W) and
+ * grad_distances (E,).  Deterministic: no atomics; grad_table is reduced per distance bin
+ * in sorted-edge order.  mix_mode FEQ_MIX_BF16X3 (float32-level accuracy) or FEQ_MIX_BF16
+ * selects the tensor-core arithmetic of the two mixes it runs (W_t A and G W_t^T).
+ * grad_distances follows the reference's expression, NaN at distance 0 when some
+ * l_in + l_out > 0 (as the reference). */
+size_t feq_block_diagonal_bwd_workspace_bytes(int64_t num_edges, int32_t c_in, int32_t c_out,
+                                              const int32_t *lvals_in, int32_t n_lvals_in,
+                                              const int32_t *lvals_out, int32_t n_lvals_out,
+                                              int32_t num_bins, int32_t mix_mode);
+int feq_block_diagonal_bwd(const float *grad_output, const float *features, const float *radial_table,
+                           const float *distances, int64_t num_edges, int32_t c_in, int32_t c_out,
+                           const int32_t *lvals_in, int32_t n_lvals_in, const int32_t *lvals_out,
+                           int32_t n_lvals_out, float sh_scale, float bin_param1, float bin_param2,
+                           int32_t num_bins, int32_t log_bins, int32_t mix_mode, float *grad_features,
+                           float *grad_table, float *grad_distances, void *workspace,
+                           size_t workspace_bytes, feq_stream_t stream);
+
 /* Same operation as feq_block_diagonal_fwd for callers that cannot allocate device
  * memory: code running where cudaMalloc is unavailable or not allowed (a host
  * framework that owns every allocation, a plugin without an allocator handle), or
