@@ -18,7 +18,7 @@ import torch
 import torch.nn as nn
 
 from ..cuda import ops
-from ..cuda.block_diagonal import forward_only
+from ..cuda.block_diagonal import block_diagonal_cuda, forward_only
 from ..representations import ProductRepr, Repr
 from ..representations.wigner import LazyBasis, basis_source
 from .radial import SeparableRadialNet
@@ -69,6 +69,11 @@ class EquivariantEdgewiseLinear(nn.Module):
         p1, p2 = rw.binning_params()
         table = rw()
         dist = distances.to(torch.float32)
+        if torch.is_grad_enabled() and any(
+                t is not None and t.requires_grad for t in (x, table, dist, edge_add,
+                                                            P if torch.is_tensor(P) else None,
+                                                            Q if torch.is_tensor(Q) else None)):
+            return self._run_autograd(P, Q, x, dist, table, p1, p2, src, edge_add)
         dP, dQ = basis_source(P, self._lin), basis_source(Q, self._lout)
         fused = dP is not None and dQ is not None and dP is dQ
         Pd = Qd = None
@@ -84,6 +89,22 @@ class EquivariantEdgewiseLinear(nn.Module):
                 mix=self.mix_precision)
 
         return forward_only(run, x, table, dist, edge_add, Pd, Qd)
+
+    def _run_autograd(self, P, Q, x, dist, table, p1, p2, src, edge_add):
+        """The reference's three steps (linear.py:135-160) with autograd: bmm into the edge
+        frame, block_diagonal_cuda (native forward and backward), bmm back out."""
+        for M in (P, Q):
+            d = M.directions if isinstance(M, LazyBasis) else None
+            if d is not None and d.requires_grad:
+                raise NotImplementedError("flash-eq B200: gradients with respect to edge directions are not "
+                                          "supported (the Wigner basis is computed without autograd)")
+        f = x[src] if src is not None else x
+        if edge_add is not None:
+            f = f + edge_add
+        f_diag = torch.bmm(f, _dense(P))
+        out_diag = block_diagonal_cuda(f_diag, table, dist, self.product_repr, p1, p2, self.radial_weights.num_bins,
+                                       self.radial_weights.log, self.solid_harmonic_scale)
+        return torch.bmm(out_diag, _dense(Q).mT)
 
     def extra_repr(self) -> str:
         rw = self.radial_weights

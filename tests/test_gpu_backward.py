@@ -84,3 +84,39 @@ def test_backward_zero_distance_nan_like_reference(cuda_device):
     ok = ~torch.isnan(rd)
     assert rel_l2(gd.cpu()[ok], rd[ok]) < 1e-4
     assert rel_l2(gf, rf) < 1e-4 and rel_l2(gt, rt) < 1e-4
+
+
+def test_edgewise_layer_training_step_matches_oracle(cuda_device):
+    """Gradients of EquivariantEdgewiseLinear (inputs and radial-MLP parameters) against the
+    oracle chain bmm -> block-diagonal backward -> bmm, with the table's own autograd."""
+    dev = cuda_device
+    lin, lout = [0, 1, 2], [0, 1]
+    torch.manual_seed(0)
+    rin, rout = fe.Repr(lin, mult=8), fe.Repr(lout, mult=6)
+    layer = fe.EquivariantEdgewiseLinear(rin, rout).to(dev)
+    ref_layer = fe.EquivariantEdgewiseLinear(rin, rout).to(dev)
+    ref_layer.load_state_dict(layer.state_dict())
+    g = torch.Generator().manual_seed(2)
+    E = 500
+    x = torch.randn(E, 8, rin.dim(), generator=g)
+    dirs = torch.randn(E, 3, generator=g)
+    dist = torch.rand(E, generator=g) * 9 + 0.2
+    go = torch.randn(E, 6, rout.dim(), generator=g)
+    P, Q = fe.WignerDBasis([rin, rout])(dirs.to(dev))
+    xg = x.to(dev).requires_grad_()
+    out = layer(P, Q, xg, dist.to(dev))
+    out.backward(go.to(dev))
+    # oracle chain on the same table
+    rw = ref_layer.radial_weights
+    table = rw()
+    p1, p2 = rw.binning_params()
+    Pc, Qc = P.double().cpu(), Q.double().cpu()
+    f_diag = torch.bmm(x.double(), Pc)
+    go_diag = torch.bmm(go.double(), Qc)                      # d/d out_diag of <go, out_diag Q^T>
+    gfd, gtab, _ = orc.block_diagonal_bwd(go_diag, f_diag, table.detach().double().cpu(), dist.double(), lin, lout,
+                                          layer.solid_harmonic_scale, p1, p2, rw.num_bins, rw.log)
+    gx = torch.bmm(gfd, Pc.mT)
+    assert rel_l2(xg.grad, gx) < 1e-4
+    table.backward(gtab.to(dev, torch.float32))
+    for (n, a), (_, b) in zip(layer.named_parameters(), ref_layer.named_parameters()):
+        assert rel_l2(a.grad, b.grad) < 1e-4, n
