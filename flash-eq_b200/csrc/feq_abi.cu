@@ -78,11 +78,16 @@ int launch_bwd_rows(const float *gA, const float *gAd, int ld_g, const __nv_bflo
                     const float *dist, const int64_t *perm, int64_t E, int Cin, int Din, int Cout, int Dout,
                     const TcPosMap &in1, const TcPosMap &out1, const TcPosMap &in2, const TcPosMap &out2,
                     Binning bins, float sh_scale, int any_l, float *grad_f, float *grad_d, cudaStream_t s);
-int launch_bwd_table_gemm(const __nv_bfloat16 *Ghi, const __nv_bfloat16 *Glo, int ld_g, int g_col0, int N,
-                          const __nv_bfloat16 *Ahi, const __nv_bfloat16 *Alo, int ld_a, int a_col0, int K,
-                          const int64_t *offsets, const float *tval, int nb, float *dB, cudaStream_t s);
 int launch_bwd_table_convert(const float *dB, const DbOff &dboff, int nb1, int Cout, int Cin, int W,
                              const MixLayout &M, float *grad_table, cudaStream_t s);
+int launch_bwd_segments(const int64_t *offsets, int nb, int64_t *seg, cudaStream_t s);
+int launch_bwd_transpose_rows(const __nv_bfloat16 *Xhi, const __nv_bfloat16 *Xlo, int ld, int ncols,
+                              const int64_t *offsets, const int64_t *seg, int nb, const float *tval, int wmode,
+                              int64_t pcols, __nv_bfloat16 *Yhi, __nv_bfloat16 *Ylo, cudaStream_t s);
+int launch_tc_gram(int split, const __nv_bfloat16 *Gt0, const __nv_bfloat16 *Gt0l, const __nv_bfloat16 *Gt1,
+                   const __nv_bfloat16 *Gt1l, int64_t g_rows, const __nv_bfloat16 *At, const __nv_bfloat16 *Atl,
+                   int64_t a_rows, int64_t p_cols, int n_blocks, const TcGramBlock *blk, int nb, const int64_t *seg,
+                   float *dB, int32_t *status, cudaStream_t s);
 
 static thread_local std::string g_last_error;
 static std::atomic<long long> g_launches{0};
@@ -502,6 +507,8 @@ struct BwdBuffers {
     TcBuffers f;                     // A, B, H, tval, keys, perm, offsets, tiles, sort scratch
     __nv_bfloat16 *G_hi, *G_lo, *Bt_hi, *Bt_lo;
     float *Tt, *gA, *gAd, *dB;
+    int64_t *seg, pcols;
+    __nv_bfloat16 *Gt0_hi, *Gt0_lo, *Gt1_hi, *Gt1_lo, *At_hi, *At_lo;
 };
 
 static void carve_bwd(WsCarver &w, int64_t E, int nb, const BwdPlan &P, bool split, BwdBuffers &b) {
@@ -515,6 +522,15 @@ static void carve_bwd(WsCarver &w, int64_t E, int nb, const BwdPlan &P, bool spl
     b.gA = (float *)w.take(4 * (size_t)E1 * P.T2.n_total);
     b.gAd = (float *)w.take(4 * (size_t)E1 * P.T2.n_total);
     b.dB = (float *)w.take(4 * (size_t)std::max<int64_t>(P.db_total, 1));
+    b.seg = (int64_t *)w.take(8 * (size_t)(nb + 1));
+    b.pcols = (E1 + 63) / 64 * 64 + 64 * (int64_t)nb;        // every bin padded to a multiple of 64
+    const size_t gsz = 2 * (size_t)P.T2.k_total * b.pcols, asz = 2 * (size_t)P.T.k_total * b.pcols;
+    b.Gt0_hi = (__nv_bfloat16 *)w.take(gsz);
+    b.Gt0_lo = split ? (__nv_bfloat16 *)w.take(gsz) : nullptr;
+    b.Gt1_hi = (__nv_bfloat16 *)w.take(gsz);
+    b.Gt1_lo = split ? (__nv_bfloat16 *)w.take(gsz) : nullptr;
+    b.At_hi = (__nv_bfloat16 *)w.take(asz);
+    b.At_lo = split ? (__nv_bfloat16 *)w.take(asz) : nullptr;
 }
 
 static int run_bwd(const BwdPlan &P, const BwdBuffers &b, const float *go, const float *f, const float *table,
@@ -572,13 +588,31 @@ static int run_bwd(const BwdPlan &P, const BwdBuffers &b, const float *go, const
             return rc;
     }
     ProfScope ps("bwd_table", s);
+    if ((rc = launch_bwd_segments(t.offsets, nb, b.seg, s)) != FEQ_OK) return rc;
+    if ((rc = launch_bwd_transpose_rows(b.G_hi, b.G_lo, T2.k_total, T2.k_total, t.offsets, b.seg, nb, t.tval, 1,
+                                        b.pcols, b.Gt0_hi, b.Gt0_lo, s)) != FEQ_OK)
+        return rc;
+    if ((rc = launch_bwd_transpose_rows(b.G_hi, b.G_lo, T2.k_total, T2.k_total, t.offsets, b.seg, nb, t.tval, 2,
+                                        b.pcols, b.Gt1_hi, b.Gt1_lo, s)) != FEQ_OK)
+        return rc;
+    if ((rc = launch_bwd_transpose_rows(t.A_hi, t.A_lo, T.k_total, T.k_total, t.offsets, b.seg, nb, t.tval, 0,
+                                        b.pcols, b.At_hi, b.At_lo, s)) != FEQ_OK)
+        return rc;
+    TcGramBlock gb[kMaxBlocks];
     for (int m = 0; m < T.G.n_blocks; m++) {
         const TcBlockGeom &g = T.G.g[m];
-        const int N = Cout * g.mult * g.n_out, K = Cin * g.mult * g.n_in;
-        if ((rc = launch_bwd_table_gemm(b.G_hi, b.G_lo, T2.k_total, T2.koff[m], N, t.A_hi, t.A_lo, T.k_total,
-                                        T.koff[m], K, t.offsets, t.tval, nb, b.dB + P.dboff.off[m], s)) != FEQ_OK)
-            return rc;
+        gb[m].N = Cout * g.mult * g.n_out;
+        gb[m].K = Cin * g.mult * g.n_in;
+        gb[m].n_tiles = (gb[m].N + 127) / 128;
+        gb[m].k_tiles = (gb[m].K + 127) / 128;
+        gb[m].g_row0 = T2.koff[m];
+        gb[m].a_row0 = T.koff[m];
+        gb[m].dboff = P.dboff.off[m];
+        gb[m].item0 = 0;
     }
+    if ((rc = launch_tc_gram(split ? 3 : 1, b.Gt0_hi, b.Gt0_lo, b.Gt1_hi, b.Gt1_lo, T2.k_total, b.At_hi, b.At_lo,
+                             T.k_total, b.pcols, T.G.n_blocks, gb, nb, b.seg, b.dB, status, s)) != FEQ_OK)
+        return rc;
     return launch_bwd_table_convert(b.dB, P.dboff, nb + 1, Cout, Cin, P.M.wdim, P.M, grad_table, s);
 }
 

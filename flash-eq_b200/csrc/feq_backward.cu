@@ -11,7 +11,8 @@
 // block matrix:
 //   grad_f[k]       = s^l_i  (G W_t)[k]                       tensor-core mix of G with W^T
 //   grad_W[bin b]   = sum_{p in b} (1 - t_p) G_p^T A_p + sum_{p in b-1} t_p G_p^T A_p
-//                                                              per-bin reduction (fixed order)
+//                                                              per-bin tensor-core reduction over the
+//                                                              transposed, bin-padded G and A (tc_gram)
 //   dL/dt           = sum_k A[k] (G (W[lo+1] - W[lo]))[k]      second epilogue output of the mix
 //   dL/ds * s       = sum_k l_i A[k] (G W_t)[k] + sum_n l_o G[n] (W_t A)[n]
 //   grad_d          = dL/dt dt/dd + (dL/ds * s) * scale / (d (d + scale))
@@ -192,72 +193,6 @@ __global__ void bwd_rows_kernel(const float *__restrict__ gA, const float *__res
     }
 }
 
-// Per-bin reduction of one m-block, a 64 x 64 tile of dB_b[n][k] per CTA:
-//   dB_b = sum_{p in bin b} (1 - t_p) G[p][n] A[p][k] + sum_{p in bin b-1} t_p G[p][n] A[p][k]
-// Rows in sorted order, 16 per step through shared memory; each thread holds 4 x 4 sums.
-constexpr int kBT = 64, kBR = 16;
-__global__ void __launch_bounds__(256)
-bwd_table_gemm_kernel(const __nv_bfloat16 *__restrict__ Ghi, const __nv_bfloat16 *__restrict__ Glo, int ld_g,
-                      int g_col0, int N, const __nv_bfloat16 *__restrict__ Ahi,
-                      const __nv_bfloat16 *__restrict__ Alo, int ld_a, int a_col0, int K,
-                      const int64_t *__restrict__ offsets, const float *__restrict__ tval, int nb,
-                      float *__restrict__ dB) {
-    __shared__ float gs[kBR][kBT], as_[kBR][kBT];
-    const int n0 = blockIdx.x * kBT, k0 = blockIdx.y * kBT, b = blockIdx.z;
-    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;      // k and n sub-tiles of 4
-    float acc[4][4] = {};
-    for (int side = 0; side < 2; side++) {                      // 0: bin b (1 - t), 1: bin b - 1 (t)
-        const int bb = side == 0 ? b : b - 1;
-        if (bb < 0 || bb >= nb) continue;
-        const int64_t r0 = offsets[bb], r1 = offsets[bb + 1];
-        for (int64_t c0 = r0; c0 < r1; c0 += kBR) {
-            const int cn = (int)min64(kBR, r1 - c0);
-            __syncthreads();
-            for (int i = threadIdx.x; i < kBR * kBT; i += blockDim.x) {
-                const int r = i / kBT, c = i - r * kBT;
-                float gv = 0.0f, av = 0.0f;
-                if (r < cn) {
-                    const int64_t p = c0 + r;
-                    const float t = tval[p];
-                    const float wgt = side == 0 ? 1.0f - t : t;
-                    if (n0 + c < N) {
-                        const int64_t gi = p * (int64_t)ld_g + g_col0 + n0 + c;
-                        gv = wgt * (__bfloat162float(Ghi[gi]) + (Glo ? __bfloat162float(Glo[gi]) : 0.0f));
-                    }
-                    if (k0 + c < K) {
-                        const int64_t ai = p * (int64_t)ld_a + a_col0 + k0 + c;
-                        av = __bfloat162float(Ahi[ai]) + (Alo ? __bfloat162float(Alo[ai]) : 0.0f);
-                    }
-                }
-                gs[r][c] = gv;
-                as_[r][c] = av;
-            }
-            __syncthreads();
-#pragma unroll 4
-            for (int r = 0; r < cn; r++) {
-                float gv[4], av[4];
-#pragma unroll
-                for (int u = 0; u < 4; u++) {
-                    gv[u] = gs[r][ty * 4 + u];
-                    av[u] = as_[r][tx * 4 + u];
-                }
-#pragma unroll
-                for (int u = 0; u < 4; u++)
-#pragma unroll
-                    for (int v = 0; v < 4; v++) acc[u][v] = fmaf(gv[u], av[v], acc[u][v]);
-            }
-        }
-    }
-    for (int u = 0; u < 4; u++) {
-        const int n = n0 + ty * 4 + u;
-        if (n >= N) continue;
-        for (int v = 0; v < 4; v++) {
-            const int k = k0 + tx * 4 + v;
-            if (k < K) dB[((int64_t)b * N + n) * K + k] = acc[u][v];
-        }
-    }
-}
-
 // dB (per block m: (nb + 1, N_m, K_m) at dboff[m]) -> grad_table (nb + 1, Cout, Cin, W):
 // m = 0: dT[co][ci][w_off + o n_in + i] = dB[o Cout + co][i Cin + ci];
 // m > 0: a = dB[re][re] + dB[im][im], b = dB[re][im] - dB[im][re] with n = (2o + re/im) Cout + co,
@@ -354,22 +289,98 @@ int launch_bwd_rows(const float *gA, const float *gAd, int ld_g, const __nv_bflo
     return FEQ_OK;
 }
 
-int launch_bwd_table_gemm(const __nv_bfloat16 *Ghi, const __nv_bfloat16 *Glo, int ld_g, int g_col0, int N,
-                          const __nv_bfloat16 *Ahi, const __nv_bfloat16 *Alo, int ld_a, int a_col0, int K,
-                          const int64_t *offsets, const float *tval, int nb, float *dB, cudaStream_t s) {
-    if (N == 0 || K == 0) return FEQ_OK;
-    dim3 grid((unsigned)((N + kBT - 1) / kBT), (unsigned)((K + kBT - 1) / kBT), (unsigned)(nb + 1));
-    bwd_table_gemm_kernel<<<grid, 256, 0, s>>>(Ghi, Glo, ld_g, g_col0, N, Ahi, Alo, ld_a, a_col0, K, offsets, tval,
-                                              nb, dB);
-    FEQ_LAUNCH_CHECK();
-    return FEQ_OK;
-}
-
 int launch_bwd_table_convert(const float *dB, const DbOff &dboff, int nb1, int Cout, int Cin, int W,
                              const MixLayout &M, float *grad_table, cudaStream_t s) {
     const int64_t total = (int64_t)nb1 * Cout * Cin * W;
     if (total == 0) return FEQ_OK;
     bwd_table_convert_kernel<<<grid_for(total, 256), 256, 0, s>>>(dB, dboff, nb1, Cout, Cin, W, M, grad_table);
+    FEQ_LAUNCH_CHECK();
+    return FEQ_OK;
+}
+
+// Padded segment starts: bin b occupies [seg[b], seg[b] + count_b) of the padded sorted
+// order, seg[b + 1] = seg[b] + count_b rounded up to 64; seg[nb] = total.
+__global__ void bwd_segments_kernel(const int64_t *__restrict__ offsets, int nb, int64_t *__restrict__ seg) {
+    if (blockIdx.x != 0 || threadIdx.x != 0) return;
+    int64_t acc = 0;
+    for (int b = 0; b < nb; b++) {
+        seg[b] = acc;
+        acc += (offsets[b + 1] - offsets[b] + 63) / 64 * 64;
+    }
+    seg[nb] = acc;
+}
+
+// Y[c][p'] = w(p) X[p][c] for c < ncols and every padded position p' < pcols (zero where p'
+// holds no row), X and Y bf16 hi (+ lo).  wmode: 0 -> 1, 1 -> 1 - t_p, 2 -> t_p.
+__global__ void bwd_transpose_rows_kernel(const __nv_bfloat16 *__restrict__ Xhi, const __nv_bfloat16 *__restrict__ Xlo,
+                                          int ld, int ncols, const int64_t *__restrict__ offsets,
+                                          const int64_t *__restrict__ seg, int nb, const float *__restrict__ tval,
+                                          int wmode, int64_t pcols, __nv_bfloat16 *__restrict__ Yhi,
+                                          __nv_bfloat16 *__restrict__ Ylo) {
+    __shared__ float tile[32][33];
+    __shared__ int64_t rowp[32];
+    __shared__ float roww[32];
+    const int64_t p0 = (int64_t)blockIdx.x * 32;
+    const int c0 = blockIdx.y * 32;
+    if (threadIdx.y == 0) {
+        const int64_t pp = p0 + threadIdx.x;
+        int64_t prow = -1;
+        float wt = 0.0f;
+        if (pp < seg[nb]) {
+            int lo = 0, hi = nb - 1;                 // last b with seg[b] <= pp
+            while (lo < hi) {
+                const int mid = (lo + hi + 1) >> 1;
+                if (seg[mid] <= pp) lo = mid; else hi = mid - 1;
+            }
+            const int64_t local = pp - seg[lo];
+            if (local < offsets[lo + 1] - offsets[lo]) {
+                prow = offsets[lo] + local;
+                const float t = tval[prow];
+                wt = wmode == 0 ? 1.0f : (wmode == 1 ? 1.0f - t : t);
+            }
+        }
+        rowp[threadIdx.x] = prow;
+        roww[threadIdx.x] = wt;
+    }
+    __syncthreads();
+    for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+        const int64_t prow = rowp[r];
+        const int c = c0 + threadIdx.x;
+        float v = 0.0f;
+        if (prow >= 0 && c < ncols) {
+            const int64_t i = prow * (int64_t)ld + c;
+            v = __bfloat162float(Xhi[i]);
+            if (Xlo) v += __bfloat162float(Xlo[i]);
+            v *= roww[r];
+        }
+        tile[r][threadIdx.x] = v;
+    }
+    __syncthreads();
+    for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+        const int c = c0 + r;
+        const int64_t pp = p0 + threadIdx.x;
+        if (c >= ncols || pp >= pcols) continue;
+        const float v = tile[threadIdx.x][r];
+        const __nv_bfloat16 h = __float2bfloat16_rn(v);
+        Yhi[(int64_t)c * pcols + pp] = h;
+        if (Ylo) Ylo[(int64_t)c * pcols + pp] = __float2bfloat16_rn(v - __bfloat162float(h));
+    }
+}
+
+int launch_bwd_segments(const int64_t *offsets, int nb, int64_t *seg, cudaStream_t s) {
+    bwd_segments_kernel<<<1, 32, 0, s>>>(offsets, nb, seg);
+    FEQ_LAUNCH_CHECK();
+    return FEQ_OK;
+}
+
+int launch_bwd_transpose_rows(const __nv_bfloat16 *Xhi, const __nv_bfloat16 *Xlo, int ld, int ncols,
+                              const int64_t *offsets, const int64_t *seg, int nb, const float *tval, int wmode,
+                              int64_t pcols, __nv_bfloat16 *Yhi, __nv_bfloat16 *Ylo, cudaStream_t s) {
+    if (pcols == 0 || ncols == 0) return FEQ_OK;
+    if ((pcols + 31) / 32 > 0x7fffffffll || (ncols + 31) / 32 > 65535) return FEQ_ERR_UNSUPPORTED;
+    dim3 grid((unsigned)((pcols + 31) / 32), (unsigned)((ncols + 31) / 32));
+    bwd_transpose_rows_kernel<<<grid, dim3(32, 8), 0, s>>>(Xhi, Xlo, ld, ncols, offsets, seg, nb, tval, wmode, pcols,
+                                                          Yhi, Ylo);
     FEQ_LAUNCH_CHECK();
     return FEQ_OK;
 }

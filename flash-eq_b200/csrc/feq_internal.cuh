@@ -161,6 +161,12 @@ struct DbOff {
     int64_t off[kMaxBlocks];
 };
 
+// One m-block of the backward's tensor-core per-bin reduction.
+struct TcGramBlock {
+    int N, K, n_tiles, k_tiles, g_row0, a_row0;
+    int64_t dboff, item0;
+};
+
 struct WsCarver {
     char *base;
     size_t used, cap;

@@ -232,6 +232,197 @@ tc_mix_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ 
     if (threadIdx.x == 0 && abort_s && P.status) atomicMax(P.status, 2);
 }
 
+// ---------------------------------------------------------------------------
+// Per-bin weight-gradient reduction of the backward on the tensor cores:
+//   dB_b[n][k] = sum_{p in bin b} (1 - t_p) G[p][n] A[p][k] + sum_{p in bin b-1} t_p G[p][n] A[p][k]
+// The reduction runs over edges, so both operands are the transposes Gt[n][p'], At[k][p']
+// (K-major over the padded sorted position p': every bin's segment starts at a multiple of
+// 64, gaps are zero), with the weights folded into two copies of Gt.  Work item =
+// (m-block, bin, 128 n rows, 128 k columns); roles as in tc_mix_kernel.
+// ---------------------------------------------------------------------------
+struct TcGramParams {
+    int n_blocks, nb;
+    int64_t n_items;
+    TcGramBlock blk[kMaxBlocks];
+    const int64_t *seg;     // (nb + 1,) padded segment starts, seg[nb] = end
+    float *dB;
+    int32_t *status;
+};
+
+struct GramItem {
+    int m, b, nt, kt, s0, s1;
+    int64_t x0, x1;         // first p' of the lo segment (bin b) and of the hi segment (bin b - 1)
+};
+
+__device__ __forceinline__ GramItem gram_item(const TcGramParams &P, int64_t item) {
+    GramItem g;
+    int m = 0;
+    while (m + 1 < P.n_blocks && P.blk[m + 1].item0 <= item) m++;
+    const TcGramBlock &B = P.blk[m];
+    const int64_t loc = item - B.item0, per_bin = (int64_t)B.n_tiles * B.k_tiles;
+    g.m = m;
+    g.b = (int)(loc / per_bin);
+    const int r = (int)(loc - g.b * per_bin);
+    g.nt = r / B.k_tiles;
+    g.kt = r - g.nt * B.k_tiles;
+    g.s0 = g.b < P.nb ? (int)((P.seg[g.b + 1] - P.seg[g.b]) / kTcK) : 0;
+    g.s1 = g.b >= 1 ? (int)((P.seg[g.b] - P.seg[g.b - 1]) / kTcK) : 0;
+    g.x0 = g.b < P.nb ? P.seg[g.b] : 0;
+    g.x1 = g.b >= 1 ? P.seg[g.b - 1] : 0;
+    return g;
+}
+
+template <int kSplit>
+__global__ void __launch_bounds__(kTcThreads, 1)
+tc_gram_kernel(const __grid_constant__ CUtensorMap mG0, const __grid_constant__ CUtensorMap mG0l,
+               const __grid_constant__ CUtensorMap mG1, const __grid_constant__ CUtensorMap mG1l,
+               const __grid_constant__ CUtensorMap mA, const __grid_constant__ CUtensorMap mAl,
+               const __grid_constant__ TcGramParams P) {
+    constexpr int kTiles = kSplit == 1 ? 2 : 4;      // Gt, At [, Gt.lo, At.lo]
+    constexpr int kStages = kSplit == 1 ? 6 : 3;
+    constexpr uint32_t kStageBytes = kTiles * kTcTileBytes;
+    constexpr uint32_t kIdesc = idesc_bf16_f32(kTcRows, kTcN);
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    __shared__ uint64_t full_bar[kStages], empty_bar[kStages], tfull_bar[2], tempty_bar[2], drain_bar;
+    __shared__ uint32_t tmem_base_s;
+    __shared__ int abort_s;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; s++) {
+            mbar_init(&full_bar[s], 1);
+            mbar_init(&empty_bar[s], 1);
+        }
+        for (int b = 0; b < 2; b++) {
+            mbar_init(&tfull_bar[b], 1);
+            mbar_init(&tempty_bar[b], 128);
+        }
+        mbar_init(&drain_bar, 1);
+        abort_s = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0 && lane == 0) {
+        prefetch_tmap(&mG0);
+        prefetch_tmap(&mG1);
+        prefetch_tmap(&mA);
+    }
+    if (warp == 1) {
+        tmem_alloc(&tmem_base_s, 256);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_base_s;
+    volatile int *abort_flag = &abort_s;
+
+    if (warp == 0 && lane == 0) {
+        // ---------------- TMA producer ----------------
+        int it = 0;
+        for (int64_t item = blockIdx.x; item < P.n_items && !*abort_flag; item += gridDim.x) {
+            const GramItem g = gram_item(P, item);
+            const TcGramBlock &B = P.blk[g.m];
+            const int gy = B.g_row0 + g.nt * kTcRows, ay = B.a_row0 + g.kt * kTcRows;
+            bool ok = true;
+            for (int ks = 0; ks < g.s0 + g.s1; ks++, it++) {
+                const int s = it % kStages, r = it / kStages;
+                if (r > 0 && !mbar_wait(&empty_bar[s], (r - 1) & 1, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                uint8_t *base = smem + (size_t)s * kStageBytes;
+                const bool lo_seg = ks < g.s0;
+                const int x = (int)(lo_seg ? g.x0 + (int64_t)ks * kTcK : g.x1 + (int64_t)(ks - g.s0) * kTcK);
+                mbar_arrive_expect_tx(&full_bar[s], kStageBytes);
+                tma_load_2d(base, lo_seg ? &mG0 : &mG1, x, gy, &full_bar[s]);
+                tma_load_2d(base + kTcTileBytes, &mA, x, ay, &full_bar[s]);
+                if (kSplit == 3) {
+                    tma_load_2d(base + 2 * kTcTileBytes, lo_seg ? &mG0l : &mG1l, x, gy, &full_bar[s]);
+                    tma_load_2d(base + 3 * kTcTileBytes, &mAl, x, ay, &full_bar[s]);
+                }
+            }
+            if (!ok) break;
+        }
+        for (int k = max(0, it - kStages); k < it; k++) mbar_wait_drain(&full_bar[k % kStages], (k / kStages) & 1);
+    } else if (warp == 1 && lane == 0) {
+        // ---------------- MMA issuer ----------------
+        int it = 0, j = 0;
+        for (int64_t item = blockIdx.x; item < P.n_items && !*abort_flag; item += gridDim.x, j++) {
+            const GramItem g = gram_item(P, item);
+            const int buf = j & 1, rr = j >> 1;
+            if (rr > 0 && !mbar_wait(&tempty_bar[buf], (rr - 1) & 1, abort_flag)) break;
+            tc_fence_after();
+            const uint32_t d = tmem + buf * kTcN;
+            bool ok = true;
+            for (int ks = 0; ks < g.s0 + g.s1; ks++, it++) {
+                const int s = it % kStages, r = it / kStages;
+                if (!mbar_wait(&full_bar[s], r & 1, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t base = smem_u32(smem + (size_t)s * kStageBytes);
+#pragma unroll
+                for (int kk = 0; kk < kTcK / 16; kk++) {
+                    const uint32_t koff = kk * 32;
+                    const uint64_t a = smem_desc_sw128(base + koff);
+                    const uint64_t b = smem_desc_sw128(base + kTcTileBytes + koff);
+                    umma_f16(d, a, b, kIdesc, (ks > 0 || kk > 0) ? 1u : 0u);
+                    if (kSplit == 3) {
+                        const uint64_t a2 = smem_desc_sw128(base + 2 * kTcTileBytes + koff);
+                        const uint64_t b2 = smem_desc_sw128(base + 3 * kTcTileBytes + koff);
+                        umma_f16(d, a, b2, kIdesc, 1u);
+                        umma_f16(d, a2, b, kIdesc, 1u);
+                    }
+                }
+                umma_commit(&empty_bar[s]);
+            }
+            if (!ok) break;
+            umma_commit(&tfull_bar[buf]);     // also for an item without steps: the epilogue writes zeros
+        }
+        umma_commit(&drain_bar);
+        mbar_wait_drain(&drain_bar, 0);
+    } else if (warp >= 2) {
+        // ---------------- epilogue ----------------
+        const int q = warp & 3;
+        const int row = q * 32 + lane;         // n within the tile
+        int j = 0;
+        for (int64_t item = blockIdx.x; item < P.n_items; item += gridDim.x, j++) {
+            const int buf = j & 1, rr = j >> 1;
+            if (!mbar_wait(&tfull_bar[buf], rr & 1, abort_flag)) break;
+            tc_fence_after();
+            const GramItem g = gram_item(P, item);
+            const TcGramBlock &B = P.blk[g.m];
+            const int n = g.nt * kTcRows + row;
+            const bool empty = g.s0 + g.s1 == 0;
+            float *drow = P.dB + B.dboff + ((int64_t)g.b * B.N + n) * B.K;
+            const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + buf * kTcN;
+#pragma unroll 1
+            for (int c0 = 0; c0 < kTcN; c0 += 32) {
+                uint32_t v[32];
+                tmem_ld32(taddr + c0, v);
+                tmem_wait_ld();
+                const int k0 = g.kt * kTcN + c0;
+                if (n < B.N) {
+#pragma unroll
+                    for (int c = 0; c < 32; c++)
+                        if (k0 + c < B.K) drow[k0 + c] = empty ? 0.0f : __uint_as_float(v[c]);
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&tempty_bar[buf]);
+        }
+    }
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 256);
+    }
+    if (threadIdx.x == 0 && abort_s && P.status) atomicMax(P.status, 2);
+}
+
 // B operand: per block m and bin b a (npad x kpad) K-major bf16 matrix (rows = output
 // columns n = (o, re/im, co), cols = k = (i, re/im, ci); channel fastest), zero padded; the m > 0 2x2
 // blocks are written as [[a, b], [-b, a]].  With a second buffer the float32 weight is
@@ -456,6 +647,62 @@ int launch_tc_mix(int split, const __nv_bfloat16 *A, const __nv_bfloat16 *A2, in
     } else {
         FEQ_CUDA_TRY(cudaFuncSetAttribute(tc_mix_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
         tc_mix_kernel<3><<<grid, kTcThreads, smem, s>>>(mA, mA2, mB, mB2, P);
+    }
+    FEQ_LAUNCH_CHECK();
+    return FEQ_OK;
+}
+
+}  // namespace feq
+
+namespace feq {
+
+// Per-bin gradient reduction (see tc_gram_kernel).  Gt0 / Gt1: (1 - t) and t weighted
+// transposes of G (g_rows x p_cols), At: transpose of A (a_rows x p_cols); blk[m] holds the
+// block geometry (item0 is filled here); seg: device (nb + 1,) segment starts.
+int launch_tc_gram(int split, const __nv_bfloat16 *Gt0, const __nv_bfloat16 *Gt0l, const __nv_bfloat16 *Gt1,
+                   const __nv_bfloat16 *Gt1l, int64_t g_rows, const __nv_bfloat16 *At, const __nv_bfloat16 *Atl,
+                   int64_t a_rows, int64_t p_cols, int n_blocks, const TcGramBlock *blk, int nb, const int64_t *seg,
+                   float *dB, int32_t *status, cudaStream_t s) {
+    TcGramParams P;
+    memset(&P, 0, sizeof(P));
+    P.n_blocks = n_blocks;
+    P.nb = nb;
+    int64_t items = 0;
+    for (int m = 0; m < n_blocks; m++) {
+        P.blk[m] = blk[m];
+        P.blk[m].item0 = items;
+        items += (int64_t)(nb + 1) * blk[m].n_tiles * blk[m].k_tiles;
+    }
+    P.n_items = items;
+    P.seg = seg;
+    P.dB = dB;
+    P.status = status;
+    if (items == 0) return FEQ_OK;
+    CUtensorMap m0, m0l, m1, m1l, ma, mal;
+    int rc;
+    if ((rc = make_map(&m0, Gt0, p_cols, g_rows)) != FEQ_OK) return rc;
+    if ((rc = make_map(&m1, Gt1, p_cols, g_rows)) != FEQ_OK) return rc;
+    if ((rc = make_map(&ma, At, p_cols, a_rows)) != FEQ_OK) return rc;
+    if (split == 3) {
+        if ((rc = make_map(&m0l, Gt0l, p_cols, g_rows)) != FEQ_OK) return rc;
+        if ((rc = make_map(&m1l, Gt1l, p_cols, g_rows)) != FEQ_OK) return rc;
+        if ((rc = make_map(&mal, Atl, p_cols, a_rows)) != FEQ_OK) return rc;
+    } else {
+        m0l = m0;
+        m1l = m1;
+        mal = ma;
+    }
+    int dev = 0, sms = 148;
+    FEQ_CUDA_TRY(cudaGetDevice(&dev));
+    FEQ_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    const int grid = (int)min64(sms, items);
+    const size_t smem = (size_t)(split == 1 ? 6 * 2 : 3 * 4) * kTcTileBytes + 1024;
+    if (split == 1) {
+        FEQ_CUDA_TRY(cudaFuncSetAttribute(tc_gram_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        tc_gram_kernel<1><<<grid, kTcThreads, smem, s>>>(m0, m0l, m1, m1l, ma, mal, P);
+    } else {
+        FEQ_CUDA_TRY(cudaFuncSetAttribute(tc_gram_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        tc_gram_kernel<3><<<grid, kTcThreads, smem, s>>>(m0, m0l, m1, m1l, ma, mal, P);
     }
     FEQ_LAUNCH_CHECK();
     return FEQ_OK;
