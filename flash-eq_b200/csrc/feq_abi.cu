@@ -81,6 +81,8 @@ int launch_bwd_rows(const float *gA, const float *gAd, int ld_g, const __nv_bflo
 int launch_bwd_table_convert(const float *dB, const DbOff &dboff, int nb1, int Cout, int Cin, int W,
                              const MixLayout &M, float *grad_table, cudaStream_t s);
 int launch_bwd_segments(const int64_t *offsets, int nb, int64_t *seg, cudaStream_t s);
+int launch_unprep_rows(const float *H, int ld, const float *dist, const int64_t *perm, int64_t E, int C, int D,
+                       const TcPosMap &Mp, float sh_scale, float *out, cudaStream_t s);
 int launch_bwd_transpose_rows(const __nv_bfloat16 *Xhi, const __nv_bfloat16 *Xlo, int ld, int ncols,
                               const int64_t *offsets, const int64_t *seg, int nb, const float *tval, int wmode,
                               int64_t pcols, __nv_bfloat16 *Yhi, __nv_bfloat16 *Ylo, cudaStream_t s);
@@ -762,6 +764,83 @@ int feq_block_diagonal_fwd(const float *features, const float *radial_table, con
     Binning b{bin_param1, bin_param2, num_bins, log_bins ? 1 : 0};
     return run_mix(p, features, radial_table, distances, num_edges, c_in, c_out, din, dout, M, b, sh_scale,
                    output, (cudaStream_t)stream);
+}
+
+size_t feq_block_diagonal_fwd_mix_workspace_bytes(int64_t num_edges, int32_t c_in, int32_t c_out,
+                                                  const int32_t *lvals_in, int32_t n_lvals_in,
+                                                  const int32_t *lvals_out, int32_t n_lvals_out, int32_t num_bins,
+                                                  int32_t mix_mode) {
+    if (mix_mode == FEQ_MIX_FP32)
+        return feq_block_diagonal_workspace_bytes(num_edges, c_in, c_out, lvals_in, n_lvals_in, lvals_out,
+                                                  n_lvals_out, num_bins);
+    if (!mix_args_ok(num_edges, c_in, c_out, num_bins)) return 0;
+    if (mix_mode != FEQ_MIX_BF16 && mix_mode != FEQ_MIX_BF16X3) return 0;
+    static thread_local BwdPlan P;
+    if (build_bwd_plan(lvals_in, n_lvals_in, lvals_out, n_lvals_out, c_in, c_out, num_bins, &P) != FEQ_OK) return 0;
+    WsCarver w{nullptr, 0, 0};
+    TcBuffers b;
+    carve_tc(w, num_edges, num_bins, P.T, mix_mode == FEQ_MIX_BF16X3, b);
+    return w.used + 256;
+}
+
+int feq_block_diagonal_fwd_mix(const float *features, const float *radial_table, const float *distances,
+                               int64_t num_edges, int32_t c_in, int32_t c_out, const int32_t *lvals_in,
+                               int32_t n_lvals_in, const int32_t *lvals_out, int32_t n_lvals_out, float sh_scale,
+                               float bin_param1, float bin_param2, int32_t num_bins, int32_t log_bins,
+                               int32_t mix_mode, float *output, void *workspace, size_t workspace_bytes,
+                               feq_stream_t stream) {
+    if (mix_mode == FEQ_MIX_FP32)
+        return feq_block_diagonal_fwd(features, radial_table, distances, num_edges, c_in, c_out, lvals_in,
+                                      n_lvals_in, lvals_out, n_lvals_out, sh_scale, bin_param1, bin_param2, num_bins,
+                                      log_bins, output, workspace, workspace_bytes, stream);
+    if (!mix_args_ok(num_edges, c_in, c_out, num_bins)) return FEQ_ERR_INVALID_ARGUMENT;
+    if (mix_mode != FEQ_MIX_BF16 && mix_mode != FEQ_MIX_BF16X3) return FEQ_ERR_UNSUPPORTED;
+    static thread_local BwdPlan P;
+    int rc = build_bwd_plan(lvals_in, n_lvals_in, lvals_out, n_lvals_out, c_in, c_out, num_bins, &P);
+    if (rc != FEQ_OK) return rc;
+    if (num_edges == 0) return FEQ_OK;
+    if (!features || !radial_table || !distances || !output) return FEQ_ERR_INVALID_ARGUMENT;
+    const bool split = mix_mode == FEQ_MIX_BF16X3;
+    WsCarver w{(char *)workspace, 0, workspace_bytes};
+    TcBuffers b;
+    carve_tc(w, num_edges, num_bins, P.T, split, b);
+    if (!workspace || w.used > workspace_bytes) return FEQ_ERR_WORKSPACE;
+    cudaStream_t s = (cudaStream_t)stream;
+    const TcPlan &T = P.T;
+    const int64_t E = num_edges;
+    Binning bins{bin_param1, bin_param2, num_bins, log_bins ? 1 : 0};
+    {
+        ProfScope ps("bin_sort_tiles", s);
+        if ((rc = launch_binning(distances, E, bins, b.keys, nullptr, s)) != FEQ_OK) return rc;
+        if ((rc = launch_edge_sort<int32_t>(b.keys, E, num_bins, b.perm, b.offsets, nullptr, b.sort_ws,
+                                            b.sort_ws_bytes, s)) != FEQ_OK)
+            return rc;
+        if ((rc = launch_build_tiles(b.offsets, num_bins, 128, b.tiles, b.num_tiles, s)) != FEQ_OK) return rc;
+    }
+    {
+        ProfScope ps("prep_rows", s);
+        if ((rc = launch_bwd_prep_rows(features, distances, b.perm, E, c_in, P.Li.dim, T.in_map, T.k_total, bins,
+                                       sh_scale, b.A_hi, b.A_lo, b.tval, s)) != FEQ_OK)
+            return rc;
+        if ((rc = launch_tc_relayout_b(radial_table, b.B_hi, b.B_lo, num_bins + 1, c_in, c_out, P.M.wdim, T.G,
+                                       T.b_total, s)) != FEQ_OK)
+            return rc;
+    }
+    for (int m = 0; m < T.G.n_blocks; m++) {
+        ProfScope ps("tc_mix", s);
+        const TcBlockGeom &g = T.G.g[m];
+        if ((rc = launch_tc_mix(split ? 3 : 1, b.A_hi, b.A_lo, E, T.k_total, b.B_hi + g.boff,
+                                split ? b.B_lo + g.boff : nullptr, (int64_t)(num_bins + 1) * g.npad, g, T.koff[m],
+                                T.nvalid[m], T.n_total, T.noff[m], b.tiles, b.num_tiles, b.max_tiles, b.tval, b.H,
+                                nullptr, s)) != FEQ_OK)
+            return rc;
+    }
+    ProfScope ps("unprep_rows", s);
+    if (T.G.n_blocks == 0 || T.n_total == 0) {
+        FEQ_CUDA_TRY(cudaMemsetAsync(output, 0, sizeof(float) * (size_t)E * c_out * P.Lo.dim, s));
+        return FEQ_OK;
+    }
+    return launch_unprep_rows(b.H, T.n_total, distances, b.perm, E, c_out, P.Lo.dim, T.out_map, sh_scale, output, s);
 }
 
 size_t feq_block_diagonal_bwd_workspace_bytes(int64_t num_edges, int32_t c_in, int32_t c_out,

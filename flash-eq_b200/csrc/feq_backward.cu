@@ -385,4 +385,42 @@ int launch_bwd_transpose_rows(const __nv_bfloat16 *Xhi, const __nv_bfloat16 *Xlo
     return FEQ_OK;
 }
 
+// out[e][c][j] = s^l(j) H[p][base[j] + c] (0 where base < 0): sorted mix rows back to m-first
+// edge rows (E, C, D).  One warp per row, staged in shared memory for coalesced stores.
+__global__ void unprep_rows_kernel(const float *__restrict__ H, int ld, const float *__restrict__ dist,
+                                   const int64_t *__restrict__ perm, int64_t E, int C, int D,
+                                   const __grid_constant__ TcPosMap Mp, float sh_scale, float *__restrict__ out) {
+    extern __shared__ float un_s[];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int row = C * D;
+    float *rs = un_s + (size_t)w * row;
+    for (int64_t p = (int64_t)blockIdx.x * nw + w; p < E; p += (int64_t)gridDim.x * nw) {
+        const int64_t e = perm[p];
+        const float dd = dist[e];
+        const float s = dd / (dd + sh_scale);
+        const float *hr = H + p * (int64_t)ld;
+        for (int j = 0; j < D; j++) {
+            const int b = Mp.base[j];
+            const float sl = ipowf(s, Mp.l[j]);
+            for (int c = lane; c < C; c += 32) rs[c * D + j] = b < 0 ? 0.0f : hr[b + c] * sl;
+        }
+        __syncwarp();
+        float *orow = out + e * (int64_t)row;
+        for (int i = lane; i < row; i += 32) orow[i] = rs[i];
+        __syncwarp();
+    }
+}
+
+int launch_unprep_rows(const float *H, int ld, const float *dist, const int64_t *perm, int64_t E, int C, int D,
+                       const TcPosMap &Mp, float sh_scale, float *out, cudaStream_t s) {
+    if (E == 0) return FEQ_OK;
+    const int nw = rows_warps((size_t)C * D);
+    if (nw == 0) return FEQ_ERR_UNSUPPORTED;
+    const size_t smem = (size_t)nw * C * D * 4;
+    FEQ_CUDA_TRY(cudaFuncSetAttribute(unprep_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    unprep_rows_kernel<<<grid_for(E, nw), nw * 32, smem, s>>>(H, ld, dist, perm, E, C, D, Mp, sh_scale, out);
+    FEQ_LAUNCH_CHECK();
+    return FEQ_OK;
+}
+
 }  // namespace feq

@@ -73,6 +73,13 @@ SIGNATURES = {
                                               c_i32p, ctypes.c_int32, c_i32p, ctypes.c_int32, ctypes.c_float,
                                               ctypes.c_float, ctypes.c_float, ctypes.c_int32, ctypes.c_int32,
                                               c_vp, c_vp, ctypes.c_size_t, c_vp]),
+    "feq_block_diagonal_fwd_mix_workspace_bytes": (ctypes.c_size_t, [ctypes.c_int64, ctypes.c_int32,
+                                                                     ctypes.c_int32, c_i32p, ctypes.c_int32, c_i32p,
+                                                                     ctypes.c_int32, ctypes.c_int32, ctypes.c_int32]),
+    "feq_block_diagonal_fwd_mix": (ctypes.c_int, [c_vp, c_vp, c_vp, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32,
+                                                  c_i32p, ctypes.c_int32, c_i32p, ctypes.c_int32, ctypes.c_float,
+                                                  ctypes.c_float, ctypes.c_float, ctypes.c_int32, ctypes.c_int32,
+                                                  ctypes.c_int32, c_vp, c_vp, ctypes.c_size_t, c_vp]),
     "feq_block_diagonal_bwd_workspace_bytes": (ctypes.c_size_t, [ctypes.c_int64, ctypes.c_int32, ctypes.c_int32,
                                                                  c_i32p, ctypes.c_int32, c_i32p, ctypes.c_int32,
                                                                  ctypes.c_int32, ctypes.c_int32]),

@@ -66,8 +66,15 @@ def block_diagonal_cuda(
     num_bins: int,
     log_bins: bool = False,
     sh_scale: float = 0.1,
+    *,
+    mix: str = "fp32",
 ) -> torch.Tensor:
-    """out[e] = Lambda(r_e) f[e] in the m-first basis (see module docstring)."""
+    """out[e] = Lambda(r_e) f[e] in the m-first basis (see module docstring).
+
+    ``mix`` (not a reference argument): "fp32" CUDA-core float32 (default), "bf16x3" or
+    "bf16" tensor cores.  The backward always runs on the tensor cores ("bf16x3" unless
+    "bf16" is asked for).
+    """
     if not torch.cuda.is_available():
         raise CUDANotAvailableError("flash-eq requires a CUDA-capable GPU. No CUDA device was detected.")
     lvals_in = product_repr.rep1.lvals.tolist()
@@ -81,11 +88,11 @@ def block_diagonal_cuda(
         raise RuntimeError("Maximum l-value exceeds supported limit (16).")
     dist = distances.to(features.dtype)
     cfg = (tuple(lvals_in), tuple(lvals_out), float(sh_scale), float(bin_param1), float(bin_param2), int(num_bins),
-           bool(log_bins))
+           bool(log_bins), mix)
     if torch.is_grad_enabled() and any(t.requires_grad for t in (features, radial_table, dist)):
         return _BlockDiagonalFunction.apply(features, radial_table, dist, cfg)
     return ops.block_diagonal_fwd(features.detach(), radial_table.detach(), dist.detach(), lvals_in, lvals_out,
-                                  sh_scale, bin_param1, bin_param2, num_bins, log_bins)
+                                  sh_scale, bin_param1, bin_param2, num_bins, log_bins, mix=mix)
 
 
 class _BlockDiagonalFunction(torch.autograd.Function):
@@ -93,17 +100,18 @@ class _BlockDiagonalFunction(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, features, radial_table, dist, cfg):
-        lin, lout, sh, p1, p2, nb, log = cfg
+        lin, lout, sh, p1, p2, nb, log, mix = cfg
         ctx.cfg = cfg
         ctx.save_for_backward(features, radial_table, dist)
         return ops.block_diagonal_fwd(features.detach(), radial_table.detach(), dist.detach(), list(lin), list(lout),
-                                      sh, p1, p2, nb, log)
+                                      sh, p1, p2, nb, log, mix=mix)
 
     @staticmethod
     def backward(ctx, grad_out):
-        lin, lout, sh, p1, p2, nb, log = ctx.cfg
+        lin, lout, sh, p1, p2, nb, log, mix = ctx.cfg
         features, radial_table, dist = ctx.saved_tensors
         gf, gt, gd = ops.block_diagonal_bwd(grad_out.contiguous(), features.detach(), radial_table.detach(),
-                                            dist.detach(), list(lin), list(lout), sh, p1, p2, nb, log)
+                                            dist.detach(), list(lin), list(lout), sh, p1, p2, nb, log,
+                                            mix="bf16" if mix == "bf16" else "bf16x3")
         return (gf if ctx.needs_input_grad[0] else None, gt if ctx.needs_input_grad[1] else None,
                 gd if ctx.needs_input_grad[2] else None, None)

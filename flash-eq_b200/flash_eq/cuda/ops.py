@@ -102,7 +102,7 @@ def edge_sort(keys: torch.Tensor, num_keys: int):
 
 
 def block_diagonal_fwd(features, radial_table, distances, lvals_in, lvals_out, sh_scale, p1, p2,
-                       num_bins, log_bins):
+                       num_bins, log_bins, mix="fp32"):
     lib = _require_cuda(features, radial_table, distances)
     features = _f32(features, "features")
     radial_table = _f32(radial_table, "radial_table")
@@ -120,15 +120,16 @@ def block_diagonal_fwd(features, radial_table, distances, lvals_in, lvals_out, s
         return out
     ai, ni = _lib.i32_array(lvals_in)
     ao, no = _lib.i32_array(lvals_out)
-    ws_bytes = lib.feq_block_diagonal_workspace_bytes(E, c_in, c_out, ai, ni, ao, no, int(num_bins))
+    mode = _lib.FEQ_MIX[mix]
+    ws_bytes = lib.feq_block_diagonal_fwd_mix_workspace_bytes(E, c_in, c_out, ai, ni, ao, no, int(num_bins), mode)
     if ws_bytes == 0:
         raise RuntimeError("block-diagonal: unsupported layout (l <= 16, <= 64 irreps)")
     ws = _workspace(ws_bytes, features.device)
-    rc = lib.feq_block_diagonal_fwd(_p(features), _p(radial_table), _p(distances), E, c_in, c_out, ai, ni, ao,
-                                    no, float(sh_scale), float(p1), float(p2), int(num_bins),
-                                    int(bool(log_bins)), _p(out), _p(ws), ws.numel(),
-                                    _stream(features.device))
-    _lib.check(rc, "feq_block_diagonal_fwd")
+    rc = lib.feq_block_diagonal_fwd_mix(_p(features), _p(radial_table), _p(distances), E, c_in, c_out, ai, ni,
+                                        ao, no, float(sh_scale), float(p1), float(p2), int(num_bins),
+                                        int(bool(log_bins)), mode, _p(out), _p(ws), ws.numel(),
+                                        _stream(features.device))
+    _lib.check(rc, "feq_block_diagonal_fwd_mix")
     return out
 
 

@@ -103,7 +103,7 @@ class EquivariantEdgewiseLinear(nn.Module):
             f = f + edge_add
         f_diag = torch.bmm(f, _dense(P))
         out_diag = block_diagonal_cuda(f_diag, table, dist, self.product_repr, p1, p2, self.radial_weights.num_bins,
-                                       self.radial_weights.log, self.solid_harmonic_scale)
+                                       self.radial_weights.log, self.solid_harmonic_scale, mix=self.mix_precision)
         return torch.bmm(out_diag, _dense(Q).mT)
 
     def extra_repr(self) -> str:

@@ -133,6 +133,21 @@ int feq_block_diagonal_fwd(const float *features, const float *radial_table,
                            int32_t log_bins, float *output, void *workspace,
                            size_t workspace_bytes, feq_stream_t stream);
 
+/* feq_block_diagonal_fwd with a selectable mix arithmetic (no counterpart in the reference):
+ * FEQ_MIX_FP32 is feq_block_diagonal_fwd itself; FEQ_MIX_BF16X3 / FEQ_MIX_BF16 run the
+ * tensor-core (tcgen05) mix on the m-first rows (sort by bin, rows to the mix layout, mix,
+ * rows back), the forward used by training. */
+size_t feq_block_diagonal_fwd_mix_workspace_bytes(int64_t num_edges, int32_t c_in, int32_t c_out,
+                                                  const int32_t *lvals_in, int32_t n_lvals_in,
+                                                  const int32_t *lvals_out, int32_t n_lvals_out,
+                                                  int32_t num_bins, int32_t mix_mode);
+int feq_block_diagonal_fwd_mix(const float *features, const float *radial_table, const float *distances,
+                               int64_t num_edges, int32_t c_in, int32_t c_out, const int32_t *lvals_in,
+                               int32_t n_lvals_in, const int32_t *lvals_out, int32_t n_lvals_out,
+                               float sh_scale, float bin_param1, float bin_param2, int32_t num_bins,
+                               int32_t log_bins, int32_t mix_mode, float *output, void *workspace,
+                               size_t workspace_bytes, feq_stream_t stream);
+
 /* Backward of feq_block_diagonal_fwd.
  * Replaces _block_diagonal_cuda.backward (flash_eq/cuda/csrc/block_diagonal.cu:1543-1758,
  * kernels :747-1161; wrapper _BlockDiagonalFunction.backward, block_diagonal.py:140-174):

@@ -120,3 +120,13 @@ def test_edgewise_layer_training_step_matches_oracle(cuda_device):
     table.backward(gtab.to(dev, torch.float32))
     for (n, a), (_, b) in zip(layer.named_parameters(), ref_layer.named_parameters()):
         assert rel_l2(a.grad, b.grad) < 1e-4, n
+
+
+@pytest.mark.parametrize("mode", ["bf16x3", "bf16"])
+@pytest.mark.parametrize("case", CASES[:5], ids=[f"{c[0]}-{c[1]}" for c in CASES[:5]])
+def test_block_diagonal_tensor_core_forward(cuda_device, mode, case):
+    lin, lout, f, tb, d, go, p1, p2, nb, log = _inputs(case, seed=9)
+    y = ops.block_diagonal_fwd(f.to(cuda_device), tb.to(cuda_device), d.to(cuda_device), lin, lout, 0.1, p1, p2, nb,
+                               log, mix=mode)
+    ref = orc.block_diagonal_fwd(f.double(), tb.double(), d.double(), lin, lout, 0.1, p1, p2, nb, log)
+    assert rel_l2(y, ref) < TOL[mode]
