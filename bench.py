@@ -511,6 +511,70 @@ def run_e2e(args, wl, layer, basis, dev, pg, world):
             "d2h_bytes_per_step": out_h.numel() * 4, "ms_per_step": ms, "steps": steps, "chunks": n_chunks}
 
 
+# Published single-layer numbers of the reference (fwd + bwd + Adam, float32, H100, C = 32,
+# 64 bins): (lmax, edges) -> ms per step, README.md:281-290 of hmblair/flash-eq.
+PUBLISHED_TRAIN_MS = {(1, 32000): 5.3, (2, 32000): 11.5, (4, 5000): 7.1, (6, 5000): 14.7, (4, 20000): 21.5,
+                      (6, 20000): 50.6, (4, 50000): 50.1, (6, 50000): 123.5, (4, 128000): 125.6,
+                      (6, 128000): 309.7}
+
+
+def run_train(args):
+    """The reference's published single-layer training step (its benchmarks/compare_all.py
+    harness, restated): EquivariantEdgewiseLinear(Repr(0..L, 32)), 64 bins over [0, 10],
+    random unit directions, U[0, 10] distances, MSE to a random target, Adam."""
+    import flash_eq as fe
+
+    world, rank, local, pg = dist_setup(args)
+    dev = torch.device("cuda", local)
+    lmax, E, C = args.lmax, args.edges, 32
+    torch.manual_seed(SEED + rank)
+    r = fe.Repr(list(range(lmax + 1)), mult=C)
+    layer = fe.EquivariantEdgewiseLinear(r, r, num_bins=64, min_dist=0.0, max_dist=10.0).to(dev)
+    layer.mix_precision = args.mix if args.mix != "fp32" else "bf16x3"
+    basis = fe.WignerDBasis([r, r]).to(dev)
+    opt = torch.optim.Adam(layer.parameters(), lr=1e-4)
+    g = torch.Generator(device=dev).manual_seed(SEED + rank)
+    feats = torch.randn(E, C, r.dim(), device=dev, generator=g).requires_grad_()
+    dirs = torch.randn(E, 3, device=dev, generator=g)
+    dirs = dirs / dirs.norm(dim=-1, keepdim=True)
+    dists = torch.rand(E, device=dev, generator=g) * 10.0
+    target = torch.randn(E, C, r.dim(), device=dev, generator=g)
+    P, Q = basis(dirs)
+
+    def step():
+        opt.zero_grad()
+        out = layer(P, Q, feats, dists)
+        loss = ((out - target) ** 2).mean()
+        loss.backward()
+        opt.step()
+
+    for _ in range(args.warmup):
+        step()
+    barrier(pg)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(args.steps):
+        step()
+    t1.record()
+    barrier(pg)
+    ms = max_over_ranks(pg, t0.elapsed_time(t1) / args.steps)
+    if rank == 0:
+        pub = PUBLISHED_TRAIN_MS.get((lmax, E))
+        print(json.dumps({
+            "metric": "edges/sec (fwd+bwd+Adam, EquivariantEdgewiseLinear)", "value": E * world / (ms / 1e3),
+            "unit": "edges/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "mix": layer.mix_precision,
+            "config": {"workload": f"reference single-layer training step: Repr(0..{lmax}, 32), E={E}, 64 bins",
+                       "edges_per_gpu": E},
+            "published_reference_ms_h100": pub,
+            "note": "published number is the reference on an H100 (README), context only"}), flush=True)
+    if pg is not None:
+        pg.barrier()
+        pg.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -523,6 +587,10 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--e2e-chunks", type=int, default=8,
                     help="edge chunks per end-to-end step (output copy of one overlaps compute of the next)")
+    ap.add_argument("--workload", choices=["config2", "train"], default="config2",
+                    help="config2: the metric (default); train: the reference's published single-layer "
+                         "fwd+bwd+Adam step (--lmax, --edges)")
+    ap.add_argument("--edges", type=int, default=None)
     ap.add_argument("--lmax", type=int, default=4,
                     help="degrees 0..lmax in and out (default 4 = config 2); other values are variants, not the metric")
     ap.add_argument("--mix", choices=["fp32", "bf16x3", "bf16"], default="bf16x3",
@@ -530,6 +598,11 @@ def main():
     args = ap.parse_args()
     global LVALS
     LVALS = list(range(args.lmax + 1))
+    if args.workload == "train":
+        if args.lmax == 4 and args.edges is None:
+            args.edges = 128000
+        args.edges = args.edges or 32000
+        return run_train(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)
