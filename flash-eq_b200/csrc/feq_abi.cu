@@ -86,13 +86,6 @@ int launch_unprep_rows(const float *H, int ld, const float *dist, const int64_t 
 int launch_bwd_transpose_rows(const __nv_bfloat16 *Xhi, const __nv_bfloat16 *Xlo, int ld, int ncols,
                               const int64_t *offsets, const int64_t *seg, int nb, const float *tval, int wmode,
                               int64_t pcols, __nv_bfloat16 *Yhi, __nv_bfloat16 *Ylo, cudaStream_t s);
-bool fused_edgewise_supported(const TcPlan &T, const ReprLayout &Li, const ReprLayout &Lo);
-int64_t fused_bq_elems(const TcPlan &T, int nb1);
-int launch_fused_edgewise(const TcPlan &T, const ReprLayout &Li, const ReprLayout &Lo, const __nv_bfloat16 *B,
-                          __nv_bfloat16 *Bq, int nb, const float *x, const int64_t *src, int64_t nsrc,
-                          const float *dirs, const float *dist, const int64_t *perm, const int4 *tiles,
-                          const int *num_tiles, int64_t max_tiles, Binning bins, float sh_scale, float *out,
-                          int32_t *status, cudaStream_t s);
 int launch_tc_gram(int split, const __nv_bfloat16 *Gt0, const __nv_bfloat16 *Gt0l, const __nv_bfloat16 *Gt1,
                    const __nv_bfloat16 *Gt1l, int64_t g_rows, const __nv_bfloat16 *At, const __nv_bfloat16 *Atl,
                    int64_t a_rows, int64_t p_cols, int n_blocks, const TcGramBlock *blk, int nb, const int64_t *seg,
@@ -300,6 +293,14 @@ static bool mix_args_ok(int64_t E, int Cin, int Cout, int nb) {
 // ---------------------------------------------------------------------------
 // Tensor-core plan: GEMM geometry per m-block and the row maps of A and H.
 // ---------------------------------------------------------------------------
+struct TcPlan {
+    TcGeom G;
+    int koff[kMaxBlocks], noff[kMaxBlocks], nvalid[kMaxBlocks];
+    int k_total, n_total;
+    int c_in, c_out;
+    int64_t b_total;
+    TcPosMap in_map, out_map;
+};
 
 // Offset of block m in m-first order when every irrep with l >= m contributes
 // (wigner.py:243-272), independent of whether the block takes part in the mix.
@@ -417,52 +418,6 @@ static void carve_tc(WsCarver &w, int64_t E, int nb, const TcPlan &T, bool split
     b.num_tiles = (int *)w.take(16);
     b.sort_ws_bytes = edge_sort_workspace(E, nb);
     b.sort_ws = w.take(b.sort_ws_bytes);
-}
-
-// One-kernel path (bf16 mix, small representations): no A or H matrices in HBM.
-static bool use_fused(const FeqEdgewiseArgs *a, const TcPlan &T, const ReprLayout &Li, const ReprLayout &Lo) {
-    return a->mix_mode == FEQ_MIX_BF16 && a->directions && !a->edge_add && fused_edgewise_supported(T, Li, Lo);
-}
-
-static void carve_fused(WsCarver &w, int64_t E, int nb, const TcPlan &T, TcBuffers &b, __nv_bfloat16 *&Bq) {
-    const int64_t E1 = std::max<int64_t>(E, 1);
-    memset(&b, 0, sizeof(b));
-    b.B_hi = (__nv_bfloat16 *)w.take(2 * (size_t)T.b_total);
-    Bq = (__nv_bfloat16 *)w.take(2 * (size_t)fused_bq_elems(T, nb + 1));
-    b.keys = (int32_t *)w.take(4 * (size_t)E1);
-    b.perm = (int64_t *)w.take(8 * (size_t)E1);
-    b.offsets = (int64_t *)w.take(8 * (size_t)(nb + 1));
-    b.max_tiles = mix_max_tiles(E, nb, 128);
-    b.tiles = (int4 *)w.take(sizeof(int4) * b.max_tiles);
-    b.num_tiles = (int *)w.take(16);
-    b.sort_ws_bytes = edge_sort_workspace(E, nb);
-    b.sort_ws = w.take(b.sort_ws_bytes);
-}
-
-static int run_edgewise_fused(const FeqEdgewiseArgs *a, const MixLayout &M, const ReprLayout &Li,
-                              const ReprLayout &Lo, const TcPlan &T, const TcBuffers &b, __nv_bfloat16 *Bq,
-                              cudaStream_t s) {
-    const int64_t E = a->num_edges;
-    Binning bins{a->bin_param1, a->bin_param2, a->num_bins, a->log_bins ? 1 : 0};
-    int rc;
-    {
-        ProfScope ps("bin_sort_tiles", s);
-        if ((rc = launch_binning(a->distances, E, bins, b.keys, nullptr, s)) != FEQ_OK) return rc;
-        if ((rc = launch_edge_sort<int32_t>(b.keys, E, a->num_bins, b.perm, b.offsets, nullptr, b.sort_ws,
-                                            b.sort_ws_bytes, s)) != FEQ_OK)
-            return rc;
-        if ((rc = launch_build_tiles(b.offsets, a->num_bins, 128, b.tiles, b.num_tiles, s)) != FEQ_OK) return rc;
-    }
-    {
-        ProfScope ps("relayout_table", s);
-        if ((rc = launch_tc_relayout_b(a->radial_table, b.B_hi, nullptr, a->num_bins + 1, a->c_in, a->c_out, M.wdim,
-                                       T.G, T.b_total, s)) != FEQ_OK)
-            return rc;
-    }
-    ProfScope ps("fused_edgewise", s);
-    return launch_fused_edgewise(T, Li, Lo, b.B_hi, Bq, a->num_bins, a->x, a->src, a->num_src_rows, a->directions,
-                                 a->distances, b.perm, b.tiles, b.num_tiles, b.max_tiles, bins, a->sh_scale, a->out,
-                                 a->status, s);
 }
 
 static int run_edgewise_tc(const FeqEdgewiseArgs *a, const MixLayout &M, const ReprLayout &Li,
@@ -945,12 +900,7 @@ size_t feq_edgewise_workspace_bytes(const FeqEdgewiseArgs *a) {
         if (build_tc_plan(M, Li, Lo, a->c_in, a->c_out, a->num_bins, &T) != FEQ_OK) return 0;
         WsCarver w{nullptr, 0, 0};
         TcBuffers b;
-        if (use_fused(a, T, Li, Lo)) {
-            __nv_bfloat16 *Bq;
-            carve_fused(w, a->num_edges, a->num_bins, T, b, Bq);
-        } else {
-            carve_tc(w, a->num_edges, a->num_bins, T, a->mix_mode == FEQ_MIX_BF16X3, b);
-        }
+        carve_tc(w, a->num_edges, a->num_bins, T, a->mix_mode == FEQ_MIX_BF16X3, b);
         return w.used + 256;
     }
     const int64_t E1 = std::max<int64_t>(a->num_edges, 1);
@@ -982,12 +932,6 @@ int feq_edgewise_fwd(const FeqEdgewiseArgs *a, void *workspace, size_t workspace
         if ((rc = build_tc_plan(M, Li, Lo, a->c_in, a->c_out, a->num_bins, &T)) != FEQ_OK) return rc;
         WsCarver w{(char *)workspace, 0, workspace_bytes};
         TcBuffers b;
-        if (use_fused(a, T, Li, Lo)) {
-            __nv_bfloat16 *Bq;
-            carve_fused(w, E, a->num_bins, T, b, Bq);
-            if (!workspace || w.used > workspace_bytes) return FEQ_ERR_WORKSPACE;
-            return run_edgewise_fused(a, M, Li, Lo, T, b, Bq, s);
-        }
         carve_tc(w, E, a->num_bins, T, a->mix_mode == FEQ_MIX_BF16X3, b);
         if (!workspace || w.used > workspace_bytes) return FEQ_ERR_WORKSPACE;
         return run_edgewise_tc(a, M, Li, Lo, T, b, s);
