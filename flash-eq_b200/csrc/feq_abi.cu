@@ -636,7 +636,7 @@ const char *feq_status_string(int status) {
     }
 }
 
-int feq_abi_version(void) { return 2; }
+int feq_abi_version(void) { return 3; }
 
 const char *feq_last_error(void) { return g_last_error.c_str(); }
 

@@ -47,7 +47,15 @@ class FeqAttnArgs(ctypes.Structure):
     ]
 
 
-FEQ_ABI_VERSION = 2   # must equal feq_abi_version() of the loaded library
+class FeqAttnBwdArgs(ctypes.Structure):
+    _fields_ = [
+        ("fwd", FeqAttnArgs), ("grad_out", c_vp), ("dst", c_vp), ("src_perm", c_vp), ("src_offsets", c_vp),
+        ("grad_q", c_vp), ("ldq", ctypes.c_int64), ("grad_k", c_vp), ("ldk", ctypes.c_int64), ("grad_v", c_vp),
+        ("grad_distances", c_vp), ("grad_scale_partial", c_vp), ("edge_scratch", c_vp),
+    ]
+
+
+FEQ_ABI_VERSION = 3   # must equal feq_abi_version() of the loaded library
 
 # name -> (restype, argtypes)
 SIGNATURES = {
@@ -101,6 +109,15 @@ SIGNATURES = {
     "feq_segment_pool": (ctypes.c_int, [c_vp, ctypes.c_int64, c_vp, ctypes.c_int32, c_vp, c_vp, ctypes.c_int64,
                                         ctypes.c_int32, c_vp, c_vp]),
     "feq_attn_pool_fwd": (ctypes.c_int, [ctypes.POINTER(FeqAttnArgs), c_vp]),
+    "feq_attn_pool_bwd": (ctypes.c_int, [ctypes.POINTER(FeqAttnBwdArgs), c_vp]),
+    "feq_segment_softmax_bwd": (ctypes.c_int, [c_vp, c_vp, ctypes.c_int64, ctypes.c_int32, c_vp, c_vp,
+                                               ctypes.c_int64, c_vp, c_vp]),
+    "feq_edge_attention_weights_bwd": (ctypes.c_int, [c_vp, c_vp, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32,
+                                                      ctypes.c_float, ctypes.c_float, c_vp, c_vp, ctypes.c_int64,
+                                                      c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp]),
+    "feq_segment_pool_bwd": (ctypes.c_int, [c_vp, ctypes.c_int64, c_vp, ctypes.c_int32, c_vp, c_vp, c_vp,
+                                            ctypes.c_int64, ctypes.c_int64, ctypes.c_int32, c_vp, c_vp, c_vp, c_vp,
+                                            c_vp, c_vp, c_vp]),
 }
 
 _lock = threading.Lock()

@@ -334,6 +334,130 @@ def attn_pool(qk, v, src, distances, perm, offsets, num_nodes, num_heads, scale,
     return out
 
 
+def attn_pool_bwd(grad_out, qk, v, src, dst, distances, perm, offsets, src_perm, src_offsets, num_nodes, num_heads,
+                  scale, decay, reduce="sum", k=None, need_distances=False):
+    """Backward of :func:`attn_pool` -> (grad_qk, grad_k, grad_v, grad_distances, grad_log_scale).
+
+    Without ``k``: grad_qk has qk's shape (both the Q and the K halves) and grad_k is None.
+    With ``k``: grad_qk is dL/dQ (num_nodes, C, d) and grad_k is dL/dk (N_src, C, d).
+    grad_distances (the distance-decay term) is None unless ``need_distances``.
+    ``src_perm`` / ``src_offsets``: :func:`edge_sort` of ``src`` over the source rows.
+    """
+    lib = _require_cuda(grad_out, qk, v, src, dst, perm, offsets, src_perm, src_offsets)
+    qk, v, grad_out = _f32(qk, "QK"), _f32(v, "V"), _f32(grad_out, "grad_out")
+    if k is not None:
+        k = _f32(k, "K")
+    E, c_v, d_v = v.shape
+    N = int(num_nodes)
+    d = qk.shape[-1]
+    qrow = qk.shape[1] * d if k is not None else qk.shape[1] * d // 2
+    dev = qk.device
+    grad_qk = torch.empty_like(qk)
+    grad_k = torch.empty_like(k) if k is not None else None
+    grad_v = torch.empty_like(v)
+    grad_d = torch.zeros(E, dtype=torch.float32, device=dev) if need_distances and decay is not None else None
+    if E == 0:    # the forward is identically zero
+        return (torch.zeros_like(qk), None if k is None else torch.zeros_like(k), grad_v, grad_d,
+                torch.zeros((), dtype=torch.float32, device=dev))
+    part = torch.empty(N, dtype=torch.float32, device=dev)
+    scratch = torch.empty(max(2 * E * int(num_heads), 1), dtype=torch.float32, device=dev)
+    b = _lib.FeqAttnBwdArgs()
+    a = b.fwd
+    src, dst = src.contiguous(), dst.contiguous()
+    a.qk, a.v, a.src = qk.data_ptr(), v.data_ptr(), src.data_ptr()
+    if decay is not None:
+        distances = _f32(distances, "distances")
+        a.distances = distances.data_ptr()
+        a.decay_scale = float(decay)
+    a.perm, a.offsets = perm.data_ptr(), offsets.data_ptr()
+    a.num_nodes, a.num_edges = N, E
+    a.c_qk, a.d_qk, a.c_v, a.d_v, a.num_heads = qrow // d, d, c_v, d_v, int(num_heads)
+    a.scale = float(scale)
+    a.reduce = _lib.FEQ_REDUCE[reduce]
+    b.grad_out, b.dst = grad_out.data_ptr(), dst.data_ptr()
+    b.src_perm, b.src_offsets = src_perm.data_ptr(), src_offsets.data_ptr()
+    if k is not None:
+        a.k = k.data_ptr()
+        a.num_src_nodes = int(k.shape[0])
+        b.grad_q, b.ldq = grad_qk.data_ptr(), qrow
+        b.grad_k, b.ldk = grad_k.data_ptr(), qrow
+    else:
+        b.grad_q, b.ldq = grad_qk.data_ptr(), 2 * qrow
+        b.grad_k, b.ldk = grad_qk.data_ptr() + 4 * qrow, 2 * qrow
+    b.grad_v = grad_v.data_ptr()
+    if grad_d is not None:
+        b.grad_distances = grad_d.data_ptr()
+    b.grad_scale_partial = part.data_ptr()
+    b.edge_scratch = scratch.data_ptr()
+    rc = lib.feq_attn_pool_bwd(ctypes.byref(b), _stream(dev))
+    _lib.check(rc, "feq_attn_pool_bwd")
+    return grad_qk, grad_k, grad_v, grad_d, part.sum()
+
+
+def segment_softmax_bwd(weights, grad_weights, perm, offsets, num_nodes):
+    lib = _require_cuda(weights, grad_weights, perm, offsets)
+    weights, grad_weights = _f32(weights, "weights"), _f32(grad_weights, "grad_weights")
+    E, H = weights.shape
+    gl = torch.zeros_like(weights)
+    if E == 0:
+        return gl
+    rc = lib.feq_segment_softmax_bwd(_p(weights), _p(grad_weights), E, H, _p(perm), _p(offsets), int(num_nodes),
+                                     _p(gl), _stream(weights.device))
+    _lib.check(rc, "feq_segment_softmax_bwd")
+    return gl
+
+
+def edge_attention_weights_bwd(grad_weights, weights, Q, K, scale, decay, perm, offsets, num_nodes,
+                               need_distances=False):
+    """Backward of :func:`edge_attention_weights` -> (grad_Q, grad_K, grad_distances, grad_log_scale)."""
+    lib = _require_cuda(grad_weights, weights, Q, K, perm, offsets)
+    Q, K = _f32(Q, "Q"), _f32(K, "K")
+    weights, grad_weights = _f32(weights, "weights"), _f32(grad_weights, "grad_weights")
+    E, H, D = Q.shape
+    dev = Q.device
+    gQ, gK = torch.zeros_like(Q), torch.zeros_like(K)
+    gd = torch.zeros(E, dtype=torch.float32, device=dev) if need_distances and decay is not None else None
+    part = torch.zeros(E, dtype=torch.float32, device=dev)
+    if E == 0:
+        return gQ, gK, gd, part.sum()
+    gl = torch.empty(E, H, dtype=torch.float32, device=dev)
+    rc = lib.feq_edge_attention_weights_bwd(_p(Q), _p(K), E, H, D, float(scale),
+                                            float(decay) if decay is not None else 0.0, _p(perm), _p(offsets),
+                                            int(num_nodes), _p(weights), _p(grad_weights), _p(gl), _p(gQ), _p(gK),
+                                            _p(gd), _p(part), _stream(dev))
+    _lib.check(rc, "feq_edge_attention_weights_bwd")
+    return gQ, gK, gd, part.sum()
+
+
+def segment_pool_bwd(grad_out, rows, out, dst, perm, offsets, num_nodes, reduce="sum", weights=None):
+    """Backward of :func:`segment_pool` -> (grad_rows, grad_weights or None)."""
+    lib = _require_cuda(grad_out, rows, dst, perm, offsets, weights)
+    rows, grad_out = _f32(rows, "edge_features"), _f32(grad_out, "grad_out")
+    E = rows.shape[0]
+    grows = torch.zeros_like(rows)
+    gw = None
+    H = 0
+    wptr = None
+    if weights is not None:
+        weights = _f32(weights, "weights")
+        H = weights.shape[1]
+        wptr = _p(weights)
+        gw = torch.zeros_like(weights)
+    if E == 0:
+        return grows, gw
+    L = rows[0].numel()
+    ties = None
+    if reduce == "max":
+        out = _f32(out, "out")
+        ties = torch.empty(int(num_nodes), L, dtype=torch.float32, device=rows.device)
+    dst = dst.contiguous()
+    rc = lib.feq_segment_pool_bwd(_p(rows), L, wptr, H, _p(dst), _p(perm), _p(offsets), int(num_nodes), E,
+                                  _lib.FEQ_REDUCE[reduce], _p(out) if reduce == "max" else None, _p(grad_out),
+                                  _p(ties), _p(grows), _p(gw), None, _stream(rows.device))
+    _lib.check(rc, "feq_segment_pool_bwd")
+    return grows, gw
+
+
 def profile_enable(on: bool = True) -> None:
     """Start (or stop) recording CUDA-event stage timings inside the native library."""
     _lib.load().feq_profile_enable(1 if on else 0)

@@ -20,6 +20,7 @@ class Graph:
     dst: torch.Tensor
     num_nodes: int
     _csr: tuple | None = field(default=None, init=False, repr=False, compare=False)
+    _src_csr: tuple | None = field(default=None, init=False, repr=False, compare=False)
 
     def __post_init__(self) -> None:
         if self.src.dim() != 1:
@@ -78,4 +79,20 @@ class Graph:
         if bad_src is not None and bool(bad_src):
             raise ValueError("graph.src has indices outside [0, num_nodes)")
         self._csr = (key, perm, offsets)
+        return perm, offsets
+
+    def _num_src_rows(self) -> int:
+        return self.num_nodes
+
+    def src_segments(self):
+        """(perm, offsets): out-edges of source row m are perm[offsets[m]:offsets[m+1]], in edge-id
+        order (used by the backward of the attention, which reduces over each source's edges)."""
+        key = self._key()
+        if self._src_csr is not None and self._src_csr[0] == key:
+            return self._src_csr[1], self._src_csr[2]
+        from .cuda import ops
+
+        self.dst_segments()            # validates src / dst
+        perm, offsets, _ = ops.edge_sort(self.src, self._num_src_rows())
+        self._src_csr = (key, perm, offsets)
         return perm, offsets

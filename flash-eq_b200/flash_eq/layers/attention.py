@@ -11,14 +11,18 @@ projection in PyTorch; V = fused gather (x[src] + edge features) + edgewise
 linear in one native call; then one fused native kernel computes the logits
 from Q[dst] and K[src], the online softmax and the weighted pooling onto each
 destination, without materialising Q[dst], K[src] or the weighted edges.
+
+Under autograd every operator here has a native backward
+(``flash_eq.cuda.attention_autograd``): gradients reach Q/K (and through them the
+norm and projection), V (and the edgewise linear), log_scale and the distances.
 """
 from __future__ import annotations
 
 import torch
 import torch.nn as nn
 
+from ..cuda import attention_autograd as aag
 from ..cuda import ops
-from ..cuda.block_diagonal import forward_only
 from ..graph import Graph
 from ..partition import PartitionedGraph
 from ..representations import Repr
@@ -65,18 +69,15 @@ class EquivariantEdgeAttention(nn.Module):
     def _neighbor_softmax(self, logits: torch.Tensor, dst_indices: torch.Tensor, num_nodes: int) -> torch.Tensor:
         """Softmax of (E, H) logits over edges sharing a destination (attention.py:108-141)."""
         perm, offsets, status = ops.edge_sort(dst_indices, num_nodes)
-        return forward_only(lambda lg: ops.segment_softmax(lg.detach(), perm, offsets, num_nodes), logits)
+        if int(status.item()) != 0:
+            raise ValueError("dst_indices has indices outside [0, num_nodes)")
+        return aag.segment_softmax(logits, perm, offsets, num_nodes)
 
     def attention_weights(self, Q, K, graph: Graph, distances=None) -> torch.Tensor:
-        perm, offsets = graph.dst_segments()
+        """(E, H) softmax weights of the logits scale * <Q, K> (- d / decay); differentiable in
+        Q, K, distances and log_scale."""
         decay = self.distance_decay_scale if distances is not None else None
-        scale = self._scale_value()
-
-        def run(q, k, d):
-            return ops.edge_attention_weights(q.detach(), k.detach(), scale, None if d is None else d.detach(),
-                                              decay, perm, offsets, graph.num_nodes)
-
-        return forward_only(run, Q, K, distances)
+        return aag.edge_attention_weights(Q, K, distances, self.log_scale, graph, self._scale_value(), decay)
 
     def forward(self, Q, K, V, graph: Graph, distances: torch.Tensor | None = None) -> torch.Tensor:
         w = self.dropout(self.attention_weights(Q, K, graph, distances))
@@ -120,7 +121,6 @@ class EquivariantAttention(nn.Module):
         """(N, Cin, d_in) node features -> (N, Cout, d_out)."""
         mult = self.in_repr.mult
         qk = self.linear_qk(self.norm_qk(node_features))        # (N, 2C, d) node level
-        perm, offsets = graph.dst_segments()
         k_src = None
         x_src = node_features
         if isinstance(graph, PartitionedGraph):
@@ -134,18 +134,10 @@ class EquivariantAttention(nn.Module):
             decay = att.distance_decay_scale
             scale = att._scale_value()
             if k_src is not None:
-                def run_k(q, v, d, k):
-                    return ops.attn_pool(q.detach(), v.detach(), graph.src, None if d is None else d.detach(), perm,
-                                         offsets, graph.num_nodes, self.num_heads, scale, decay, self.pool.reduce,
-                                         k=k.detach())
-                return forward_only(run_k, qk[:, :mult].contiguous(), V, distances if decay is not None else None,
-                                    k_src)
-
-            def run(q, v, d):
-                return ops.attn_pool(q.detach(), v.detach(), graph.src, None if d is None else d.detach(), perm,
-                                     offsets, graph.num_nodes, self.num_heads, scale, decay, self.pool.reduce)
-
-            return forward_only(run, qk, V, distances if decay is not None else None)
+                return aag.attn_pool(qk[:, :mult].contiguous(), V, distances, att.log_scale, graph, self.num_heads,
+                                     scale, decay, self.pool.reduce, k=k_src)
+            return aag.attn_pool(qk, V, distances, att.log_scale, graph, self.num_heads, scale, decay,
+                                 self.pool.reduce)
         # max pooling or attention dropout: materialise per-edge weights
         E = graph.num_edges
         Qe = qk[:, :mult][graph.dst].reshape(E, self.num_heads, -1)

@@ -9,8 +9,7 @@ from __future__ import annotations
 import torch
 import torch.nn as nn
 
-from ..cuda import ops
-from ..cuda.block_diagonal import forward_only
+from ..cuda import attention_autograd as aag
 from ..graph import Graph
 
 _REDUCES = ("sum", "mean", "max")
@@ -18,14 +17,11 @@ _REDUCES = ("sum", "mean", "max")
 
 def pool_edges(edge_features: torch.Tensor, graph: Graph, reduce: str = "sum",
                weights: torch.Tensor | None = None) -> torch.Tensor:
-    """(E, C, d) -> (N, C, d); optional per-head weights (E, H) multiply each head's channels."""
-    perm, offsets = graph.dst_segments()
-
-    def run(x, w):
-        return ops.segment_pool(x.detach(), perm, offsets, graph.num_nodes, reduce,
-                                None if w is None else w.detach())
-
-    return forward_only(run, edge_features, weights)
+    """(E, C, d) -> (N, C, d); optional per-head weights (E, H) multiply each head's channels.
+    Differentiable in edge_features and weights (native backward)."""
+    if reduce not in _REDUCES:
+        raise ValueError(f"reduce must be one of {list(_REDUCES)}, got '{reduce}'")
+    return aag.segment_pool(edge_features, graph, reduce, weights)
 
 
 class GraphPooling(nn.Module):

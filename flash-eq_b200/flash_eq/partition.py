@@ -63,6 +63,9 @@ class PartitionedGraph(Graph):
     def _check_src(self):
         return ((self.src < 0) | (self.src >= self.num_src_nodes)).any() if self.num_edges else None
 
+    def _num_src_rows(self) -> int:
+        return self.num_src_nodes
+
     def to(self, device) -> "PartitionedGraph":
         mv = lambda t: None if t is None else t.to(device)
         return PartitionedGraph(src=self.src.to(device), dst=self.dst.to(device), num_nodes=self.num_nodes,
@@ -76,11 +79,19 @@ class PartitionedGraph(Graph):
         return coordinates[self.src_global] - coordinates[self.dst_global]
 
     def gather_nodes(self, owned: torch.Tensor) -> torch.Tensor:
-        """All ranks' owned rows (num_nodes, ...) -> (world_size * rows_per_rank, ...)."""
+        """All ranks' owned rows (num_nodes, ...) -> (world_size * rows_per_rank, ...).
+
+        Differentiable: the backward sums every rank's gradient of the gathered array
+        (a reduce-scatter) and keeps this rank's owned rows."""
         if owned.shape[0] != self.num_nodes:
             raise ValueError(f"expected {self.num_nodes} owned rows, got {owned.shape[0]}")
         if self.world_size == 1:
             return owned.contiguous()
+        if torch.is_grad_enabled() and owned.requires_grad:
+            return _GatherNodes.apply(owned, self)
+        return self._all_gather(owned.detach())
+
+    def _all_gather(self, owned: torch.Tensor) -> torch.Tensor:
         import torch.distributed as dist
 
         pad = owned.new_zeros((self.rows_per_rank,) + tuple(owned.shape[1:]))
@@ -92,6 +103,30 @@ class PartitionedGraph(Graph):
         out = owned.new_empty((self.world_size * self.rows_per_rank,) + tuple(owned.shape[1:]))
         dist.all_gather_into_tensor(out, pad, group=self.group)
         return out
+
+
+class _GatherNodes(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, owned, part):
+        ctx.part = part
+        return part._all_gather(owned)
+
+    @staticmethod
+    def backward(ctx, grad):
+        import torch.distributed as dist
+
+        part = ctx.part
+        rows = part.rows_per_rank
+        grad = grad.contiguous()
+        if dist.get_backend(part.group) == "gloo":      # host-side runs (tests): all-reduce, then slice
+            total = grad.clone()
+            dist.all_reduce(total, group=part.group)
+            mine = total[part.rank * rows: part.rank * rows + part.num_nodes]
+        else:
+            out = grad.new_empty((rows,) + tuple(grad.shape[1:]))
+            dist.reduce_scatter_tensor(out, grad, group=part.group)
+            mine = out[: part.num_nodes]
+        return mine.contiguous(), None
 
 
 def partition_graph(graph: Graph, world_size: int, rank: int, group=None) -> PartitionedGraph:

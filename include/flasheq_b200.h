@@ -59,7 +59,8 @@ enum feq_status_code {
  * Library
  * ------------------------------------------------------------------------ */
 const char *feq_status_string(int status);
-/* 2: FeqAttnArgs gained k / num_src_nodes (partitioned graphs). */
+/* 2: FeqAttnArgs gained k / num_src_nodes (partitioned graphs).
+ * 3: attention / pooling backward entry points. */
 int feq_abi_version(void);
 /* Human-readable last CUDA error seen by this thread (empty when none). */
 const char *feq_last_error(void);
@@ -305,6 +306,72 @@ typedef struct FeqAttnArgs {
 } FeqAttnArgs;
 
 int feq_attn_pool_fwd(const FeqAttnArgs *args, feq_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Backward of the attention and pooling operators.  The reference has no native
+ * backward for these: PyTorch autograd differentiates its scatter / gather ops
+ * (attention.py:92-167, pooling.py:21-57).  Softmax gradient
+ *   dl = w (dw - sum_seg w dw),   w = exp(l - max) / (sum_seg exp(. - max) + 1e-8),
+ * with the segment max held constant (its derivative is below 1e-8 relative).
+ * All reductions run over sorted segments in a fixed order: deterministic.
+ * ------------------------------------------------------------------------ */
+
+/* Backward of feq_attn_pool_fwd.  fwd holds the forward's arguments (fwd.out and
+ * fwd.status are not read / may be set).  Writes
+ *   grad_q (num_nodes rows, row stride ldq floats): dL/dQ of every destination row,
+ *   grad_k (num_src rows, stride ldk): dL/dK of every source row (num_src = num_nodes,
+ *          or fwd.num_src_nodes when fwd.k is set); for the unsplit QK layout pass
+ *          grad_q = grad_qk, grad_k = grad_qk + c_qk*d_qk, ldq = ldk = 2*c_qk*d_qk,
+ *   grad_v (E, c_v, d_v), grad_distances (E,) (the distance-decay term only; NULL to
+ *   skip), grad_scale_partial (num_nodes,): per destination node, the share of
+ *   dL/dlog(scale) (sum them for the scalar).
+ * src_perm / src_offsets: feq_edge_sort of src over num_src keys.  edge_scratch:
+ * 2 * E * num_heads floats. */
+typedef struct FeqAttnBwdArgs {
+    FeqAttnArgs fwd;
+    const float *grad_out;        /* (N, c_v, d_v) */
+    const int64_t *dst;           /* (E,) */
+    const int64_t *src_perm;      /* (E,) */
+    const int64_t *src_offsets;   /* (num_src + 1,) */
+    float *grad_q;
+    int64_t ldq;
+    float *grad_k;
+    int64_t ldk;
+    float *grad_v;
+    float *grad_distances;
+    float *grad_scale_partial;
+    float *edge_scratch;
+} FeqAttnBwdArgs;
+
+int feq_attn_pool_bwd(const FeqAttnBwdArgs *args, feq_stream_t stream);
+
+/* Backward of feq_segment_softmax: grad_logits = w * (grad_w - sum_seg w grad_w).
+ * grad_logits may alias grad_weights. */
+int feq_segment_softmax_bwd(const float *weights, const float *grad_weights, int64_t num_edges,
+                            int32_t num_heads, const int64_t *perm, const int64_t *offsets,
+                            int64_t num_nodes, float *grad_logits, feq_stream_t stream);
+
+/* Backward of feq_edge_attention_weights (weights = its output).  grad_logits (E, H)
+ * is written (scratch or result); grad_Q, grad_K (E, H, qk_dim), grad_distances (E,)
+ * (-sum_h dl / decay; 0 when decay_scale <= 0) and grad_scale_partial (E,) (per edge
+ * share of dL/dlog(scale)) may each be NULL. */
+int feq_edge_attention_weights_bwd(const float *Q, const float *K, int64_t num_edges, int32_t num_heads,
+                                   int32_t qk_dim, float scale, float decay_scale, const int64_t *perm,
+                                   const int64_t *offsets, int64_t num_nodes, const float *weights,
+                                   const float *grad_weights, float *grad_logits, float *grad_Q,
+                                   float *grad_K, float *grad_distances, float *grad_scale_partial,
+                                   feq_stream_t stream);
+
+/* Backward of feq_segment_pool.  dst (E,) is each edge's destination; perm / offsets
+ * the dst-sorted segments; out the forward's output and tie_scratch (N, row_len)
+ * floats, both needed for max only (the gradient of an output element is split
+ * evenly between the edges equal to it, like torch's scatter_reduce amax).
+ * grad_rows (E, row_len); grad_weights (E, H) when weights != NULL (may be NULL). */
+int feq_segment_pool_bwd(const float *edge_rows, int64_t row_len, const float *weights, int32_t num_heads,
+                         const int64_t *dst, const int64_t *perm, const int64_t *offsets, int64_t num_nodes,
+                         int64_t num_edges, int32_t reduce, const float *out, const float *grad_out,
+                         float *tie_scratch, float *grad_rows, float *grad_weights, int32_t *status,
+                         feq_stream_t stream);
 
 #ifdef __cplusplus
 }

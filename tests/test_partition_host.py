@@ -76,7 +76,13 @@ def _worker(rank, world, port, q):
         x = torch.randn(gr.num_nodes, 4, 9, generator=torch.Generator().manual_seed(5))
         p = partition_graph(gr, world, rank)
         full = p.gather_nodes(x[p.node_start:p.node_end].contiguous())
-        q.put((rank, bool(torch.equal(full[p.src], x[p.src_global])), full.shape[0] == world * p.rows_per_rank))
+        ok = bool(torch.equal(full[p.src], x[p.src_global])) and full.shape[0] == world * p.rows_per_rank
+        # backward: every rank's gradient of its gathered rows is summed onto the owner
+        coef = torch.randn(gr.num_edges, 4, 9, generator=torch.Generator().manual_seed(6))
+        xo = x[p.node_start:p.node_end].clone().requires_grad_()
+        (p.gather_nodes(xo)[p.src] * coef[p.edge_ids]).sum().backward()
+        want = torch.zeros_like(x).index_add_(0, gr.src, coef)[p.node_start:p.node_end]
+        q.put((rank, ok, bool(torch.allclose(xo.grad, want, atol=1e-5))))
     finally:
         dist.destroy_process_group()
 
@@ -92,4 +98,4 @@ def test_gather_nodes_two_gloo_ranks():
     for pr in procs:
         pr.join(timeout=60)
         assert pr.exitcode == 0
-    assert all(ok and shape for _, ok, shape in res)
+    assert all(ok and grad_ok for _, ok, grad_ok in res)
