@@ -86,13 +86,6 @@ int launch_unprep_rows(const float *H, int ld, const float *dist, const int64_t 
 int launch_bwd_transpose_rows(const __nv_bfloat16 *Xhi, const __nv_bfloat16 *Xlo, int ld, int ncols,
                               const int64_t *offsets, const int64_t *seg, int nb, const float *tval, int wmode,
                               int64_t pcols, __nv_bfloat16 *Yhi, __nv_bfloat16 *Ylo, cudaStream_t s);
-bool tc_mix_out_supported(const TcPlan &T, const ReprLayout &Lo);
-int64_t tc_mix_out_bq_elems(const TcPlan &T, int nb1);
-int launch_tc_chunk_b(const TcPlan &T, const __nv_bfloat16 *B, __nv_bfloat16 *Bq, int nb, cudaStream_t s);
-int launch_tc_mix_out(const TcPlan &T, const ReprLayout &Lo, const __nv_bfloat16 *A, int64_t E,
-                      const __nv_bfloat16 *Bq, int nb, const float *dirs, const float *dist, const float *tval,
-                      const int64_t *perm, const int4 *tiles, const int *num_tiles, int64_t max_tiles,
-                      float sh_scale, float *out, int32_t *status, cudaStream_t s);
 int launch_tc_gram(int split, const __nv_bfloat16 *Gt0, const __nv_bfloat16 *Gt0l, const __nv_bfloat16 *Gt1,
                    const __nv_bfloat16 *Gt1l, int64_t g_rows, const __nv_bfloat16 *At, const __nv_bfloat16 *Atl,
                    int64_t a_rows, int64_t p_cols, int n_blocks, const TcGramBlock *blk, int nb, const int64_t *seg,
@@ -300,6 +293,14 @@ static bool mix_args_ok(int64_t E, int Cin, int Cout, int nb) {
 // ---------------------------------------------------------------------------
 // Tensor-core plan: GEMM geometry per m-block and the row maps of A and H.
 // ---------------------------------------------------------------------------
+struct TcPlan {
+    TcGeom G;
+    int koff[kMaxBlocks], noff[kMaxBlocks], nvalid[kMaxBlocks];
+    int k_total, n_total;
+    int c_in, c_out;
+    int64_t b_total;
+    TcPosMap in_map, out_map;
+};
 
 // Offset of block m in m-first order when every irrep with l >= m contributes
 // (wigner.py:243-272), independent of whether the block takes part in the mix.
@@ -390,7 +391,7 @@ static int build_tc_plan(const MixLayout &M, const ReprLayout &Li, const ReprLay
 }
 
 struct TcBuffers {
-    __nv_bfloat16 *A_hi, *A_lo, *B_hi, *B_lo, *Bq;
+    __nv_bfloat16 *A_hi, *A_lo, *B_hi, *B_lo;
     float *H, *tval;
     int32_t *keys;
     int64_t *perm, *offsets;
@@ -401,22 +402,13 @@ struct TcBuffers {
     int64_t max_tiles;
 };
 
-// The bf16 mix of a small output representation runs the mix and the rotation back in
-// one kernel (feq_mixout.cu): no H matrix, a chunk-major weight copy instead.
-static bool use_mix_out(const FeqEdgewiseArgs *a, const TcPlan &T, const ReprLayout &Lo) {
-    return a->mix_mode == FEQ_MIX_BF16 && a->directions && !(reinterpret_cast<uintptr_t>(a->out) & 15) &&
-           tc_mix_out_supported(T, Lo);
-}
-
-static void carve_tc(WsCarver &w, int64_t E, int nb, const TcPlan &T, bool split, TcBuffers &b,
-                     bool mix_out = false) {
+static void carve_tc(WsCarver &w, int64_t E, int nb, const TcPlan &T, bool split, TcBuffers &b) {
     const int64_t E1 = std::max<int64_t>(E, 1);
     b.A_hi = (__nv_bfloat16 *)w.take(2 * (size_t)E1 * T.k_total);
     b.A_lo = split ? (__nv_bfloat16 *)w.take(2 * (size_t)E1 * T.k_total) : nullptr;
     b.B_hi = (__nv_bfloat16 *)w.take(2 * (size_t)T.b_total);
     b.B_lo = split ? (__nv_bfloat16 *)w.take(2 * (size_t)T.b_total) : nullptr;
-    b.Bq = mix_out ? (__nv_bfloat16 *)w.take(2 * (size_t)tc_mix_out_bq_elems(T, nb + 1)) : nullptr;
-    b.H = mix_out ? nullptr : (float *)w.take(4 * (size_t)E1 * T.n_total);
+    b.H = (float *)w.take(4 * (size_t)E1 * T.n_total);
     b.tval = (float *)w.take(4 * (size_t)E1);
     b.keys = (int32_t *)w.take(4 * (size_t)E1);
     b.perm = (int64_t *)w.take(8 * (size_t)E1);
@@ -460,15 +452,6 @@ static int run_edgewise_tc(const FeqEdgewiseArgs *a, const MixLayout &M, const R
                                  b.A_lo, b.tval, a->status, s);
     }
     if (rc != FEQ_OK) return rc;
-    if (b.Bq) {
-        {
-            ProfScope ps("relayout_table", s);
-            if ((rc = launch_tc_chunk_b(T, b.B_hi, b.Bq, a->num_bins, s)) != FEQ_OK) return rc;
-        }
-        ProfScope ps("tc_mix_out", s);
-        return launch_tc_mix_out(T, Lo, b.A_hi, E, b.Bq, a->num_bins, a->directions, a->distances, b.tval, b.perm,
-                                 b.tiles, b.num_tiles, b.max_tiles, a->sh_scale, a->out, a->status, s);
-    }
     for (int m = 0; m < T.G.n_blocks; m++) {
         const TcBlockGeom &g = T.G.g[m];
         const int64_t b_rows = (int64_t)(a->num_bins + 1) * g.npad;
@@ -918,13 +901,7 @@ size_t feq_edgewise_workspace_bytes(const FeqEdgewiseArgs *a) {
         WsCarver w{nullptr, 0, 0};
         TcBuffers b;
         carve_tc(w, a->num_edges, a->num_bins, T, a->mix_mode == FEQ_MIX_BF16X3, b);
-        size_t used = w.used;
-        if (a->mix_mode == FEQ_MIX_BF16 && tc_mix_out_supported(T, Lo)) {   // either path must fit
-            WsCarver w2{nullptr, 0, 0};
-            carve_tc(w2, a->num_edges, a->num_bins, T, false, b, true);
-            used = std::max(used, w2.used);
-        }
-        return used + 256;
+        return w.used + 256;
     }
     const int64_t E1 = std::max<int64_t>(a->num_edges, 1);
     WsCarver w{nullptr, 0, 0};
@@ -955,7 +932,7 @@ int feq_edgewise_fwd(const FeqEdgewiseArgs *a, void *workspace, size_t workspace
         if ((rc = build_tc_plan(M, Li, Lo, a->c_in, a->c_out, a->num_bins, &T)) != FEQ_OK) return rc;
         WsCarver w{(char *)workspace, 0, workspace_bytes};
         TcBuffers b;
-        carve_tc(w, E, a->num_bins, T, a->mix_mode == FEQ_MIX_BF16X3, b, use_mix_out(a, T, Lo));
+        carve_tc(w, E, a->num_bins, T, a->mix_mode == FEQ_MIX_BF16X3, b);
         if (!workspace || w.used > workspace_bytes) return FEQ_ERR_WORKSPACE;
         return run_edgewise_tc(a, M, Li, Lo, T, b, s);
     }

@@ -155,17 +155,6 @@ struct ProfScope {
     ~ProfScope() { prof_end(s); }
 };
 
-// Geometry of the tensor-core mix: per-block A column offsets (koff, padded to 64),
-// H column offsets (noff) and the position maps of both representations.
-struct TcPlan {
-    TcGeom G;
-    int koff[kMaxBlocks], noff[kMaxBlocks], nvalid[kMaxBlocks];
-    int k_total, n_total;
-    int c_in, c_out;
-    int64_t b_total;
-    TcPosMap in_map, out_map;
-};
-
 // Workspace carving: every region 256-byte aligned.
 // Per-block float offsets of the backward's per-bin reduction buffer.
 struct DbOff {

@@ -139,44 +139,6 @@ __device__ __forceinline__ void rot_irrep2(const float *__restrict__ tr, int lma
     for (int o = 0; o < N; o++) emit(o, h0[o], h1[o]);
 }
 
-// rot_irrep2 with the edge's scaled M block (WA<Lg>::wm) and azimuth trig cos / sin(m phi)
-// computed once per edge by the caller (kernels that rotate many channel groups of an edge).
-template <int Lg, bool kT, typename Get, typename Emit>
-__device__ __forceinline__ void rot_irrep2_pre(const float (&m)[WA<Lg>::kNnz], const float *cp, const float *sp,
-                                               Get get, Emit emit) {
-    constexpr int N = 2 * Lg + 1;
-    float g0[N], g1[N];
-#pragma unroll
-    for (int q = 0; q < N; q++) {
-        const float2 v = get(q);
-        g0[q] = v.x;
-        g1[q] = v.y;
-    }
-#pragma unroll
-    for (int mm = 1; mm <= Lg; mm++) {
-        const int a = Lg - mm, b = Lg + mm;
-        const float c = cp[mm], s = sp[mm];
-        float t0 = g0[a] * c - g0[b] * s, t1 = g0[a] * s + g0[b] * c;
-        g0[a] = t0; g0[b] = t1;
-        t0 = g1[a] * c - g1[b] * s; t1 = g1[a] * s + g1[b] * c;
-        g1[a] = t0; g1[b] = t1;
-    }
-    float h0[N], h1[N];
-    WA<Lg>::template wa<kT>(m, g0, h0);
-    WA<Lg>::template wa<kT>(m, g1, h1);
-#pragma unroll
-    for (int mm = 1; mm <= Lg; mm++) {
-        const int a = Lg - mm, b = Lg + mm;
-        const float c = cp[mm], s = sp[mm];
-        float t0 = h0[a] * c + h0[b] * s, t1 = h0[b] * c - h0[a] * s;
-        h0[a] = t0; h0[b] = t1;
-        t0 = h1[a] * c + h1[b] * s; t1 = h1[b] * c - h1[a] * s;
-        h1[a] = t0; h1[b] = t1;
-    }
-#pragma unroll
-    for (int o = 0; o < N; o++) emit(o, h0[o], h1[o]);
-}
-
 template <bool kT, typename Get, typename Emit>
 __device__ __forceinline__ void rot_irrep2_any(int l, const float *tr, int lmax, float sl, Get get, Emit emit) {
     switch (l) {

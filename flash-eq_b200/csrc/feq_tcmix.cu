@@ -571,22 +571,6 @@ static EncodeTiledFn encode_fn() {
     return fn;
 }
 
-// 2D bf16 tensor map (cols fastest), boxes of 64 columns x box_rows rows, 128-byte swizzle.
-int tc_make_map_box(CUtensorMap *m, const void *base, int64_t cols, int64_t rows, int box_rows) {
-    EncodeTiledFn fn = encode_fn();
-    if (!fn) return FEQ_ERR_CUDA;
-    if ((reinterpret_cast<uintptr_t>(base) & 15) || (cols * 2) % 16) return FEQ_ERR_INVALID_ARGUMENT;
-    if (box_rows < 8 || box_rows > 256 || box_rows % 8) return FEQ_ERR_INVALID_ARGUMENT;
-    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-    cuuint64_t strides[1] = {(cuuint64_t)(cols * 2)};
-    cuuint32_t box[2] = {(cuuint32_t)kTcK, (cuuint32_t)box_rows};
-    cuuint32_t estr[2] = {1, 1};
-    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box, estr,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    return r == CUDA_SUCCESS ? FEQ_OK : FEQ_ERR_INVALID_ARGUMENT;
-}
-
 // 2D bf16 K-major tensor (inner = cols), box 64 x 128, 128-byte swizzle, zero OOB fill.
 static int make_map(CUtensorMap *m, const void *base, int64_t cols, int64_t rows) {
     EncodeTiledFn fn = encode_fn();
@@ -601,9 +585,6 @@ static int make_map(CUtensorMap *m, const void *base, int64_t cols, int64_t rows
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? FEQ_OK : FEQ_ERR_INVALID_ARGUMENT;
 }
-
-// A matrices of the mix (rows of K bf16), boxes of 64 columns x 128 rows.
-int tc_make_map_a(CUtensorMap *m, const void *base, int64_t cols, int64_t rows) { return make_map(m, base, cols, rows); }
 
 int launch_tc_relayout_b(const float *T, __nv_bfloat16 *Bhi, __nv_bfloat16 *Blo, int nb1, int Cin, int Cout,
                          int wdim, const TcGeom &G, int64_t total, cudaStream_t s) {
