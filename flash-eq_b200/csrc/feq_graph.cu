@@ -268,6 +268,11 @@ attn_pool_kernel(const __grid_constant__ FeqAttnArgs a) {
 
     const bool split_k = a.k != nullptr;   // Q rows in qk, K rows in k (partitioned graphs)
     const int64_t nsrc = split_k ? a.num_src_nodes : a.num_nodes;
+    const float *kbase = split_k ? a.k : a.qk + qrow;
+    const int64_t k_ld = split_k ? qrow : 2 * (int64_t)qrow;
+    // per-thread dot products need 16-byte aligned K rows and head segments
+    const bool per_thread = hd <= 128 && (hd & 3) == 0 && (qrow & 3) == 0 &&
+                            ((reinterpret_cast<uintptr_t>(kbase) | reinterpret_cast<uintptr_t>(a.qk)) & 15) == 0;
     const float *qn = a.qk + n * (int64_t)(split_k ? qrow : 2 * qrow);
     for (int j = threadIdx.x; j < qrow; j += kAttnThreads) q_s[j] = __ldg(qn + j);
     for (int j = threadIdx.x; j < vrow; j += kAttnThreads) acc_s[j] = 0.0f;
@@ -291,22 +296,45 @@ attn_pool_kernel(const __grid_constant__ FeqAttnArgs a) {
             sid_s[threadIdx.x] = sidx;
         }
         __syncthreads();
-        // logits: one warp per (edge, head) pair
-        for (int pr = warp; pr < cn * H; pr += nwarps) {
-            const int k = pr / H, h = pr - k * H;
-            const int64_t sidx = sid_s[k];
-            float acc = 0.0f;
-            if (sidx >= 0) {
-                const float *kr = split_k ? a.k + sidx * (int64_t)qrow + h * hd
-                                          : a.qk + sidx * (int64_t)(2 * qrow) + qrow + h * hd;
-                const float *qr = q_s + h * hd;
-                for (int i = lane; i < hd; i += 32) acc = fmaf(qr[i], __ldg(kr + i), acc);
-            }
-            acc = warp_sum(acc);
-            if (lane == 0) {
-                float v = acc * a.scale;
+        if (per_thread) {
+            // logits, short heads: one thread per (edge, head) pair, float4 loads of the K row
+            for (int pr = threadIdx.x; pr < cn * H; pr += kAttnThreads) {
+                const int k = pr / H, h = pr - k * H;
+                const int64_t sidx = sid_s[k];
+                float acc0 = 0.0f, acc1 = 0.0f;
+                if (sidx >= 0) {
+                    const float4 *kr = reinterpret_cast<const float4 *>(kbase + sidx * k_ld + h * hd);
+                    const float4 *qr = reinterpret_cast<const float4 *>(q_s + h * hd);
+#pragma unroll 2
+                    for (int i = 0; i < hd / 4; i++) {
+                        const float4 kv = __ldg(kr + i), qv = qr[i];
+                        acc0 = fmaf(qv.x, kv.x, acc0);
+                        acc1 = fmaf(qv.y, kv.y, acc1);
+                        acc0 = fmaf(qv.z, kv.z, acc0);
+                        acc1 = fmaf(qv.w, kv.w, acc1);
+                    }
+                }
+                float v = (acc0 + acc1) * a.scale;
                 if (a.decay_scale > 0.0f && a.distances) v -= a.distances[eid_s[k]] / a.decay_scale;
                 lg_s[k][h] = v;
+            }
+        } else {
+            // logits, long heads: one warp per (edge, head) pair
+            for (int pr = warp; pr < cn * H; pr += nwarps) {
+                const int k = pr / H, h = pr - k * H;
+                const int64_t sidx = sid_s[k];
+                float acc = 0.0f;
+                if (sidx >= 0) {
+                    const float *kr = kbase + sidx * k_ld + h * hd;
+                    const float *qr = q_s + h * hd;
+                    for (int i = lane; i < hd; i += 32) acc = fmaf(qr[i], __ldg(kr + i), acc);
+                }
+                acc = warp_sum(acc);
+                if (lane == 0) {
+                    float v = acc * a.scale;
+                    if (a.decay_scale > 0.0f && a.distances) v -= a.distances[eid_s[k]] / a.decay_scale;
+                    lg_s[k][h] = v;
+                }
             }
         }
         __syncthreads();

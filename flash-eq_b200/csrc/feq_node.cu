@@ -1,0 +1,353 @@
+// feq_node.cu -- node-level operators of the transformer block (inference path).
+//
+// Reference behaviour replaced (PyTorch in the reference, one launch per elementary op):
+//   SeparableEquivariantLayerNorm   flash_eq/layers/norm.py:177-249
+//       scalars (l = 0 positions): LayerNorm over channels, (x - mu) / (sd + eps) * w + b
+//       higher degrees: one RMS over channels and positions, x * w[c] / sqrt(mean x^2 + eps)
+//   EquivariantLayerNorm            flash_eq/layers/norm.py:111-174
+//       norms[c, r] = sqrt(sum_{pos in irrep r} x^2 + eps); LayerNorm of norms over channels
+//       per irrep (weight / bias over channels, eps 1e-5); x * ln / (norms + eps)
+//   RepNorm                         flash_eq/layers/norm.py:19-64
+//   EquivariantGating (the gate)    flash_eq/layers/gating.py:17-76: x * sigmoid(z)[c, irrep]
+//
+// One warp per node: the node's row (C x d floats) is staged in shared memory once, the
+// per-node statistics are warp reductions, and the output row is written coalesced.
+// All four are memory-bound: one read and one write of the row (plus z / norms).
+#include <cuda_runtime.h>
+#include <math.h>
+#include <string.h>
+
+#include "feq_internal.cuh"
+
+namespace feq {
+namespace {
+
+constexpr int kNodeWarps = 4;
+constexpr int kNodeMaxIrreps = 32;
+constexpr int kNodeMaxScalars = 16;
+
+__device__ __forceinline__ float nwsum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+struct NodeRepr {
+    int C, d, n_irreps;
+    int8_t irr_l[kNodeMaxIrreps];
+    int16_t irr_off[kNodeMaxIrreps];
+    int8_t pos_irr[kMaxDim];          // position -> irrep
+};
+
+struct SepLnArgs {
+    NodeRepr R;
+    int nscalar, n_higher;            // scalar positions, higher positions
+    int16_t scalar_pos[kNodeMaxScalars];
+    int8_t scalar_idx[kMaxDim];       // position -> scalar index, -1 for higher positions
+    const float *x, *w_s, *b_s, *w_h;  // w_s, b_s: (C, nscalar); w_h: (C)
+    float eps;
+    float *out;
+    int64_t N;
+};
+
+__device__ __forceinline__ void stage_row(float *row, const float *src, int n, int lane) {
+    if ((n & 3) == 0 && ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(row)) & 15) == 0) {
+        const float4 *s4 = reinterpret_cast<const float4 *>(src);
+        float4 *r4 = reinterpret_cast<float4 *>(row);
+        for (int i = lane; i < n / 4; i += 32) r4[i] = __ldg(s4 + i);
+    } else {
+        for (int i = lane; i < n; i += 32) row[i] = __ldg(src + i);
+    }
+    __syncwarp();
+}
+
+__global__ void __launch_bounds__(kNodeWarps * 32) sep_layernorm_kernel(const __grid_constant__ SepLnArgs a) {
+    extern __shared__ float nsm[];
+    const int C = a.R.C, d = a.R.d, n = C * d;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float *row = nsm + (size_t)warp * n;
+    __shared__ float mu_s[kNodeWarps][kNodeMaxScalars], inv_s[kNodeWarps][kNodeMaxScalars], rms_s[kNodeWarps];
+    for (int64_t node = (int64_t)blockIdx.x * kNodeWarps + warp; node < a.N; node += (int64_t)gridDim.x * kNodeWarps) {
+        stage_row(row, a.x + node * n, n, lane);
+        for (int s = 0; s < a.nscalar; s++) {
+            const int p = a.scalar_pos[s];
+            float sum = 0.0f;
+            for (int c = lane; c < C; c += 32) sum += row[c * d + p];
+            const float mu = nwsum(sum) / (float)C;
+            float sq = 0.0f;
+            for (int c = lane; c < C; c += 32) {
+                const float t = row[c * d + p] - mu;
+                sq = fmaf(t, t, sq);
+            }
+            const float sd = sqrtf(nwsum(sq) / (float)C);
+            if (lane == 0) {
+                mu_s[warp][s] = mu;
+                inv_s[warp][s] = sd + a.eps;
+            }
+        }
+        if (a.n_higher > 0) {
+            float sq = 0.0f;
+            for (int j = lane; j < n; j += 32)
+                if (a.scalar_idx[j % d] < 0) sq = fmaf(row[j], row[j], sq);
+            sq = nwsum(sq);
+            if (lane == 0) rms_s[warp] = sqrtf(sq / (float)(C * a.n_higher) + a.eps);
+        }
+        __syncwarp();
+        float *orow = a.out + node * n;
+        for (int j = lane; j < n; j += 32) {
+            const int c = j / d, p = j - c * d;
+            float v = row[j];
+            const int s = a.scalar_idx[p];
+            if (s >= 0) {
+                v = (v - mu_s[warp][s]) / inv_s[warp][s] * a.w_s[c * a.nscalar + s] + a.b_s[c * a.nscalar + s];
+            } else {
+                v = v * (a.w_h[c] / rms_s[warp]);
+            }
+            orow[j] = v;
+        }
+        __syncwarp();
+    }
+}
+
+struct EqLnArgs {
+    NodeRepr R;
+    const float *x, *ln_w, *ln_b;   // ln_w / ln_b: (C) or NULL (mult 1: no LayerNorm)
+    float ln_eps, rn_eps, eps;
+    float *out;
+    int64_t N;
+};
+
+// norms of this warp's node row into nrm[c * n_irreps + r]
+__device__ __forceinline__ void row_norms(const NodeRepr &R, const float *row, float rn_eps, float *nrm, int lane) {
+    const int C = R.C, d = R.d;
+    for (int i = lane; i < C * R.n_irreps; i += 32) {
+        const int c = i / R.n_irreps, r = i - c * R.n_irreps;
+        const int off = R.irr_off[r], k = 2 * R.irr_l[r] + 1;
+        float s = 0.0f;
+        for (int m = 0; m < k; m++) {
+            const float v = row[c * d + off + m];
+            s = fmaf(v, v, s);
+        }
+        nrm[i] = sqrtf(s + rn_eps);
+    }
+    __syncwarp();
+}
+
+__global__ void __launch_bounds__(kNodeWarps * 32) equi_layernorm_kernel(const __grid_constant__ EqLnArgs a) {
+    extern __shared__ float nsm[];
+    const int C = a.R.C, d = a.R.d, n = C * d, nr = a.R.n_irreps;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float *row = nsm + (size_t)warp * (n + C * nr);
+    float *nrm = row + n;               // norms, then the rescaling factors
+    for (int64_t node = (int64_t)blockIdx.x * kNodeWarps + warp; node < a.N; node += (int64_t)gridDim.x * kNodeWarps) {
+        stage_row(row, a.x + node * n, n, lane);
+        row_norms(a.R, row, a.rn_eps, nrm, lane);
+        for (int r = 0; r < nr; r++) {
+            if (a.ln_w) {
+                float s = 0.0f;
+                for (int c = lane; c < C; c += 32) s += nrm[c * nr + r];
+                const float mu = nwsum(s) / (float)C;
+                float q = 0.0f;
+                for (int c = lane; c < C; c += 32) {
+                    const float t = nrm[c * nr + r] - mu;
+                    q = fmaf(t, t, q);
+                }
+                const float rstd = rsqrtf(nwsum(q) / (float)C + a.ln_eps);
+                for (int c = lane; c < C; c += 32) {
+                    const float v = nrm[c * nr + r];
+                    const float ln = (v - mu) * rstd * a.ln_w[c] + a.ln_b[c];
+                    nrm[c * nr + r] = ln / (v + a.eps);
+                }
+            } else {
+                for (int c = lane; c < C; c += 32) nrm[c * nr + r] = 1.0f / (nrm[c * nr + r] + a.eps);
+            }
+        }
+        __syncwarp();
+        float *orow = a.out + node * n;
+        for (int j = lane; j < n; j += 32) {
+            const int c = j / d, p = j - c * d;
+            orow[j] = row[j] * nrm[c * nr + a.R.pos_irr[p]];
+        }
+        __syncwarp();
+    }
+}
+
+struct RepNormArgs {
+    NodeRepr R;
+    const float *x;
+    float eps;
+    float *norms;    // (N, C, n_irreps)
+    const float *z;  // gate: (N, C * n_irreps) pre-activation
+    float *out;      // gate: (N, C, d)
+    int64_t N;
+};
+
+__global__ void __launch_bounds__(kNodeWarps * 32) rep_norm_kernel(const __grid_constant__ RepNormArgs a) {
+    extern __shared__ float nsm[];
+    const int C = a.R.C, d = a.R.d, n = C * d, nr = a.R.n_irreps;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float *row = nsm + (size_t)warp * n;
+    for (int64_t node = (int64_t)blockIdx.x * kNodeWarps + warp; node < a.N; node += (int64_t)gridDim.x * kNodeWarps) {
+        stage_row(row, a.x + node * n, n, lane);
+        float *o = a.norms + node * (int64_t)C * nr;
+        for (int i = lane; i < C * nr; i += 32) {
+            const int c = i / nr, r = i - c * nr;
+            const int off = a.R.irr_off[r], k = 2 * a.R.irr_l[r] + 1;
+            float s = 0.0f;
+            for (int m = 0; m < k; m++) {
+                const float v = row[c * d + off + m];
+                s = fmaf(v, v, s);
+            }
+            o[i] = sqrtf(s + a.eps);
+        }
+        __syncwarp();
+    }
+}
+
+// out[n, c, p] = x[n, c, p] * sigmoid(z[n, c * n_irreps + irrep(p)]), elementwise over the rows.
+__global__ void gate_kernel(const __grid_constant__ RepNormArgs a) {
+    const int C = a.R.C, d = a.R.d, nr = a.R.n_irreps;
+    const int64_t total = a.N * C * d;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t node_c = i / d;
+        const int p = (int)(i - node_c * d);
+        const float zz = __ldg(a.z + node_c * nr + a.R.pos_irr[p]);
+        a.out[i] = a.x[i] * (1.0f / (1.0f + expf(-zz)));
+    }
+}
+
+int fill_node_repr(const int32_t *lvals, int32_t n, int32_t C, NodeRepr *R) {
+    if (!lvals || n < 1 || n > kNodeMaxIrreps || C < 1) return FEQ_ERR_INVALID_ARGUMENT;
+    memset(R, 0, sizeof(*R));
+    int off = 0;
+    for (int r = 0; r < n; r++) {
+        if (lvals[r] < 0 || lvals[r] > kMaxL) return FEQ_ERR_INVALID_ARGUMENT;
+        R->irr_l[r] = (int8_t)lvals[r];
+        R->irr_off[r] = (int16_t)off;
+        for (int m = 0; m < 2 * lvals[r] + 1; m++) {
+            if (off + m >= kMaxDim) return FEQ_ERR_UNSUPPORTED;
+            R->pos_irr[off + m] = (int8_t)r;
+        }
+        off += 2 * lvals[r] + 1;
+    }
+    R->C = C;
+    R->d = off;
+    R->n_irreps = n;
+    return FEQ_OK;
+}
+
+int node_grid(int64_t N) { return (int)min64((N + kNodeWarps - 1) / kNodeWarps, 148 * 16); }
+
+int set_smem(const void *fn, size_t smem) {
+    if (smem > 200 * 1024) return FEQ_ERR_UNSUPPORTED;
+    if (smem > 48 * 1024)
+        FEQ_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    return FEQ_OK;
+}
+
+}  // namespace
+}  // namespace feq
+
+using namespace feq;
+
+extern "C" {
+
+int feq_node_sep_layernorm(const float *x, int64_t num_nodes, int32_t C, const int32_t *lvals, int32_t n_lvals,
+                           const float *w_scalar, const float *b_scalar, const float *w_higher, float eps, float *out,
+                           feq_stream_t stream) {
+    SepLnArgs a;
+    memset(&a, 0, sizeof(a));
+    int rc = fill_node_repr(lvals, n_lvals, C, &a.R);
+    if (rc != FEQ_OK) return rc;
+    if (num_nodes < 0) return FEQ_ERR_INVALID_ARGUMENT;
+    if (num_nodes == 0) return FEQ_OK;
+    memset(a.scalar_idx, -1, sizeof(a.scalar_idx));
+    for (int r = 0; r < n_lvals; r++) {
+        if (lvals[r] == 0) {
+            if (a.nscalar >= kNodeMaxScalars) return FEQ_ERR_UNSUPPORTED;
+            a.scalar_idx[a.R.irr_off[r]] = (int8_t)a.nscalar;
+            a.scalar_pos[a.nscalar++] = a.R.irr_off[r];
+        }
+    }
+    a.n_higher = a.R.d - a.nscalar;
+    if (!x || !out || (a.nscalar > 0 && (!w_scalar || !b_scalar)) || (a.n_higher > 0 && !w_higher))
+        return FEQ_ERR_INVALID_ARGUMENT;
+    a.x = x;
+    a.w_s = w_scalar;
+    a.b_s = b_scalar;
+    a.w_h = w_higher;
+    a.eps = eps;
+    a.out = out;
+    a.N = num_nodes;
+    const size_t smem = sizeof(float) * kNodeWarps * (size_t)C * a.R.d;
+    if ((rc = set_smem((const void *)sep_layernorm_kernel, smem)) != FEQ_OK) return rc;
+    sep_layernorm_kernel<<<node_grid(num_nodes), kNodeWarps * 32, smem, (cudaStream_t)stream>>>(a);
+    FEQ_LAUNCH_CHECK();
+    return FEQ_OK;
+}
+
+int feq_node_layernorm(const float *x, int64_t num_nodes, int32_t C, const int32_t *lvals, int32_t n_lvals,
+                       const float *ln_weight, const float *ln_bias, float ln_eps, float rep_eps, float eps, float *out,
+                       feq_stream_t stream) {
+    EqLnArgs a;
+    memset(&a, 0, sizeof(a));
+    int rc = fill_node_repr(lvals, n_lvals, C, &a.R);
+    if (rc != FEQ_OK) return rc;
+    if (num_nodes < 0 || (ln_weight == nullptr) != (ln_bias == nullptr)) return FEQ_ERR_INVALID_ARGUMENT;
+    if (num_nodes == 0) return FEQ_OK;
+    if (!x || !out) return FEQ_ERR_INVALID_ARGUMENT;
+    a.x = x;
+    a.ln_w = ln_weight;
+    a.ln_b = ln_bias;
+    a.ln_eps = ln_eps;
+    a.rn_eps = rep_eps;
+    a.eps = eps;
+    a.out = out;
+    a.N = num_nodes;
+    const size_t smem = sizeof(float) * kNodeWarps * ((size_t)C * a.R.d + (size_t)C * n_lvals);
+    if ((rc = set_smem((const void *)equi_layernorm_kernel, smem)) != FEQ_OK) return rc;
+    equi_layernorm_kernel<<<node_grid(num_nodes), kNodeWarps * 32, smem, (cudaStream_t)stream>>>(a);
+    FEQ_LAUNCH_CHECK();
+    return FEQ_OK;
+}
+
+int feq_node_rep_norm(const float *x, int64_t num_nodes, int32_t C, const int32_t *lvals, int32_t n_lvals, float eps,
+                      float *norms, feq_stream_t stream) {
+    RepNormArgs a;
+    memset(&a, 0, sizeof(a));
+    int rc = fill_node_repr(lvals, n_lvals, C, &a.R);
+    if (rc != FEQ_OK) return rc;
+    if (num_nodes < 0) return FEQ_ERR_INVALID_ARGUMENT;
+    if (num_nodes == 0) return FEQ_OK;
+    if (!x || !norms) return FEQ_ERR_INVALID_ARGUMENT;
+    a.x = x;
+    a.eps = eps;
+    a.norms = norms;
+    a.N = num_nodes;
+    const size_t smem = sizeof(float) * kNodeWarps * (size_t)C * a.R.d;
+    if ((rc = set_smem((const void *)rep_norm_kernel, smem)) != FEQ_OK) return rc;
+    rep_norm_kernel<<<node_grid(num_nodes), kNodeWarps * 32, smem, (cudaStream_t)stream>>>(a);
+    FEQ_LAUNCH_CHECK();
+    return FEQ_OK;
+}
+
+int feq_node_gate(const float *x, const float *z, int64_t num_nodes, int32_t C, const int32_t *lvals, int32_t n_lvals,
+                  float *out, feq_stream_t stream) {
+    RepNormArgs a;
+    memset(&a, 0, sizeof(a));
+    int rc = fill_node_repr(lvals, n_lvals, C, &a.R);
+    if (rc != FEQ_OK) return rc;
+    if (num_nodes < 0) return FEQ_ERR_INVALID_ARGUMENT;
+    if (num_nodes == 0) return FEQ_OK;
+    if (!x || !z || !out) return FEQ_ERR_INVALID_ARGUMENT;
+    a.x = x;
+    a.z = z;
+    a.out = out;
+    a.N = num_nodes;
+    const int64_t total = num_nodes * C * a.R.d;
+    gate_kernel<<<(unsigned)min64((total + 255) / 256, 148 * 32), 256, 0, (cudaStream_t)stream>>>(a);
+    FEQ_LAUNCH_CHECK();
+    return FEQ_OK;
+}
+
+}  // extern "C"

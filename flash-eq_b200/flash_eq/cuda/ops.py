@@ -458,6 +458,70 @@ def segment_pool_bwd(grad_out, rows, out, dst, perm, offsets, num_nodes, reduce=
     return grows, gw
 
 
+# ---------------------------------------------------------------------------
+# Node-level operators (forward)
+# ---------------------------------------------------------------------------
+def _node_rows(x, what):
+    x = _f32(x, what)
+    if x.dim() < 2:
+        raise ValueError(f"{what} must have shape (..., C, d)")
+    return x.reshape(-1, x.shape[-2], x.shape[-1])
+
+
+def node_sep_layernorm(x, lvals, w_scalar, b_scalar, w_higher, eps):
+    """SeparableEquivariantLayerNorm forward (see feq_node_sep_layernorm)."""
+    lib = _require_cuda(x, w_scalar, b_scalar, w_higher)
+    rows = _node_rows(x, "features")
+    out = torch.empty_like(rows)
+    arr, n = _lib.i32_array(lvals)
+    c = lambda t: None if t is None else _f32(t, "weight")
+    ws, bs, wh = c(w_scalar), c(b_scalar), c(w_higher)
+    rc = lib.feq_node_sep_layernorm(_p(rows), rows.shape[0], rows.shape[1], arr, n, _p(ws), _p(bs), _p(wh),
+                                    float(eps), _p(out), _stream(rows.device))
+    _lib.check(rc, "feq_node_sep_layernorm")
+    return out.view(x.shape)
+
+
+def node_layernorm(x, lvals, ln_weight, ln_bias, ln_eps, rep_eps, eps):
+    """EquivariantLayerNorm forward (see feq_node_layernorm); ln_weight None for mult 1."""
+    lib = _require_cuda(x, ln_weight, ln_bias)
+    rows = _node_rows(x, "features")
+    out = torch.empty_like(rows)
+    arr, n = _lib.i32_array(lvals)
+    lw = None if ln_weight is None else _f32(ln_weight, "weight")
+    lb = None if ln_bias is None else _f32(ln_bias, "bias")
+    rc = lib.feq_node_layernorm(_p(rows), rows.shape[0], rows.shape[1], arr, n, _p(lw), _p(lb), float(ln_eps),
+                                float(rep_eps), float(eps), _p(out), _stream(rows.device))
+    _lib.check(rc, "feq_node_layernorm")
+    return out.view(x.shape)
+
+
+def node_rep_norm(x, lvals, eps):
+    """RepNorm forward: (..., C, d) -> (..., C, n_irreps)."""
+    lib = _require_cuda(x)
+    rows = _node_rows(x, "features")
+    arr, n = _lib.i32_array(lvals)
+    norms = torch.empty(rows.shape[0], rows.shape[1], n, dtype=torch.float32, device=rows.device)
+    rc = lib.feq_node_rep_norm(_p(rows), rows.shape[0], rows.shape[1], arr, n, float(eps), _p(norms),
+                               _stream(rows.device))
+    _lib.check(rc, "feq_node_rep_norm")
+    return norms.view(*x.shape[:-1], n)
+
+
+def node_gate(x, z, lvals):
+    """x * sigmoid(z)[..., c, irrep(position)]; z (..., C * n_irreps)."""
+    lib = _require_cuda(x, z)
+    rows = _node_rows(x, "features")
+    z = _f32(z, "gate")
+    out = torch.empty_like(rows)
+    arr, n = _lib.i32_array(lvals)
+    if z.numel() != rows.shape[0] * rows.shape[1] * n:
+        raise ValueError("gate pre-activation has the wrong size")
+    rc = lib.feq_node_gate(_p(rows), _p(z), rows.shape[0], rows.shape[1], arr, n, _p(out), _stream(rows.device))
+    _lib.check(rc, "feq_node_gate")
+    return out.view(x.shape)
+
+
 def profile_enable(on: bool = True) -> None:
     """Start (or stop) recording CUDA-event stage timings inside the native library."""
     _lib.load().feq_profile_enable(1 if on else 0)

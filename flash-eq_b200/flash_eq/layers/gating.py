@@ -1,4 +1,8 @@
-"""Norm-based gating (flash_eq/layers/gating.py:17-76 in the reference); node-level PyTorch."""
+"""Norm-based gating (flash_eq/layers/gating.py:17-76 in the reference).
+
+Without autograd tracking on CUDA float32 inputs the irrep norms and the sigmoid gate are
+native kernels (csrc/feq_node.cu); the (C * nreps)^2 linear between them is a library GEMM.
+"""
 from __future__ import annotations
 
 import torch
@@ -6,7 +10,7 @@ import torch.nn as nn
 
 from ..representations import Repr
 from ..utils import init_linear_weights
-from .norm import RepNorm
+from .norm import RepNorm, native_node_ok
 
 
 class EquivariantGating(nn.Module):
@@ -26,5 +30,10 @@ class EquivariantGating(nn.Module):
     def forward(self, st: torch.Tensor) -> torch.Tensor:
         norms = self.norm(st)
         *b, _, _ = norms.size()
+        if native_node_ok(st, self.linear.weight, self.linear.bias):
+            from ..cuda import ops
+
+            # norms and the gate run natively; the dense (C * nreps)^2 linear stays a library GEMM
+            return ops.node_gate(st, self.linear(norms.flatten(-2, -1)), self.norm._lvals)
         g = self.activation(self.linear(norms.flatten(-2, -1)).view(*b, *self.outdims))
         return st * g[..., self.ix]

@@ -129,16 +129,25 @@ class EquivariantLinear(nn.Module):
         self.expanddims = (1, out_repr.mult, in_repr.dim())
         self.outdims = (in_repr.nreps(), out_repr.mult, in_repr.dim())
         nscalar, self.scalar_locs = in_repr.find_scalar()
+        self.register_buffer("_scalar_ix", torch.tensor(self.scalar_locs, dtype=torch.long), persistent=False)
         self.bias: nn.Parameter | None
         self.bias = nn.Parameter(torch.zeros(out_repr.mult, nscalar)) if (nscalar > 0 and bias) else None
         self.activation = activation if activation is not None else nn.Identity()
 
     def forward(self, f: torch.Tensor) -> torch.Tensor:
-        *b, _, _ = f.shape
-        out = (self.weight @ f).view(*b, *self.outdims)
-        ix = self.indices.expand(*b, *self.expanddims)
-        out = out.gather(dim=-3, index=ix).squeeze(-3)
+        """out[..., co, p] = sum_ci W_{irrep(p)}[co, ci] f[..., ci, p] (+ bias on l = 0 positions).
+
+        The reference forms (weight @ f) for every irrep at every position and gathers the
+        matching one (linear.py:230-268).  Here the rows of each position's own irrep are
+        gathered first and one batched GEMM over positions does only the needed products:
+        the same sums, 1 / nreps of the FLOPs, no (nreps x) intermediate."""
+        *b, cin, d = f.shape
+        x = f.reshape(-1, cin, d)
+        nreps = self.outdims[0]
+        cout = self.expanddims[1]
+        w = self.weight.view(nreps, cout, cin).index_select(0, self.indices)    # (d, Cout, Cin)
+        y = torch.bmm(w, x.permute(2, 1, 0))                                     # (d, Cout, N)
         if self.bias is not None:
-            out = out.clone()
-            out[..., self.scalar_locs] = self.activation(out[..., self.scalar_locs] + self.bias).to(out.dtype)
-        return out
+            ys = y.index_select(0, self._scalar_ix) + self.bias.t().unsqueeze(-1)
+            y = y.index_copy(0, self._scalar_ix, self.activation(ys).to(y.dtype))
+        return y.permute(2, 1, 0).reshape(*b, cout, d)

@@ -1,9 +1,11 @@
 """Equivariant normalisation (flash_eq/layers/norm.py in the reference, :19-249).
 
-Node-level work; kept in PyTorch with the reference's parameter names:
-``RepNorm`` (per-irrep norms), ``EquivariantLayerNorm`` (LayerNorm over the
-multiplicity of the irrep norms), ``SeparableEquivariantLayerNorm`` (LayerNorm
-over channels for l = 0, one shared RMS for all l > 0 with a per-channel scale).
+Node-level work with the reference's parameter names: ``RepNorm`` (per-irrep norms),
+``EquivariantLayerNorm`` (LayerNorm over the multiplicity of the irrep norms),
+``SeparableEquivariantLayerNorm`` (LayerNorm over channels for l = 0, one shared RMS for
+all l > 0 with a per-channel scale).  On CUDA float32 inputs with autograd not tracking,
+each runs as one native kernel (csrc/feq_node.cu, one warp per node); under autograd the
+PyTorch formulation below (the reference's) is used so that gradients flow.
 """
 from __future__ import annotations
 
@@ -14,6 +16,15 @@ from ..representations import Repr
 from ..utils import get_epsilon
 
 
+def native_node_ok(x: torch.Tensor, *params) -> bool:
+    """True when the native node kernel may run: CUDA float32 and nothing for autograd to track."""
+    if not (torch.is_tensor(x) and x.is_cuda and x.dtype == torch.float32 and x.dim() >= 2):
+        return False
+    if torch.is_grad_enabled() and (x.requires_grad or any(p is not None and p.requires_grad for p in params)):
+        return False
+    return True
+
+
 class RepNorm(nn.Module):
     """Norm of every irrep component: (..., dim) -> (..., nreps)."""
 
@@ -21,10 +32,15 @@ class RepNorm(nn.Module):
         super().__init__()
         self.num_reps = repr.nreps()
         self._epsilon = epsilon
+        self._lvals = tuple(repr.lvals.tolist())
         self.register_buffer("indices", torch.tensor(repr.indices(), dtype=torch.long))
 
     def forward(self, st: torch.Tensor) -> torch.Tensor:
         eps = self._epsilon if self._epsilon is not None else get_epsilon(st.dtype)
+        if native_node_ok(st) and st.shape[-1] == len(self.indices):
+            from ..cuda import ops
+
+            return ops.node_rep_norm(st, self._lvals, eps)
         sq = st * st
         out = torch.zeros(*sq.shape[:-1], self.num_reps, device=sq.device, dtype=sq.dtype)
         out.scatter_add_(-1, self.indices.expand(sq.shape), sq)
@@ -71,9 +87,17 @@ class EquivariantLayerNorm(nn.Module):
         self.lnorm = nn.LayerNorm(repr.mult) if repr.mult > 1 else None
         self._epsilon = epsilon
         self.register_buffer("ix", torch.tensor(repr.indices(), dtype=torch.long))
+        self._lvals = tuple(repr.lvals.tolist())
 
     def forward(self, f: torch.Tensor) -> torch.Tensor:
         eps = self._epsilon if self._epsilon is not None else get_epsilon(f.dtype)
+        ln = self.lnorm
+        if native_node_ok(f, *(() if ln is None else (ln.weight, ln.bias))) and f.shape[-2] == self.mult:
+            from ..cuda import ops
+
+            rep_eps = self.norm._epsilon if self.norm._epsilon is not None else get_epsilon(f.dtype)
+            return ops.node_layernorm(f, self._lvals, None if ln is None else ln.weight,
+                                      None if ln is None else ln.bias, 0.0 if ln is None else ln.eps, rep_eps, eps)
         norms = self.norm(f)
         if self.lnorm is None:
             return f * (1.0 / (norms + eps))[..., self.ix]
@@ -91,6 +115,9 @@ class SeparableEquivariantLayerNorm(nn.Module):
         mask = torch.ones(repr.dim(), dtype=torch.bool)
         mask[self.scalar_locs] = False
         self.register_buffer("higher_mask", mask)
+        # device index vectors (not in the state dict): indexing with them needs no host sync
+        self.register_buffer("_scalar_ix", torch.tensor(self.scalar_locs, dtype=torch.long), persistent=False)
+        self.register_buffer("_higher_ix", torch.nonzero(mask).flatten(), persistent=False)
         self.nhigher = repr.nreps() - self.nscalar
         if self.nscalar > 0:
             self.scalar_norm = _ChannelLayerNorm(repr.mult, self.nscalar, epsilon)
@@ -98,11 +125,21 @@ class SeparableEquivariantLayerNorm(nn.Module):
             self.higher_norm = _EquivariantRMSNorm(repr.mult, epsilon)
 
     def forward(self, f: torch.Tensor) -> torch.Tensor:
+        sn = self.scalar_norm if self.nscalar > 0 else None
+        hn = self.higher_norm if self.nhigher > 0 else None
+        params = (() if sn is None else (sn.weight, sn.bias)) + (() if hn is None else (hn.weight,))
+        if native_node_ok(f, *params) and f.shape[-2] == self.repr.mult:
+            from ..cuda import ops
+
+            eps_of = lambda m: m._epsilon if m._epsilon is not None else get_epsilon(f.dtype)
+            eps = eps_of(sn) if sn is not None else eps_of(hn)
+            return ops.node_sep_layernorm(f, tuple(self.repr.lvals.tolist()), None if sn is None else sn.weight,
+                                          None if sn is None else sn.bias, None if hn is None else hn.weight, eps)
         out = f.clone()
         if self.nscalar > 0:
-            out[..., self.scalar_locs] = self.scalar_norm(f[..., self.scalar_locs])
+            out[..., self._scalar_ix] = self.scalar_norm(f[..., self._scalar_ix])
         if self.nhigher > 0:
-            out[..., self.higher_mask] = self.higher_norm(f[..., self.higher_mask])
+            out[..., self._higher_ix] = self.higher_norm(f[..., self._higher_ix])
         return out
 
     def extra_repr(self) -> str:

@@ -60,7 +60,7 @@ enum feq_status_code {
  * ------------------------------------------------------------------------ */
 const char *feq_status_string(int status);
 /* 2: FeqAttnArgs gained k / num_src_nodes (partitioned graphs).
- * 3: attention / pooling backward entry points. */
+ * 3: attention / pooling backward entry points, node-level operators. */
 int feq_abi_version(void);
 /* Human-readable last CUDA error seen by this thread (empty when none). */
 const char *feq_last_error(void);
@@ -372,6 +372,32 @@ int feq_segment_pool_bwd(const float *edge_rows, int64_t row_len, const float *w
                          int64_t num_edges, int32_t reduce, const float *out, const float *grad_out,
                          float *tie_scratch, float *grad_rows, float *grad_weights, int32_t *status,
                          feq_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Node-level operators of the transformer block (forward; no counterpart kernels in
+ * the reference, which composes them from PyTorch ops).  x, out: (N, C, d) float32
+ * with d = sum(2 l + 1) over lvals.
+ * ------------------------------------------------------------------------ */
+/* SeparableEquivariantLayerNorm (flash_eq/layers/norm.py:177-249): every l = 0 position
+ * p_s gets a LayerNorm over channels, (x - mean) / (std + eps) * w_scalar[c, s] +
+ * b_scalar[c, s] (std biased; w/b (C, n_scalar)); all other positions share one RMS,
+ * x * w_higher[c] / sqrt(mean(x^2) + eps). */
+int feq_node_sep_layernorm(const float *x, int64_t num_nodes, int32_t C, const int32_t *lvals, int32_t n_lvals,
+                           const float *w_scalar, const float *b_scalar, const float *w_higher, float eps,
+                           float *out, feq_stream_t stream);
+/* EquivariantLayerNorm (norm.py:111-174): norms[c, r] = sqrt(sum over irrep r of x^2 +
+ * rep_eps); when ln_weight != NULL a LayerNorm of the norms over channels per irrep
+ * (ln_eps, affine (C,)); out = x * ln / (norms + eps) (1 / (norms + eps) without it). */
+int feq_node_layernorm(const float *x, int64_t num_nodes, int32_t C, const int32_t *lvals, int32_t n_lvals,
+                       const float *ln_weight, const float *ln_bias, float ln_eps, float rep_eps, float eps,
+                       float *out, feq_stream_t stream);
+/* RepNorm (norm.py:19-64): norms (N, C, n_lvals) = sqrt(sum over each irrep of x^2 + eps). */
+int feq_node_rep_norm(const float *x, int64_t num_nodes, int32_t C, const int32_t *lvals, int32_t n_lvals,
+                      float eps, float *norms, feq_stream_t stream);
+/* EquivariantGating's gate (gating.py:17-76): out = x * sigmoid(z)[c, irrep of the
+ * position], z (N, C * n_lvals) the pre-activation. */
+int feq_node_gate(const float *x, const float *z, int64_t num_nodes, int32_t C, const int32_t *lvals,
+                  int32_t n_lvals, float *out, feq_stream_t stream);
 
 #ifdef __cplusplus
 }
