@@ -17,6 +17,8 @@
 #include <math.h>
 #include <string.h>
 
+#include <algorithm>
+
 #include "feq_internal.cuh"
 
 namespace feq {
@@ -50,13 +52,53 @@ struct SepLnArgs {
     int64_t N;
 };
 
+// Walk the row elements j = lane, lane + 32, ... with their (channel, position) pair
+// updated incrementally (no integer division per element).
+struct RowWalk {
+    int c, p, dc, dp, d;
+    __device__ __forceinline__ RowWalk(int lane, int d_) : d(d_) {
+        c = lane / d_;
+        p = lane - c * d_;
+        dc = 32 / d_;
+        dp = 32 - dc * d_;
+    }
+    __device__ __forceinline__ void next() {
+        c += dc;
+        p += dp;
+        if (p >= d) {
+            p -= d;
+            c++;
+        }
+    }
+};
+
+// Copy one node row into shared memory, all of a lane's loads issued before its stores
+// (a load -> store pair per iteration would serialise on the load latency).
 __device__ __forceinline__ void stage_row(float *row, const float *src, int n, int lane) {
+    constexpr int kB = 8;
     if ((n & 3) == 0 && ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(row)) & 15) == 0) {
         const float4 *s4 = reinterpret_cast<const float4 *>(src);
         float4 *r4 = reinterpret_cast<float4 *>(row);
-        for (int i = lane; i < n / 4; i += 32) r4[i] = __ldg(s4 + i);
+        const int n4 = n / 4;
+        for (int i0 = lane; i0 < n4; i0 += 32 * kB) {
+            float4 v[kB];
+#pragma unroll
+            for (int u = 0; u < kB; u++)
+                if (i0 + 32 * u < n4) v[u] = __ldg(s4 + i0 + 32 * u);
+#pragma unroll
+            for (int u = 0; u < kB; u++)
+                if (i0 + 32 * u < n4) r4[i0 + 32 * u] = v[u];
+        }
     } else {
-        for (int i = lane; i < n; i += 32) row[i] = __ldg(src + i);
+        for (int i0 = lane; i0 < n; i0 += 32 * kB) {
+            float v[kB];
+#pragma unroll
+            for (int u = 0; u < kB; u++)
+                if (i0 + 32 * u < n) v[u] = __ldg(src + i0 + 32 * u);
+#pragma unroll
+            for (int u = 0; u < kB; u++)
+                if (i0 + 32 * u < n) row[i0 + 32 * u] = v[u];
+        }
     }
     __syncwarp();
 }
@@ -67,6 +109,9 @@ __global__ void __launch_bounds__(kNodeWarps * 32) sep_layernorm_kernel(const __
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     float *row = nsm + (size_t)warp * n;
     __shared__ float mu_s[kNodeWarps][kNodeMaxScalars], inv_s[kNodeWarps][kNodeMaxScalars], rms_s[kNodeWarps];
+    __shared__ int8_t sidx_s[kMaxDim];     // per-lane lookups from shared memory, not the parameter bank
+    for (int i = threadIdx.x; i < d; i += blockDim.x) sidx_s[i] = a.scalar_idx[i];
+    __syncthreads();
     for (int64_t node = (int64_t)blockIdx.x * kNodeWarps + warp; node < a.N; node += (int64_t)gridDim.x * kNodeWarps) {
         stage_row(row, a.x + node * n, n, lane);
         for (int s = 0; s < a.nscalar; s++) {
@@ -87,21 +132,23 @@ __global__ void __launch_bounds__(kNodeWarps * 32) sep_layernorm_kernel(const __
         }
         if (a.n_higher > 0) {
             float sq = 0.0f;
-            for (int j = lane; j < n; j += 32)
-                if (a.scalar_idx[j % d] < 0) sq = fmaf(row[j], row[j], sq);
+            RowWalk w(lane, d);
+            for (int j = lane; j < n; j += 32, w.next())
+                if (sidx_s[w.p] < 0) sq = fmaf(row[j], row[j], sq);
             sq = nwsum(sq);
             if (lane == 0) rms_s[warp] = sqrtf(sq / (float)(C * a.n_higher) + a.eps);
         }
         __syncwarp();
         float *orow = a.out + node * n;
-        for (int j = lane; j < n; j += 32) {
-            const int c = j / d, p = j - c * d;
+        const float rms = a.n_higher > 0 ? rms_s[warp] : 1.0f;
+        RowWalk w(lane, d);
+        for (int j = lane; j < n; j += 32, w.next()) {
             float v = row[j];
-            const int s = a.scalar_idx[p];
+            const int s = sidx_s[w.p];
             if (s >= 0) {
-                v = (v - mu_s[warp][s]) / inv_s[warp][s] * a.w_s[c * a.nscalar + s] + a.b_s[c * a.nscalar + s];
+                v = (v - mu_s[warp][s]) / inv_s[warp][s] * a.w_s[w.c * a.nscalar + s] + a.b_s[w.c * a.nscalar + s];
             } else {
-                v = v * (a.w_h[c] / rms_s[warp]);
+                v = v * (a.w_h[w.c] / rms);
             }
             orow[j] = v;
         }
@@ -117,12 +164,13 @@ struct EqLnArgs {
     int64_t N;
 };
 
-// norms of this warp's node row into nrm[c * n_irreps + r]
-__device__ __forceinline__ void row_norms(const NodeRepr &R, const float *row, float rn_eps, float *nrm, int lane) {
+// norms of this warp's node row into nrm[c * n_irreps + r] (irrep offsets / sizes from shared memory)
+__device__ __forceinline__ void row_norms(const NodeRepr &R, const int16_t *ioff, const int16_t *ik, const float *row,
+                                          float rn_eps, float *nrm, int lane) {
     const int C = R.C, d = R.d;
     for (int i = lane; i < C * R.n_irreps; i += 32) {
         const int c = i / R.n_irreps, r = i - c * R.n_irreps;
-        const int off = R.irr_off[r], k = 2 * R.irr_l[r] + 1;
+        const int off = ioff[r], k = ik[r];
         float s = 0.0f;
         for (int m = 0; m < k; m++) {
             const float v = row[c * d + off + m];
@@ -139,9 +187,17 @@ __global__ void __launch_bounds__(kNodeWarps * 32) equi_layernorm_kernel(const _
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     float *row = nsm + (size_t)warp * (n + C * nr);
     float *nrm = row + n;               // norms, then the rescaling factors
+    __shared__ int8_t pirr_s[kMaxDim];
+    __shared__ int16_t ioff_s[kNodeMaxIrreps], ik_s[kNodeMaxIrreps];
+    for (int i = threadIdx.x; i < d; i += blockDim.x) pirr_s[i] = a.R.pos_irr[i];
+    for (int i = threadIdx.x; i < nr; i += blockDim.x) {
+        ioff_s[i] = a.R.irr_off[i];
+        ik_s[i] = 2 * a.R.irr_l[i] + 1;
+    }
+    __syncthreads();
     for (int64_t node = (int64_t)blockIdx.x * kNodeWarps + warp; node < a.N; node += (int64_t)gridDim.x * kNodeWarps) {
         stage_row(row, a.x + node * n, n, lane);
-        row_norms(a.R, row, a.rn_eps, nrm, lane);
+        row_norms(a.R, ioff_s, ik_s, row, a.rn_eps, nrm, lane);
         for (int r = 0; r < nr; r++) {
             if (a.ln_w) {
                 float s = 0.0f;
@@ -164,10 +220,8 @@ __global__ void __launch_bounds__(kNodeWarps * 32) equi_layernorm_kernel(const _
         }
         __syncwarp();
         float *orow = a.out + node * n;
-        for (int j = lane; j < n; j += 32) {
-            const int c = j / d, p = j - c * d;
-            orow[j] = row[j] * nrm[c * nr + a.R.pos_irr[p]];
-        }
+        RowWalk w(lane, d);
+        for (int j = lane; j < n; j += 32, w.next()) orow[j] = row[j] * nrm[w.c * nr + pirr_s[w.p]];
         __syncwarp();
     }
 }
@@ -187,12 +241,18 @@ __global__ void __launch_bounds__(kNodeWarps * 32) rep_norm_kernel(const __grid_
     const int C = a.R.C, d = a.R.d, n = C * d, nr = a.R.n_irreps;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     float *row = nsm + (size_t)warp * n;
+    __shared__ int16_t ioff_s[kNodeMaxIrreps], ik_s[kNodeMaxIrreps];
+    for (int i = threadIdx.x; i < nr; i += blockDim.x) {
+        ioff_s[i] = a.R.irr_off[i];
+        ik_s[i] = 2 * a.R.irr_l[i] + 1;
+    }
+    __syncthreads();
     for (int64_t node = (int64_t)blockIdx.x * kNodeWarps + warp; node < a.N; node += (int64_t)gridDim.x * kNodeWarps) {
         stage_row(row, a.x + node * n, n, lane);
         float *o = a.norms + node * (int64_t)C * nr;
         for (int i = lane; i < C * nr; i += 32) {
             const int c = i / nr, r = i - c * nr;
-            const int off = a.R.irr_off[r], k = 2 * a.R.irr_l[r] + 1;
+            const int off = ioff_s[r], k = ik_s[r];
             float s = 0.0f;
             for (int m = 0; m < k; m++) {
                 const float v = row[c * d + off + m];
@@ -204,15 +264,176 @@ __global__ void __launch_bounds__(kNodeWarps * 32) rep_norm_kernel(const __grid_
     }
 }
 
-// out[n, c, p] = x[n, c, p] * sigmoid(z[n, c * n_irreps + irrep(p)]), elementwise over the rows.
-__global__ void gate_kernel(const __grid_constant__ RepNormArgs a) {
-    const int C = a.R.C, d = a.R.d, nr = a.R.n_irreps;
-    const int64_t total = a.N * C * d;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t node_c = i / d;
-        const int p = (int)(i - node_c * d);
-        const float zz = __ldg(a.z + node_c * nr + a.R.pos_irr[p]);
-        a.out[i] = a.x[i] * (1.0f / (1.0f + expf(-zz)));
+// out[n, c, p] = x[n, c, p] * sigmoid(z[n, c * n_irreps + irrep(p)]); one warp per node,
+// the node's gates computed once into shared memory.
+__global__ void __launch_bounds__(kNodeWarps * 32) gate_kernel(const __grid_constant__ RepNormArgs a) {
+    extern __shared__ float nsm[];
+    const int C = a.R.C, d = a.R.d, n = C * d, nr = a.R.n_irreps;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float *gs = nsm + (size_t)warp * C * nr;
+    __shared__ int8_t pirr_s[kMaxDim];
+    for (int i = threadIdx.x; i < d; i += blockDim.x) pirr_s[i] = a.R.pos_irr[i];
+    __syncthreads();
+    for (int64_t node = (int64_t)blockIdx.x * kNodeWarps + warp; node < a.N; node += (int64_t)gridDim.x * kNodeWarps) {
+        const float *zr = a.z + node * (int64_t)C * nr;
+        for (int i = lane; i < C * nr; i += 32) gs[i] = 1.0f / (1.0f + expf(-__ldg(zr + i)));
+        __syncwarp();
+        const float *xr = a.x + node * n;
+        float *orow = a.out + node * n;
+        RowWalk w(lane, d);
+        for (int j = lane; j < n; j += 32, w.next()) orow[j] = __ldg(xr + j) * gs[w.c * nr + pirr_s[w.p]];
+        __syncwarp();
+    }
+}
+
+// ---------------------------------------------------------------------------
+// EquivariantLinear (flash_eq/layers/linear.py:172-268):
+//   y[n, co, p] = sum_ci W[irrep(p) * Cout + co, ci] x[n, ci, p]  (+ bias[co, s] at the
+//   s-th l = 0 position).  The reference multiplies every irrep's weight block with every
+//   position and gathers; here each position only meets its own irrep's block.
+// CTA = 4096 / Cout nodes.  Per irrep r the x tile is re-laid in shared memory as a
+// (Cin x nodes * K_r) matrix whose columns are the (node, position) pairs of the irrep,
+// and the weight block
+// W_r^T as (Cin x Cout): the irrep's product is one small GEMM.  Thread = 4 consecutive
+// output channels x K_r quads of 4 consecutive columns; per input channel one float4
+// weight load and K_r float4 x loads feed 16 K_r FMAs.  Float32 CUDA-core FMAs, results
+// stored straight to y.
+// ---------------------------------------------------------------------------
+constexpr int kLinThreads = 256;
+
+struct LinArgs {
+    NodeRepr R;                    // input and output share the degrees
+    int Cin, Cout;
+    int8_t scalar_idx[kNodeMaxIrreps];   // irrep -> bias column (-1: not a scalar irrep)
+    int nscalar;
+    const float *x, *w, *bias;
+    float *y;
+    int64_t N;
+};
+
+// QPT column quads per thread, starting at quad q0 + g (the thread's group g), K = 2l+1.
+template <int K, int QPT>
+__device__ __forceinline__ void lin_gemm(const LinArgs &a, const float *xs, const float *wt, int wld, int tn,
+                                         int64_t n0, int n_nodes, int r, int q0) {
+    const int Cin = a.Cin, Cout = a.Cout, d = a.R.d, off = a.R.irr_off[r];
+    const int ncol = tn * K;                       // columns: (node, position) pairs, node-major
+    const int nq4 = Cout / 4, groups = kLinThreads / nq4;
+    const int t = threadIdx.x, cq = t % nq4, g = t / nq4;
+    const int sb = a.scalar_idx[r];
+    float acc[QPT][4][4];
+#pragma unroll
+    for (int u = 0; u < QPT; u++)
+#pragma unroll
+        for (int c = 0; c < 4; c++)
+#pragma unroll
+            for (int j = 0; j < 4; j++) acc[u][c][j] = 0.0f;
+    const float *wp = wt + 4 * cq;
+    const float *xp = xs + 4 * (q0 + g);
+#pragma unroll 2
+    for (int ci = 0; ci < Cin; ci++, wp += wld, xp += ncol) {
+        const float4 w = *reinterpret_cast<const float4 *>(wp);
+#pragma unroll
+        for (int u = 0; u < QPT; u++) {
+            const float4 xv = *reinterpret_cast<const float4 *>(xp + 4 * u * groups);
+            const float xa[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                acc[u][0][j] = fmaf(w.x, xa[j], acc[u][0][j]);
+                acc[u][1][j] = fmaf(w.y, xa[j], acc[u][1][j]);
+                acc[u][2][j] = fmaf(w.z, xa[j], acc[u][2][j]);
+                acc[u][3][j] = fmaf(w.w, xa[j], acc[u][3][j]);
+            }
+        }
+    }
+    float b[4];
+#pragma unroll
+    for (int c = 0; c < 4; c++) b[c] = sb >= 0 ? a.bias[(4 * cq + c) * a.nscalar + sb] : 0.0f;
+    float *yb = a.y + (n0 * Cout + 4 * cq) * d + off;
+#pragma unroll
+    for (int u = 0; u < QPT; u++) {
+        const int col0 = 4 * (q0 + g + u * groups);
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int col = col0 + j, node = col / K, m = col - node * K;   // K constant: no division
+            if (node >= n_nodes) continue;
+            float *yr = yb + (int64_t)node * Cout * d + m;
+#pragma unroll
+            for (int c = 0; c < 4; c++) yr[c * d] = acc[u][c][j] + b[c];
+        }
+    }
+}
+
+// One irrep of 2l+1 = K positions: re-lay its x columns, then the GEMM in passes of <= 5 quads.
+template <int K>
+__device__ __forceinline__ void lin_irrep(const LinArgs &a, float *xs, const float *wt, int wld, int tn,
+                                          const float *xg, int64_t n0, int n_nodes, int r) {
+    const int Cin = a.Cin, d = a.R.d, off = a.R.irr_off[r], ncol = tn * K;
+    // xs[ci][node * K + m] = x[n0 + node, ci, off + m], a batch of loads per thread before the stores
+    constexpr int kB = 8;
+    for (int i0 = threadIdx.x; i0 < Cin * ncol; i0 += kLinThreads * kB) {
+        float v[kB];
+#pragma unroll
+        for (int u = 0; u < kB; u++) {
+            const int i = i0 + u * kLinThreads;
+            const int ci = i / ncol, col = i - ci * ncol, node = col / K, m = col - node * K;
+            v[u] = (i < Cin * ncol && node < n_nodes) ? __ldg(xg + ((int64_t)node * Cin + ci) * d + off + m) : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < kB; u++) {
+            const int i = i0 + u * kLinThreads;
+            if (i < Cin * ncol) xs[i] = v[u];
+        }
+    }
+    __syncthreads();
+    const int groups = kLinThreads / (a.Cout / 4);
+    // K * groups column quads: each group takes K of them
+    if constexpr (K <= 5) {
+        lin_gemm<K, K>(a, xs, wt, wld, tn, n0, n_nodes, r, 0);
+    } else {
+        lin_gemm<K, 5>(a, xs, wt, wld, tn, n0, n_nodes, r, 0);
+        lin_gemm<K, K - 5>(a, xs, wt, wld, tn, n0, n_nodes, r, 5 * groups);
+    }
+}
+
+__global__ void __launch_bounds__(kLinThreads, 1) node_linear_kernel(const __grid_constant__ LinArgs a) {
+    extern __shared__ float lsm[];
+    const int Cin = a.Cin, Cout = a.Cout, d = a.R.d;
+    const int wld = Cout + 4;
+    const int nq4 = Cout / 4, groups = kLinThreads / nq4, tn = 4 * groups;   // nodes of this CTA
+    float *wt = lsm;                                   // Cin x (Cout + 4)
+    float *xs = wt + (size_t)Cin * wld;                // Cin x (tn K_r) for the current irrep
+    const int64_t n0 = (int64_t)blockIdx.x * tn;
+    const int n_nodes = (int)min64(tn, a.N - n0);
+    const float *xg = a.x + n0 * Cin * d;
+    for (int r = 0; r < a.R.n_irreps; r++) {
+        __syncthreads();   // the previous irrep's tiles are no longer read
+        const float *wr = a.w + (int64_t)r * Cout * Cin;
+        constexpr int kV = 8;
+        for (int i0 = threadIdx.x * 4; i0 < Cout * Cin; i0 += kLinThreads * 4 * kV) {
+            float4 v[kV];
+#pragma unroll
+            for (int u = 0; u < kV; u++) {
+                const int i = i0 + u * kLinThreads * 4;
+                v[u] = i < Cout * Cin ? __ldg(reinterpret_cast<const float4 *>(wr + i)) : make_float4(0, 0, 0, 0);
+            }
+#pragma unroll
+            for (int u = 0; u < kV; u++) {
+                const int i = i0 + u * kLinThreads * 4;
+                if (i >= Cout * Cin) break;
+                const int co = i / Cin, ci = i - co * Cin;     // Cin % 4 == 0: the 4 share co
+                wt[ci * wld + co] = v[u].x;
+                wt[(ci + 1) * wld + co] = v[u].y;
+                wt[(ci + 2) * wld + co] = v[u].z;
+                wt[(ci + 3) * wld + co] = v[u].w;
+            }
+        }
+        switch (a.R.irr_l[r]) {
+            case 0: lin_irrep<1>(a, xs, wt, wld, tn, xg, n0, n_nodes, r); break;
+            case 1: lin_irrep<3>(a, xs, wt, wld, tn, xg, n0, n_nodes, r); break;
+            case 2: lin_irrep<5>(a, xs, wt, wld, tn, xg, n0, n_nodes, r); break;
+            case 3: lin_irrep<7>(a, xs, wt, wld, tn, xg, n0, n_nodes, r); break;
+            default: lin_irrep<9>(a, xs, wt, wld, tn, xg, n0, n_nodes, r); break;
+        }
     }
 }
 
@@ -331,6 +552,40 @@ int feq_node_rep_norm(const float *x, int64_t num_nodes, int32_t C, const int32_
     return FEQ_OK;
 }
 
+int feq_node_linear(const float *x, int64_t num_nodes, int32_t c_in, int32_t c_out, const int32_t *lvals,
+                    int32_t n_lvals, const float *weight, const float *bias, float *y, feq_stream_t stream) {
+    LinArgs a;
+    memset(&a, 0, sizeof(a));
+    int rc = fill_node_repr(lvals, n_lvals, c_in, &a.R);
+    if (rc != FEQ_OK) return rc;
+    if (num_nodes < 0 || c_out < 1) return FEQ_ERR_INVALID_ARGUMENT;
+    if (num_nodes == 0) return FEQ_OK;
+    if (!x || !weight || !y) return FEQ_ERR_INVALID_ARGUMENT;
+    // channel quads must tile the threads (Cout in 4 .. 1024, a power-of-two multiple of 4)
+    if (c_in % 4 || c_out % 4 || c_out > 1024 || kLinThreads % (c_out / 4) || (reinterpret_cast<uintptr_t>(weight) & 15))
+        return FEQ_ERR_UNSUPPORTED;
+    int kmax = 1;
+    for (int r = 0; r < n_lvals; r++) {
+        if (lvals[r] > 4) return FEQ_ERR_UNSUPPORTED;
+        a.scalar_idx[r] = -1;
+        if (lvals[r] == 0 && bias) a.scalar_idx[r] = (int8_t)a.nscalar++;
+        kmax = std::max(kmax, 2 * lvals[r] + 1);
+    }
+    a.Cin = c_in;
+    a.Cout = c_out;
+    a.x = x;
+    a.w = weight;
+    a.bias = bias;
+    a.y = y;
+    a.N = num_nodes;
+    const int tn = 4 * (kLinThreads / (c_out / 4));
+    const size_t smem = sizeof(float) * ((size_t)c_in * (c_out + 4) + (size_t)c_in * tn * kmax);
+    if ((rc = set_smem((const void *)node_linear_kernel, smem)) != FEQ_OK) return rc;
+    node_linear_kernel<<<(unsigned)((num_nodes + tn - 1) / tn), kLinThreads, smem, (cudaStream_t)stream>>>(a);
+    FEQ_LAUNCH_CHECK();
+    return FEQ_OK;
+}
+
 int feq_node_gate(const float *x, const float *z, int64_t num_nodes, int32_t C, const int32_t *lvals, int32_t n_lvals,
                   float *out, feq_stream_t stream) {
     RepNormArgs a;
@@ -344,8 +599,9 @@ int feq_node_gate(const float *x, const float *z, int64_t num_nodes, int32_t C, 
     a.z = z;
     a.out = out;
     a.N = num_nodes;
-    const int64_t total = num_nodes * C * a.R.d;
-    gate_kernel<<<(unsigned)min64((total + 255) / 256, 148 * 32), 256, 0, (cudaStream_t)stream>>>(a);
+    const size_t smem = sizeof(float) * kNodeWarps * (size_t)C * n_lvals;
+    if ((rc = set_smem((const void *)gate_kernel, smem)) != FEQ_OK) return rc;
+    gate_kernel<<<node_grid(num_nodes), kNodeWarps * 32, smem, (cudaStream_t)stream>>>(a);
     FEQ_LAUNCH_CHECK();
     return FEQ_OK;
 }

@@ -116,6 +116,8 @@ SIGNATURES = {
                                           ctypes.c_float, ctypes.c_float, ctypes.c_float, c_vp, c_vp]),
     "feq_node_rep_norm": (ctypes.c_int, [c_vp, ctypes.c_int64, ctypes.c_int32, c_i32p, ctypes.c_int32, ctypes.c_float,
                                          c_vp, c_vp]),
+    "feq_node_linear": (ctypes.c_int, [c_vp, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, c_i32p, ctypes.c_int32,
+                                       c_vp, c_vp, c_vp, c_vp]),
     "feq_node_gate": (ctypes.c_int, [c_vp, c_vp, ctypes.c_int64, ctypes.c_int32, c_i32p, ctypes.c_int32, c_vp, c_vp]),
     "feq_segment_softmax_bwd": (ctypes.c_int, [c_vp, c_vp, ctypes.c_int64, ctypes.c_int32, c_vp, c_vp,
                                                ctypes.c_int64, c_vp, c_vp]),

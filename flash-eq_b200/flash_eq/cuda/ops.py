@@ -508,6 +508,20 @@ def node_rep_norm(x, lvals, eps):
     return norms.view(*x.shape[:-1], n)
 
 
+def node_linear(x, lvals, weight, bias, c_out):
+    """EquivariantLinear forward (identity activation): (..., Cin, d) -> (..., Cout, d)."""
+    lib = _require_cuda(x, weight, bias)
+    rows = _node_rows(x, "features")
+    w = _f32(weight, "weight")
+    b = None if bias is None else _f32(bias, "bias")
+    y = torch.empty(rows.shape[0], int(c_out), rows.shape[2], dtype=torch.float32, device=rows.device)
+    arr, n = _lib.i32_array(lvals)
+    rc = lib.feq_node_linear(_p(rows), rows.shape[0], rows.shape[1], int(c_out), arr, n, _p(w), _p(b), _p(y),
+                             _stream(rows.device))
+    _lib.check(rc, "feq_node_linear")
+    return y.view(*x.shape[:-2], int(c_out), x.shape[-1])
+
+
 def node_gate(x, z, lvals):
     """x * sigmoid(z)[..., c, irrep(position)]; z (..., C * n_irreps)."""
     lib = _require_cuda(x, z)

@@ -10,7 +10,8 @@ handles) for the same directions, the kernel rebuilds their blocks from the
 directions and never reads the dense matrices; any other P / Q is applied as a
 dense matrix exactly like the reference's bmm.
 
-``EquivariantLinear`` is node-level and stays in PyTorch (linear.py:172-268).
+``EquivariantLinear`` (linear.py:172-268) is node-level: a native per-irrep kernel on the
+inference path (csrc/feq_node.cu), one batched GEMM over positions under autograd.
 """
 from __future__ import annotations
 
@@ -21,6 +22,7 @@ from ..cuda import ops
 from ..cuda.block_diagonal import block_diagonal_cuda, forward_only
 from ..representations import ProductRepr, Repr
 from ..representations.wigner import LazyBasis, basis_source
+from .norm import native_node_ok
 from .radial import SeparableRadialNet
 
 
@@ -133,6 +135,11 @@ class EquivariantLinear(nn.Module):
         self.bias: nn.Parameter | None
         self.bias = nn.Parameter(torch.zeros(out_repr.mult, nscalar)) if (nscalar > 0 and bias) else None
         self.activation = activation if activation is not None else nn.Identity()
+        self._lvals = tuple(in_repr.lvals.tolist())
+        # the native kernel: identity activation, degrees <= 4, channel counts in quads
+        self._native_ok = (isinstance(self.activation, nn.Identity) and max(self._lvals) <= 4
+                           and in_repr.mult % 4 == 0 and out_repr.mult % 4 == 0 and out_repr.mult <= 1024
+                           and 256 % (out_repr.mult // 4) == 0)
 
     def forward(self, f: torch.Tensor) -> torch.Tensor:
         """out[..., co, p] = sum_ci W_{irrep(p)}[co, ci] f[..., ci, p] (+ bias on l = 0 positions).
@@ -142,9 +149,11 @@ class EquivariantLinear(nn.Module):
         gathered first and one batched GEMM over positions does only the needed products:
         the same sums, 1 / nreps of the FLOPs, no (nreps x) intermediate."""
         *b, cin, d = f.shape
-        x = f.reshape(-1, cin, d)
         nreps = self.outdims[0]
         cout = self.expanddims[1]
+        if self._native_ok and native_node_ok(f, self.weight, self.bias):
+            return ops.node_linear(f, self._lvals, self.weight, self.bias, cout)
+        x = f.reshape(-1, cin, d)
         w = self.weight.view(nreps, cout, cin).index_select(0, self.indices)    # (d, Cout, Cin)
         y = torch.bmm(w, x.permute(2, 1, 0))                                     # (d, Cout, N)
         if self.bias is not None:

@@ -394,6 +394,12 @@ int feq_node_layernorm(const float *x, int64_t num_nodes, int32_t C, const int32
 /* RepNorm (norm.py:19-64): norms (N, C, n_lvals) = sqrt(sum over each irrep of x^2 + eps). */
 int feq_node_rep_norm(const float *x, int64_t num_nodes, int32_t C, const int32_t *lvals, int32_t n_lvals,
                       float eps, float *norms, feq_stream_t stream);
+/* EquivariantLinear (linear.py:172-268), identity activation:
+ *   y[n, co, p] = sum_ci weight[irrep(p) * c_out + co, ci] x[n, ci, p] (+ bias[co, s] at the
+ *   s-th l = 0 irrep when bias != NULL; bias (c_out, n_scalar)).  x (N, c_in, d),
+ *   y (N, c_out, d), weight (n_lvals * c_out, c_in); degrees <= 4. */
+int feq_node_linear(const float *x, int64_t num_nodes, int32_t c_in, int32_t c_out, const int32_t *lvals,
+                    int32_t n_lvals, const float *weight, const float *bias, float *y, feq_stream_t stream);
 /* EquivariantGating's gate (gating.py:17-76): out = x * sigmoid(z)[c, irrep of the
  * position], z (N, C * n_lvals) the pre-activation. */
 int feq_node_gate(const float *x, const float *z, int64_t num_nodes, int32_t C, const int32_t *lvals,

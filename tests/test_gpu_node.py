@@ -77,3 +77,34 @@ def test_native_and_autograd_paths_agree(cuda_device):
             a = mod(inp)
         b = mod(inp.clone().requires_grad_())
         assert rel_l2(a, b.detach()) < 1e-5, type(mod).__name__
+
+
+def _linear_reference(m, f):
+    """EquivariantLinear.forward as the reference writes it (linear.py:230-268)."""
+    b = f.shape[:-2]
+    out = (m.weight @ f).view(*b, *m.outdims)
+    out = out.gather(dim=-3, index=m.indices.expand(*b, *m.expanddims)).squeeze(-3)
+    if m.bias is not None:
+        out = out.clone()
+        out[..., m.scalar_locs] = m.activation(out[..., m.scalar_locs] + m.bias)
+    return out
+
+
+LINEAR_CASES = [([0, 1, 2], 64, 128, True), ([0, 1, 2], 128, 64, True), ([0, 0, 1, 2], 8, 6, True),
+                ([1, 2], 5, 7, False), ([0, 1, 2, 3], 128, 128, True), ([0, 1, 2, 3, 4], 16, 24, True),
+                ([3, 0], 3, 70, True)]
+
+
+@pytest.mark.parametrize("lv,cin,cout,bias", LINEAR_CASES, ids=[f"{c[0]}-{c[1]}-{c[2]}" for c in LINEAR_CASES])
+def test_equivariant_linear(cuda_device, lv, cin, cout, bias):
+    m = fe.EquivariantLinear(fe.Repr(lv, mult=cin), fe.Repr(lv, mult=cout), bias=bias)
+    if m.bias is not None:
+        with torch.no_grad():
+            m.bias.normal_()
+    f = torch.randn(3, 37, cin, fe.Repr(lv, 1).dim(), generator=torch.Generator().manual_seed(8))
+    ref = _linear_reference(copy.deepcopy(m).double(), f.double())
+    with torch.no_grad():
+        y = m.to(cuda_device)(f.to(cuda_device))
+    assert y.shape == ref.shape and rel_l2(y, ref) < 1e-5
+    yg = m(f.to(cuda_device).requires_grad_())       # the autograd formulation
+    assert rel_l2(yg.detach(), ref) < 1e-5
