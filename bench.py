@@ -575,6 +575,243 @@ def run_train(args):
     return 0
 
 
+# ---------------------------------------------------------------------------
+# EquivariantTransformerBlock forward on batched small graphs
+# ---------------------------------------------------------------------------
+BLOCK_GRAPHS, BLOCK_NODES, BLOCK_RADIUS, BLOCK_HEADS, BLOCK_SEED = 256, 30, 5.0, 8, 2
+
+
+def make_block_workload(seed, device):
+    """256 molecule-like graphs of 30 nodes, coordinates N(0, 1.5^2) per axis, all directed
+    pairs within 5 A (no self loops), features (N, 64, 9) ~ N(0, 1): BASELINE config 3."""
+    g = torch.Generator().manual_seed(seed)
+    coords = torch.randn(BLOCK_GRAPHS, BLOCK_NODES, 3, generator=g) * 1.5
+    x = torch.randn(BLOCK_GRAPHS * BLOCK_NODES, 64, 9, generator=g)
+    dd = torch.cdist(coords, coords)
+    mask = (dd < BLOCK_RADIUS) & ~torch.eye(BLOCK_NODES, dtype=torch.bool)[None]
+    gi, a, b = torch.nonzero(mask, as_tuple=True)
+    src, dst = gi * BLOCK_NODES + a, gi * BLOCK_NODES + b     # src -> dst within each graph
+    return {"coords": coords.reshape(-1, 3), "x": x, "src": src, "dst": dst}
+
+
+def build_block(device):
+    import flash_eq as fe
+
+    torch.manual_seed(BLOCK_SEED)
+    r = fe.Repr([0, 1, 2], mult=64)
+    blk = fe.EquivariantTransformerBlock(r, r, num_heads=BLOCK_HEADS, max_dist=MAX_DIST).to(device).eval()
+    return blk, fe.WignerDBasis([r]).to(device), r
+
+
+def block_step_fn(blk, basis, graph, coords, x):
+    def step():
+        with torch.no_grad():
+            vec = coords[graph.src] - coords[graph.dst]           # src - dst (transformer.py:406)
+            P = basis.lazy(vec)[0]
+            return blk(P, P, x, vec.norm(dim=-1), graph)
+    return step
+
+
+def cpu_block_setup(n_graphs):
+    """The reference algorithm of the block on the host cores: the module's node-level parts
+    in PyTorch and the attention layer restated with the oracle (matrix_exp basis, bmm,
+    block-diagonal mix, bmm, scatter softmax, scatter pooling), on n_graphs graphs."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import feq_oracle as orc
+    import flash_eq as fe
+
+    wl = make_block_workload(BLOCK_SEED, "cpu")
+    blk, _, r = build_block("cpu")
+    lv = [0, 1, 2]
+    nn_ = n_graphs * BLOCK_NODES
+    keep = wl["dst"] < nn_
+    src, dst = wl["src"][keep], wl["dst"][keep]
+    coords, x = wl["coords"][:nn_], wl["x"][:nn_]
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    att = blk.attn
+
+    def attention(P, Q, xin, dist, graph, edge_features=None):
+        E = src.numel()
+        qk = att.linear_qk(att.norm_qk(xin))
+        Qe = qk[:, :64][dst].reshape(E, BLOCK_HEADS, -1)
+        Ke = qk[:, 64:][src].reshape(E, BLOCK_HEADS, -1)
+        rw = att.linear_v.radial_weights
+        p1, p2 = rw.binning_params()
+        V = orc.edgewise_fwd(P, P, xin[src], dist, rw(), lv, lv, att.linear_v.solid_harmonic_scale, p1, p2,
+                             rw.num_bins, rw.log, nthreads=threads)
+        w = orc.edge_attention(Qe, Ke, V, dst, nn_, att.attention.log_scale.exp(), BLOCK_HEADS)
+        return orc.pool(w, dst, nn_, "sum")
+
+    att.forward = attention
+    graph = fe.Graph(src=src, dst=dst, num_nodes=nn_)
+
+    def step():
+        with torch.no_grad():
+            vec = coords[src] - coords[dst]
+            P = orc.wigner_basis(vec, lv)
+            return blk(P, P, x, vec.norm(dim=-1), graph)
+
+    return step, int(src.numel()), threads
+
+
+def run_block(args):
+    """One step = the block forward (basis handles from the edge vectors, attention with the
+    edgewise V, gated MLP) on the whole batch; data-parallel by graph batch under torchrun."""
+    import flash_eq as fe
+
+    if args.impl == "reference":
+        if int(os.environ.get("RANK", "0")) != 0:
+            return 0
+        step, n, threads = cpu_block_setup(8)
+        for _ in range(max(1, args.warmup)):
+            step()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            step()
+        dt = (time.perf_counter() - t0) / args.steps
+        print(json.dumps({
+            "metric": "edges/sec (EquivariantTransformerBlock fwd)", "impl": "reference", "value": n / dt,
+            "unit": "edges/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic",
+            "config": block_config(args.gpus, int(make_block_workload(BLOCK_SEED, "cpu")["src"].numel())),
+            "cpu_baseline": {"value": n / dt, "unit": "edges/s", "cores": threads, "kind": "port",
+                             "sample": f"8 of the 256 graphs ({n} edges) per step (CPU: {cpu_model()})"},
+            "e2e": {"value": n / dt, "unit": "edges/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+            flush=True)
+        return 0
+    world, rank, local, pg = dist_setup(args)
+    dev = torch.device("cuda", local)
+    from flash_eq.cuda import _lib
+    from flash_eq.cuda import ops as feq_ops
+
+    lib = _lib.load()
+    wl = make_block_workload(BLOCK_SEED + rank, dev)
+    blk, basis, r = build_block(dev)
+    for m in blk.modules():
+        if isinstance(m, fe.EquivariantEdgewiseLinear):
+            m.mix_precision = args.mix
+    N = wl["x"].shape[0]
+    graph = fe.Graph(src=wl["src"].to(dev), dst=wl["dst"].to(dev), num_nodes=N)
+    coords, x = wl["coords"].to(dev), wl["x"].to(dev)
+    E = graph.num_edges
+    eager = block_step_fn(blk, basis, graph, coords, x)
+    for _ in range(max(3, args.warmup)):
+        eager()
+    torch.cuda.synchronize()
+    # the whole forward replayed as one CUDA graph (the library's ops are stream-ordered and
+    # allocate through torch's caching allocator, so the step captures as is)
+    side = torch.cuda.Stream(device=dev)
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(2):
+            eager()
+    torch.cuda.current_stream().wait_stream(side)
+    cg = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(cg):
+        out_static = eager()
+    step = cg.replay
+
+    def timed(fn, steps):
+        barrier(pg)
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for _ in range(steps):
+            fn()
+        t1.record()
+        barrier(pg)
+        return max_over_ranks(pg, t0.elapsed_time(t1) / steps)
+
+    for _ in range(args.warmup):
+        step()
+    clk = ClockSampler(gpu_index_for(local))
+    clk.start()
+    n0 = lib.feq_launch_count()
+    ms = timed(step, args.steps)
+    launches = lib.feq_launch_count() - n0
+    clocks = clk.stop()
+    ms_eager = timed(eager, max(3, args.steps // 4))
+    value = E * world / (ms / 1e3)
+    # per-stage device times of the library's kernels (eager steps, events on their streams)
+    prof_steps = 3
+    feq_ops.profile_enable(True)
+    for _ in range(prof_steps):
+        eager()
+    torch.cuda.synchronize()
+    stages = {k: {"ms": v[0] / prof_steps, "launches": v[1] // prof_steps} for k, v in feq_ops.profile_read().items()}
+    feq_ops.profile_enable(False)
+    hbm_peak, tc_peak, peak_kind = measured_peaks()
+    # algorithmic bytes per edge of the edge stages (fp32 rows C * d = 576 floats; bf16 A)
+    row = 64 * 9 * 4
+    nsplit = 2 if args.mix == "bf16x3" else 1
+    stage_bytes = {"rotate_in": row + 32 + 64 * 9 * 2 * nsplit, "rotate_out": 2 * row + 24,
+                   "tc_mix": 64 * 9 * 2 * nsplit + row + 4, "attn_pool": row + 16}
+    for k, v in stages.items():
+        if k in stage_bytes:
+            v["hbm_gbs"] = E * stage_bytes[k] / (v["ms"] / 1e3) / 1e9
+    dom = max((k for k in stages if k in stage_bytes), key=lambda k: stages[k]["ms"], default=None)
+    roofline = None
+    if dom is not None:
+        gbs = stages[dom]["hbm_gbs"]
+        roofline = {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak,
+                    "traffic": None, "kernel": f"{dom} (largest edge stage; CUDA events on its stream)",
+                    "peak_kind": peak_kind, "bytes_per_edge": stage_bytes[dom]}
+    e2e = None
+    if args.e2e_steps > 0:
+        x_h, c_h = wl["x"].pin_memory(), wl["coords"].pin_memory()
+        s_h, d_h = wl["src"].pin_memory(), wl["dst"].pin_memory()
+        out_h = torch.empty(N, 64, 9, pin_memory=True)
+
+        def e2e_step():
+            xd, cd = x_h.to(dev, non_blocking=True), c_h.to(dev, non_blocking=True)
+            g = fe.Graph(src=s_h.to(dev, non_blocking=True), dst=d_h.to(dev, non_blocking=True), num_nodes=N)
+            out_h.copy_(block_step_fn(blk, basis, g, cd, xd)(), non_blocking=True)
+
+        e2e_step()
+        ms_e = timed(e2e_step, args.e2e_steps)
+        e2e = {"value": E * world / (ms_e / 1e3), "unit": "edges/s",
+               "h2d_bytes_per_step": (x_h.numel() + c_h.numel()) * 4 + (s_h.numel() + d_h.numel()) * 8,
+               "d2h_bytes_per_step": out_h.numel() * 4, "ms_per_step": ms_e, "steps": args.e2e_steps,
+               "note": "eager steps through the public API (Graph built per step: its dst sort and "
+                       "validation included)"}
+    if rank == 0:
+        result = {
+            "metric": "edges/sec (EquivariantTransformerBlock fwd, device-timed)", "value": value, "unit": "edges/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16" if args.mix == "bf16" else "f32", "data": "synthetic",
+            "config": block_config(world, E), "roofline": roofline, "stages_ms_per_step": stages,
+            "eager_ms_per_step": ms_eager, "mix": args.mix, "clocks": clocks, "e2e": e2e,
+            "gpu_launches": int(launches), "note": "value: the step replayed as one CUDA graph; "
+                                                   "eager_ms_per_step: the same step launched op by op"}
+        if world == 1 and not args.no_cpu_baseline:
+            try:
+                cstep, n, threads = cpu_block_setup(8)
+                cstep()
+                t0 = time.perf_counter()
+                for _ in range(2):
+                    cstep()
+                dt = (time.perf_counter() - t0) / 2
+                result["cpu_baseline"] = {"value": n / dt, "unit": "edges/s", "cores": threads, "kind": "port",
+                                          "sample": f"8 of the 256 graphs ({n} edges), 2 reps (CPU: {cpu_model()})"}
+            except Exception as exc:  # the baseline must not hide the GPU number
+                result["cpu_baseline"] = {"value": None, "error": repr(exc)}
+        print(json.dumps(result), flush=True)
+    del cg
+    if pg is not None:
+        pg.barrier()
+        pg.destroy_process_group()
+    return 0
+
+
+def block_config(n_gpus, E):
+    return {"workload": "config3: EquivariantTransformerBlock forward, Repr([0,1,2],64) -> same, 8 heads, "
+                        "256 graphs x 30 nodes, coords N(0,1.5^2), all pairs within 5 A, 100 bins over [0,10]",
+            "edges_per_gpu": E, "global_edges": E * n_gpus, "parallelism": f"dp{n_gpus} (graph batch per GPU)",
+            "l2": "no flush: 0.9 GB of edge rows (V) written and read per step >> 126 MB L2"}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -587,9 +824,10 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--e2e-chunks", type=int, default=8,
                     help="edge chunks per end-to-end step (output copy of one overlaps compute of the next)")
-    ap.add_argument("--workload", choices=["config2", "train"], default="config2",
-                    help="config2: the metric (default); train: the reference's published single-layer "
-                         "fwd+bwd+Adam step (--lmax, --edges)")
+    ap.add_argument("--workload", choices=["config2", "block", "train"], default="config2",
+                    help="config2: the metric (default); block: BASELINE config 3 (transformer block "
+                         "forward); train: the reference's published single-layer fwd+bwd+Adam step "
+                         "(--lmax, --edges)")
     ap.add_argument("--edges", type=int, default=None)
     ap.add_argument("--lmax", type=int, default=4,
                     help="degrees 0..lmax in and out (default 4 = config 2); other values are variants, not the metric")
@@ -603,6 +841,8 @@ def main():
             args.edges = 128000
         args.edges = args.edges or 32000
         return run_train(args)
+    if args.workload == "block":
+        return run_block(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)

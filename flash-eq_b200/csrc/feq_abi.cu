@@ -997,6 +997,7 @@ int feq_attn_pool_fwd(const FeqAttnArgs *a, feq_stream_t stream) {
         return FEQ_ERR_INVALID_ARGUMENT;
     if (a->decay_scale > 0.0f && !a->distances) return FEQ_ERR_INVALID_ARGUMENT;
     if (a->k && a->num_src_nodes < 0) return FEQ_ERR_INVALID_ARGUMENT;
+    ProfScope ps("attn_pool", (cudaStream_t)stream);
     return launch_attn_pool(*a, (cudaStream_t)stream);
 }
 

@@ -502,6 +502,7 @@ int feq_node_sep_layernorm(const float *x, int64_t num_nodes, int32_t C, const i
     a.N = num_nodes;
     const size_t smem = sizeof(float) * kNodeWarps * (size_t)C * a.R.d;
     if ((rc = set_smem((const void *)sep_layernorm_kernel, smem)) != FEQ_OK) return rc;
+    ProfScope ps("node_norm", (cudaStream_t)stream);
     sep_layernorm_kernel<<<node_grid(num_nodes), kNodeWarps * 32, smem, (cudaStream_t)stream>>>(a);
     FEQ_LAUNCH_CHECK();
     return FEQ_OK;
@@ -527,6 +528,7 @@ int feq_node_layernorm(const float *x, int64_t num_nodes, int32_t C, const int32
     a.N = num_nodes;
     const size_t smem = sizeof(float) * kNodeWarps * ((size_t)C * a.R.d + (size_t)C * n_lvals);
     if ((rc = set_smem((const void *)equi_layernorm_kernel, smem)) != FEQ_OK) return rc;
+    ProfScope ps("node_norm", (cudaStream_t)stream);
     equi_layernorm_kernel<<<node_grid(num_nodes), kNodeWarps * 32, smem, (cudaStream_t)stream>>>(a);
     FEQ_LAUNCH_CHECK();
     return FEQ_OK;
@@ -547,6 +549,7 @@ int feq_node_rep_norm(const float *x, int64_t num_nodes, int32_t C, const int32_
     a.N = num_nodes;
     const size_t smem = sizeof(float) * kNodeWarps * (size_t)C * a.R.d;
     if ((rc = set_smem((const void *)rep_norm_kernel, smem)) != FEQ_OK) return rc;
+    ProfScope ps("node_norm", (cudaStream_t)stream);
     rep_norm_kernel<<<node_grid(num_nodes), kNodeWarps * 32, smem, (cudaStream_t)stream>>>(a);
     FEQ_LAUNCH_CHECK();
     return FEQ_OK;
@@ -581,6 +584,7 @@ int feq_node_linear(const float *x, int64_t num_nodes, int32_t c_in, int32_t c_o
     const int tn = 4 * (kLinThreads / (c_out / 4));
     const size_t smem = sizeof(float) * ((size_t)c_in * (c_out + 4) + (size_t)c_in * tn * kmax);
     if ((rc = set_smem((const void *)node_linear_kernel, smem)) != FEQ_OK) return rc;
+    ProfScope ps("node_linear", (cudaStream_t)stream);
     node_linear_kernel<<<(unsigned)((num_nodes + tn - 1) / tn), kLinThreads, smem, (cudaStream_t)stream>>>(a);
     FEQ_LAUNCH_CHECK();
     return FEQ_OK;
@@ -601,6 +605,7 @@ int feq_node_gate(const float *x, const float *z, int64_t num_nodes, int32_t C, 
     a.N = num_nodes;
     const size_t smem = sizeof(float) * kNodeWarps * (size_t)C * n_lvals;
     if ((rc = set_smem((const void *)gate_kernel, smem)) != FEQ_OK) return rc;
+    ProfScope ps("node_gate", (cudaStream_t)stream);
     gate_kernel<<<node_grid(num_nodes), kNodeWarps * 32, smem, (cudaStream_t)stream>>>(a);
     FEQ_LAUNCH_CHECK();
     return FEQ_OK;
