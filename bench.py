@@ -709,8 +709,10 @@ def run_block(args):
             eager()
     torch.cuda.current_stream().wait_stream(side)
     cg = torch.cuda.CUDAGraph()
+    n_cap = lib.feq_launch_count()
     with torch.cuda.graph(cg):
         out_static = eager()
+    per_replay = lib.feq_launch_count() - n_cap      # the library's kernels in one captured step
     step = cg.replay
 
     def timed(fn, steps):
@@ -727,9 +729,8 @@ def run_block(args):
         step()
     clk = ClockSampler(gpu_index_for(local))
     clk.start()
-    n0 = lib.feq_launch_count()
     ms = timed(step, args.steps)
-    launches = lib.feq_launch_count() - n0
+    launches = per_replay * args.steps
     clocks = clk.stop()
     ms_eager = timed(eager, max(3, args.steps // 4))
     value = E * world / (ms / 1e3)

@@ -69,6 +69,9 @@ __global__ void __launch_bounds__(kThreads) attn_pool_bwd_dst_kernel(const __gri
     const bool decay = a.decay_scale > 0.0f && a.distances != nullptr;
     const int64_t s0 = a.offsets[n], s1 = a.offsets[n + 1];
     const float cnt = (float)max64(s1 - s0, 1);
+    // per-thread dot products need float4-aligned rows and head slices
+    const bool per_thread = hd <= 128 && vhd <= 128 && ((hd | vhd | qrow | vrow) & 3) == 0 &&
+                            ((reinterpret_cast<uintptr_t>(kbase) | reinterpret_cast<uintptr_t>(a.v)) & 15) == 0;
     for (int j = threadIdx.x; j < qrow; j += kThreads) {
         q_s[j] = __ldg(a.qk + n * qk_ld + j);
         gq_s[j] = 0.0f;
@@ -101,27 +104,58 @@ __global__ void __launch_bounds__(kThreads) attn_pool_bwd_dst_kernel(const __gri
             sid_s[threadIdx.x] = sidx;
         }
         __syncthreads();
-        for (int pr = warp; pr < cn * H; pr += nwarps) {
-            const int k = pr / H, h = pr - k * H;
-            const int64_t e = eid_s[k], sidx = sid_s[k];
-            float acc = 0.0f, accg = 0.0f;
-            if (sidx >= 0) {
-                const float *kr = kbase + sidx * qk_ld + h * hd;
-                const float *qr = q_s + h * hd;
-                for (int i = lane; i < hd; i += 32) acc = fmaf(qr[i], __ldg(kr + i), acc);
-            }
-            const float *vr = a.v + e * (int64_t)vrow + h * vhd;
-            const float *gr = g_s + h * vhd;
-            for (int i = lane; i < vhd; i += 32) accg = fmaf(gr[i], __ldg(vr + i), accg);
-            acc = wsum(acc);
-            accg = wsum(accg);
-            if (lane == 0) {
+        if (per_thread) {
+            // short heads: one thread per (edge, head) pair, float4 rows of K and V
+            for (int pr = threadIdx.x; pr < cn * H; pr += kThreads) {
+                const int k = pr / H, h = pr - k * H;
+                const int64_t e = eid_s[k], sidx = sid_s[k];
+                float acc = 0.0f, accg = 0.0f;
+                if (sidx >= 0) {
+                    const float4 *kr = reinterpret_cast<const float4 *>(kbase + sidx * qk_ld + h * hd);
+                    const float4 *qr = reinterpret_cast<const float4 *>(q_s + h * hd);
+#pragma unroll 6
+                    for (int i = 0; i < hd / 4; i++) {
+                        const float4 kv = __ldg(kr + i), qv = qr[i];
+                        acc = fmaf(qv.x, kv.x, fmaf(qv.y, kv.y, fmaf(qv.z, kv.z, fmaf(qv.w, kv.w, acc))));
+                    }
+                }
+                const float4 *vr = reinterpret_cast<const float4 *>(a.v + e * (int64_t)vrow + h * vhd);
+                const float4 *gr = reinterpret_cast<const float4 *>(g_s + h * vhd);
+#pragma unroll 6
+                for (int i = 0; i < vhd / 4; i++) {
+                    const float4 vv = __ldg(vr + i), gv = gr[i];
+                    accg = fmaf(gv.x, vv.x, fmaf(gv.y, vv.y, fmaf(gv.z, vv.z, fmaf(gv.w, vv.w, accg))));
+                }
                 float v = acc * a.scale;
                 if (decay) v -= a.distances[e] / a.decay_scale;
                 x_s[k][h] = v;
                 y_s[k][h] = accg;
                 lg_e[e * H + h] = v;
                 gl_e[e * H + h] = accg;
+            }
+        } else {
+            for (int pr = warp; pr < cn * H; pr += nwarps) {
+                const int k = pr / H, h = pr - k * H;
+                const int64_t e = eid_s[k], sidx = sid_s[k];
+                float acc = 0.0f, accg = 0.0f;
+                if (sidx >= 0) {
+                    const float *kr = kbase + sidx * qk_ld + h * hd;
+                    const float *qr = q_s + h * hd;
+                    for (int i = lane; i < hd; i += 32) acc = fmaf(qr[i], __ldg(kr + i), acc);
+                }
+                const float *vr = a.v + e * (int64_t)vrow + h * vhd;
+                const float *gr = g_s + h * vhd;
+                for (int i = lane; i < vhd; i += 32) accg = fmaf(gr[i], __ldg(vr + i), accg);
+                acc = wsum(acc);
+                accg = wsum(accg);
+                if (lane == 0) {
+                    float v = acc * a.scale;
+                    if (decay) v -= a.distances[e] / a.decay_scale;
+                    x_s[k][h] = v;
+                    y_s[k][h] = accg;
+                    lg_e[e * H + h] = v;
+                    gl_e[e * H + h] = accg;
+                }
             }
         }
         __syncthreads();
@@ -189,9 +223,16 @@ __global__ void __launch_bounds__(kThreads) attn_pool_bwd_dst_kernel(const __gri
         for (int j = threadIdx.x; j < qrow; j += kThreads) {
             const int h = j / hd;
             float acc = gq_s[j];
-            for (int k = 0; k < cn; k++) {
-                const int64_t sidx = sid_s[k];
-                if (sidx >= 0) acc = fmaf(y_s[k][h] * a.scale, __ldg(kbase + sidx * qk_ld + j), acc);
+            for (int k0 = 0; k0 < cn; k0 += 8) {      // 8 K loads in flight per batch
+                float kv[8];
+#pragma unroll
+                for (int u = 0; u < 8; u++) {
+                    const int64_t sidx = k0 + u < cn ? sid_s[k0 + u] : -1;
+                    kv[u] = sidx >= 0 ? __ldg(kbase + sidx * qk_ld + j) : 0.0f;
+                }
+#pragma unroll
+                for (int u = 0; u < 8; u++)
+                    if (k0 + u < cn) acc = fmaf(y_s[k0 + u][h] * a.scale, kv[u], acc);
             }
             gq_s[j] = acc;
         }
@@ -245,9 +286,16 @@ __global__ void __launch_bounds__(kThreads) attn_pool_bwd_src_kernel(const __gri
         for (int j = threadIdx.x; j < qrow; j += kThreads) {
             const int h = j / hd;
             float acc = gk_s[j];
-            for (int k = 0; k < cn; k++) {
-                const int64_t dd = did_s[k];
-                if (dd >= 0) acc = fmaf(gl_s[k][h], __ldg(a.qk + dd * qk_ld + j), acc);
+            for (int k0 = 0; k0 < cn; k0 += 8) {      // 8 Q loads in flight per batch
+                float qv[8];
+#pragma unroll
+                for (int u = 0; u < 8; u++) {
+                    const int64_t dd = k0 + u < cn ? did_s[k0 + u] : -1;
+                    qv[u] = dd >= 0 ? __ldg(a.qk + dd * qk_ld + j) : 0.0f;
+                }
+#pragma unroll
+                for (int u = 0; u < 8; u++)
+                    if (k0 + u < cn) acc = fmaf(gl_s[k0 + u][h], qv[u], acc);
             }
             gk_s[j] = acc;
         }

@@ -270,6 +270,9 @@ attn_pool_kernel(const __grid_constant__ FeqAttnArgs a) {
     const int64_t nsrc = split_k ? a.num_src_nodes : a.num_nodes;
     const float *kbase = split_k ? a.k : a.qk + qrow;
     const int64_t k_ld = split_k ? qrow : 2 * (int64_t)qrow;
+    // float4 V rows: whole float4 per head slice, aligned rows and accumulators
+    const bool v_vec = (vhd & 3) == 0 && (vrow & 3) == 0 && (qrow & 3) == 0 &&
+                       (reinterpret_cast<uintptr_t>(a.v) & 15) == 0;
     // per-thread dot products need 16-byte aligned K rows and head segments
     const bool per_thread = hd <= 128 && (hd & 3) == 0 && (qrow & 3) == 0 &&
                             ((reinterpret_cast<uintptr_t>(kbase) | reinterpret_cast<uintptr_t>(a.qk)) & 15) == 0;
@@ -305,7 +308,7 @@ attn_pool_kernel(const __grid_constant__ FeqAttnArgs a) {
                 if (sidx >= 0) {
                     const float4 *kr = reinterpret_cast<const float4 *>(kbase + sidx * k_ld + h * hd);
                     const float4 *qr = reinterpret_cast<const float4 *>(q_s + h * hd);
-#pragma unroll 2
+#pragma unroll 6
                     for (int i = 0; i < hd / 4; i++) {
                         const float4 kv = __ldg(kr + i), qv = qr[i];
                         acc0 = fmaf(qv.x, kv.x, acc0);
@@ -356,12 +359,51 @@ attn_pool_kernel(const __grid_constant__ FeqAttnArgs a) {
             corr_s[h] = corr;
         }
         __syncthreads();
-        // weighted V accumulation
-        for (int j = threadIdx.x; j < vrow; j += kAttnThreads) {
-            const int h = j / vhd;
-            float acc = acc_s[j] * corr_s[h];
-            for (int k = 0; k < cn; k++) acc = fmaf(lg_s[k][h], __ldg(a.v + eid_s[k] * (int64_t)vrow + j), acc);
-            acc_s[j] = acc;
+        // weighted V accumulation (float4 rows when a head's slice is a whole number of float4)
+        if (v_vec) {
+            const float4 *v4 = reinterpret_cast<const float4 *>(a.v);
+            float4 *acc4 = reinterpret_cast<float4 *>(acc_s);
+            const int vrow4 = vrow / 4;
+            for (int j = threadIdx.x; j < vrow4; j += kAttnThreads) {
+                const int h = (4 * j) / vhd;
+                const float c = corr_s[h];
+                float4 acc = acc4[j];
+                acc.x *= c;
+                acc.y *= c;
+                acc.z *= c;
+                acc.w *= c;
+                // batches of 16 edges (the last one predicated): 16 row loads in flight together
+                for (int k = 0; k < cn; k += 16) {
+                    float4 v[16];
+#pragma unroll
+                    for (int u = 0; u < 16; u++)
+                        v[u] = k + u < cn ? __ldg(v4 + eid_s[k + u] * (int64_t)vrow4 + j) : make_float4(0, 0, 0, 0);
+#pragma unroll
+                    for (int u = 0; u < 16; u++) {
+                        const float p = k + u < cn ? lg_s[k + u][h] : 0.0f;
+                        acc.x = fmaf(p, v[u].x, acc.x);
+                        acc.y = fmaf(p, v[u].y, acc.y);
+                        acc.z = fmaf(p, v[u].z, acc.z);
+                        acc.w = fmaf(p, v[u].w, acc.w);
+                    }
+                }
+                acc4[j] = acc;
+            }
+        } else {
+            for (int j = threadIdx.x; j < vrow; j += kAttnThreads) {
+                const int h = j / vhd;
+                float acc = acc_s[j] * corr_s[h];
+                int k = 0;
+                for (; k + 8 <= cn; k += 8) {
+                    float v[8];
+#pragma unroll
+                    for (int u = 0; u < 8; u++) v[u] = __ldg(a.v + eid_s[k + u] * (int64_t)vrow + j);
+#pragma unroll
+                    for (int u = 0; u < 8; u++) acc = fmaf(lg_s[k + u][h], v[u], acc);
+                }
+                for (; k < cn; k++) acc = fmaf(lg_s[k][h], __ldg(a.v + eid_s[k] * (int64_t)vrow + j), acc);
+                acc_s[j] = acc;
+            }
         }
     }
     __syncthreads();

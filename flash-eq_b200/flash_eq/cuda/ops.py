@@ -458,6 +458,43 @@ def segment_pool_bwd(grad_out, rows, out, dst, perm, offsets, num_nodes, reduce=
     return grows, gw
 
 
+def knn(coords, k, cell=None):
+    """(N, k) int64 indices of the k nearest other points of every point (ascending
+    distance, ties by index; -1 where fewer exist).  ``cell``: the cell side of the search
+    grid (any positive value gives the same result); by default the median k-th neighbour
+    distance of 64 sampled points."""
+    lib = _require_cuda(coords)
+    xyz = _f32(coords, "coordinates")
+    if xyz.dim() != 2 or xyz.shape[1] != 3:
+        raise ValueError("coordinates must have shape (N, 3)")
+    N = xyz.shape[0]
+    k = int(k)
+    if not 1 <= k <= 64:
+        raise ValueError("k must be in [1, 64]")
+    nbr = torch.full((N, k), -1, dtype=torch.int64, device=xyz.device)
+    if N < 2:
+        return nbr
+    lo = xyz.min(dim=0).values
+    if cell is None:
+        g = torch.Generator(device="cpu").manual_seed(0)
+        sample = xyz[torch.randint(0, N, (min(64, N),), generator=g).to(xyz.device)]
+        kk = min(k + 1, N)
+        kth = torch.cdist(sample, xyz).topk(kk, dim=1, largest=False).values[:, -1]
+        cell = float(kth.median())
+        if not cell > 0.0:
+            span = float((xyz.max(dim=0).values - lo).max())
+            cell = span if span > 0.0 else 1.0
+    status = torch.zeros(1, dtype=torch.int32, device=xyz.device)
+    ws = _workspace(lib.feq_knn_workspace_bytes(N), xyz.device)
+    x0, y0, z0 = (float(v) for v in lo.tolist())
+    rc = lib.feq_knn_graph(_p(xyz), N, k, float(cell), x0, y0, z0, _p(nbr), _p(status), _p(ws), ws.numel(),
+                           _stream(xyz.device))
+    _lib.check(rc, "feq_knn_graph")
+    if int(status.item()) != 0:
+        raise RuntimeError("feq_knn_graph: search stopped before it was exact (cell too small)")
+    return nbr
+
+
 # ---------------------------------------------------------------------------
 # Node-level operators (forward)
 # ---------------------------------------------------------------------------

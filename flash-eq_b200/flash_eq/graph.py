@@ -56,6 +56,21 @@ class Graph:
         dst = torch.randint(0, num_nodes, (num_edges,), device=device)
         return Graph(src=src, dst=dst, num_nodes=num_nodes)
 
+    @staticmethod
+    def knn(coordinates: torch.Tensor, k: int) -> "Graph":
+        """k-nearest-neighbour graph on the GPU (no counterpart in the reference): edges
+        src -> dst where src ranges over the k nearest other nodes of dst, grouped by dst."""
+        from .cuda import ops
+
+        nbr = ops.knn(coordinates, k)
+        n = coordinates.shape[0]
+        dst = torch.arange(n, device=coordinates.device).repeat_interleave(k)
+        src = nbr.reshape(-1)
+        keep = src >= 0
+        if not bool(keep.all()):
+            src, dst = src[keep], dst[keep]
+        return Graph(src=src, dst=dst, num_nodes=n)
+
     # -- dst-sorted view ----------------------------------------------------
     def _check_src(self):
         """Device bool: some src index lies outside [0, num_nodes) (None without edges)."""

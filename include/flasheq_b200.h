@@ -405,6 +405,20 @@ int feq_node_linear(const float *x, int64_t num_nodes, int32_t c_in, int32_t c_o
 int feq_node_gate(const float *x, const float *z, int64_t num_nodes, int32_t C, const int32_t *lvals,
                   int32_t n_lvals, float *out, feq_stream_t stream);
 
+/* ---------------------------------------------------------------------------
+ * k-nearest-neighbour graph construction (no counterpart in the reference, which leaves
+ * graph building to the user; its examples use torch.cdist + topk).  xyz (N, 3) float32;
+ * nbr (N, k) int64: the k nearest other points of every point by Euclidean distance,
+ * ascending (ties by index), -1 when fewer than k exist.  Points are binned into cubic
+ * cells of side `cell` with corner (x0, y0, z0) (any cell > 0 gives the exact result;
+ * about the k-th neighbour distance is fastest); status (may be NULL) is set to 1 when a
+ * point's search stopped before it was exact (cell far smaller than the point spacing).
+ * 1 <= k <= 64, N < 2^31.
+ * ------------------------------------------------------------------------ */
+size_t feq_knn_workspace_bytes(int64_t num_points);
+int feq_knn_graph(const float *xyz, int64_t num_points, int32_t k, float cell, float x0, float y0, float z0,
+                  int64_t *nbr, int32_t *status, void *workspace, size_t workspace_bytes, feq_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
