@@ -372,14 +372,14 @@ attn_pool_kernel(const __grid_constant__ FeqAttnArgs a) {
                 acc.y *= c;
                 acc.z *= c;
                 acc.w *= c;
-                // batches of 16 edges (the last one predicated): 16 row loads in flight together
-                for (int k = 0; k < cn; k += 16) {
-                    float4 v[16];
+                // batches of 8 edges (the last one predicated): 8 row loads in flight together
+                for (int k = 0; k < cn; k += 8) {
+                    float4 v[8];
 #pragma unroll
-                    for (int u = 0; u < 16; u++)
+                    for (int u = 0; u < 8; u++)
                         v[u] = k + u < cn ? __ldg(v4 + eid_s[k + u] * (int64_t)vrow4 + j) : make_float4(0, 0, 0, 0);
 #pragma unroll
-                    for (int u = 0; u < 16; u++) {
+                    for (int u = 0; u < 8; u++) {
                         const float p = k + u < cn ? lg_s[k + u][h] : 0.0f;
                         acc.x = fmaf(p, v[u].x, acc.x);
                         acc.y = fmaf(p, v[u].y, acc.y);

@@ -43,10 +43,17 @@ def test_knn_matches_brute_force(cuda_device, kind, n, k):
     assert (nbr[:, kk:] == -1).all()
     got = nbr[:, :kk]
     gd = (xyz.double()[got] - xyz.double()[:, None, :]).norm(dim=-1)
-    # same distances in the same order; the indices agree except between exactly equal distances
+    # same distances in the same order (float32 vs float64 distances may order near-equal
+    # pairs differently, e.g. the two chain neighbours of a random walk, both 3.8 A away) ...
     assert torch.allclose(gd, dist, rtol=1e-6, atol=1e-6)
-    same = got == idx
-    assert same.float().mean() > 0.999
+    # ... and the same neighbour sets, except where the k-th distance ties the next one
+    if n - 1 > kk:
+        dnext = _brute(xyz, kk + 1)[0][:, -1]
+        tie = (dnext - dist[:, -1]).abs() <= 1e-5 * dist[:, -1].clamp(min=1e-6)
+    else:
+        tie = torch.zeros(n, dtype=torch.bool)
+    sets_equal = (got.sort(dim=1).values == idx.sort(dim=1).values).all(dim=1)
+    assert bool((sets_equal | tie).all())
 
 
 def test_knn_graph_matches_cdist_convention(cuda_device):
@@ -55,7 +62,7 @@ def test_knn_graph_matches_cdist_convention(cuda_device):
     _, idx = _brute(xyz, 16)
     assert gr.num_edges == 2000 * 16
     assert torch.equal(gr.dst.cpu(), torch.arange(2000).repeat_interleave(16))
-    assert (gr.src.cpu().view(2000, 16) == idx).float().mean() > 0.999
+    assert (gr.src.cpu().view(2000, 16).sort(dim=1).values == idx.sort(dim=1).values).float().mean() > 0.999
 
 
 def test_knn_cell_size_does_not_change_result(cuda_device):
