@@ -287,154 +287,54 @@ __global__ void __launch_bounds__(kNodeWarps * 32) gate_kernel(const __grid_cons
 }
 
 // ---------------------------------------------------------------------------
-// EquivariantLinear (flash_eq/layers/linear.py:172-268):
-//   y[n, co, p] = sum_ci W[irrep(p) * Cout + co, ci] x[n, ci, p]  (+ bias[co, s] at the
-//   s-th l = 0 position).  The reference multiplies every irrep's weight block with every
-//   position and gathers; here each position only meets its own irrep's block.
-// CTA = 4096 / Cout nodes.  Per irrep r the x tile is re-laid in shared memory as a
-// (Cin x nodes * K_r) matrix whose columns are the (node, position) pairs of the irrep,
-// and the weight block
-// W_r^T as (Cin x Cout): the irrep's product is one small GEMM.  Thread = 4 consecutive
-// output channels x K_r quads of 4 consecutive columns; per input channel one float4
-// weight load and K_r float4 x loads feed 16 K_r FMAs.  Float32 CUDA-core FMAs, results
-// stored straight to y.
+// Position-major layout for EquivariantLinear (flash_eq/layers/linear.py:172-268):
+// xt[p][n][c] = x[n][c][p].  Each irrep's positions p = off .. off + 2l are then one
+// contiguous ((2l+1) N x C) matrix and its channel mix y = W_r x a single plain GEMM
+// (a library SGEMM, 1 / nreps of the reference's FLOPs: the reference multiplies every
+// irrep's weight block with every position and gathers).  CTA = 8 nodes: the node rows
+// are read contiguously into shared memory and each position's (8 x C) slab written
+// contiguously (and the reverse on the way back, with the bias added).
 // ---------------------------------------------------------------------------
-constexpr int kLinThreads = 256;
+constexpr int kPmNodes = 8;
 
-struct LinArgs {
-    NodeRepr R;                    // input and output share the degrees
-    int Cin, Cout;
-    int8_t scalar_idx[kNodeMaxIrreps];   // irrep -> bias column (-1: not a scalar irrep)
-    int nscalar;
-    const float *x, *w, *bias;
-    float *y;
-    int64_t N;
-};
-
-// QPT column quads per thread, starting at quad q0 + g (the thread's group g), K = 2l+1.
-template <int K, int QPT>
-__device__ __forceinline__ void lin_gemm(const LinArgs &a, const float *xs, const float *wt, int wld, int tn,
-                                         int64_t n0, int n_nodes, int r, int q0) {
-    const int Cin = a.Cin, Cout = a.Cout, d = a.R.d, off = a.R.irr_off[r];
-    const int ncol = tn * K;                       // columns: (node, position) pairs, node-major
-    const int nq4 = Cout / 4, groups = kLinThreads / nq4;
-    const int t = threadIdx.x, cq = t % nq4, g = t / nq4;
-    const int sb = a.scalar_idx[r];
-    float acc[QPT][4][4];
-#pragma unroll
-    for (int u = 0; u < QPT; u++)
-#pragma unroll
-        for (int c = 0; c < 4; c++)
-#pragma unroll
-            for (int j = 0; j < 4; j++) acc[u][c][j] = 0.0f;
-    const float *wp = wt + 4 * cq;
-    const float *xp = xs + 4 * (q0 + g);
-#pragma unroll 2
-    for (int ci = 0; ci < Cin; ci++, wp += wld, xp += ncol) {
-        const float4 w = *reinterpret_cast<const float4 *>(wp);
-#pragma unroll
-        for (int u = 0; u < QPT; u++) {
-            const float4 xv = *reinterpret_cast<const float4 *>(xp + 4 * u * groups);
-            const float xa[4] = {xv.x, xv.y, xv.z, xv.w};
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                acc[u][0][j] = fmaf(w.x, xa[j], acc[u][0][j]);
-                acc[u][1][j] = fmaf(w.y, xa[j], acc[u][1][j]);
-                acc[u][2][j] = fmaf(w.z, xa[j], acc[u][2][j]);
-                acc[u][3][j] = fmaf(w.w, xa[j], acc[u][3][j]);
-            }
-        }
-    }
-    float b[4];
-#pragma unroll
-    for (int c = 0; c < 4; c++) b[c] = sb >= 0 ? a.bias[(4 * cq + c) * a.nscalar + sb] : 0.0f;
-    float *yb = a.y + (n0 * Cout + 4 * cq) * d + off;
-#pragma unroll
-    for (int u = 0; u < QPT; u++) {
-        const int col0 = 4 * (q0 + g + u * groups);
-#pragma unroll
-        for (int j = 0; j < 4; j++) {
-            const int col = col0 + j, node = col / K, m = col - node * K;   // K constant: no division
-            if (node >= n_nodes) continue;
-            float *yr = yb + (int64_t)node * Cout * d + m;
-#pragma unroll
-            for (int c = 0; c < 4; c++) yr[c * d] = acc[u][c][j] + b[c];
-        }
+__global__ void __launch_bounds__(256) to_posmajor_kernel(const float *__restrict__ x, int64_t N, int C, int d,
+                                                          float *__restrict__ xt) {
+    extern __shared__ float tsm[];
+    const int64_t n0 = (int64_t)blockIdx.x * kPmNodes;
+    const int nn = (int)min64(kPmNodes, N - n0);
+    const int tile = nn * C * d;
+    const float *src = x + n0 * C * d;
+    for (int i = threadIdx.x; i < tile; i += blockDim.x) tsm[i] = __ldg(src + i);
+    __syncthreads();
+    const int slab = nn * C;                 // (nodes x channels) of one position
+    for (int i = threadIdx.x; i < d * slab; i += blockDim.x) {
+        const int p = i / slab, r = i - p * slab;      // r = node * C + c
+        xt[(int64_t)p * N * C + n0 * C + r] = tsm[r * d + p];
     }
 }
 
-// One irrep of 2l+1 = K positions: re-lay its x columns, then the GEMM in passes of <= 5 quads.
-template <int K>
-__device__ __forceinline__ void lin_irrep(const LinArgs &a, float *xs, const float *wt, int wld, int tn,
-                                          const float *xg, int64_t n0, int n_nodes, int r) {
-    const int Cin = a.Cin, d = a.R.d, off = a.R.irr_off[r], ncol = tn * K;
-    // xs[ci][node * K + m] = x[n0 + node, ci, off + m], a batch of loads per thread before the stores
-    constexpr int kB = 8;
-    for (int i0 = threadIdx.x; i0 < Cin * ncol; i0 += kLinThreads * kB) {
-        float v[kB];
-#pragma unroll
-        for (int u = 0; u < kB; u++) {
-            const int i = i0 + u * kLinThreads;
-            const int ci = i / ncol, col = i - ci * ncol, node = col / K, m = col - node * K;
-            v[u] = (i < Cin * ncol && node < n_nodes) ? __ldg(xg + ((int64_t)node * Cin + ci) * d + off + m) : 0.0f;
-        }
-#pragma unroll
-        for (int u = 0; u < kB; u++) {
-            const int i = i0 + u * kLinThreads;
-            if (i < Cin * ncol) xs[i] = v[u];
-        }
+// y[n][c][p] = yt[p][n][c] (+ bias[c, s] at the s-th scalar position)
+__global__ void __launch_bounds__(256) from_posmajor_kernel(const float *__restrict__ yt, int64_t N, int C, int d,
+                                                            const float *__restrict__ bias, int nscalar,
+                                                            const int8_t *__restrict__ scalar_idx_d,
+                                                            float *__restrict__ y) {
+    extern __shared__ float tsm[];
+    __shared__ int8_t sidx[kMaxDim];
+    for (int p = threadIdx.x; p < d; p += blockDim.x) sidx[p] = scalar_idx_d ? scalar_idx_d[p] : (int8_t)-1;
+    const int64_t n0 = (int64_t)blockIdx.x * kPmNodes;
+    const int nn = (int)min64(kPmNodes, N - n0);
+    const int slab = nn * C;
+    __syncthreads();
+    for (int i = threadIdx.x; i < d * slab; i += blockDim.x) {
+        const int p = i / slab, r = i - p * slab;
+        float v = __ldg(yt + (int64_t)p * N * C + n0 * C + r);
+        const int sb = sidx[p];
+        if (bias && sb >= 0) v += __ldg(bias + (r % C) * nscalar + sb);
+        tsm[r * d + p] = v;
     }
     __syncthreads();
-    const int groups = kLinThreads / (a.Cout / 4);
-    // K * groups column quads: each group takes K of them
-    if constexpr (K <= 5) {
-        lin_gemm<K, K>(a, xs, wt, wld, tn, n0, n_nodes, r, 0);
-    } else {
-        lin_gemm<K, 5>(a, xs, wt, wld, tn, n0, n_nodes, r, 0);
-        lin_gemm<K, K - 5>(a, xs, wt, wld, tn, n0, n_nodes, r, 5 * groups);
-    }
-}
-
-__global__ void __launch_bounds__(kLinThreads, 1) node_linear_kernel(const __grid_constant__ LinArgs a) {
-    extern __shared__ float lsm[];
-    const int Cin = a.Cin, Cout = a.Cout, d = a.R.d;
-    const int wld = Cout + 4;
-    const int nq4 = Cout / 4, groups = kLinThreads / nq4, tn = 4 * groups;   // nodes of this CTA
-    float *wt = lsm;                                   // Cin x (Cout + 4)
-    float *xs = wt + (size_t)Cin * wld;                // Cin x (tn K_r) for the current irrep
-    const int64_t n0 = (int64_t)blockIdx.x * tn;
-    const int n_nodes = (int)min64(tn, a.N - n0);
-    const float *xg = a.x + n0 * Cin * d;
-    for (int r = 0; r < a.R.n_irreps; r++) {
-        __syncthreads();   // the previous irrep's tiles are no longer read
-        const float *wr = a.w + (int64_t)r * Cout * Cin;
-        constexpr int kV = 8;
-        for (int i0 = threadIdx.x * 4; i0 < Cout * Cin; i0 += kLinThreads * 4 * kV) {
-            float4 v[kV];
-#pragma unroll
-            for (int u = 0; u < kV; u++) {
-                const int i = i0 + u * kLinThreads * 4;
-                v[u] = i < Cout * Cin ? __ldg(reinterpret_cast<const float4 *>(wr + i)) : make_float4(0, 0, 0, 0);
-            }
-#pragma unroll
-            for (int u = 0; u < kV; u++) {
-                const int i = i0 + u * kLinThreads * 4;
-                if (i >= Cout * Cin) break;
-                const int co = i / Cin, ci = i - co * Cin;     // Cin % 4 == 0: the 4 share co
-                wt[ci * wld + co] = v[u].x;
-                wt[(ci + 1) * wld + co] = v[u].y;
-                wt[(ci + 2) * wld + co] = v[u].z;
-                wt[(ci + 3) * wld + co] = v[u].w;
-            }
-        }
-        switch (a.R.irr_l[r]) {
-            case 0: lin_irrep<1>(a, xs, wt, wld, tn, xg, n0, n_nodes, r); break;
-            case 1: lin_irrep<3>(a, xs, wt, wld, tn, xg, n0, n_nodes, r); break;
-            case 2: lin_irrep<5>(a, xs, wt, wld, tn, xg, n0, n_nodes, r); break;
-            case 3: lin_irrep<7>(a, xs, wt, wld, tn, xg, n0, n_nodes, r); break;
-            default: lin_irrep<9>(a, xs, wt, wld, tn, xg, n0, n_nodes, r); break;
-        }
-    }
+    float *dst = y + n0 * C * d;
+    for (int i = threadIdx.x; i < slab * d; i += blockDim.x) dst[i] = tsm[i];
 }
 
 int fill_node_repr(const int32_t *lvals, int32_t n, int32_t C, NodeRepr *R) {
@@ -555,37 +455,35 @@ int feq_node_rep_norm(const float *x, int64_t num_nodes, int32_t C, const int32_
     return FEQ_OK;
 }
 
-int feq_node_linear(const float *x, int64_t num_nodes, int32_t c_in, int32_t c_out, const int32_t *lvals,
-                    int32_t n_lvals, const float *weight, const float *bias, float *y, feq_stream_t stream) {
-    LinArgs a;
-    memset(&a, 0, sizeof(a));
-    int rc = fill_node_repr(lvals, n_lvals, c_in, &a.R);
-    if (rc != FEQ_OK) return rc;
-    if (num_nodes < 0 || c_out < 1) return FEQ_ERR_INVALID_ARGUMENT;
+int feq_node_to_posmajor(const float *x, int64_t num_nodes, int32_t C, int32_t d, float *xt, feq_stream_t stream) {
+    if (num_nodes < 0 || C < 1 || d < 1 || d > kMaxDim) return FEQ_ERR_INVALID_ARGUMENT;
     if (num_nodes == 0) return FEQ_OK;
-    if (!x || !weight || !y) return FEQ_ERR_INVALID_ARGUMENT;
-    // channel quads must tile the threads (Cout in 4 .. 1024, a power-of-two multiple of 4)
-    if (c_in % 4 || c_out % 4 || c_out > 1024 || kLinThreads % (c_out / 4) || (reinterpret_cast<uintptr_t>(weight) & 15))
-        return FEQ_ERR_UNSUPPORTED;
-    int kmax = 1;
-    for (int r = 0; r < n_lvals; r++) {
-        if (lvals[r] > 4) return FEQ_ERR_UNSUPPORTED;
-        a.scalar_idx[r] = -1;
-        if (lvals[r] == 0 && bias) a.scalar_idx[r] = (int8_t)a.nscalar++;
-        kmax = std::max(kmax, 2 * lvals[r] + 1);
-    }
-    a.Cin = c_in;
-    a.Cout = c_out;
-    a.x = x;
-    a.w = weight;
-    a.bias = bias;
-    a.y = y;
-    a.N = num_nodes;
-    const int tn = 4 * (kLinThreads / (c_out / 4));
-    const size_t smem = sizeof(float) * ((size_t)c_in * (c_out + 4) + (size_t)c_in * tn * kmax);
-    if ((rc = set_smem((const void *)node_linear_kernel, smem)) != FEQ_OK) return rc;
-    ProfScope ps("node_linear", (cudaStream_t)stream);
-    node_linear_kernel<<<(unsigned)((num_nodes + tn - 1) / tn), kLinThreads, smem, (cudaStream_t)stream>>>(a);
+    if (!x || !xt) return FEQ_ERR_INVALID_ARGUMENT;
+    const size_t smem = sizeof(float) * kPmNodes * (size_t)C * d;
+    int rc;
+    if ((rc = set_smem((const void *)to_posmajor_kernel, smem)) != FEQ_OK) return rc;
+    ProfScope ps("node_layout", (cudaStream_t)stream);
+    to_posmajor_kernel<<<(unsigned)((num_nodes + kPmNodes - 1) / kPmNodes), 256, smem, (cudaStream_t)stream>>>(
+        x, num_nodes, C, d, xt);
+    FEQ_LAUNCH_CHECK();
+    return FEQ_OK;
+}
+
+int feq_node_from_posmajor(const float *yt, int64_t num_nodes, int32_t C, const int32_t *lvals, int32_t n_lvals,
+                           const float *bias, const int8_t *scalar_index, float *y, feq_stream_t stream) {
+    NodeRepr R;
+    int rc = fill_node_repr(lvals, n_lvals, C, &R);
+    if (rc != FEQ_OK) return rc;
+    if (num_nodes < 0) return FEQ_ERR_INVALID_ARGUMENT;
+    if (num_nodes == 0) return FEQ_OK;
+    if (!yt || !y || (bias && !scalar_index)) return FEQ_ERR_INVALID_ARGUMENT;
+    int nscalar = 0;
+    for (int r = 0; r < n_lvals; r++) nscalar += lvals[r] == 0;
+    const size_t smem = sizeof(float) * kPmNodes * (size_t)C * R.d;
+    if ((rc = set_smem((const void *)from_posmajor_kernel, smem)) != FEQ_OK) return rc;
+    ProfScope ps("node_layout", (cudaStream_t)stream);
+    from_posmajor_kernel<<<(unsigned)((num_nodes + kPmNodes - 1) / kPmNodes), 256, smem, (cudaStream_t)stream>>>(
+        yt, num_nodes, C, R.d, bias, nscalar, scalar_index, y);
     FEQ_LAUNCH_CHECK();
     return FEQ_OK;
 }

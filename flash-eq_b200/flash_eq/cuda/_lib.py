@@ -116,8 +116,9 @@ SIGNATURES = {
                                           ctypes.c_float, ctypes.c_float, ctypes.c_float, c_vp, c_vp]),
     "feq_node_rep_norm": (ctypes.c_int, [c_vp, ctypes.c_int64, ctypes.c_int32, c_i32p, ctypes.c_int32, ctypes.c_float,
                                          c_vp, c_vp]),
-    "feq_node_linear": (ctypes.c_int, [c_vp, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, c_i32p, ctypes.c_int32,
-                                       c_vp, c_vp, c_vp, c_vp]),
+    "feq_node_to_posmajor": (ctypes.c_int, [c_vp, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, c_vp, c_vp]),
+    "feq_node_from_posmajor": (ctypes.c_int, [c_vp, ctypes.c_int64, ctypes.c_int32, c_i32p, ctypes.c_int32, c_vp,
+                                              c_vp, c_vp, c_vp]),
     "feq_knn_workspace_bytes": (ctypes.c_size_t, [ctypes.c_int64]),
     "feq_knn_graph": (ctypes.c_int, [c_vp, ctypes.c_int64, ctypes.c_int32, ctypes.c_float, ctypes.c_float,
                                      ctypes.c_float, ctypes.c_float, c_vp, c_vp, c_vp, ctypes.c_size_t, c_vp]),

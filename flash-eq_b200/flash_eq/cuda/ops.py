@@ -545,18 +545,32 @@ def node_rep_norm(x, lvals, eps):
     return norms.view(*x.shape[:-1], n)
 
 
-def node_linear(x, lvals, weight, bias, c_out):
-    """EquivariantLinear forward (identity activation): (..., Cin, d) -> (..., Cout, d)."""
+def node_linear(x, lvals, weight, bias, c_out, scalar_index):
+    """EquivariantLinear forward (identity activation): (..., Cin, d) -> (..., Cout, d).
+    Position-major layout kernels around one library GEMM per irrep; ``scalar_index``:
+    (d,) int8 device tensor, position -> bias column (-1 elsewhere)."""
     lib = _require_cuda(x, weight, bias)
     rows = _node_rows(x, "features")
-    w = _f32(weight, "weight")
-    b = None if bias is None else _f32(bias, "bias")
-    y = torch.empty(rows.shape[0], int(c_out), rows.shape[2], dtype=torch.float32, device=rows.device)
+    N, cin, d = rows.shape
+    cout = int(c_out)
+    dev = rows.device
+    xt = torch.empty(d, N, cin, dtype=torch.float32, device=dev)
+    rc = lib.feq_node_to_posmajor(_p(rows), N, cin, d, _p(xt), _stream(dev))
+    _lib.check(rc, "feq_node_to_posmajor")
+    yt = torch.empty(d, N, cout, dtype=torch.float32, device=dev)
+    w = _f32(weight, "weight").view(len(lvals), cout, cin)
+    off = 0
+    for r, l in enumerate(lvals):
+        k = 2 * int(l) + 1
+        torch.matmul(xt[off:off + k].view(k * N, cin), w[r].t(), out=yt[off:off + k].view(k * N, cout))
+        off += k
+    y = torch.empty(N, cout, d, dtype=torch.float32, device=dev)
     arr, n = _lib.i32_array(lvals)
-    rc = lib.feq_node_linear(_p(rows), rows.shape[0], rows.shape[1], int(c_out), arr, n, _p(w), _p(b), _p(y),
-                             _stream(rows.device))
-    _lib.check(rc, "feq_node_linear")
-    return y.view(*x.shape[:-2], int(c_out), x.shape[-1])
+    b = None if bias is None else _f32(bias, "bias")
+    rc = lib.feq_node_from_posmajor(_p(yt), N, cout, arr, n, _p(b), _p(scalar_index) if b is not None else None,
+                                    _p(y), _stream(dev))
+    _lib.check(rc, "feq_node_from_posmajor")
+    return y.view(*x.shape[:-2], cout, d)
 
 
 def node_gate(x, z, lvals):

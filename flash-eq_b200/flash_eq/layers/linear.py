@@ -10,8 +10,9 @@ handles) for the same directions, the kernel rebuilds their blocks from the
 directions and never reads the dense matrices; any other P / Q is applied as a
 dense matrix exactly like the reference's bmm.
 
-``EquivariantLinear`` (linear.py:172-268) is node-level: a native per-irrep kernel on the
-inference path (csrc/feq_node.cu), one batched GEMM over positions under autograd.
+``EquivariantLinear`` (linear.py:172-268) is node-level: on the inference path native
+position-major layout kernels (csrc/feq_node.cu) around one library GEMM per irrep; under
+autograd one batched GEMM over positions.
 """
 from __future__ import annotations
 
@@ -136,10 +137,12 @@ class EquivariantLinear(nn.Module):
         self.bias = nn.Parameter(torch.zeros(out_repr.mult, nscalar)) if (nscalar > 0 and bias) else None
         self.activation = activation if activation is not None else nn.Identity()
         self._lvals = tuple(in_repr.lvals.tolist())
-        # the native kernel: identity activation, degrees <= 4, channel counts in quads
-        self._native_ok = (isinstance(self.activation, nn.Identity) and max(self._lvals) <= 4
-                           and in_repr.mult % 4 == 0 and out_repr.mult % 4 == 0 and out_repr.mult <= 1024
-                           and 256 % (out_repr.mult // 4) == 0)
+        # inference path: position-major layout kernels around one GEMM per irrep (identity activation)
+        self._native_ok = isinstance(self.activation, nn.Identity)
+        pos_ix = torch.full((in_repr.dim(),), -1, dtype=torch.int8)
+        for s_i, loc in enumerate(self.scalar_locs):
+            pos_ix[loc] = s_i
+        self.register_buffer("_pos_scalar_ix", pos_ix, persistent=False)
 
     def forward(self, f: torch.Tensor) -> torch.Tensor:
         """out[..., co, p] = sum_ci W_{irrep(p)}[co, ci] f[..., ci, p] (+ bias on l = 0 positions).
@@ -152,7 +155,7 @@ class EquivariantLinear(nn.Module):
         nreps = self.outdims[0]
         cout = self.expanddims[1]
         if self._native_ok and native_node_ok(f, self.weight, self.bias):
-            return ops.node_linear(f, self._lvals, self.weight, self.bias, cout)
+            return ops.node_linear(f, self._lvals, self.weight, self.bias, cout, self._pos_scalar_ix)
         x = f.reshape(-1, cin, d)
         w = self.weight.view(nreps, cout, cin).index_select(0, self.indices)    # (d, Cout, Cin)
         y = torch.bmm(w, x.permute(2, 1, 0))                                     # (d, Cout, N)

@@ -394,12 +394,14 @@ int feq_node_layernorm(const float *x, int64_t num_nodes, int32_t C, const int32
 /* RepNorm (norm.py:19-64): norms (N, C, n_lvals) = sqrt(sum over each irrep of x^2 + eps). */
 int feq_node_rep_norm(const float *x, int64_t num_nodes, int32_t C, const int32_t *lvals, int32_t n_lvals,
                       float eps, float *norms, feq_stream_t stream);
-/* EquivariantLinear (linear.py:172-268), identity activation:
- *   y[n, co, p] = sum_ci weight[irrep(p) * c_out + co, ci] x[n, ci, p] (+ bias[co, s] at the
- *   s-th l = 0 irrep when bias != NULL; bias (c_out, n_scalar)).  x (N, c_in, d),
- *   y (N, c_out, d), weight (n_lvals * c_out, c_in); degrees <= 4. */
-int feq_node_linear(const float *x, int64_t num_nodes, int32_t c_in, int32_t c_out, const int32_t *lvals,
-                    int32_t n_lvals, const float *weight, const float *bias, float *y, feq_stream_t stream);
+/* EquivariantLinear (linear.py:172-268) in three steps: feq_node_to_posmajor
+ * (xt[p][n][c] = x[n][c][p], xt (d, N, C)); one plain GEMM per irrep on the contiguous
+ * rows p = off .. off + 2l of xt (the caller's BLAS: y_r = x_r W_r^T); feq_node_from_posmajor
+ * (y[n][c][p] = yt[p][n][c] + bias[c, scalar_index[p]] where scalar_index[p] >= 0; bias
+ * (C, n_scalar) and scalar_index (d,) int8 device arrays, both NULL for no bias). */
+int feq_node_to_posmajor(const float *x, int64_t num_nodes, int32_t C, int32_t d, float *xt, feq_stream_t stream);
+int feq_node_from_posmajor(const float *yt, int64_t num_nodes, int32_t C, const int32_t *lvals, int32_t n_lvals,
+                           const float *bias, const int8_t *scalar_index, float *y, feq_stream_t stream);
 /* EquivariantGating's gate (gating.py:17-76): out = x * sigmoid(z)[c, irrep of the
  * position], z (N, C * n_lvals) the pre-activation. */
 int feq_node_gate(const float *x, const float *z, int64_t num_nodes, int32_t C, const int32_t *lvals,
