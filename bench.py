@@ -729,7 +729,9 @@ def run_block(args):
         step()
     clk = ClockSampler(gpu_index_for(local))
     clk.start()
+    torch.cuda.profiler.start()      # lets `ncu --profile-from-start off` capture just the timed steps
     ms = timed(step, args.steps)
+    torch.cuda.profiler.stop()
     launches = per_replay * args.steps
     clocks = clk.stop()
     ms_eager = timed(eager, max(3, args.steps // 4))

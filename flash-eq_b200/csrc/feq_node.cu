@@ -291,50 +291,79 @@ __global__ void __launch_bounds__(kNodeWarps * 32) gate_kernel(const __grid_cons
 // xt[p][n][c] = x[n][c][p].  Each irrep's positions p = off .. off + 2l are then one
 // contiguous ((2l+1) N x C) matrix and its channel mix y = W_r x a single plain GEMM
 // (a library SGEMM, 1 / nreps of the reference's FLOPs: the reference multiplies every
-// irrep's weight block with every position and gathers).  CTA = 8 nodes: the node rows
+// irrep's weight block with every position and gathers).  CTA = up to 16 nodes: the node rows
 // are read contiguously into shared memory and each position's (8 x C) slab written
 // contiguously (and the reverse on the way back, with the bias added).
 // ---------------------------------------------------------------------------
-constexpr int kPmNodes = 8;
+constexpr int kPmNodes = 16;
+
+// nodes per CTA: up to 16, as many as fit 96 KB of shared memory
+inline int pm_nodes(int C, int d) {
+    return (int)std::min<int64_t>(kPmNodes, (int64_t)(96 * 1024) / ((int64_t)C * d * 4));
+}
+
+// the (nodes x C x d) tile of this CTA into shared memory, float4 when aligned
+__device__ __forceinline__ void pm_load_tile(float *tsm, const float *src, int tile) {
+    if ((tile & 3) == 0 && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+        const float4 *s4 = reinterpret_cast<const float4 *>(src);
+        float4 *t4 = reinterpret_cast<float4 *>(tsm);
+        for (int i = threadIdx.x; i < tile / 4; i += blockDim.x) t4[i] = __ldg(s4 + i);
+    } else {
+        for (int i = threadIdx.x; i < tile; i += blockDim.x) tsm[i] = __ldg(src + i);
+    }
+}
 
 __global__ void __launch_bounds__(256) to_posmajor_kernel(const float *__restrict__ x, int64_t N, int C, int d,
-                                                          float *__restrict__ xt) {
+                                                          int tn, float *__restrict__ xt) {
     extern __shared__ float tsm[];
-    const int64_t n0 = (int64_t)blockIdx.x * kPmNodes;
-    const int nn = (int)min64(kPmNodes, N - n0);
-    const int tile = nn * C * d;
-    const float *src = x + n0 * C * d;
-    for (int i = threadIdx.x; i < tile; i += blockDim.x) tsm[i] = __ldg(src + i);
+    const int64_t n0 = (int64_t)blockIdx.x * tn;
+    const int nn = (int)min64(tn, N - n0);
+    pm_load_tile(tsm, x + n0 * C * d, nn * C * d);
     __syncthreads();
-    const int slab = nn * C;                 // (nodes x channels) of one position
-    for (int i = threadIdx.x; i < d * slab; i += blockDim.x) {
-        const int p = i / slab, r = i - p * slab;      // r = node * C + c
-        xt[(int64_t)p * N * C + n0 * C + r] = tsm[r * d + p];
+    const int slab = nn * C;                 // (nodes x channels) of one position, a multiple of 4
+    for (int p = 0; p < d; p++) {
+        float4 *dst = reinterpret_cast<float4 *>(xt + (int64_t)p * N * C + n0 * C);
+        for (int r = 4 * threadIdx.x; r < slab; r += 4 * blockDim.x)     // r = node * C + c
+            dst[r / 4] = make_float4(tsm[r * d + p], tsm[(r + 1) * d + p], tsm[(r + 2) * d + p], tsm[(r + 3) * d + p]);
     }
 }
 
 // y[n][c][p] = yt[p][n][c] (+ bias[c, s] at the s-th scalar position)
 __global__ void __launch_bounds__(256) from_posmajor_kernel(const float *__restrict__ yt, int64_t N, int C, int d,
                                                             const float *__restrict__ bias, int nscalar,
-                                                            const int8_t *__restrict__ scalar_idx_d,
+                                                            const int8_t *__restrict__ scalar_idx_d, int tn,
                                                             float *__restrict__ y) {
     extern __shared__ float tsm[];
-    __shared__ int8_t sidx[kMaxDim];
-    for (int p = threadIdx.x; p < d; p += blockDim.x) sidx[p] = scalar_idx_d ? scalar_idx_d[p] : (int8_t)-1;
-    const int64_t n0 = (int64_t)blockIdx.x * kPmNodes;
-    const int nn = (int)min64(kPmNodes, N - n0);
+    const int64_t n0 = (int64_t)blockIdx.x * tn;
+    const int nn = (int)min64(tn, N - n0);
     const int slab = nn * C;
-    __syncthreads();
-    for (int i = threadIdx.x; i < d * slab; i += blockDim.x) {
-        const int p = i / slab, r = i - p * slab;
-        float v = __ldg(yt + (int64_t)p * N * C + n0 * C + r);
-        const int sb = sidx[p];
-        if (bias && sb >= 0) v += __ldg(bias + (r % C) * nscalar + sb);
-        tsm[r * d + p] = v;
+    for (int p = 0; p < d; p++) {
+        const float4 *src = reinterpret_cast<const float4 *>(yt + (int64_t)p * N * C + n0 * C);
+        const int sb = (bias && scalar_idx_d) ? scalar_idx_d[p] : -1;
+        for (int r = 4 * threadIdx.x; r < slab; r += 4 * blockDim.x) {
+            float4 v = __ldg(src + r / 4);
+            if (sb >= 0) {
+                const int c = r % C;             // C % 4 == 0: r .. r + 3 share the node
+                v.x += __ldg(bias + c * nscalar + sb);
+                v.y += __ldg(bias + (c + 1) * nscalar + sb);
+                v.z += __ldg(bias + (c + 2) * nscalar + sb);
+                v.w += __ldg(bias + (c + 3) * nscalar + sb);
+            }
+            tsm[r * d + p] = v.x;
+            tsm[(r + 1) * d + p] = v.y;
+            tsm[(r + 2) * d + p] = v.z;
+            tsm[(r + 3) * d + p] = v.w;
+        }
     }
     __syncthreads();
+    const int tile = slab * d;
     float *dst = y + n0 * C * d;
-    for (int i = threadIdx.x; i < slab * d; i += blockDim.x) dst[i] = tsm[i];
+    if ((tile & 3) == 0 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+        for (int i = threadIdx.x; i < tile / 4; i += blockDim.x)
+            reinterpret_cast<float4 *>(dst)[i] = reinterpret_cast<const float4 *>(tsm)[i];
+    } else {
+        for (int i = threadIdx.x; i < tile; i += blockDim.x) dst[i] = tsm[i];
+    }
 }
 
 int fill_node_repr(const int32_t *lvals, int32_t n, int32_t C, NodeRepr *R) {
@@ -459,12 +488,15 @@ int feq_node_to_posmajor(const float *x, int64_t num_nodes, int32_t C, int32_t d
     if (num_nodes < 0 || C < 1 || d < 1 || d > kMaxDim) return FEQ_ERR_INVALID_ARGUMENT;
     if (num_nodes == 0) return FEQ_OK;
     if (!x || !xt) return FEQ_ERR_INVALID_ARGUMENT;
-    const size_t smem = sizeof(float) * kPmNodes * (size_t)C * d;
+    if (C % 4 || (reinterpret_cast<uintptr_t>(xt) & 15)) return FEQ_ERR_UNSUPPORTED;
+    const int tn = pm_nodes(C, d);
+    if (tn < 1) return FEQ_ERR_UNSUPPORTED;
+    const size_t smem = sizeof(float) * tn * (size_t)C * d;
     int rc;
     if ((rc = set_smem((const void *)to_posmajor_kernel, smem)) != FEQ_OK) return rc;
     ProfScope ps("node_layout", (cudaStream_t)stream);
-    to_posmajor_kernel<<<(unsigned)((num_nodes + kPmNodes - 1) / kPmNodes), 256, smem, (cudaStream_t)stream>>>(
-        x, num_nodes, C, d, xt);
+    to_posmajor_kernel<<<(unsigned)((num_nodes + tn - 1) / tn), 256, smem, (cudaStream_t)stream>>>(
+        x, num_nodes, C, d, tn, xt);
     FEQ_LAUNCH_CHECK();
     return FEQ_OK;
 }
@@ -477,13 +509,16 @@ int feq_node_from_posmajor(const float *yt, int64_t num_nodes, int32_t C, const 
     if (num_nodes < 0) return FEQ_ERR_INVALID_ARGUMENT;
     if (num_nodes == 0) return FEQ_OK;
     if (!yt || !y || (bias && !scalar_index)) return FEQ_ERR_INVALID_ARGUMENT;
+    if (C % 4 || (reinterpret_cast<uintptr_t>(yt) & 15)) return FEQ_ERR_UNSUPPORTED;
     int nscalar = 0;
     for (int r = 0; r < n_lvals; r++) nscalar += lvals[r] == 0;
-    const size_t smem = sizeof(float) * kPmNodes * (size_t)C * R.d;
+    const int tn = pm_nodes(C, R.d);
+    if (tn < 1) return FEQ_ERR_UNSUPPORTED;
+    const size_t smem = sizeof(float) * tn * (size_t)C * R.d;
     if ((rc = set_smem((const void *)from_posmajor_kernel, smem)) != FEQ_OK) return rc;
     ProfScope ps("node_layout", (cudaStream_t)stream);
-    from_posmajor_kernel<<<(unsigned)((num_nodes + kPmNodes - 1) / kPmNodes), 256, smem, (cudaStream_t)stream>>>(
-        yt, num_nodes, C, R.d, bias, nscalar, scalar_index, y);
+    from_posmajor_kernel<<<(unsigned)((num_nodes + tn - 1) / tn), 256, smem, (cudaStream_t)stream>>>(
+        yt, num_nodes, C, R.d, bias, nscalar, scalar_index, tn, y);
     FEQ_LAUNCH_CHECK();
     return FEQ_OK;
 }

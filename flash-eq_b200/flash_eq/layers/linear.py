@@ -138,7 +138,8 @@ class EquivariantLinear(nn.Module):
         self.activation = activation if activation is not None else nn.Identity()
         self._lvals = tuple(in_repr.lvals.tolist())
         # inference path: position-major layout kernels around one GEMM per irrep (identity activation)
-        self._native_ok = isinstance(self.activation, nn.Identity)
+        self._native_ok = (isinstance(self.activation, nn.Identity) and in_repr.mult % 4 == 0
+                           and out_repr.mult % 4 == 0)
         pos_ix = torch.full((in_repr.dim(),), -1, dtype=torch.int8)
         for s_i, loc in enumerate(self.scalar_locs):
             pos_ix[loc] = s_i

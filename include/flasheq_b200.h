@@ -398,7 +398,8 @@ int feq_node_rep_norm(const float *x, int64_t num_nodes, int32_t C, const int32_
  * (xt[p][n][c] = x[n][c][p], xt (d, N, C)); one plain GEMM per irrep on the contiguous
  * rows p = off .. off + 2l of xt (the caller's BLAS: y_r = x_r W_r^T); feq_node_from_posmajor
  * (y[n][c][p] = yt[p][n][c] + bias[c, scalar_index[p]] where scalar_index[p] >= 0; bias
- * (C, n_scalar) and scalar_index (d,) int8 device arrays, both NULL for no bias). */
+ * (C, n_scalar) and scalar_index (d,) int8 device arrays, both NULL for no bias).  C a
+ * multiple of 4 and xt / yt 16-byte aligned (FEQ_ERR_UNSUPPORTED otherwise). */
 int feq_node_to_posmajor(const float *x, int64_t num_nodes, int32_t C, int32_t d, float *xt, feq_stream_t stream);
 int feq_node_from_posmajor(const float *yt, int64_t num_nodes, int32_t C, const int32_t *lvals, int32_t n_lvals,
                            const float *bias, const int8_t *scalar_index, float *y, feq_stream_t stream);
