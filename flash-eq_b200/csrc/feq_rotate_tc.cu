@@ -24,6 +24,9 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
+#include <numeric>
+
 #include "feq_internal.cuh"
 #include "feq_sm100.cuh"
 #include "_build/feq_wigner_tables.inc"
@@ -547,20 +550,32 @@ basis_warp_kernel(const float *__restrict__ dirs, int64_t E, const __grid_consta
     }
 }
 
-// Dense basis, one lane per edge.  For each irrep (uniform over the warp) every lane
-// builds its edge's M_l in registers and forms the block row by row:
-//   row a of D   (kT = false):  u = R[a] M,    v = R u
-//   row a of D^T (kT = true):   u = M R[a]^T,  v = R u
-// (R = R(phi): R[x][x] = cos m phi, R[l-m][l+m] = sin m phi, R[l+m][l-m] = -sin m phi),
-// which equals D = R M R^T entry by entry.  Up to kBasisRows consecutive output rows
-// of the 32 edges of the group are staged in shared memory (zeros outside the block)
-// and written per edge as one contiguous run of rows.
-constexpr int kBasisRows = 5;
+// Dense basis, one lane per edge, in two phases per group of 32 edges.
+//  1. Every lane builds its edge's block of each DISTINCT degree (irreps of equal degree
+//     share it) in registers and writes it, compact, to its row of the warp's stage:
+//       row a of D   (kT = false):  u = R[a] M,    v = R u
+//       row a of D^T (kT = true):   u = M R[a]^T,  v = R u
+//     (R = R(phi): R[x][x] = cos m phi, R[l-m][l+m] = sin m phi, R[l+m][l-m] = -sin m phi),
+//     which equals D = R M R^T entry by entry.  The stage row stride is odd, so the lanes'
+//     writes fall in distinct banks, and slot `zero` of every row holds 0.
+//  2. The warp streams the group's output -- 32 * d * d contiguous floats -- as float4
+//     stores.  Output float f of a period of P edges (P * d * d a multiple of 4) comes
+//     from stage float pos[f] (computed once per block: the edge within the period times
+//     the row stride, plus the compact entry or the zero slot).
+constexpr int kBasisMaxStage = 200 * 1024;
+
+struct BasisCompact {
+    int stride;        // floats per stage row (odd)
+    int zero;          // slot holding 0
+    int period;        // edges after which the float4 pattern repeats (1, 2 or 4)
+    int entries;       // float4 entries of one period
+    int nwarps;        // warps per block
+    int per_warp;      // floats of shared memory per warp (trig + stage)
+    size_t smem;       // dynamic shared memory bytes
+};
 
 template <int Lg, bool kT>
-__device__ __forceinline__ void basis_irrep(const float *__restrict__ tr, int lmax, int off, const int16_t *colpos,
-                                            float *stage, int S, int lane, int ng, float *__restrict__ out,
-                                            int d, int64_t g0) {
+__device__ __forceinline__ void basis_block(const float *__restrict__ tr, int lmax, float *__restrict__ mine) {
     constexpr int N = 2 * Lg + 1;
     const float *tv = tr, *cp = tr + 2 * lmax + 1, *sp = cp + lmax + 1;
     float M[N * N];
@@ -573,93 +588,74 @@ __device__ __forceinline__ void basis_irrep(const float *__restrict__ tr, int lm
     }
     auto rdiag = [&](int x) { return x == Lg ? 1.0f : c[x < Lg ? Lg - x : x - Lg]; };
     auto roff = [&](int x) { return x < Lg ? sn[Lg - x] : (x > Lg ? -sn[x - Lg] : 0.0f); };
-    const int64_t dd = (int64_t)d * d;
-    float *mine = stage + lane * S;
 #pragma unroll
-    for (int a0 = 0; a0 < N; a0 += kBasisRows) {
-        constexpr int kR = kBasisRows;
-        const int rows = N - a0 < kR ? N - a0 : kR;
+    for (int a = 0; a < N; a++) {
+        const int pa = 2 * Lg - a;
+        float u[N];
 #pragma unroll
-        for (int ar = 0; ar < kR; ar++) {
-            const int a = a0 + ar;
-            if (a >= N) break;
-            const int pa = 2 * Lg - a;
-            float u[N];
-#pragma unroll
-            for (int q = 0; q < N; q++) {
-                const float mq = kT ? M[q * N + a] : M[a * N + q];
-                const float mp = kT ? M[q * N + pa] : M[pa * N + q];
-                u[q] = a == Lg ? mq : rdiag(a) * mq + roff(a) * mp;
-            }
-#pragma unroll
-            for (int b = 0; b < N; b++) {
-                const int pb = 2 * Lg - b;
-                mine[ar * d + colpos[off + b]] = b == Lg ? u[b] : rdiag(b) * u[b] + roff(b) * u[pb];
-            }
+        for (int q = 0; q < N; q++) {
+            const float mq = kT ? M[q * N + a] : M[a * N + q];
+            const float mp = kT ? M[q * N + pa] : M[pa * N + q];
+            u[q] = a == Lg ? mq : rdiag(a) * mq + roff(a) * mp;
         }
-        __syncwarp();
-        const int run = rows * d;
-        for (int e = 0; e < ng; e++) {
-            float *dst = out + (g0 + e) * dd + (int64_t)(off + a0) * d;
-            const float *srow = stage + e * S;
-            for (int i = lane; i < run; i += 32) dst[i] = srow[i];
-        }
-        __syncwarp();
 #pragma unroll
-        for (int ar = 0; ar < kR; ar++) {
-            if (a0 + ar >= N) break;
-#pragma unroll
-            for (int b = 0; b < N; b++) mine[ar * d + colpos[off + b]] = 0.0f;
+        for (int b = 0; b < N; b++) {
+            const int pb = 2 * Lg - b;
+            mine[a * N + b] = b == Lg ? u[b] : rdiag(b) * u[b] + roff(b) * u[pb];
         }
-        __syncwarp();
     }
 }
 
-__global__ void __launch_bounds__(kRotWarps * 32)
-basis_lane_kernel(const float *__restrict__ dirs, int64_t E, const __grid_constant__ ReprLayout Lp, int mfirst,
-                  int per_warp, float *__restrict__ out) {
+__global__ void basis_compact_kernel(const float *__restrict__ dirs, int64_t E, const __grid_constant__ ReprLayout Lp,
+                                     int mfirst, BasisCompact B, float *__restrict__ out) {
     extern __shared__ __align__(128) float dsm[];
     __shared__ ReprLayout L;
-    __shared__ int16_t colpos[kMaxDim];
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     copy_layout(Lp, L);
     __syncthreads();
-    // std position of a D column -> output column (m-first position, or itself)
-    for (int i = threadIdx.x; i < L.dim; i += blockDim.x) colpos[i] = mfirst ? L.inv_perm[i] : (int16_t)i;
-    __syncthreads();
-    const int d = L.dim, S = (kBasisRows * d) | 1, TF = trig_floats(L.lmax);
-    float *trig = dsm + (size_t)w * per_warp;
+    const int d = L.dim, dd = d * d, TF = trig_floats(L.lmax);
+    short4 *pos = reinterpret_cast<short4 *>(dsm);
+    // output float f of a period -> stage float (one-time table; divisions are fine here)
+    for (int t = threadIdx.x; t < B.entries; t += blockDim.x) {
+        short v[4];
+#pragma unroll
+        for (int s = 0; s < 4; s++) {
+            const int f = 4 * t + s, er = f / dd, p = f - er * dd, k = p / d, j = p - k * d;
+            const int sj = mfirst ? L.perm[j] : j;       // std column carried by output column j
+            const int r = L.std_irrep[k];
+            int c = B.zero;
+            if (L.std_irrep[sj] == r) {
+                const int off = L.irrep_off[r], n = 2 * L.irrep_l[r] + 1;
+                c = L.unique_doff[L.irrep_slot[r]] + (k - off) * n + (sj - off);
+            }
+            v[s] = (short)(er * B.stride + c);
+        }
+        pos[t] = make_short4(v[0], v[1], v[2], v[3]);
+    }
+    float *trig = dsm + 2 * pad4(B.entries) + (size_t)w * B.per_warp;
     float *stage = trig + pad4(kGroup * TF);
-    for (int i = lane; i < kGroup * S; i += 32) stage[i] = 0.0f;
-    __syncwarp();
+    stage[lane * B.stride + B.zero] = 0.0f;
+    __syncthreads();
     const float *tr = trig + lane * TF;
-    for (int64_t g0 = ((int64_t)blockIdx.x * kRotWarps + w) * kGroup; g0 < E;
-         g0 += (int64_t)gridDim.x * kRotWarps * kGroup) {
+    float *mine = stage + lane * B.stride;
+    const int pstride = B.period * B.stride;
+    for (int64_t g0 = ((int64_t)blockIdx.x * B.nwarps + w) * kGroup; g0 < E;
+         g0 += (int64_t)gridDim.x * B.nwarps * kGroup) {
         const int ng = (int)min64(kGroup, E - g0);
         {
             const int64_t e = g0 + min(lane, ng - 1);
             edge_trig_compact(dirs[e * 3], dirs[e * 3 + 1], dirs[e * 3 + 2], L.lmax, trig + lane * TF);
         }
         __syncwarp();
-        for (int r = 0; r < L.n_irreps; r++) {
-            const int l = L.irrep_l[r], off = L.irrep_off[r];
-#define FEQ_BASIS_CASE(LL)                                                                                   \
-    case LL:                                                                                                 \
-        if (mfirst) basis_irrep<LL, false>(tr, L.lmax, off, colpos, stage, S, lane, ng, out, d, g0);           \
-        else basis_irrep<LL, true>(tr, L.lmax, off, colpos, stage, S, lane, ng, out, d, g0);                   \
+        for (int u = 0; u < L.n_unique; u++) {
+            float *blk = mine + L.unique_doff[u];
+#define FEQ_BASIS_CASE(LL)                                                  \
+    case LL:                                                                \
+        if (mfirst) basis_block<LL, false>(tr, L.lmax, blk);                \
+        else basis_block<LL, true>(tr, L.lmax, blk);                        \
         break;
-            switch (l) {
-                case 0: {
-                    stage[lane * S + colpos[off]] = 1.0f;
-                    __syncwarp();
-                    for (int e = 0; e < ng; e++)
-                        for (int j = lane; j < d; j += 32)
-                            out[(g0 + e) * (int64_t)d * d + (int64_t)off * d + j] = stage[e * S + j];
-                    __syncwarp();
-                    stage[lane * S + colpos[off]] = 0.0f;
-                    __syncwarp();
-                    break;
-                }
+            switch (L.unique_l[u]) {
+                case 0: blk[0] = 1.0f; break;
                 FEQ_BASIS_CASE(1)
                 FEQ_BASIS_CASE(2)
                 FEQ_BASIS_CASE(3)
@@ -668,6 +664,37 @@ basis_lane_kernel(const float *__restrict__ dirs, int64_t E, const __grid_consta
                 FEQ_BASIS_CASE(6)
             }
 #undef FEQ_BASIS_CASE
+        }
+        __syncwarp();
+        // the group's output is contiguous and starts 16-byte aligned (g0 is a multiple of 32)
+        const int nf = ng * dd, nq = nf >> 2;
+        float4 *o4 = reinterpret_cast<float4 *>(out + g0 * (int64_t)dd);
+        int t = lane, pb = 0;
+        while (t >= B.entries) {
+            t -= B.entries;
+            pb += pstride;
+        }
+#pragma unroll 4
+        for (int q = lane; q < nq; q += 32) {
+            const short4 ix = pos[t];
+            float4 v;
+            v.x = stage[pb + ix.x];
+            v.y = stage[pb + ix.y];
+            v.z = stage[pb + ix.z];
+            v.w = stage[pb + ix.w];
+            o4[q] = v;
+            t += 32;
+            while (t >= B.entries) {
+                t -= B.entries;
+                pb += pstride;
+            }
+        }
+        if (lane == 0 && (nf & 3)) {               // ragged last group: the trailing floats
+            const int tt = nq % B.entries, pp = (nq / B.entries) * pstride;
+            const short4 ix = pos[tt];
+            const short iv[4] = {ix.x, ix.y, ix.z, ix.w};
+            float *o = out + g0 * (int64_t)dd + 4 * (int64_t)nq;
+            for (int s = 0; s < (nf & 3); s++) o[s] = stage[pp + iv[s]];
         }
         __syncwarp();
     }
@@ -746,20 +773,46 @@ int launch_rot_out_stream(const float *H, int h_ld, const float *dirs, const flo
     return FEQ_OK;
 }
 
-// Dense basis matrices, warp per edge.  FEQ_ERR_UNSUPPORTED when the layout does not fit.
+// Dense basis matrices: the compact lane-per-edge kernel where its tables fit in shared
+// memory, else warp per edge.  FEQ_ERR_UNSUPPORTED when neither layout fits.
+static bool basis_compact_plan(const ReprLayout &L, BasisCompact &B) {
+    if (L.lmax > kFactoredLmax) return false;
+    const int64_t dd = (int64_t)L.dim * L.dim;
+    B.stride = (L.dblock_floats + 1) | 1;
+    B.zero = L.dblock_floats;
+    B.period = (int)(4 / std::gcd<int64_t>(dd, 4));
+    if (B.period * dd / 4 > (int64_t)kBasisMaxStage / 8) return false;
+    B.entries = (int)(B.period * dd / 4);
+    B.per_warp = pad4(kGroup * trig_floats(L.lmax)) + pad4(kGroup * B.stride);
+    const size_t table = (size_t)pad4(B.entries) * 8;
+    for (int nw = kRotWarps; nw >= 1; nw--) {
+        const size_t smem = table + (size_t)nw * B.per_warp * 4;
+        if (smem <= (size_t)kBasisMaxStage) {
+            B.nwarps = nw;
+            B.smem = smem;
+            return true;
+        }
+    }
+    return false;
+}
+
 int launch_basis_stream(const float *dirs, int64_t E, const ReprLayout &L, int mfirst, float *out, cudaStream_t s) {
     if (E == 0) return FEQ_OK;
-    if (L.lmax <= kFactoredLmax) {
-        const int per_warp = pad4(kGroup * trig_floats(L.lmax)) + pad4(kGroup * ((kBasisRows * L.dim) | 1));
-        const size_t smem = (size_t)kRotWarps * per_warp * 4;
-        if (smem <= 160 * 1024) {
-            FEQ_CUDA_TRY(cudaFuncSetAttribute(basis_lane_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                              (int)smem));
-            const int grid = rot_grid((const void *)basis_lane_kernel, smem, E);
-            basis_lane_kernel<<<grid, kRotWarps * 32, smem, s>>>(dirs, E, L, mfirst, per_warp, out);
-            FEQ_LAUNCH_CHECK();
-            return FEQ_OK;
-        }
+    BasisCompact B;
+    if (aligned16(out) && basis_compact_plan(L, B)) {
+        FEQ_CUDA_TRY(cudaFuncSetAttribute(basis_compact_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)B.smem));
+        int dev = 0, sms = 148, per_sm = 1;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, basis_compact_kernel, B.nwarps * 32, B.smem) !=
+                cudaSuccess || per_sm < 1)
+            per_sm = 1;
+        const int64_t want = (E + B.nwarps * kGroup - 1) / (B.nwarps * kGroup);
+        const int grid = (int)std::max<int64_t>(1, min64(want, (int64_t)sms * per_sm));
+        basis_compact_kernel<<<grid, B.nwarps * 32, B.smem, s>>>(dirs, E, L, mfirst, B, out);
+        FEQ_LAUNCH_CHECK();
+        return FEQ_OK;
     }
     const int scratch = rot_scratch(L).total();
     const size_t smem = (size_t)kRotWarps * scratch * 4;

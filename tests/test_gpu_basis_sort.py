@@ -48,6 +48,28 @@ def test_basis_matches_oracle_large(cuda_device, lvals):
     assert err < 3e-5, err
 
 
+def _oracle_rot_to_ez(dirs, lvals):
+    eps = 1e-8
+    d = dirs / (torch.linalg.norm(dirs, dim=-1, keepdim=True) + eps)
+    axis = torch.stack([-d[..., 1], d[..., 0], torch.zeros_like(d[..., 0])], dim=-1)
+    axis = axis / (torch.linalg.norm(axis, dim=-1, keepdim=True) + eps)
+    angle = torch.arccos(d[..., 2].clamp(-1 + eps, 1 - eps))
+    return orc.rot(axis, angle, lvals).mT
+
+
+@pytest.mark.parametrize("lvals", [[0], [1], [0, 0], [2, 2, 1], [0, 1, 2], [4, 1]])
+@pytest.mark.parametrize("n", [1, 31, 33, 97, 1029])
+def test_basis_ragged_groups(cuda_device, lvals, n):
+    """Edge counts that leave a partial group of 32 and a dense output whose length is not a
+    multiple of 4 floats, in both column orders (m-first basis, std-order rot_to_ez)."""
+    g = torch.Generator().manual_seed(n)
+    dirs = torch.randn(n, 3, generator=g)
+    (ours,) = fe.WignerDBasis([fe.Repr(lvals)])(dirs.to(cuda_device))
+    assert (ours.cpu() - orc.wigner_basis(dirs, lvals)).abs().max().item() < 3e-5
+    rz = fe.WignerD(fe.Repr(lvals)).to(cuda_device).rot_to_ez(dirs.to(cuda_device))
+    assert (rz.cpu() - _oracle_rot_to_ez(dirs, lvals)).abs().max().item() < 3e-5
+
+
 def test_basis_high_degree_against_float64(cuda_device):
     """l up to 16 (the reference's MAX_LVALS limit) against a float64 matrix exponential."""
     g = torch.Generator().manual_seed(3)
