@@ -44,6 +44,9 @@ def _stream(device) -> ctypes.c_void_p:
     return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
 
 
+EDGEWISE_WS_CAP = None     # scratch cap of one edgewise call in bytes; None: 1/8 of the device memory, >= 1 GiB
+
+
 def _workspace(nbytes: int, device) -> torch.Tensor:
     return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
 
@@ -230,9 +233,39 @@ def edgewise_fwd(x, distances, radial_table, lvals_in, lvals_out, c_out, sh_scal
     ws_bytes = lib.feq_edgewise_workspace_bytes(ctypes.byref(args))
     if ws_bytes == 0:
         raise RuntimeError("edgewise: unsupported layout (l <= 16, <= 64 irreps, dim <= 512)")
-    ws = _workspace(ws_bytes, dev)
-    rc = lib.feq_edgewise_fwd(ctypes.byref(args), _p(ws), ws.numel(), _stream(dev))
-    _lib.check(rc, "feq_edgewise_fwd")
+    # Edges are independent, so a call whose scratch would exceed the cap runs as
+    # consecutive edge ranges through one reused workspace (same results row by row).
+    cap = EDGEWISE_WS_CAP or max(1 << 30, torch.cuda.get_device_properties(dev).total_memory // 8)
+    if ws_bytes <= cap:
+        ws = _workspace(ws_bytes, dev)
+        rc = lib.feq_edgewise_fwd(ctypes.byref(args), _p(ws), ws.numel(), _stream(dev))
+        _lib.check(rc, "feq_edgewise_fwd")
+        return out
+    n_chunks = -(-ws_bytes // cap)
+    chunk = -(-E // n_chunks)
+    chunk = -(-chunk // 128) * 128
+    args.num_edges = chunk
+    ws = _workspace(lib.feq_edgewise_workspace_bytes(ctypes.byref(args)), dev)
+    row_in, row_out = c_in * d_in * 4, c_out * d_out * 4
+    base = {f: getattr(args, f) for f in ("src", "x", "edge_add", "directions", "P_in", "Q_out", "distances", "out")}
+    for e0 in range(0, E, chunk):
+        n = min(chunk, E - e0)
+        args.num_edges = n
+        args.distances = base["distances"] + 4 * e0
+        args.out = base["out"] + row_out * e0
+        if src is not None:
+            args.src = base["src"] + 8 * e0
+        else:
+            args.x = base["x"] + row_in * e0
+        if edge_add is not None:
+            args.edge_add = base["edge_add"] + row_in * e0
+        if directions is not None:
+            args.directions = base["directions"] + 12 * e0
+        else:
+            args.P_in = base["P_in"] + 4 * d_in * d_in * e0
+            args.Q_out = base["Q_out"] + 4 * d_out * d_out * e0
+        rc = lib.feq_edgewise_fwd(ctypes.byref(args), _p(ws), ws.numel(), _stream(dev))
+        _lib.check(rc, "feq_edgewise_fwd")
     return out
 
 

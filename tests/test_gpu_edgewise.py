@@ -165,6 +165,35 @@ def test_deterministic(cuda_device):
     assert torch.equal(a, b)
 
 
+@pytest.mark.parametrize("gather", [False, True])
+def test_edge_range_chunking_is_exact(cuda_device, gather, monkeypatch):
+    """A call whose scratch exceeds the cap runs as consecutive edge ranges: the result is
+    bit-identical to the single call (edges are independent)."""
+    from flash_eq.cuda import ops
+
+    r = fe.Repr([0, 1, 2], mult=32)
+    layer = fe.EquivariantEdgewiseLinear(r, r).to(cuda_device)
+    g = torch.Generator().manual_seed(12)
+    E, N = 7001, 900
+    dirs = torch.randn(E, 3, generator=g).to(cuda_device)
+    dist = (torch.rand(E, generator=g) * 10).to(cuda_device)
+    if gather:
+        x = torch.randn(N, 32, 9, generator=g).to(cuda_device)
+        src = torch.randint(0, N, (E,), generator=g).to(cuda_device)
+        ea = torch.randn(E, 32, 9, generator=g).to(cuda_device)
+        bases = fe.WignerDBasis([r, r]).lazy(dirs)
+        call = lambda: layer._run(bases[0], bases[1], x, dist, src=src, edge_add=ea)
+    else:
+        f = torch.randn(E, 32, 9, generator=g).to(cuda_device)
+        P, Q = fe.WignerDBasis([r, r])(dirs)
+        call = lambda: layer(P, Q, f, dist)
+    with torch.no_grad():
+        whole = call()
+        monkeypatch.setattr(ops, "EDGEWISE_WS_CAP", 1 << 20)
+        parts = call()
+    assert torch.equal(whole, parts)
+
+
 @pytest.mark.parametrize("lin,lout,mult,E,log_bins", [
     ([0, 1, 2], [0, 1, 2], 32, 5000, False), ([0, 1, 2, 3, 4], [0, 1], 16, 2000, True),
     ([1, 2, 2], [0, 1], 5, 333, False), ([0], [0, 1, 2], 3, 1, False)])
