@@ -11,7 +11,8 @@
 //   EquivariantGating (the gate)    flash_eq/layers/gating.py:17-76: x * sigmoid(z)[c, irrep]
 //
 // One warp per node: the node's row (C x d floats) is staged in shared memory once, the
-// per-node statistics are warp reductions, and the output row is written coalesced.
+// per-node statistics are warp reductions, the transform runs in place with lane = channel,
+// and the output row is written coalesced.
 // All four are memory-bound: one read and one write of the row (plus z / norms).
 #include <cuda_runtime.h>
 #include <math.h>
@@ -25,6 +26,7 @@ namespace feq {
 namespace {
 
 constexpr int kNodeWarps = 4;
+constexpr int kNodeBlocksPerSm = 6;      // 24 warps per SM: <= 85 registers per thread
 constexpr int kNodeMaxIrreps = 32;
 constexpr int kNodeMaxScalars = 16;
 
@@ -103,57 +105,163 @@ __device__ __forceinline__ void stage_row(float *row, const float *src, int n, i
     __syncwarp();
 }
 
-__global__ void __launch_bounds__(kNodeWarps * 32) sep_layernorm_kernel(const __grid_constant__ SepLnArgs a) {
+// Row layout in shared memory: element (c, p) at c * ds + p, with the channel stride ds = d
+// for odd d and d + 1 for even d.  The per-node transforms then run with lane = channel over
+// the positions p: the 32 lanes read 32 rows ds apart (distinct banks, as ds is odd), the
+// branch on the position's kind is uniform across the warp and no (c, p) pair is decoded
+// from a flat index.
+__host__ __device__ __forceinline__ int odd_stride(int d) { return d | 1; }
+
+// Node row -> row[c * ds + p]: a straight float4 copy when ds == d, else scalar loads
+// (all of a batch issued before its stores) scattered through a RowWalk.
+__device__ __forceinline__ void stage_row_ds(float *row, const float *src, int C, int d, int ds, int lane) {
+    const int n = C * d;
+    if (ds == d) {
+        stage_row(row, src, n, lane);
+        return;
+    }
+    constexpr int kB = 8;
+    RowWalk w(lane, d);
+    for (int i0 = lane; i0 < n; i0 += 32 * kB) {
+        float v[kB];
+#pragma unroll
+        for (int u = 0; u < kB; u++)
+            if (i0 + 32 * u < n) v[u] = __ldg(src + i0 + 32 * u);
+#pragma unroll
+        for (int u = 0; u < kB; u++)
+            if (i0 + 32 * u < n) {
+                row[w.c * ds + w.p] = v[u];
+                w.next();
+            }
+    }
+    __syncwarp();
+}
+
+// row[c * ds + p] -> node row in global memory, coalesced (float4 when ds == d and aligned)
+__device__ __forceinline__ void write_row_ds(float *dst, const float *row, int C, int d, int ds, int lane) {
+    const int n = C * d;
+    __syncwarp();
+    if (ds == d && (n & 3) == 0 && ((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(row)) & 15) == 0) {
+        const float4 *r4 = reinterpret_cast<const float4 *>(row);
+        float4 *d4 = reinterpret_cast<float4 *>(dst);
+        for (int i = lane; i < n / 4; i += 32) d4[i] = r4[i];
+    } else if (ds == d) {
+        for (int i = lane; i < n; i += 32) dst[i] = row[i];
+    } else {
+        RowWalk w(lane, d);
+        for (int i = lane; i < n; i += 32, w.next()) dst[i] = row[w.c * ds + w.p];
+    }
+    __syncwarp();
+}
+
+// ---- node loop: the next node's row is copied into shared memory (cp.async, 16 bytes a
+// lane) while the current one is transformed.  kAsync needs ds == d, C * d % 4 == 0 and
+// 16-byte aligned rows; otherwise each row is staged through registers (stage_row_ds).
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(smem))),
+                 "l"(gmem)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+
+// body(node, row) reads the staged row (C * ds floats) and writes the node's outputs.
+template <bool kAsync, typename Body>
+__device__ __forceinline__ void node_loop(const float *__restrict__ x, int64_t N, int C, int d, int ds, float *buf,
+                                          int lane, int64_t first, int64_t stride, Body body) {
+    const int n = C * d;
+    if constexpr (!kAsync) {
+        for (int64_t node = first; node < N; node += stride) {
+            stage_row_ds(buf, x + node * n, C, d, ds, lane);
+            body(node, buf);
+            __syncwarp();
+        }
+    } else {
+        const int slot_floats = C * ds;
+        auto issue = [&](float *dst, int64_t node) {
+            const float4 *s4 = reinterpret_cast<const float4 *>(x + node * n);
+            float4 *d4 = reinterpret_cast<float4 *>(dst);
+            for (int i = lane; i < n / 4; i += 32) cp_async16(d4 + i, s4 + i);
+        };
+        if (first < N) issue(buf, first);
+        cp_async_commit();
+        int slot = 0;
+        for (int64_t node = first; node < N; node += stride, slot ^= 1) {
+            if (node + stride < N) issue(buf + (slot ^ 1) * slot_floats, node + stride);
+            cp_async_commit();
+            cp_async_wait1();                // this lane's copies of the current row have landed
+            __syncwarp();                    // ... and every other lane's
+            body(node, buf + slot * slot_floats);
+            __syncwarp();                    // this slot is refilled by the next iteration's copies
+        }
+    }
+}
+
+// Shared memory: per warp the node row (C * ds floats); per block the weights w_s, b_s
+// (C x nscalar) and w_h (C).
+template <bool kAsync>
+__global__ void __launch_bounds__(kNodeWarps * 32, kNodeBlocksPerSm) sep_layernorm_kernel(const __grid_constant__ SepLnArgs a) {
     extern __shared__ float nsm[];
-    const int C = a.R.C, d = a.R.d, n = C * d;
+    const int C = a.R.C, d = a.R.d, n = C * d, ds = odd_stride(d), ns = a.nscalar;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    float *row = nsm + (size_t)warp * n;
-    __shared__ float mu_s[kNodeWarps][kNodeMaxScalars], inv_s[kNodeWarps][kNodeMaxScalars], rms_s[kNodeWarps];
-    __shared__ int8_t sidx_s[kMaxDim];     // per-lane lookups from shared memory, not the parameter bank
+    float *buf = nsm + (size_t)warp * 2 * C * ds;
+    float *ws = nsm + (size_t)kNodeWarps * 2 * C * ds, *bs = ws + C * ns, *wh = bs + C * ns;
+    __shared__ float mu_s[kNodeWarps][kNodeMaxScalars], inv_s[kNodeWarps][kNodeMaxScalars];
+    __shared__ int8_t sidx_s[kMaxDim];
     for (int i = threadIdx.x; i < d; i += blockDim.x) sidx_s[i] = a.scalar_idx[i];
+    for (int i = threadIdx.x; i < C * ns; i += blockDim.x) {
+        ws[i] = a.w_s[i];
+        bs[i] = a.b_s[i];
+    }
+    if (a.n_higher > 0)
+        for (int i = threadIdx.x; i < C; i += blockDim.x) wh[i] = a.w_h[i];
     __syncthreads();
-    for (int64_t node = (int64_t)blockIdx.x * kNodeWarps + warp; node < a.N; node += (int64_t)gridDim.x * kNodeWarps) {
-        stage_row(row, a.x + node * n, n, lane);
-        for (int s = 0; s < a.nscalar; s++) {
+    node_loop<kAsync>(a.x, a.N, C, d, ds, buf, lane, (int64_t)blockIdx.x * kNodeWarps + warp,
+                      (int64_t)gridDim.x * kNodeWarps, [&](int64_t node, float *row) {
+        // scalar positions: LayerNorm over the channels (mean, then the biased variance)
+        for (int s = 0; s < ns; s++) {
             const int p = a.scalar_pos[s];
             float sum = 0.0f;
-            for (int c = lane; c < C; c += 32) sum += row[c * d + p];
+            for (int c = lane; c < C; c += 32) sum += row[c * ds + p];
             const float mu = nwsum(sum) / (float)C;
             float sq = 0.0f;
             for (int c = lane; c < C; c += 32) {
-                const float t = row[c * d + p] - mu;
+                const float t = row[c * ds + p] - mu;
                 sq = fmaf(t, t, sq);
             }
             const float sd = sqrtf(nwsum(sq) / (float)C);
             if (lane == 0) {
                 mu_s[warp][s] = mu;
-                inv_s[warp][s] = sd + a.eps;
+                inv_s[warp][s] = 1.0f / (sd + a.eps);
             }
         }
+        // higher positions: one RMS over every channel and higher position
+        float inv_rms = 1.0f;
         if (a.n_higher > 0) {
             float sq = 0.0f;
-            RowWalk w(lane, d);
-            for (int j = lane; j < n; j += 32, w.next())
-                if (sidx_s[w.p] < 0) sq = fmaf(row[j], row[j], sq);
-            sq = nwsum(sq);
-            if (lane == 0) rms_s[warp] = sqrtf(sq / (float)(C * a.n_higher) + a.eps);
+            for (int c = lane; c < C; c += 32)
+#pragma unroll 4
+                for (int p = 0; p < d; p++)
+                    if (sidx_s[p] < 0) {
+                        const float v = row[c * ds + p];
+                        sq = fmaf(v, v, sq);
+                    }
+            inv_rms = 1.0f / sqrtf(nwsum(sq) / (float)(C * a.n_higher) + a.eps);
         }
         __syncwarp();
-        float *orow = a.out + node * n;
-        const float rms = a.n_higher > 0 ? rms_s[warp] : 1.0f;
-        RowWalk w(lane, d);
-        for (int j = lane; j < n; j += 32, w.next()) {
-            float v = row[j];
-            const int s = sidx_s[w.p];
-            if (s >= 0) {
-                v = (v - mu_s[warp][s]) / inv_s[warp][s] * a.w_s[w.c * a.nscalar + s] + a.b_s[w.c * a.nscalar + s];
-            } else {
-                v = v * (a.w_h[w.c] / rms);
+        for (int c = lane; c < C; c += 32) {
+            const float hs = a.n_higher > 0 ? wh[c] * inv_rms : 0.0f;
+#pragma unroll 4
+            for (int p = 0; p < d; p++) {
+                const int s = sidx_s[p];
+                float v = row[c * ds + p];
+                if (s >= 0) v = fmaf(v - mu_s[warp][s], ws[c * ns + s] * inv_s[warp][s], bs[c * ns + s]);
+                else v *= hs;
+                row[c * ds + p] = v;
             }
-            orow[j] = v;
         }
-        __syncwarp();
-    }
+        write_row_ds(a.out + node * n, row, C, d, ds, lane);
+    });
 }
 
 struct EqLnArgs {
@@ -164,29 +272,27 @@ struct EqLnArgs {
     int64_t N;
 };
 
-// norms of this warp's node row into nrm[c * n_irreps + r] (irrep offsets / sizes from shared memory)
+// norms of this warp's node row: nrm[c * nrs + r] = sqrt(sum over irrep r's positions of
+// x^2 + rn_eps), lane = channel (nrs: odd stride >= n_irreps)
 __device__ __forceinline__ void row_norms(const NodeRepr &R, const int16_t *ioff, const int16_t *ik, const float *row,
-                                          float rn_eps, float *nrm, int lane) {
-    const int C = R.C, d = R.d;
-    for (int i = lane; i < C * R.n_irreps; i += 32) {
-        const int c = i / R.n_irreps, r = i - c * R.n_irreps;
-        const int off = ioff[r], k = ik[r];
-        float s = 0.0f;
-        for (int m = 0; m < k; m++) {
-            const float v = row[c * d + off + m];
-            s = fmaf(v, v, s);
+                                          int ds, float rn_eps, float *nrm, int nrs, int lane) {
+    for (int c = lane; c < R.C; c += 32)
+        for (int r = 0; r < R.n_irreps; r++) {
+            const float *v = row + c * ds + ioff[r];
+            float s = 0.0f;
+            for (int m = 0; m < ik[r]; m++) s = fmaf(v[m], v[m], s);
+            nrm[c * nrs + r] = sqrtf(s + rn_eps);
         }
-        nrm[i] = sqrtf(s + rn_eps);
-    }
     __syncwarp();
 }
 
-__global__ void __launch_bounds__(kNodeWarps * 32) equi_layernorm_kernel(const __grid_constant__ EqLnArgs a) {
+template <bool kAsync>
+__global__ void __launch_bounds__(kNodeWarps * 32, kNodeBlocksPerSm) equi_layernorm_kernel(const __grid_constant__ EqLnArgs a) {
     extern __shared__ float nsm[];
-    const int C = a.R.C, d = a.R.d, n = C * d, nr = a.R.n_irreps;
+    const int C = a.R.C, d = a.R.d, n = C * d, nr = a.R.n_irreps, ds = odd_stride(d), nrs = odd_stride(nr);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    float *row = nsm + (size_t)warp * (n + C * nr);
-    float *nrm = row + n;               // norms, then the rescaling factors
+    float *buf = nsm + (size_t)warp * (2 * C * ds + C * nrs);
+    float *nrm = buf + 2 * C * ds;      // norms, then the rescaling factors
     __shared__ int8_t pirr_s[kMaxDim];
     __shared__ int16_t ioff_s[kNodeMaxIrreps], ik_s[kNodeMaxIrreps];
     for (int i = threadIdx.x; i < d; i += blockDim.x) pirr_s[i] = a.R.pos_irr[i];
@@ -195,35 +301,35 @@ __global__ void __launch_bounds__(kNodeWarps * 32) equi_layernorm_kernel(const _
         ik_s[i] = 2 * a.R.irr_l[i] + 1;
     }
     __syncthreads();
-    for (int64_t node = (int64_t)blockIdx.x * kNodeWarps + warp; node < a.N; node += (int64_t)gridDim.x * kNodeWarps) {
-        stage_row(row, a.x + node * n, n, lane);
-        row_norms(a.R, ioff_s, ik_s, row, a.rn_eps, nrm, lane);
+    node_loop<kAsync>(a.x, a.N, C, d, ds, buf, lane, (int64_t)blockIdx.x * kNodeWarps + warp,
+                      (int64_t)gridDim.x * kNodeWarps, [&](int64_t node, float *row) {
+        row_norms(a.R, ioff_s, ik_s, row, ds, a.rn_eps, nrm, nrs, lane);
         for (int r = 0; r < nr; r++) {
             if (a.ln_w) {
                 float s = 0.0f;
-                for (int c = lane; c < C; c += 32) s += nrm[c * nr + r];
+                for (int c = lane; c < C; c += 32) s += nrm[c * nrs + r];
                 const float mu = nwsum(s) / (float)C;
                 float q = 0.0f;
                 for (int c = lane; c < C; c += 32) {
-                    const float t = nrm[c * nr + r] - mu;
+                    const float t = nrm[c * nrs + r] - mu;
                     q = fmaf(t, t, q);
                 }
                 const float rstd = rsqrtf(nwsum(q) / (float)C + a.ln_eps);
                 for (int c = lane; c < C; c += 32) {
-                    const float v = nrm[c * nr + r];
+                    const float v = nrm[c * nrs + r];
                     const float ln = (v - mu) * rstd * a.ln_w[c] + a.ln_b[c];
-                    nrm[c * nr + r] = ln / (v + a.eps);
+                    nrm[c * nrs + r] = ln / (v + a.eps);
                 }
             } else {
-                for (int c = lane; c < C; c += 32) nrm[c * nr + r] = 1.0f / (nrm[c * nr + r] + a.eps);
+                for (int c = lane; c < C; c += 32) nrm[c * nrs + r] = 1.0f / (nrm[c * nrs + r] + a.eps);
             }
         }
         __syncwarp();
-        float *orow = a.out + node * n;
-        RowWalk w(lane, d);
-        for (int j = lane; j < n; j += 32, w.next()) orow[j] = row[j] * nrm[w.c * nr + pirr_s[w.p]];
-        __syncwarp();
-    }
+        for (int c = lane; c < C; c += 32)
+#pragma unroll 4
+            for (int p = 0; p < d; p++) row[c * ds + p] *= nrm[c * nrs + pirr_s[p]];
+        write_row_ds(a.out + node * n, row, C, d, ds, lane);
+    });
 }
 
 struct RepNormArgs {
@@ -236,56 +342,66 @@ struct RepNormArgs {
     int64_t N;
 };
 
-__global__ void __launch_bounds__(kNodeWarps * 32) rep_norm_kernel(const __grid_constant__ RepNormArgs a) {
+template <bool kAsync>
+__global__ void __launch_bounds__(kNodeWarps * 32, kNodeBlocksPerSm) rep_norm_kernel(const __grid_constant__ RepNormArgs a) {
     extern __shared__ float nsm[];
-    const int C = a.R.C, d = a.R.d, n = C * d, nr = a.R.n_irreps;
+    const int C = a.R.C, d = a.R.d, nr = a.R.n_irreps, ds = odd_stride(d);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    float *row = nsm + (size_t)warp * n;
+    float *buf = nsm + (size_t)warp * 2 * C * ds;
     __shared__ int16_t ioff_s[kNodeMaxIrreps], ik_s[kNodeMaxIrreps];
     for (int i = threadIdx.x; i < nr; i += blockDim.x) {
         ioff_s[i] = a.R.irr_off[i];
         ik_s[i] = 2 * a.R.irr_l[i] + 1;
     }
     __syncthreads();
-    for (int64_t node = (int64_t)blockIdx.x * kNodeWarps + warp; node < a.N; node += (int64_t)gridDim.x * kNodeWarps) {
-        stage_row(row, a.x + node * n, n, lane);
+    node_loop<kAsync>(a.x, a.N, C, d, ds, buf, lane, (int64_t)blockIdx.x * kNodeWarps + warp,
+                      (int64_t)gridDim.x * kNodeWarps, [&](int64_t node, float *row) {
         float *o = a.norms + node * (int64_t)C * nr;
-        for (int i = lane; i < C * nr; i += 32) {
-            const int c = i / nr, r = i - c * nr;
-            const int off = ioff_s[r], k = ik_s[r];
-            float s = 0.0f;
-            for (int m = 0; m < k; m++) {
-                const float v = row[c * d + off + m];
-                s = fmaf(v, v, s);
+        for (int c = lane; c < C; c += 32)
+            for (int r = 0; r < nr; r++) {
+                const float *v = row + c * ds + ioff_s[r];
+                float s = 0.0f;
+                for (int m = 0; m < ik_s[r]; m++) s = fmaf(v[m], v[m], s);
+                o[c * nr + r] = sqrtf(s + a.eps);
             }
-            o[i] = sqrtf(s + a.eps);
-        }
-        __syncwarp();
-    }
+    });
 }
 
-// out[n, c, p] = x[n, c, p] * sigmoid(z[n, c * n_irreps + irrep(p)]); one warp per node,
-// the node's gates computed once into shared memory.
-__global__ void __launch_bounds__(kNodeWarps * 32) gate_kernel(const __grid_constant__ RepNormArgs a) {
+// out[n, c, p] = x[n, c, p] * sigmoid(z[n, c * n_irreps + irrep(p)]); one warp per node:
+// the node's gates into shared memory (coalesced z reads), the row staged, scaled with
+// lane = channel and written back coalesced.
+template <bool kAsync>
+__global__ void __launch_bounds__(kNodeWarps * 32, kNodeBlocksPerSm) gate_kernel(const __grid_constant__ RepNormArgs a) {
     extern __shared__ float nsm[];
-    const int C = a.R.C, d = a.R.d, n = C * d, nr = a.R.n_irreps;
+    const int C = a.R.C, d = a.R.d, n = C * d, nr = a.R.n_irreps, ds = odd_stride(d);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    float *gs = nsm + (size_t)warp * C * nr;
+    float *buf = nsm + (size_t)warp * (2 * C * ds + C * nr);
+    float *gs = buf + 2 * C * ds;
     __shared__ int8_t pirr_s[kMaxDim];
     for (int i = threadIdx.x; i < d; i += blockDim.x) pirr_s[i] = a.R.pos_irr[i];
     __syncthreads();
-    for (int64_t node = (int64_t)blockIdx.x * kNodeWarps + warp; node < a.N; node += (int64_t)gridDim.x * kNodeWarps) {
+    node_loop<kAsync>(a.x, a.N, C, d, ds, buf, lane, (int64_t)blockIdx.x * kNodeWarps + warp,
+                      (int64_t)gridDim.x * kNodeWarps, [&](int64_t node, float *row) {
         const float *zr = a.z + node * (int64_t)C * nr;
-        for (int i = lane; i < C * nr; i += 32) gs[i] = 1.0f / (1.0f + expf(-__ldg(zr + i)));
+        {
+            constexpr int kB = 8;            // all of a batch's loads in flight before the stores
+            for (int i0 = lane; i0 < C * nr; i0 += 32 * kB) {
+                float z[kB];
+#pragma unroll
+                for (int u = 0; u < kB; u++)
+                    if (i0 + 32 * u < C * nr) z[u] = __ldg(zr + i0 + 32 * u);
+#pragma unroll
+                for (int u = 0; u < kB; u++)
+                    if (i0 + 32 * u < C * nr) gs[i0 + 32 * u] = 1.0f / (1.0f + expf(-z[u]));
+            }
+        }
         __syncwarp();
-        const float *xr = a.x + node * n;
-        float *orow = a.out + node * n;
-        RowWalk w(lane, d);
-        for (int j = lane; j < n; j += 32, w.next()) orow[j] = __ldg(xr + j) * gs[w.c * nr + pirr_s[w.p]];
-        __syncwarp();
-    }
+        for (int c = lane; c < C; c += 32)
+#pragma unroll 4
+            for (int p = 0; p < d; p++) row[c * ds + p] *= gs[c * nr + pirr_s[p]];
+        write_row_ds(a.out + node * n, row, C, d, ds, lane);
+    });
 }
-
 // ---------------------------------------------------------------------------
 // Position-major layout for EquivariantLinear (flash_eq/layers/linear.py:172-268):
 // xt[p][n][c] = x[n][c][p].  Each irrep's positions p = off .. off + 2l are then one
@@ -386,6 +502,11 @@ int fill_node_repr(const int32_t *lvals, int32_t n, int32_t C, NodeRepr *R) {
     return FEQ_OK;
 }
 
+// the cp.async row pipeline applies: odd d (no row padding), whole float4 rows, aligned input
+bool node_async(const float *x, int C, int d) {
+    return (d & 1) && ((int64_t)C * d) % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+}
+
 int node_grid(int64_t N) { return (int)min64((N + kNodeWarps - 1) / kNodeWarps, 148 * 16); }
 
 int set_smem(const void *fn, size_t smem) {
@@ -429,10 +550,11 @@ int feq_node_sep_layernorm(const float *x, int64_t num_nodes, int32_t C, const i
     a.eps = eps;
     a.out = out;
     a.N = num_nodes;
-    const size_t smem = sizeof(float) * kNodeWarps * (size_t)C * a.R.d;
-    if ((rc = set_smem((const void *)sep_layernorm_kernel, smem)) != FEQ_OK) return rc;
+    const size_t smem = sizeof(float) * ((size_t)kNodeWarps * 2 * C * odd_stride(a.R.d) + (size_t)C * (2 * a.nscalar + 1));
+    const auto k = node_async(x, C, a.R.d) ? sep_layernorm_kernel<true> : sep_layernorm_kernel<false>;
+    if ((rc = set_smem((const void *)k, smem)) != FEQ_OK) return rc;
     ProfScope ps("node_norm", (cudaStream_t)stream);
-    sep_layernorm_kernel<<<node_grid(num_nodes), kNodeWarps * 32, smem, (cudaStream_t)stream>>>(a);
+    k<<<node_grid(num_nodes), kNodeWarps * 32, smem, (cudaStream_t)stream>>>(a);
     FEQ_LAUNCH_CHECK();
     return FEQ_OK;
 }
@@ -455,10 +577,11 @@ int feq_node_layernorm(const float *x, int64_t num_nodes, int32_t C, const int32
     a.eps = eps;
     a.out = out;
     a.N = num_nodes;
-    const size_t smem = sizeof(float) * kNodeWarps * ((size_t)C * a.R.d + (size_t)C * n_lvals);
-    if ((rc = set_smem((const void *)equi_layernorm_kernel, smem)) != FEQ_OK) return rc;
+    const size_t smem = sizeof(float) * kNodeWarps * ((size_t)2 * C * odd_stride(a.R.d) + (size_t)C * odd_stride(n_lvals));
+    const auto k = node_async(x, C, a.R.d) ? equi_layernorm_kernel<true> : equi_layernorm_kernel<false>;
+    if ((rc = set_smem((const void *)k, smem)) != FEQ_OK) return rc;
     ProfScope ps("node_norm", (cudaStream_t)stream);
-    equi_layernorm_kernel<<<node_grid(num_nodes), kNodeWarps * 32, smem, (cudaStream_t)stream>>>(a);
+    k<<<node_grid(num_nodes), kNodeWarps * 32, smem, (cudaStream_t)stream>>>(a);
     FEQ_LAUNCH_CHECK();
     return FEQ_OK;
 }
@@ -476,10 +599,11 @@ int feq_node_rep_norm(const float *x, int64_t num_nodes, int32_t C, const int32_
     a.eps = eps;
     a.norms = norms;
     a.N = num_nodes;
-    const size_t smem = sizeof(float) * kNodeWarps * (size_t)C * a.R.d;
-    if ((rc = set_smem((const void *)rep_norm_kernel, smem)) != FEQ_OK) return rc;
+    const size_t smem = sizeof(float) * kNodeWarps * (size_t)2 * C * odd_stride(a.R.d);
+    const auto k = node_async(x, C, a.R.d) ? rep_norm_kernel<true> : rep_norm_kernel<false>;
+    if ((rc = set_smem((const void *)k, smem)) != FEQ_OK) return rc;
     ProfScope ps("node_norm", (cudaStream_t)stream);
-    rep_norm_kernel<<<node_grid(num_nodes), kNodeWarps * 32, smem, (cudaStream_t)stream>>>(a);
+    k<<<node_grid(num_nodes), kNodeWarps * 32, smem, (cudaStream_t)stream>>>(a);
     FEQ_LAUNCH_CHECK();
     return FEQ_OK;
 }
@@ -536,10 +660,11 @@ int feq_node_gate(const float *x, const float *z, int64_t num_nodes, int32_t C, 
     a.z = z;
     a.out = out;
     a.N = num_nodes;
-    const size_t smem = sizeof(float) * kNodeWarps * (size_t)C * n_lvals;
-    if ((rc = set_smem((const void *)gate_kernel, smem)) != FEQ_OK) return rc;
+    const size_t smem = sizeof(float) * kNodeWarps * ((size_t)2 * C * odd_stride(a.R.d) + (size_t)C * n_lvals);
+    const auto k = node_async(x, C, a.R.d) ? gate_kernel<true> : gate_kernel<false>;
+    if ((rc = set_smem((const void *)k, smem)) != FEQ_OK) return rc;
     ProfScope ps("node_gate", (cudaStream_t)stream);
-    gate_kernel<<<node_grid(num_nodes), kNodeWarps * 32, smem, (cudaStream_t)stream>>>(a);
+    k<<<node_grid(num_nodes), kNodeWarps * 32, smem, (cudaStream_t)stream>>>(a);
     FEQ_LAUNCH_CHECK();
     return FEQ_OK;
 }
