@@ -105,6 +105,26 @@ def test_attn_pool_backward_matches_autograd_of_reference(cuda_device, H, reduce
         _close(kg.grad, k64.grad, k32.grad, OP_TOL, "k")
 
 
+@pytest.mark.parametrize("Cv,dv,H", [(64, 25, 8), (64, 9, 8), (32, 16, 4), (7, 9, 1)])
+def test_attn_pool_forward_row_sizes(cuda_device, Cv, dv, H):
+    """Forward pooling across V row sizes: chunks of 9 to 32 edges through shared memory
+    (bulk-copied rows), and rows that do not split into whole float4 head slices (7 x 9)."""
+    dev = cuda_device
+    N, E, C, d = 50, 600, 16, 9
+    src, dst = _graph_edges(N, E, seed=Cv + dv)
+    E = src.shape[0]
+    g = torch.Generator().manual_seed(5)
+    qk = torch.randn(N, 2 * C, d, generator=g)
+    v = torch.randn(E, Cv, dv, generator=g)
+    log_scale = torch.tensor(-1.2)
+    graph = fe.Graph(src=src.to(dev), dst=dst.to(dev), num_nodes=N)
+    out = aag.attn_pool(qk.to(dev), v.to(dev), None, log_scale.to(dev), graph, H, float(log_scale.exp()), None,
+                        "sum")
+    r64 = _ref_attn_pool(qk.double(), v.double(), src, dst, N, H, log_scale.double(), None, None, "sum")
+    r32 = _ref_attn_pool(qk, v, src, dst, N, H, log_scale, None, None, "sum")
+    _close(out, r64, r32, OP_TOL, "out")
+
+
 def test_attn_pool_backward_deterministic_and_empty(cuda_device):
     dev = cuda_device
     N, E = 40, 700
