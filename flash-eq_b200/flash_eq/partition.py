@@ -4,9 +4,12 @@ No counterpart in the reference, which runs a graph on one device.  Rank r owns 
 contiguous node range [starts[r], starts[r+1]) — boundaries chosen on the cumulative
 in-degree so every rank holds about E / world_size edges — and every edge whose dst it
 owns.  Softmax, pooling and the edgewise mix of an edge then only need the src-side
-node rows; those are exchanged once per attention layer with one NCCL
-``all_gather_into_tensor`` of each rank's owned rows (padded to a common row count, so
-the gathered array is indexed by ``rank * rows_per_rank + local row``).
+node rows.  A rank's edges read its own rows plus a halo: the other ranks' nodes that
+are the src of one of its edges.  Once per attention layer the halo rows are exchanged
+with one NCCL ``all_to_all_single`` (each owner sends exactly the rows each peer reads),
+and ``src`` indexes the array [owned rows; halo rows] (halo in global node order).  Every
+rank holds the whole graph, so every rank derives every rank's halo locally and the
+exchange plan needs no communication.
 
     part = partition_graph(graph, world_size, rank, group)
     y_owned = model(coordinates, x[part.node_start:part.node_end], part)
@@ -38,23 +41,28 @@ def dst_range_bounds(dst: torch.Tensor, num_nodes: int, world_size: int) -> torc
 
 @dataclass
 class PartitionedGraph(Graph):
-    """The edges of one rank: ``src`` indexes the gathered (padded) node array, ``dst`` the
-    rank's own rows; ``num_nodes`` is the number of owned rows."""
+    """The edges of one rank: ``src`` indexes [owned rows; halo rows] (``num_src_nodes``
+    rows), ``dst`` the rank's own rows; ``num_nodes`` is the number of owned rows.
+    Exchange plan: ``send_idx`` lists the owned rows the peers read, grouped by peer
+    (``send_counts``); ``recv_counts[r]`` halo rows come from rank r."""
     num_src_nodes: int = 0
     node_start: int = 0
     node_end: int = 0
-    rows_per_rank: int = 0
     world_size: int = 1
     rank: int = 0
     src_global: torch.Tensor | None = None
     dst_global: torch.Tensor | None = None
     edge_ids: torch.Tensor | None = None
+    halo_global: torch.Tensor | None = None
+    send_idx: torch.Tensor | None = None
+    send_counts: list = field(default_factory=list)
+    recv_counts: list = field(default_factory=list)
     group: object = field(default=None, repr=False, compare=False)
 
     def __post_init__(self) -> None:
         if self.src.dim() != 1 or self.dst.dim() != 1 or self.src.shape[0] != self.dst.shape[0]:
             raise ValueError("src and dst must be 1D tensors of the same length")
-        if self.num_nodes < 0 or self.num_src_nodes < 1:
+        if self.num_nodes < 0 or self.num_src_nodes < 0 or self.num_src_nodes < self.num_nodes:
             raise ValueError(f"bad partition sizes: {self.num_nodes} owned rows, {self.num_src_nodes} source rows")
 
     def _key(self):
@@ -66,67 +74,94 @@ class PartitionedGraph(Graph):
     def _num_src_rows(self) -> int:
         return self.num_src_nodes
 
+    @property
+    def num_halo(self) -> int:
+        return self.num_src_nodes - self.num_nodes
+
     def to(self, device) -> "PartitionedGraph":
         mv = lambda t: None if t is None else t.to(device)
         return PartitionedGraph(src=self.src.to(device), dst=self.dst.to(device), num_nodes=self.num_nodes,
                                 num_src_nodes=self.num_src_nodes, node_start=self.node_start,
-                                node_end=self.node_end, rows_per_rank=self.rows_per_rank,
-                                world_size=self.world_size, rank=self.rank, src_global=mv(self.src_global),
-                                dst_global=mv(self.dst_global), edge_ids=mv(self.edge_ids), group=self.group)
+                                node_end=self.node_end, world_size=self.world_size, rank=self.rank,
+                                src_global=mv(self.src_global), dst_global=mv(self.dst_global),
+                                edge_ids=mv(self.edge_ids), halo_global=mv(self.halo_global),
+                                send_idx=mv(self.send_idx), send_counts=list(self.send_counts),
+                                recv_counts=list(self.recv_counts), group=self.group)
 
     def edge_vectors(self, coordinates: torch.Tensor) -> torch.Tensor:
         """coordinates[src] - coordinates[dst] with global node ids (coordinates: (N, 3))."""
         return coordinates[self.src_global] - coordinates[self.dst_global]
 
     def gather_nodes(self, owned: torch.Tensor) -> torch.Tensor:
-        """All ranks' owned rows (num_nodes, ...) -> (world_size * rows_per_rank, ...).
+        """Owned rows (num_nodes, ...) -> [owned rows; halo rows] (num_src_nodes, ...).
 
-        Differentiable: the backward sums every rank's gradient of the gathered array
-        (a reduce-scatter) and keeps this rank's owned rows."""
+        Differentiable: the backward returns each halo row's gradient to its owner (the
+        reverse exchange) and adds it, peer by peer in rank order, onto the owned rows."""
         if owned.shape[0] != self.num_nodes:
             raise ValueError(f"expected {self.num_nodes} owned rows, got {owned.shape[0]}")
         if self.world_size == 1:
             return owned.contiguous()
         if torch.is_grad_enabled() and owned.requires_grad:
             return _GatherNodes.apply(owned, self)
-        return self._all_gather(owned.detach())
+        return self._forward_exchange(owned.detach())
 
-    def _all_gather(self, owned: torch.Tensor) -> torch.Tensor:
-        import torch.distributed as dist
+    def _forward_exchange(self, owned: torch.Tensor) -> torch.Tensor:
+        owned = owned.contiguous()
+        send = owned.index_select(0, self.send_idx)
+        halo = _exchange(send, self.send_counts, self.recv_counts, self.group)
+        return torch.cat([owned, halo])
 
-        pad = owned.new_zeros((self.rows_per_rank,) + tuple(owned.shape[1:]))
-        pad[: owned.shape[0]] = owned
-        if dist.get_backend(self.group) == "gloo":      # host-side runs (tests): list form
-            parts = [torch.empty_like(pad) for _ in range(self.world_size)]
-            dist.all_gather(parts, pad, group=self.group)
-            return torch.cat(parts)
-        out = owned.new_empty((self.world_size * self.rows_per_rank,) + tuple(owned.shape[1:]))
-        dist.all_gather_into_tensor(out, pad, group=self.group)
-        return out
+
+def _exchange(send: torch.Tensor, send_counts, recv_counts, group) -> torch.Tensor:
+    """Rows send[...] split by ``send_counts`` go to ranks 0..W-1; returns the rows received,
+    split by ``recv_counts`` in rank order."""
+    import torch.distributed as dist
+
+    recv = send.new_empty((int(sum(recv_counts)),) + tuple(send.shape[1:]))
+    if dist.get_backend(group) == "gloo":          # host-side runs (tests): point to point
+        me = dist.get_rank(group)
+        so = [0] + list(torch.tensor(send_counts).cumsum(0).tolist())
+        ro = [0] + list(torch.tensor(recv_counts).cumsum(0).tolist())
+        reqs = []
+        for r in range(len(send_counts)):
+            if r == me:
+                recv[ro[r]:ro[r + 1]] = send[so[r]:so[r + 1]]
+                continue
+            if send_counts[r]:
+                reqs.append(dist.isend(send[so[r]:so[r + 1]].contiguous(), r, group=group))
+            if recv_counts[r]:
+                buf = torch.empty_like(recv[ro[r]:ro[r + 1]])
+                reqs.append((dist.irecv(buf, r, group=group), ro[r], buf))
+        for q in reqs:
+            if isinstance(q, tuple):
+                q[0].wait()
+                recv[q[1]:q[1] + q[2].shape[0]] = q[2]
+            else:
+                q.wait()
+        return recv
+    dist.all_to_all_single(recv, send.contiguous(), output_split_sizes=list(recv_counts),
+                           input_split_sizes=list(send_counts), group=group)
+    return recv
 
 
 class _GatherNodes(torch.autograd.Function):
     @staticmethod
     def forward(ctx, owned, part):
         ctx.part = part
-        return part._all_gather(owned)
+        return part._forward_exchange(owned)
 
     @staticmethod
     def backward(ctx, grad):
-        import torch.distributed as dist
-
         part = ctx.part
-        rows = part.rows_per_rank
         grad = grad.contiguous()
-        if dist.get_backend(part.group) == "gloo":      # host-side runs (tests): all-reduce, then slice
-            total = grad.clone()
-            dist.all_reduce(total, group=part.group)
-            mine = total[part.rank * rows: part.rank * rows + part.num_nodes]
-        else:
-            out = grad.new_empty((rows,) + tuple(grad.shape[1:]))
-            dist.reduce_scatter_tensor(out, grad, group=part.group)
-            mine = out[: part.num_nodes]
-        return mine.contiguous(), None
+        mine = grad[: part.num_nodes].clone()
+        back = _exchange(grad[part.num_nodes:].contiguous(), part.recv_counts, part.send_counts, part.group)
+        off = 0
+        for c in part.send_counts:                 # fixed order: bitwise reproducible sums
+            if c:
+                mine.index_add_(0, part.send_idx[off:off + c], back[off:off + c])
+            off += c
+        return mine, None
 
 
 def partition_graph(graph: Graph, world_size: int, rank: int, group=None) -> PartitionedGraph:
@@ -134,18 +169,31 @@ def partition_graph(graph: Graph, world_size: int, rank: int, group=None) -> Par
     if not 0 <= rank < world_size:
         raise ValueError(f"rank {rank} outside [0, {world_size})")
     N = graph.num_nodes
-    bounds = dst_range_bounds(graph.dst, N, world_size).to(graph.src.device)
-    counts = bounds[1:] - bounds[:-1]
-    rows = max(1, int(counts.max()))
+    dev = graph.src.device
+    bounds = dst_range_bounds(graph.dst, N, world_size).to(dev)
     start, end = int(bounds[rank]), int(bounds[rank + 1])
     dst = graph.dst.to(torch.int64)
     src = graph.src.to(torch.int64)
-    mask = (dst >= start) & (dst < end)
-    eids = torch.nonzero(mask, as_tuple=False).flatten()          # original edge order kept
+    own_e = torch.searchsorted(bounds[1:], dst, right=True)       # rank holding each edge
+    own_s = torch.searchsorted(bounds[1:], src, right=True)       # rank owning its src row
+    # every rank's halo: unique (reader, node) pairs with a src owned elsewhere, sorted by
+    # reader, then node id (so each reader's halo is grouped by owner, in rank order)
+    cross = own_s != own_e
+    pairs = torch.unique(own_e[cross] * max(N, 1) + src[cross])
+    reader, node = pairs // max(N, 1), pairs % max(N, 1)
+    node_owner = torch.searchsorted(bounds[1:], node, right=True)
+    halo = node[reader == rank]
+    recv_counts = torch.bincount(node_owner[reader == rank], minlength=world_size).tolist()
+    sent = node_owner == rank
+    send_idx = node[sent] - start
+    send_counts = torch.bincount(reader[sent], minlength=world_size).tolist()
+    # this rank's edges, original edge order kept
+    eids = torch.nonzero(own_e == rank, as_tuple=False).flatten()
     s_g, d_g = src[eids], dst[eids]
-    owner = torch.searchsorted(bounds[1:], s_g, right=True)
-    s_pad = owner * rows + (s_g - bounds[owner])
-    return PartitionedGraph(src=s_pad, dst=d_g - start, num_nodes=end - start,
-                            num_src_nodes=world_size * rows, node_start=start, node_end=end,
-                            rows_per_rank=rows, world_size=world_size, rank=rank, src_global=s_g,
-                            dst_global=d_g, edge_ids=eids, group=group)
+    local = (s_g >= start) & (s_g < end)
+    s_loc = torch.where(local, s_g - start, (end - start) + torch.searchsorted(halo, s_g))
+    return PartitionedGraph(src=s_loc, dst=d_g - start, num_nodes=end - start,
+                            num_src_nodes=(end - start) + int(halo.shape[0]), node_start=start, node_end=end,
+                            world_size=world_size, rank=rank, src_global=s_g, dst_global=d_g, edge_ids=eids,
+                            halo_global=halo, send_idx=send_idx, send_counts=send_counts,
+                            recv_counts=recv_counts, group=group)

@@ -1,5 +1,6 @@
 """Host logic of the dst-range partition (no GPU): boundaries, edge ownership, the
-padded src numbering and the row exchange, with two gloo ranks on CPU."""
+[owned; halo] src numbering, the exchange plan and the row exchange (forward and
+backward), with two and three gloo ranks on CPU."""
 from __future__ import annotations
 
 import os
@@ -41,17 +42,32 @@ def test_partition_covers_every_edge_once_and_balances(world):
         assert int(p.dst.min()) >= 0 and int(p.dst.max()) < p.num_nodes
 
 
-def test_padded_src_numbering_matches_gathered_rows():
+@pytest.mark.parametrize("world", [2, 4])
+def test_halo_numbering_and_exchange_plan(world):
     gr = _graph(n=301)
-    world = 4
     parts = [partition_graph(gr, world, r) for r in range(world)]
     x = torch.randn(gr.num_nodes, 3, 2)
-    rows = parts[0].rows_per_rank
-    gathered = torch.zeros(world * rows, 3, 2)
-    for r, p in enumerate(parts):
-        gathered[r * rows: r * rows + p.num_nodes] = x[p.node_start:p.node_end]
     for p in parts:
-        assert torch.equal(gathered[p.src], x[p.src_global])
+        # src indexes [owned rows; halo rows], the halo in global node order
+        rows = torch.cat([x[p.node_start:p.node_end], x[p.halo_global]])
+        assert rows.shape[0] == p.num_src_nodes
+        assert torch.equal(rows[p.src], x[p.src_global])
+        assert torch.equal(torch.sort(p.halo_global).values, p.halo_global)
+        assert not bool(((p.halo_global >= p.node_start) & (p.halo_global < p.node_end)).any())
+        # the halo is exactly the foreign src nodes of this rank's edges
+        foreign = p.src_global[(p.src_global < p.node_start) | (p.src_global >= p.node_end)]
+        assert torch.equal(torch.unique(foreign), p.halo_global)
+    for a in range(world):
+        for b in range(world):
+            assert parts[a].send_counts[b] == parts[b].recv_counts[a]
+        # what a sends to b, in order, is b's halo block owned by a
+        off = 0
+        for b in range(world):
+            c = parts[a].send_counts[b]
+            sent = parts[a].send_idx[off:off + c] + parts[a].node_start
+            ro = sum(parts[b].recv_counts[:a])
+            assert torch.equal(sent, parts[b].halo_global[ro:ro + c])
+            off += c
 
 
 def test_bounds_empty_and_single():
@@ -76,7 +92,7 @@ def _worker(rank, world, port, q):
         x = torch.randn(gr.num_nodes, 4, 9, generator=torch.Generator().manual_seed(5))
         p = partition_graph(gr, world, rank)
         full = p.gather_nodes(x[p.node_start:p.node_end].contiguous())
-        ok = bool(torch.equal(full[p.src], x[p.src_global])) and full.shape[0] == world * p.rows_per_rank
+        ok = bool(torch.equal(full[p.src], x[p.src_global])) and full.shape[0] == p.num_src_nodes
         # backward: every rank's gradient of its gathered rows is summed onto the owner
         coef = torch.randn(gr.num_edges, 4, 9, generator=torch.Generator().manual_seed(6))
         xo = x[p.node_start:p.node_end].clone().requires_grad_()
@@ -87,11 +103,12 @@ def _worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def test_gather_nodes_two_gloo_ranks():
+@pytest.mark.parametrize("world", [2, 3])
+def test_gather_nodes_gloo_ranks(world):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
     for pr in procs:
         pr.start()
     res = [q.get(timeout=120) for _ in procs]
