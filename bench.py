@@ -833,7 +833,7 @@ def make_walk(n: int, seed: int) -> torch.Tensor:
 
 def run_giant(args):
     """One step = the 2-layer EquivariantTransformer forward over the rank's dst range of the
-    1 M-node graph; per layer the src-side rows are all-gathered (NCCL) from their owners.
+    1 M-node graph; per layer the rank's halo rows come from their owners (NCCL all-to-all).
     Graph built once (GPU kNN) and partitioned before the timed region; strong scaling."""
     import flash_eq as fe
     from flash_eq.cuda import _lib
@@ -870,6 +870,7 @@ def run_giant(args):
     lo, hi = (part.node_start, part.node_end) if world > 1 else (0, n)
     x_own = x[lo:hi].to(dev)
     E_total, E_rank = graph.num_edges, part.num_edges
+    halo_rows = part.num_halo if world > 1 else 0          # rows received per exchange
     del graph
 
     def step():
@@ -947,9 +948,11 @@ def run_giant(args):
             "config": {"workload": f"config5: 3-D random walk of {n} nodes (3.8 A isotropic steps, seed 4), "
                                    f"16-NN graph built on the GPU (Graph.knn), E={E_total}; 2-layer "
                                    "EquivariantTransformer, Repr([0,1,2],64) in/hidden/out, 8 heads, max_dist 10",
-                       "global_edges": E_total, "edges_rank0": E_rank,
-                       "parallelism": f"dst-range partition over {world} GPU(s), NCCL all-gather of the src-side "
-                                      "rows per layer" if world > 1 else "whole graph on one GPU",
+                       "global_edges": E_total, "edges_rank0": E_rank, "owned_rows_rank0": hi - lo,
+                       "halo_rows_rank0": halo_rows,
+                       "parallelism": f"dst-range partition over {world} GPU(s), NCCL halo exchange "
+                                      "(all_to_all_single) of the src-side rows per layer" if world > 1
+                                      else "whole graph on one GPU",
                        "graph_build_s": t_build,
                        "l2": f"no flush: {E_rank * row / 1e9:.1f} GB of edge rows per layer >> 126 MB L2"},
             "roofline": roofline, "stages_ms_per_step_rank0": stages, "mix": args.mix, "clocks": clocks,
