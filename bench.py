@@ -48,6 +48,11 @@ NUM_BINS = 100
 MAX_DIST = 10.0
 SEED = 1
 
+# One metric string per workload, printed by both arms (ours and --impl reference), so the
+# two lines can be compared directly.
+METRIC_CONFIG2 = "edges/sec (WignerDBasis + EquivariantEdgewiseLinear fwd)"
+METRIC_BLOCK = "edges/sec (EquivariantTransformerBlock fwd)"
+
 
 # ---------------------------------------------------------------------------
 # Workload
@@ -215,6 +220,43 @@ def cpu_reference_setup(sample_edges: int):
     return step, int(sel.numel()), threads
 
 
+def parity_rows(dist: torch.Tensor, p1: float, p2: float, num_bins: int, n_rows: int = 16384, seed: int = 0):
+    """A fixed sample of edge ids for the parity check of a timed output: up to 48 edges of
+    every distance bin present, up to 2048 of the most populated bin, the rest drawn
+    uniformly (seeded), n_rows in all, sorted.  Linear bins, as the workload uses."""
+    dist = dist.detach().float().cpu()
+    E = dist.numel()
+    lo = ((dist - p1) * p2).clamp(0.0, float(num_bins)).floor().long().clamp(max=num_bins - 1)
+    order = torch.argsort(lo, stable=True)
+    counts = torch.bincount(lo, minlength=num_bins)
+    starts = torch.cumsum(counts, 0) - counts
+    picks = []
+    for b in torch.nonzero(counts).flatten().tolist():
+        picks.append(order[starts[b]:starts[b] + min(48, int(counts[b]))])
+    top = int(torch.argmax(counts))
+    picks.append(order[starts[top]:starts[top] + min(2048, int(counts[top]))])
+    sel = torch.unique(torch.cat(picks))
+    if sel.numel() < min(n_rows, E):
+        taken = torch.zeros(E, dtype=torch.bool)
+        taken[sel] = True
+        rest = torch.randperm(E, generator=torch.Generator().manual_seed(seed))
+        rest = rest[~taken[rest]][: min(n_rows, E) - sel.numel()]
+        sel = torch.cat([sel, rest])
+    return torch.sort(sel).values, int((counts > 0).sum())
+
+
+def parity_vs_oracle(y_rows, f_rows, vec_rows, dist_rows, table, lvals, sh_scale, p1, p2, num_bins):
+    """Relative L2 error of output rows y_rows against the CPU restatement of the reference
+    path (matrix_exp basis, bmm, block-diagonal mix, bmm) in float64 on the same rows."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import feq_oracle as orc
+
+    P = orc.wigner_basis(vec_rows.double(), lvals)
+    ref = orc.edgewise_fwd(P, P, f_rows.double(), dist_rows.double(), table.double().cpu(), lvals, lvals,
+                           sh_scale, p1, p2, num_bins, False)
+    return float((y_rows.double().cpu() - ref).norm() / ref.norm())
+
+
 _CPU_WL = {}
 
 
@@ -265,7 +307,7 @@ def run_reference(args):
     dt = (time.perf_counter() - t0) / args.steps
     value = n / dt
     line = {
-        "metric": "edges/sec (fwd)", "impl": "reference", "value": value, "unit": "edges/s",
+        "metric": METRIC_CONFIG2, "impl": "reference", "value": value, "unit": "edges/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": config_block(args.gpus),
@@ -405,6 +447,8 @@ def run_ours(args):
         exe = alg * tensor_mult
         roofline = {"bound": "tensor", "achieved": alg, "peak": tc_sustained, "unit": "TFLOP/s",
                     "frac": alg / tc_sustained, "traffic": profiled_traffic("tc_mix", E),
+                    "traffic_source": "committed ncu summary profiles/tc_mix_config2.md (DRAM bytes per edge, "
+                                      "scaled to E); not measured in this run",
                     "kernel": f"tc_mix ({per_step[dom]['launches']} launches per step, one per m-block), "
                               f"CUDA events on its stream, {prof_steps} steps",
                     "peak_kind": "measured bf16 sustained (MEASURED_PEAKS.json)",
@@ -416,7 +460,9 @@ def run_ours(args):
         t = per_step[dom]["ms"] / 1e3
         gbs = E * stage_bytes.get(dom, 0) / t / 1e9
         roofline = {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak,
-                    "traffic": profiled_traffic(dom, E), "kernel": dom, "peak_kind": peak_kind}
+                    "traffic": profiled_traffic(dom, E), "kernel": dom, "peak_kind": peak_kind,
+                    "traffic_source": f"committed ncu summary profiles/{dom}_config2.md (DRAM bytes per edge, "
+                                      "scaled to E); not measured in this run"}
     for k, v in per_step.items():
         if k in stage_bytes and k != "tc_mix":
             v["hbm_gbs"] = E * stage_bytes[k] / (v["ms"] / 1e3) / 1e9
@@ -428,13 +474,33 @@ def run_ours(args):
                      "note": "whole step against the fused-path algorithmic bytes per edge "
                              "(input row + output row + 16 B, fp32)"}
 
+    # --- parity of the timed computation: one more step, a fixed row sample (every distance
+    # bin present, the most populated bin) against the float64 CPU restatement (oracle)
+    parity = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        with torch.no_grad():
+            y = step()
+        rw = layer.radial_weights
+        p1, p2 = rw.binning_params()
+        sel, nbins = parity_rows(dist_e, p1, p2, rw.num_bins)
+        sel_d = sel.to(dev)
+        with torch.no_grad():
+            table = rw()
+        err = parity_vs_oracle(y[sel_d], x[src[sel_d]], vec[sel_d], dist_e[sel_d], table, LVALS,
+                               layer.solid_harmonic_scale, p1, p2, rw.num_bins)
+        tol = 2e-2 if args.mix == "bf16" else 1e-4
+        parity = {"rel_l2": err, "tolerance": tol, "ok": err < tol, "rows": int(sel.numel()),
+                  "bins_covered": nbins, "against": "CPU restatement of the reference path in float64 "
+                                                   "(oracle/), same inputs, one step's output"}
+        del y
+
     # --- end to end through the public API from pinned host buffers
     e2e = run_e2e(args, wl, layer, basis, dev, pg, world) if args.e2e_steps > 0 else None
 
     result = None
     if rank == 0:
         result = {
-            "metric": "edges/sec (fwd, device-timed)", "value": value, "unit": "edges/s", "n_gpus": world,
+            "metric": METRIC_CONFIG2, "value": value, "unit": "edges/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16" if args.mix == "bf16" else "f32",
             "data": "synthetic", "config": config_block(world, args.nodes),
@@ -446,6 +512,8 @@ def run_ours(args):
             "e2e": e2e,
             "gpu_launches": int(launches),
         }
+        if world == 1 and not args.no_cpu_baseline:
+            result["parity"] = parity
         if world == 1 and not args.no_cpu_baseline and args.nodes == N_NODES:
             try:
                 sample, threads = pick_cpu_sample(3.0)
@@ -671,7 +739,7 @@ def run_block(args):
             step()
         dt = (time.perf_counter() - t0) / args.steps
         print(json.dumps({
-            "metric": "edges/sec (EquivariantTransformerBlock fwd)", "impl": "reference", "value": n / dt,
+            "metric": METRIC_BLOCK, "impl": "reference", "value": n / dt,
             "unit": "edges/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f32", "data": "synthetic",
@@ -780,7 +848,7 @@ def run_block(args):
                        "validation included)"}
     if rank == 0:
         result = {
-            "metric": "edges/sec (EquivariantTransformerBlock fwd, device-timed)", "value": value, "unit": "edges/s",
+            "metric": METRIC_BLOCK, "value": value, "unit": "edges/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "bf16" if args.mix == "bf16" else "f32", "data": "synthetic",

@@ -96,6 +96,10 @@ static std::atomic<long long> g_launches{0};
 
 void count_launches(int n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
 
+static std::atomic<uint64_t> g_wait_limit_ns{4000000000ull};
+
+uint64_t wait_limit_ns() { return g_wait_limit_ns.load(std::memory_order_relaxed); }
+
 struct ProfRec {
     std::string name;
     cudaEvent_t a = nullptr, b = nullptr;
@@ -636,7 +640,11 @@ const char *feq_status_string(int status) {
     }
 }
 
-int feq_abi_version(void) { return 3; }
+int feq_abi_version(void) { return 4; }
+
+uint64_t feq_set_wait_limit_ns(uint64_t limit_ns) {
+    return feq::g_wait_limit_ns.exchange(limit_ns ? limit_ns : 4000000000ull);
+}
 
 const char *feq_last_error(void) { return g_last_error.c_str(); }
 

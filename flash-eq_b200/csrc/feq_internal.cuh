@@ -142,6 +142,8 @@ int build_repr_layout(const int32_t *lvals, int32_t n, ReprLayout *out);
 int build_mix_layout(const int32_t *lin, int32_t nin, const int32_t *lout, int32_t nout,
                      int c_in, int c_out, MixLayout *out);
 void record_cuda_error(cudaError_t err);
+// Limit of every pipeline wait in the tensor-core kernels, in ns (feq_set_wait_limit_ns).
+uint64_t wait_limit_ns();
 void record_error_text(const char *msg);
 void count_launches(int n);
 

@@ -6,14 +6,14 @@
 // point gives them the block-diagonal radial mix with its scratch taken from a fixed
 // array that lives in the library's own device memory.
 //
-// The array's name is only a host-side stand-in in host code, so the host looks up
-// its device address with cudaGetSymbolAddress, once per device, with that device
-// current, and passes that address as the workspace of the ordinary entry point.
+// The array's name is only a host-side stand-in in host code, so on every call the
+// host looks up its device address with cudaGetSymbolAddress (with the caller's device
+// current) and passes that address as the workspace of the ordinary entry point.  The
+// lookup allocates nothing; doing it per call (instead of caching it) keeps the address
+// right after a device reset or a new primary context on that device.
 // Every call shares the array; overlapping calls race (see include/flasheq_b200.h).
 #include <cuda_runtime.h>
 #include <stdio.h>
-
-#include <mutex>
 
 #include "feq_internal.cuh"
 
@@ -21,22 +21,11 @@ namespace feq {
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[FEQ_NOALLOC_SCRATCH_BYTES];
 
-constexpr int kMaxDevices = 64;
-static void *g_scratch_addr[kMaxDevices];
-static std::mutex g_scratch_mutex;
-
-// Device address of g_noalloc_scratch on the current device (looked up once per device).
+// Device address of g_noalloc_scratch on the current device.
 static int scratch_address(void **addr) {
-    int dev = 0;
-    FEQ_CUDA_TRY(cudaGetDevice(&dev));
-    if (dev < 0 || dev >= kMaxDevices) return FEQ_ERR_UNSUPPORTED;
-    std::lock_guard<std::mutex> lock(g_scratch_mutex);
-    if (!g_scratch_addr[dev]) {
-        void *p = nullptr;
-        FEQ_CUDA_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch));
-        g_scratch_addr[dev] = p;
-    }
-    *addr = g_scratch_addr[dev];
+    void *p = nullptr;
+    FEQ_CUDA_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+    *addr = p;
     return FEQ_OK;
 }
 

@@ -237,12 +237,14 @@ struct RotShared {
 // Per-warp dynamic shared memory (floats): in[2] rows, the out row, scratch.
 struct RotWarpLayout {
     int in_row, out_row, scratch;   // floats, each a multiple of 4
+    uint64_t wait_ns;               // limit of each row wait (wait_limit_ns())
     __host__ __device__ int total() const { return 2 * in_row + out_row + scratch; }
 };
 
 // Bounded wait for row buffer `b`; false on time-out (status 2, the CTA aborts).
-__device__ __forceinline__ bool wait_row(RotShared &S, int w, int b, uint32_t &phase_bits, int32_t *status) {
-    const bool ok = sm100::mbar_wait(&S.bar[w][b], (phase_bits >> b) & 1u, &S.abort_flag);
+__device__ __forceinline__ bool wait_row(RotShared &S, int w, int b, uint32_t &phase_bits, int32_t *status,
+                                         uint64_t limit_ns) {
+    const bool ok = sm100::mbar_wait(&S.bar[w][b], (phase_bits >> b) & 1u, &S.abort_flag, limit_ns);
     if (ok) phase_bits ^= 1u << b;
     else set_status(status, 2);
     return ok;
@@ -335,7 +337,7 @@ rot_in_kernel(const float *__restrict__ x, const int64_t *__restrict__ src, int6
             const float *trj = trig + j * TF;
             float *fb = ws + b * WL.in_row;
             if (xr >= 0) {
-                if (!wait_row(S, w, b, phase_bits, status)) {
+                if (!wait_row(S, w, b, phase_bits, status, WL.wait_ns)) {
                     alive = false;
                     break;
                 }
@@ -462,7 +464,7 @@ rot_out_kernel(const float *__restrict__ H, int h_ld, const float *__restrict__ 
             if (j + 1 < ng) issue(j + 1);
             if constexpr (!kFactored) build_all_rblocks<false>(L, S.rdoff, trig + j * TF, s, m_s, r_s, lane);
             const float *trj = trig + j * TF;
-            if (!wait_row(S, w, b, phase_bits, status)) {
+            if (!wait_row(S, w, b, phase_bits, status, WL.wait_ns)) {
                 alive = false;
                 break;
             }
@@ -729,6 +731,7 @@ int launch_rot_in_stream(const float *x, const int64_t *src, int64_t nsrc, const
     RotWarpLayout WL;
     WL.in_row = pad4(C * L.dim);
     WL.out_row = 0;
+    WL.wait_ns = wait_limit_ns();
     const bool factored = L.lmax <= kFactoredLmax;
     WL.scratch = factored ? rot_scratch(L).trig : rot_scratch(L).total();
     const size_t smem = ((size_t)pad4(L.dim) + (size_t)kRotWarps * WL.total()) * 4;
@@ -761,6 +764,7 @@ int launch_rot_out_stream(const float *H, int h_ld, const float *dirs, const flo
     RotWarpLayout WL;
     WL.in_row = pad4(h_ld);
     WL.out_row = pad4(C * L.dim);
+    WL.wait_ns = wait_limit_ns();
     const bool factored = L.lmax <= kFactoredLmax;
     WL.scratch = factored ? rot_scratch(L).trig : rot_scratch(L).total();
     const size_t smem = ((size_t)pad4(L.dim) + (size_t)kRotWarps * WL.total()) * 4;

@@ -3,9 +3,11 @@
 // (no multicast), TMEM allocation, tcgen05.mma / commit / ld and the UMMA shared-
 // memory and instruction descriptors.
 //
-// Every wait is bounded by wall-clock time (%globaltimer): after kWaitLimitNs the
-// waiter raises the kernel's abort flag and returns false, so a lost arrival ends
-// the kernel with an error status instead of hanging the GPU.
+// Every wait is bounded by wall-clock time (%globaltimer): after a limit the waiter
+// raises the kernel's abort flag and returns false, so a lost arrival ends the kernel
+// with an error status instead of hanging the GPU.  The limit of the pipeline waits is
+// a launch parameter (feq_set_wait_limit_ns; default kWaitLimitNs); the drains of work
+// already in flight always use kWaitLimitNs.
 #pragma once
 
 #include <cuda.h>
@@ -14,7 +16,7 @@
 namespace feq {
 namespace sm100 {
 
-constexpr uint64_t kWaitLimitNs = 4000000000ull;   // 4 s
+constexpr uint64_t kWaitLimitNs = 4000000000ull;   // 4 s: default and drain limit
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -56,8 +58,9 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 
 // Wait for phase `parity` of `bar` to complete.  Gives up (returns false) when the
-// CTA's abort flag is raised or after kWaitLimitNs, raising the flag itself.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
+// CTA's abort flag is raised or after limit_ns, raising the flag itself.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag,
+                                          uint64_t limit_ns) {
     const uint32_t b = smem_u32(bar);
     if (mbar_try_wait(b, parity)) return true;
     const uint64_t t0 = globaltimer();
@@ -65,7 +68,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volati
         if (mbar_try_wait(b, parity)) return true;
         if ((i & 63) == 0) {
             if (*abort_flag) return false;
-            if (globaltimer() - t0 > kWaitLimitNs) {
+            if (globaltimer() - t0 > limit_ns) {
                 *abort_flag = 1;
                 return false;
             }

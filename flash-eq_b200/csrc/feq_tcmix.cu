@@ -48,6 +48,7 @@ struct TcGemmParams {
     float *H;               // (E, h_ld) sorted rows
     float *Hd;              // optional, same layout: D_hi - D_lo (the t-derivative of H)
     int32_t *status;        // set to 2 when a wait timed out
+    uint64_t wait_ns;       // limit of each pipeline wait (wait_limit_ns())
 };
 
 template <int kSplit>
@@ -108,7 +109,7 @@ tc_mix_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ 
             const int rb0 = T.z * P.npad + nt * kTcN, rb1 = rb0 + P.npad;
             for (int ks = 0; ks < P.k_steps; ks++, it++) {
                 const int s = it % kStages, r = it / kStages;
-                if (r > 0 && !mbar_wait(&empty_bar[s], (r - 1) & 1, abort_flag)) break;
+                if (r > 0 && !mbar_wait(&empty_bar[s], (r - 1) & 1, abort_flag, P.wait_ns)) break;
                 uint8_t *base = smem + (size_t)s * kStageBytes;
                 mbar_arrive_expect_tx(&full_bar[s], kStageBytes);
                 const int ax = P.a_col0 + ks * kTcK, bx = ks * kTcK;
@@ -129,13 +130,13 @@ tc_mix_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ 
         int it = 0, j = 0;
         for (int item = blockIdx.x; item < n_items && !*abort_flag; item += gridDim.x, j++) {
             const int buf = j & 1, rr = j >> 1;
-            if (rr > 0 && !mbar_wait(&tempty_bar[buf], (rr - 1) & 1, abort_flag)) break;
+            if (rr > 0 && !mbar_wait(&tempty_bar[buf], (rr - 1) & 1, abort_flag, P.wait_ns)) break;
             tc_fence_after();
             const uint32_t d_lo = tmem + buf * 2 * kTcN;
             bool ok = true;
             for (int ks = 0; ks < P.k_steps; ks++, it++) {
                 const int s = it % kStages, r = it / kStages;
-                if (!mbar_wait(&full_bar[s], r & 1, abort_flag)) {
+                if (!mbar_wait(&full_bar[s], r & 1, abort_flag, P.wait_ns)) {
                     ok = false;
                     break;
                 }
@@ -173,7 +174,7 @@ tc_mix_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ 
         int j = 0;
         for (int item = blockIdx.x; item < n_items; item += gridDim.x, j++) {
             const int buf = j & 1, rr = j >> 1;
-            if (!mbar_wait(&tfull_bar[buf], rr & 1, abort_flag)) break;
+            if (!mbar_wait(&tfull_bar[buf], rr & 1, abort_flag, P.wait_ns)) break;
             tc_fence_after();
             const int tile = item / P.n_tiles_n, nt = item - tile * P.n_tiles_n;
             const int4 T = P.tiles[tile];
@@ -247,6 +248,7 @@ struct TcGramParams {
     const int64_t *seg;     // (nb + 1,) padded segment starts, seg[nb] = end
     float *dB;
     int32_t *status;
+    uint64_t wait_ns;       // limit of each pipeline wait (wait_limit_ns())
 };
 
 struct GramItem {
@@ -328,7 +330,7 @@ tc_gram_kernel(const __grid_constant__ CUtensorMap mG0, const __grid_constant__ 
             bool ok = true;
             for (int ks = 0; ks < g.s0 + g.s1; ks++, it++) {
                 const int s = it % kStages, r = it / kStages;
-                if (r > 0 && !mbar_wait(&empty_bar[s], (r - 1) & 1, abort_flag)) {
+                if (r > 0 && !mbar_wait(&empty_bar[s], (r - 1) & 1, abort_flag, P.wait_ns)) {
                     ok = false;
                     break;
                 }
@@ -352,13 +354,13 @@ tc_gram_kernel(const __grid_constant__ CUtensorMap mG0, const __grid_constant__ 
         for (int64_t item = blockIdx.x; item < P.n_items && !*abort_flag; item += gridDim.x, j++) {
             const GramItem g = gram_item(P, item);
             const int buf = j & 1, rr = j >> 1;
-            if (rr > 0 && !mbar_wait(&tempty_bar[buf], (rr - 1) & 1, abort_flag)) break;
+            if (rr > 0 && !mbar_wait(&tempty_bar[buf], (rr - 1) & 1, abort_flag, P.wait_ns)) break;
             tc_fence_after();
             const uint32_t d = tmem + buf * kTcN;
             bool ok = true;
             for (int ks = 0; ks < g.s0 + g.s1; ks++, it++) {
                 const int s = it % kStages, r = it / kStages;
-                if (!mbar_wait(&full_bar[s], r & 1, abort_flag)) {
+                if (!mbar_wait(&full_bar[s], r & 1, abort_flag, P.wait_ns)) {
                     ok = false;
                     break;
                 }
@@ -391,7 +393,7 @@ tc_gram_kernel(const __grid_constant__ CUtensorMap mG0, const __grid_constant__ 
         int j = 0;
         for (int64_t item = blockIdx.x; item < P.n_items; item += gridDim.x, j++) {
             const int buf = j & 1, rr = j >> 1;
-            if (!mbar_wait(&tfull_bar[buf], rr & 1, abort_flag)) break;
+            if (!mbar_wait(&tfull_bar[buf], rr & 1, abort_flag, P.wait_ns)) break;
             tc_fence_after();
             const GramItem g = gram_item(P, item);
             const TcGramBlock &B = P.blk[g.m];
@@ -635,6 +637,7 @@ int launch_tc_mix(int split, const __nv_bfloat16 *A, const __nv_bfloat16 *A2, in
     P.H = H;
     P.Hd = Hd;
     P.status = status;
+    P.wait_ns = wait_limit_ns();
     int dev = 0, sms = 148;
     FEQ_CUDA_TRY(cudaGetDevice(&dev));
     FEQ_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
@@ -677,6 +680,7 @@ int launch_tc_gram(int split, const __nv_bfloat16 *Gt0, const __nv_bfloat16 *Gt0
     P.seg = seg;
     P.dB = dB;
     P.status = status;
+    P.wait_ns = wait_limit_ns();
     if (items == 0) return FEQ_OK;
     CUtensorMap m0, m0l, m1, m1l, ma, mal;
     int rc;

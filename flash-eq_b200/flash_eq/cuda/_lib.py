@@ -55,7 +55,7 @@ class FeqAttnBwdArgs(ctypes.Structure):
     ]
 
 
-FEQ_ABI_VERSION = 3   # must equal feq_abi_version() of the loaded library
+FEQ_ABI_VERSION = 4   # must equal feq_abi_version() of the loaded library
 
 # name -> (restype, argtypes)
 SIGNATURES = {
@@ -63,6 +63,7 @@ SIGNATURES = {
     "feq_abi_version": (ctypes.c_int, []),
     "feq_last_error": (ctypes.c_char_p, []),
     "feq_launch_count": (ctypes.c_int64, []),
+    "feq_set_wait_limit_ns": (ctypes.c_uint64, [ctypes.c_uint64]),
     "feq_profile_enable": (ctypes.c_int, [ctypes.c_int32]),
     "feq_profile_read": (ctypes.c_int, [ctypes.c_int32, ctypes.c_char_p, ctypes.c_int32,
                                         ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int64)]),

@@ -124,7 +124,8 @@ class EquivariantAttention(nn.Module):
         k_src = None
         x_src = node_features
         if isinstance(graph, PartitionedGraph):
-            # src rows live on other ranks: one all-gather of the inputs and one of K per layer
+            # src rows live on other ranks: per layer one halo exchange of the inputs and one of K
+            # (all_to_all_single of just the rows this rank's edges read)
             x_src = graph.gather_nodes(node_features)
             k_src = graph.gather_nodes(qk[:, mult:].contiguous())
         V = self.linear_v._run(P, Q_basis, x_src, distances, src=graph.src, edge_add=edge_features)

@@ -114,31 +114,12 @@ class PartitionedGraph(Graph):
 
 def _exchange(send: torch.Tensor, send_counts, recv_counts, group) -> torch.Tensor:
     """Rows send[...] split by ``send_counts`` go to ranks 0..W-1; returns the rows received,
-    split by ``recv_counts`` in rank order."""
+    split by ``recv_counts`` in rank order.  One ``all_to_all_single`` on every backend (NCCL
+    on the GPUs, gloo in the host tests): a collective, so a peer that has left ends it with
+    an error (gloo) or a process-group timeout (NCCL) instead of a wait without end."""
     import torch.distributed as dist
 
     recv = send.new_empty((int(sum(recv_counts)),) + tuple(send.shape[1:]))
-    if dist.get_backend(group) == "gloo":          # host-side runs (tests): point to point
-        me = dist.get_rank(group)
-        so = [0] + list(torch.tensor(send_counts).cumsum(0).tolist())
-        ro = [0] + list(torch.tensor(recv_counts).cumsum(0).tolist())
-        reqs = []
-        for r in range(len(send_counts)):
-            if r == me:
-                recv[ro[r]:ro[r + 1]] = send[so[r]:so[r + 1]]
-                continue
-            if send_counts[r]:
-                reqs.append(dist.isend(send[so[r]:so[r + 1]].contiguous(), r, group=group))
-            if recv_counts[r]:
-                buf = torch.empty_like(recv[ro[r]:ro[r + 1]])
-                reqs.append((dist.irecv(buf, r, group=group), ro[r], buf))
-        for q in reqs:
-            if isinstance(q, tuple):
-                q[0].wait()
-                recv[q[1]:q[1] + q[2].shape[0]] = q[2]
-            else:
-                q.wait()
-        return recv
     dist.all_to_all_single(recv, send.contiguous(), output_split_sizes=list(recv_counts),
                            input_split_sizes=list(send_counts), group=group)
     return recv

@@ -60,8 +60,17 @@ enum feq_status_code {
  * ------------------------------------------------------------------------ */
 const char *feq_status_string(int status);
 /* 2: FeqAttnArgs gained k / num_src_nodes (partitioned graphs).
- * 3: attention / pooling backward entry points, node-level operators. */
+ * 3: attention / pooling backward entry points, node-level operators.
+ * 4: feq_set_wait_limit_ns; the separable (low-rank) edgewise entry point. */
 int feq_abi_version(void);
+/* Limit, in nanoseconds, of every pipeline wait of the tensor-core kernels launched
+ * after this call (no counterpart in the reference).  A wait that runs past it ends
+ * its kernel early with status 2 ("a tensor-core wait timed out", result invalid)
+ * instead of waiting on; the kernel first waits for its own copies and MMAs in flight
+ * and releases its tensor memory, so the context stays usable.  0 restores the
+ * default (4 s).  Returns the previous limit.  Process-wide; meant for tests of the
+ * time-out path and for callers that want a tighter bound. */
+uint64_t feq_set_wait_limit_ns(uint64_t limit_ns);
 /* Human-readable last CUDA error seen by this thread (empty when none). */
 const char *feq_last_error(void);
 /* Kernels this library has enqueued since load (its own kernels; each CUB radix
@@ -179,8 +188,10 @@ int feq_block_diagonal_bwd(const float *grad_output, const float *features, cons
  *     device memory (every GPU that loads the library holds it until exit); inputs
  *     and the output are still the caller's.  A problem whose scratch would exceed
  *     it returns FEQ_ERR_WORKSPACE and feq_last_error() gives the sizes.
- *   - The first call on a device looks up the array's device address on that device
- *     (with that device current); make that first call before any stream capture.
+ *   - Every call looks up the array's device address on the current device
+ *     (cudaGetSymbolAddress, which allocates nothing), so the address stays right
+ *     after a device reset.  The first call on a device also loads the library's
+ *     module there; make that first call before any stream capture.
  *   - All calls share the one array and it keeps the previous call's contents (no
  *     part needs to start at zero: each call writes every region before reading it).
  *     Calls whose GPU work overlaps in time race on it: serialise them (one stream,

@@ -18,7 +18,11 @@ import sys
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    here = os.path.dirname(os.path.abspath(__file__))
+    default_ref = os.environ.get("FEQ_REFERENCE_ROOT") or os.path.join(os.path.dirname(os.path.dirname(here)),
+                                                                        "reference")
+    ap.add_argument("--ref", default=default_ref,
+                    help="reference source tree ($FEQ_REFERENCE_ROOT, else 'reference' beside this repository)")
     ap.add_argument("--out", default=os.path.join(os.path.dirname(__file__), "_ref"))
     args = ap.parse_args()
 

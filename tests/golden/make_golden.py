@@ -1,8 +1,9 @@
 """Generate the golden fixtures under tests/golden/ by running the REFERENCE.
 
-Run in a container that has the reference tree (default /root/reference):
+Run where the reference tree is available ($FEQ_REFERENCE_ROOT, else a directory
+named ``reference`` beside this repository):
 
-    python tests/golden/make_golden.py [--ref /root/reference]
+    python tests/golden/make_golden.py [--ref PATH]
 
 What it does:
 * stubs ``sphericart`` / ``sphericart.torch`` (imported at module level by the
@@ -75,7 +76,8 @@ def knn_graph(coords: torch.Tensor, k: int, batch: torch.Tensor | None = None):
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("FEQ_REFERENCE_ROOT")
+                    or os.path.join(os.path.dirname(ROOT), "reference"))
     args = ap.parse_args()
     fe, orc = import_reference(args.ref)
     from flash_eq.layers.linear import EquivariantEdgewiseLinear

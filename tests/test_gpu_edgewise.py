@@ -224,25 +224,46 @@ def _reference_kernel():
     return mod
 
 
-def test_block_diagonal_matches_reference_cuda_kernel(cuda_device):
-    """Second oracle: the reference's own kernel compiled for sm_100a (oracle/_ref)."""
+REF_KERNEL_CASES = [
+    # lvals_in, lvals_out, mult, E, num_bins, log_bins, mix, tolerance
+    ([0, 1, 2], [0, 1, 2], 16, 3000, 50, False, "fp32", 1e-5),
+    ([0, 1, 1, 3], [2, 0], 6, 999, 50, False, "fp32", 1e-5),
+    ([0, 1, 2, 3, 4], [0, 1, 2, 3, 4], 64, 4000, 100, False, "fp32", 1e-5),     # config-2 shapes
+    ([0, 1, 2, 3, 4], [0, 1, 2, 3, 4], 64, 4000, 100, False, "bf16x3", 1e-4),
+    ([0, 1, 2, 3, 4], [0, 1, 2, 3, 4], 64, 4000, 100, False, "bf16", 2e-2),
+    ([0, 1, 2, 3, 4], [0, 1, 2, 3, 4], 64, 3000, 100, True, "bf16x3", 1e-4),     # log bins
+    ([0, 1, 2], [0, 1, 2], 64, 6000, 100, True, "fp32", 1e-5),
+    ([0, 1], [0, 1, 2, 3], 32, 2000, 64, False, "bf16x3", 1e-4),
+]
+
+
+@pytest.mark.parametrize("case", REF_KERNEL_CASES, ids=lambda c: f"L{max(c[0])}-{max(c[1])}_C{c[2]}_"
+                         f"{'log' if c[5] else 'lin'}_{c[6]}")
+def test_block_diagonal_matches_reference_cuda_kernel(cuda_device, case):
+    """Second oracle: the reference's own kernel compiled for sm_100a (oracle/_ref), at small
+    shapes and at the benched config-2 shapes (L <= 4, mult 64), linear and log bins, for the
+    CUDA-core (fp32) mix and both tensor-core mixes."""
     ref = _reference_kernel()
     if ref is None:
         pytest.skip("oracle/_ref not built")
     from flash_eq.cuda import block_diagonal_cuda
-    g = torch.Generator().manual_seed(5)
-    for lin, lout, mult, E in (([0, 1, 2], [0, 1, 2], 16, 3000), ([0, 1, 1, 3], [2, 0], 6, 999)):
-        rin, rout = fe.Repr(lin, mult), fe.Repr(lout, mult)
-        pr = fe.ProductRepr(rin, rout)
-        nb = 50
-        table = torch.randn(nb + 1, mult, mult, pr.nreps(), generator=g).to(cuda_device)
-        f = torch.randn(E, mult, rin.dim(), generator=g).to(cuda_device)
+    lin, lout, mult, E, nb, log_bins, mix, tol = case
+    g = torch.Generator().manual_seed(5 + E)
+    rin, rout = fe.Repr(lin, mult), fe.Repr(lout, mult)
+    pr = fe.ProductRepr(rin, rout)
+    table = torch.randn(nb + 1, mult, mult, pr.nreps(), generator=g).to(cuda_device)
+    f = torch.randn(E, mult, rin.dim(), generator=g).to(cuda_device)
+    if log_bins:
+        lo_d, hi_d = 0.5, 10.0
+        dist = (lo_d + torch.rand(E, generator=g) * (hi_d - lo_d)).to(cuda_device)
+        p1, p2 = orc.binning_params(nb, lo_d, hi_d, True)
+    else:
         dist = (torch.rand(E, generator=g) * 10).to(cuda_device)
         p1, p2 = 0.0, nb / 10.0
-        lvi = torch.tensor(lin, dtype=torch.int32, device=cuda_device)
-        lvo = torch.tensor(lout, dtype=torch.int32, device=cuda_device)
-        mi = max(max(lin), max(lout))
-        max_in = max((1 if m == 0 else 2) * sum(l >= m for l in lin) for m in range(mi + 1))
-        (yr,) = ref.forward(f, table, dist, 0.1, p1, p2, nb, False, lvi, lvo, mult, rout.dim(), max_in)
-        y = block_diagonal_cuda(f, table, dist, pr, p1, p2, nb, False, 0.1)
-        assert rel_l2(y, yr) < 1e-5
+    lvi = torch.tensor(lin, dtype=torch.int32, device=cuda_device)
+    lvo = torch.tensor(lout, dtype=torch.int32, device=cuda_device)
+    mi = max(max(lin), max(lout))
+    max_in = max((1 if m == 0 else 2) * sum(l >= m for l in lin) for m in range(mi + 1))
+    (yr,) = ref.forward(f, table, dist, 0.1, p1, p2, nb, log_bins, lvi, lvo, mult, rout.dim(), max_in)
+    y = block_diagonal_cuda(f, table, dist, pr, p1, p2, nb, log_bins, 0.1, mix=mix)
+    assert rel_l2(y, yr) < tol

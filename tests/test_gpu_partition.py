@@ -1,5 +1,6 @@
-"""dst-range partitioned EquivariantTransformer on 2 GPUs (NCCL all-gather of the src-side
-rows per layer) against the same model run whole on one GPU.  Child processes, one per
+"""dst-range partitioned EquivariantTransformer on 2 GPUs (per layer an NCCL halo exchange,
+all_to_all_single of just the src-side rows each rank reads) against the same model run whole
+on one GPU.  Child processes, one per
 GPU; NVLS off.  Skipped with fewer than 2 GPUs."""
 from __future__ import annotations
 
