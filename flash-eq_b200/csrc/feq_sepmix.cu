@@ -1,0 +1,726 @@
+// feq_sepmix.cu -- the edgewise linear out = Q . Lambda(r) . P^T . f as ONE kernel, for the
+// radial tables that EquivariantEdgewiseLinear builds: gather by src, rotation into the edge
+// frame, the distance-interpolated block-diagonal mix and the rotation back, with neither
+// the rotated rows nor the mix output ever leaving the SM.
+//
+// Reference behaviour replaced (flash_eq/layers/linear.py:100-160 with its radial net):
+//   table[b, o, i, w] = sum_k C[k, o, i] f[b, k, w]        SeparableRadialNet.forward,
+//                                                          flash_eq/layers/radial.py:259-275
+//   f_diag = bmm(x[src], P)                                 linear.py:135-140
+//   out_diag = block_diagonal_cuda(f_diag, table, r)        block_diagonal.cu:558-733
+//   out = bmm(out_diag, Q^T)                                linear.py:160
+//
+// Formulation.  The table is separable with rank R (the module's ``rank``), so the
+// interpolated weight of an edge is lerp_t(table)[o, i, w] = sum_k C[k, o, i] g_k[w] with
+// g_k = (1 - t) f[lo, k] + t f[lo + 1, k].  The mix therefore factors into
+//   Z_k[o, j] = sum_i C[k, o, i] a[i, j]         a = s^l_in (f . D) (rotated input, m-first)
+//   h[o, q]   = sum_k sum_j G_k[q, j] Z_k[o, j]  G_k = the block-diagonal position mix of g_k
+// The first step is one GEMM whose weight C is the same for every edge (kept in shared
+// memory for the whole kernel): tcgen05.mma with C as the M side (rows (o, k)) and the
+// rotated rows of a tile of edges as the N side, accumulating Z in TMEM.  No bin sort, no
+// re-laid table, no two-bin doubling.  The second step is per-edge CUDA-core work in the
+// epilogue, straight from TMEM, followed by the rotation back (s^l_out folded in) and one
+// bulk store per output row.
+//
+// Roles (288 threads, persistent, one CTA per SM, one edge tile after another):
+//   warp 0      TMEM allocator; one thread issues tcgen05.mma
+//   warps 1..4  rotation in: bulk-copy x[src[e]] into shared memory, rotate two channels per
+//               lane with the factored Wigner blocks, write bf16 (hi, and lo in bf16x3 mode)
+//               into the K-major 128-byte-swizzled N-side tile; per edge also the trig of
+//               the rotations, s = d / (d + sh_scale) and the lerped g_k for the epilogue
+//   warps 5..8  epilogue: tcgen05.ld of Z, position mix, sum over k across lane pairs,
+//               rotation back, bulk store
+// Rings: 2 N-side tiles, 2 TMEM accumulator sets, 4 per-tile edge-scalar slots.  Every
+// wait is bounded (limit from the launch); on time-out the kernel sets status 2, drains
+// its copies and MMAs, frees TMEM and returns.  No TMA multicast anywhere.
+//
+// bf16x3 (float32-level accuracy): both operands split x = hi + lo, Z accumulates
+// hi.hi + hi.lo + lo.hi.  bf16: hi only.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include "feq_internal.cuh"
+#include "feq_rot_common.cuh"
+#include "feq_sm100.cuh"
+
+namespace feq {
+namespace sep {
+
+using namespace sm100;
+using namespace rot;
+
+constexpr int kThreads = 288;
+constexpr int kRotWarp0 = 1, kNumRot = 4;
+constexpr int kEpiWarp0 = 5, kNumEpi = 4;
+constexpr int kStages = 2;      // N-side tiles
+constexpr int kSlots = 4;       // per-tile edge scalars
+constexpr int kBufs = 2;        // TMEM accumulator sets
+constexpr int kCin = 64;        // K (one 128-byte swizzle row of bf16)
+constexpr int kCout = 64;
+constexpr int kRank = 4;
+constexpr int kG = 128 / kCout;             // k values per 128-row slice and output channel
+constexpr int kSlices = kRank / kG;         // 128-row M slices
+constexpr uint32_t kTileBytes = 128 * 128;  // 128 rows x 128 B
+static_assert(kRank % kG == 0, "rank must split evenly over the slices");
+static_assert(kG == 2, "the lane-pair exchange below assumes two k values per slice");
+
+// Compile-time geometry of lvals_in = [0..LIN] -> lvals_out = [0..LOUT].
+template <int LIN, int LOUT>
+struct Geo {
+    static constexpr int LI = LIN, LO = LOUT;
+    static constexpr int DIN = (LIN + 1) * (LIN + 1);
+    static constexpr int DOUT = (LOUT + 1) * (LOUT + 1);
+    static constexpr int MB = LIN < LOUT ? LIN : LOUT;     // last m-block with inputs and outputs
+    static constexpr int LMAX = LIN > LOUT ? LIN : LOUT;
+    static constexpr int ES = DIN <= 16 ? 16 : 32;          // TMEM columns / N rows per edge
+    static constexpr int TE = 128 / ES;                     // edges per tile
+    static constexpr int TF = trig_floats(LMAX);
+    __host__ __device__ static constexpr int nin(int m) { return LIN - m + 1; }
+    __host__ __device__ static constexpr int nout(int m) { return LOUT - m + 1; }
+    __host__ __device__ static constexpr int mul(int m) { return m == 0 ? 1 : 2; }
+    // block_diagonal.cu:1191-1266: offsets of block m (every block up to MB is non-empty)
+    __host__ __device__ static constexpr int in_off(int m) {
+        int o = 0;
+        for (int q = 0; q < m; q++) o += mul(q) * nin(q);
+        return o;
+    }
+    __host__ __device__ static constexpr int out_off(int m) {
+        int o = 0;
+        for (int q = 0; q < m; q++) o += mul(q) * nout(q);
+        return o;
+    }
+    __host__ __device__ static constexpr int w_off(int m) {
+        int o = 0;
+        for (int q = 0; q < m; q++) o += mul(q) * nin(q) * nout(q);
+        return o;
+    }
+    __host__ __device__ static constexpr int gsize(int m) { return mul(m) * nin(m) * nout(m); }
+    __host__ __device__ static constexpr int gpad(int m) { return (gsize(m) + 3) & ~3; }
+    __host__ __device__ static constexpr int goff(int m) {
+        int o = 0;
+        for (int q = 0; q < m; q++) o += gpad(q);
+        return o;
+    }
+    static constexpr int W = w_off(MB + 1);      // ProductRepr(in, out).nreps()
+    static constexpr int GP = goff(MB + 1);      // floats of one k's g, each block padded to 4
+    // m-first position of (l, m) (flash_eq/representations/wigner.py:243-272)
+    __host__ __device__ static constexpr int mf_in(int l, int m) {
+        return m == 0 ? l : in_off(m < 0 ? -m : m) + 2 * (l - (m < 0 ? -m : m)) + (m < 0 ? 1 : 0);
+    }
+    __host__ __device__ static constexpr int mf_out(int l, int m) {
+        return m == 0 ? l : out_off(m < 0 ? -m : m) + 2 * (l - (m < 0 ? -m : m)) + (m < 0 ? 1 : 0);
+    }
+    // per-edge scalar slot: trig (padded), s (padded to 4), g for every k
+    static constexpr int SLOT_TRIG = 0;
+    static constexpr int SLOT_S = pad4(TF);
+    static constexpr int SLOT_G = SLOT_S + 4;
+    static constexpr int SLOT_EDGE = SLOT_G + kRank * GP;     // floats per edge
+    static constexpr int STAGE_ROW = ((kCout * DOUT + 15) / 32) * 32 + 16;   // == 16 mod 32 floats
+};
+
+struct SepParams {
+    const float *x;
+    const int64_t *src;
+    int64_t nsrc;
+    const float *edge_add;
+    const float *dirs;
+    const float *dist;
+    const float *cpat;        // (rank, c_out, c_in)
+    const float *ftab;        // (num_bins + 1, rank, W)
+    float *out;
+    int32_t *status;
+    int64_t E;
+    int64_t num_tiles;
+    Binning bins;
+    float sh_scale;
+    uint64_t wait_ns;
+};
+
+// Byte offset of element (row r, column c) in a 128-row K-major tile of 64 bf16 per row with
+// the 128-byte swizzle (16-byte chunk index XOR row % 8; 8-row atoms of 1024 B).
+__device__ __forceinline__ uint32_t swz(int r, int c) {
+    return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((((c >> 3) ^ (r & 7))) << 4) + ((c & 7) << 1));
+}
+
+__device__ __forceinline__ void named_bar(int id, int n) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+
+template <int N>
+__device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&r)[N]);
+template <>
+__device__ __forceinline__ void tmem_ld<32>(uint32_t taddr, uint32_t (&r)[32]) {
+    tmem_ld32(taddr, r);
+}
+template <>
+__device__ __forceinline__ void tmem_ld<16>(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+
+// One channel of one irrep of degree Lg, in registers, through D = R(phi) M R(phi)^T
+// (as rot::rot_irrep2, for a single channel): kT = false y = x D, kT = true y = x D^T.
+template <int Lg, bool kT, typename Get, typename Emit>
+__device__ __forceinline__ void rot_irrep1(const float *__restrict__ tr, int lmax, float sl, Get get, Emit emit) {
+    if constexpr (Lg == 0) {
+        emit(0, get(0) * sl);
+    } else {
+        constexpr int N = 2 * Lg + 1;
+        const float *tv = tr, *cp = tr + 2 * lmax + 1, *sp = cp + lmax + 1;
+        float m[WA<Lg>::kNnz];
+        WA<Lg>::wm(tv, sl, m);
+        float g[N];
+#pragma unroll
+        for (int q = 0; q < N; q++) g[q] = get(q);
+#pragma unroll
+        for (int mm = 1; mm <= Lg; mm++) {
+            const int a = Lg - mm, b = Lg + mm;
+            const float c = cp[mm], s = sp[mm];
+            const float t0 = g[a] * c - g[b] * s, t1 = g[a] * s + g[b] * c;
+            g[a] = t0;
+            g[b] = t1;
+        }
+        float h[N];
+        WA<Lg>::template wa<kT>(m, g, h);
+#pragma unroll
+        for (int mm = 1; mm <= Lg; mm++) {
+            const int a = Lg - mm, b = Lg + mm;
+            const float c = cp[mm], s = sp[mm];
+            const float t0 = h[a] * c + h[b] * s, t1 = h[b] * c - h[a] * s;
+            h[a] = t0;
+            h[b] = t1;
+        }
+#pragma unroll
+        for (int o = 0; o < N; o++) emit(o, h[o]);
+    }
+}
+
+template <int Lg, bool kT, typename Get, typename Emit>
+__device__ __forceinline__ void rot_irrep2c(const float *__restrict__ tr, int lmax, float sl, Get get, Emit emit) {
+    if constexpr (Lg == 0) {
+        const float2 v = get(0);
+        emit(0, v.x * sl, v.y * sl);
+    } else {
+        rot_irrep2<Lg, kT>(tr, lmax, sl, get, emit);
+    }
+}
+
+// h[q] += sum_j G[q, j] Z[j] for the blocks m = M..MB of one k (G in shared memory, padded
+// per block; Z this thread's TMEM row for one edge).  m = 0: out[o] += g[o n_in + i] z[i];
+// m > 0: 2x2 [[a, b], [-b, a]] on the (+m, -m) pairs (block_diagonal.cu:558-733).
+template <class GE, int M, int ES>
+__device__ __forceinline__ void pos_mix(const uint32_t (&Z)[ES], const float *__restrict__ G,
+                                        float (&h)[GE::DOUT]) {
+    if constexpr (M <= GE::MB) {
+        constexpr int ni = GE::nin(M), no = GE::nout(M), io = GE::in_off(M), oo_ = GE::out_off(M);
+        constexpr int np = GE::gpad(M);
+        float g[np];
+        const float4 *g4 = reinterpret_cast<const float4 *>(G + GE::goff(M));
+#pragma unroll
+        for (int v = 0; v < np / 4; v++) {
+            const float4 t = g4[v];
+            g[4 * v] = t.x;
+            g[4 * v + 1] = t.y;
+            g[4 * v + 2] = t.z;
+            g[4 * v + 3] = t.w;
+        }
+        if constexpr (M == 0) {
+#pragma unroll
+            for (int o = 0; o < no; o++) {
+                float acc = h[oo_ + o];
+#pragma unroll
+                for (int i = 0; i < ni; i++) acc = fmaf(g[o * ni + i], __uint_as_float(Z[io + i]), acc);
+                h[oo_ + o] = acc;
+            }
+        } else {
+#pragma unroll
+            for (int o = 0; o < no; o++) {
+                float re = h[oo_ + 2 * o], im = h[oo_ + 2 * o + 1];
+#pragma unroll
+                for (int i = 0; i < ni; i++) {
+                    const float a = g[2 * (o * ni + i)], b = g[2 * (o * ni + i) + 1];
+                    const float zr = __uint_as_float(Z[io + 2 * i]), zi = __uint_as_float(Z[io + 2 * i + 1]);
+                    re = fmaf(a, zr, fmaf(b, zi, re));
+                    im = fmaf(a, zi, fmaf(-b, zr, im));
+                }
+                h[oo_ + 2 * o] = re;
+                h[oo_ + 2 * o + 1] = im;
+            }
+        }
+        pos_mix<GE, M + 1, ES>(Z, G, h);
+    }
+}
+
+// Input rotation of one irrep degree L (recursing to LIN) for the channel pair (c, c + 1).
+template <class GE, int L, bool kSplit>
+__device__ __forceinline__ void rotate_in_all(const float *__restrict__ tr, float s, const float *__restrict__ f0,
+                                              const float *__restrict__ f1, uint8_t *bhi, uint8_t *blo, int row0,
+                                              int c) {
+    if constexpr (L <= GE::LI) {
+        constexpr int off = L * L;    // standard offset of degree L in [0..LIN]
+        auto get = [&](int q) { return make_float2(f0[off + q], f1[off + q]); };
+        auto emit = [&](int o, float y0, float y1) {
+            const int r = row0 + GE::mf_in(L, o - L);
+            const __nv_bfloat162 hi = __floats2bfloat162_rn(y0, y1);
+            *reinterpret_cast<__nv_bfloat162 *>(bhi + swz(r, c)) = hi;
+            if (kSplit) {
+                const float2 hf = __bfloat1622float2(hi);
+                *reinterpret_cast<__nv_bfloat162 *>(blo + swz(r, c)) = __floats2bfloat162_rn(y0 - hf.x, y1 - hf.y);
+            }
+        };
+        rot_irrep2c<L, false>(tr, GE::LMAX, ipowf(s, L), get, emit);
+        rotate_in_all<GE, L + 1, kSplit>(tr, s, f0, f1, bhi, blo, row0, c);
+    }
+}
+
+// Output rotation of every degree of [0..LOUT] for one channel of one edge, into the
+// staging row (standard order).
+template <class GE, int L>
+__device__ __forceinline__ void rotate_out_all(const float *__restrict__ tr, float s, const float (&h)[GE::DOUT],
+                                               float *__restrict__ orow) {
+    if constexpr (L <= GE::LO) {
+        constexpr int off = L * L;
+        auto get = [&](int q) { return h[GE::mf_out(L, q - L)]; };
+        auto emit = [&](int o, float y) { orow[off + o] = y; };
+        rot_irrep1<L, true>(tr, GE::LMAX, ipowf(s, L), get, emit);
+        rotate_out_all<GE, L + 1>(tr, s, h, orow);
+    }
+}
+
+template <int LIN, int LOUT, bool kSplit>
+__global__ void __launch_bounds__(kThreads, 1) sep_edgewise_kernel(const __grid_constant__ SepParams P) {
+    using GE = Geo<LIN, LOUT>;
+    constexpr int ES = GE::ES, TE = GE::TE, DIN = GE::DIN, DOUT = GE::DOUT;
+    constexpr int ROWF = kCin * DIN;                       // input row floats
+    constexpr int ROWF_PAD = (ROWF + 3) & ~3;
+    constexpr int OUTF = kCout * DOUT;                     // output row floats
+    constexpr uint32_t kIdesc = idesc_bf16_f32(128, 128);
+    constexpr int kSplitN = kSplit ? 2 : 1;
+    static_assert(TE % kNumRot == 0 && TE % kG == 0, "tile edges split over the warps");
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *a_hi = smem;                                            // kSlices tiles
+    uint8_t *a_lo = a_hi + kSlices * kTileBytes;                      // (split only)
+    uint8_t *b_base = a_hi + kSplitN * kSlices * kTileBytes;          // kStages x (hi [, lo])
+    float *xrows = reinterpret_cast<float *>(b_base + kStages * kSplitN * kTileBytes);
+    float *slots = xrows + kNumRot * 2 * ROWF_PAD;
+    float *stage = slots + kSlots * TE * GE::SLOT_EDGE;
+
+    __shared__ uint64_t b_full[kStages], b_empty[kStages], t_full[kBufs], t_empty[kBufs], s_empty[kSlots];
+    __shared__ uint64_t x_bar[kNumRot][2], drain_bar;
+    __shared__ uint32_t tmem_base_s;
+    __shared__ int abort_s, epi_stop_s;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        epi_stop_s = 0;
+        for (int i = 0; i < kStages; i++) {
+            mbar_init(&b_full[i], kNumRot);
+            mbar_init(&b_empty[i], 1);
+        }
+        for (int i = 0; i < kBufs; i++) {
+            mbar_init(&t_full[i], 1);
+            mbar_init(&t_empty[i], kNumEpi);
+        }
+        for (int i = 0; i < kSlots; i++) mbar_init(&s_empty[i], kNumEpi);
+        for (int i = 0; i < kNumRot; i++) {
+            mbar_init(&x_bar[i][0], 1);
+            mbar_init(&x_bar[i][1], 1);
+        }
+        mbar_init(&drain_bar, 1);
+        abort_s = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0) {
+        tmem_alloc(&tmem_base_s, 512);
+        tmem_relinquish();
+    }
+    // Channel patterns -> M-side tiles: slice s, row r = co * kG + kk holds C[s * kG + kk][co][:].
+    for (int idx = threadIdx.x; idx < kSlices * 128 * kCin; idx += kThreads) {
+        const int s = idx / (128 * kCin), rem = idx - s * 128 * kCin;
+        const int r = rem / kCin, c = rem - r * kCin;
+        const int co = r / kG, k = s * kG + (r % kG);
+        const float v = __ldg(P.cpat + ((int64_t)k * kCout + co) * kCin + c);
+        const __nv_bfloat16 hi = __float2bfloat16_rn(v);
+        *reinterpret_cast<__nv_bfloat16 *>(a_hi + s * kTileBytes + swz(r, c)) = hi;
+        if (kSplit)
+            *reinterpret_cast<__nv_bfloat16 *>(a_lo + s * kTileBytes + swz(r, c)) =
+                __float2bfloat16_rn(v - __bfloat162float(hi));
+    }
+    // N-side tiles start at zero: rows of the padding positions (j >= d_in of every edge)
+    // are never written again.
+    for (int i = threadIdx.x; i < (int)(kStages * kSplitN * kTileBytes / 16); i += kThreads)
+        reinterpret_cast<uint4 *>(b_base)[i] = make_uint4(0u, 0u, 0u, 0u);
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_base_s;
+    volatile int *abort_flag = &abort_s;
+    const int64_t n_local = P.num_tiles > blockIdx.x ? (P.num_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- MMA issuer ----------------
+            for (int64_t i = 0; i < n_local && !*abort_flag; i++) {
+                const int st = (int)(i % kStages), buf = (int)(i % kBufs);
+                if (!mbar_wait(&b_full[st], (uint32_t)((i / kStages) & 1), abort_flag, P.wait_ns)) break;
+                if (i >= kBufs && !mbar_wait(&t_empty[buf], (uint32_t)((i / kBufs - 1) & 1), abort_flag, P.wait_ns))
+                    break;
+                tc_fence_after();
+                const uint32_t bh = smem_u32(b_base + st * kSplitN * kTileBytes);
+                const uint32_t bl = bh + kTileBytes;
+#pragma unroll
+                for (int s = 0; s < kSlices; s++) {
+                    const uint32_t d = tmem + (uint32_t)(buf * kSlices * 128 + s * 128);
+                    const uint32_t ah = smem_u32(a_hi + s * kTileBytes), al = smem_u32(a_lo + s * kTileBytes);
+#pragma unroll
+                    for (int ks = 0; ks < kCin / 16; ks++) {
+                        const uint32_t ko = ks * 32;
+                        umma_f16(d, smem_desc_sw128(ah + ko), smem_desc_sw128(bh + ko), kIdesc, ks > 0 ? 1u : 0u);
+                        if (kSplit) {
+                            umma_f16(d, smem_desc_sw128(ah + ko), smem_desc_sw128(bl + ko), kIdesc, 1u);
+                            umma_f16(d, smem_desc_sw128(al + ko), smem_desc_sw128(bh + ko), kIdesc, 1u);
+                        }
+                    }
+                }
+                umma_commit(&b_empty[st]);
+                umma_commit(&t_full[buf]);
+            }
+            umma_commit(&drain_bar);
+            mbar_wait_drain(&drain_bar, 0);
+        }
+    } else if (warp < kEpiWarp0) {
+        // ---------------- rotation in ----------------
+        const int w = warp - kRotWarp0;
+        constexpr int EPW = TE / kNumRot;                  // edges of one tile per rotation warp
+        const int64_t n_jobs = n_local * EPW;
+        float *xb = xrows + (size_t)w * 2 * ROWF_PAD;
+        uint32_t xphase = 0;
+        int pending = 0;
+        auto edge_of = [&](int64_t j, int &el) -> int64_t {
+            const int64_t i = j / EPW;
+            el = w + kNumRot * (int)(j - i * EPW);
+            return (blockIdx.x + i * gridDim.x) * TE + el;
+        };
+        // row of x feeding job j, -1 when none (past the end, or a bad src index)
+        auto src_row = [&](int64_t e) -> int64_t {
+            if (e >= P.E) return -1;
+            if (!P.src) return e;
+            const int64_t r = P.src[e];
+            if (r < 0 || r >= P.nsrc) {
+                if (lane == 0) set_status(P.status, 1);
+                return -2;
+            }
+            return r;
+        };
+        auto issue = [&](int64_t j) {
+            int el;
+            const int64_t e = edge_of(j, el);
+            const int64_t r = src_row(e);
+            const int b = (int)(j & 1);
+            if (r >= 0) {
+                if (lane == 0) {
+                    fence_async_smem();
+                    mbar_arrive_expect_tx(&x_bar[w][b], ROWF * 4);
+                    bulk_load(xb + b * ROWF_PAD, P.x + r * (int64_t)ROWF, ROWF * 4, &x_bar[w][b]);
+                }
+                pending |= 1 << b;
+            }
+            return r;
+        };
+        int64_t r_next = n_jobs > 0 ? issue(0) : -1;
+        bool alive = true;
+        for (int64_t j = 0; j < n_jobs && alive; j++) {
+            const int64_t i = j / EPW;
+            const int st = (int)(i % kStages), slot = (int)(i % kSlots);
+            int el;
+            const int64_t e = edge_of(j, el);
+            const int64_t r_cur = r_next;
+            const int b = (int)(j & 1);
+            if (j + 1 < n_jobs) r_next = issue(j + 1);
+            if (j % EPW == 0) {       // first edge of this warp in tile i: wait for its buffers
+                if (i >= kStages &&
+                    !mbar_wait(&b_empty[st], (uint32_t)((i / kStages - 1) & 1), abort_flag, P.wait_ns)) {
+                    alive = false;
+                    break;
+                }
+                if (i >= kSlots &&
+                    !mbar_wait(&s_empty[slot], (uint32_t)((i / kSlots - 1) & 1), abort_flag, P.wait_ns)) {
+                    alive = false;
+                    break;
+                }
+            }
+            if (e < P.E) {
+                float *sl = slots + (size_t)(slot * TE + el) * GE::SLOT_EDGE;
+                // per-edge scalars (every lane computes them; lane 0 stores the trig)
+                const float dd = P.dist[e];
+                const float s = dd / (dd + P.sh_scale);
+                int lo;
+                float t;
+                bin_of(dd, P.bins, lo, t);
+                float tr[GE::TF];
+                edge_trig_compact(P.dirs[e * 3], P.dirs[e * 3 + 1], P.dirs[e * 3 + 2], GE::LMAX, tr);
+                if (lane == 0) {
+#pragma unroll
+                    for (int q = 0; q < GE::TF; q++) sl[GE::SLOT_TRIG + q] = tr[q];
+                    sl[GE::SLOT_S] = s;
+                }
+                // g_k = (1 - t) f[lo, k] + t f[lo + 1, k], per block padded to 4 floats
+                {
+                    const float *f_lo = P.ftab + (int64_t)lo * kRank * GE::W, *f_hi = f_lo + kRank * GE::W;
+                    const float omt = 1.0f - t;
+                    for (int idx = lane; idx < kRank * GE::GP; idx += 32) {
+                        const int k = idx / GE::GP, p = idx - k * GE::GP;
+                        int m = 0;
+#pragma unroll
+                        for (int q = 1; q <= GE::MB; q++) m += p >= GE::goff(q) ? 1 : 0;
+                        int goff_m = 0, gsize_m = 0, woff_m = 0;
+#pragma unroll
+                        for (int q = 0; q <= GE::MB; q++)
+                            if (q == m) {
+                                goff_m = GE::goff(q);
+                                gsize_m = GE::gsize(q);
+                                woff_m = GE::w_off(q);
+                            }
+                        const int loc = p - goff_m;
+                        float v = 0.0f;
+                        if (loc < gsize_m) {
+                            const int wi = k * GE::W + woff_m + loc;
+                            v = omt * __ldg(f_lo + wi) + t * __ldg(f_hi + wi);
+                        }
+                        sl[GE::SLOT_G + idx] = v;
+                    }
+                }
+                // the input row: bulk copy in flight since the previous edge
+                float *fb = xb + b * ROWF_PAD;
+                if (r_cur >= 0) {
+                    if (!mbar_wait(&x_bar[w][b], (xphase >> b) & 1u, abort_flag, P.wait_ns)) {
+                        set_status(P.status, 2);
+                        alive = false;
+                        break;
+                    }
+                    xphase ^= 1u << b;
+                    pending &= ~(1 << b);
+                } else {
+                    for (int q = lane; q < ROWF; q += 32) fb[q] = 0.0f;
+                }
+                if (P.edge_add) {
+                    const float4 *ea = reinterpret_cast<const float4 *>(P.edge_add + e * (int64_t)ROWF);
+                    float4 *f4 = reinterpret_cast<float4 *>(fb);
+                    for (int q = lane; q < ROWF / 4; q += 32) {
+                        const float4 a = __ldg(ea + q);
+                        float4 v = f4[q];
+                        v.x += a.x;
+                        v.y += a.y;
+                        v.z += a.z;
+                        v.w += a.w;
+                        f4[q] = v;
+                    }
+                }
+                __syncwarp();
+                uint8_t *bh = b_base + st * kSplitN * kTileBytes;
+                const int c = 2 * lane;
+                rotate_in_all<GE, 0, kSplit>(tr, s, fb + c * DIN, fb + (c + 1) * DIN, bh, bh + kTileBytes,
+                                             el * ES, c);
+            }
+            __syncwarp();
+            if (j % EPW == EPW - 1) {     // this warp's part of tile i is in shared memory
+                fence_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&b_full[st]);
+            }
+        }
+        for (int b = 0; b < 2; b++)
+            if (pending & (1 << b)) mbar_wait_drain(&x_bar[w][b], (xphase >> b) & 1u);
+    } else {
+        // ---------------- epilogue ----------------
+        const int q4 = warp & 3;                       // TMEM lane quadrant of this warp
+        const int row = q4 * 32 + lane;                // M row: co * kG + kk
+        const int co = row / kG, kk = row % kG;
+        const bool leader = warp == kEpiWarp0 && lane == 0;
+        for (int64_t i = 0; i < n_local; i++) {
+            const int buf = (int)(i % kBufs), slot = (int)(i % kSlots);
+            // The four epilogue warps meet at named barriers below, so they must leave the
+            // loop together: a failed wait in any of them stops all four.
+            if (!mbar_wait(&t_full[buf], (uint32_t)((i / kBufs) & 1), abort_flag, P.wait_ns) && lane == 0)
+                epi_stop_s = 1;
+            named_bar(2, kNumEpi * 32);
+            if (*reinterpret_cast<volatile int *>(&epi_stop_s)) break;
+            tc_fence_after();
+            const int64_t e0 = (blockIdx.x + i * gridDim.x) * TE;
+            const float *slot_base = slots + (size_t)slot * TE * GE::SLOT_EDGE;
+#pragma unroll 1
+            for (int gi = 0; gi < TE / kG; gi++) {
+                float h[kG][DOUT];
+#pragma unroll
+                for (int ee = 0; ee < kG; ee++)
+#pragma unroll
+                    for (int q = 0; q < DOUT; q++) h[ee][q] = 0.0f;
+#pragma unroll
+                for (int ee = 0; ee < kG; ee++) {
+                    const int el = gi * kG + ee;
+                    const float *G = slot_base + el * GE::SLOT_EDGE + GE::SLOT_G;
+#pragma unroll
+                    for (int s = 0; s < kSlices; s++) {
+                        uint32_t Z[ES];
+                        tmem_ld<ES>(tmem + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(buf * kSlices * 128 + s * 128 + el * ES),
+                                    Z);
+                        tmem_wait_ld();
+                        pos_mix<GE, 0, ES>(Z, G + (s * kG + kk) * GE::GP, h[ee]);
+                    }
+                }
+                // sum over k across the lane pair; lane kk keeps edge gi * kG + kk
+                float hf[DOUT];
+#pragma unroll
+                for (int q = 0; q < DOUT; q++) {
+                    const float send = kk == 0 ? h[1][q] : h[0][q];
+                    const float keep = kk == 0 ? h[0][q] : h[1][q];
+                    hf[q] = keep + __shfl_xor_sync(0xffffffffu, send, 1);
+                }
+                const int el = gi * kG + kk;
+                const float *es = slot_base + el * GE::SLOT_EDGE;
+                float tr[GE::TF];
+#pragma unroll
+                for (int q = 0; q < GE::TF; q++) tr[q] = es[GE::SLOT_TRIG + q];
+                const float s = es[GE::SLOT_S];
+                if (leader) bulk_wait_read0();           // the previous group's rows have left
+                named_bar(1, kNumEpi * 32);
+                rotate_out_all<GE, 0>(tr, s, hf, stage + kk * GE::STAGE_ROW + co * DOUT);
+                fence_async_smem();
+                named_bar(1, kNumEpi * 32);
+                if (leader) {
+#pragma unroll
+                    for (int ee = 0; ee < kG; ee++) {
+                        const int64_t e = e0 + gi * kG + ee;
+                        if (e < P.E) bulk_store(P.out + e * (int64_t)OUTF, stage + ee * GE::STAGE_ROW, OUTF * 4);
+                    }
+                    bulk_commit();
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&t_empty[buf]);
+                mbar_arrive(&s_empty[slot]);
+            }
+        }
+        if (leader) bulk_wait0();
+    }
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+    if (threadIdx.x == 0 && abort_s) set_status(P.status, 2);
+}
+
+template <int LIN, int LOUT, bool kSplit>
+size_t smem_bytes() {
+    using GE = Geo<LIN, LOUT>;
+    constexpr int kSplitN = kSplit ? 2 : 1;
+    size_t b = 1024;                                                     // alignment slack
+    b += (size_t)kSplitN * kSlices * kTileBytes;                         // M side
+    b += (size_t)kStages * kSplitN * kTileBytes;                         // N side
+    b += (size_t)kNumRot * 2 * ((kCin * GE::DIN + 3) & ~3) * 4;          // input rows
+    b += (size_t)kSlots * GE::TE * GE::SLOT_EDGE * 4;                    // edge scalars
+    b += (size_t)kG * GE::STAGE_ROW * 4;                                 // output staging
+    return b;
+}
+
+template <int LIN, int LOUT, bool kSplit>
+int launch(const SepParams &P, cudaStream_t stream) {
+    auto kern = sep_edgewise_kernel<LIN, LOUT, kSplit>;
+    size_t smem = smem_bytes<LIN, LOUT, kSplit>();
+    // more than half of the SM's shared memory: one CTA per SM, so one TMEM allocation
+    if (smem < 120 * 1024) smem = 120 * 1024;
+    FEQ_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    int dev = 0, sms = 148;
+    FEQ_CUDA_TRY(cudaGetDevice(&dev));
+    FEQ_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    const int64_t grid = P.num_tiles < sms ? P.num_tiles : sms;
+    kern<<<(unsigned)grid, kThreads, smem, stream>>>(P);
+    FEQ_LAUNCH_CHECK();
+    return FEQ_OK;
+}
+
+// (LIN, LOUT) pairs this build instantiates: lvals [0..L] in and out, L <= 4.
+template <bool kSplit>
+int dispatch(int lin, int lout, const SepParams &P, cudaStream_t s) {
+    if (lin == 1 && lout == 1) return launch<1, 1, kSplit>(P, s);
+    if (lin == 2 && lout == 2) return launch<2, 2, kSplit>(P, s);
+    if (lin == 3 && lout == 3) return launch<3, 3, kSplit>(P, s);
+    if (lin == 4 && lout == 4) return launch<4, 4, kSplit>(P, s);
+    return FEQ_ERR_UNSUPPORTED;
+}
+
+template <int LIN, int LOUT>
+int tiles_of(int64_t E) {
+    return (int)((E + Geo<LIN, LOUT>::TE - 1) / Geo<LIN, LOUT>::TE);
+}
+
+// lvals == [0, 1, ..., L]?  Returns L, or -1.
+int contiguous_lmax(const int32_t *lv, int32_t n) {
+    if (!lv || n < 1 || n > 5) return -1;
+    for (int i = 0; i < n; i++)
+        if (lv[i] != i) return -1;
+    return n - 1;
+}
+
+}  // namespace sep
+}  // namespace feq
+
+using namespace feq;
+
+extern "C" int feq_edgewise_separable_supported(const FeqSeparableArgs *a) {
+    if (!a) return 0;
+    const int lin = sep::contiguous_lmax(a->lvals_in, a->n_lvals_in);
+    const int lout = sep::contiguous_lmax(a->lvals_out, a->n_lvals_out);
+    if (lin < 1 || lin != lout) return 0;
+    if (a->c_in != sep::kCin || a->c_out != sep::kCout || a->rank != sep::kRank) return 0;
+    if (a->mix_mode != FEQ_MIX_BF16 && a->mix_mode != FEQ_MIX_BF16X3) return 0;
+    if (!a->directions) return 0;
+    return 1;
+}
+
+extern "C" int feq_edgewise_separable_fwd(const FeqSeparableArgs *a, feq_stream_t stream) {
+    if (!a) return FEQ_ERR_INVALID_ARGUMENT;
+    if (a->num_edges < 0 || a->num_bins < 1) return FEQ_ERR_INVALID_ARGUMENT;
+    if (!feq_edgewise_separable_supported(a)) return FEQ_ERR_UNSUPPORTED;
+    if (a->num_edges == 0) return FEQ_OK;
+    if (!a->x || !a->distances || !a->channel_patterns || !a->radial_features || !a->out)
+        return FEQ_ERR_INVALID_ARGUMENT;
+    if ((reinterpret_cast<uintptr_t>(a->x) | reinterpret_cast<uintptr_t>(a->out) |
+         reinterpret_cast<uintptr_t>(a->edge_add)) & 15)
+        return FEQ_ERR_INVALID_ARGUMENT;      // bulk copies need 16-byte aligned rows
+    const int L = a->n_lvals_in - 1;
+    sep::SepParams P;
+    P.x = a->x;
+    P.src = a->src;
+    P.nsrc = a->src ? a->num_src_rows : a->num_edges;
+    P.edge_add = a->edge_add;
+    P.dirs = a->directions;
+    P.dist = a->distances;
+    P.cpat = a->channel_patterns;
+    P.ftab = a->radial_features;
+    P.out = a->out;
+    P.status = a->status;
+    P.E = a->num_edges;
+    P.bins.p1 = a->bin_param1;
+    P.bins.p2 = a->bin_param2;
+    P.bins.num_bins = a->num_bins;
+    P.bins.log_bins = a->log_bins;
+    P.sh_scale = a->sh_scale;
+    P.wait_ns = wait_limit_ns();
+    const int te = 128 / ((L + 1) * (L + 1) <= 16 ? 16 : 32);
+    P.num_tiles = (a->num_edges + te - 1) / te;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    ProfScope prof("sep_edgewise", s);
+    return a->mix_mode == FEQ_MIX_BF16X3 ? sep::dispatch<true>(L, L, P, s) : sep::dispatch<false>(L, L, P, s);
+}

@@ -36,6 +36,18 @@ class FeqEdgewiseArgs(ctypes.Structure):
     ]
 
 
+class FeqSeparableArgs(ctypes.Structure):
+    _fields_ = [
+        ("x", c_vp), ("src", c_vp), ("num_src_rows", ctypes.c_int64), ("edge_add", c_vp),
+        ("directions", c_vp), ("distances", c_vp), ("channel_patterns", c_vp), ("radial_features", c_vp),
+        ("num_edges", ctypes.c_int64), ("c_in", ctypes.c_int32), ("c_out", ctypes.c_int32),
+        ("rank", ctypes.c_int32), ("lvals_in", c_i32p), ("n_lvals_in", ctypes.c_int32),
+        ("lvals_out", c_i32p), ("n_lvals_out", ctypes.c_int32), ("sh_scale", ctypes.c_float),
+        ("bin_param1", ctypes.c_float), ("bin_param2", ctypes.c_float), ("num_bins", ctypes.c_int32),
+        ("log_bins", ctypes.c_int32), ("out", c_vp), ("status", c_vp), ("mix_mode", ctypes.c_int32),
+    ]
+
+
 class FeqAttnArgs(ctypes.Structure):
     _fields_ = [
         ("qk", c_vp), ("v", c_vp), ("src", c_vp), ("distances", c_vp), ("perm", c_vp), ("offsets", c_vp),
@@ -102,6 +114,8 @@ SIGNATURES = {
                                                       ctypes.c_float, ctypes.c_int32, ctypes.c_int32, c_vp, c_vp]),
     "feq_edgewise_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(FeqEdgewiseArgs)]),
     "feq_edgewise_fwd": (ctypes.c_int, [ctypes.POINTER(FeqEdgewiseArgs), c_vp, ctypes.c_size_t, c_vp]),
+    "feq_edgewise_separable_supported": (ctypes.c_int, [ctypes.POINTER(FeqSeparableArgs)]),
+    "feq_edgewise_separable_fwd": (ctypes.c_int, [ctypes.POINTER(FeqSeparableArgs), c_vp]),
     "feq_segment_softmax": (ctypes.c_int, [c_vp, ctypes.c_int64, ctypes.c_int32, c_vp, c_vp, ctypes.c_int64,
                                            c_vp, c_vp]),
     "feq_edge_attention_weights": (ctypes.c_int, [c_vp, c_vp, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32,
@@ -123,6 +137,14 @@ SIGNATURES = {
     "feq_knn_workspace_bytes": (ctypes.c_size_t, [ctypes.c_int64]),
     "feq_knn_graph": (ctypes.c_int, [c_vp, ctypes.c_int64, ctypes.c_int32, ctypes.c_float, ctypes.c_float,
                                      ctypes.c_float, ctypes.c_float, c_vp, c_vp, c_vp, ctypes.c_size_t, c_vp]),
+    "feq_radius_workspace_bytes": (ctypes.c_size_t, [ctypes.c_int64]),
+    "feq_radius_pairs_workspace_bytes": (ctypes.c_size_t, [ctypes.c_int64]),
+    "feq_radius_count": (ctypes.c_int, [c_vp, c_vp, ctypes.c_int64, ctypes.c_float, ctypes.c_int32, ctypes.c_float,
+                                        ctypes.c_float, ctypes.c_float, ctypes.c_float, c_vp, c_vp, c_vp,
+                                        ctypes.c_size_t, c_vp]),
+    "feq_radius_fill": (ctypes.c_int, [c_vp, c_vp, ctypes.c_int64, ctypes.c_float, ctypes.c_int32, ctypes.c_float,
+                                       ctypes.c_float, ctypes.c_float, ctypes.c_float, c_vp, ctypes.c_int64, c_vp,
+                                       c_vp, c_vp, ctypes.c_size_t, c_vp, ctypes.c_size_t, c_vp]),
     "feq_node_gate": (ctypes.c_int, [c_vp, c_vp, ctypes.c_int64, ctypes.c_int32, c_i32p, ctypes.c_int32, c_vp, c_vp]),
     "feq_segment_softmax_bwd": (ctypes.c_int, [c_vp, c_vp, ctypes.c_int64, ctypes.c_int32, c_vp, c_vp,
                                                ctypes.c_int64, c_vp, c_vp]),

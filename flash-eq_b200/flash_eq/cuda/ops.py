@@ -269,6 +269,82 @@ def edgewise_fwd(x, distances, radial_table, lvals_in, lvals_out, c_out, sh_scal
     return out
 
 
+def _separable_args(lvals_in, lvals_out, c_in, c_out, rank, mix):
+    args = _lib.FeqSeparableArgs()
+    ai, ni = _lib.i32_array(lvals_in)
+    ao, no = _lib.i32_array(lvals_out)
+    args.lvals_in, args.n_lvals_in = ai, ni
+    args.lvals_out, args.n_lvals_out = ao, no
+    args.c_in, args.c_out, args.rank = int(c_in), int(c_out), int(rank)
+    args.mix_mode = _lib.FEQ_MIX.get(mix, -1)
+    args.directions = 1          # the fused basis is the only one this kernel takes
+    return args, (ai, ao)
+
+
+def separable_supported(lvals_in, lvals_out, c_in, c_out, rank, mix) -> bool:
+    """Whether feq_edgewise_separable_fwd runs this layer shape (else use edgewise_fwd)."""
+    if mix not in ("bf16x3", "bf16"):
+        return False
+    args, _keep = _separable_args(lvals_in, lvals_out, c_in, c_out, rank, mix)
+    return bool(_lib.load().feq_edgewise_separable_supported(ctypes.byref(args)))
+
+
+def _aligned16(t):
+    return t if t.data_ptr() % 16 == 0 else t.clone()
+
+
+def edgewise_separable_fwd(x, distances, channel_patterns, radial_features, lvals_in, lvals_out, sh_scale, p1, p2,
+                           num_bins, log_bins, *, directions, src=None, edge_add=None, status=None, mix="bf16x3"):
+    """Q . Lambda(r) . P^T . f in one kernel for a separable radial table
+    table[b, o, i, w] = sum_k channel_patterns[k, o, i] radial_features[b, k, w].
+
+    Rows f[e] = x[src[e]] (+ edge_add[e]) or x[e]; basis from ``directions`` (E, 3).
+    ``mix``: "bf16x3" (float32-level accuracy) or "bf16".  No workspace."""
+    lib = _require_cuda(x, distances, channel_patterns, radial_features, src, edge_add, directions)
+    x = _aligned16(_f32(x, "x"))
+    distances = _f32(distances, "distances")
+    cp = _f32(channel_patterns, "channel_patterns")
+    rf = _f32(radial_features, "radial_features")
+    directions = _f32(directions, "directions")
+    E = distances.numel()
+    rank, c_out, c_in = cp.shape
+    d_in, d_out = dim_of(lvals_in), dim_of(lvals_out)
+    if x.shape[1] != c_in or x.shape[2] != d_in:
+        raise ValueError(f"x {tuple(x.shape)} does not match (rows, {c_in}, {d_in})")
+    if rf.shape[0] != num_bins + 1 or rf.shape[1] != rank:
+        raise ValueError(f"radial_features {tuple(rf.shape)} does not match ({num_bins + 1}, {rank}, W)")
+    dev = x.device
+    out = torch.empty(E, c_out, d_out, dtype=torch.float32, device=dev)
+    if E == 0:
+        return out
+    args, _keep = _separable_args(lvals_in, lvals_out, c_in, c_out, rank, mix)
+    args.x = x.data_ptr()
+    if src is not None:
+        src = src.contiguous()
+        if src.dtype != torch.int64:
+            src = src.to(torch.int64)
+        args.src = src.data_ptr()
+        args.num_src_rows = x.shape[0]
+    elif x.shape[0] != E:
+        raise ValueError("edge features must have one row per edge")
+    if edge_add is not None:
+        edge_add = _aligned16(_f32(edge_add, "edge_features"))
+        args.edge_add = edge_add.data_ptr()
+    args.directions = directions.data_ptr()
+    args.distances = distances.data_ptr()
+    args.channel_patterns = cp.data_ptr()
+    args.radial_features = rf.data_ptr()
+    args.num_edges = E
+    args.sh_scale, args.bin_param1, args.bin_param2 = float(sh_scale), float(p1), float(p2)
+    args.num_bins, args.log_bins = int(num_bins), int(bool(log_bins))
+    args.out = out.data_ptr()
+    if status is not None:
+        args.status = status.data_ptr()
+    rc = lib.feq_edgewise_separable_fwd(ctypes.byref(args), _stream(dev))
+    _lib.check(rc, "feq_edgewise_separable_fwd")
+    return out
+
+
 def segment_softmax(logits, perm, offsets, num_nodes):
     lib = _require_cuda(logits, perm, offsets)
     logits = _f32(logits, "logits")
@@ -526,6 +602,52 @@ def knn(coords, k, cell=None):
     if int(status.item()) != 0:
         raise RuntimeError("feq_knn_graph: search stopped before it was exact (cell too small)")
     return nbr
+
+
+def radius_graph(coords, r, batch=None, loop=False):
+    """(src, dst) int64 of every ordered pair of points of the same batch entry closer than
+    ``r`` (strictly), without self pairs unless ``loop``; in (src, dst) order.  One host
+    synchronisation (the edge count)."""
+    lib = _require_cuda(coords, batch)
+    xyz = _f32(coords, "coordinates")
+    if xyz.dim() != 2 or xyz.shape[1] != 3:
+        raise ValueError("coordinates must have shape (N, 3)")
+    r = float(r)
+    if not r > 0.0:
+        raise ValueError(f"r must be > 0, got {r}")
+    N = xyz.shape[0]
+    dev = xyz.device
+    empty = torch.empty(0, dtype=torch.int64, device=dev)
+    if N == 0:
+        return empty, empty
+    if batch is not None:
+        batch = batch.to(device=dev, dtype=torch.int64).contiguous()
+        if batch.shape != (N,):
+            raise ValueError(f"batch must have shape ({N},), got {tuple(batch.shape)}")
+    lo = xyz.min(dim=0).values
+    span = float((xyz.max(dim=0).values - lo).max())
+    cell = max(r, span / 16000.0)           # <= 16384 cells per axis
+    x0, y0, z0 = (float(v) - cell for v in lo.tolist())     # one empty cell of margin
+    offsets = torch.empty(N + 1, dtype=torch.int64, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    ws = _workspace(lib.feq_radius_workspace_bytes(N), dev)
+    stream = _stream(dev)
+    rc = lib.feq_radius_count(_p(xyz), _p(batch), N, r, int(bool(loop)), cell, x0, y0, z0, _p(offsets), _p(status),
+                              _p(ws), ws.numel(), stream)
+    _lib.check(rc, "feq_radius_count")
+    E = int(offsets[N].item())
+    if int(status.item()) != 0:
+        raise RuntimeError("feq_radius_count: a point has a non-finite coordinate, lies outside the cell grid or "
+                           "has a batch id out of range")
+    src = torch.empty(E, dtype=torch.int64, device=dev)
+    dst = torch.empty(E, dtype=torch.int64, device=dev)
+    if E == 0:
+        return src, dst
+    pws = _workspace(lib.feq_radius_pairs_workspace_bytes(E), dev)
+    rc = lib.feq_radius_fill(_p(xyz), _p(batch), N, r, int(bool(loop)), cell, x0, y0, z0, _p(offsets), E, _p(src),
+                             _p(dst), _p(ws), ws.numel(), _p(pws), pws.numel(), stream)
+    _lib.check(rc, "feq_radius_fill")
+    return src, dst
 
 
 # ---------------------------------------------------------------------------

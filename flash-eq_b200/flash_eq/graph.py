@@ -71,6 +71,17 @@ class Graph:
             src, dst = src[keep], dst[keep]
         return Graph(src=src, dst=dst, num_nodes=n)
 
+    @staticmethod
+    def radius(coordinates: torch.Tensor, r: float, batch: torch.Tensor | None = None,
+               loop: bool = False) -> "Graph":
+        """Radius graph on the GPU (no counterpart in the reference): an edge src -> dst for
+        every ordered pair of nodes of the same graph (``batch`` ids; None: one graph) closer
+        than ``r``, in (src, dst) order; no self loops unless ``loop``."""
+        from .cuda import ops
+
+        src, dst = ops.radius_graph(coordinates, r, batch=batch, loop=loop)
+        return Graph(src=src, dst=dst, num_nodes=coordinates.shape[0])
+
     # -- dst-sorted view ----------------------------------------------------
     def _check_src(self):
         """Device bool: some src index lies outside [0, num_nodes) (None without edges)."""

@@ -70,15 +70,25 @@ class EquivariantEdgewiseLinear(nn.Module):
         if E == 0:
             return torch.zeros(0, self.channels_out, self.out_repr.dim(), device=x.device, dtype=x.dtype)
         p1, p2 = rw.binning_params()
-        table = rw()
         dist = distances.to(torch.float32)
-        if torch.is_grad_enabled() and any(
-                t is not None and t.requires_grad for t in (x, table, dist, edge_add,
-                                                            P if torch.is_tensor(P) else None,
-                                                            Q if torch.is_tensor(Q) else None)):
-            return self._run_autograd(P, Q, x, dist, table, p1, p2, src, edge_add)
+        grad = torch.is_grad_enabled() and (
+            any(t is not None and t.requires_grad for t in (x, dist, edge_add, P if torch.is_tensor(P) else None,
+                                                            Q if torch.is_tensor(Q) else None))
+            or any(p.requires_grad for p in rw.parameters()))
         dP, dQ = basis_source(P, self._lin), basis_source(Q, self._lout)
         fused = dP is not None and dQ is not None and dP is dQ
+        if not grad and fused and self._separable_ok(x):
+            # the table is never formed: one kernel interpolates the radial features per
+            # edge and applies the channel patterns on the tensor cores
+            with torch.no_grad():
+                feats = rw.radial_features()
+            return ops.edgewise_separable_fwd(
+                x.detach(), dist.detach(), rw.channel_patterns.detach(), feats, self._lin, self._lout,
+                self.solid_harmonic_scale, p1, p2, rw.num_bins, rw.log, directions=dP, src=src,
+                edge_add=None if edge_add is None else edge_add.detach(), mix=self.mix_precision)
+        table = rw()
+        if grad:
+            return self._run_autograd(P, Q, x, dist, table, p1, p2, src, edge_add)
         Pd = Qd = None
         if not fused:
             Pd, Qd = _dense(P), _dense(Q)
@@ -92,6 +102,18 @@ class EquivariantEdgewiseLinear(nn.Module):
                 mix=self.mix_precision)
 
         return forward_only(run, x, table, dist, edge_add, Pd, Qd)
+
+    def _separable_ok(self, x) -> bool:
+        """Whether the one-kernel separable path serves this call (layer shape, mix and a
+        CUDA float32 input); cached per mix mode."""
+        if not (x.is_cuda and x.dtype == torch.float32):
+            return False
+        key = self.mix_precision
+        cache = self.__dict__.setdefault("_sep_cache", {})
+        if key not in cache:
+            cache[key] = ops.separable_supported(self._lin, self._lout, self.channels_in, self.channels_out,
+                                                 self.rank, key)
+        return cache[key]
 
     def _run_autograd(self, P, Q, x, dist, table, p1, p2, src, edge_add):
         """The reference's three steps (linear.py:135-160) with autograd: bmm into the edge

@@ -88,10 +88,14 @@ class SeparableRadialNet(nn.Module):
         ang = x.unsqueeze(-1) * self.frequencies
         return torch.cat([torch.sin(ang) * env.unsqueeze(-1), torch.cos(ang) * env.unsqueeze(-1)], dim=-1)
 
-    def forward(self) -> torch.Tensor:
+    def radial_features(self) -> torch.Tensor:
+        """f_k(r_b, w) at the bin edges, (num_bins + 1, rank, weight_dim): the factor of the
+        table that depends on distance (radial.py:259-267)."""
         f = self.head(self.trunk(self._sinusoidal_basis(self.bin_edges)))
-        f = f.view(-1, self.rank, self.weight_dim)
-        return torch.einsum("koi,bkw->boiw", self.channel_patterns, f)
+        return f.view(-1, self.rank, self.weight_dim)
+
+    def forward(self) -> torch.Tensor:
+        return torch.einsum("koi,bkw->boiw", self.channel_patterns, self.radial_features())
 
     def binning_params(self) -> tuple[float, float]:
         if self.log:

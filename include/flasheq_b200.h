@@ -256,6 +256,49 @@ int feq_edgewise_fwd(const FeqEdgewiseArgs *args, void *workspace, size_t worksp
                      feq_stream_t stream);
 
 /* ---------------------------------------------------------------------------
+ * Separable edgewise linear: the same result as feq_edgewise_fwd for the radial tables
+ * EquivariantEdgewiseLinear builds, in ONE kernel (gather, rotation in, mix, rotation
+ * back), without a workspace.
+ * Replaces EquivariantEdgewiseLinear.forward (flash_eq/layers/linear.py:100-160) together
+ * with the table its SeparableRadialNet materialises (flash_eq/layers/radial.py:259-275):
+ *   table[b, o, i, w] = sum_k channel_patterns[k, o, i] * radial_features[b, k, w]
+ * is never formed; the kernel interpolates radial_features per edge and applies
+ * channel_patterns on the tensor cores (tcgen05) with a weight shared by every edge.
+ *   radial_features: (num_bins + 1, rank, W) = the radial net's head output viewed as
+ *   (B, K, W) (radial.py:266-267); channel_patterns: (rank, c_out, c_in).
+ * Input rows f[e] = x[src[e]] (+ edge_add[e]) or x[e]; the basis comes from directions.
+ * feq_edgewise_separable_supported() says whether this build runs a request (lvals
+ * [0..L] in and out with L <= 4, c_in = c_out = 64, rank 4, mix FEQ_MIX_BF16X3 or
+ * FEQ_MIX_BF16, directions given); otherwise use feq_edgewise_fwd with the table.
+ * status (optional): 1 = a src index was out of range (that row reads as zero),
+ * 2 = a tensor-core wait timed out (result invalid).
+ * ------------------------------------------------------------------------ */
+typedef struct FeqSeparableArgs {
+    const float *x;                 /* (E or N, c_in, d_in) standard order, 16-byte aligned */
+    const int64_t *src;             /* optional (E,) gather index into x */
+    int64_t num_src_rows;           /* rows of x when src != NULL */
+    const float *edge_add;          /* optional (E, c_in, d_in), 16-byte aligned */
+    const float *directions;        /* (E, 3) */
+    const float *distances;         /* (E,) */
+    const float *channel_patterns;  /* (rank, c_out, c_in) */
+    const float *radial_features;   /* (num_bins + 1, rank, W) */
+    int64_t num_edges;
+    int32_t c_in, c_out, rank;
+    const int32_t *lvals_in;        /* host array */
+    int32_t n_lvals_in;
+    const int32_t *lvals_out;       /* host array */
+    int32_t n_lvals_out;
+    float sh_scale, bin_param1, bin_param2;
+    int32_t num_bins, log_bins;
+    float *out;                     /* (E, c_out, d_out) standard order, 16-byte aligned */
+    int32_t *status;
+    int32_t mix_mode;               /* FEQ_MIX_BF16X3 or FEQ_MIX_BF16 */
+} FeqSeparableArgs;
+
+int feq_edgewise_separable_supported(const FeqSeparableArgs *args);
+int feq_edgewise_separable_fwd(const FeqSeparableArgs *args, feq_stream_t stream);
+
+/* ---------------------------------------------------------------------------
  * Segment softmax over edges that share a destination
  * (EquivariantEdgeAttention._neighbor_softmax, flash_eq/layers/attention.py:108-141):
  *   w[e, h] = exp(l[e,h] - max_seg) / (sum_seg exp(. - max_seg) + 1e-8)
@@ -432,6 +475,34 @@ int feq_node_gate(const float *x, const float *z, int64_t num_nodes, int32_t C, 
 size_t feq_knn_workspace_bytes(int64_t num_points);
 int feq_knn_graph(const float *xyz, int64_t num_points, int32_t k, float cell, float x0, float y0, float z0,
                   int64_t *nbr, int32_t *status, void *workspace, size_t workspace_bytes, feq_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Radius graph construction (no counterpart in the reference, which leaves graph building
+ * to the user, README.md:49-52; its benchmark graphs are "all pairs within r"): every
+ * ordered pair (i, j) of points with batch[i] == batch[j] (batch may be NULL: one graph),
+ * j != i unless loop != 0, and |x_j - x_i| < r, with the squared distance rounded as the
+ * float32 expression (dx*dx + dy*dy) + dz*dz (no fused multiply-add), so the edge set equals
+ * a brute-force evaluation bit for bit.  Edges come out as src = i, dst = j in (src, dst)
+ * order.  Two calls:
+ *   1. feq_radius_count fills offsets (N + 1 int64): point i has offsets[i + 1] - offsets[i]
+ *      neighbours, offsets[N] = the edge count (read it, then allocate src / dst).
+ *   2. feq_radius_fill writes src / dst (num_edges each) from the same inputs and the SAME
+ *      workspace, untouched since the count (it holds the sorted cell lists), plus a pair
+ *      workspace of feq_radius_pairs_workspace_bytes(num_edges).
+ * Cells are cubes of side `cell` >= r with corner (x0, y0, z0); at most 16384 cells per axis
+ * and batch ids below 2^21.  status (may be NULL) is set to 1 when a point falls outside
+ * that grid, has a non-finite coordinate or a batch id out of range (result invalid).
+ * N < 2^31.
+ * ------------------------------------------------------------------------ */
+size_t feq_radius_workspace_bytes(int64_t num_points);
+size_t feq_radius_pairs_workspace_bytes(int64_t num_edges);
+int feq_radius_count(const float *xyz, const int64_t *batch, int64_t num_points, float r, int32_t loop, float cell,
+                     float x0, float y0, float z0, int64_t *offsets, int32_t *status, void *workspace,
+                     size_t workspace_bytes, feq_stream_t stream);
+int feq_radius_fill(const float *xyz, const int64_t *batch, int64_t num_points, float r, int32_t loop, float cell,
+                    float x0, float y0, float z0, const int64_t *offsets, int64_t num_edges, int64_t *src,
+                    int64_t *dst, const void *workspace, size_t workspace_bytes, void *pair_workspace,
+                    size_t pair_workspace_bytes, feq_stream_t stream);
 
 #ifdef __cplusplus
 }

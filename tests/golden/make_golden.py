@@ -74,12 +74,60 @@ def knn_graph(coords: torch.Tensor, k: int, batch: torch.Tensor | None = None):
     return src, dst
 
 
+def seeded_parameters(model, seed: int) -> None:
+    """Fill every parameter (not buffer) of ``model`` from one generator, in sorted-name
+    order: U(-1, 1) / sqrt(last dim).  The B200 modules have the same parameter names and
+    shapes, so the same call reproduces the weights without storing them."""
+    g = torch.Generator().manual_seed(seed)
+    with torch.no_grad():
+        for name, p in sorted(model.named_parameters()):
+            scale = 1.0 / max(1, p.shape[-1]) ** 0.5 if p.dim() else 0.1
+            p.copy_((torch.rand(p.shape, generator=g, dtype=torch.float64) * 2 - 1).to(p.dtype) * scale)
+
+
+def knn_within(coords: torch.Tensor, batch: torch.Tensor, k: int):
+    """k nearest neighbours inside each graph of a batch, src -> dst, grouped by dst."""
+    return knn_graph(coords, k, batch)
+
+
+def make_model_config4(fe) -> dict:
+    """BASELINE config 4 at reduced size: EquivariantTransformer in Repr([0,1],32), hidden
+    Repr([0,1,2,3],128), 8 heads, 16-NN within each graph, coordinates N(0, 2^2), seed 3.
+    Out Repr([0], 8) instead of Repr([0], 1): the reference rejects 8 heads on out mult 1
+    (attention.py:233-236).  3 layers (in -> hidden, hidden -> hidden, hidden -> out) on
+    4 graphs of 50 nodes; weights from seeded_parameters(model, 3)."""
+    n_graphs, npg, k = 4, 50, 16
+    g = torch.Generator().manual_seed(3)
+    coords = torch.randn(n_graphs * npg, 3, generator=g) * 2.0
+    batch = torch.arange(n_graphs).repeat_interleave(npg)
+    src, dst = knn_within(coords, batch, k)
+    x = torch.randn(n_graphs * npg, 32, 4, generator=g)
+    rin, rh, rout = fe.Repr([0, 1], mult=32), fe.Repr([0, 1, 2, 3], mult=128), fe.Repr([0], mult=8)
+    model = fe.EquivariantTransformer(rin, rh, rout, num_layers=3, num_heads=8, max_dist=10.0).eval()
+    seeded_parameters(model, 3)
+    graph = fe.Graph(src=src, dst=dst, num_nodes=len(coords))
+    caps = []
+    hooks = [lay.register_forward_hook(lambda mod, inp, outp: caps.append(outp)) for lay in model.layers]
+    with torch.no_grad():
+        y = model(coords, x, graph)
+    for h in hooks:
+        h.remove()
+    return {"coords": coords, "src": src, "dst": dst, "x": x, "output": y, "first_layer_output": caps[0],
+            "param_seed": 3, "num_layers": 3, "num_heads": 8}
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
+    ap.add_argument("--only", choices=["all", "model4"], default="all",
+                    help="model4: only the config-4 model fixture (model_config4.pt)")
     ap.add_argument("--ref", default=os.environ.get("FEQ_REFERENCE_ROOT")
                     or os.path.join(os.path.dirname(ROOT), "reference"))
     args = ap.parse_args()
     fe, orc = import_reference(args.ref)
+    if args.only == "model4":
+        torch.save(make_model_config4(fe), os.path.join(HERE, "model_config4.pt"))
+        print("model_config4.pt", os.path.getsize(os.path.join(HERE, "model_config4.pt")))
+        return 0
     from flash_eq.layers.linear import EquivariantEdgewiseLinear
     from flash_eq.representations.wigner import _build_m_order_permutation
 
@@ -275,6 +323,7 @@ def main() -> int:
         h.remove()
     torch.save({"coords": coords, "src": src, "dst": dst, "x": x, "state": model.state_dict(),
                 "output": y, "layer_outputs": caps}, os.path.join(HERE, "transformer.pt"))
+    torch.save(make_model_config4(fe), os.path.join(HERE, "model_config4.pt"))
 
     sizes = {f: os.path.getsize(os.path.join(HERE, f)) for f in os.listdir(HERE) if f.endswith((".pt", ".json"))}
     print(json.dumps(sizes, indent=1))

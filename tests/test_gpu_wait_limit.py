@@ -76,3 +76,35 @@ def test_wait_limit_setter_round_trips():
         assert lib.feq_set_wait_limit_ns(prev) == 4_000_000_000
     finally:
         lib.feq_set_wait_limit_ns(prev)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("mix", ["bf16x3", "bf16"])
+def test_separable_kernel_short_wait_limit(cuda_device, mix):
+    """The same for the one-kernel separable edgewise path (feq_edgewise_separable_fwd)."""
+    lib = _lib.load()
+    lv, mult, E = [0, 1, 2, 3, 4], 64, 20000
+    layer, f, dirs, dist, table, p1, p2 = _problem(cuda_device, lv, mult, E, seed=5)
+    rw = layer.radial_weights
+
+    def call(status):
+        with torch.no_grad():
+            return ops.edgewise_separable_fwd(f.to(cuda_device), dist.to(cuda_device), rw.channel_patterns,
+                                              rw.radial_features(), lv, lv, 0.1, p1, p2, rw.num_bins, False,
+                                              directions=dirs.to(cuda_device), status=status, mix=mix)
+
+    status = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    prev = lib.feq_set_wait_limit_ns(1000)
+    try:
+        call(status)
+        torch.cuda.synchronize()
+    finally:
+        lib.feq_set_wait_limit_ns(prev)
+    assert int(status.item()) == 2
+    status.zero_()
+    y = call(status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    ref = orc.edgewise_fwd(orc.wigner_basis(dirs, lv), orc.wigner_basis(dirs, lv), f, dist, table.cpu(), lv, lv,
+                           0.1, p1, p2, rw.num_bins, False)
+    assert rel_l2(y, ref) < (1e-4 if mix == "bf16x3" else 2e-2)
