@@ -347,6 +347,9 @@ def dist_setup(args):
 
         import torch.distributed as dist
 
+        # communicator set-up lines (rank, device, transport) in the log
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
         pg = dist
@@ -539,6 +542,16 @@ def run_ours(args):
                                                     f"(CPU: {cpu_model()})"}
             except Exception as exc:  # the baseline must not hide the GPU number
                 result["cpu_baseline"] = {"value": None, "error": repr(exc)}
+    if world > 1 and not args.no_config5:
+        # the scaling run of this default workload exercises no collective (independent graphs);
+        # the same run also measures config 5 (one graph, dst-range partition, NCCL halo
+        # exchange per layer) at this GPU count, with its exchange time and stage table
+        del wl, x, src, coords, vec, dist_e
+        torch.cuda.empty_cache()
+        rec5 = giant_measure(args, world, rank, local, pg, GIANT_NODES, 10, 3, 0)
+        if rank == 0:
+            result["config5_partitioned"] = rec5
+    if rank == 0:
         print(json.dumps(result), flush=True)
     if pg is not None:
         pg.barrier()
@@ -1176,26 +1189,18 @@ def make_walk(n: int, seed: int) -> torch.Tensor:
     return torch.cumsum(GIANT_STEP * steps / steps.norm(dim=1, keepdim=True), 0)
 
 
-def run_giant(args):
-    """One step = the 2-layer EquivariantTransformer forward over the rank's dst range of the
-    1 M-node graph; per layer the rank's halo rows come from their owners (NCCL all-to-all).
-    Graph built once (GPU kNN) and partitioned before the timed region; strong scaling."""
+def giant_measure(args, world, rank, local, pg, n, steps, warmup, e2e_steps):
+    """Config 5 on the ranks of pg: build the graph (GPU kNN), partition it by dst range, time
+    `steps` forward steps of the 2-layer transformer (max over ranks), then a few profiled
+    steps: per-stage device times (rank 0), the per-layer NCCL exchanges (CUDA events around
+    each all_to_all_single, max over ranks) and every rank's halo size.  Returns rank 0's
+    record (other ranks: None)."""
     import flash_eq as fe
+    from flash_eq import partition as fpart
     from flash_eq.cuda import _lib
     from flash_eq.cuda import ops as feq_ops
     from flash_eq.partition import partition_graph
 
-    n = args.nodes if args.nodes != N_NODES else GIANT_NODES
-    if args.impl == "reference":
-        if int(os.environ.get("RANK", "0")) == 0:
-            print(json.dumps({"impl": "reference", "unavailable": "config 5 has no CPU arm: the oracle port of the "
-                              "2-layer transformer over 16 M edges takes hours on the host cores; the block "
-                              "workload carries the transformer CPU baseline"}), flush=True)
-        return 0
-    # 16 M edge rows per layer: let the caching allocator grow segments instead of
-    # fragmenting across the per-layer edge tensors (read at the first CUDA use)
-    os.environ.setdefault("PYTORCH_CUDA_ALLOC_CONF", "expandable_segments:True")
-    world, rank, local, pg = dist_setup(args)
     dev = torch.device("cuda", local)
     lib = _lib.load()
     coords = make_walk(n, GIANT_SEED)
@@ -1215,14 +1220,13 @@ def run_giant(args):
     lo, hi = (part.node_start, part.node_end) if world > 1 else (0, n)
     x_own = x[lo:hi].to(dev)
     E_total, E_rank = graph.num_edges, part.num_edges
-    halo_rows = part.num_halo if world > 1 else 0          # rows received per exchange
     del graph
 
     def step():
         with torch.no_grad():
             return model(coords_d, x_own, part)
 
-    for _ in range(max(3, args.warmup)):
+    for _ in range(max(3, warmup)):
         step()
     barrier(pg)
     clk = ClockSampler(gpu_index_for(local))
@@ -1231,38 +1235,59 @@ def run_giant(args):
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier(pg)
     t0.record()
-    for _ in range(args.steps):
+    for _ in range(steps):
         step()
     t1.record()
     barrier(pg)
     launches = lib.feq_launch_count() - n0
     clocks = clk.stop()
-    ms = max_over_ranks(pg, t0.elapsed_time(t1) / args.steps)
+    ms = max_over_ranks(pg, t0.elapsed_time(t1) / steps)
     value = E_total / (ms / 1e3)
-    # per-stage device times (events on the library's streams), a few extra steps
+    # profiled steps: library stages (rank 0) and the exchanges (every rank)
     feq_ops.profile_enable(True)
-    for _ in range(2):
+    fpart.EXCHANGE_EVENTS = [] if world > 1 else None
+    prof_steps = 2
+    for _ in range(prof_steps):
         step()
     torch.cuda.synchronize()
-    stages = {k: {"ms": v[0] / 2, "launches": v[1] // 2} for k, v in feq_ops.profile_read().items()}
+    stages = {k: {"ms": v[0] / prof_steps, "launches": v[1] // prof_steps} for k, v in feq_ops.profile_read().items()}
     feq_ops.profile_enable(False)
+    exchange = None
+    if world > 1:
+        ev = fpart.EXCHANGE_EVENTS
+        fpart.EXCHANGE_EVENTS = None
+        per = [a.elapsed_time(b) for a, b in ev]
+        k = len(per) // prof_steps
+        ex_ms = max_over_ranks(pg, sum(per) / prof_steps)
+        halos = torch.zeros(world, dtype=torch.float64, device=dev)
+        halos[rank] = part.num_halo
+        owned = torch.zeros(world, dtype=torch.float64, device=dev)
+        owned[rank] = hi - lo
+        pg.all_reduce(halos)
+        pg.all_reduce(owned)
+        exchange = {"ms_per_step_max_rank": ex_ms, "exchanges_per_step": k,
+                    "ms_each_rank0": [round(v, 4) for v in per[:k]],
+                    "halo_rows_per_rank": [int(v) for v in halos.tolist()],
+                    "owned_rows_per_rank": [int(v) for v in owned.tolist()],
+                    "bytes_per_exchange_rank0": int(part.num_halo) * 64 * 9 * 4}
     hbm_peak, _, peak_kind = measured_peaks()
     row = 64 * 9 * 4
     nsplit = 2 if args.mix == "bf16x3" else 1
     stage_bytes = {"rotate_in": row + 32 + 64 * 9 * 2 * nsplit, "rotate_out": 2 * row + 24,
                    "attn_pool": row + 16, "sep_edgewise": 2 * row + 16}
-    for k, v in stages.items():
-        if k in stage_bytes:
-            v["hbm_gbs"] = 2 * E_rank * stage_bytes[k] / (v["ms"] / 1e3) / 1e9     # 2 layers per step
-    dom = max((k for k in stages if k in stage_bytes), key=lambda k: stages[k]["ms"], default=None)
+    for k_, v in stages.items():
+        if k_ in stage_bytes:
+            v["hbm_gbs"] = 2 * E_rank * stage_bytes[k_] / (v["ms"] / 1e3) / 1e9     # 2 layers per step
+    dom = max((k_ for k_ in stages if k_ in stage_bytes), key=lambda k_: stages[k_]["ms"], default=None)
     roofline = None
     if dom is not None:
         gbs = stages[dom]["hbm_gbs"]
         roofline = {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak,
                     "traffic": None, "kernel": f"{dom} (largest HBM-bound edge stage, rank 0; CUDA events on its stream)",
                     "peak_kind": peak_kind, "bytes_per_edge": stage_bytes[dom]}
+    lib_ms = sum(v["ms"] for v in stages.values())
     e2e = None
-    if args.e2e_steps > 0:
+    if e2e_steps > 0:
         x_h = x[lo:hi].pin_memory()
         out_h = torch.empty(hi - lo, 64, 9, pin_memory=True)
 
@@ -1275,34 +1300,152 @@ def run_giant(args):
         barrier(pg)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        for _ in range(args.e2e_steps):
+        for _ in range(e2e_steps):
             e2e_step()
         e1.record()
         barrier(pg)
-        ms_e = max_over_ranks(pg, e0.elapsed_time(e1) / args.e2e_steps)
+        ms_e = max_over_ranks(pg, e0.elapsed_time(e1) / e2e_steps)
         e2e = {"value": E_total / (ms_e / 1e3), "unit": "edges/s", "h2d_bytes_per_step": x_h.numel() * 4,
-               "d2h_bytes_per_step": out_h.numel() * 4, "ms_per_step": ms_e, "steps": args.e2e_steps,
+               "d2h_bytes_per_step": out_h.numel() * 4, "ms_per_step": ms_e, "steps": e2e_steps,
                "note": "per rank: owned node features in from pinned host memory, owned outputs back; the "
                        "graph and its partition stay resident (built once)"}
+    rec = None
     if rank == 0:
-        print(json.dumps({
+        largest = max(stages.items(), key=lambda kv: kv[1]["ms"]) if stages else None
+        rec = {
             "metric": "edges/sec (2-layer EquivariantTransformer fwd, dst-range partitioned, device-timed)",
-            "value": value, "unit": "edges/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "value": value, "unit": "edges/s", "n_gpus": world, "steps": steps, "warmup": warmup,
             "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "bf16" if args.mix == "bf16" else "f32", "data": "synthetic",
             "config": {"workload": f"config5: 3-D random walk of {n} nodes (3.8 A isotropic steps, seed 4), "
                                    f"16-NN graph built on the GPU (Graph.knn), E={E_total}; 2-layer "
                                    "EquivariantTransformer, Repr([0,1,2],64) in/hidden/out, 8 heads, max_dist 10",
                        "global_edges": E_total, "edges_rank0": E_rank, "owned_rows_rank0": hi - lo,
-                       "halo_rows_rank0": halo_rows,
+                       "halo_rows_rank0": part.num_halo if world > 1 else 0,
                        "parallelism": f"dst-range partition over {world} GPU(s), NCCL halo exchange "
                                       "(all_to_all_single) of the src-side rows per layer" if world > 1
                                       else "whole graph on one GPU",
                        "graph_build_s": t_build,
                        "l2": f"no flush: {E_rank * row / 1e9:.1f} GB of edge rows per layer >> 126 MB L2"},
-            "roofline": roofline, "stages_ms_per_step_rank0": stages, "mix": args.mix, "clocks": clocks,
-            "e2e": e2e, "gpu_launches": int(launches),
-            "memory_gb_rank0": torch.cuda.max_memory_allocated(dev) / 1e9}), flush=True)
+            "roofline": roofline, "stages_ms_per_step_rank0": stages, "exchange": exchange,
+            "step_breakdown_rank0_ms": {"library_kernels": lib_ms,
+                                        "nccl_exchange": exchange["ms_per_step_max_rank"] if exchange else 0.0,
+                                        "other (torch node GEMMs, glue)": max(0.0, ms - lib_ms - (
+                                            exchange["ms_per_step_max_rank"] if exchange else 0.0)),
+                                        "largest_library_stage": largest[0] if largest else None},
+            "mix": args.mix, "clocks": clocks, "e2e": e2e, "gpu_launches": int(launches),
+            "memory_gb_rank0": torch.cuda.max_memory_allocated(dev) / 1e9}
+    del model, part, coords_d, x_own
+    torch.cuda.empty_cache()
+    return rec
+
+
+def run_giant(args):
+    """One step = the 2-layer EquivariantTransformer forward over the rank's dst range of the
+    1 M-node graph; per layer the rank's halo rows come from their owners (NCCL all-to-all).
+    Graph built once (GPU kNN) and partitioned before the timed region; strong scaling."""
+    n = args.nodes if args.nodes != N_NODES else GIANT_NODES
+    if args.impl == "reference":
+        if int(os.environ.get("RANK", "0")) == 0:
+            print(json.dumps({"impl": "reference", "unavailable": "config 5 has no CPU arm: the oracle port of the "
+                              "2-layer transformer over 16 M edges takes hours on the host cores; the block "
+                              "workload carries the transformer CPU baseline"}), flush=True)
+        return 0
+    # 16 M edge rows per layer: let the caching allocator grow segments instead of
+    # fragmenting across the per-layer edge tensors (read at the first CUDA use)
+    os.environ.setdefault("PYTORCH_CUDA_ALLOC_CONF", "expandable_segments:True")
+    world, rank, local, pg = dist_setup(args)
+    rec = giant_measure(args, world, rank, local, pg, n, args.steps, args.warmup, args.e2e_steps)
+    if rank == 0:
+        print(json.dumps(rec), flush=True)
+    if pg is not None:
+        pg.destroy_process_group()
+    return 0
+
+
+# Published PatchedConvSE3 forward times of the reference (FULL fuse, C = 32, 500 bins, one
+# ConvSE3 layer, NVIDIA H100): (L, edges) -> (SE(3)-T ms, patched ms), README.md:371-380.
+PUBLISHED_PATCH_MS = {(2, 4096): (0.71, 1.03), (2, 16384): (2.20, 2.41), (2, 65536): (8.87, 7.70),
+                      (3, 4096): (1.48, 1.42), (3, 16384): (5.42, 3.86), (3, 65536): (21.80, 13.39)}
+
+
+def run_patch(args):
+    """The reference's patch benchmark shapes through flash_eq.patch.PatchedConvSE3: one
+    convolution forward (gather, rotation, 500-bin mix with sh_scale = 0, rotation back,
+    edge -> node sum), C = 32, L = 2 / 3, 4K / 16K / 65K edges on a random graph of E / 16
+    nodes; a synthetic converted table (the NVIDIA model is not part of this build)."""
+    import flash_eq as fe
+    from types import SimpleNamespace
+
+    from flash_eq.patch import PatchedConvSE3
+
+    if args.impl == "reference":
+        if int(os.environ.get("RANK", "0")) == 0:
+            print(json.dumps({"impl": "reference", "unavailable": "the reference patch path needs NVIDIA's "
+                              "SE(3)-Transformer and DGL (not in this image); its published H100 times are "
+                              "carried in the line as context"}), flush=True)
+        return 0
+    world, rank, local, pg = dist_setup(args)
+    dev = torch.device("cuda", local)
+    rows = []
+    for L in (2, 3):
+        for E in (4096, 16384, 65536):
+            C, nb, N = 32, 500, E // 16
+            gen = torch.Generator().manual_seed(1000 * L + E)
+            lv = list(range(L + 1))
+            rin = fe.Repr(lv, mult=C)
+            pr = fe.ProductRepr(rin, rin)
+            table = (torch.randn(nb + 1, C, C, pr.nreps(), generator=gen) * 0.05).to(dev)
+            conv = SimpleNamespace(pool=True, fiber_in=SimpleNamespace(degrees=lv),
+                                   fiber_out=SimpleNamespace(degrees=lv), self_interaction=False)
+            mod = PatchedConvSE3(conv, table, pr, rin, rin, nb, 0.0, 10.0)
+            mod.mix_precision = args.mix
+            node = {str(d): torch.randn(N, C, 2 * d + 1, generator=gen).to(dev) for d in lv}
+            src = torch.randint(0, N, (E,), generator=gen).to(dev)
+            dst = torch.randint(0, N, (E,), generator=gen).to(dev)
+            rel = (torch.randn(E, 3, generator=gen) * 3.0).to(dev)
+
+            class G:
+                def edges(self):
+                    return src, dst
+
+                def num_nodes(self):
+                    return N
+
+            graph = G()
+            basis_mod = fe.WignerDBasis([fe.Repr(lv)]).to(dev)
+
+            def step():
+                with torch.no_grad():
+                    dist = rel.norm(dim=-1)
+                    (M,) = basis_mod(rel / dist[:, None])
+                    return mod(node, {}, graph, {"_P": M, "_Q": M, "_distances": dist})
+
+            for _ in range(max(3, args.warmup)):
+                step()
+            torch.cuda.synchronize()
+            t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            t0.record()
+            for _ in range(args.steps):
+                step()
+            t1.record()
+            torch.cuda.synchronize()
+            ms = t0.elapsed_time(t1) / args.steps
+            se3t, patched = PUBLISHED_PATCH_MS[(L, E)]
+            rows.append({"L": L, "edges": E, "ms": ms, "edges_per_s": E / (ms / 1e3),
+                         "published_h100_patched_ms": patched, "published_h100_se3t_ms": se3t})
+    if rank == 0:
+        last = rows[-1]
+        print(json.dumps({
+            "metric": "edges/sec (PatchedConvSE3 fwd, L=3, 65K edges)", "value": last["edges_per_s"],
+            "unit": "edges/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": last["ms"], "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16" if args.mix == "bf16" else "f32", "data": "synthetic",
+            "config": {"workload": "patch: one PatchedConvSE3 forward (FULL fuse, C=32, 500 bins, sh_scale 0, "
+                                   "edge->node sum) on a random graph of E/16 nodes, synthetic table; step includes "
+                                   "the WignerDBasis of the edge directions"},
+            "table": rows, "mix": args.mix,
+            "note": "published numbers: the reference on an NVIDIA H100 (README), context only"}), flush=True)
     if pg is not None:
         pg.destroy_process_group()
     return 0
@@ -1315,12 +1458,15 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-config5", action="store_true",
+                    help="at N > 1, skip the config-5 (partitioned giant graph) record of the default run")
     ap.add_argument("--nodes", type=int, default=N_NODES,
                     help="graph size (default: the config-2 size); smaller values only for profiling captures")
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--e2e-chunks", type=int, default=8,
                     help="edge chunks per end-to-end step (output copy of one overlaps compute of the next)")
-    ap.add_argument("--workload", choices=["config2", "block", "model", "train", "giant"], default="config2",
+    ap.add_argument("--workload", choices=["config2", "block", "model", "train", "giant", "patch"],
+                    default="config2",
                     help="config2: the metric (default); block: BASELINE config 3 (transformer block "
                          "forward); model: BASELINE config 4 (6-layer transformer forward on 4096 graphs); "
                          "train: the reference's published single-layer fwd+bwd+Adam step "
@@ -1343,6 +1489,8 @@ def main():
         return run_block(args)
     if args.workload == "model":
         return run_model(args)
+    if args.workload == "patch":
+        return run_patch(args)
     if args.workload == "giant":
         return run_giant(args)
     if args.impl == "reference":

@@ -22,7 +22,8 @@ from .layers import (
     SeparableS2Activation,
     SequencePositionEncoding,
 )
-from .layers._not_in_build import S2Grid, lebedev_grid, patch, real_spherical_harmonics
+from .layers._not_in_build import S2Grid, lebedev_grid, real_spherical_harmonics
+from .patch import patch
 from .layers.radial import RadialBasisFunctions, RadialMLP, SeparableRadialNet
 from .representations import Irrep, ProductIrrep, ProductRepr, Repr, WignerD, WignerDBasis, random_rotation
 

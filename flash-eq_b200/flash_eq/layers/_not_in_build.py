@@ -1,8 +1,8 @@
 """Names of the reference package that are outside the edge-message path.
 
 They import (so ``from flash_eq import ...`` keeps working) but raise on use:
-the S^2 / Lebedev activation (needs sphericart), the sequence-distance edge
-encoding and the NVIDIA SE(3)-Transformer patcher are not part of this build.
+the S^2 / Lebedev activation (needs sphericart) and the sequence-distance edge
+encoding are not part of this build.
 """
 from __future__ import annotations
 
@@ -35,6 +35,3 @@ def real_spherical_harmonics(*args, **kwargs):
 def lebedev_grid(*args, **kwargs):
     raise NotImplementedError("lebedev_grid is not part of flash-eq B200.")
 
-
-def patch(*args, **kwargs):
-    raise NotImplementedError("flash_eq.patch (NVIDIA SE(3)-Transformer conversion) is not part of flash-eq B200.")

@@ -112,6 +112,12 @@ class PartitionedGraph(Graph):
         return torch.cat([owned, halo])
 
 
+# Exchange timing (no counterpart in the reference): when set to a list, every exchange
+# appends a (start, end) pair of CUDA events recorded on the current stream around its
+# collective; benchmarks read the elapsed times after synchronising.
+EXCHANGE_EVENTS: list | None = None
+
+
 def _exchange(send: torch.Tensor, send_counts, recv_counts, group) -> torch.Tensor:
     """Rows send[...] split by ``send_counts`` go to ranks 0..W-1; returns the rows received,
     split by ``recv_counts`` in rank order.  One ``all_to_all_single`` on every backend (NCCL
@@ -120,8 +126,15 @@ def _exchange(send: torch.Tensor, send_counts, recv_counts, group) -> torch.Tens
     import torch.distributed as dist
 
     recv = send.new_empty((int(sum(recv_counts)),) + tuple(send.shape[1:]))
+    ev = None
+    if EXCHANGE_EVENTS is not None and send.is_cuda:
+        ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+        ev[0].record()
     dist.all_to_all_single(recv, send.contiguous(), output_split_sizes=list(recv_counts),
                            input_split_sizes=list(send_counts), group=group)
+    if ev is not None:
+        ev[1].record()
+        EXCHANGE_EVENTS.append(ev)
     return recv
 
 
