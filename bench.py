@@ -251,9 +251,9 @@ def parity_vs_oracle(y_rows, f_rows, vec_rows, dist_rows, table, lvals, sh_scale
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import feq_oracle as orc
 
-    P = orc.wigner_basis(vec_rows.double(), lvals)
-    ref = orc.edgewise_fwd(P, P, f_rows.double(), dist_rows.double(), table.double().cpu(), lvals, lvals,
-                           sh_scale, p1, p2, num_bins, False)
+    P = orc.wigner_basis(vec_rows.double().cpu(), lvals)
+    ref = orc.edgewise_fwd(P, P, f_rows.double().cpu(), dist_rows.double().cpu(), table.double().cpu(), lvals,
+                           lvals, sh_scale, p1, p2, num_bins, False)
     return float((y_rows.double().cpu() - ref).norm() / ref.norm())
 
 

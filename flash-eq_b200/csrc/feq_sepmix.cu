@@ -22,15 +22,18 @@
 // epilogue, straight from TMEM, followed by the rotation back (s^l_out folded in) and one
 // bulk store per output row.
 //
-// Roles (288 threads, persistent, one CTA per SM, one edge tile after another):
+// Roles (320 threads, persistent, one CTA per SM, one edge tile after another):
 //   warp 0      TMEM allocator; one thread issues tcgen05.mma
-//   warps 1..4  rotation in: bulk-copy x[src[e]] into shared memory, rotate two channels per
-//               lane with the factored Wigner blocks, write bf16 (hi, and lo in bf16x3 mode)
-//               into the K-major 128-byte-swizzled N-side tile; per edge also the trig of
-//               the rotations, s = d / (d + sh_scale) and the lerped g_k for the epilogue
-//   warps 5..8  epilogue: tcgen05.ld of Z, position mix, sum over k across lane pairs,
+//   warp 1      loader: lane per edge, up to 32 edges ahead of the rotation warps: the
+//               edge's scalars (bin, t, s = d / (d + sh_scale), the trig of the rotations)
+//               and a bulk copy of its input row x[src[e]] into a ring of row buffers, so
+//               that enough bytes are in flight to cover the HBM latency
+//   warps 2..5  rotation in: rotate two channels per lane with the factored Wigner blocks,
+//               write bf16 (hi, and lo in bf16x3 mode) into the K-major 128-byte-swizzled
+//               N-side tile; per edge also the lerped g_k for the epilogue
+//   warps 6..9  epilogue: tcgen05.ld of Z, position mix, sum over k across lane pairs,
 //               rotation back, bulk store
-// Rings: 2 N-side tiles, 2 TMEM accumulator sets, 4 per-tile edge-scalar slots.  Every
+// Rings: input rows, 2 N-side tiles, 2 TMEM accumulator sets, 4 per-tile slots.  Every
 // wait is bounded (limit from the launch); on time-out the kernel sets status 2, drains
 // its copies and MMAs, frees TMEM and returns.  No TMA multicast anywhere.
 //
@@ -50,9 +53,11 @@ namespace sep {
 using namespace sm100;
 using namespace rot;
 
-constexpr int kThreads = 288;
-constexpr int kRotWarp0 = 1, kNumRot = 4;
-constexpr int kEpiWarp0 = 5, kNumEpi = 4;
+constexpr int kThreads = 320;
+constexpr int kLoadWarp = 1;
+constexpr int kRotWarp0 = 2, kNumRot = 4;
+constexpr int kEpiWarp0 = 6, kNumEpi = 4;
+constexpr int kMaxRing = 32;    // input rows in flight per CTA (bulk copies), at most
 constexpr int kStages = 2;      // N-side tiles
 constexpr int kSlots = 4;       // per-tile edge scalars
 constexpr int kBufs = 2;        // TMEM accumulator sets
@@ -117,6 +122,10 @@ struct Geo {
     static constexpr int SLOT_G = SLOT_S + 4;
     static constexpr int SLOT_EDGE = SLOT_G + kRank * GP;     // floats per edge
     static constexpr int STAGE_ROW = ((kCout * DOUT + 15) / 32) * 32 + 16;   // == 16 mod 32 floats
+    // per-job scalars written by the loader: trig, s, t, bin (int), row flag (int)
+    static constexpr int JOB_TRIG = 0;
+    static constexpr int JOB_S = TF, JOB_T = TF + 1, JOB_LO = TF + 2, JOB_FLAG = TF + 3;
+    static constexpr int JOB_FLOATS = pad4(TF + 4);
 };
 
 struct SepParams {
@@ -135,6 +144,7 @@ struct SepParams {
     Binning bins;
     float sh_scale;
     uint64_t wait_ns;
+    int nr;                   // input-row ring size (<= kMaxRing)
 };
 
 // Byte offset of element (row r, column c) in a 128-row K-major tile of 64 bf16 per row with
@@ -301,6 +311,7 @@ __global__ void __launch_bounds__(kThreads, 1) sep_edgewise_kernel(const __grid_
     constexpr int OUTF = kCout * DOUT;                     // output row floats
     constexpr uint32_t kIdesc = idesc_bf16_f32(128, 128);
     constexpr int kSplitN = kSplit ? 2 : 1;
+    constexpr int JS = GE::JOB_FLOATS;
     static_assert(TE % kNumRot == 0 && TE % kG == 0, "tile edges split over the warps");
 
     extern __shared__ uint8_t smem_raw[];
@@ -308,16 +319,19 @@ __global__ void __launch_bounds__(kThreads, 1) sep_edgewise_kernel(const __grid_
     uint8_t *a_hi = smem;                                            // kSlices tiles
     uint8_t *a_lo = a_hi + kSlices * kTileBytes;                      // (split only)
     uint8_t *b_base = a_hi + kSplitN * kSlices * kTileBytes;          // kStages x (hi [, lo])
-    float *xrows = reinterpret_cast<float *>(b_base + kStages * kSplitN * kTileBytes);
-    float *slots = xrows + kNumRot * 2 * ROWF_PAD;
+    float *slots = reinterpret_cast<float *>(b_base + kStages * kSplitN * kTileBytes);
     float *stage = slots + kSlots * TE * GE::SLOT_EDGE;
+    float *jobs = stage + kG * GE::STAGE_ROW;                         // nr x JS per-edge scalars
+    float *rows = jobs + (size_t)P.nr * JS;                           // nr input rows
 
     __shared__ uint64_t b_full[kStages], b_empty[kStages], t_full[kBufs], t_empty[kBufs], s_empty[kSlots];
-    __shared__ uint64_t x_bar[kNumRot][2], drain_bar;
+    __shared__ uint64_t r_full[kMaxRing], r_free[kMaxRing], drain_bar;
+    __shared__ int64_t r_issued[kMaxRing];
     __shared__ uint32_t tmem_base_s;
     __shared__ int abort_s, epi_stop_s;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int NR = P.nr;
     if (threadIdx.x == 0) {
         epi_stop_s = 0;
         for (int i = 0; i < kStages; i++) {
@@ -329,9 +343,10 @@ __global__ void __launch_bounds__(kThreads, 1) sep_edgewise_kernel(const __grid_
             mbar_init(&t_empty[i], kNumEpi);
         }
         for (int i = 0; i < kSlots; i++) mbar_init(&s_empty[i], kNumEpi);
-        for (int i = 0; i < kNumRot; i++) {
-            mbar_init(&x_bar[i][0], 1);
-            mbar_init(&x_bar[i][1], 1);
+        for (int i = 0; i < kMaxRing; i++) {
+            mbar_init(&r_full[i], 1);
+            mbar_init(&r_free[i], 1);
+            r_issued[i] = -1;
         }
         mbar_init(&drain_bar, 1);
         abort_s = 0;
@@ -364,6 +379,10 @@ __global__ void __launch_bounds__(kThreads, 1) sep_edgewise_kernel(const __grid_
     const uint32_t tmem = tmem_base_s;
     volatile int *abort_flag = &abort_s;
     const int64_t n_local = P.num_tiles > blockIdx.x ? (P.num_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    const int64_t n_jobs = n_local * TE;     // job j = edge j % TE of this CTA's tile j / TE
+    auto edge_of_job = [&](int64_t j) -> int64_t {
+        return (blockIdx.x + (j / TE) * gridDim.x) * TE + (j % TE);
+    };
 
     if (warp == 0) {
         if (lane == 0) {
@@ -396,82 +415,93 @@ __global__ void __launch_bounds__(kThreads, 1) sep_edgewise_kernel(const __grid_
             umma_commit(&drain_bar);
             mbar_wait_drain(&drain_bar, 0);
         }
+    } else if (warp == kLoadWarp) {
+        // ---------------- loader: edge scalars + input rows, lane per edge ----------------
+        const int NB = NR < 32 ? NR : 32;
+        for (int64_t base = 0; base < n_jobs; base += NB) {
+            const int64_t j = base + lane;
+            bool ok = true;
+            if (lane < NB && j < n_jobs) {
+                const int r = (int)(j % NR);
+                if (j >= NR) ok = mbar_wait(&r_free[r], (uint32_t)((j / NR - 1) & 1), abort_flag, P.wait_ns);
+                if (ok) {
+                    float *sc = jobs + (size_t)r * JS;
+                    int *sci = reinterpret_cast<int *>(sc);
+                    const int64_t e = edge_of_job(j);
+                    int flag = 2;                         // 0 row copied, 1 bad src (zero row), 2 no edge
+                    int64_t row = -1;
+                    if (e < P.E) {
+                        const float dd = P.dist[e];
+                        int lo;
+                        float t;
+                        bin_of(dd, P.bins, lo, t);
+                        float tr[GE::TF];
+                        edge_trig_compact(P.dirs[e * 3], P.dirs[e * 3 + 1], P.dirs[e * 3 + 2], GE::LMAX, tr);
+#pragma unroll
+                        for (int q = 0; q < GE::TF; q++) sc[GE::JOB_TRIG + q] = tr[q];
+                        sc[GE::JOB_S] = dd / (dd + P.sh_scale);
+                        sc[GE::JOB_T] = t;
+                        sci[GE::JOB_LO] = lo;
+                        row = P.src ? P.src[e] : e;
+                        if (row < 0 || row >= P.nsrc) {
+                            set_status(P.status, 1);
+                            flag = 1;
+                        } else {
+                            flag = 0;
+                        }
+                    }
+                    sci[GE::JOB_FLAG] = flag;
+                    r_issued[r] = j;
+                    if (flag == 0) {
+                        fence_async_smem();
+                        mbar_arrive_expect_tx(&r_full[r], ROWF * 4);
+                        bulk_load(rows + (size_t)r * ROWF_PAD, P.x + row * (int64_t)ROWF, ROWF * 4, &r_full[r]);
+                    } else {
+                        mbar_arrive(&r_full[r]);
+                    }
+                }
+            }
+            if (__any_sync(0xffffffffu, !ok)) break;
+        }
+        __syncwarp();
+        // drain: every copy issued must have landed before the CTA exits
+        if (lane == 0)
+            for (int r = 0; r < NR; r++)
+                if (r_issued[r] >= 0) mbar_wait_drain(&r_full[r], (uint32_t)((r_issued[r] / NR) & 1));
     } else if (warp < kEpiWarp0) {
         // ---------------- rotation in ----------------
         const int w = warp - kRotWarp0;
         constexpr int EPW = TE / kNumRot;                  // edges of one tile per rotation warp
-        const int64_t n_jobs = n_local * EPW;
-        float *xb = xrows + (size_t)w * 2 * ROWF_PAD;
-        uint32_t xphase = 0;
-        int pending = 0;
-        auto edge_of = [&](int64_t j, int &el) -> int64_t {
-            const int64_t i = j / EPW;
-            el = w + kNumRot * (int)(j - i * EPW);
-            return (blockIdx.x + i * gridDim.x) * TE + el;
-        };
-        // row of x feeding job j, -1 when none (past the end, or a bad src index)
-        auto src_row = [&](int64_t e) -> int64_t {
-            if (e >= P.E) return -1;
-            if (!P.src) return e;
-            const int64_t r = P.src[e];
-            if (r < 0 || r >= P.nsrc) {
-                if (lane == 0) set_status(P.status, 1);
-                return -2;
-            }
-            return r;
-        };
-        auto issue = [&](int64_t j) {
-            int el;
-            const int64_t e = edge_of(j, el);
-            const int64_t r = src_row(e);
-            const int b = (int)(j & 1);
-            if (r >= 0) {
-                if (lane == 0) {
-                    fence_async_smem();
-                    mbar_arrive_expect_tx(&x_bar[w][b], ROWF * 4);
-                    bulk_load(xb + b * ROWF_PAD, P.x + r * (int64_t)ROWF, ROWF * 4, &x_bar[w][b]);
-                }
-                pending |= 1 << b;
-            }
-            return r;
-        };
-        int64_t r_next = n_jobs > 0 ? issue(0) : -1;
-        bool alive = true;
-        for (int64_t j = 0; j < n_jobs && alive; j++) {
-            const int64_t i = j / EPW;
+        const int64_t n_mine = n_local * EPW;
+        for (int64_t q = 0; q < n_mine; q++) {
+            const int64_t i = q / EPW;
             const int st = (int)(i % kStages), slot = (int)(i % kSlots);
-            int el;
-            const int64_t e = edge_of(j, el);
-            const int64_t r_cur = r_next;
-            const int b = (int)(j & 1);
-            if (j + 1 < n_jobs) r_next = issue(j + 1);
-            if (j % EPW == 0) {       // first edge of this warp in tile i: wait for its buffers
+            const int el = w + kNumRot * (int)(q - i * EPW);
+            const int64_t j = i * TE + el;
+            const int r = (int)(j % NR);
+            if (q % EPW == 0) {       // first edge of this warp in tile i: wait for its buffers
                 if (i >= kStages &&
-                    !mbar_wait(&b_empty[st], (uint32_t)((i / kStages - 1) & 1), abort_flag, P.wait_ns)) {
-                    alive = false;
+                    !mbar_wait(&b_empty[st], (uint32_t)((i / kStages - 1) & 1), abort_flag, P.wait_ns))
                     break;
-                }
-                if (i >= kSlots &&
-                    !mbar_wait(&s_empty[slot], (uint32_t)((i / kSlots - 1) & 1), abort_flag, P.wait_ns)) {
-                    alive = false;
+                if (i >= kSlots && !mbar_wait(&s_empty[slot], (uint32_t)((i / kSlots - 1) & 1), abort_flag, P.wait_ns))
                     break;
-                }
             }
-            if (e < P.E) {
+            if (!mbar_wait(&r_full[r], (uint32_t)((j / NR) & 1), abort_flag, P.wait_ns)) {
+                set_status(P.status, 2);
+                break;
+            }
+            const float *sc = jobs + (size_t)r * JS;
+            const int flag = reinterpret_cast<const int *>(sc)[GE::JOB_FLAG];
+            if (flag != 2) {
+                const int64_t e = edge_of_job(j);
                 float *sl = slots + (size_t)(slot * TE + el) * GE::SLOT_EDGE;
-                // per-edge scalars (every lane computes them; lane 0 stores the trig)
-                const float dd = P.dist[e];
-                const float s = dd / (dd + P.sh_scale);
-                int lo;
-                float t;
-                bin_of(dd, P.bins, lo, t);
                 float tr[GE::TF];
-                edge_trig_compact(P.dirs[e * 3], P.dirs[e * 3 + 1], P.dirs[e * 3 + 2], GE::LMAX, tr);
-                if (lane == 0) {
 #pragma unroll
-                    for (int q = 0; q < GE::TF; q++) sl[GE::SLOT_TRIG + q] = tr[q];
-                    sl[GE::SLOT_S] = s;
-                }
+                for (int qq = 0; qq < GE::TF; qq++) tr[qq] = sc[GE::JOB_TRIG + qq];
+                const float s = sc[GE::JOB_S], t = sc[GE::JOB_T];
+                const int lo = reinterpret_cast<const int *>(sc)[GE::JOB_LO];
+                if (lane < GE::TF) sl[GE::SLOT_TRIG + lane] = sc[GE::JOB_TRIG + lane];
+                if (lane == 0) sl[GE::SLOT_S] = s;
                 // g_k = (1 - t) f[lo, k] + t f[lo + 1, k], per block padded to 4 floats
                 {
                     const float *f_lo = P.ftab + (int64_t)lo * kRank * GE::W, *f_hi = f_lo + kRank * GE::W;
@@ -480,14 +510,14 @@ __global__ void __launch_bounds__(kThreads, 1) sep_edgewise_kernel(const __grid_
                         const int k = idx / GE::GP, p = idx - k * GE::GP;
                         int m = 0;
 #pragma unroll
-                        for (int q = 1; q <= GE::MB; q++) m += p >= GE::goff(q) ? 1 : 0;
+                        for (int qq = 1; qq <= GE::MB; qq++) m += p >= GE::goff(qq) ? 1 : 0;
                         int goff_m = 0, gsize_m = 0, woff_m = 0;
 #pragma unroll
-                        for (int q = 0; q <= GE::MB; q++)
-                            if (q == m) {
-                                goff_m = GE::goff(q);
-                                gsize_m = GE::gsize(q);
-                                woff_m = GE::w_off(q);
+                        for (int qq = 0; qq <= GE::MB; qq++)
+                            if (qq == m) {
+                                goff_m = GE::goff(qq);
+                                gsize_m = GE::gsize(qq);
+                                woff_m = GE::w_off(qq);
                             }
                         const int loc = p - goff_m;
                         float v = 0.0f;
@@ -498,30 +528,20 @@ __global__ void __launch_bounds__(kThreads, 1) sep_edgewise_kernel(const __grid_
                         sl[GE::SLOT_G + idx] = v;
                     }
                 }
-                // the input row: bulk copy in flight since the previous edge
-                float *fb = xb + b * ROWF_PAD;
-                if (r_cur >= 0) {
-                    if (!mbar_wait(&x_bar[w][b], (xphase >> b) & 1u, abort_flag, P.wait_ns)) {
-                        set_status(P.status, 2);
-                        alive = false;
-                        break;
-                    }
-                    xphase ^= 1u << b;
-                    pending &= ~(1 << b);
-                } else {
-                    for (int q = lane; q < ROWF; q += 32) fb[q] = 0.0f;
-                }
+                float *fb = rows + (size_t)r * ROWF_PAD;
+                if (flag == 1)
+                    for (int qq = lane; qq < ROWF; qq += 32) fb[qq] = 0.0f;
                 if (P.edge_add) {
                     const float4 *ea = reinterpret_cast<const float4 *>(P.edge_add + e * (int64_t)ROWF);
                     float4 *f4 = reinterpret_cast<float4 *>(fb);
-                    for (int q = lane; q < ROWF / 4; q += 32) {
-                        const float4 a = __ldg(ea + q);
-                        float4 v = f4[q];
+                    for (int qq = lane; qq < ROWF / 4; qq += 32) {
+                        const float4 a = __ldg(ea + qq);
+                        float4 v = f4[qq];
                         v.x += a.x;
                         v.y += a.y;
                         v.z += a.z;
                         v.w += a.w;
-                        f4[q] = v;
+                        f4[qq] = v;
                     }
                 }
                 __syncwarp();
@@ -531,14 +551,13 @@ __global__ void __launch_bounds__(kThreads, 1) sep_edgewise_kernel(const __grid_
                                              el * ES, c);
             }
             __syncwarp();
-            if (j % EPW == EPW - 1) {     // this warp's part of tile i is in shared memory
+            if (lane == 0) mbar_arrive(&r_free[r]);       // the row buffer may be refilled
+            if (q % EPW == EPW - 1) {     // this warp's part of tile i is in shared memory
                 fence_async_smem();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&b_full[st]);
             }
         }
-        for (int b = 0; b < 2; b++)
-            if (pending & (1 << b)) mbar_wait_drain(&x_bar[w][b], (xphase >> b) & 1u);
     } else {
         // ---------------- epilogue ----------------
         const int q4 = warp & 3;                       // TMEM lane quadrant of this warp
@@ -556,6 +575,7 @@ __global__ void __launch_bounds__(kThreads, 1) sep_edgewise_kernel(const __grid_
             tc_fence_after();
             const int64_t e0 = (blockIdx.x + i * gridDim.x) * TE;
             const float *slot_base = slots + (size_t)slot * TE * GE::SLOT_EDGE;
+            const uint32_t tbase = tmem + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(buf * kSlices * 128);
 #pragma unroll 1
             for (int gi = 0; gi < TE / kG; gi++) {
                 float h[kG][DOUT];
@@ -567,14 +587,12 @@ __global__ void __launch_bounds__(kThreads, 1) sep_edgewise_kernel(const __grid_
                 for (int ee = 0; ee < kG; ee++) {
                     const int el = gi * kG + ee;
                     const float *G = slot_base + el * GE::SLOT_EDGE + GE::SLOT_G;
+                    uint32_t Z[kSlices][ES];
 #pragma unroll
-                    for (int s = 0; s < kSlices; s++) {
-                        uint32_t Z[ES];
-                        tmem_ld<ES>(tmem + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(buf * kSlices * 128 + s * 128 + el * ES),
-                                    Z);
-                        tmem_wait_ld();
-                        pos_mix<GE, 0, ES>(Z, G + (s * kG + kk) * GE::GP, h[ee]);
-                    }
+                    for (int s = 0; s < kSlices; s++) tmem_ld<ES>(tbase + (uint32_t)(s * 128 + el * ES), Z[s]);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int s = 0; s < kSlices; s++) pos_mix<GE, 0, ES>(Z[s], G + (s * kG + kk) * GE::GP, h[ee]);
                 }
                 // sum over k across the lane pair; lane kk keeps edge gi * kG + kk
                 float hf[DOUT];
@@ -621,23 +639,34 @@ __global__ void __launch_bounds__(kThreads, 1) sep_edgewise_kernel(const __grid_
     if (threadIdx.x == 0 && abort_s) set_status(P.status, 2);
 }
 
+// Shared memory without the input-row ring, and the bytes of one ring entry (row + scalars).
 template <int LIN, int LOUT, bool kSplit>
-size_t smem_bytes() {
+size_t smem_fixed_bytes() {
     using GE = Geo<LIN, LOUT>;
     constexpr int kSplitN = kSplit ? 2 : 1;
     size_t b = 1024;                                                     // alignment slack
     b += (size_t)kSplitN * kSlices * kTileBytes;                         // M side
     b += (size_t)kStages * kSplitN * kTileBytes;                         // N side
-    b += (size_t)kNumRot * 2 * ((kCin * GE::DIN + 3) & ~3) * 4;          // input rows
-    b += (size_t)kSlots * GE::TE * GE::SLOT_EDGE * 4;                    // edge scalars
+    b += (size_t)kSlots * GE::TE * GE::SLOT_EDGE * 4;                    // per-tile slots
     b += (size_t)kG * GE::STAGE_ROW * 4;                                 // output staging
     return b;
 }
+template <int LIN, int LOUT>
+size_t ring_entry_bytes() {
+    using GE = Geo<LIN, LOUT>;
+    return ((size_t)((kCin * GE::DIN + 3) & ~3) + GE::JOB_FLOATS) * 4;
+}
+
+constexpr size_t kSmemCap = 227 * 1024;
 
 template <int LIN, int LOUT, bool kSplit>
-int launch(const SepParams &P, cudaStream_t stream) {
+int launch(SepParams P, cudaStream_t stream) {
     auto kern = sep_edgewise_kernel<LIN, LOUT, kSplit>;
-    size_t smem = smem_bytes<LIN, LOUT, kSplit>();
+    const size_t fixed = smem_fixed_bytes<LIN, LOUT, kSplit>(), entry = ring_entry_bytes<LIN, LOUT>();
+    if (fixed + 4 * entry > kSmemCap) return FEQ_ERR_UNSUPPORTED;
+    int nr = (int)((kSmemCap - fixed) / entry);
+    P.nr = nr < kMaxRing ? nr : kMaxRing;
+    size_t smem = fixed + (size_t)P.nr * entry;
     // more than half of the SM's shared memory: one CTA per SM, so one TMEM allocation
     if (smem < 120 * 1024) smem = 120 * 1024;
     FEQ_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
@@ -658,11 +687,6 @@ int dispatch(int lin, int lout, const SepParams &P, cudaStream_t s) {
     if (lin == 3 && lout == 3) return launch<3, 3, kSplit>(P, s);
     if (lin == 4 && lout == 4) return launch<4, 4, kSplit>(P, s);
     return FEQ_ERR_UNSUPPORTED;
-}
-
-template <int LIN, int LOUT>
-int tiles_of(int64_t E) {
-    return (int)((E + Geo<LIN, LOUT>::TE - 1) / Geo<LIN, LOUT>::TE);
 }
 
 // lvals == [0, 1, ..., L]?  Returns L, or -1.

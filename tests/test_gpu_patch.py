@@ -17,6 +17,7 @@ import flash_eq as fe
 from conftest import rel_l2
 from flash_eq.patch import PatchedConvSE3
 
+
 class _FakeGraph:
     def __init__(self, src, dst, n):
         self._s, self._d, self._n = src, dst, n
