@@ -116,16 +116,29 @@ struct Geo {
     __host__ __device__ static constexpr int mf_out(int l, int m) {
         return m == 0 ? l : out_off(m < 0 ? -m : m) + 2 * (l - (m < 0 ? -m : m)) + (m < 0 ? 1 : 0);
     }
-    // per-edge scalar slot: trig (padded), s (padded to 4), g for every k
-    static constexpr int SLOT_TRIG = 0;
-    static constexpr int SLOT_S = pad4(TF);
-    static constexpr int SLOT_G = SLOT_S + 4;
+    // the nonzeros of the factored Wigner block M_l (s^l folded in) of every degree 1..LMAX,
+    // each degree's run padded to 4 floats
+    __host__ __device__ static constexpr int mnnz(int l) {
+        return l == 1 ? FEQ_WM_NNZ_1 : l == 2 ? FEQ_WM_NNZ_2 : l == 3 ? FEQ_WM_NNZ_3 : l == 4 ? FEQ_WM_NNZ_4 : 0;
+    }
+    __host__ __device__ static constexpr int moff(int l) {
+        int o = 0;
+        for (int q = 1; q < l; q++) o += pad4(mnnz(q));
+        return o;
+    }
+    static constexpr int MF = moff(LMAX + 1);
+    // per-edge record shared by the loader (writes), the rotation warps and the epilogue:
+    // trig (cos / sin of the polar multiples and of m phi), s, t, bin (int), row flag (int),
+    // then the M_l nonzeros
+    static constexpr int REC_TRIG = 0;
+    static constexpr int REC_S = TF, REC_T = TF + 1, REC_LO = TF + 2, REC_FLAG = TF + 3;
+    static constexpr int REC_M = pad4(TF + 4);
+    static constexpr int REC_FLOATS = REC_M + MF;
+    // per-tile slot of one edge for the epilogue: the record, then g for every k
+    static constexpr int SLOT_G = REC_FLOATS;
     static constexpr int SLOT_EDGE = SLOT_G + kRank * GP;     // floats per edge
     static constexpr int STAGE_ROW = ((kCout * DOUT + 15) / 32) * 32 + 16;   // == 16 mod 32 floats
-    // per-job scalars written by the loader: trig, s, t, bin (int), row flag (int)
-    static constexpr int JOB_TRIG = 0;
-    static constexpr int JOB_S = TF, JOB_T = TF + 1, JOB_LO = TF + 2, JOB_FLAG = TF + 3;
-    static constexpr int JOB_FLOATS = pad4(TF + 4);
+    static constexpr int JOB_FLOATS = REC_FLOATS;
 };
 
 struct SepParams {
@@ -220,6 +233,120 @@ __device__ __forceinline__ void rot_irrep2c(const float *__restrict__ tr, int lm
     }
 }
 
+template <int NZ>
+__device__ __forceinline__ void load_m(const float *__restrict__ src, float (&m)[NZ]) {
+    const float4 *s4 = reinterpret_cast<const float4 *>(src);
+#pragma unroll
+    for (int v = 0; v < NZ / 4; v++) {
+        const float4 t = s4[v];
+        m[4 * v] = t.x;
+        m[4 * v + 1] = t.y;
+        m[4 * v + 2] = t.z;
+        m[4 * v + 3] = t.w;
+    }
+#pragma unroll
+    for (int v = (NZ / 4) * 4; v < NZ; v++) m[v] = src[v];
+}
+
+// One irrep of degree Lg through D = R(phi) M R(phi)^T with the nonzeros of M (s^l folded
+// in) read from msm; cp / sp: cos / sin of m phi.  Two channels (emit(o, y0, y1)).
+template <int Lg, bool kT, typename Get, typename Emit>
+__device__ __forceinline__ void rot2_pre(const float *__restrict__ msm, const float *__restrict__ cp,
+                                         const float *__restrict__ sp, Get get, Emit emit) {
+    if constexpr (Lg == 0) {
+        const float2 v = get(0);
+        emit(0, v.x, v.y);
+    } else {
+        constexpr int N = 2 * Lg + 1;
+        float m[WA<Lg>::kNnz];
+        load_m(msm, m);
+        float g0[N], g1[N];
+#pragma unroll
+        for (int q = 0; q < N; q++) {
+            const float2 v = get(q);
+            g0[q] = v.x;
+            g1[q] = v.y;
+        }
+#pragma unroll
+        for (int mm = 1; mm <= Lg; mm++) {
+            const int a = Lg - mm, b = Lg + mm;
+            const float c = cp[mm], sn = sp[mm];
+            float t0 = g0[a] * c - g0[b] * sn, t1 = g0[a] * sn + g0[b] * c;
+            g0[a] = t0;
+            g0[b] = t1;
+            t0 = g1[a] * c - g1[b] * sn;
+            t1 = g1[a] * sn + g1[b] * c;
+            g1[a] = t0;
+            g1[b] = t1;
+        }
+        float h0[N], h1[N];
+        WA<Lg>::template wa<kT>(m, g0, h0);
+        WA<Lg>::template wa<kT>(m, g1, h1);
+#pragma unroll
+        for (int mm = 1; mm <= Lg; mm++) {
+            const int a = Lg - mm, b = Lg + mm;
+            const float c = cp[mm], sn = sp[mm];
+            float t0 = h0[a] * c + h0[b] * sn, t1 = h0[b] * c - h0[a] * sn;
+            h0[a] = t0;
+            h0[b] = t1;
+            t0 = h1[a] * c + h1[b] * sn;
+            t1 = h1[b] * c - h1[a] * sn;
+            h1[a] = t0;
+            h1[b] = t1;
+        }
+#pragma unroll
+        for (int o = 0; o < N; o++) emit(o, h0[o], h1[o]);
+    }
+}
+
+// The same for one channel.
+template <int Lg, bool kT, typename Get, typename Emit>
+__device__ __forceinline__ void rot1_pre(const float *__restrict__ msm, const float *__restrict__ cp,
+                                         const float *__restrict__ sp, Get get, Emit emit) {
+    if constexpr (Lg == 0) {
+        emit(0, get(0));
+    } else {
+        constexpr int N = 2 * Lg + 1;
+        float m[WA<Lg>::kNnz];
+        load_m(msm, m);
+        float g[N];
+#pragma unroll
+        for (int q = 0; q < N; q++) g[q] = get(q);
+#pragma unroll
+        for (int mm = 1; mm <= Lg; mm++) {
+            const int a = Lg - mm, b = Lg + mm;
+            const float c = cp[mm], sn = sp[mm];
+            const float t0 = g[a] * c - g[b] * sn, t1 = g[a] * sn + g[b] * c;
+            g[a] = t0;
+            g[b] = t1;
+        }
+        float h[N];
+        WA<Lg>::template wa<kT>(m, g, h);
+#pragma unroll
+        for (int mm = 1; mm <= Lg; mm++) {
+            const int a = Lg - mm, b = Lg + mm;
+            const float c = cp[mm], sn = sp[mm];
+            const float t0 = h[a] * c + h[b] * sn, t1 = h[b] * c - h[a] * sn;
+            h[a] = t0;
+            h[b] = t1;
+        }
+#pragma unroll
+        for (int o = 0; o < N; o++) emit(o, h[o]);
+    }
+}
+
+// M_l nonzeros of every degree 1..LMAX of one edge (s^l folded in) into rec + REC_M.
+template <class GE, int L>
+__device__ __forceinline__ void fill_m(const float *__restrict__ tv, float s, float *__restrict__ rec) {
+    if constexpr (L <= GE::LMAX) {
+        float m[WA<L>::kNnz];
+        WA<L>::wm(tv, ipowf(s, L), m);
+#pragma unroll
+        for (int v = 0; v < WA<L>::kNnz; v++) rec[GE::REC_M + GE::moff(L) + v] = m[v];
+        fill_m<GE, L + 1>(tv, s, rec);
+    }
+}
+
 // h[q] += sum_j G[q, j] Z[j] for the blocks m = M..MB of one k (G in shared memory, padded
 // per block; Z this thread's TMEM row for one edge).  m = 0: out[o] += g[o n_in + i] z[i];
 // m > 0: 2x2 [[a, b], [-b, a]] on the (+m, -m) pairs (block_diagonal.cu:558-733).
@@ -266,9 +393,11 @@ __device__ __forceinline__ void pos_mix(const uint32_t (&Z)[ES], const float *__
     }
 }
 
-// Input rotation of one irrep degree L (recursing to LIN) for the channel pair (c, c + 1).
+// Input rotation of one irrep degree L (recursing to LIN) for the channel pair (c, c + 1);
+// rec: the edge's record (trig, M_l nonzeros).
 template <class GE, int L, bool kSplit>
-__device__ __forceinline__ void rotate_in_all(const float *__restrict__ tr, float s, const float *__restrict__ f0,
+__device__ __forceinline__ void rotate_in_all(const float *__restrict__ rec, const float *__restrict__ cp,
+                                              const float *__restrict__ sp, const float *__restrict__ f0,
                                               const float *__restrict__ f1, uint8_t *bhi, uint8_t *blo, int row0,
                                               int c) {
     if constexpr (L <= GE::LI) {
@@ -283,22 +412,23 @@ __device__ __forceinline__ void rotate_in_all(const float *__restrict__ tr, floa
                 *reinterpret_cast<__nv_bfloat162 *>(blo + swz(r, c)) = __floats2bfloat162_rn(y0 - hf.x, y1 - hf.y);
             }
         };
-        rot_irrep2c<L, false>(tr, GE::LMAX, ipowf(s, L), get, emit);
-        rotate_in_all<GE, L + 1, kSplit>(tr, s, f0, f1, bhi, blo, row0, c);
+        rot2_pre<L, false>(rec + GE::REC_M + GE::moff(L), cp, sp, get, emit);
+        rotate_in_all<GE, L + 1, kSplit>(rec, cp, sp, f0, f1, bhi, blo, row0, c);
     }
 }
 
 // Output rotation of every degree of [0..LOUT] for one channel of one edge, into the
 // staging row (standard order).
 template <class GE, int L>
-__device__ __forceinline__ void rotate_out_all(const float *__restrict__ tr, float s, const float (&h)[GE::DOUT],
+__device__ __forceinline__ void rotate_out_all(const float *__restrict__ rec, const float *__restrict__ cp,
+                                               const float *__restrict__ sp, const float (&h)[GE::DOUT],
                                                float *__restrict__ orow) {
     if constexpr (L <= GE::LO) {
         constexpr int off = L * L;
         auto get = [&](int q) { return h[GE::mf_out(L, q - L)]; };
         auto emit = [&](int o, float y) { orow[off + o] = y; };
-        rot_irrep1<L, true>(tr, GE::LMAX, ipowf(s, L), get, emit);
-        rotate_out_all<GE, L + 1>(tr, s, h, orow);
+        rot1_pre<L, true>(rec + GE::REC_M + GE::moff(L), cp, sp, get, emit);
+        rotate_out_all<GE, L + 1>(rec, cp, sp, h, orow);
     }
 }
 
@@ -327,6 +457,7 @@ __global__ void __launch_bounds__(kThreads, 1) sep_edgewise_kernel(const __grid_
     __shared__ uint64_t b_full[kStages], b_empty[kStages], t_full[kBufs], t_empty[kBufs], s_empty[kSlots];
     __shared__ uint64_t r_full[kMaxRing], r_free[kMaxRing], drain_bar;
     __shared__ int64_t r_issued[kMaxRing];
+    __shared__ int16_t gidx_s[kRank * GE::GP];     // g slot -> index into one bin row of f (-1: pad)
     __shared__ uint32_t tmem_base_s;
     __shared__ int abort_s, epi_stop_s;
 
@@ -372,6 +503,14 @@ __global__ void __launch_bounds__(kThreads, 1) sep_edgewise_kernel(const __grid_
     // are never written again.
     for (int i = threadIdx.x; i < (int)(kStages * kSplitN * kTileBytes / 16); i += kThreads)
         reinterpret_cast<uint4 *>(b_base)[i] = make_uint4(0u, 0u, 0u, 0u);
+    // g layout: per k, per m-block, the block's weights padded to 4 floats
+    for (int idx = threadIdx.x; idx < kRank * GE::GP; idx += kThreads) {
+        const int k = idx / GE::GP, p = idx - k * GE::GP;
+        int wi = -1;
+        for (int m = 0; m <= GE::MB; m++)
+            if (p >= GE::goff(m) && p - GE::goff(m) < GE::gsize(m)) wi = k * GE::W + GE::w_off(m) + (p - GE::goff(m));
+        gidx_s[idx] = (int16_t)wi;
+    }
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
@@ -438,10 +577,12 @@ __global__ void __launch_bounds__(kThreads, 1) sep_edgewise_kernel(const __grid_
                         float tr[GE::TF];
                         edge_trig_compact(P.dirs[e * 3], P.dirs[e * 3 + 1], P.dirs[e * 3 + 2], GE::LMAX, tr);
 #pragma unroll
-                        for (int q = 0; q < GE::TF; q++) sc[GE::JOB_TRIG + q] = tr[q];
-                        sc[GE::JOB_S] = dd / (dd + P.sh_scale);
-                        sc[GE::JOB_T] = t;
-                        sci[GE::JOB_LO] = lo;
+                        for (int q = 0; q < GE::TF; q++) sc[GE::REC_TRIG + q] = tr[q];
+                        const float sw = dd / (dd + P.sh_scale);
+                        sc[GE::REC_S] = sw;
+                        sc[GE::REC_T] = t;
+                        sci[GE::REC_LO] = lo;
+                        fill_m<GE, 1>(tr, sw, sc);
                         row = P.src ? P.src[e] : e;
                         if (row < 0 || row >= P.nsrc) {
                             set_status(P.status, 1);
@@ -450,7 +591,7 @@ __global__ void __launch_bounds__(kThreads, 1) sep_edgewise_kernel(const __grid_
                             flag = 0;
                         }
                     }
-                    sci[GE::JOB_FLAG] = flag;
+                    sci[GE::REC_FLAG] = flag;
                     r_issued[r] = j;
                     if (flag == 0) {
                         fence_async_smem();
@@ -491,41 +632,23 @@ __global__ void __launch_bounds__(kThreads, 1) sep_edgewise_kernel(const __grid_
                 break;
             }
             const float *sc = jobs + (size_t)r * JS;
-            const int flag = reinterpret_cast<const int *>(sc)[GE::JOB_FLAG];
+            const int flag = reinterpret_cast<const int *>(sc)[GE::REC_FLAG];
             if (flag != 2) {
                 const int64_t e = edge_of_job(j);
                 float *sl = slots + (size_t)(slot * TE + el) * GE::SLOT_EDGE;
                 float tr[GE::TF];
 #pragma unroll
-                for (int qq = 0; qq < GE::TF; qq++) tr[qq] = sc[GE::JOB_TRIG + qq];
-                const float s = sc[GE::JOB_S], t = sc[GE::JOB_T];
-                const int lo = reinterpret_cast<const int *>(sc)[GE::JOB_LO];
-                if (lane < GE::TF) sl[GE::SLOT_TRIG + lane] = sc[GE::JOB_TRIG + lane];
-                if (lane == 0) sl[GE::SLOT_S] = s;
+                for (int qq = 0; qq < GE::TF; qq++) tr[qq] = sc[GE::REC_TRIG + qq];
+                const float t = sc[GE::REC_T];
+                const int lo = reinterpret_cast<const int *>(sc)[GE::REC_LO];
+                for (int qq = lane; qq < GE::REC_FLOATS; qq += 32) sl[qq] = sc[qq];   // record for the epilogue
                 // g_k = (1 - t) f[lo, k] + t f[lo + 1, k], per block padded to 4 floats
                 {
                     const float *f_lo = P.ftab + (int64_t)lo * kRank * GE::W, *f_hi = f_lo + kRank * GE::W;
                     const float omt = 1.0f - t;
                     for (int idx = lane; idx < kRank * GE::GP; idx += 32) {
-                        const int k = idx / GE::GP, p = idx - k * GE::GP;
-                        int m = 0;
-#pragma unroll
-                        for (int qq = 1; qq <= GE::MB; qq++) m += p >= GE::goff(qq) ? 1 : 0;
-                        int goff_m = 0, gsize_m = 0, woff_m = 0;
-#pragma unroll
-                        for (int qq = 0; qq <= GE::MB; qq++)
-                            if (qq == m) {
-                                goff_m = GE::goff(qq);
-                                gsize_m = GE::gsize(qq);
-                                woff_m = GE::w_off(qq);
-                            }
-                        const int loc = p - goff_m;
-                        float v = 0.0f;
-                        if (loc < gsize_m) {
-                            const int wi = k * GE::W + woff_m + loc;
-                            v = omt * __ldg(f_lo + wi) + t * __ldg(f_hi + wi);
-                        }
-                        sl[GE::SLOT_G + idx] = v;
+                        const int wi = gidx_s[idx];
+                        sl[GE::SLOT_G + idx] = wi >= 0 ? omt * __ldg(f_lo + wi) + t * __ldg(f_hi + wi) : 0.0f;
                     }
                 }
                 float *fb = rows + (size_t)r * ROWF_PAD;
@@ -547,7 +670,8 @@ __global__ void __launch_bounds__(kThreads, 1) sep_edgewise_kernel(const __grid_
                 __syncwarp();
                 uint8_t *bh = b_base + st * kSplitN * kTileBytes;
                 const int c = 2 * lane;
-                rotate_in_all<GE, 0, kSplit>(tr, s, fb + c * DIN, fb + (c + 1) * DIN, bh, bh + kTileBytes,
+                const float *cp = tr + 2 * GE::LMAX + 1, *sp = cp + GE::LMAX + 1;
+                rotate_in_all<GE, 0, kSplit>(sc, cp, sp, fb + c * DIN, fb + (c + 1) * DIN, bh, bh + kTileBytes,
                                              el * ES, c);
             }
             __syncwarp();
@@ -578,39 +702,38 @@ __global__ void __launch_bounds__(kThreads, 1) sep_edgewise_kernel(const __grid_
             const uint32_t tbase = tmem + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(buf * kSlices * 128);
 #pragma unroll 1
             for (int gi = 0; gi < TE / kG; gi++) {
-                float h[kG][DOUT];
-#pragma unroll
-                for (int ee = 0; ee < kG; ee++)
-#pragma unroll
-                    for (int q = 0; q < DOUT; q++) h[ee][q] = 0.0f;
-#pragma unroll
+                // every lane of a pair computes its k's share of both edges of the group; the
+                // pair sums its shares, and lane kk keeps edge gi * kG + kk
+                float hf[DOUT];
+#pragma unroll 1
                 for (int ee = 0; ee < kG; ee++) {
                     const int el = gi * kG + ee;
                     const float *G = slot_base + el * GE::SLOT_EDGE + GE::SLOT_G;
-                    uint32_t Z[kSlices][ES];
+                    float h[DOUT];
 #pragma unroll
-                    for (int s = 0; s < kSlices; s++) tmem_ld<ES>(tbase + (uint32_t)(s * 128 + el * ES), Z[s]);
-                    tmem_wait_ld();
+                    for (int q = 0; q < DOUT; q++) h[q] = 0.0f;
+#pragma unroll 1
+                    for (int s = 0; s < kSlices; s++) {
+                        uint32_t Z[ES];
+                        tmem_ld<ES>(tbase + (uint32_t)(s * 128 + el * ES), Z);
+                        tmem_wait_ld();
+                        pos_mix<GE, 0, ES>(Z, G + (s * kG + kk) * GE::GP, h);
+                    }
 #pragma unroll
-                    for (int s = 0; s < kSlices; s++) pos_mix<GE, 0, ES>(Z[s], G + (s * kG + kk) * GE::GP, h[ee]);
-                }
-                // sum over k across the lane pair; lane kk keeps edge gi * kG + kk
-                float hf[DOUT];
-#pragma unroll
-                for (int q = 0; q < DOUT; q++) {
-                    const float send = kk == 0 ? h[1][q] : h[0][q];
-                    const float keep = kk == 0 ? h[0][q] : h[1][q];
-                    hf[q] = keep + __shfl_xor_sync(0xffffffffu, send, 1);
+                    for (int q = 0; q < DOUT; q++) {
+                        const float v = h[q] + __shfl_xor_sync(0xffffffffu, h[q], 1);
+                        if (kk == ee) hf[q] = v;
+                    }
                 }
                 const int el = gi * kG + kk;
                 const float *es = slot_base + el * GE::SLOT_EDGE;
                 float tr[GE::TF];
 #pragma unroll
-                for (int q = 0; q < GE::TF; q++) tr[q] = es[GE::SLOT_TRIG + q];
-                const float s = es[GE::SLOT_S];
+                for (int q = 0; q < GE::TF; q++) tr[q] = es[GE::REC_TRIG + q];
+                const float *cp = tr + 2 * GE::LMAX + 1, *sp = cp + GE::LMAX + 1;
                 if (leader) bulk_wait_read0();           // the previous group's rows have left
                 named_bar(1, kNumEpi * 32);
-                rotate_out_all<GE, 0>(tr, s, hf, stage + kk * GE::STAGE_ROW + co * DOUT);
+                rotate_out_all<GE, 0>(es, cp, sp, hf, stage + kk * GE::STAGE_ROW + co * DOUT);
                 fence_async_smem();
                 named_bar(1, kNumEpi * 32);
                 if (leader) {
