@@ -780,14 +780,17 @@ size_t ring_entry_bytes() {
     return ((size_t)((kCin * GE::DIN + 3) & ~3) + GE::JOB_FLOATS) * 4;
 }
 
-constexpr size_t kSmemCap = 227 * 1024;
+constexpr size_t kSmemPerBlock = 227 * 1024;     // dynamic + static shared memory of one CTA
 
 template <int LIN, int LOUT, bool kSplit>
 int launch(SepParams P, cudaStream_t stream) {
     auto kern = sep_edgewise_kernel<LIN, LOUT, kSplit>;
+    cudaFuncAttributes fa;
+    FEQ_CUDA_TRY(cudaFuncGetAttributes(&fa, kern));
+    const size_t cap = kSmemPerBlock - fa.sharedSizeBytes;
     const size_t fixed = smem_fixed_bytes<LIN, LOUT, kSplit>(), entry = ring_entry_bytes<LIN, LOUT>();
-    if (fixed + 4 * entry > kSmemCap) return FEQ_ERR_UNSUPPORTED;
-    int nr = (int)((kSmemCap - fixed) / entry);
+    if (fixed + 4 * entry > cap) return FEQ_ERR_UNSUPPORTED;
+    int nr = (int)((cap - fixed) / entry);
     P.nr = nr < kMaxRing ? nr : kMaxRing;
     size_t smem = fixed + (size_t)P.nr * entry;
     // more than half of the SM's shared memory: one CTA per SM, so one TMEM allocation
