@@ -53,10 +53,10 @@ namespace sep {
 using namespace sm100;
 using namespace rot;
 
-constexpr int kThreads = 320;
 constexpr int kLoadWarp = 1;
 constexpr int kRotWarp0 = 2, kNumRot = 4;
-constexpr int kEpiWarp0 = 6, kNumEpi = 4;
+constexpr int kEpiWarp0 = 6, kNumEpi = 4;   // warps per epilogue warpgroup (one per TMEM lane quadrant)
+__host__ __device__ constexpr int threads_for(int ewg) { return (kEpiWarp0 + kNumEpi * ewg) * 32; }
 constexpr int kMaxRing = 32;    // input rows in flight per CTA (bulk copies), at most
 constexpr int kStages = 2;      // N-side tiles
 constexpr int kSlots = 4;       // per-tile edge scalars
@@ -432,9 +432,12 @@ __device__ __forceinline__ void rotate_out_all(const float *__restrict__ rec, co
     }
 }
 
-template <int LIN, int LOUT, bool kSplit>
-__global__ void __launch_bounds__(kThreads, 1) sep_edgewise_kernel(const __grid_constant__ SepParams P) {
+// EWG epilogue warpgroups (1 or 2): with 2 the groups of a tile alternate between them, so each
+// SM sub-partition runs two epilogue warps and one hides the other's latencies.
+template <int LIN, int LOUT, bool kSplit, int EWG>
+__global__ void __launch_bounds__(threads_for(EWG), 1) sep_edgewise_kernel(const __grid_constant__ SepParams P) {
     using GE = Geo<LIN, LOUT>;
+    constexpr int kThreads = threads_for(EWG);
     constexpr int ES = GE::ES, TE = GE::TE, DIN = GE::DIN, DOUT = GE::DOUT;
     constexpr int ROWF = kCin * DIN;                       // input row floats
     constexpr int ROWF_PAD = (ROWF + 3) & ~3;
@@ -451,7 +454,7 @@ __global__ void __launch_bounds__(kThreads, 1) sep_edgewise_kernel(const __grid_
     uint8_t *b_base = a_hi + kSplitN * kSlices * kTileBytes;          // kStages x (hi [, lo])
     float *slots = reinterpret_cast<float *>(b_base + kStages * kSplitN * kTileBytes);
     float *stage = slots + kSlots * TE * GE::SLOT_EDGE;
-    float *jobs = stage + kG * GE::STAGE_ROW;                         // nr x JS per-edge scalars
+    float *jobs = stage + EWG * kG * GE::STAGE_ROW;                   // nr x JS per-edge records
     float *rows = jobs + (size_t)P.nr * JS;                           // nr input rows
 
     __shared__ uint64_t b_full[kStages], b_empty[kStages], t_full[kBufs], t_empty[kBufs], s_empty[kSlots];
@@ -471,9 +474,9 @@ __global__ void __launch_bounds__(kThreads, 1) sep_edgewise_kernel(const __grid_
         }
         for (int i = 0; i < kBufs; i++) {
             mbar_init(&t_full[i], 1);
-            mbar_init(&t_empty[i], kNumEpi);
+            mbar_init(&t_empty[i], kNumEpi * EWG);
         }
-        for (int i = 0; i < kSlots; i++) mbar_init(&s_empty[i], kNumEpi);
+        for (int i = 0; i < kSlots; i++) mbar_init(&s_empty[i], kNumEpi * EWG);
         for (int i = 0; i < kMaxRing; i++) {
             mbar_init(&r_full[i], 1);
             mbar_init(&r_free[i], 1);
@@ -642,13 +645,18 @@ __global__ void __launch_bounds__(kThreads, 1) sep_edgewise_kernel(const __grid_
                 const float t = sc[GE::REC_T];
                 const int lo = reinterpret_cast<const int *>(sc)[GE::REC_LO];
                 for (int qq = lane; qq < GE::REC_FLOATS; qq += 32) sl[qq] = sc[qq];   // record for the epilogue
-                // g_k = (1 - t) f[lo, k] + t f[lo + 1, k], per block padded to 4 floats
+                // g_k = (1 - t) f[lo, k] + t f[lo + 1, k], per block padded to 4 floats: the table
+                // rows come from L2, so the loads are issued here and used after the rotation
+                constexpr int GI = (kRank * GE::GP + 31) / 32;
+                float gl[GI], gh[GI];
                 {
                     const float *f_lo = P.ftab + (int64_t)lo * kRank * GE::W, *f_hi = f_lo + kRank * GE::W;
-                    const float omt = 1.0f - t;
-                    for (int idx = lane; idx < kRank * GE::GP; idx += 32) {
-                        const int wi = gidx_s[idx];
-                        sl[GE::SLOT_G + idx] = wi >= 0 ? omt * __ldg(f_lo + wi) + t * __ldg(f_hi + wi) : 0.0f;
+#pragma unroll
+                    for (int u = 0; u < GI; u++) {
+                        const int idx = lane + 32 * u;
+                        const int wi = idx < kRank * GE::GP ? gidx_s[idx] : -1;
+                        gl[u] = wi >= 0 ? __ldg(f_lo + wi) : 0.0f;
+                        gh[u] = wi >= 0 ? __ldg(f_hi + wi) : 0.0f;
                     }
                 }
                 float *fb = rows + (size_t)r * ROWF_PAD;
@@ -673,6 +681,14 @@ __global__ void __launch_bounds__(kThreads, 1) sep_edgewise_kernel(const __grid_
                 const float *cp = tr + 2 * GE::LMAX + 1, *sp = cp + GE::LMAX + 1;
                 rotate_in_all<GE, 0, kSplit>(sc, cp, sp, fb + c * DIN, fb + (c + 1) * DIN, bh, bh + kTileBytes,
                                              el * ES, c);
+                {
+                    const float omt = 1.0f - t;
+#pragma unroll
+                    for (int u = 0; u < GI; u++) {
+                        const int idx = lane + 32 * u;
+                        if (idx < kRank * GE::GP) sl[GE::SLOT_G + idx] = omt * gl[u] + t * gh[u];
+                    }
+                }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&r_free[r]);       // the row buffer may be refilled
@@ -687,21 +703,24 @@ __global__ void __launch_bounds__(kThreads, 1) sep_edgewise_kernel(const __grid_
         const int q4 = warp & 3;                       // TMEM lane quadrant of this warp
         const int row = q4 * 32 + lane;                // M row: co * kG + kk
         const int co = row / kG, kk = row % kG;
-        const bool leader = warp == kEpiWarp0 && lane == 0;
+        const int wg = (warp - kEpiWarp0) / kNumEpi;   // this warp's epilogue warpgroup
+        const int bar_id = 3 + wg;                     // named barrier of the warpgroup
+        const bool leader = warp == kEpiWarp0 + kNumEpi * wg && lane == 0;
+        float *my_stage = stage + wg * kG * GE::STAGE_ROW;
         for (int64_t i = 0; i < n_local; i++) {
             const int buf = (int)(i % kBufs), slot = (int)(i % kSlots);
             // The four epilogue warps meet at named barriers below, so they must leave the
             // loop together: a failed wait in any of them stops all four.
             if (!mbar_wait(&t_full[buf], (uint32_t)((i / kBufs) & 1), abort_flag, P.wait_ns) && lane == 0)
                 epi_stop_s = 1;
-            named_bar(2, kNumEpi * 32);
+            named_bar(2, EWG * kNumEpi * 32);
             if (*reinterpret_cast<volatile int *>(&epi_stop_s)) break;
             tc_fence_after();
             const int64_t e0 = (blockIdx.x + i * gridDim.x) * TE;
             const float *slot_base = slots + (size_t)slot * TE * GE::SLOT_EDGE;
             const uint32_t tbase = tmem + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(buf * kSlices * 128);
 #pragma unroll 1
-            for (int gi = 0; gi < TE / kG; gi++) {
+            for (int gi = wg; gi < TE / kG; gi += EWG) {
                 // every lane of a pair computes its k's share of both edges of the group; the
                 // pair sums its shares, and lane kk keeps edge gi * kG + kk
                 float hf[DOUT];
@@ -712,12 +731,21 @@ __global__ void __launch_bounds__(kThreads, 1) sep_edgewise_kernel(const __grid_
                     float h[DOUT];
 #pragma unroll
                     for (int q = 0; q < DOUT; q++) h[q] = 0.0f;
-#pragma unroll 1
-                    for (int s = 0; s < kSlices; s++) {
-                        uint32_t Z[ES];
-                        tmem_ld<ES>(tbase + (uint32_t)(s * 128 + el * ES), Z);
+                    if constexpr (ES == 16) {          // both slices' rows in one round trip
+                        uint32_t Z[kSlices][ES];
+#pragma unroll
+                        for (int s = 0; s < kSlices; s++) tmem_ld<ES>(tbase + (uint32_t)(s * 128 + el * ES), Z[s]);
                         tmem_wait_ld();
-                        pos_mix<GE, 0, ES>(Z, G + (s * kG + kk) * GE::GP, h);
+#pragma unroll
+                        for (int s = 0; s < kSlices; s++) pos_mix<GE, 0, ES>(Z[s], G + (s * kG + kk) * GE::GP, h);
+                    } else {
+#pragma unroll 1
+                        for (int s = 0; s < kSlices; s++) {
+                            uint32_t Z[ES];
+                            tmem_ld<ES>(tbase + (uint32_t)(s * 128 + el * ES), Z);
+                            tmem_wait_ld();
+                            pos_mix<GE, 0, ES>(Z, G + (s * kG + kk) * GE::GP, h);
+                        }
                     }
 #pragma unroll
                     for (int q = 0; q < DOUT; q++) {
@@ -732,15 +760,15 @@ __global__ void __launch_bounds__(kThreads, 1) sep_edgewise_kernel(const __grid_
                 for (int q = 0; q < GE::TF; q++) tr[q] = es[GE::REC_TRIG + q];
                 const float *cp = tr + 2 * GE::LMAX + 1, *sp = cp + GE::LMAX + 1;
                 if (leader) bulk_wait_read0();           // the previous group's rows have left
-                named_bar(1, kNumEpi * 32);
-                rotate_out_all<GE, 0>(es, cp, sp, hf, stage + kk * GE::STAGE_ROW + co * DOUT);
+                named_bar(bar_id, kNumEpi * 32);
+                rotate_out_all<GE, 0>(es, cp, sp, hf, my_stage + kk * GE::STAGE_ROW + co * DOUT);
                 fence_async_smem();
-                named_bar(1, kNumEpi * 32);
+                named_bar(bar_id, kNumEpi * 32);
                 if (leader) {
 #pragma unroll
                     for (int ee = 0; ee < kG; ee++) {
                         const int64_t e = e0 + gi * kG + ee;
-                        if (e < P.E) bulk_store(P.out + e * (int64_t)OUTF, stage + ee * GE::STAGE_ROW, OUTF * 4);
+                        if (e < P.E) bulk_store(P.out + e * (int64_t)OUTF, my_stage + ee * GE::STAGE_ROW, OUTF * 4);
                     }
                     bulk_commit();
                 }
@@ -763,7 +791,7 @@ __global__ void __launch_bounds__(kThreads, 1) sep_edgewise_kernel(const __grid_
 }
 
 // Shared memory without the input-row ring, and the bytes of one ring entry (row + scalars).
-template <int LIN, int LOUT, bool kSplit>
+template <int LIN, int LOUT, bool kSplit, int EWG>
 size_t smem_fixed_bytes() {
     using GE = Geo<LIN, LOUT>;
     constexpr int kSplitN = kSplit ? 2 : 1;
@@ -771,7 +799,7 @@ size_t smem_fixed_bytes() {
     b += (size_t)kSplitN * kSlices * kTileBytes;                         // M side
     b += (size_t)kStages * kSplitN * kTileBytes;                         // N side
     b += (size_t)kSlots * GE::TE * GE::SLOT_EDGE * 4;                    // per-tile slots
-    b += (size_t)kG * GE::STAGE_ROW * 4;                                 // output staging
+    b += (size_t)EWG * kG * GE::STAGE_ROW * 4;                           // output staging
     return b;
 }
 template <int LIN, int LOUT>
@@ -782,13 +810,14 @@ size_t ring_entry_bytes() {
 
 constexpr size_t kSmemPerBlock = 227 * 1024;     // dynamic + static shared memory of one CTA
 
-template <int LIN, int LOUT, bool kSplit>
+template <int LIN, int LOUT, bool kSplit, int EWG>
 int launch(SepParams P, cudaStream_t stream) {
-    auto kern = sep_edgewise_kernel<LIN, LOUT, kSplit>;
+    auto kern = sep_edgewise_kernel<LIN, LOUT, kSplit, EWG>;
+    constexpr int kThreads = threads_for(EWG);
     cudaFuncAttributes fa;
     FEQ_CUDA_TRY(cudaFuncGetAttributes(&fa, kern));
     const size_t cap = kSmemPerBlock - fa.sharedSizeBytes;
-    const size_t fixed = smem_fixed_bytes<LIN, LOUT, kSplit>(), entry = ring_entry_bytes<LIN, LOUT>();
+    const size_t fixed = smem_fixed_bytes<LIN, LOUT, kSplit, EWG>(), entry = ring_entry_bytes<LIN, LOUT>();
     if (fixed + 4 * entry > cap) return FEQ_ERR_UNSUPPORTED;
     int nr = (int)((cap - fixed) / entry);
     P.nr = nr < kMaxRing ? nr : kMaxRing;
@@ -808,10 +837,11 @@ int launch(SepParams P, cudaStream_t stream) {
 // (LIN, LOUT) pairs this build instantiates: lvals [0..L] in and out, L <= 4.
 template <bool kSplit>
 int dispatch(int lin, int lout, const SepParams &P, cudaStream_t s) {
-    if (lin == 1 && lout == 1) return launch<1, 1, kSplit>(P, s);
-    if (lin == 2 && lout == 2) return launch<2, 2, kSplit>(P, s);
-    if (lin == 3 && lout == 3) return launch<3, 3, kSplit>(P, s);
-    if (lin == 4 && lout == 4) return launch<4, 4, kSplit>(P, s);
+    // two epilogue warpgroups where the registers allow it (the L <= 3 kernels use <= 128)
+    if (lin == 1 && lout == 1) return launch<1, 1, kSplit, 2>(P, s);
+    if (lin == 2 && lout == 2) return launch<2, 2, kSplit, 2>(P, s);
+    if (lin == 3 && lout == 3) return launch<3, 3, kSplit, 2>(P, s);
+    if (lin == 4 && lout == 4) return launch<4, 4, kSplit, 1>(P, s);
     return FEQ_ERR_UNSUPPORTED;
 }
 
