@@ -233,6 +233,15 @@ __device__ __forceinline__ void rot_irrep2c(const float *__restrict__ tr, int lm
     }
 }
 
+// n floats from 16-byte aligned shared memory into registers (float4 loads).
+template <int NZ>
+__device__ __forceinline__ void load_m(const float *__restrict__ src, float (&m)[NZ]);
+
+template <int NZ>
+__device__ __forceinline__ void load_regs(const float *__restrict__ src, float (&m)[NZ]) {
+    load_m<NZ>(src, m);
+}
+
 template <int NZ>
 __device__ __forceinline__ void load_m(const float *__restrict__ src, float (&m)[NZ]) {
     const float4 *s4 = reinterpret_cast<const float4 *>(src);
@@ -395,25 +404,29 @@ __device__ __forceinline__ void pos_mix(const uint32_t (&Z)[ES], const float *__
 
 // Input rotation of one irrep degree L (recursing to LIN) for the channel pair (c, c + 1);
 // rec: the edge's record (trig, M_l nonzeros).
+// The N-side rows of an edge start at a multiple of 8 rows (ES is 16 or 32), so the 128-byte
+// swizzle of row r = row0 + j depends on j only: byte offset j * 128 + xo[j & 7], with
+// xo[k] = ((c / 8) ^ k) * 16 + (c % 8) * 2 for this lane's channel pair c (swz above).
 template <class GE, int L, bool kSplit>
 __device__ __forceinline__ void rotate_in_all(const float *__restrict__ rec, const float *__restrict__ cp,
                                               const float *__restrict__ sp, const float *__restrict__ f0,
-                                              const float *__restrict__ f1, uint8_t *bhi, uint8_t *blo, int row0,
-                                              int c) {
+                                              const float *__restrict__ f1, uint8_t *bhi, uint8_t *blo,
+                                              const uint32_t (&xo)[8]) {
     if constexpr (L <= GE::LI) {
         constexpr int off = L * L;    // standard offset of degree L in [0..LIN]
         auto get = [&](int q) { return make_float2(f0[off + q], f1[off + q]); };
         auto emit = [&](int o, float y0, float y1) {
-            const int r = row0 + GE::mf_in(L, o - L);
+            const int jm = GE::mf_in(L, o - L);
+            const uint32_t bo = (uint32_t)jm * 128u + xo[jm & 7];
             const __nv_bfloat162 hi = __floats2bfloat162_rn(y0, y1);
-            *reinterpret_cast<__nv_bfloat162 *>(bhi + swz(r, c)) = hi;
+            *reinterpret_cast<__nv_bfloat162 *>(bhi + bo) = hi;
             if (kSplit) {
                 const float2 hf = __bfloat1622float2(hi);
-                *reinterpret_cast<__nv_bfloat162 *>(blo + swz(r, c)) = __floats2bfloat162_rn(y0 - hf.x, y1 - hf.y);
+                *reinterpret_cast<__nv_bfloat162 *>(blo + bo) = __floats2bfloat162_rn(y0 - hf.x, y1 - hf.y);
             }
         };
         rot2_pre<L, false>(rec + GE::REC_M + GE::moff(L), cp, sp, get, emit);
-        rotate_in_all<GE, L + 1, kSplit>(rec, cp, sp, f0, f1, bhi, blo, row0, c);
+        rotate_in_all<GE, L + 1, kSplit>(rec, cp, sp, f0, f1, bhi, blo, xo);
     }
 }
 
@@ -616,6 +629,9 @@ __global__ void __launch_bounds__(threads_for(EWG), 1) sep_edgewise_kernel(const
         // ---------------- rotation in ----------------
         const int w = warp - kRotWarp0;
         constexpr int EPW = TE / kNumRot;                  // edges of one tile per rotation warp
+        uint32_t xo[8];
+#pragma unroll
+        for (int k = 0; k < 8; k++) xo[k] = (uint32_t)((((lane >> 2) ^ k) << 4) + ((2 * lane) & 7) * 2);
         const int64_t n_mine = n_local * EPW;
         for (int64_t q = 0; q < n_mine; q++) {
             const int64_t i = q / EPW;
@@ -640,8 +656,7 @@ __global__ void __launch_bounds__(threads_for(EWG), 1) sep_edgewise_kernel(const
                 const int64_t e = edge_of_job(j);
                 float *sl = slots + (size_t)(slot * TE + el) * GE::SLOT_EDGE;
                 float tr[GE::TF];
-#pragma unroll
-                for (int qq = 0; qq < GE::TF; qq++) tr[qq] = sc[GE::REC_TRIG + qq];
+                load_regs<GE::TF>(sc + GE::REC_TRIG, tr);
                 const float t = sc[GE::REC_T];
                 const int lo = reinterpret_cast<const int *>(sc)[GE::REC_LO];
                 for (int qq = lane; qq < GE::REC_FLOATS; qq += 32) sl[qq] = sc[qq];   // record for the epilogue
@@ -679,8 +694,8 @@ __global__ void __launch_bounds__(threads_for(EWG), 1) sep_edgewise_kernel(const
                 uint8_t *bh = b_base + st * kSplitN * kTileBytes;
                 const int c = 2 * lane;
                 const float *cp = tr + 2 * GE::LMAX + 1, *sp = cp + GE::LMAX + 1;
-                rotate_in_all<GE, 0, kSplit>(sc, cp, sp, fb + c * DIN, fb + (c + 1) * DIN, bh, bh + kTileBytes,
-                                             el * ES, c);
+                uint8_t *rb = bh + el * ES * 128;
+                rotate_in_all<GE, 0, kSplit>(sc, cp, sp, fb + c * DIN, fb + (c + 1) * DIN, rb, rb + kTileBytes, xo);
                 {
                     const float omt = 1.0f - t;
 #pragma unroll
@@ -756,8 +771,7 @@ __global__ void __launch_bounds__(threads_for(EWG), 1) sep_edgewise_kernel(const
                 const int el = gi * kG + kk;
                 const float *es = slot_base + el * GE::SLOT_EDGE;
                 float tr[GE::TF];
-#pragma unroll
-                for (int q = 0; q < GE::TF; q++) tr[q] = es[GE::REC_TRIG + q];
+                load_regs<GE::TF>(es + GE::REC_TRIG, tr);
                 const float *cp = tr + 2 * GE::LMAX + 1, *sp = cp + GE::LMAX + 1;
                 if (leader) bulk_wait_read0();           // the previous group's rows have left
                 named_bar(bar_id, kNumEpi * 32);

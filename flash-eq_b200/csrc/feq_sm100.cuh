@@ -66,7 +66,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volati
     const uint64_t t0 = globaltimer();
     for (uint32_t i = 1;; i++) {
         if (mbar_try_wait(b, parity)) return true;
-        if ((i & 63) == 0) {
+        if ((i & 7) == 0) {       // (try_wait itself suspends the thread for a while)
             if (*abort_flag) return false;
             if (globaltimer() - t0 > limit_ns) {
                 *abort_flag = 1;
