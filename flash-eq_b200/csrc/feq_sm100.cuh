@@ -57,22 +57,6 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 
-// try_wait with a suspend-time hint: the waiting thread is parked (woken when the phase
-// completes) for up to hint_ns instead of spinning through issue slots.
-__device__ __forceinline__ bool mbar_try_wait_hint(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(bar), "r"(parity), "r"(hint_ns)
-        : "memory");
-    return ok != 0;
-}
-
-constexpr uint32_t kSuspendHintNs = 20000;   // 20 us per try (checks below stay bounded)
-
 // Wait for phase `parity` of `bar` to complete.  Gives up (returns false) when the
 // CTA's abort flag is raised or after limit_ns, raising the flag itself.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag,
@@ -80,9 +64,8 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volati
     const uint32_t b = smem_u32(bar);
     if (mbar_try_wait(b, parity)) return true;
     const uint64_t t0 = globaltimer();
-    const uint32_t hint = limit_ns < kSuspendHintNs ? (uint32_t)limit_ns : kSuspendHintNs;
     for (uint32_t i = 1;; i++) {
-        if (mbar_try_wait_hint(b, parity, hint)) return true;
+        if (mbar_try_wait(b, parity)) return true;
         if ((i & 7) == 0) {       // (try_wait itself suspends the thread for a while)
             if (*abort_flag) return false;
             if (globaltimer() - t0 > limit_ns) {
