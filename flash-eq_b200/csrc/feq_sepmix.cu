@@ -832,9 +832,17 @@ int launch(SepParams P, cudaStream_t stream) {
     FEQ_CUDA_TRY(cudaFuncGetAttributes(&fa, kern));
     const size_t cap = kSmemPerBlock - fa.sharedSizeBytes;
     const size_t fixed = smem_fixed_bytes<LIN, LOUT, kSplit, EWG>(), entry = ring_entry_bytes<LIN, LOUT>();
-    if (fixed + 4 * entry > cap) return FEQ_ERR_UNSUPPORTED;
+    // The ring size is a multiple of the tile's edge count: then job j and job j + nr are the
+    // same edge slot of their tiles, so every ring buffer is only ever read by one rotation
+    // warp, which takes its jobs in order.  Each wait on a buffer's "full" barrier is then for
+    // the phase right after the one that warp last consumed, and a parity wait cannot match a
+    // phase two ahead.  (With another size a warp could run two phases ahead of the loader on
+    // a buffer another warp still owes, and its parity wait would pass early.)
     int nr = (int)((cap - fixed) / entry);
-    P.nr = nr < kMaxRing ? nr : kMaxRing;
+    nr = nr < kMaxRing ? nr : kMaxRing;
+    nr -= nr % Geo<LIN, LOUT>::TE;
+    if (nr < Geo<LIN, LOUT>::TE || fixed + (size_t)nr * entry > cap) return FEQ_ERR_UNSUPPORTED;
+    P.nr = nr;
     size_t smem = fixed + (size_t)P.nr * entry;
     // more than half of the SM's shared memory: one CTA per SM, so one TMEM allocation
     if (smem < 120 * 1024) smem = 120 * 1024;
