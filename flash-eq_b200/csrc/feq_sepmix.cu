@@ -458,6 +458,8 @@ __global__ void __launch_bounds__(threads_for(EWG), 1) sep_edgewise_kernel(const
     constexpr uint32_t kIdesc = idesc_bf16_f32(128, 128);
     constexpr int kSplitN = kSplit ? 2 : 1;
     constexpr int JS = GE::JOB_FLOATS;
+    constexpr int FRB = 2 * kRank * GE::W * 4;                        // bytes of two rows of f
+    constexpr int FR = (2 * kRank * GE::W + 3) & ~3;
     static_assert(TE % kNumRot == 0 && TE % kG == 0, "tile edges split over the warps");
 
     extern __shared__ uint8_t smem_raw[];
@@ -468,7 +470,8 @@ __global__ void __launch_bounds__(threads_for(EWG), 1) sep_edgewise_kernel(const
     float *slots = reinterpret_cast<float *>(b_base + kStages * kSplitN * kTileBytes);
     float *stage = slots + kSlots * TE * GE::SLOT_EDGE;
     float *jobs = stage + EWG * kG * GE::STAGE_ROW;                   // nr x JS per-edge records
-    float *rows = jobs + (size_t)P.nr * JS;                           // nr input rows
+    float *frows = jobs + (size_t)P.nr * JS;                          // nr x FR: rows lo, lo + 1 of f
+    float *rows = frows + (size_t)P.nr * FR;                          // nr input rows
 
     __shared__ uint64_t b_full[kStages], b_empty[kStages], t_full[kBufs], t_empty[kBufs], s_empty[kSlots];
     __shared__ uint64_t r_full[kMaxRing], r_free[kMaxRing], drain_bar;
@@ -572,8 +575,30 @@ __global__ void __launch_bounds__(threads_for(EWG), 1) sep_edgewise_kernel(const
         }
     } else if (warp == kLoadWarp) {
         // ---------------- loader: edge scalars + input rows, lane per edge ----------------
-        const int NB = NR < 32 ? NR : 32;
+        // Batches of NB = nr / 2 jobs: a batch only waits for the buffers of the batch two back,
+        // so one batch is always in flight while the next is prepared.  The next batch's edge
+        // inputs (distance, direction, src) are fetched before this batch is processed.
+        const int NB = NR / 2 < 32 ? NR / 2 : 32;
+        float nd = 0.0f, nx = 0.0f, ny = 0.0f, nz = 0.0f;
+        int64_t nrow = -1;
+        auto fetch = [&](int64_t b0) {
+            const int64_t j = b0 + lane;
+            if (lane < NB && j < n_jobs) {
+                const int64_t e = edge_of_job(j);
+                if (e < P.E) {
+                    nd = P.dist[e];
+                    nx = P.dirs[e * 3];
+                    ny = P.dirs[e * 3 + 1];
+                    nz = P.dirs[e * 3 + 2];
+                    nrow = P.src ? P.src[e] : e;
+                }
+            }
+        };
+        fetch(0);
         for (int64_t base = 0; base < n_jobs; base += NB) {
+            const float dd = nd, vx = nx, vy = ny, vz = nz;
+            const int64_t row = nrow;
+            fetch(base + NB);
             const int64_t j = base + lane;
             bool ok = true;
             if (lane < NB && j < n_jobs) {
@@ -584,14 +609,12 @@ __global__ void __launch_bounds__(threads_for(EWG), 1) sep_edgewise_kernel(const
                     int *sci = reinterpret_cast<int *>(sc);
                     const int64_t e = edge_of_job(j);
                     int flag = 2;                         // 0 row copied, 1 bad src (zero row), 2 no edge
-                    int64_t row = -1;
+                    int lo = 0;
                     if (e < P.E) {
-                        const float dd = P.dist[e];
-                        int lo;
                         float t;
                         bin_of(dd, P.bins, lo, t);
                         float tr[GE::TF];
-                        edge_trig_compact(P.dirs[e * 3], P.dirs[e * 3 + 1], P.dirs[e * 3 + 2], GE::LMAX, tr);
+                        edge_trig_compact(vx, vy, vz, GE::LMAX, tr);
 #pragma unroll
                         for (int q = 0; q < GE::TF; q++) sc[GE::REC_TRIG + q] = tr[q];
                         const float sw = dd / (dd + P.sh_scale);
@@ -599,7 +622,6 @@ __global__ void __launch_bounds__(threads_for(EWG), 1) sep_edgewise_kernel(const
                         sc[GE::REC_T] = t;
                         sci[GE::REC_LO] = lo;
                         fill_m<GE, 1>(tr, sw, sc);
-                        row = P.src ? P.src[e] : e;
                         if (row < 0 || row >= P.nsrc) {
                             set_status(P.status, 1);
                             flag = 1;
@@ -609,10 +631,13 @@ __global__ void __launch_bounds__(threads_for(EWG), 1) sep_edgewise_kernel(const
                     }
                     sci[GE::REC_FLAG] = flag;
                     r_issued[r] = j;
-                    if (flag == 0) {
+                    if (flag != 2) {
+                        // the edge's two rows of radial features (bins lo, lo + 1) and its input row
                         fence_async_smem();
-                        mbar_arrive_expect_tx(&r_full[r], ROWF * 4);
-                        bulk_load(rows + (size_t)r * ROWF_PAD, P.x + row * (int64_t)ROWF, ROWF * 4, &r_full[r]);
+                        mbar_arrive_expect_tx(&r_full[r], FRB + (flag == 0 ? ROWF * 4 : 0));
+                        bulk_load(frows + (size_t)r * FR, P.ftab + (int64_t)lo * kRank * GE::W, FRB, &r_full[r]);
+                        if (flag == 0)
+                            bulk_load(rows + (size_t)r * ROWF_PAD, P.x + row * (int64_t)ROWF, ROWF * 4, &r_full[r]);
                     } else {
                         mbar_arrive(&r_full[r]);
                     }
@@ -658,20 +683,19 @@ __global__ void __launch_bounds__(threads_for(EWG), 1) sep_edgewise_kernel(const
                 float tr[GE::TF];
                 load_regs<GE::TF>(sc + GE::REC_TRIG, tr);
                 const float t = sc[GE::REC_T];
-                const int lo = reinterpret_cast<const int *>(sc)[GE::REC_LO];
                 for (int qq = lane; qq < GE::REC_FLOATS; qq += 32) sl[qq] = sc[qq];   // record for the epilogue
-                // g_k = (1 - t) f[lo, k] + t f[lo + 1, k], per block padded to 4 floats: the table
-                // rows come from L2, so the loads are issued here and used after the rotation
+                // g_k = (1 - t) f[lo, k] + t f[lo + 1, k], per block padded to 4 floats (the two
+                // rows of f arrived with the input row)
                 constexpr int GI = (kRank * GE::GP + 31) / 32;
                 float gl[GI], gh[GI];
                 {
-                    const float *f_lo = P.ftab + (int64_t)lo * kRank * GE::W, *f_hi = f_lo + kRank * GE::W;
+                    const float *f_lo = frows + (size_t)r * FR, *f_hi = f_lo + kRank * GE::W;
 #pragma unroll
                     for (int u = 0; u < GI; u++) {
                         const int idx = lane + 32 * u;
                         const int wi = idx < kRank * GE::GP ? gidx_s[idx] : -1;
-                        gl[u] = wi >= 0 ? __ldg(f_lo + wi) : 0.0f;
-                        gh[u] = wi >= 0 ? __ldg(f_hi + wi) : 0.0f;
+                        gl[u] = wi >= 0 ? f_lo[wi] : 0.0f;
+                        gh[u] = wi >= 0 ? f_hi[wi] : 0.0f;
                     }
                 }
                 float *fb = rows + (size_t)r * ROWF_PAD;
@@ -819,7 +843,7 @@ size_t smem_fixed_bytes() {
 template <int LIN, int LOUT>
 size_t ring_entry_bytes() {
     using GE = Geo<LIN, LOUT>;
-    return ((size_t)((kCin * GE::DIN + 3) & ~3) + GE::JOB_FLOATS) * 4;
+    return ((size_t)((kCin * GE::DIN + 3) & ~3) + GE::JOB_FLOATS + ((2 * kRank * GE::W + 3) & ~3)) * 4;
 }
 
 constexpr size_t kSmemPerBlock = 227 * 1024;     // dynamic + static shared memory of one CTA
@@ -899,7 +923,7 @@ extern "C" int feq_edgewise_separable_fwd(const FeqSeparableArgs *a, feq_stream_
     if (!a->x || !a->distances || !a->channel_patterns || !a->radial_features || !a->out)
         return FEQ_ERR_INVALID_ARGUMENT;
     if ((reinterpret_cast<uintptr_t>(a->x) | reinterpret_cast<uintptr_t>(a->out) |
-         reinterpret_cast<uintptr_t>(a->edge_add)) & 15)
+         reinterpret_cast<uintptr_t>(a->edge_add) | reinterpret_cast<uintptr_t>(a->radial_features)) & 15)
         return FEQ_ERR_INVALID_ARGUMENT;      // bulk copies need 16-byte aligned rows
     const int L = a->n_lvals_in - 1;
     sep::SepParams P;

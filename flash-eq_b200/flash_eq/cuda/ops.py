@@ -304,7 +304,7 @@ def edgewise_separable_fwd(x, distances, channel_patterns, radial_features, lval
     x = _aligned16(_f32(x, "x"))
     distances = _f32(distances, "distances")
     cp = _f32(channel_patterns, "channel_patterns")
-    rf = _f32(radial_features, "radial_features")
+    rf = _aligned16(_f32(radial_features, "radial_features"))
     directions = _f32(directions, "directions")
     E = distances.numel()
     rank, c_out, c_in = cp.shape

@@ -281,7 +281,7 @@ typedef struct FeqSeparableArgs {
     const float *directions;        /* (E, 3) */
     const float *distances;         /* (E,) */
     const float *channel_patterns;  /* (rank, c_out, c_in) */
-    const float *radial_features;   /* (num_bins + 1, rank, W) */
+    const float *radial_features;   /* (num_bins + 1, rank, W), 16-byte aligned */
     int64_t num_edges;
     int32_t c_in, c_out, rank;
     const int32_t *lvals_in;        /* host array */
