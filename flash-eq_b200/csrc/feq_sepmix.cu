@@ -54,9 +54,10 @@ using namespace sm100;
 using namespace rot;
 
 constexpr int kLoadWarp = 1;
-constexpr int kRotWarp0 = 2, kNumRot = 4;
-constexpr int kEpiWarp0 = 6, kNumEpi = 4;   // warps per epilogue warpgroup (one per TMEM lane quadrant)
-__host__ __device__ constexpr int threads_for(int ewg) { return (kEpiWarp0 + kNumEpi * ewg) * 32; }
+constexpr int kRotWarp0 = 2;
+constexpr int kNumEpi = 4;   // warps per epilogue warpgroup (one per TMEM lane quadrant)
+// NROT rotation warps (warps 2 .. 2 + NROT - 1), then EWG epilogue warpgroups
+__host__ __device__ constexpr int threads_for(int ewg, int nrot) { return (kRotWarp0 + nrot + kNumEpi * ewg) * 32; }
 constexpr int kMaxRing = 32;    // input rows in flight per CTA (bulk copies), at most
 constexpr int kStages = 2;      // N-side tiles
 constexpr int kSlots = 4;       // per-tile edge scalars
@@ -446,11 +447,16 @@ __device__ __forceinline__ void rotate_out_all(const float *__restrict__ rec, co
 }
 
 // EWG epilogue warpgroups (1 or 2): with 2 the groups of a tile alternate between them, so each
-// SM sub-partition runs two epilogue warps and one hides the other's latencies.
-template <int LIN, int LOUT, bool kSplit, int EWG>
-__global__ void __launch_bounds__(threads_for(EWG), 1) sep_edgewise_kernel(const __grid_constant__ SepParams P) {
+// SM sub-partition runs two epilogue warps and one hides the other's latencies.  NROT rotation
+// warps (4 or 8) share the edges of a tile the same way.  Every warp runs long dependent chains,
+// so where the registers allow, more warps per sub-partition is what keeps the issue slots busy.
+template <int LIN, int LOUT, bool kSplit, int EWG, int NROT>
+__global__ void __launch_bounds__(threads_for(EWG, NROT), 1)
+sep_edgewise_kernel(const __grid_constant__ SepParams P) {
     using GE = Geo<LIN, LOUT>;
-    constexpr int kThreads = threads_for(EWG);
+    constexpr int kThreads = threads_for(EWG, NROT);
+    constexpr int kNumRot = NROT;
+    constexpr int kEpiWarp0 = kRotWarp0 + NROT;
     constexpr int ES = GE::ES, TE = GE::TE, DIN = GE::DIN, DOUT = GE::DOUT;
     constexpr int ROWF = kCin * DIN;                       // input row floats
     constexpr int ROWF_PAD = (ROWF + 3) & ~3;
@@ -848,10 +854,10 @@ size_t ring_entry_bytes() {
 
 constexpr size_t kSmemPerBlock = 227 * 1024;     // dynamic + static shared memory of one CTA
 
-template <int LIN, int LOUT, bool kSplit, int EWG>
+template <int LIN, int LOUT, bool kSplit, int EWG, int NROT>
 int launch(SepParams P, cudaStream_t stream) {
-    auto kern = sep_edgewise_kernel<LIN, LOUT, kSplit, EWG>;
-    constexpr int kThreads = threads_for(EWG);
+    auto kern = sep_edgewise_kernel<LIN, LOUT, kSplit, EWG, NROT>;
+    constexpr int kThreads = threads_for(EWG, NROT);
     cudaFuncAttributes fa;
     FEQ_CUDA_TRY(cudaFuncGetAttributes(&fa, kern));
     const size_t cap = kSmemPerBlock - fa.sharedSizeBytes;
@@ -883,11 +889,12 @@ int launch(SepParams P, cudaStream_t stream) {
 // (LIN, LOUT) pairs this build instantiates: lvals [0..L] in and out, L <= 4.
 template <bool kSplit>
 int dispatch(int lin, int lout, const SepParams &P, cudaStream_t s) {
-    // two epilogue warpgroups where the registers allow it (the L <= 3 kernels use <= 128)
-    if (lin == 1 && lout == 1) return launch<1, 1, kSplit, 2>(P, s);
-    if (lin == 2 && lout == 2) return launch<2, 2, kSplit, 2>(P, s);
-    if (lin == 3 && lout == 3) return launch<3, 3, kSplit, 2>(P, s);
-    if (lin == 4 && lout == 4) return launch<4, 4, kSplit, 1>(P, s);
+    // as many warps as the registers allow: L <= 2 (<= 100 registers) 8 rotation warps and two
+    // epilogue warpgroups, L = 3 (128) 4 and two, L = 4 (168) 4 and one
+    if (lin == 1 && lout == 1) return launch<1, 1, kSplit, 2, 8>(P, s);
+    if (lin == 2 && lout == 2) return launch<2, 2, kSplit, 2, 8>(P, s);
+    if (lin == 3 && lout == 3) return launch<3, 3, kSplit, 2, 4>(P, s);
+    if (lin == 4 && lout == 4) return launch<4, 4, kSplit, 1, 4>(P, s);
     return FEQ_ERR_UNSUPPORTED;
 }
 
