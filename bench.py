@@ -347,8 +347,10 @@ def dist_setup(args):
 
         import torch.distributed as dist
 
-        # communicator set-up lines (rank, device, transport) in the log
-        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        # communicator set-up lines (rank, device, transport) in the log, even where the
+        # environment asks only for the version line
+        if os.environ.get("NCCL_DEBUG", "").upper() not in ("INFO", "TRACE"):
+            os.environ["NCCL_DEBUG"] = "INFO"
         os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
