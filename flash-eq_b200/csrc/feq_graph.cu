@@ -416,8 +416,127 @@ attn_pool_kernel(const __grid_constant__ FeqAttnArgs a) {
     }
 }
 
+// Warp-per-destination variant for rows that split evenly over the lanes: lane l owns the
+// S contiguous floats [l S, (l + 1) S) of the Q, K and V rows; with 32 % H == 0 each head is a
+// group of 32 / H lanes, so a head's logit is a shuffle reduction within the group and the
+// online softmax (max, rescale, sum) runs per lane on values the group agrees on.  The next
+// edge's K and V slices are loaded while the current edge is folded in; no block barriers.
+// Same arithmetic as attn_pool_kernel: logit = scale <q, k> (- d / decay), running max m,
+// p = exp(logit - m_new), acc = acc exp(m_old - m_new) + p v, out = acc / (sum + 1e-8).
+template <int S>
+__global__ void __launch_bounds__(128)
+attn_pool_warp_kernel(const __grid_constant__ FeqAttnArgs a) {
+    const int lane = threadIdx.x & 31;
+    const int64_t n = (int64_t)blockIdx.x * 4 + (threadIdx.x >> 5);
+    if (n >= a.num_nodes) return;
+    const int qrow = a.c_qk * a.d_qk;
+    const int H = a.num_heads, gl = 32 / H;      // lanes per head
+    const bool split_k = a.k != nullptr;
+    const int64_t nsrc = split_k ? a.num_src_nodes : a.num_nodes;
+    const float *kbase = split_k ? a.k : a.qk + qrow;
+    const int64_t k_ld = split_k ? qrow : 2 * (int64_t)qrow;
+    const float *qn = a.qk + n * (int64_t)(split_k ? qrow : 2 * qrow) + lane * S;
+    float q[S], acc[S];
+#pragma unroll
+    for (int i = 0; i < S; i++) {
+        q[i] = __ldg(qn + i);
+        acc[i] = 0.0f;
+    }
+    float m = -INFINITY, ssum = 0.0f;
+    const int64_t s0 = a.offsets[n], s1 = a.offsets[n + 1];
+    float kn[S], vn[S];
+    int64_t en = 0;
+    auto fetch = [&](int64_t pos) {
+        en = a.perm[pos];
+        int64_t sidx = a.src[en];
+        if (sidx < 0 || sidx >= nsrc) {
+            if (lane == 0) set_status(a.status, 1);
+            sidx = -1;
+        }
+        const float *kr = kbase + (sidx >= 0 ? sidx : 0) * k_ld + lane * S;
+        const float *vr = a.v + en * (int64_t)(32 * S) + lane * S;
+        if constexpr ((S & 1) == 0) {      // 8-byte aligned slices: float2 loads
+#pragma unroll
+            for (int i = 0; i < S; i += 2) {
+                const float2 kk = __ldg(reinterpret_cast<const float2 *>(kr + i));
+                const float2 vv = __ldg(reinterpret_cast<const float2 *>(vr + i));
+                kn[i] = sidx >= 0 ? kk.x : 0.0f;
+                kn[i + 1] = sidx >= 0 ? kk.y : 0.0f;
+                vn[i] = vv.x;
+                vn[i + 1] = vv.y;
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < S; i++) {
+                kn[i] = sidx >= 0 ? __ldg(kr + i) : 0.0f;
+                vn[i] = __ldg(vr + i);
+            }
+        }
+    };
+    if (s0 < s1) fetch(s0);
+    for (int64_t pos = s0; pos < s1; pos++) {
+        float kc[S], vc[S];
+#pragma unroll
+        for (int i = 0; i < S; i++) {
+            kc[i] = kn[i];
+            vc[i] = vn[i];
+        }
+        const int64_t ec = en;
+        if (pos + 1 < s1) fetch(pos + 1);
+        float d0 = 0.0f, d1 = 0.0f;
+#pragma unroll
+        for (int i = 0; i + 1 < S; i += 2) {
+            d0 = fmaf(q[i], kc[i], d0);
+            d1 = fmaf(q[i + 1], kc[i + 1], d1);
+        }
+        if (S & 1) d0 = fmaf(q[S - 1], kc[S - 1], d0);
+        float dot = d0 + d1;
+        for (int o = 1; o < gl; o <<= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+        float lg = dot * a.scale;
+        if (a.decay_scale > 0.0f && a.distances) lg -= a.distances[ec] / a.decay_scale;
+        const float mnew = fmaxf(m, lg);
+        const float corr = (m == -INFINITY) ? 0.0f : expf(m - mnew);
+        const float p = expf(lg - mnew);
+        ssum = ssum * corr + p;
+#pragma unroll
+        for (int i = 0; i < S; i++) acc[i] = fmaf(p, vc[i], acc[i] * corr);
+        m = mnew;
+    }
+    const float inv = 1.0f / (ssum + 1e-8f);
+    const float cnt = (float)max64(s1 - s0, 1);
+    float *on = a.out + n * (int64_t)(32 * S) + lane * S;
+#pragma unroll
+    for (int i = 0; i < S; i++) {
+        float v = acc[i] * inv;
+        if (a.reduce == FEQ_REDUCE_MEAN) v /= cnt;
+        on[i] = v;
+    }
+}
+
+template <int S>
+static int launch_attn_pool_warp(const FeqAttnArgs &a, cudaStream_t s) {
+    attn_pool_warp_kernel<S><<<(unsigned)((a.num_nodes + 3) / 4), 128, 0, s>>>(a);
+    FEQ_LAUNCH_CHECK();
+    return FEQ_OK;
+}
+
 int launch_attn_pool(const FeqAttnArgs &a, cudaStream_t s) {
     if (a.num_nodes == 0) return FEQ_OK;
+    {
+        // warp-per-destination path: Q / K and V rows of equal length split over 32 lanes,
+        // whole heads per lane group
+        const int qrow = a.c_qk * a.d_qk, vrow = a.c_v * a.d_v, H = a.num_heads;
+        const bool aligned = ((reinterpret_cast<uintptr_t>(a.qk) | reinterpret_cast<uintptr_t>(a.v) |
+                               reinterpret_cast<uintptr_t>(a.k)) & 7) == 0;
+        if (qrow == vrow && qrow % 32 == 0 && H >= 1 && H <= 32 && 32 % H == 0 && aligned &&
+            a.num_nodes <= 0x1ffffffffll) {
+            const int S = qrow / 32;
+            if (S == 18) return launch_attn_pool_warp<18>(a, s);    // Repr([0,1,2], 64)
+            if (S == 9) return launch_attn_pool_warp<9>(a, s);      // Repr([0,1,2], 32)
+            if (S == 16) return launch_attn_pool_warp<16>(a, s);    // Repr([0..3], 32)
+            if (S == 8) return launch_attn_pool_warp<8>(a, s);      // Repr([0,1], 64)
+        }
+    }
     if (a.num_heads < 1 || a.num_heads > kAttnMaxHeads) return FEQ_ERR_UNSUPPORTED;
     if (a.num_nodes > 0x7fffffffll) return FEQ_ERR_UNSUPPORTED;
     const size_t smem = sizeof(float) * ((size_t)a.c_qk * a.d_qk + (size_t)a.c_v * a.d_v);
