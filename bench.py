@@ -121,7 +121,7 @@ class ClockSampler:
     def start(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-lms", "200", "-i", str(self.gpu_index)],
+                                          "-lms", "100", "-i", str(self.gpu_index)],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self._t = threading.Thread(target=self._read, daemon=True)
             self._t.start()
@@ -400,11 +400,13 @@ def run_ours(args):
             P, Q = basis(vec)
             return layer(P, Q, x[src], dist_e)
 
+    # nvidia-smi takes ~0.1 s to its first sample: started before the warm-up, it covers the
+    # (short) timed region too
+    clk = ClockSampler(gpu_index_for(local))
+    clk.start()
     for _ in range(args.warmup):
         step()
     barrier(pg)
-    clk = ClockSampler(gpu_index_for(local))
-    clk.start()
     n0 = lib.feq_launch_count()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier(pg)
@@ -468,12 +470,13 @@ def run_ours(args):
         es = 16 if d <= 16 else 32
         exe = E * 4 * MULT * es * MULT * 2 * {"bf16x3": 3, "bf16": 1}.get(args.mix, 0) / t / 1e12
         roofline = {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak,
-                    "traffic": None, "kernel": f"sep_edgewise (one launch per step: gather rows in, rotation, "
+                    "traffic": profiled_traffic("sep_edgewise", E), "kernel": f"sep_edgewise (one launch per step: gather rows in, rotation, "
                                               f"separable mix on tcgen05, rotation back, rows out), CUDA events on "
                                               f"its stream, {prof_steps} steps",
                     "peak_kind": f"{peak_kind} HBM copy bandwidth (MEASURED_PEAKS.json)",
                     "bytes_per_edge": byts,
-                    "traffic_source": "see profiles/sep_edgewise_config2.md (ncu DRAM bytes of a small case)",
+                    "traffic_source": "committed ncu summary profiles/sep_edgewise_config2.md (DRAM bytes per edge of a "
+                                      "small case of this workload, scaled to E); not measured in this run",
                     "alg_mix_tflops": E * mix_flops / t / 1e12,
                     "executed_tensor_tflops": exe, "executed_tensor_frac": exe / tc_sustained}
     elif dom is not None:
@@ -870,10 +873,10 @@ def run_block(args):
         barrier(pg)
         return max_over_ranks(pg, t0.elapsed_time(t1) / steps)
 
+    clk = ClockSampler(gpu_index_for(local))      # started before the warm-up (see run_ours)
+    clk.start()
     for _ in range(args.warmup):
         step()
-    clk = ClockSampler(gpu_index_for(local))
-    clk.start()
     torch.cuda.profiler.start()      # lets `ncu --profile-from-start off` capture just the timed steps
     ms = timed(step, args.steps)
     torch.cuda.profiler.stop()
@@ -1086,11 +1089,11 @@ def run_model(args):
         with torch.no_grad():
             return model(coords, x, graph)
 
+    clk = ClockSampler(gpu_index_for(local))      # started before the warm-up (see run_ours)
+    clk.start()
     for _ in range(max(3, args.warmup)):
         step()
     barrier(pg)
-    clk = ClockSampler(gpu_index_for(local))
-    clk.start()
     n_l0 = lib.feq_launch_count()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier(pg)
@@ -1228,11 +1231,11 @@ def giant_measure(args, world, rank, local, pg, n, steps, warmup, e2e_steps):
         with torch.no_grad():
             return model(coords_d, x_own, part)
 
+    clk = ClockSampler(gpu_index_for(local))      # started before the warm-up (see run_ours)
+    clk.start()
     for _ in range(max(3, warmup)):
         step()
     barrier(pg)
-    clk = ClockSampler(gpu_index_for(local))
-    clk.start()
     n0 = lib.feq_launch_count()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier(pg)

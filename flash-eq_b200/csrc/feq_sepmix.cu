@@ -28,6 +28,9 @@
 //               edge's scalars (bin, t, s = d / (d + sh_scale), the trig of the rotations)
 //               and a bulk copy of its input row x[src[e]] into a ring of row buffers, so
 //               that enough bytes are in flight to cover the HBM latency
+//               (at L >= 3 the loader only bins the edge and issues its copies: the rotation
+//               warp forms the trig and the M_l nonzeros of its edge with all 32 lanes, since a
+//               short ring of large rows would leave the lane-per-edge loader only a few edges)
 //   warps 2..5  rotation in: rotate two channels per lane with the factored Wigner blocks,
 //               write bf16 (hi, and lo in bf16x3 mode) into the K-major 128-byte-swizzled
 //               N-side tile; per edge also the lerped g_k for the epilogue
@@ -259,17 +262,16 @@ __device__ __forceinline__ void load_m(const float *__restrict__ src, float (&m)
 }
 
 // One irrep of degree Lg through D = R(phi) M R(phi)^T with the nonzeros of M (s^l folded
-// in) read from msm; cp / sp: cos / sin of m phi.  Two channels (emit(o, y0, y1)).
+// in) given in registers; cp / sp: cos / sin of m phi.  Two channels (emit(o, y0, y1)).
 template <int Lg, bool kT, typename Get, typename Emit>
-__device__ __forceinline__ void rot2_pre(const float *__restrict__ msm, const float *__restrict__ cp,
-                                         const float *__restrict__ sp, Get get, Emit emit) {
+__device__ __forceinline__ void rot2_m(const float (&m)[Lg == 0 ? 1 : WA<(Lg > 0 ? Lg : 1)>::kNnz],
+                                       const float *__restrict__ cp, const float *__restrict__ sp, Get get,
+                                       Emit emit) {
     if constexpr (Lg == 0) {
         const float2 v = get(0);
         emit(0, v.x, v.y);
     } else {
         constexpr int N = 2 * Lg + 1;
-        float m[WA<Lg>::kNnz];
-        load_m(msm, m);
         float g0[N], g1[N];
 #pragma unroll
         for (int q = 0; q < N; q++) {
@@ -306,6 +308,20 @@ __device__ __forceinline__ void rot2_pre(const float *__restrict__ msm, const fl
         }
 #pragma unroll
         for (int o = 0; o < N; o++) emit(o, h0[o], h1[o]);
+    }
+}
+
+// The same with the nonzeros of M read from msm (shared memory).
+template <int Lg, bool kT, typename Get, typename Emit>
+__device__ __forceinline__ void rot2_pre(const float *__restrict__ msm, const float *__restrict__ cp,
+                                         const float *__restrict__ sp, Get get, Emit emit) {
+    if constexpr (Lg == 0) {
+        const float2 v = get(0);
+        emit(0, v.x, v.y);
+    } else {
+        float m[WA<Lg>::kNnz];
+        load_m(msm, m);
+        rot2_m<Lg, kT>(m, cp, sp, get, emit);
     }
 }
 
@@ -431,6 +447,45 @@ __device__ __forceinline__ void rotate_in_all(const float *__restrict__ rec, con
     }
 }
 
+// As rotate_in_all, but the warp forms the M_l nonzeros of every degree itself from the edge's
+// trig (tv) and s (every lane the same values), rotates with them from registers and stores them
+// at rec + REC_M for the epilogue's rotation back.
+template <class GE, int L, bool kSplit>
+__device__ __forceinline__ void rotate_in_all_m(const float *__restrict__ tv, float s, float *__restrict__ rec,
+                                                const float *__restrict__ cp, const float *__restrict__ sp,
+                                                const float *__restrict__ f0, const float *__restrict__ f1,
+                                                uint8_t *bhi, uint8_t *blo, const uint32_t (&xo)[8]) {
+    if constexpr (L <= GE::LI) {
+        constexpr int off = L * L;
+        auto get = [&](int q) { return make_float2(f0[off + q], f1[off + q]); };
+        auto emit = [&](int o, float y0, float y1) {
+            const int jm = GE::mf_in(L, o - L);
+            const uint32_t bo = (uint32_t)jm * 128u + xo[jm & 7];
+            const __nv_bfloat162 hi = __floats2bfloat162_rn(y0, y1);
+            *reinterpret_cast<__nv_bfloat162 *>(bhi + bo) = hi;
+            if (kSplit) {
+                const float2 hf = __bfloat1622float2(hi);
+                *reinterpret_cast<__nv_bfloat162 *>(blo + bo) = __floats2bfloat162_rn(y0 - hf.x, y1 - hf.y);
+            }
+        };
+        if constexpr (L == 0) {
+            float m0[1] = {1.0f};
+            rot2_m<0, false>(m0, cp, sp, get, emit);
+        } else {
+            constexpr int NZ = WA<L>::kNnz;
+            float m[NZ];
+            WA<L>::wm(tv, ipowf(s, L), m);
+            float *dst = rec + GE::REC_M + GE::moff(L);
+#pragma unroll
+            for (int v = 0; v + 3 < NZ; v += 4) *reinterpret_cast<float4 *>(dst + v) = make_float4(m[v], m[v + 1], m[v + 2], m[v + 3]);
+#pragma unroll
+            for (int v = (NZ / 4) * 4; v < NZ; v++) dst[v] = m[v];
+            rot2_m<L, false>(m, cp, sp, get, emit);
+        }
+        rotate_in_all_m<GE, L + 1, kSplit>(tv, s, rec, cp, sp, f0, f1, bhi, blo, xo);
+    }
+}
+
 // Output rotation of every degree of [0..LOUT] for one channel of one edge, into the
 // staging row (standard order).
 template <class GE, int L>
@@ -466,6 +521,10 @@ sep_edgewise_kernel(const __grid_constant__ SepParams P) {
     constexpr int JS = GE::JOB_FLOATS;
     constexpr int FRB = 2 * kRank * GE::W * 4;                        // bytes of two rows of f
     constexpr int FR = (2 * kRank * GE::W + 3) & ~3;
+    // L >= 3: the per-edge trig and M_l nonzeros are formed by the rotation warp (32 lanes per
+    // edge) instead of the loader (a lane per edge): with the short row ring of large rows the
+    // loader would otherwise prepare only a few edges at a time.
+    constexpr bool kRotRec = GE::LMAX >= 3;
     static_assert(TE % kNumRot == 0 && TE % kG == 0, "tile edges split over the warps");
 
     extern __shared__ uint8_t smem_raw[];
@@ -601,15 +660,16 @@ sep_edgewise_kernel(const __grid_constant__ SepParams P) {
             }
         };
         fetch(0);
-        for (int64_t base = 0; base < n_jobs; base += NB) {
+        uint32_t bidx = 0;
+        for (int64_t base = 0; base < n_jobs; base += NB, bidx++) {
             const float dd = nd, vx = nx, vy = ny, vz = nz;
             const int64_t row = nrow;
             fetch(base + NB);
             const int64_t j = base + lane;
             bool ok = true;
             if (lane < NB && j < n_jobs) {
-                const int r = (int)(j % NR);
-                if (j >= NR) ok = mbar_wait(&r_free[r], (uint32_t)((j / NR - 1) & 1), abort_flag, P.wait_ns);
+                const int r = (int)(bidx & 1u) * NB + lane;
+                if (bidx >= 2) ok = mbar_wait(&r_free[r], ((bidx >> 1) - 1u) & 1u, abort_flag, P.wait_ns);
                 if (ok) {
                     float *sc = jobs + (size_t)r * JS;
                     int *sci = reinterpret_cast<int *>(sc);
@@ -619,15 +679,21 @@ sep_edgewise_kernel(const __grid_constant__ SepParams P) {
                     if (e < P.E) {
                         float t;
                         bin_of(dd, P.bins, lo, t);
-                        float tr[GE::TF];
-                        edge_trig_compact(vx, vy, vz, GE::LMAX, tr);
-#pragma unroll
-                        for (int q = 0; q < GE::TF; q++) sc[GE::REC_TRIG + q] = tr[q];
                         const float sw = dd / (dd + P.sh_scale);
+                        if constexpr (kRotRec) {          // the rotation warp derives the rest
+                            sc[GE::REC_TRIG] = vx;
+                            sc[GE::REC_TRIG + 1] = vy;
+                            sc[GE::REC_TRIG + 2] = vz;
+                        } else {
+                            float tr[GE::TF];
+                            edge_trig_compact(vx, vy, vz, GE::LMAX, tr);
+#pragma unroll
+                            for (int q = 0; q < GE::TF; q++) sc[GE::REC_TRIG + q] = tr[q];
+                            fill_m<GE, 1>(tr, sw, sc);
+                        }
                         sc[GE::REC_S] = sw;
                         sc[GE::REC_T] = t;
                         sci[GE::REC_LO] = lo;
-                        fill_m<GE, 1>(tr, sw, sc);
                         if (row < 0 || row >= P.nsrc) {
                             set_status(P.status, 1);
                             flag = 1;
@@ -664,12 +730,19 @@ sep_edgewise_kernel(const __grid_constant__ SepParams P) {
 #pragma unroll
         for (int k = 0; k < 8; k++) xo[k] = (uint32_t)((((lane >> 2) ^ k) << 4) + ((2 * lane) & 7) * 2);
         const int64_t n_mine = n_local * EPW;
+        const int NT = NR / TE;
+        int ti = 0;
+        uint32_t pass = 0;
         for (int64_t q = 0; q < n_mine; q++) {
             const int64_t i = q / EPW;
             const int st = (int)(i % kStages), slot = (int)(i % kSlots);
-            const int el = w + kNumRot * (int)(q - i * EPW);
-            const int64_t j = i * TE + el;
-            const int r = (int)(j % NR);
+            const int sub = (int)(q - i * EPW);
+            const int el = w + kNumRot * sub;
+            if (q > 0 && sub == 0 && ++ti == NT) {
+                ti = 0;
+                pass++;
+            }
+            const int r = ti * TE + el;
             if (q % EPW == 0) {       // first edge of this warp in tile i: wait for its buffers
                 if (i >= kStages &&
                     !mbar_wait(&b_empty[st], (uint32_t)((i / kStages - 1) & 1), abort_flag, P.wait_ns))
@@ -677,19 +750,28 @@ sep_edgewise_kernel(const __grid_constant__ SepParams P) {
                 if (i >= kSlots && !mbar_wait(&s_empty[slot], (uint32_t)((i / kSlots - 1) & 1), abort_flag, P.wait_ns))
                     break;
             }
-            if (!mbar_wait(&r_full[r], (uint32_t)((j / NR) & 1), abort_flag, P.wait_ns)) {
+            if (!mbar_wait(&r_full[r], pass & 1u, abort_flag, P.wait_ns)) {
                 set_status(P.status, 2);
                 break;
             }
             const float *sc = jobs + (size_t)r * JS;
             const int flag = reinterpret_cast<const int *>(sc)[GE::REC_FLAG];
             if (flag != 2) {
-                const int64_t e = edge_of_job(j);
+                const int64_t e = edge_of_job(i * TE + el);
                 float *sl = slots + (size_t)(slot * TE + el) * GE::SLOT_EDGE;
                 float tr[GE::TF];
-                load_regs<GE::TF>(sc + GE::REC_TRIG, tr);
                 const float t = sc[GE::REC_T];
-                for (int qq = lane; qq < GE::REC_FLOATS; qq += 32) sl[qq] = sc[qq];   // record for the epilogue
+                if constexpr (kRotRec) {
+                    // every lane forms the edge's trig (the same values); the record for the
+                    // epilogue gets it here and the M_l nonzeros in rotate_in_all_m
+                    edge_trig_compact(sc[GE::REC_TRIG], sc[GE::REC_TRIG + 1], sc[GE::REC_TRIG + 2], GE::LMAX, tr);
+#pragma unroll
+                    for (int q = 0; q < GE::TF; q++) sl[GE::REC_TRIG + q] = tr[q];
+                    if (lane < 4) sl[GE::REC_S + lane] = sc[GE::REC_S + lane];     // s, t, bin, flag
+                } else {
+                    load_regs<GE::TF>(sc + GE::REC_TRIG, tr);
+                    for (int qq = lane; qq < GE::REC_FLOATS; qq += 32) sl[qq] = sc[qq];   // record for the epilogue
+                }
                 // g_k = (1 - t) f[lo, k] + t f[lo + 1, k], per block padded to 4 floats (the two
                 // rows of f arrived with the input row)
                 constexpr int GI = (kRank * GE::GP + 31) / 32;
@@ -725,7 +807,11 @@ sep_edgewise_kernel(const __grid_constant__ SepParams P) {
                 const int c = 2 * lane;
                 const float *cp = tr + 2 * GE::LMAX + 1, *sp = cp + GE::LMAX + 1;
                 uint8_t *rb = bh + el * ES * 128;
-                rotate_in_all<GE, 0, kSplit>(sc, cp, sp, fb + c * DIN, fb + (c + 1) * DIN, rb, rb + kTileBytes, xo);
+                if constexpr (kRotRec)
+                    rotate_in_all_m<GE, 0, kSplit>(tr, sc[GE::REC_S], sl, cp, sp, fb + c * DIN, fb + (c + 1) * DIN, rb,
+                                                   rb + kTileBytes, xo);
+                else
+                    rotate_in_all<GE, 0, kSplit>(sc, cp, sp, fb + c * DIN, fb + (c + 1) * DIN, rb, rb + kTileBytes, xo);
                 {
                     const float omt = 1.0f - t;
 #pragma unroll

@@ -28,10 +28,12 @@ from .radial import SeparableRadialNet
 
 
 DEFAULT_MIX_PRECISION = "bf16x3"
-# Highest degree for which the layer takes the one-kernel separable path on the GPU.  Above it
-# the binned three-kernel pipeline is faster on a B200 (config 2, L <= 4, mult 64: 6.8 ms
-# against 8.6 ms per 640 000 edges); at L <= 2 the one-kernel path is faster.
-SEPARABLE_MAX_L = 2
+# Highest degree, per mix mode, for which the layer takes the one-kernel separable path on the
+# GPU (lvals [0..L], mult 64).  Measured on a B200 at 640 000 edges of the config-2 graph, the
+# one-kernel path against the binned three-kernel pipeline: bf16x3 L <= 2 1.49 / 2.38 ms,
+# L = 3 4.41 / 8.36 ms, L = 4 6.18 / 7.32 ms; bf16 L = 3 4.09 / 7.41 ms, but L = 4 6.03 /
+# 5.05 ms, so bf16 at L = 4 stays on the binned pipeline.
+SEPARABLE_MAX_L = {"bf16x3": 4, "bf16": 3}
 
 
 def _dense(M):
@@ -112,7 +114,7 @@ class EquivariantEdgewiseLinear(nn.Module):
         CUDA float32 input); cached per mix mode."""
         if not (x.is_cuda and x.dtype == torch.float32):
             return False
-        if max(self._lin + self._lout) > SEPARABLE_MAX_L:
+        if max(self._lin + self._lout) > SEPARABLE_MAX_L.get(self.mix_precision, -1):
             return False
         key = self.mix_precision
         cache = self.__dict__.setdefault("_sep_cache", {})
