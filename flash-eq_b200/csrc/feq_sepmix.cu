@@ -63,7 +63,7 @@ constexpr int kNumEpi = 4;   // warps per epilogue warpgroup (one per TMEM lane 
 __host__ __device__ constexpr int threads_for(int ewg, int nrot) { return (kRotWarp0 + nrot + kNumEpi * ewg) * 32; }
 constexpr int kMaxRing = 32;    // input rows in flight per CTA (bulk copies), at most
 constexpr int kStages = 2;      // N-side tiles
-constexpr int kSlots = 4;       // per-tile edge scalars
+constexpr int kMaxSlots = 4;    // per-tile edge scalars (Geo::SLOTS of them)
 constexpr int kBufs = 2;        // TMEM accumulator sets
 constexpr int kCin = 64;        // K (one 128-byte swizzle row of bf16)
 constexpr int kCout = 64;
@@ -142,7 +142,18 @@ struct Geo {
     static constexpr int SLOT_G = REC_FLOATS;
     static constexpr int SLOT_EDGE = SLOT_G + kRank * GP;     // floats per edge
     static constexpr int STAGE_ROW = ((kCout * DOUT + 15) / 32) * 32 + 16;   // == 16 mod 32 floats
-    static constexpr int JOB_FLOATS = REC_FLOATS;
+    // L >= 3 (ROTREC): the rotation warp forms the trig and the M_l nonzeros of its edge and
+    // reads the edge's two rows of radial features from L2 itself, so a ring entry carries only
+    // the input row and a short job (direction, s, t, bin, flag).  This keeps entries small
+    // enough for a ring that prefetches (8 rows at L = 4, bf16x3).  Below, the loader forms the
+    // whole record and the feature rows travel in the ring.
+    static constexpr bool ROTREC = LMAX >= 3;
+    static constexpr int J_S = ROTREC ? 3 : REC_S, J_T = J_S + 1, J_LO = J_S + 2, J_FLAG = J_S + 3;
+    static constexpr int JOB_FLOATS = ROTREC ? 8 : REC_FLOATS;
+    static constexpr int FR = ROTREC ? 0 : (2 * kRank * W + 3) & ~3;     // feature-row floats per entry
+    // per-tile slots of edge scalars: 4, or 3 at L >= 3 where shared memory is short (the
+    // rotation warps then run at most 3 tiles ahead of the epilogue)
+    static constexpr int SLOTS = ROTREC ? 3 : 4;
 };
 
 struct SepParams {
@@ -520,11 +531,11 @@ sep_edgewise_kernel(const __grid_constant__ SepParams P) {
     constexpr int kSplitN = kSplit ? 2 : 1;
     constexpr int JS = GE::JOB_FLOATS;
     constexpr int FRB = 2 * kRank * GE::W * 4;                        // bytes of two rows of f
-    constexpr int FR = (2 * kRank * GE::W + 3) & ~3;
+    constexpr int FR = GE::FR;
     // L >= 3: the per-edge trig and M_l nonzeros are formed by the rotation warp (32 lanes per
-    // edge) instead of the loader (a lane per edge): with the short row ring of large rows the
+    // edge) instead of the loader (a lane per edge): with a short row ring of large rows the
     // loader would otherwise prepare only a few edges at a time.
-    constexpr bool kRotRec = GE::LMAX >= 3;
+    constexpr bool kRotRec = GE::ROTREC;
     static_assert(TE % kNumRot == 0 && TE % kG == 0, "tile edges split over the warps");
 
     extern __shared__ uint8_t smem_raw[];
@@ -533,22 +544,22 @@ sep_edgewise_kernel(const __grid_constant__ SepParams P) {
     uint8_t *a_lo = a_hi + kSlices * kTileBytes;                      // (split only)
     uint8_t *b_base = a_hi + kSplitN * kSlices * kTileBytes;          // kStages x (hi [, lo])
     float *slots = reinterpret_cast<float *>(b_base + kStages * kSplitN * kTileBytes);
-    float *stage = slots + kSlots * TE * GE::SLOT_EDGE;
+    float *stage = slots + GE::SLOTS * TE * GE::SLOT_EDGE;
     float *jobs = stage + EWG * kG * GE::STAGE_ROW;                   // nr x JS per-edge records
     float *frows = jobs + (size_t)P.nr * JS;                          // nr x FR: rows lo, lo + 1 of f
     float *rows = frows + (size_t)P.nr * FR;                          // nr input rows
 
-    __shared__ uint64_t b_full[kStages], b_empty[kStages], t_full[kBufs], t_empty[kBufs], s_empty[kSlots];
+    __shared__ uint64_t b_full[kStages], b_empty[kStages], t_full[kBufs], t_empty[kBufs], s_empty[kMaxSlots];
     __shared__ uint64_t r_full[kMaxRing], r_free[kMaxRing], drain_bar;
     __shared__ int64_t r_issued[kMaxRing];
     __shared__ int16_t gidx_s[kRank * GE::GP];     // g slot -> index into one bin row of f (-1: pad)
     __shared__ uint32_t tmem_base_s;
-    __shared__ int abort_s, epi_stop_s;
+    __shared__ int abort_s, epi_stop_s[4];    // per epilogue warpgroup
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int NR = P.nr;
     if (threadIdx.x == 0) {
-        epi_stop_s = 0;
+        for (int i = 0; i < 4; i++) epi_stop_s[i] = 0;
         for (int i = 0; i < kStages; i++) {
             mbar_init(&b_full[i], kNumRot);
             mbar_init(&b_empty[i], 1);
@@ -557,7 +568,7 @@ sep_edgewise_kernel(const __grid_constant__ SepParams P) {
             mbar_init(&t_full[i], 1);
             mbar_init(&t_empty[i], kNumEpi * EWG);
         }
-        for (int i = 0; i < kSlots; i++) mbar_init(&s_empty[i], kNumEpi * EWG);
+        for (int i = 0; i < GE::SLOTS; i++) mbar_init(&s_empty[i], kNumEpi * EWG);
         for (int i = 0; i < kMaxRing; i++) {
             mbar_init(&r_full[i], 1);
             mbar_init(&r_free[i], 1);
@@ -691,9 +702,9 @@ sep_edgewise_kernel(const __grid_constant__ SepParams P) {
                             for (int q = 0; q < GE::TF; q++) sc[GE::REC_TRIG + q] = tr[q];
                             fill_m<GE, 1>(tr, sw, sc);
                         }
-                        sc[GE::REC_S] = sw;
-                        sc[GE::REC_T] = t;
-                        sci[GE::REC_LO] = lo;
+                        sc[GE::J_S] = sw;
+                        sc[GE::J_T] = t;
+                        sci[GE::J_LO] = lo;
                         if (row < 0 || row >= P.nsrc) {
                             set_status(P.status, 1);
                             flag = 1;
@@ -701,13 +712,16 @@ sep_edgewise_kernel(const __grid_constant__ SepParams P) {
                             flag = 0;
                         }
                     }
-                    sci[GE::REC_FLAG] = flag;
+                    sci[GE::J_FLAG] = flag;
                     r_issued[r] = j;
-                    if (flag != 2) {
-                        // the edge's two rows of radial features (bins lo, lo + 1) and its input row
+                    constexpr uint32_t kFrb = FR > 0 ? FRB : 0;
+                    if (flag == 0 || (flag == 1 && FR > 0)) {
+                        // the edge's input row, and (L <= 2) its two rows of radial features
+                        // (bins lo, lo + 1)
                         fence_async_smem();
-                        mbar_arrive_expect_tx(&r_full[r], FRB + (flag == 0 ? ROWF * 4 : 0));
-                        bulk_load(frows + (size_t)r * FR, P.ftab + (int64_t)lo * kRank * GE::W, FRB, &r_full[r]);
+                        mbar_arrive_expect_tx(&r_full[r], kFrb + (flag == 0 ? ROWF * 4 : 0));
+                        if constexpr (FR > 0)
+                            bulk_load(frows + (size_t)r * FR, P.ftab + (int64_t)lo * kRank * GE::W, FRB, &r_full[r]);
                         if (flag == 0)
                             bulk_load(rows + (size_t)r * ROWF_PAD, P.x + row * (int64_t)ROWF, ROWF * 4, &r_full[r]);
                     } else {
@@ -735,7 +749,7 @@ sep_edgewise_kernel(const __grid_constant__ SepParams P) {
         uint32_t pass = 0;
         for (int64_t q = 0; q < n_mine; q++) {
             const int64_t i = q / EPW;
-            const int st = (int)(i % kStages), slot = (int)(i % kSlots);
+            const int st = (int)(i % kStages), slot = (int)(i % GE::SLOTS);
             const int sub = (int)(q - i * EPW);
             const int el = w + kNumRot * sub;
             if (q > 0 && sub == 0 && ++ti == NT) {
@@ -747,7 +761,8 @@ sep_edgewise_kernel(const __grid_constant__ SepParams P) {
                 if (i >= kStages &&
                     !mbar_wait(&b_empty[st], (uint32_t)((i / kStages - 1) & 1), abort_flag, P.wait_ns))
                     break;
-                if (i >= kSlots && !mbar_wait(&s_empty[slot], (uint32_t)((i / kSlots - 1) & 1), abort_flag, P.wait_ns))
+                if (i >= GE::SLOTS &&
+                    !mbar_wait(&s_empty[slot], (uint32_t)((i / GE::SLOTS - 1) & 1), abort_flag, P.wait_ns))
                     break;
             }
             if (!mbar_wait(&r_full[r], pass & 1u, abort_flag, P.wait_ns)) {
@@ -755,29 +770,33 @@ sep_edgewise_kernel(const __grid_constant__ SepParams P) {
                 break;
             }
             const float *sc = jobs + (size_t)r * JS;
-            const int flag = reinterpret_cast<const int *>(sc)[GE::REC_FLAG];
+            const int flag = reinterpret_cast<const int *>(sc)[GE::J_FLAG];
             if (flag != 2) {
                 const int64_t e = edge_of_job(i * TE + el);
                 float *sl = slots + (size_t)(slot * TE + el) * GE::SLOT_EDGE;
                 float tr[GE::TF];
-                const float t = sc[GE::REC_T];
+                const float t = sc[GE::J_T];
                 if constexpr (kRotRec) {
                     // every lane forms the edge's trig (the same values); the record for the
                     // epilogue gets it here and the M_l nonzeros in rotate_in_all_m
                     edge_trig_compact(sc[GE::REC_TRIG], sc[GE::REC_TRIG + 1], sc[GE::REC_TRIG + 2], GE::LMAX, tr);
 #pragma unroll
                     for (int q = 0; q < GE::TF; q++) sl[GE::REC_TRIG + q] = tr[q];
-                    if (lane < 4) sl[GE::REC_S + lane] = sc[GE::REC_S + lane];     // s, t, bin, flag
+                    if (lane < 4) sl[GE::REC_S + lane] = sc[GE::J_S + lane];     // s, t, bin, flag
                 } else {
                     load_regs<GE::TF>(sc + GE::REC_TRIG, tr);
                     for (int qq = lane; qq < GE::REC_FLOATS; qq += 32) sl[qq] = sc[qq];   // record for the epilogue
                 }
-                // g_k = (1 - t) f[lo, k] + t f[lo + 1, k], per block padded to 4 floats (the two
-                // rows of f arrived with the input row)
+                // g_k = (1 - t) f[lo, k] + t f[lo + 1, k], per block padded to 4 floats
                 constexpr int GI = (kRank * GE::GP + 31) / 32;
                 float gl[GI], gh[GI];
                 {
-                    const float *f_lo = frows + (size_t)r * FR, *f_hi = f_lo + kRank * GE::W;
+                    const float *f_lo;
+                    if constexpr (FR > 0)           // arrived with the input row
+                        f_lo = frows + (size_t)r * FR;
+                    else                            // read from L2 (the table is small)
+                        f_lo = P.ftab + (int64_t)reinterpret_cast<const int *>(sc)[GE::J_LO] * kRank * GE::W;
+                    const float *f_hi = f_lo + kRank * GE::W;
 #pragma unroll
                     for (int u = 0; u < GI; u++) {
                         const int idx = lane + 32 * u;
@@ -808,7 +827,7 @@ sep_edgewise_kernel(const __grid_constant__ SepParams P) {
                 const float *cp = tr + 2 * GE::LMAX + 1, *sp = cp + GE::LMAX + 1;
                 uint8_t *rb = bh + el * ES * 128;
                 if constexpr (kRotRec)
-                    rotate_in_all_m<GE, 0, kSplit>(tr, sc[GE::REC_S], sl, cp, sp, fb + c * DIN, fb + (c + 1) * DIN, rb,
+                    rotate_in_all_m<GE, 0, kSplit>(tr, sc[GE::J_S], sl, cp, sp, fb + c * DIN, fb + (c + 1) * DIN, rb,
                                                    rb + kTileBytes, xo);
                 else
                     rotate_in_all<GE, 0, kSplit>(sc, cp, sp, fb + c * DIN, fb + (c + 1) * DIN, rb, rb + kTileBytes, xo);
@@ -838,20 +857,38 @@ sep_edgewise_kernel(const __grid_constant__ SepParams P) {
         const int bar_id = 3 + wg;                     // named barrier of the warpgroup
         const bool leader = warp == kEpiWarp0 + kNumEpi * wg && lane == 0;
         float *my_stage = stage + wg * kG * GE::STAGE_ROW;
+        // When the groups of a tile split evenly over the warpgroups, warpgroup wg takes groups
+        // wg, wg + EWG, ... of every tile and all epilogue warps meet once per tile.  Otherwise
+        // (three warpgroups, four groups per tile) the groups go round-robin over all tiles
+        // (group i * GPT + gi to warpgroup (i * GPT + gi) mod EWG) and each warpgroup meets only
+        // itself, so none waits for the others.  Either way every warp waits for every tile's
+        // accumulators and releases them, so a release never precedes the tile's MMAs.
+        constexpr int GPT = TE / kG;
+        constexpr bool kRoundRobin = GPT % EWG != 0;
+        const int stop_ix = kRoundRobin ? wg : 0;
+        int rr = 0;
         for (int64_t i = 0; i < n_local; i++) {
-            const int buf = (int)(i % kBufs), slot = (int)(i % kSlots);
-            // The four epilogue warps meet at named barriers below, so they must leave the
-            // loop together: a failed wait in any of them stops all four.
+            const int buf = (int)(i % kBufs), slot = (int)(i % GE::SLOTS);
+            // The warps that meet at named barriers below must leave the loop together: a failed
+            // wait in any of them stops all of them.
             if (!mbar_wait(&t_full[buf], (uint32_t)((i / kBufs) & 1), abort_flag, P.wait_ns) && lane == 0)
-                epi_stop_s = 1;
-            named_bar(2, EWG * kNumEpi * 32);
-            if (*reinterpret_cast<volatile int *>(&epi_stop_s)) break;
+                epi_stop_s[stop_ix] = 1;
+            if (kRoundRobin)
+                named_bar(bar_id, kNumEpi * 32);
+            else
+                named_bar(2, EWG * kNumEpi * 32);
+            if (*reinterpret_cast<volatile int *>(&epi_stop_s[stop_ix])) break;
             tc_fence_after();
             const int64_t e0 = (blockIdx.x + i * gridDim.x) * TE;
             const float *slot_base = slots + (size_t)slot * TE * GE::SLOT_EDGE;
             const uint32_t tbase = tmem + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(buf * kSlices * 128);
 #pragma unroll 1
-            for (int gi = wg; gi < TE / kG; gi += EWG) {
+            for (int gi = kRoundRobin ? 0 : wg; gi < GPT; gi += kRoundRobin ? 1 : EWG) {
+                if (kRoundRobin) {
+                    const bool mine = rr == wg;
+                    rr = rr + 1 == EWG ? 0 : rr + 1;
+                    if (!mine) continue;
+                }
                 // every lane of a pair computes its k's share of both edges of the group; the
                 // pair sums its shares, and lane kk keeps edge gi * kG + kk
                 float hf[DOUT];
@@ -928,14 +965,14 @@ size_t smem_fixed_bytes() {
     size_t b = 1024;                                                     // alignment slack
     b += (size_t)kSplitN * kSlices * kTileBytes;                         // M side
     b += (size_t)kStages * kSplitN * kTileBytes;                         // N side
-    b += (size_t)kSlots * GE::TE * GE::SLOT_EDGE * 4;                    // per-tile slots
+    b += (size_t)GE::SLOTS * GE::TE * GE::SLOT_EDGE * 4;                 // per-tile slots
     b += (size_t)EWG * kG * GE::STAGE_ROW * 4;                           // output staging
     return b;
 }
 template <int LIN, int LOUT>
 size_t ring_entry_bytes() {
     using GE = Geo<LIN, LOUT>;
-    return ((size_t)((kCin * GE::DIN + 3) & ~3) + GE::JOB_FLOATS + ((2 * kRank * GE::W + 3) & ~3)) * 4;
+    return ((size_t)((kCin * GE::DIN + 3) & ~3) + GE::JOB_FLOATS + GE::FR) * 4;
 }
 
 constexpr size_t kSmemPerBlock = 227 * 1024;     // dynamic + static shared memory of one CTA
@@ -975,10 +1012,10 @@ int launch(SepParams P, cudaStream_t stream) {
 // (LIN, LOUT) pairs this build instantiates: lvals [0..L] in and out, L <= 4.
 template <bool kSplit>
 int dispatch(int lin, int lout, const SepParams &P, cudaStream_t s) {
-    // as many warps as the registers allow: L <= 2 (<= 100 registers) 8 rotation warps and two
+    // as many warps as the registers allow: L <= 2 (80 registers) 8 rotation warps and three
     // epilogue warpgroups, L = 3 (128) 4 and two, L = 4 (168) 4 and one
-    if (lin == 1 && lout == 1) return launch<1, 1, kSplit, 2, 8>(P, s);
-    if (lin == 2 && lout == 2) return launch<2, 2, kSplit, 2, 8>(P, s);
+    if (lin == 1 && lout == 1) return launch<1, 1, kSplit, 3, 8>(P, s);
+    if (lin == 2 && lout == 2) return launch<2, 2, kSplit, 3, 8>(P, s);
     if (lin == 3 && lout == 3) return launch<3, 3, kSplit, 2, 4>(P, s);
     if (lin == 4 && lout == 4) return launch<4, 4, kSplit, 1, 4>(P, s);
     return FEQ_ERR_UNSUPPORTED;
