@@ -700,15 +700,39 @@ def node_rep_norm(x, lvals, eps):
     return norms.view(*x.shape[:-1], n)
 
 
+NODE_LINEAR_MIX = "bf16x3"      # tensor-core arithmetic of feq_node_linear_tc (float32-level accuracy)
+
+
+def node_linear_tc_supported(lvals, c_in, c_out, mix=NODE_LINEAR_MIX) -> bool:
+    """Whether feq_node_linear_tc serves this shape (else the three-step path)."""
+    arr, n = _lib.i32_array(lvals)
+    return _lib.load().feq_node_linear_tc_workspace_bytes(int(c_in), int(c_out), arr, n, _lib.FEQ_MIX[mix]) > 0
+
+
 def node_linear(x, lvals, weight, bias, c_out, scalar_index):
     """EquivariantLinear forward (identity activation): (..., Cin, d) -> (..., Cout, d).
-    Position-major layout kernels around one library GEMM per irrep; ``scalar_index``:
-    (d,) int8 device tensor, position -> bias column (-1 elsewhere)."""
+
+    One tensor-core kernel (feq_node_linear_tc, bf16x3) where it serves the shape; otherwise
+    position-major layout kernels around one library GEMM per irrep.  ``scalar_index``: (d,)
+    int8 device tensor, position -> bias column (-1 elsewhere)."""
     lib = _require_cuda(x, weight, bias)
     rows = _node_rows(x, "features")
     N, cin, d = rows.shape
     cout = int(c_out)
     dev = rows.device
+    arr, n = _lib.i32_array(lvals)
+    mode = _lib.FEQ_MIX[NODE_LINEAR_MIX]
+    wsb = lib.feq_node_linear_tc_workspace_bytes(cin, cout, arr, n, mode)
+    if wsb > 0:
+        rows = _aligned16(rows)
+        y = torch.empty(N, cout, d, dtype=torch.float32, device=dev)
+        ws = _workspace(wsb, dev)
+        w = _f32(weight, "weight").contiguous()
+        b = None if bias is None else _f32(bias, "bias").contiguous()
+        rc = lib.feq_node_linear_tc(_p(rows), N, cin, cout, arr, n, _p(w), _p(b), mode, _p(y), _p(ws), wsb, None,
+                                    _stream(dev))
+        _lib.check(rc, "feq_node_linear_tc")
+        return y.view(*x.shape[:-2], cout, d)
     xt = torch.empty(d, N, cin, dtype=torch.float32, device=dev)
     rc = lib.feq_node_to_posmajor(_p(rows), N, cin, d, _p(xt), _stream(dev))
     _lib.check(rc, "feq_node_to_posmajor")

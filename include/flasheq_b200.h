@@ -457,6 +457,20 @@ int feq_node_rep_norm(const float *x, int64_t num_nodes, int32_t C, const int32_
 int feq_node_to_posmajor(const float *x, int64_t num_nodes, int32_t C, int32_t d, float *xt, feq_stream_t stream);
 int feq_node_from_posmajor(const float *yt, int64_t num_nodes, int32_t C, const int32_t *lvals, int32_t n_lvals,
                            const float *bias, const int8_t *scalar_index, float *y, feq_stream_t stream);
+/* EquivariantLinear (linear.py:172-268) as one tensor-core (tcgen05) kernel: y (N, c_out, d)
+ * = per irrep r, W_r x over the positions of r, plus bias[co] at the l = 0 position; x
+ * (N, c_in, d) node rows, weight (n_lvals, c_out, c_in) float32 (the module's weight viewed per
+ * irrep), bias (c_out,) or NULL.  mix_mode FEQ_MIX_BF16X3 (float32-level accuracy) or
+ * FEQ_MIX_BF16.  Shapes served: lvals [0..L] with L <= 2 and (c_in, c_out) in {(64, 64),
+ * (64, 128), (128, 64)} (FEQ_ERR_UNSUPPORTED otherwise: use the three-step path above).  The
+ * workspace (feq_node_linear_tc_workspace_bytes, 16-byte aligned) receives the weights re-laid
+ * as tensor-core tiles; x and y 16-byte aligned; status (may be NULL) is set to 2 when a
+ * pipeline wait ran out (feq_set_wait_limit_ns). */
+size_t feq_node_linear_tc_workspace_bytes(int32_t c_in, int32_t c_out, const int32_t *lvals, int32_t n_lvals,
+                                          int32_t mix_mode);
+int feq_node_linear_tc(const float *x, int64_t num_nodes, int32_t c_in, int32_t c_out, const int32_t *lvals,
+                       int32_t n_lvals, const float *weight, const float *bias, int32_t mix_mode, float *y,
+                       void *workspace, size_t workspace_bytes, int32_t *status, feq_stream_t stream);
 /* EquivariantGating's gate (gating.py:17-76): out = x * sigmoid(z)[c, irrep of the
  * position], z (N, C * n_lvals) the pre-activation. */
 int feq_node_gate(const float *x, const float *z, int64_t num_nodes, int32_t C, const int32_t *lvals,

@@ -10,6 +10,7 @@ import pytest
 import torch
 
 import flash_eq as fe
+from flash_eq.cuda import ops
 from conftest import rel_l2
 from flash_eq.layers.gating import EquivariantGating
 from flash_eq.layers.norm import EquivariantLayerNorm, RepNorm, SeparableEquivariantLayerNorm
@@ -105,6 +106,9 @@ def test_equivariant_linear(cuda_device, lv, cin, cout, bias):
     ref = _linear_reference(copy.deepcopy(m).double(), f.double())
     with torch.no_grad():
         y = m.to(cuda_device)(f.to(cuda_device))
-    assert y.shape == ref.shape and rel_l2(y, ref) < 1e-5
+    # shapes the tensor-core kernel serves compute in bf16x3 (float32-level, 1e-4 like the
+    # edge path); the others go through the float32 library GEMM
+    tol = 1e-4 if ops.node_linear_tc_supported(lv, cin, cout) else 1e-5
+    assert y.shape == ref.shape and rel_l2(y, ref) < tol
     yg = m(f.to(cuda_device).requires_grad_())       # the autograd formulation
     assert rel_l2(yg.detach(), ref) < 1e-5
