@@ -18,6 +18,8 @@
 #include <math.h>
 
 #include "feq_internal.cuh"
+#include "feq_rot_common.cuh"
+#include "feq_sm100.cuh"
 
 namespace feq {
 
@@ -513,6 +515,149 @@ attn_pool_warp_kernel(const __grid_constant__ FeqAttnArgs a) {
     }
 }
 
+// The same pooling with the K and V rows of each destination's edges brought into a
+// per-warp ring of kAttnRing shared-memory slots by bulk copies, kAttnRing edges ahead.  The
+// warp-per-edge chain of the kernel above -- perm[pos], then src[e], then the K / V rows,
+// three round trips to L2 or HBM per edge -- is what bounds it; here the lanes load a whole
+// batch of 32 edge ids and src ids with one coalesced load each, and lane 0 keeps the rows of
+// the next kAttnRing edges in flight while the current one is folded in.  Arithmetic, and so
+// the result, is that of attn_pool_warp_kernel.  Every wait is bounded: on time-out the kernel
+// sets status 2, waits for its copies and leaves.
+constexpr int kAttnRing = 4;
+
+template <int S>
+__global__ void __launch_bounds__(128)
+attn_pool_ring_kernel(const __grid_constant__ FeqAttnArgs a, uint64_t wait_ns) {
+    constexpr int ROW = 32 * S;                 // floats of one K or V row
+    constexpr uint32_t RB = ROW * 4;            // bytes of one row
+    extern __shared__ __align__(128) float attn_ring_sm[];
+    __shared__ uint64_t bars[4][kAttnRing];
+    __shared__ int abort_s[4];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float *ring = attn_ring_sm + (size_t)warp * kAttnRing * 2 * ROW;
+    if (lane == 0) {
+        for (int r = 0; r < kAttnRing; r++) sm100::mbar_init(&bars[warp][r], 1);
+        abort_s[warp] = 0;
+        sm100::fence_mbar_init();
+    }
+    __syncwarp();
+    const int64_t n = (int64_t)blockIdx.x * 4 + warp;
+    if (n >= a.num_nodes) return;
+    volatile int *abort_flag = &abort_s[warp];
+    const int qrow = a.c_qk * a.d_qk;
+    const int H = a.num_heads, gl = 32 / H;
+    const bool split_k = a.k != nullptr;
+    const int64_t nsrc = split_k ? a.num_src_nodes : a.num_nodes;
+    const float *kbase = split_k ? a.k : a.qk + qrow;
+    const int64_t k_ld = split_k ? qrow : 2 * (int64_t)qrow;
+    const float *qn = a.qk + n * (int64_t)(split_k ? qrow : 2 * qrow) + lane * S;
+    const bool decay = a.decay_scale > 0.0f && a.distances;
+    float q[S], acc[S];
+#pragma unroll
+    for (int i = 0; i < S; i++) {
+        q[i] = __ldg(qn + i);
+        acc[i] = 0.0f;
+    }
+    float m = -INFINITY, ssum = 0.0f;
+    const int64_t s0 = a.offsets[n], s1 = a.offsets[n + 1];
+    uint32_t issued = 0, used = 0;              // copies issued / consumed by this warp
+    bool ok = true;
+    for (int64_t base = s0; base < s1 && ok; base += 32) {
+        const int cnt = (int)((s1 - base) < 32 ? (s1 - base) : 32);
+        int64_t my_e = 0, my_s = -1;
+        float my_d = 0.0f;
+        if (lane < cnt) {
+            my_e = a.perm[base + lane];
+            my_s = a.src[my_e];
+            if (my_s < 0 || my_s >= nsrc) {
+                set_status(a.status, 1);
+                my_s = -1;
+            }
+            if (decay) my_d = a.distances[my_e];
+        }
+        auto issue = [&](int k) {                // edge k of the batch into the next slot
+            const int64_t e = __shfl_sync(0xffffffffu, my_e, k);
+            const int64_t sidx = __shfl_sync(0xffffffffu, my_s, k);
+            if (lane == 0) {
+                const int slot = (int)(issued % kAttnRing);
+                float *dst = ring + (size_t)slot * 2 * ROW;
+                sm100::mbar_arrive_expect_tx(&bars[warp][slot], sidx >= 0 ? 2 * RB : RB);
+                if (sidx >= 0) rot::bulk_load(dst, kbase + sidx * k_ld, RB, &bars[warp][slot]);
+                rot::bulk_load(dst + ROW, a.v + e * (int64_t)ROW, RB, &bars[warp][slot]);
+            }
+            issued++;
+        };
+        const int pre = cnt < kAttnRing ? cnt : kAttnRing;
+        for (int k = 0; k < pre; k++) issue(k);
+        for (int k = 0; k < cnt; k++) {
+            const int slot = (int)(used % kAttnRing);
+            if (!sm100::mbar_wait(&bars[warp][slot], (used / kAttnRing) & 1u, abort_flag, wait_ns)) {
+                set_status(a.status, 2);
+                ok = false;
+                break;
+            }
+            used++;
+            const float *row = ring + (size_t)slot * 2 * ROW + lane * S;
+            const bool has_k = __shfl_sync(0xffffffffu, my_s, k) >= 0;
+            const float dd = __shfl_sync(0xffffffffu, my_d, k);
+            float kc[S], vc[S];
+#pragma unroll
+            for (int i = 0; i < S; i++) {
+                kc[i] = has_k ? row[i] : 0.0f;
+                vc[i] = row[ROW + i];
+            }
+            // every lane has read the slot: it may be refilled (generic reads before the
+            // async-proxy writes of the next copy)
+            rot::fence_async_smem();
+            __syncwarp();
+            if (k + kAttnRing < cnt) issue(k + kAttnRing);
+            float d0 = 0.0f, d1 = 0.0f;
+#pragma unroll
+            for (int i = 0; i + 1 < S; i += 2) {
+                d0 = fmaf(q[i], kc[i], d0);
+                d1 = fmaf(q[i + 1], kc[i + 1], d1);
+            }
+            if (S & 1) d0 = fmaf(q[S - 1], kc[S - 1], d0);
+            float dot = d0 + d1;
+            for (int o = 1; o < gl; o <<= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+            float lg = dot * a.scale;
+            if (decay) lg -= dd / a.decay_scale;
+            const float mnew = fmaxf(m, lg);
+            const float corr = (m == -INFINITY) ? 0.0f : expf(m - mnew);
+            const float p = expf(lg - mnew);
+            ssum = ssum * corr + p;
+#pragma unroll
+            for (int i = 0; i < S; i++) acc[i] = fmaf(p, vc[i], acc[i] * corr);
+            m = mnew;
+        }
+    }
+    if (!ok) {                                   // copies still in flight land before the exit
+        if (lane == 0)
+            for (; used < issued; used++)
+                sm100::mbar_wait_drain(&bars[warp][used % kAttnRing], (used / kAttnRing) & 1u);
+        __syncwarp();
+        return;
+    }
+    const float inv = 1.0f / (ssum + 1e-8f);
+    const float cnt_all = (float)max64(s1 - s0, 1);
+    float *on = a.out + n * (int64_t)ROW + lane * S;
+#pragma unroll
+    for (int i = 0; i < S; i++) {
+        float v = acc[i] * inv;
+        if (a.reduce == FEQ_REDUCE_MEAN) v /= cnt_all;
+        on[i] = v;
+    }
+}
+
+template <int S>
+static int launch_attn_pool_ring(const FeqAttnArgs &a, cudaStream_t s) {
+    const size_t smem = (size_t)4 * kAttnRing * 2 * 32 * S * sizeof(float);
+    FEQ_CUDA_TRY(cudaFuncSetAttribute(attn_pool_ring_kernel<S>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    attn_pool_ring_kernel<S><<<(unsigned)((a.num_nodes + 3) / 4), 128, smem, s>>>(a, wait_limit_ns());
+    FEQ_LAUNCH_CHECK();
+    return FEQ_OK;
+}
+
 template <int S>
 static int launch_attn_pool_warp(const FeqAttnArgs &a, cudaStream_t s) {
     attn_pool_warp_kernel<S><<<(unsigned)((a.num_nodes + 3) / 4), 128, 0, s>>>(a);
@@ -531,6 +676,15 @@ int launch_attn_pool(const FeqAttnArgs &a, cudaStream_t s) {
         if (qrow == vrow && qrow % 32 == 0 && H >= 1 && H <= 32 && 32 % H == 0 && aligned &&
             a.num_nodes <= 0x1ffffffffll) {
             const int S = qrow / 32;
+            // rows by bulk copy: 16-byte aligned rows (32 S floats are a multiple of 16 bytes)
+            const bool aligned16 = ((reinterpret_cast<uintptr_t>(a.qk) | reinterpret_cast<uintptr_t>(a.v) |
+                                     reinterpret_cast<uintptr_t>(a.k)) & 15) == 0;
+            if (aligned16) {
+                if (S == 18) return launch_attn_pool_ring<18>(a, s);
+                if (S == 9) return launch_attn_pool_ring<9>(a, s);
+                if (S == 16) return launch_attn_pool_ring<16>(a, s);
+                if (S == 8) return launch_attn_pool_ring<8>(a, s);
+            }
             if (S == 18) return launch_attn_pool_warp<18>(a, s);    // Repr([0,1,2], 64)
             if (S == 9) return launch_attn_pool_warp<9>(a, s);      // Repr([0,1,2], 32)
             if (S == 16) return launch_attn_pool_warp<16>(a, s);    // Repr([0..3], 32)

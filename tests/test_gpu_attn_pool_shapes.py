@@ -63,3 +63,28 @@ def test_attn_pool_bad_src_sets_status(cuda_device):
     torch.cuda.synchronize()
     assert int(status.item()) == 1
     assert torch.isfinite(out).all()
+
+
+@pytest.mark.parametrize("decay", [None, 2.0])
+def test_attn_pool_hub_destination(cuda_device, decay):
+    """One destination with 300 in-edges (its edge ids arrive in batches of 32), the others
+    with one edge or none: the batched index loads and the row ring across batch boundaries."""
+    gen = torch.Generator().manual_seed(17)
+    N, C, d, H = 40, 64, 9, 8
+    hub = torch.full((300,), 3, dtype=torch.int64)
+    single = torch.arange(10, 30)
+    dst = torch.cat([hub, single])
+    E = dst.numel()
+    src = torch.randint(0, N, (E,), generator=gen)
+    qk = torch.randn(N, 2 * C, d, generator=gen)
+    V = torch.randn(E, C, d, generator=gen)
+    dist = torch.rand(E, generator=gen) * 6
+    perm, offsets, _ = ops.edge_sort(dst.to(cuda_device), N)
+    out = ops.attn_pool(qk.to(cuda_device), V.to(cuda_device), src.to(cuda_device), dist.to(cuda_device), perm,
+                        offsets, N, H, 0.25, decay, "sum")
+    torch.cuda.synchronize()
+    Qe = qk[:, :C][dst].reshape(E, H, -1)
+    Ke = qk[:, C:][src].reshape(E, H, -1)
+    w = orc.edge_attention(Qe, Ke, V, dst, N, torch.tensor(0.25), H, dist if decay else None, decay)
+    ref = orc.pool(w, dst, N, "sum")
+    assert rel_l2(out, ref) < 1e-5
