@@ -752,6 +752,30 @@ def node_linear(x, lvals, weight, bias, c_out, scalar_index):
     return y.view(*x.shape[:-2], cout, d)
 
 
+def dense_linear_tc_supported(m, k, mix=NODE_LINEAR_MIX) -> bool:
+    """Whether feq_dense_linear_tc serves y = x w^T + b with w (m, k)."""
+    return _lib.load().feq_dense_linear_tc_workspace_bytes(int(m), int(k), _lib.FEQ_MIX[mix]) > 0
+
+
+def dense_linear(x, weight, bias=None, mix=NODE_LINEAR_MIX):
+    """nn.Linear forward y = x w^T + b on the tensor cores (feq_dense_linear_tc, bf16x3 by
+    default); x (..., k), weight (m, k).  Raises for shapes the kernel does not serve."""
+    lib = _require_cuda(x, weight, bias)
+    m, k = weight.shape
+    xx = _aligned16(_f32(x, "x").reshape(-1, k).contiguous())
+    n = xx.shape[0]
+    dev = xx.device
+    y = torch.empty(n, m, dtype=torch.float32, device=dev)
+    mode = _lib.FEQ_MIX[mix]
+    wsb = lib.feq_dense_linear_tc_workspace_bytes(m, k, mode)
+    ws = _workspace(wsb, dev)
+    w = _f32(weight, "weight").contiguous()
+    b = None if bias is None else _f32(bias, "bias").contiguous()
+    rc = lib.feq_dense_linear_tc(_p(xx), n, m, k, _p(w), _p(b), mode, _p(y), _p(ws), wsb, None, _stream(dev))
+    _lib.check(rc, "feq_dense_linear_tc")
+    return y.view(*x.shape[:-1], m)
+
+
 def node_gate(x, z, lvals):
     """x * sigmoid(z)[..., c, irrep(position)]; z (..., C * n_irreps)."""
     lib = _require_cuda(x, z)

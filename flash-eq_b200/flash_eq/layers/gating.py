@@ -1,7 +1,8 @@
 """Norm-based gating (flash_eq/layers/gating.py:17-76 in the reference).
 
 Without autograd tracking on CUDA float32 inputs the irrep norms and the sigmoid gate are
-native kernels (csrc/feq_node.cu); the (C * nreps)^2 linear between them is a library GEMM.
+native kernels (csrc/feq_node.cu); the (C * nreps)^2 linear between them runs on the tensor
+cores (csrc/feq_dense.cu) where its size allows.
 """
 from __future__ import annotations
 
@@ -33,7 +34,14 @@ class EquivariantGating(nn.Module):
         if native_node_ok(st, self.linear.weight, self.linear.bias):
             from ..cuda import ops
 
-            # norms and the gate run natively; the dense (C * nreps)^2 linear stays a library GEMM
-            return ops.node_gate(st, self.linear(norms.flatten(-2, -1)), self.norm._lvals)
+            # norms and the gate run natively; the dense (C * nreps)^2 linear on the tensor cores
+            # (bf16x3) where the kernel serves its size, else a library GEMM
+            flat = norms.flatten(-2, -1)
+            w = self.linear.weight
+            if ops.dense_linear_tc_supported(w.shape[0], w.shape[1]):
+                z = ops.dense_linear(flat, w, self.linear.bias)
+            else:
+                z = self.linear(flat)
+            return ops.node_gate(st, z, self.norm._lvals)
         g = self.activation(self.linear(norms.flatten(-2, -1)).view(*b, *self.outdims))
         return st * g[..., self.ix]

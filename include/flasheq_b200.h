@@ -471,6 +471,17 @@ size_t feq_node_linear_tc_workspace_bytes(int32_t c_in, int32_t c_out, const int
 int feq_node_linear_tc(const float *x, int64_t num_nodes, int32_t c_in, int32_t c_out, const int32_t *lvals,
                        int32_t n_lvals, const float *weight, const float *bias, int32_t mix_mode, float *y,
                        void *workspace, size_t workspace_bytes, int32_t *status, feq_stream_t stream);
+/* The dense nn.Linear of EquivariantGating (gating.py:17-76: z = Linear(irrep norms), the
+ * (C * n_lvals)^2 mix before the sigmoid) on the tensor cores: y (n, m) = x (n, k) w^T + bias,
+ * w (m, k) float32 as nn.Linear holds it, bias (m,) or NULL, all row-major; m a multiple of
+ * 128 up to 512, k a multiple of 64 up to 512 (FEQ_ERR_UNSUPPORTED otherwise: use a library
+ * GEMM).  mix_mode FEQ_MIX_BF16X3 (float32-level accuracy) or FEQ_MIX_BF16.  The workspace
+ * (feq_dense_linear_tc_workspace_bytes, 16-byte aligned) receives w re-laid as tensor-core
+ * tiles; x 16-byte aligned; status (may be NULL) is set to 2 when a pipeline wait ran out. */
+size_t feq_dense_linear_tc_workspace_bytes(int32_t m, int32_t k, int32_t mix_mode);
+int feq_dense_linear_tc(const float *x, int64_t n, int32_t m, int32_t k, const float *weight, const float *bias,
+                        int32_t mix_mode, float *y, void *workspace, size_t workspace_bytes, int32_t *status,
+                        feq_stream_t stream);
 /* EquivariantGating's gate (gating.py:17-76): out = x * sigmoid(z)[c, irrep of the
  * position], z (N, C * n_lvals) the pre-activation. */
 int feq_node_gate(const float *x, const float *z, int64_t num_nodes, int32_t C, const int32_t *lvals,
