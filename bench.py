@@ -1335,7 +1335,7 @@ def giant_measure(args, world, rank, local, pg, n, steps, warmup, e2e_steps):
             "roofline": roofline, "stages_ms_per_step_rank0": stages, "exchange": exchange,
             "step_breakdown_rank0_ms": {"library_kernels": lib_ms,
                                         "nccl_exchange": exchange["ms_per_step_max_rank"] if exchange else 0.0,
-                                        "other (torch node GEMMs, glue)": max(0.0, ms - lib_ms - (
+                                        "other (torch glue: radial net, residual adds, LayerScale, gathers)": max(0.0, ms - lib_ms - (
                                             exchange["ms_per_step_max_rank"] if exchange else 0.0)),
                                         "largest_library_stage": largest[0] if largest else None},
             "mix": args.mix, "clocks": clocks, "e2e": e2e, "gpu_launches": int(launches),
