@@ -78,15 +78,22 @@ class EquivariantTransformerBlock(nn.Module):
         self.layer_scale_mlp = LayerScale(layer_scale_init) if layer_scale_init is not None else nn.Identity()
         self.drop_path = DropPath(drop_path) if drop_path > 0.0 else nn.Identity()
 
+    def _residual(self, x: torch.Tensor, y: torch.Tensor, scale: nn.Module) -> torch.Tensor:
+        """x + drop_path(scale(y)); with LayerScale and no stochastic depth in effect, one
+        fused x + y * gamma (torch.addcmul) instead of a multiply and an add."""
+        if isinstance(scale, LayerScale) and isinstance(self.drop_path, nn.Identity):
+            return torch.addcmul(x, y, scale.gamma)
+        return x + self.drop_path(scale(y))
+
     def forward(self, P, Q, node_features: torch.Tensor, distances: torch.Tensor, graph: Graph,
                 edge_features: torch.Tensor | None = None) -> torch.Tensor:
         attn_out = self.attn(P, Q, self.norm1(node_features), distances, graph, edge_features=edge_features)
         if self._use_attn_residual:
-            x = node_features + self.drop_path(self.layer_scale_attn(attn_out))
+            x = self._residual(node_features, attn_out, self.layer_scale_attn)
         else:
             x = attn_out
         mlp_out = self.mlp_down(self.mlp_act(self.mlp_up(self.norm2(x))))
-        return x + self.drop_path(self.layer_scale_mlp(mlp_out))
+        return self._residual(x, mlp_out, self.layer_scale_mlp)
 
     def extra_repr(self) -> str:
         return f"in_repr={self.in_repr}, out_repr={self.out_repr}, attn_residual={self._use_attn_residual}"
