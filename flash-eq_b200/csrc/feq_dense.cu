@@ -75,7 +75,7 @@ dense_kernel(const float *__restrict__ x, int64_t N, int M, int K, const uint8_t
 
     __shared__ uint64_t w_full[kMaxStages], w_empty[kMaxStages], x_ready, t_full[2], t_empty[2], drain_bar;
     __shared__ uint32_t tmem_s;
-    __shared__ int abort_s;
+    __shared__ int abort_s, conv_stop_s;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
         for (int s = 0; s < stages; s++) {
@@ -89,6 +89,7 @@ dense_kernel(const float *__restrict__ x, int64_t N, int M, int K, const uint8_t
         }
         mbar_init(&drain_bar, 1);
         abort_s = 0;
+        conv_stop_s = 0;
         fence_mbar_init();
     }
     const uint32_t tcols = (uint32_t)(2 * MT * TR) <= 256 ? 256u : 512u;
@@ -202,8 +203,13 @@ dense_kernel(const float *__restrict__ x, int64_t N, int M, int K, const uint8_t
             if (lane == 0) mbar_arrive(&t_empty[buf]);
         };
         for (int64_t i = 0; i < n_local; i++) {
-            // the previous tile's MMAs have read the operand before it is rewritten
-            if (i >= 1 && !mbar_wait(&t_full[(i - 1) & 1], (uint32_t)(((i - 1) >> 1) & 1), abort_flag, wait_ns)) {
+            // the previous tile's MMAs have read the operand before it is rewritten.  The four
+            // converter warps meet at named barrier 1, so they leave the loop together: a failed
+            // wait in any of them is posted in conv_stop_s before the barrier and read after it.
+            if (i >= 1 && !mbar_wait(&t_full[(i - 1) & 1], (uint32_t)(((i - 1) >> 1) & 1), abort_flag, wait_ns))
+                conv_stop_s = 1;
+            named_bar(1, 128);
+            if (*reinterpret_cast<volatile int *>(&conv_stop_s)) {
                 ok = false;
                 break;
             }
@@ -226,10 +232,7 @@ dense_kernel(const float *__restrict__ x, int64_t N, int M, int K, const uint8_t
             fence_async_smem();
             named_bar(1, 128);
             if (ct == 0) mbar_arrive(&x_ready);
-            if (i >= 1) {
-                epilogue(i - 1);
-                if (!ok) break;
-            }
+            if (i >= 1) epilogue(i - 1);     // its accumulators were waited for above: no time-out here
         }
         if (ok && n_local > 0) epilogue(n_local - 1);
     }

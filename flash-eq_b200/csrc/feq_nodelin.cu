@@ -112,13 +112,14 @@ nodelin_kernel(const float *__restrict__ x, int64_t N, const uint8_t *__restrict
     uint8_t *bsm = wsm + WB;                                    // operand chunks [kc][s]
     float *stg = reinterpret_cast<float *>(bsm + G::KC * SP * G::BCHUNK);   // TN x COUT x D output rows
 
-    __shared__ uint64_t w_bar, mma_bar;
+    __shared__ uint64_t w_bar, mma_bar, drain_bar;
     __shared__ uint32_t tmem_s;
     __shared__ int abort_s;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) {
         mbar_init(&w_bar, 1);
         mbar_init(&mma_bar, 1);
+        mbar_init(&drain_bar, 1);
         abort_s = 0;
         fence_mbar_init();
     }
@@ -257,7 +258,15 @@ nodelin_kernel(const float *__restrict__ x, int64_t N, const uint8_t *__restrict
             stored = true;
         }
     }
-    if (tid == 0) bulk_wait0();
+    if (tid == 0) {
+        // before TMEM and shared memory are released, everything in flight lands, also after a
+        // wait ran out: the weight copies, every MMA issued (this thread issued them all) and the
+        // last output rows
+        mbar_wait_drain(&w_bar, 0);
+        umma_commit(&drain_bar);
+        mbar_wait_drain(&drain_bar, 0);
+        bulk_wait0();
+    }
     tc_fence_before();
     __syncthreads();
     if (warp == 0) {

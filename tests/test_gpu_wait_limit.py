@@ -110,3 +110,114 @@ def test_separable_kernel_short_wait_limit(cuda_device, mix):
     ref = orc.edgewise_fwd(orc.wigner_basis(dirs, lv), orc.wigner_basis(dirs, lv), f, dist, table.cpu(), lv, lv,
                            0.1, p1, p2, rw.num_bins, False)
     assert rel_l2(y, ref) < (1e-4 if mix == "bf16x3" else 2e-2)
+
+
+def _short_limit_then_recover(run, check, must_time_out=True):
+    """run(status) with a 1 ns pipeline-wait limit must come back (no hang, no fault) with
+    status 2 -- or 0 when must_time_out is False: a kernel whose waits are all short may see
+    each phase complete before it first looks at the timer (every 8 polls) -- and with the
+    default limit give a result that check() accepts."""
+    lib = _lib.load()
+    dev = torch.device("cuda:0")
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    prev = lib.feq_set_wait_limit_ns(1)
+    try:
+        run(status)
+        torch.cuda.synchronize()
+    finally:
+        lib.feq_set_wait_limit_ns(prev)
+    if must_time_out:
+        assert int(status.item()) == 2, "a 1 ns wait limit should have timed out at least one wait"
+    else:
+        assert int(status.item()) in (0, 2)
+    status.zero_()
+    out = run(status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    check(out)
+
+
+@pytest.mark.gpu
+def test_node_linear_kernel_short_wait_limit(cuda_device):
+    """The tensor-core EquivariantLinear (feq_node_linear_tc): weight copies and MMAs drained
+    before the kernel frees its tensor memory."""
+    import ctypes
+    g = torch.Generator().manual_seed(2)
+    N, cin, cout, lv = 50000, 64, 128, [0, 1, 2]
+    f = torch.randn(N, cin, 9, generator=g).to(cuda_device)
+    w = torch.randn(3, cout, cin, generator=g).to(cuda_device)
+    lib = _lib.load()
+    arr, n = _lib.i32_array(lv)
+    wsb = lib.feq_node_linear_tc_workspace_bytes(cin, cout, arr, n, _lib.FEQ_MIX["bf16x3"])
+    ws = torch.empty(wsb, dtype=torch.uint8, device=cuda_device)
+
+    def run(status):
+        y = torch.empty(N, cout, 9, device=cuda_device)
+        rc = lib.feq_node_linear_tc(ctypes.c_void_p(f.data_ptr()), N, cin, cout, arr, n, ctypes.c_void_p(w.data_ptr()),
+                                    None, _lib.FEQ_MIX["bf16x3"], ctypes.c_void_p(y.data_ptr()),
+                                    ctypes.c_void_p(ws.data_ptr()), wsb, ctypes.c_void_p(status.data_ptr()),
+                                    ops._stream(cuda_device))
+        _lib.check(rc, "feq_node_linear_tc")
+        return y
+
+    def check(y):
+        fd, wd = f.double().cpu(), w.double().cpu()
+        ref = torch.empty(N, cout, 9, dtype=torch.float64)
+        for r, (a, b) in enumerate(((0, 1), (1, 4), (4, 9))):
+            ref[:, :, a:b] = torch.einsum("oi,nip->nop", wd[r], fd[:, :, a:b])
+        assert rel_l2(y.cpu().double(), ref) < 1e-4
+
+    # one MMA group and one weight copy per CTA to wait for, each shorter than the polls
+    # before the first look at the timer: the limit may not be reached
+    _short_limit_then_recover(run, check, must_time_out=False)
+
+
+@pytest.mark.gpu
+def test_dense_linear_kernel_short_wait_limit(cuda_device):
+    """The tensor-core dense linear (feq_dense_linear_tc): producer, MMA and converter warps
+    leave together, copies and MMAs drained."""
+    import ctypes
+    g = torch.Generator().manual_seed(4)
+    n, m, k = 60000, 384, 384
+    x = torch.randn(n, k, generator=g).to(cuda_device)
+    w = torch.randn(m, k, generator=g).to(cuda_device)
+    lib = _lib.load()
+    wsb = lib.feq_dense_linear_tc_workspace_bytes(m, k, _lib.FEQ_MIX["bf16x3"])
+    ws = torch.empty(wsb, dtype=torch.uint8, device=cuda_device)
+
+    def run(status):
+        y = torch.empty(n, m, device=cuda_device)
+        rc = lib.feq_dense_linear_tc(ctypes.c_void_p(x.data_ptr()), n, m, k, ctypes.c_void_p(w.data_ptr()), None,
+                                     _lib.FEQ_MIX["bf16x3"], ctypes.c_void_p(y.data_ptr()),
+                                     ctypes.c_void_p(ws.data_ptr()), wsb, ctypes.c_void_p(status.data_ptr()),
+                                     ops._stream(cuda_device))
+        _lib.check(rc, "feq_dense_linear_tc")
+        return y
+
+    def check(y):
+        assert rel_l2(y.cpu().double(), x.cpu().double() @ w.cpu().double().t()) < 1e-4
+
+    _short_limit_then_recover(run, check)
+
+
+@pytest.mark.gpu
+def test_attention_pooling_ring_short_wait_limit(cuda_device):
+    """The ring attention pooling kernel: each warp waits for its copies in flight and leaves."""
+    g = torch.Generator().manual_seed(6)
+    N, E, C, d, H = 20000, 400000, 64, 9, 8
+    src = torch.randint(0, N, (E,), generator=g).to(cuda_device)
+    dst = torch.randint(0, N, (E,), generator=g).to(cuda_device)
+    qk = torch.randn(N, 2 * C, d, generator=g).to(cuda_device)
+    V = torch.randn(E, C, d, generator=g).to(cuda_device)
+    perm, offsets, _ = ops.edge_sort(dst, N)
+
+    def run(status):
+        return ops.attn_pool(qk, V, src, None, perm, offsets, N, H, 0.3, None, "sum", status=status)
+
+    def check(out):
+        ref = ops.attn_pool(qk, V, src, None, perm, offsets, N, H, 0.3, None, "sum")
+        assert torch.equal(out, ref)                  # deterministic: bitwise the same result
+
+    # the rows are copied four edges ahead of their use, so a wait rarely outlasts the polls
+    # before the first look at the timer: the limit may not be reached
+    _short_limit_then_recover(run, check, must_time_out=False)
