@@ -22,23 +22,25 @@
 // epilogue, straight from TMEM, followed by the rotation back (s^l_out folded in) and one
 // bulk store per output row.
 //
-// Roles (320 threads, persistent, one CTA per SM, one edge tile after another):
+// Roles (persistent, one CTA per SM, one edge tile after another):
 //   warp 0      TMEM allocator; one thread issues tcgen05.mma
 //   warp 1      loader: lane per edge, up to 32 edges ahead of the rotation warps: the
-//               edge's scalars (bin, t, s = d / (d + sh_scale), the trig of the rotations)
-//               and a bulk copy of its input row x[src[e]] into a ring of row buffers, so
-//               that enough bytes are in flight to cover the HBM latency
-//               (at L >= 3 the loader only bins the edge and issues its copies: the rotation
-//               warp forms the trig and the M_l nonzeros of its edge with all 32 lanes, since a
-//               short ring of large rows would leave the lane-per-edge loader only a few edges)
-//   warps 2..5  rotation in: rotate two channels per lane with the factored Wigner blocks,
+//               edge's scalars (bin, t, s = d / (d + sh_scale)) and a bulk copy of its input
+//               row x[src[e]] into a ring of row buffers, so that enough bytes are in flight
+//               to cover the HBM latency.  At L <= 2 it also forms the trig of the rotations
+//               and the M_l nonzeros and copies the edge's two radial-feature rows into the
+//               ring; at L >= 3 the rotation warp forms those with all 32 lanes and reads the
+//               feature rows from L2 (a short ring of large rows would leave the
+//               lane-per-edge loader only a few edges at a time)
+//   next NROT   rotation in: rotate two channels per lane with the factored Wigner blocks,
 //               write bf16 (hi, and lo in bf16x3 mode) into the K-major 128-byte-swizzled
 //               N-side tile; per edge also the lerped g_k for the epilogue
-//   warps 6..9  epilogue: tcgen05.ld of Z, position mix, sum over k across lane pairs,
-//               rotation back, bulk store
-// Rings: input rows, 2 N-side tiles, 2 TMEM accumulator sets, 4 per-tile slots.  Every
-// wait is bounded (limit from the launch); on time-out the kernel sets status 2, drains
-// its copies and MMAs, frees TMEM and returns.  No TMA multicast anywhere.
+//   then EWG    epilogue warpgroups: tcgen05.ld of Z, position mix, sum over k across lane
+//               pairs, rotation back, bulk store
+//   (L <= 2: 8 rotation warps, 3 epilogue warpgroups; L = 3: 4 and 2; L = 4: 4 and 1)
+// Rings: input rows, 2 N-side tiles, 2 TMEM accumulator sets, 4 (L <= 2) or 3 per-tile
+// slots.  Every wait is bounded (limit from the launch); on time-out the kernel sets status
+// 2, drains its copies and MMAs, frees TMEM and returns.  No TMA multicast anywhere.
 //
 // bf16x3 (float32-level accuracy): both operands split x = hi + lo, Z accumulates
 // hi.hi + hi.lo + lo.hi.  bf16: hi only.
