@@ -7,17 +7,18 @@
 // that reads every node row once and writes every output row once:
 //   - a tile is 16 nodes; its rows (node, position) are grouped by irrep, so irrep r owns
 //     16 (2r + 1) consecutive rows -- a legal MMA N (a multiple of 16) for every degree;
-//   - the node rows are loaded with 16-byte loads (the next tile's while this one is in the
-//     MMAs and the epilogue) and written by the CUDA cores as the K-major, 128-byte-swizzled
-//     bf16 operand (hi, and lo for bf16x3);
-//   - the weights, re-laid once per call into the same swizzled tiles (hi / lo) by
+//   - the weights, re-laid once per call into 128-byte-swizzled bf16 tiles (hi / lo) by
 //     nodelin_wtiles_kernel, stay in shared memory for the whole kernel;
+//   - converter warps (4, 8 or 16, a few nodes each) load their node rows with 16-byte loads
+//     (the next tile's while the MMAs run) and write them as the K-major swizzled bf16 operand
+//     (hi, and lo for bf16x3) into one of two operand stages;
 //   - one thread issues tcgen05.mma kind::f16 per irrep (M = C_out rows of W_r, or 64),
-//     accumulating in TMEM; bf16x3 accumulates hi.hi + hi.lo + lo.hi;
-//   - the epilogue reads TMEM (lane = output channel), adds the bias, stages the tile's output
-//     rows in shared memory and writes them with one bulk store (16 node rows are contiguous).
-// Every wait is bounded; on time-out the kernel sets status 2 and every thread leaves.  No
-// TMA multicast.
+//     into one of two TMEM accumulator sets; bf16x3 accumulates hi.hi + hi.lo + lo.hi;
+//   - four epilogue warps (one per TMEM lane quadrant, lane = output channel) add the bias,
+//     stage four nodes' rows of their 32 (or 16) channels and bulk-store them;
+// so one tile's operand is written while the previous tile's MMAs run and the one before is
+// stored.  Every wait is bounded; on time-out the kernel sets status 2, drains and leaves.
+// No TMA multicast.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -34,7 +35,6 @@ using namespace sm100;
 using namespace rot;
 
 constexpr int TN = 16;            // nodes per tile
-constexpr int kThreads = 256;     // 8 warps: two per TMEM lane quadrant in the epilogue
 
 template <int L, int CIN, int COUT>
 struct NG {
@@ -50,8 +50,6 @@ struct NG {
     static constexpr uint32_t TALLOC = TCOLS <= 32 ? 32 : TCOLS <= 64 ? 64 : TCOLS <= 128 ? 128
                                      : TCOLS <= 256 ? 256 : 512;
     static constexpr int ROWF = CIN * D;                        // floats of one input row
-    static constexpr int VPT = TN * ROWF / 4 / kThreads;        // float4 loads per thread per tile
-    static_assert((TN * ROWF) % (4 * kThreads) == 0, "tile loads split evenly over the threads");
     __host__ __device__ static constexpr int roff(int r) { return TN * r * r; }     // first row of irrep r
 };
 
@@ -64,13 +62,6 @@ template <int L, int CIN, int COUT, bool kSplit>
 constexpr uint32_t w_bytes() {
     using G = NG<L, CIN, COUT>;
     return (uint32_t)G::NR * G::KC * G::MT * (kSplit ? 2 : 1) * G::WTILE;
-}
-
-template <int L, int CIN, int COUT, bool kSplit>
-constexpr size_t smem_bytes() {
-    using G = NG<L, CIN, COUT>;
-    return 1024 + (size_t)w_bytes<L, CIN, COUT, kSplit>() + (size_t)G::KC * (kSplit ? 2 : 1) * G::BCHUNK
-         + (size_t)TN * COUT * G::D * 4;
 }
 
 // Weights (NR, COUT, CIN) float32 -> swizzled bf16 tiles [r][kc][mt][hi, lo].
@@ -91,40 +82,93 @@ __global__ void nodelin_wtiles_kernel(const float *__restrict__ w, uint8_t *__re
     }
 }
 
-// 8 consecutive 32-bit TMEM columns of this thread's lane.
-__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
-    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+// Warp roles of the pipelined kernel: warp 0 issues the MMAs (and allocates TMEM), NCONV
+// converter warps turn node rows into the operand (TN / NCONV nodes each), four epilogue
+// warps (one per TMEM lane quadrant) turn accumulators into output rows.
+template <int L, int CIN>
+struct Roles {
+    static constexpr int ROWF = CIN * (L + 1) * (L + 1);
+    static constexpr int NCONV = ROWF <= 512 ? 4 : ROWF <= 576 ? 8 : 16;
+    static constexpr int NPC = TN / NCONV;                       // nodes per converter warp
+    static constexpr int VPL = NPC * ROWF / 4 / 32;              // float4s per lane per tile
+    static constexpr bool XDB = NCONV == 4 && VPL <= 8;          // next tile's rows double-buffered (small rows)
+    static constexpr int THREADS = (1 + NCONV + 4) * 32;
+    static constexpr int CONV0 = 1, EPI0 = 1 + NCONV;
+    static_assert(NPC * ROWF % 128 == 0, "a converter warp's rows split into float4s over 32 lanes");
+};
+
+__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+
+// 4 consecutive 32-bit TMEM columns of this thread's lane.
+__device__ __forceinline__ void tmem_ld4(uint32_t taddr, uint32_t *r) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
                  : "r"(taddr));
 }
 
 template <int L, int CIN, int COUT, bool kSplit>
-__global__ void __launch_bounds__(kThreads, 1)
+constexpr uint32_t bufcols() {           // TMEM columns of one accumulator set, 256-aligned sets
+    return (uint32_t)NG<L, CIN, COUT>::TCOLS <= 256 ? 256u : 512u;
+}
+
+template <int L, int CIN, int COUT, bool kSplit>
+constexpr size_t smem_bytes_for(int bstages) {
+    using G = NG<L, CIN, COUT>;
+    constexpr int CW = G::MROWS == 128 ? 32 : 16;                 // output channels per epilogue warp
+    return 1024 + (size_t)w_bytes<L, CIN, COUT, kSplit>() + (size_t)bstages * G::KC * (kSplit ? 2 : 1) * G::BCHUNK
+         + (size_t)4 * 2 * 4 * CW * G::D * 4;
+}
+// operand stages: two where shared memory allows (the converters fill one while the MMAs read
+// the other), else one
+template <int L, int CIN, int COUT, bool kSplit>
+constexpr int bstages() { return smem_bytes_for<L, CIN, COUT, kSplit>(2) <= 227 * 1024 ? 2 : 1; }
+template <int L, int CIN, int COUT, bool kSplit>
+constexpr size_t smem_bytes() { return smem_bytes_for<L, CIN, COUT, kSplit>(bstages<L, CIN, COUT, kSplit>()); }
+
+// The kernel, pipelined: converter warps fill operand stage i % 2 for tile i while the MMA warp
+// works on tile i - 1 and the epilogue warps drain the accumulators of tile i - 2 (two
+// accumulator sets).  mbarriers: b_full (converters -> MMA), b_empty (MMA -> converters),
+// t_full (MMA -> epilogue), t_empty (epilogue -> MMA).  No role waits at a barrier shared with
+// another role, so a time-out in one lets the others time out in turn and leave.
+template <int L, int CIN, int COUT, bool kSplit>
+__global__ void __launch_bounds__(Roles<L, CIN>::THREADS, 1)
 nodelin_kernel(const float *__restrict__ x, int64_t N, const uint8_t *__restrict__ wt, const float *__restrict__ bias,
                float *__restrict__ y, int64_t ntiles, int32_t *status, uint64_t wait_ns) {
     using G = NG<L, CIN, COUT>;
+    using R = Roles<L, CIN>;
     constexpr int SP = kSplit ? 2 : 1;
     constexpr int D = G::D;
     constexpr uint32_t WB = w_bytes<L, CIN, COUT, kSplit>();
+    constexpr uint32_t BSTAGE = G::KC * SP * G::BCHUNK;
+    constexpr int BST = bstages<L, CIN, COUT, kSplit>();
+    constexpr uint32_t BUFC = bufcols<L, CIN, COUT, kSplit>();
+    constexpr uint32_t TALLOC = 2 * BUFC;
+    constexpr int CW = G::MROWS == 128 ? 32 : 16;
+    constexpr int GROUP = 4;                                   // nodes per epilogue store group
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t *wsm = smem;                                        // weight tiles [r][kc][mt][s]
-    uint8_t *bsm = wsm + WB;                                    // operand chunks [kc][s]
-    float *stg = reinterpret_cast<float *>(bsm + G::KC * SP * G::BCHUNK);   // TN x COUT x D output rows
+    uint8_t *wsm = smem;                                       // weight tiles [r][kc][mt][s]
+    uint8_t *bsm = wsm + WB;                                   // BST operand stages [kc][s]
+    float *stg = reinterpret_cast<float *>(bsm + BST * BSTAGE);  // per epilogue warp 2 x GROUP x CW x D
 
-    __shared__ uint64_t w_bar, mma_bar, drain_bar;
+    __shared__ uint64_t w_bar, b_full[2], b_empty[2], t_full[2], t_empty[2], drain_bar;
     __shared__ uint32_t tmem_s;
     __shared__ int abort_s;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    if (tid == 0) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
         mbar_init(&w_bar, 1);
-        mbar_init(&mma_bar, 1);
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&b_full[i], R::NCONV);
+            mbar_init(&b_empty[i], 1);
+            mbar_init(&t_full[i], 1);
+            mbar_init(&t_empty[i], 4);
+        }
         mbar_init(&drain_bar, 1);
         abort_s = 0;
         fence_mbar_init();
     }
     if (warp == 0) {
-        tmem_alloc(&tmem_s, G::TALLOC);
+        tmem_alloc(&tmem_s, TALLOC);
         tmem_relinquish();
     }
     tc_fence_before();
@@ -132,153 +176,192 @@ nodelin_kernel(const float *__restrict__ x, int64_t N, const uint8_t *__restrict
     tc_fence_after();
     const uint32_t tmem = tmem_s;
     volatile int *abort_flag = &abort_s;
-    if (tid == 0) {
-        mbar_arrive_expect_tx(&w_bar, WB);
-        for (uint32_t o = 0; o < WB; o += G::WTILE) bulk_load(wsm + o, wt + o, G::WTILE, &w_bar);
-    }
+    const int64_t n_local = ntiles > blockIdx.x ? (ntiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
 
-    // this thread's share of a tile: VPT float4s at element 4 (tid + v kThreads)
-    float4 xv[G::VPT];
-    auto load_tile = [&](int64_t t) {
-        const int64_t n0 = t * TN;
-        const int64_t lim = (N - n0) * G::ROWF;                 // valid floats of the tile
-        const float4 *src = reinterpret_cast<const float4 *>(x + n0 * G::ROWF);
+    if (warp == 0) {
+        // ---------------- weights in, MMA issuer ----------------
+        if (lane == 0) {
+            mbar_arrive_expect_tx(&w_bar, WB);
+            for (uint32_t o = 0; o < WB; o += G::WTILE) bulk_load(wsm + o, wt + o, G::WTILE, &w_bar);
+            bool ok = mbar_wait(&w_bar, 0, abort_flag, wait_ns);
+            for (int64_t i = 0; ok && i < n_local; i++) {
+                const int s = (int)(i & 1), sb = (int)(i % BST);
+                if (!mbar_wait(&b_full[sb], (uint32_t)((i / BST) & 1), abort_flag, wait_ns)) break;
+                if (i >= 2 && !mbar_wait(&t_empty[s], (uint32_t)(((i >> 1) - 1) & 1), abort_flag, wait_ns)) break;
+                tc_fence_after();
+                const uint8_t *bst = bsm + (size_t)sb * BSTAGE;
 #pragma unroll
-        for (int v = 0; v < G::VPT; v++) {
-            const int e = 4 * (tid + v * kThreads);
-            xv[v] = (t < ntiles && e < lim) ? __ldg(src + tid + v * kThreads) : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-    };
-    auto put = [&](int e, float val) {
-        const int n = e / G::ROWF, rem = e - n * G::ROWF;
-        const int c = rem / D, p = rem - c * D;
-        const int r = p >= 9 ? 3 : p >= 4 ? 2 : p >= 1 ? 1 : 0;
-        const int row = G::roff(r) + n * (2 * r + 1) + (p - r * r);
-        uint8_t *chunk = bsm + (size_t)((c >> 6) * SP) * G::BCHUNK;
-        const uint32_t o = swz(row, c & 63);
-        const __nv_bfloat16 hi = __float2bfloat16_rn(val);
-        *reinterpret_cast<__nv_bfloat16 *>(chunk + o) = hi;
-        if (kSplit) *reinterpret_cast<__nv_bfloat16 *>(chunk + G::BCHUNK + o) = __float2bfloat16_rn(val - __bfloat162float(hi));
-    };
-
-    int64_t t = blockIdx.x;
-    load_tile(t);
-    uint32_t phase = 0;
-    bool stored = false;
-    if (!mbar_wait(&w_bar, 0, abort_flag, wait_ns)) set_status(status, 2);
-    __syncthreads();
-    for (; t < ntiles && !*abort_flag; t += gridDim.x) {
-        const int64_t n0 = t * TN;
-        const int nv = (int)((N - n0) < TN ? (N - n0) : TN);
-        // (1) rows -> K-major bf16 operand
+                for (int r = 0; r < G::NR; r++) {
+                    const uint32_t idesc = idesc_bf16_f32(G::MROWS, TN * (2 * r + 1));
 #pragma unroll
-        for (int v = 0; v < G::VPT; v++) {
-            const int e = 4 * (tid + v * kThreads);
-            put(e, xv[v].x);
-            put(e + 1, xv[v].y);
-            put(e + 2, xv[v].z);
-            put(e + 3, xv[v].w);
-        }
-        fence_async_smem();
-        tc_fence_before();
-        __syncthreads();
-        // (2) one MMA group per irrep and M tile
-        if (tid == 0) {
-            tc_fence_after();
+                    for (int mt = 0; mt < G::MT; mt++) {
+                        const uint32_t d = tmem + (uint32_t)s * BUFC + (uint32_t)(mt * G::ROWS + G::roff(r));
 #pragma unroll
-            for (int r = 0; r < G::NR; r++) {
-                const uint32_t idesc = idesc_bf16_f32(G::MROWS, TN * (2 * r + 1));
+                        for (int kc = 0; kc < G::KC; kc++) {
+                            const uint32_t ah = smem_u32(wsm + (size_t)(((r * G::KC + kc) * G::MT + mt) * SP) * G::WTILE);
+                            const uint32_t bh = smem_u32(bst + (size_t)(kc * SP) * G::BCHUNK) + (uint32_t)G::roff(r) * 128u;
 #pragma unroll
-                for (int mt = 0; mt < G::MT; mt++) {
-                    const uint32_t d = tmem + (uint32_t)(mt * G::ROWS + G::roff(r));
-#pragma unroll
-                    for (int kc = 0; kc < G::KC; kc++) {
-                        const uint32_t ah = smem_u32(wsm + (size_t)(((r * G::KC + kc) * G::MT + mt) * SP) * G::WTILE);
-                        const uint32_t bh = smem_u32(bsm + (size_t)(kc * SP) * G::BCHUNK) + (uint32_t)G::roff(r) * 128u;
-#pragma unroll
-                        for (int ks = 0; ks < 4; ks++) {
-                            const uint32_t ko = ks * 32;
-                            umma_f16(d, smem_desc_sw128(ah + ko), smem_desc_sw128(bh + ko), idesc, (kc | ks) ? 1u : 0u);
-                            if (kSplit) {
-                                umma_f16(d, smem_desc_sw128(ah + ko), smem_desc_sw128(bh + G::BCHUNK + ko), idesc, 1u);
-                                umma_f16(d, smem_desc_sw128(ah + G::WTILE + ko), smem_desc_sw128(bh + ko), idesc, 1u);
+                            for (int ks = 0; ks < 4; ks++) {
+                                const uint32_t ko = ks * 32;
+                                umma_f16(d, smem_desc_sw128(ah + ko), smem_desc_sw128(bh + ko), idesc, (kc | ks) ? 1u : 0u);
+                                if (kSplit) {
+                                    umma_f16(d, smem_desc_sw128(ah + ko), smem_desc_sw128(bh + G::BCHUNK + ko), idesc, 1u);
+                                    umma_f16(d, smem_desc_sw128(ah + G::WTILE + ko), smem_desc_sw128(bh + ko), idesc, 1u);
+                                }
                             }
                         }
                     }
                 }
+                umma_commit(&b_empty[sb]);             // the operand stage may be refilled
+                umma_commit(&t_full[s]);               // the accumulators are ready
             }
-            umma_commit(&mma_bar);
+            // everything in flight lands before TMEM and shared memory are released
+            mbar_wait_drain(&w_bar, 0);
+            umma_commit(&drain_bar);
+            mbar_wait_drain(&drain_bar, 0);
         }
-        // the next tile's rows are in flight during the MMAs and the epilogue
-        load_tile(t + gridDim.x);
-        if (!mbar_wait(&mma_bar, phase, abort_flag, wait_ns)) set_status(status, 2);
-        phase ^= 1;
-        if (tid == 0 && stored) bulk_wait_read0();          // the previous tile's rows have left
-        __syncthreads();
-        if (*abort_flag) break;
-        tc_fence_after();
-        // (3) epilogue: warp w reads lane quadrant w % 4 for nodes [8 (w / 4), 8 (w / 4) + 8)
-        {
-            const int q4 = warp & 3, hn = warp >> 2;
-            const bool live = G::MROWS == 128 || lane < 16;
-            const int co_l = G::MROWS == 128 ? q4 * 32 + lane : q4 * 16 + lane;   // M row of this lane
+    } else if (warp < R::EPI0) {
+        // ---------------- converters: node rows -> operand ----------------
+        const int cw = warp - R::CONV0;
+        const int nb = cw * R::NPC;                            // first node of this warp in a tile
+        auto load = [&](int64_t i, float4 (&v)[R::VPL]) {
+            const int64_t n0 = (blockIdx.x + i * gridDim.x) * (int64_t)TN + nb;
+            const int64_t lim = (N - n0) * (int64_t)R::ROWF;   // valid floats from n0 on
+            const float4 *src = reinterpret_cast<const float4 *>(x + n0 * R::ROWF);
+#pragma unroll
+            for (int k = 0; k < R::VPL; k++) {
+                const int j = lane + 32 * k;
+                v[k] = (i < n_local && 4 * j < lim) ? __ldg(src + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        };
+        auto convert = [&](int64_t i, const float4 (&v)[R::VPL]) -> bool {
+            const int sb = (int)(i % BST);
+            if (i >= BST && !mbar_wait(&b_empty[sb], (uint32_t)((i / BST - 1) & 1), abort_flag, wait_ns)) return false;
+            uint8_t *bst = bsm + (size_t)sb * BSTAGE;
+#pragma unroll
+            for (int k = 0; k < R::VPL; k++) {
+                const float vv[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    const int e = 4 * (lane + 32 * k) + q;
+                    const int nl = e / R::ROWF, rem = e - nl * R::ROWF;
+                    const int c = rem / D, p = rem - c * D;
+                    const float val = vv[q];
+                    const int r = p >= 9 ? 3 : p >= 4 ? 2 : p >= 1 ? 1 : 0;
+                    const int row = G::roff(r) + (nb + nl) * (2 * r + 1) + (p - r * r);
+                    uint8_t *chunk = bst + (size_t)((c >> 6) * SP) * G::BCHUNK;
+                    const uint32_t o = swz(row, c & 63);
+                    const __nv_bfloat16 hi = __float2bfloat16_rn(val);
+                    *reinterpret_cast<__nv_bfloat16 *>(chunk + o) = hi;
+                    if (kSplit)
+                        *reinterpret_cast<__nv_bfloat16 *>(chunk + G::BCHUNK + o) =
+                            __float2bfloat16_rn(val - __bfloat162float(hi));
+                }
+            }
+            fence_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&b_full[sb]);
+            return true;
+        };
+        if constexpr (R::XDB) {
+            float4 va[R::VPL], vb[R::VPL];
+            load(0, va);
+            for (int64_t i = 0; i < n_local; i += 2) {
+                load(i + 1, vb);                           // in flight while tile i is converted
+                if (!convert(i, va)) break;
+                if (i + 1 >= n_local) break;
+                load(i + 2, va);
+                if (!convert(i + 1, vb)) break;
+            }
+        } else {
+            // the next tile's rows are loaded right after this tile's operand is handed over, so
+            // they are in flight while the MMAs run
+            float4 va[R::VPL];
+            load(0, va);
+            for (int64_t i = 0; i < n_local; i++) {
+                if (!convert(i, va)) break;
+                load(i + 1, va);
+            }
+        }
+    } else {
+        // ---------------- epilogue: accumulators -> output rows ----------------
+        const int q4 = warp & 3;
+        const bool live = G::MROWS == 128 || lane < 16;
+        const int co_l = G::MROWS == 128 ? q4 * 32 + lane : q4 * 16 + lane;
+        const int co0 = q4 * CW;                               // first channel of this warp
+        float *wst = stg + (size_t)(warp - R::EPI0) * 2 * GROUP * CW * D;
+        uint32_t groups = 0;
+        for (int64_t i = 0; i < n_local; i++) {
+            const int s = (int)(i & 1);
+            if (!mbar_wait(&t_full[s], (uint32_t)((i >> 1) & 1), abort_flag, wait_ns)) break;
+            tc_fence_after();
+            const int64_t n0 = (blockIdx.x + i * gridDim.x) * (int64_t)TN;
 #pragma unroll
             for (int mt = 0; mt < G::MT; mt++) {
                 const int co = mt * G::MROWS + co_l;
                 const float b0 = (bias && live) ? bias[co] : 0.0f;
+#pragma unroll 1
+                for (int g = 0; g < TN / GROUP; g++, groups++) {
+                    float *sb = wst + (size_t)(groups & 1) * GROUP * CW * D;
+                    if (groups >= 2) {                    // the store from two groups back has read sb
+                        if (lane == 0) bulk_wait_read1();
+                        __syncwarp();
+                    }
 #pragma unroll
-                for (int r = 0; r < G::NR; r++) {
-                    const int w = 2 * r + 1;
+                    for (int r = 0; r < G::NR; r++) {
+                        const int w = 2 * r + 1;
+                        uint32_t v[4 * 7];                     // 4 nodes x (2r + 1) columns, r <= 3
+                        const uint32_t col = (uint32_t)s * BUFC + (uint32_t)(mt * G::ROWS + G::roff(r) + g * GROUP * w);
 #pragma unroll
-                    for (int piece = 0; piece < w; piece++) {        // 8 columns a piece
-                        uint32_t v[8];
-                        const uint32_t col = (uint32_t)(mt * G::ROWS + G::roff(r) + hn * 8 * w + piece * 8);
-                        tmem_ld8(tmem + ((uint32_t)(q4 * 32) << 16) + col, v);
+                        for (int piece = 0; piece < 7; piece++)
+                            if (piece < w) tmem_ld4(tmem + ((uint32_t)(q4 * 32) << 16) + col + piece * 4, v + piece * 4);
                         tmem_wait_ld();
                         if (live) {
 #pragma unroll
-                            for (int j = 0; j < 8; j++) {
-                                const int jj = piece * 8 + j;                 // column within the 8 w of this half
-                                const int n = hn * 8 + jj / w, p = r * r + jj % w;
-                                float val = __uint_as_float(v[j]);
-                                if (r == 0) val += b0;
-                                stg[((size_t)n * COUT + co) * D + p] = val;
+                            for (int jj = 0; jj < 4 * 7; jj++) {
+                                if (jj < GROUP * w) {
+                                    const int nl = jj / w, p = r * r + jj % w;
+                                    float val = __uint_as_float(v[jj]);
+                                    if (r == 0) val += b0;
+                                    sb[((size_t)nl * CW + (co - mt * G::MROWS - co0)) * D + p] = val;
+                                }
                             }
                         }
                     }
+                    fence_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+#pragma unroll
+                        for (int nl = 0; nl < GROUP; nl++) {
+                            const int64_t node = n0 + g * GROUP + nl;
+                            if (node < N)
+                                bulk_store(y + (node * COUT + mt * G::MROWS + co0) * (int64_t)D, sb + (size_t)nl * CW * D,
+                                           (uint32_t)CW * D * 4);
+                        }
+                        bulk_commit();
+                    }
                 }
             }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&t_empty[s]);
         }
-        tc_fence_before();
-        fence_async_smem();
-        __syncthreads();
-        if (tid == 0) {
-            bulk_store(y + n0 * (int64_t)COUT * D, stg, (uint32_t)nv * COUT * D * 4);
-            bulk_commit();
-            stored = true;
-        }
-    }
-    if (tid == 0) {
-        // before TMEM and shared memory are released, everything in flight lands, also after a
-        // wait ran out: the weight copies, every MMA issued (this thread issued them all) and the
-        // last output rows
-        mbar_wait_drain(&w_bar, 0);
-        umma_commit(&drain_bar);
-        mbar_wait_drain(&drain_bar, 0);
-        bulk_wait0();
+        if (lane == 0) bulk_wait0();
     }
     tc_fence_before();
     __syncthreads();
     if (warp == 0) {
         tc_fence_after();
-        tmem_dealloc(tmem, G::TALLOC);
+        tmem_dealloc(tmem, TALLOC);
     }
+    if (threadIdx.x == 0 && abort_s) set_status(status, 2);
 }
 
 template <int L, int CIN, int COUT, bool kSplit>
 int run(const float *x, int64_t N, const float *w, const float *bias, float *y, void *ws, size_t ws_bytes,
         int32_t *status, cudaStream_t s) {
     constexpr size_t smem = smem_bytes<L, CIN, COUT, kSplit>();
+    static_assert(smem <= 227 * 1024, "shared memory of one CTA");
     if (ws_bytes < w_bytes<L, CIN, COUT, kSplit>() || !ws) return FEQ_ERR_WORKSPACE;
     uint8_t *wt = static_cast<uint8_t *>(ws);
     const int total = NG<L, CIN, COUT>::NR * COUT * CIN;
@@ -291,7 +374,7 @@ int run(const float *x, int64_t N, const float *w, const float *bias, float *y, 
     FEQ_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     const int64_t ntiles = (N + TN - 1) / TN;
     const int64_t grid = ntiles < sms ? ntiles : sms;
-    kern<<<(unsigned)grid, kThreads, smem, s>>>(x, N, wt, bias, y, ntiles, status, wait_limit_ns());
+    kern<<<(unsigned)grid, Roles<L, CIN>::THREADS, smem, s>>>(x, N, wt, bias, y, ntiles, status, wait_limit_ns());
     FEQ_LAUNCH_CHECK();
     return FEQ_OK;
 }
