@@ -214,19 +214,37 @@ dense_kernel(const float *__restrict__ x, int64_t N, int M, int K, const uint8_t
                 break;
             }
             const int64_t r0 = (blockIdx.x + i * gridDim.x) * TR;
-            for (int idx = ct; idx < TR * rows_f4; idx += 128) {
-                const int r = idx / rows_f4, c4 = idx - r * rows_f4;
-                float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (r0 + r < N) v = __ldg(reinterpret_cast<const float4 *>(x + (r0 + r) * (int64_t)K) + c4);
-                const float vv[4] = {v.x, v.y, v.z, v.w};
+            // the tile's rows in batches of kBatch 16-byte loads per thread, all in flight before
+            // any is converted (one memory latency per batch, not per load)
+            constexpr int kBatch = 16;
+            const int total4 = TR * rows_f4;
+            for (int base = ct; base < total4; base += 128 * kBatch) {
+                float4 v[kBatch];
 #pragma unroll
-                for (int e = 0; e < 4; e++) {
-                    const int k = c4 * 4 + e;
-                    uint8_t *chunk = xs + (size_t)((k >> 6) * SP) * kXChunk;
-                    const uint32_t o = swz(r, k & 63);
-                    const __nv_bfloat16 hi = __float2bfloat16_rn(vv[e]);
-                    *reinterpret_cast<__nv_bfloat16 *>(chunk + o) = hi;
-                    if (kSplit) *reinterpret_cast<__nv_bfloat16 *>(chunk + kXChunk + o) = __float2bfloat16_rn(vv[e] - __bfloat162float(hi));
+                for (int u = 0; u < kBatch; u++) {
+                    const int idx = base + 128 * u;
+                    const int r = idx / rows_f4, c4 = idx - r * rows_f4;
+                    v[u] = (idx < total4 && r0 + r < N)
+                               ? __ldg(reinterpret_cast<const float4 *>(x + (r0 + r) * (int64_t)K) + c4)
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+#pragma unroll
+                for (int u = 0; u < kBatch; u++) {
+                    const int idx = base + 128 * u;
+                    if (idx >= total4) break;
+                    const int r = idx / rows_f4, c4 = idx - r * rows_f4;
+                    const float vv[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        const int k = c4 * 4 + e;
+                        uint8_t *chunk = xs + (size_t)((k >> 6) * SP) * kXChunk;
+                        const uint32_t o = swz(r, k & 63);
+                        const __nv_bfloat16 hi = __float2bfloat16_rn(vv[e]);
+                        *reinterpret_cast<__nv_bfloat16 *>(chunk + o) = hi;
+                        if (kSplit)
+                            *reinterpret_cast<__nv_bfloat16 *>(chunk + kXChunk + o) =
+                                __float2bfloat16_rn(vv[e] - __bfloat162float(hi));
+                    }
                 }
             }
             fence_async_smem();
