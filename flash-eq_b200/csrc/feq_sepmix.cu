@@ -37,8 +37,8 @@
 //               N-side tile; per edge also the lerped g_k for the epilogue
 //   then EWG    epilogue warpgroups: tcgen05.ld of Z, position mix, sum over k across lane
 //               pairs, rotation back, bulk store
-//   (L <= 2: 8 rotation warps, 3 epilogue warpgroups; L = 3: 4 and 2; L = 4: 4 and 1)
-// Rings: input rows, 2 N-side tiles, 2 TMEM accumulator sets, 4 (L <= 2) or 3 per-tile
+//   (L <= 2: 8 rotation warps, 3 epilogue warpgroups; L >= 3: 4 and 2)
+// Rings: input rows, 2 N-side tiles, 2 TMEM accumulator sets, 4 (L <= 2) or 2 per-tile
 // slots.  Every wait is bounded (limit from the launch); on time-out the kernel sets status
 // 2, drains its copies and MMAs, frees TMEM and returns.  No TMA multicast anywhere.
 //
@@ -153,9 +153,11 @@ struct Geo {
     static constexpr int J_S = ROTREC ? 3 : REC_S, J_T = J_S + 1, J_LO = J_S + 2, J_FLAG = J_S + 3;
     static constexpr int JOB_FLOATS = ROTREC ? 8 : REC_FLOATS;
     static constexpr int FR = ROTREC ? 0 : (2 * kRank * W + 3) & ~3;     // feature-row floats per entry
-    // per-tile slots of edge scalars: 4, or 3 at L >= 3 where shared memory is short (the
-    // rotation warps then run at most 3 tiles ahead of the epilogue)
-    static constexpr int SLOTS = ROTREC ? 3 : 4;
+    // per-tile slots of edge scalars: 4, or 2 at L >= 3 where shared memory is short (the
+    // rotation warps then run at most 2 tiles ahead of the epilogue; the memory goes to the
+    // row ring instead: at L = 4 with two epilogue warpgroups 8 rows instead of 4, 6.1 -> 5.4 ms
+    // on 640 000 edges)
+    static constexpr int SLOTS = ROTREC ? 2 : 4;
 };
 
 struct SepParams {
@@ -1015,11 +1017,11 @@ int launch(SepParams P, cudaStream_t stream) {
 template <bool kSplit>
 int dispatch(int lin, int lout, const SepParams &P, cudaStream_t s) {
     // as many warps as the registers allow: L <= 2 (80 registers) 8 rotation warps and three
-    // epilogue warpgroups, L = 3 (128) 4 and two, L = 4 (168) 4 and one
+    // epilogue warpgroups, L >= 3 (128) 4 and two
     if (lin == 1 && lout == 1) return launch<1, 1, kSplit, 3, 8>(P, s);
     if (lin == 2 && lout == 2) return launch<2, 2, kSplit, 3, 8>(P, s);
     if (lin == 3 && lout == 3) return launch<3, 3, kSplit, 2, 4>(P, s);
-    if (lin == 4 && lout == 4) return launch<4, 4, kSplit, 1, 4>(P, s);
+    if (lin == 4 && lout == 4) return launch<4, 4, kSplit, 2, 4>(P, s);
     return FEQ_ERR_UNSUPPORTED;
 }
 
