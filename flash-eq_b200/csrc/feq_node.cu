@@ -112,8 +112,29 @@ __device__ __forceinline__ void stage_row(float *row, const float *src, int n, i
 // from a flat index.
 __host__ __device__ __forceinline__ int odd_stride(int d) { return d | 1; }
 
-// Node row -> row[c * ds + p]: a straight float4 copy when ds == d, else scalar loads
-// (all of a batch issued before its stores) scattered through a RowWalk.
+// Float4 i of a row with d % 4 == 0 holds positions 4q .. 4q + 3 of one channel c; walk
+// (c, q) for i = lane, lane + 32, ... without a division per step.
+struct QuadWalk {
+    int c, q, dc, dq, d4;
+    __device__ __forceinline__ QuadWalk(int lane, int d4_) : d4(d4_) {
+        c = lane / d4_;
+        q = lane - c * d4_;
+        dc = 32 / d4_;
+        dq = 32 - dc * d4_;
+    }
+    __device__ __forceinline__ void next() {
+        c += dc;
+        q += dq;
+        if (q >= d4) {
+            q -= d4;
+            c++;
+        }
+    }
+};
+
+// Node row -> row[c * ds + p]: a straight float4 copy when ds == d; for d % 4 == 0 float4
+// loads (four positions of one channel each) scattered to the padded rows; else scalar loads.
+// All of a batch's loads are issued before its stores.
 __device__ __forceinline__ void stage_row_ds(float *row, const float *src, int C, int d, int ds, int lane) {
     const int n = C * d;
     if (ds == d) {
@@ -121,6 +142,30 @@ __device__ __forceinline__ void stage_row_ds(float *row, const float *src, int C
         return;
     }
     constexpr int kB = 8;
+    if ((d & 3) == 0 && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+        constexpr int kB4 = 4;                // float4s per lane in flight (registers are short)
+        const float4 *s4 = reinterpret_cast<const float4 *>(src);
+        const int n4 = n / 4;
+        QuadWalk w(lane, d / 4);
+        for (int i0 = lane; i0 < n4; i0 += 32 * kB4) {
+            float4 v[kB4];
+#pragma unroll
+            for (int u = 0; u < kB4; u++)
+                if (i0 + 32 * u < n4) v[u] = __ldg(s4 + i0 + 32 * u);
+#pragma unroll
+            for (int u = 0; u < kB4; u++)
+                if (i0 + 32 * u < n4) {
+                    float *r = row + w.c * ds + 4 * w.q;
+                    r[0] = v[u].x;
+                    r[1] = v[u].y;
+                    r[2] = v[u].z;
+                    r[3] = v[u].w;
+                    w.next();
+                }
+        }
+        __syncwarp();
+        return;
+    }
     RowWalk w(lane, d);
     for (int i0 = lane; i0 < n; i0 += 32 * kB) {
         float v[kB];
@@ -147,6 +192,13 @@ __device__ __forceinline__ void write_row_ds(float *dst, const float *row, int C
         for (int i = lane; i < n / 4; i += 32) d4[i] = r4[i];
     } else if (ds == d) {
         for (int i = lane; i < n; i += 32) dst[i] = row[i];
+    } else if ((d & 3) == 0 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+        float4 *d4 = reinterpret_cast<float4 *>(dst);
+        QuadWalk w(lane, d / 4);
+        for (int i = lane; i < n / 4; i += 32, w.next()) {
+            const float *r = row + w.c * ds + 4 * w.q;
+            d4[i] = make_float4(r[0], r[1], r[2], r[3]);
+        }
     } else {
         RowWalk w(lane, d);
         for (int i = lane; i < n; i += 32, w.next()) dst[i] = row[w.c * ds + w.p];
@@ -204,8 +256,9 @@ __global__ void __launch_bounds__(kNodeWarps * 32, kNodeBlocksPerSm) sep_layerno
     extern __shared__ float nsm[];
     const int C = a.R.C, d = a.R.d, n = C * d, ds = odd_stride(d), ns = a.nscalar;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    float *buf = nsm + (size_t)warp * 2 * C * ds;
-    float *ws = nsm + (size_t)kNodeWarps * 2 * C * ds, *bs = ws + C * ns, *wh = bs + C * ns;
+    constexpr int kSlots = kAsync ? 2 : 1;      // row buffers per warp (the next row in flight)
+    float *buf = nsm + (size_t)warp * kSlots * C * ds;
+    float *ws = nsm + (size_t)kNodeWarps * kSlots * C * ds, *bs = ws + C * ns, *wh = bs + C * ns;
     __shared__ float mu_s[kNodeWarps][kNodeMaxScalars], inv_s[kNodeWarps][kNodeMaxScalars];
     __shared__ int8_t sidx_s[kMaxDim];
     for (int i = threadIdx.x; i < d; i += blockDim.x) sidx_s[i] = a.scalar_idx[i];
@@ -291,8 +344,9 @@ __global__ void __launch_bounds__(kNodeWarps * 32, kNodeBlocksPerSm) equi_layern
     extern __shared__ float nsm[];
     const int C = a.R.C, d = a.R.d, n = C * d, nr = a.R.n_irreps, ds = odd_stride(d), nrs = odd_stride(nr);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    float *buf = nsm + (size_t)warp * (2 * C * ds + C * nrs);
-    float *nrm = buf + 2 * C * ds;      // norms, then the rescaling factors
+    constexpr int kSlots = kAsync ? 2 : 1;
+    float *buf = nsm + (size_t)warp * (kSlots * C * ds + C * nrs);
+    float *nrm = buf + kSlots * C * ds;      // norms, then the rescaling factors
     __shared__ int8_t pirr_s[kMaxDim];
     __shared__ int16_t ioff_s[kNodeMaxIrreps], ik_s[kNodeMaxIrreps];
     for (int i = threadIdx.x; i < d; i += blockDim.x) pirr_s[i] = a.R.pos_irr[i];
@@ -347,7 +401,8 @@ __global__ void __launch_bounds__(kNodeWarps * 32, kNodeBlocksPerSm) rep_norm_ke
     extern __shared__ float nsm[];
     const int C = a.R.C, d = a.R.d, nr = a.R.n_irreps, ds = odd_stride(d);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    float *buf = nsm + (size_t)warp * 2 * C * ds;
+    constexpr int kSlots = kAsync ? 2 : 1;
+    float *buf = nsm + (size_t)warp * kSlots * C * ds;
     __shared__ int16_t ioff_s[kNodeMaxIrreps], ik_s[kNodeMaxIrreps];
     for (int i = threadIdx.x; i < nr; i += blockDim.x) {
         ioff_s[i] = a.R.irr_off[i];
@@ -375,8 +430,9 @@ __global__ void __launch_bounds__(kNodeWarps * 32, kNodeBlocksPerSm) gate_kernel
     extern __shared__ float nsm[];
     const int C = a.R.C, d = a.R.d, n = C * d, nr = a.R.n_irreps, ds = odd_stride(d);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    float *buf = nsm + (size_t)warp * (2 * C * ds + C * nr);
-    float *gs = buf + 2 * C * ds;
+    constexpr int kSlots = kAsync ? 2 : 1;
+    float *buf = nsm + (size_t)warp * (kSlots * C * ds + C * nr);
+    float *gs = buf + kSlots * C * ds;
     __shared__ int8_t pirr_s[kMaxDim];
     for (int i = threadIdx.x; i < d; i += blockDim.x) pirr_s[i] = a.R.pos_irr[i];
     __syncthreads();
@@ -429,18 +485,78 @@ __device__ __forceinline__ void pm_load_tile(float *tsm, const float *src, int t
     }
 }
 
+// Walk (a, b) = (i / period, i % period) for i = start, start + step, ... without a division
+// per step.
+struct StepWalk {
+    int a, b, da, db, period;
+    __device__ __forceinline__ StepWalk(int start, int period_, int step) : period(period_) {
+        a = start / period_;
+        b = start - a * period_;
+        da = step / period_;
+        db = step - da * period_;
+    }
+    __device__ __forceinline__ void next() {
+        a += da;
+        b += db;
+        if (b >= period) {
+            b -= period;
+            a++;
+        }
+    }
+};
+
+// Rows of d floats (global, contiguous) <-> shared memory rows at the odd stride dsp > d, so
+// that reading one position of consecutive rows does not fall on one bank (at d = 16 a
+// stride of d put all 32 lanes on two banks).  Float4 on the global side when d % 4 == 0.
+__device__ __forceinline__ void pm_load_tile_padded(float *tsm, const float *src, int rows, int d, int dsp) {
+    if ((d & 3) == 0 && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+        const float4 *s4 = reinterpret_cast<const float4 *>(src);
+        StepWalk w(threadIdx.x, d / 4, blockDim.x);
+        for (int i = threadIdx.x; i < rows * d / 4; i += blockDim.x, w.next()) {
+            const float4 v = __ldg(s4 + i);
+            float *t = tsm + w.a * dsp + 4 * w.b;
+            t[0] = v.x;
+            t[1] = v.y;
+            t[2] = v.z;
+            t[3] = v.w;
+        }
+    } else {
+        StepWalk w(threadIdx.x, d, blockDim.x);
+        for (int i = threadIdx.x; i < rows * d; i += blockDim.x, w.next()) tsm[w.a * dsp + w.b] = __ldg(src + i);
+    }
+}
+
+__device__ __forceinline__ void pm_store_tile_padded(float *dst, const float *tsm, int rows, int d, int dsp) {
+    if ((d & 3) == 0 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+        float4 *d4 = reinterpret_cast<float4 *>(dst);
+        StepWalk w(threadIdx.x, d / 4, blockDim.x);
+        for (int i = threadIdx.x; i < rows * d / 4; i += blockDim.x, w.next()) {
+            const float *t = tsm + w.a * dsp + 4 * w.b;
+            d4[i] = make_float4(t[0], t[1], t[2], t[3]);
+        }
+    } else {
+        StepWalk w(threadIdx.x, d, blockDim.x);
+        for (int i = threadIdx.x; i < rows * d; i += blockDim.x, w.next()) dst[i] = tsm[w.a * dsp + w.b];
+    }
+}
+
 __global__ void __launch_bounds__(256) to_posmajor_kernel(const float *__restrict__ x, int64_t N, int C, int d,
                                                           int tn, float *__restrict__ xt) {
     extern __shared__ float tsm[];
     const int64_t n0 = (int64_t)blockIdx.x * tn;
     const int nn = (int)min64(tn, N - n0);
-    pm_load_tile(tsm, x + n0 * C * d, nn * C * d);
+    const int dsp = odd_stride(d);           // shared-memory row stride (== d for odd d)
+    if (dsp == d)
+        pm_load_tile(tsm, x + n0 * C * d, nn * C * d);
+    else
+        pm_load_tile_padded(tsm, x + n0 * C * d, nn * C, d, dsp);
     __syncthreads();
     const int slab = nn * C;                 // (nodes x channels) of one position, a multiple of 4
     for (int p = 0; p < d; p++) {
         float4 *dst = reinterpret_cast<float4 *>(xt + (int64_t)p * N * C + n0 * C);
         for (int r = 4 * threadIdx.x; r < slab; r += 4 * blockDim.x)     // r = node * C + c
-            dst[r / 4] = make_float4(tsm[r * d + p], tsm[(r + 1) * d + p], tsm[(r + 2) * d + p], tsm[(r + 3) * d + p]);
+            dst[r / 4] = make_float4(tsm[r * dsp + p], tsm[(r + 1) * dsp + p], tsm[(r + 2) * dsp + p],
+                                     tsm[(r + 3) * dsp + p]);
     }
 }
 
@@ -453,6 +569,7 @@ __global__ void __launch_bounds__(256) from_posmajor_kernel(const float *__restr
     const int64_t n0 = (int64_t)blockIdx.x * tn;
     const int nn = (int)min64(tn, N - n0);
     const int slab = nn * C;
+    const int dsp = odd_stride(d);
     for (int p = 0; p < d; p++) {
         const float4 *src = reinterpret_cast<const float4 *>(yt + (int64_t)p * N * C + n0 * C);
         const int sb = (bias && scalar_idx_d) ? scalar_idx_d[p] : -1;
@@ -465,16 +582,18 @@ __global__ void __launch_bounds__(256) from_posmajor_kernel(const float *__restr
                 v.z += __ldg(bias + (c + 2) * nscalar + sb);
                 v.w += __ldg(bias + (c + 3) * nscalar + sb);
             }
-            tsm[r * d + p] = v.x;
-            tsm[(r + 1) * d + p] = v.y;
-            tsm[(r + 2) * d + p] = v.z;
-            tsm[(r + 3) * d + p] = v.w;
+            tsm[r * dsp + p] = v.x;
+            tsm[(r + 1) * dsp + p] = v.y;
+            tsm[(r + 2) * dsp + p] = v.z;
+            tsm[(r + 3) * dsp + p] = v.w;
         }
     }
     __syncthreads();
     const int tile = slab * d;
     float *dst = y + n0 * C * d;
-    if ((tile & 3) == 0 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+    if (dsp != d) {
+        pm_store_tile_padded(dst, tsm, slab, d, dsp);
+    } else if ((tile & 3) == 0 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
         for (int i = threadIdx.x; i < tile / 4; i += blockDim.x)
             reinterpret_cast<float4 *>(dst)[i] = reinterpret_cast<const float4 *>(tsm)[i];
     } else {
@@ -506,6 +625,10 @@ int fill_node_repr(const int32_t *lvals, int32_t n, int32_t C, NodeRepr *R) {
 bool node_async(const float *x, int C, int d) {
     return (d & 1) && ((int64_t)C * d) % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
 }
+
+// row buffers per warp: two on the cp.async pipeline (the next row lands while the current
+// one is transformed), one when rows are staged through registers
+int node_slots(bool async) { return async ? 2 : 1; }
 
 int node_grid(int64_t N) { return (int)min64((N + kNodeWarps - 1) / kNodeWarps, 148 * 16); }
 
@@ -550,8 +673,10 @@ int feq_node_sep_layernorm(const float *x, int64_t num_nodes, int32_t C, const i
     a.eps = eps;
     a.out = out;
     a.N = num_nodes;
-    const size_t smem = sizeof(float) * ((size_t)kNodeWarps * 2 * C * odd_stride(a.R.d) + (size_t)C * (2 * a.nscalar + 1));
-    const auto k = node_async(x, C, a.R.d) ? sep_layernorm_kernel<true> : sep_layernorm_kernel<false>;
+    const bool async = node_async(x, C, a.R.d);
+    const size_t smem = sizeof(float) * ((size_t)kNodeWarps * node_slots(async) * C * odd_stride(a.R.d) +
+                                         (size_t)C * (2 * a.nscalar + 1));
+    const auto k = async ? sep_layernorm_kernel<true> : sep_layernorm_kernel<false>;
     if ((rc = set_smem((const void *)k, smem)) != FEQ_OK) return rc;
     ProfScope ps("node_norm", (cudaStream_t)stream);
     k<<<node_grid(num_nodes), kNodeWarps * 32, smem, (cudaStream_t)stream>>>(a);
@@ -577,8 +702,10 @@ int feq_node_layernorm(const float *x, int64_t num_nodes, int32_t C, const int32
     a.eps = eps;
     a.out = out;
     a.N = num_nodes;
-    const size_t smem = sizeof(float) * kNodeWarps * ((size_t)2 * C * odd_stride(a.R.d) + (size_t)C * odd_stride(n_lvals));
-    const auto k = node_async(x, C, a.R.d) ? equi_layernorm_kernel<true> : equi_layernorm_kernel<false>;
+    const bool async = node_async(x, C, a.R.d);
+    const size_t smem = sizeof(float) * kNodeWarps *
+                        ((size_t)node_slots(async) * C * odd_stride(a.R.d) + (size_t)C * odd_stride(n_lvals));
+    const auto k = async ? equi_layernorm_kernel<true> : equi_layernorm_kernel<false>;
     if ((rc = set_smem((const void *)k, smem)) != FEQ_OK) return rc;
     ProfScope ps("node_norm", (cudaStream_t)stream);
     k<<<node_grid(num_nodes), kNodeWarps * 32, smem, (cudaStream_t)stream>>>(a);
@@ -599,8 +726,9 @@ int feq_node_rep_norm(const float *x, int64_t num_nodes, int32_t C, const int32_
     a.eps = eps;
     a.norms = norms;
     a.N = num_nodes;
-    const size_t smem = sizeof(float) * kNodeWarps * (size_t)2 * C * odd_stride(a.R.d);
-    const auto k = node_async(x, C, a.R.d) ? rep_norm_kernel<true> : rep_norm_kernel<false>;
+    const bool async = node_async(x, C, a.R.d);
+    const size_t smem = sizeof(float) * kNodeWarps * (size_t)node_slots(async) * C * odd_stride(a.R.d);
+    const auto k = async ? rep_norm_kernel<true> : rep_norm_kernel<false>;
     if ((rc = set_smem((const void *)k, smem)) != FEQ_OK) return rc;
     ProfScope ps("node_norm", (cudaStream_t)stream);
     k<<<node_grid(num_nodes), kNodeWarps * 32, smem, (cudaStream_t)stream>>>(a);
@@ -613,9 +741,9 @@ int feq_node_to_posmajor(const float *x, int64_t num_nodes, int32_t C, int32_t d
     if (num_nodes == 0) return FEQ_OK;
     if (!x || !xt) return FEQ_ERR_INVALID_ARGUMENT;
     if (C % 4 || (reinterpret_cast<uintptr_t>(xt) & 15)) return FEQ_ERR_UNSUPPORTED;
-    const int tn = pm_nodes(C, d);
+    const int tn = pm_nodes(C, odd_stride(d));
     if (tn < 1) return FEQ_ERR_UNSUPPORTED;
-    const size_t smem = sizeof(float) * tn * (size_t)C * d;
+    const size_t smem = sizeof(float) * tn * (size_t)C * odd_stride(d);
     int rc;
     if ((rc = set_smem((const void *)to_posmajor_kernel, smem)) != FEQ_OK) return rc;
     ProfScope ps("node_layout", (cudaStream_t)stream);
@@ -636,9 +764,9 @@ int feq_node_from_posmajor(const float *yt, int64_t num_nodes, int32_t C, const 
     if (C % 4 || (reinterpret_cast<uintptr_t>(yt) & 15)) return FEQ_ERR_UNSUPPORTED;
     int nscalar = 0;
     for (int r = 0; r < n_lvals; r++) nscalar += lvals[r] == 0;
-    const int tn = pm_nodes(C, R.d);
+    const int tn = pm_nodes(C, odd_stride(R.d));
     if (tn < 1) return FEQ_ERR_UNSUPPORTED;
-    const size_t smem = sizeof(float) * tn * (size_t)C * R.d;
+    const size_t smem = sizeof(float) * tn * (size_t)C * odd_stride(R.d);
     if ((rc = set_smem((const void *)from_posmajor_kernel, smem)) != FEQ_OK) return rc;
     ProfScope ps("node_layout", (cudaStream_t)stream);
     from_posmajor_kernel<<<(unsigned)((num_nodes + tn - 1) / tn), 256, smem, (cudaStream_t)stream>>>(
@@ -660,8 +788,10 @@ int feq_node_gate(const float *x, const float *z, int64_t num_nodes, int32_t C, 
     a.z = z;
     a.out = out;
     a.N = num_nodes;
-    const size_t smem = sizeof(float) * kNodeWarps * ((size_t)2 * C * odd_stride(a.R.d) + (size_t)C * n_lvals);
-    const auto k = node_async(x, C, a.R.d) ? gate_kernel<true> : gate_kernel<false>;
+    const bool async = node_async(x, C, a.R.d);
+    const size_t smem =
+        sizeof(float) * kNodeWarps * ((size_t)node_slots(async) * C * odd_stride(a.R.d) + (size_t)C * n_lvals);
+    const auto k = async ? gate_kernel<true> : gate_kernel<false>;
     if ((rc = set_smem((const void *)k, smem)) != FEQ_OK) return rc;
     ProfScope ps("node_gate", (cudaStream_t)stream);
     k<<<node_grid(num_nodes), kNodeWarps * 32, smem, (cudaStream_t)stream>>>(a);
