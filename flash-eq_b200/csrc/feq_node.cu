@@ -19,6 +19,7 @@
 #include <string.h>
 
 #include <algorithm>
+#include <mutex>
 
 #include "feq_internal.cuh"
 
@@ -630,7 +631,39 @@ bool node_async(const float *x, int C, int d) {
 // one is transformed), one when rows are staged through registers
 int node_slots(bool async) { return async ? 2 : 1; }
 
-int node_grid(int64_t N) { return (int)min64((N + kNodeWarps - 1) / kNodeWarps, 148 * 16); }
+// One wave of blocks: as many as are resident on the device at once for this kernel and
+// shared memory (occupancy, cached per kernel and size), each warp then walking its nodes
+// with the next row in flight.  More blocks than that only add waves, each reloading the
+// block's weights; at a few thousand nodes (config 3) the tail of a second wave was most of
+// the launch.
+int node_grid(const void *fn, size_t smem, int64_t N) {
+    const int64_t want = (N + kNodeWarps - 1) / kNodeWarps;
+    struct Entry {
+        const void *fn;
+        size_t smem;
+        int dev, blocks;
+    };
+    static Entry cache[16];
+    static int used = 0;
+    static std::mutex mu;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
+    {
+        std::lock_guard<std::mutex> g(mu);
+        for (int i = 0; i < used; i++)
+            if (cache[i].fn == fn && cache[i].smem == smem && cache[i].dev == dev) return (int)min64(want, cache[i].blocks);
+    }
+    int sms = 0, per_sm = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms < 1) sms = 148;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kNodeWarps * 32, smem) != cudaSuccess || per_sm < 1)
+        per_sm = 1;
+    const int blocks = sms * per_sm;
+    {
+        std::lock_guard<std::mutex> g(mu);
+        if (used < 16) cache[used++] = Entry{fn, smem, dev, blocks};
+    }
+    return (int)min64(want, blocks);
+}
 
 int set_smem(const void *fn, size_t smem) {
     if (smem > 200 * 1024) return FEQ_ERR_UNSUPPORTED;
@@ -679,7 +712,7 @@ int feq_node_sep_layernorm(const float *x, int64_t num_nodes, int32_t C, const i
     const auto k = async ? sep_layernorm_kernel<true> : sep_layernorm_kernel<false>;
     if ((rc = set_smem((const void *)k, smem)) != FEQ_OK) return rc;
     ProfScope ps("node_norm", (cudaStream_t)stream);
-    k<<<node_grid(num_nodes), kNodeWarps * 32, smem, (cudaStream_t)stream>>>(a);
+    k<<<node_grid((const void *)k, smem, num_nodes), kNodeWarps * 32, smem, (cudaStream_t)stream>>>(a);
     FEQ_LAUNCH_CHECK();
     return FEQ_OK;
 }
@@ -708,7 +741,7 @@ int feq_node_layernorm(const float *x, int64_t num_nodes, int32_t C, const int32
     const auto k = async ? equi_layernorm_kernel<true> : equi_layernorm_kernel<false>;
     if ((rc = set_smem((const void *)k, smem)) != FEQ_OK) return rc;
     ProfScope ps("node_norm", (cudaStream_t)stream);
-    k<<<node_grid(num_nodes), kNodeWarps * 32, smem, (cudaStream_t)stream>>>(a);
+    k<<<node_grid((const void *)k, smem, num_nodes), kNodeWarps * 32, smem, (cudaStream_t)stream>>>(a);
     FEQ_LAUNCH_CHECK();
     return FEQ_OK;
 }
@@ -731,7 +764,7 @@ int feq_node_rep_norm(const float *x, int64_t num_nodes, int32_t C, const int32_
     const auto k = async ? rep_norm_kernel<true> : rep_norm_kernel<false>;
     if ((rc = set_smem((const void *)k, smem)) != FEQ_OK) return rc;
     ProfScope ps("node_norm", (cudaStream_t)stream);
-    k<<<node_grid(num_nodes), kNodeWarps * 32, smem, (cudaStream_t)stream>>>(a);
+    k<<<node_grid((const void *)k, smem, num_nodes), kNodeWarps * 32, smem, (cudaStream_t)stream>>>(a);
     FEQ_LAUNCH_CHECK();
     return FEQ_OK;
 }
@@ -794,7 +827,7 @@ int feq_node_gate(const float *x, const float *z, int64_t num_nodes, int32_t C, 
     const auto k = async ? gate_kernel<true> : gate_kernel<false>;
     if ((rc = set_smem((const void *)k, smem)) != FEQ_OK) return rc;
     ProfScope ps("node_gate", (cudaStream_t)stream);
-    k<<<node_grid(num_nodes), kNodeWarps * 32, smem, (cudaStream_t)stream>>>(a);
+    k<<<node_grid((const void *)k, smem, num_nodes), kNodeWarps * 32, smem, (cudaStream_t)stream>>>(a);
     FEQ_LAUNCH_CHECK();
     return FEQ_OK;
 }
