@@ -3,17 +3,21 @@
 // reference: the (C * n_irreps)^2 mix of the irrep norms before the sigmoid gate).
 //
 // X (N, K) and Y (N, M) float32 row-major, W (M, K) float32 (nn.Linear's weight), b (M,).
-// M a multiple of 128 up to 512, K a multiple of 64 up to 512.
-//   - a tile is 64 rows of X: four converter warps load them (16-byte loads) and write the
-//     K-major, 128-byte-swizzled bf16 operand (hi, and lo for bf16x3), K in chunks of 64;
-//   - W is re-laid once per call into swizzled bf16 tiles of 128 x 64 (hi / lo) by
-//     dense_wtiles_kernel and streamed from L2, tile pair after tile pair, through a two-stage
-//     shared-memory ring by a producer warp (bulk copies, mbarriers);
-//   - one thread issues tcgen05.mma kind::f16 (M = 128 rows of W, N = 64 rows of X, K = 16),
-//     bf16x3 accumulating hi.hi + hi.lo + lo.hi, into one of two TMEM accumulator sets, so the
-//     epilogue of a tile overlaps the MMAs of the next;
-//   - the converter warps are also the epilogue: tcgen05.ld (lane = output feature), + b, and
-//     coalesced stores (a warp writes 32 consecutive features of a row).
+// M a multiple of 128 up to 512, K a multiple of 64 up to 512.  A tile is 64 rows of X.
+// Warp-specialised, persistent (one CTA per SM), every role on its own mbarriers:
+//   warp 0      W producer: W is re-laid once per call into swizzled bf16 tiles of 128 x 64
+//               (hi / lo) by dense_wtiles_kernel and streamed from L2, tile pair after tile
+//               pair in the MMA's order, through a shared-memory ring (bulk copies)
+//   warp 1      one thread issues tcgen05.mma kind::f16 (M = 128 rows of W, N = 64 rows of X,
+//               K = 16), bf16x3 accumulating hi.hi + hi.lo + lo.hi, K chunk by K chunk (all
+//               M tiles of a chunk before the next chunk), into one of two TMEM accumulator
+//               sets
+//   warps 2..5  converters: each takes 16 rows of every 64-column K chunk of X (16-byte
+//               loads, the next two chunks' in flight while this one is converted) and writes the
+//               K-major, 128-byte-swizzled bf16 operand (hi, and lo for bf16x3) into a ring of
+//               chunk slots, so the conversion of a tile overlaps the MMAs of the one before
+//   warps 6..9  epilogue: tcgen05.ld (lane = output feature), + b, coalesced stores (a warp
+//               writes 32 consecutive features of a row), overlapping the next tile's MMAs
 // Every wait is bounded; on time-out the kernel sets status 2, drains and leaves.  No TMA
 // multicast.
 #include <cuda.h>
@@ -32,8 +36,10 @@ using namespace sm100;
 using namespace rot;
 
 constexpr int TR = 64;                    // rows of X per tile (UMMA N)
-constexpr int kThreads = 192;             // warp 0 producer + TMEM, warp 1 MMA, warps 2..5 convert / epilogue
-constexpr int kMaxStages = 4;             // W tile-pair ring: 4 stages where shared memory allows, else 2
+constexpr int kConvWarps = 4, kEpiWarps = 4;
+constexpr int kThreads = (2 + kConvWarps + kEpiWarps) * 32;   // producer, MMA, converters, epilogue
+constexpr int kMaxStages = 12;            // W tile-pair ring
+constexpr int kMaxXSlots = 8;             // X chunk ring
 constexpr uint32_t kWTile = 128 * 128;    // 128 rows x 64 bf16
 constexpr uint32_t kXChunk = TR * 128;    // 64 rows x 64 bf16
 constexpr int kMaxM = 512, kMaxK = 512;
@@ -59,37 +65,39 @@ __global__ void dense_wtiles_kernel(const float *__restrict__ w, int M, int K, u
     }
 }
 
-__device__ __forceinline__ void named_bar(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
 
 template <bool kSplit>
 __global__ void __launch_bounds__(kThreads, 1)
 dense_kernel(const float *__restrict__ x, int64_t N, int M, int K, const uint8_t *__restrict__ wt,
-             const float *__restrict__ bias, float *__restrict__ y, int64_t ntiles, int stages, int32_t *status,
-             uint64_t wait_ns) {
+             const float *__restrict__ bias, float *__restrict__ y, int64_t ntiles, int stages, int xslots,
+             int32_t *status, uint64_t wait_ns) {
     constexpr int SP = kSplit ? 2 : 1;
     const int MT = M >> 7, KC = K >> 6;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *wring = smem;                                    // stages x SP x kWTile
-    uint8_t *xs = wring + (size_t)stages * SP * kWTile;      // KC x SP x kXChunk
+    uint8_t *xring = wring + (size_t)stages * SP * kWTile;   // xslots x SP x kXChunk
 
-    __shared__ uint64_t w_full[kMaxStages], w_empty[kMaxStages], x_ready, t_full[2], t_empty[2], drain_bar;
+    __shared__ uint64_t w_full[kMaxStages], w_empty[kMaxStages], x_full[kMaxXSlots], x_empty[kMaxXSlots];
+    __shared__ uint64_t t_full[2], t_empty[2], drain_bar;
     __shared__ uint32_t tmem_s;
-    __shared__ int abort_s, conv_stop_s;
+    __shared__ int abort_s;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
         for (int s = 0; s < stages; s++) {
             mbar_init(&w_full[s], 1);
             mbar_init(&w_empty[s], 1);
         }
-        mbar_init(&x_ready, 1);
+        for (int s = 0; s < xslots; s++) {
+            mbar_init(&x_full[s], kConvWarps);
+            mbar_init(&x_empty[s], 1);
+        }
         for (int b = 0; b < 2; b++) {
             mbar_init(&t_full[b], 1);
-            mbar_init(&t_empty[b], 4);
+            mbar_init(&t_empty[b], kEpiWarps);
         }
         mbar_init(&drain_bar, 1);
         abort_s = 0;
-        conv_stop_s = 0;
         fence_mbar_init();
     }
     const uint32_t tcols = (uint32_t)(2 * MT * TR) <= 256 ? 256u : 512u;
@@ -103,20 +111,26 @@ dense_kernel(const float *__restrict__ x, int64_t N, int M, int K, const uint8_t
     const uint32_t tmem = tmem_s;
     volatile int *abort_flag = &abort_s;
     const int64_t n_local = ntiles > blockIdx.x ? (ntiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
-    const int pairs = MT * KC;                                // W tile pairs per row tile
 
     if (warp == 0) {
-        // ---------------- W producer ----------------
+        // ---------------- W producer: pairs in the MMA's order (chunk kc, then tile mt) ----------------
         if (lane == 0) {
             uint32_t u = 0;
             for (int64_t i = 0; i < n_local && !*abort_flag; i++) {
-                for (int p = 0; p < pairs; p++, u++) {
-                    const int s = (int)(u % stages);
-                    if (u >= (uint32_t)stages && !mbar_wait(&w_empty[s], ((u / stages) - 1) & 1u, abort_flag, wait_ns))
-                        break;
-                    mbar_arrive_expect_tx(&w_full[s], SP * kWTile);
-                    bulk_load(wring + (size_t)s * SP * kWTile, wt + (size_t)p * SP * kWTile, SP * kWTile, &w_full[s]);
-                }
+                bool ok = true;
+                for (int kc = 0; kc < KC && ok; kc++)
+                    for (int mt = 0; mt < MT; mt++, u++) {
+                        const int s = (int)(u % stages);
+                        if (u >= (uint32_t)stages &&
+                            !mbar_wait(&w_empty[s], ((u / stages) - 1) & 1u, abort_flag, wait_ns)) {
+                            ok = false;
+                            break;
+                        }
+                        mbar_arrive_expect_tx(&w_full[s], SP * kWTile);
+                        bulk_load(wring + (size_t)s * SP * kWTile, wt + (size_t)(mt * KC + kc) * SP * kWTile,
+                                  SP * kWTile, &w_full[s]);
+                    }
+                if (!ok) break;
             }
             // every copy issued has landed before the CTA leaves
             const uint32_t last = u;
@@ -127,24 +141,28 @@ dense_kernel(const float *__restrict__ x, int64_t N, int M, int K, const uint8_t
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
             const uint32_t idesc = idesc_bf16_f32(128, TR);
-            uint32_t u = 0;
-            for (int64_t i = 0; i < n_local && !*abort_flag; i++) {
+            uint32_t u = 0, c = 0;
+            bool ok = true;
+            for (int64_t i = 0; i < n_local && ok && !*abort_flag; i++) {
                 const int buf = (int)(i & 1);
-                if (!mbar_wait(&x_ready, (uint32_t)(i & 1), abort_flag, wait_ns)) break;
                 if (i >= 2 && !mbar_wait(&t_empty[buf], (uint32_t)(((i >> 1) - 1) & 1), abort_flag, wait_ns)) break;
-                tc_fence_after();
-                bool ok = true;
-                for (int mt = 0; mt < MT && ok; mt++) {
-                    const uint32_t d = tmem + (uint32_t)(buf * MT * TR + mt * TR);
-                    for (int kc = 0; kc < KC; kc++, u++) {
+                for (int kc = 0; kc < KC && ok; kc++, c++) {
+                    const int xs = (int)(c % xslots);
+                    if (!mbar_wait(&x_full[xs], (c / xslots) & 1u, abort_flag, wait_ns)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t bh = smem_u32(xring + (size_t)xs * SP * kXChunk);
+                    for (int mt = 0; mt < MT; mt++, u++) {
                         const int s = (int)(u % stages);
                         if (!mbar_wait(&w_full[s], (u / stages) & 1u, abort_flag, wait_ns)) {
                             ok = false;
                             break;
                         }
                         tc_fence_after();
+                        const uint32_t d = tmem + (uint32_t)(buf * MT * TR + mt * TR);
                         const uint32_t ah = smem_u32(wring + (size_t)s * SP * kWTile);
-                        const uint32_t bh = smem_u32(xs + (size_t)kc * SP * kXChunk);
 #pragma unroll
                         for (int ks = 0; ks < 4; ks++) {
                             const uint32_t ko = ks * 32;
@@ -156,25 +174,80 @@ dense_kernel(const float *__restrict__ x, int64_t N, int M, int K, const uint8_t
                         }
                         umma_commit(&w_empty[s]);
                     }
+                    if (ok) umma_commit(&x_empty[xs]);        // the chunk slot may be rewritten
                 }
-                if (!ok) break;
-                umma_commit(&t_full[buf]);                    // also: the X operand may be rewritten
+                if (ok) umma_commit(&t_full[buf]);
             }
             umma_commit(&drain_bar);
             mbar_wait_drain(&drain_bar, 0);
         }
-    } else {
-        // ---------------- convert X / epilogue (warps 2..5) ----------------
-        const int ct = threadIdx.x - 64;                      // 0..127
-        const int q4 = warp & 3;                              // TMEM lane quadrant
-        const int rows_f4 = K >> 2;                           // float4s per X row
-        bool ok = true;
-        auto epilogue = [&](int64_t i) {
-            const int buf = (int)(i & 1);
-            if (!mbar_wait(&t_full[buf], (uint32_t)((i >> 1) & 1), abort_flag, wait_ns)) {
-                ok = false;
-                return;
+    } else if (warp < 2 + kConvWarps) {
+        // ---------------- converters: 16 rows of every chunk per warp ----------------
+        const int cw = warp - 2;
+        const int64_t n_chunks = n_local * KC;
+        // float4 f = lane + 32 u of this warp's 16 x 64 block: row cw * 16 + f / 16, column 4 (f % 16)
+        auto load = [&](int64_t c, float4 (&v)[8]) {
+            const int64_t i = c / KC;
+            const int kc = (int)(c - i * KC);
+            const int64_t r0 = (blockIdx.x + i * gridDim.x) * TR + cw * 16;
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+                const int f = lane + 32 * u;
+                const int64_t r = r0 + (f >> 4);
+                v[u] = r < N ? __ldg(reinterpret_cast<const float4 *>(x + r * (int64_t)K + kc * 64) + (f & 15))
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
             }
+        };
+        auto store = [&](int64_t c, const float4 (&v)[8]) -> bool {
+            const int xs = (int)(c % xslots);
+            if (c >= xslots && !mbar_wait(&x_empty[xs], (uint32_t)(((c / xslots) - 1) & 1), abort_flag, wait_ns))
+                return false;
+            uint8_t *hi = xring + (size_t)xs * SP * kXChunk;
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+                const int f = lane + 32 * u;
+                const int row = cw * 16 + (f >> 4), col = (f & 15) * 4;
+                const uint32_t o = swz(row, col);         // 4 bf16 in one 16-byte chunk: one 8-byte store
+                const __nv_bfloat162 h01 = __floats2bfloat162_rn(v[u].x, v[u].y);
+                const __nv_bfloat162 h23 = __floats2bfloat162_rn(v[u].z, v[u].w);
+                uint2 hv;
+                hv.x = *reinterpret_cast<const uint32_t *>(&h01);
+                hv.y = *reinterpret_cast<const uint32_t *>(&h23);
+                *reinterpret_cast<uint2 *>(hi + o) = hv;
+                if (kSplit) {
+                    const float2 f01 = __bfloat1622float2(h01), f23 = __bfloat1622float2(h23);
+                    const __nv_bfloat162 l01 = __floats2bfloat162_rn(v[u].x - f01.x, v[u].y - f01.y);
+                    const __nv_bfloat162 l23 = __floats2bfloat162_rn(v[u].z - f23.x, v[u].w - f23.y);
+                    uint2 lv;
+                    lv.x = *reinterpret_cast<const uint32_t *>(&l01);
+                    lv.y = *reinterpret_cast<const uint32_t *>(&l23);
+                    *reinterpret_cast<uint2 *>(hi + kXChunk + o) = lv;
+                }
+            }
+            fence_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&x_full[xs]);
+            return true;
+        };
+        // three register buffers: while chunk c is converted, chunks c + 1 and c + 2 are in
+        // flight (48 KB of X per SM with the four converter warps)
+        float4 va[8], vb[8], vc[8];
+        if (n_chunks > 0) load(0, va);
+        if (n_chunks > 1) load(1, vb);
+        for (int64_t c = 0; c < n_chunks; c += 3) {
+            if (c + 2 < n_chunks) load(c + 2, vc);
+            if (!store(c, va) || c + 1 >= n_chunks) break;
+            if (c + 3 < n_chunks) load(c + 3, va);
+            if (!store(c + 1, vb) || c + 2 >= n_chunks) break;
+            if (c + 4 < n_chunks) load(c + 4, vb);
+            if (!store(c + 2, vc)) break;
+        }
+    } else {
+        // ---------------- epilogue ----------------
+        const int q4 = warp & 3;                              // TMEM lane quadrant
+        for (int64_t i = 0; i < n_local; i++) {
+            const int buf = (int)(i & 1);
+            if (!mbar_wait(&t_full[buf], (uint32_t)((i >> 1) & 1), abort_flag, wait_ns)) break;
             tc_fence_after();
             const int64_t r0 = (blockIdx.x + i * gridDim.x) * TR;
             for (int mt = 0; mt < MT; mt++) {
@@ -201,58 +274,7 @@ dense_kernel(const float *__restrict__ x, int64_t N, int M, int K, const uint8_t
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&t_empty[buf]);
-        };
-        for (int64_t i = 0; i < n_local; i++) {
-            // the previous tile's MMAs have read the operand before it is rewritten.  The four
-            // converter warps meet at named barrier 1, so they leave the loop together: a failed
-            // wait in any of them is posted in conv_stop_s before the barrier and read after it.
-            if (i >= 1 && !mbar_wait(&t_full[(i - 1) & 1], (uint32_t)(((i - 1) >> 1) & 1), abort_flag, wait_ns))
-                conv_stop_s = 1;
-            named_bar(1, 128);
-            if (*reinterpret_cast<volatile int *>(&conv_stop_s)) {
-                ok = false;
-                break;
-            }
-            const int64_t r0 = (blockIdx.x + i * gridDim.x) * TR;
-            // the tile's rows in batches of kBatch 16-byte loads per thread, all in flight before
-            // any is converted (one memory latency per batch, not per load)
-            constexpr int kBatch = 16;
-            const int total4 = TR * rows_f4;
-            for (int base = ct; base < total4; base += 128 * kBatch) {
-                float4 v[kBatch];
-#pragma unroll
-                for (int u = 0; u < kBatch; u++) {
-                    const int idx = base + 128 * u;
-                    const int r = idx / rows_f4, c4 = idx - r * rows_f4;
-                    v[u] = (idx < total4 && r0 + r < N)
-                               ? __ldg(reinterpret_cast<const float4 *>(x + (r0 + r) * (int64_t)K) + c4)
-                               : make_float4(0.f, 0.f, 0.f, 0.f);
-                }
-#pragma unroll
-                for (int u = 0; u < kBatch; u++) {
-                    const int idx = base + 128 * u;
-                    if (idx >= total4) break;
-                    const int r = idx / rows_f4, c4 = idx - r * rows_f4;
-                    const float vv[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
-#pragma unroll
-                    for (int e = 0; e < 4; e++) {
-                        const int k = c4 * 4 + e;
-                        uint8_t *chunk = xs + (size_t)((k >> 6) * SP) * kXChunk;
-                        const uint32_t o = swz(r, k & 63);
-                        const __nv_bfloat16 hi = __float2bfloat16_rn(vv[e]);
-                        *reinterpret_cast<__nv_bfloat16 *>(chunk + o) = hi;
-                        if (kSplit)
-                            *reinterpret_cast<__nv_bfloat16 *>(chunk + kXChunk + o) =
-                                __float2bfloat16_rn(vv[e] - __bfloat162float(hi));
-                    }
-                }
-            }
-            fence_async_smem();
-            named_bar(1, 128);
-            if (ct == 0) mbar_arrive(&x_ready);
-            if (i >= 1) epilogue(i - 1);     // its accumulators were waited for above: no time-out here
         }
-        if (ok && n_local > 0) epilogue(n_local - 1);
     }
     __syncthreads();
     if (warp == 0) {
@@ -271,9 +293,12 @@ int run(const float *x, int64_t N, int M, int K, const float *w, const float *b,
     uint8_t *wt = static_cast<uint8_t *>(ws);
     dense_wtiles_kernel<kSplit><<<(M * K + 255) / 256, 256, 0, s>>>(w, M, K, wt);
     FEQ_LAUNCH_CHECK();
-    const size_t xbytes = (size_t)(K / 64) * (kSplit ? 2 : 1) * kXChunk, wpair = (size_t)(kSplit ? 2 : 1) * kWTile;
-    const int stages = 1024 + xbytes + kMaxStages * wpair <= 225 * 1024 ? kMaxStages : 2;
-    const size_t smem = 1024 + (size_t)stages * wpair + xbytes;
+    // shared memory: W ring (tile pairs) + X chunk ring, bf16x3 5 + 3 (208 KB), bf16 10 + 6
+    // (208 KB).  At a million rows the split does not matter (4 + 6, 6 + 2, 2 + 6 all within
+    // 1 %); at a few thousand rows, one tile per CTA, the deeper W ring shortens the chain.
+    const size_t xchunk = (size_t)(kSplit ? 2 : 1) * kXChunk, wpair = (size_t)(kSplit ? 2 : 1) * kWTile;
+    const int stages = kSplit ? 5 : 10, xslots = kSplit ? 3 : 6;
+    const size_t smem = 1024 + (size_t)stages * wpair + (size_t)xslots * xchunk;
     auto kern = dense_kernel<kSplit>;
     FEQ_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     int dev = 0, sms = 148;
@@ -281,7 +306,7 @@ int run(const float *x, int64_t N, int M, int K, const float *w, const float *b,
     FEQ_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     const int64_t ntiles = (N + TR - 1) / TR;
     const int64_t grid = ntiles < sms ? ntiles : sms;
-    kern<<<(unsigned)grid, kThreads, smem, s>>>(x, N, M, K, wt, b, y, ntiles, stages, status, wait_limit_ns());
+    kern<<<(unsigned)grid, kThreads, smem, s>>>(x, N, M, K, wt, b, y, ntiles, stages, xslots, status, wait_limit_ns());
     FEQ_LAUNCH_CHECK();
     return FEQ_OK;
 }
