@@ -224,63 +224,155 @@ nodelin_kernel(const float *__restrict__ x, int64_t N, const uint8_t *__restrict
         // ---------------- converters: node rows -> operand ----------------
         const int cw = warp - R::CONV0;
         const int nb = cw * R::NPC;                            // first node of this warp in a tile
-        auto load = [&](int64_t i, float4 (&v)[R::VPL]) {
-            const int64_t n0 = (blockIdx.x + i * gridDim.x) * (int64_t)TN + nb;
-            const int64_t lim = (N - n0) * (int64_t)R::ROWF;   // valid floats from n0 on
-            const float4 *src = reinterpret_cast<const float4 *>(x + n0 * R::ROWF);
+        if constexpr (CIN >= 128) {
+            // 128 input channels: lane l takes channels 4 l .. 4 l + 3 of each of the warp's
+            // nodes, whose 4 D floats are contiguous in the node row (16-byte loads); the lane
+            // then holds every position of two channel pairs, so each (pair, position) is one
+            // packed bf16x2 store per operand half with compile-time row arithmetic, instead of
+            // a per-element decode and 2-byte stores (1 M nodes 128 -> 64: 2.53 -> 2.03 ms).
+            constexpr int CPL = CIN / 32;                          // channels per lane
+            constexpr int FPN = CPL * D;                           // floats per lane per node
+            constexpr int VF = R::NPC * FPN;                       // floats per lane per tile
+            static_assert(VF == 4 * R::VPL, "the same floats per lane as the float4 view");
+            auto load = [&](int64_t i, float (&v)[VF]) {
+                const int64_t n0 = (blockIdx.x + i * gridDim.x) * (int64_t)TN + nb;
 #pragma unroll
-            for (int k = 0; k < R::VPL; k++) {
-                const int j = lane + 32 * k;
-                v[k] = (i < n_local && 4 * j < lim) ? __ldg(src + j) : make_float4(0.f, 0.f, 0.f, 0.f);
-            }
-        };
-        auto convert = [&](int64_t i, const float4 (&v)[R::VPL]) -> bool {
-            const int sb = (int)(i % BST);
-            if (i >= BST && !mbar_wait(&b_empty[sb], (uint32_t)((i / BST - 1) & 1), abort_flag, wait_ns)) return false;
-            uint8_t *bst = bsm + (size_t)sb * BSTAGE;
+                for (int nl = 0; nl < R::NPC; nl++) {
+                    const bool in = i < n_local && n0 + nl < N;
+                    const float *src = x + (n0 + nl) * R::ROWF + lane * FPN;
+                    if constexpr (FPN % 4 == 0) {
 #pragma unroll
-            for (int k = 0; k < R::VPL; k++) {
-                const float vv[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
+                        for (int u = 0; u < FPN / 4; u++) {
+                            const float4 t = in ? __ldg(reinterpret_cast<const float4 *>(src) + u) : make_float4(0.f, 0.f, 0.f, 0.f);
+                            v[nl * FPN + 4 * u] = t.x;
+                            v[nl * FPN + 4 * u + 1] = t.y;
+                            v[nl * FPN + 4 * u + 2] = t.z;
+                            v[nl * FPN + 4 * u + 3] = t.w;
+                        }
+                    } else {
 #pragma unroll
-                for (int q = 0; q < 4; q++) {
-                    const int e = 4 * (lane + 32 * k) + q;
-                    const int nl = e / R::ROWF, rem = e - nl * R::ROWF;
-                    const int c = rem / D, p = rem - c * D;
-                    const float val = vv[q];
-                    const int r = p >= 9 ? 3 : p >= 4 ? 2 : p >= 1 ? 1 : 0;
-                    const int row = G::roff(r) + (nb + nl) * (2 * r + 1) + (p - r * r);
-                    uint8_t *chunk = bst + (size_t)((c >> 6) * SP) * G::BCHUNK;
-                    const uint32_t o = swz(row, c & 63);
-                    const __nv_bfloat16 hi = __float2bfloat16_rn(val);
-                    *reinterpret_cast<__nv_bfloat16 *>(chunk + o) = hi;
-                    if (kSplit)
-                        *reinterpret_cast<__nv_bfloat16 *>(chunk + G::BCHUNK + o) =
-                            __float2bfloat16_rn(val - __bfloat162float(hi));
+                        for (int u = 0; u < FPN / 2; u++) {
+                            const float2 t = in ? __ldg(reinterpret_cast<const float2 *>(src) + u) : make_float2(0.f, 0.f);
+                            v[nl * FPN + 2 * u] = t.x;
+                            v[nl * FPN + 2 * u + 1] = t.y;
+                        }
+                    }
+                }
+            };
+            auto convert = [&](int64_t i, const float (&v)[VF]) -> bool {
+                const int sb = (int)(i % BST);
+                if (i >= BST && !mbar_wait(&b_empty[sb], (uint32_t)((i / BST - 1) & 1), abort_flag, wait_ns)) return false;
+                uint8_t *bst = bsm + (size_t)sb * BSTAGE;
+#pragma unroll
+                for (int nl = 0; nl < R::NPC; nl++) {
+#pragma unroll
+                    for (int p = 0; p < D; p++) {
+                        const int r = p >= 9 ? 3 : p >= 4 ? 2 : p >= 1 ? 1 : 0;
+                        const int row = G::roff(r) + (nb + nl) * (2 * r + 1) + (p - r * r);
+#pragma unroll
+                        for (int j = 0; j < CPL / 2; j++) {
+                            const int c = lane * CPL + 2 * j;
+                            const float y0 = v[nl * FPN + (2 * j) * D + p], y1 = v[nl * FPN + (2 * j + 1) * D + p];
+                            uint8_t *chunk = bst + (size_t)((c >> 6) * SP) * G::BCHUNK;
+                            const uint32_t o = swz(row, c & 63);
+                            const __nv_bfloat162 hi = __floats2bfloat162_rn(y0, y1);
+                            *reinterpret_cast<__nv_bfloat162 *>(chunk + o) = hi;
+                            if (kSplit) {
+                                const float2 hf = __bfloat1622float2(hi);
+                                *reinterpret_cast<__nv_bfloat162 *>(chunk + G::BCHUNK + o) =
+                                    __floats2bfloat162_rn(y0 - hf.x, y1 - hf.y);
+                            }
+                        }
+                    }
+                }
+                fence_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&b_full[sb]);
+                return true;
+            };
+            if constexpr (R::XDB) {
+                float va[VF], vb[VF];
+                load(0, va);
+                for (int64_t i = 0; i < n_local; i += 2) {
+                    load(i + 1, vb);                           // in flight while tile i is converted
+                    if (!convert(i, va)) break;
+                    if (i + 1 >= n_local) break;
+                    load(i + 2, va);
+                    if (!convert(i + 1, vb)) break;
+                }
+            } else {
+                // the next tile's rows are loaded right after this tile's operand is handed over, so
+                // they are in flight while the MMAs run
+                float va[VF];
+                load(0, va);
+                for (int64_t i = 0; i < n_local; i++) {
+                    if (!convert(i, va)) break;
+                    load(i + 1, va);
                 }
             }
-            fence_async_smem();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&b_full[sb]);
-            return true;
-        };
-        if constexpr (R::XDB) {
-            float4 va[R::VPL], vb[R::VPL];
-            load(0, va);
-            for (int64_t i = 0; i < n_local; i += 2) {
-                load(i + 1, vb);                           // in flight while tile i is converted
-                if (!convert(i, va)) break;
-                if (i + 1 >= n_local) break;
-                load(i + 2, va);
-                if (!convert(i + 1, vb)) break;
-            }
         } else {
-            // the next tile's rows are loaded right after this tile's operand is handed over, so
-            // they are in flight while the MMAs run
-            float4 va[R::VPL];
-            load(0, va);
-            for (int64_t i = 0; i < n_local; i++) {
-                if (!convert(i, va)) break;
-                load(i + 1, va);
+            // 64 input channels: float4 loads along the node row (coalesced); each element is
+            // placed on its own (the lane's four floats are consecutive positions).  The
+            // channel-pair mapping above measured slower here (8-byte loads at a 72-byte lane
+            // stride): 1 M nodes 64 -> 128 1.46 -> 1.59 ms.
+            auto load = [&](int64_t i, float4 (&v)[R::VPL]) {
+                const int64_t n0 = (blockIdx.x + i * gridDim.x) * (int64_t)TN + nb;
+                const int64_t lim = (N - n0) * (int64_t)R::ROWF;   // valid floats from n0 on
+                const float4 *src = reinterpret_cast<const float4 *>(x + n0 * R::ROWF);
+#pragma unroll
+                for (int k = 0; k < R::VPL; k++) {
+                    const int j = lane + 32 * k;
+                    v[k] = (i < n_local && 4 * j < lim) ? __ldg(src + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+            };
+            auto convert = [&](int64_t i, const float4 (&v)[R::VPL]) -> bool {
+                const int sb = (int)(i % BST);
+                if (i >= BST && !mbar_wait(&b_empty[sb], (uint32_t)((i / BST - 1) & 1), abort_flag, wait_ns)) return false;
+                uint8_t *bst = bsm + (size_t)sb * BSTAGE;
+#pragma unroll
+                for (int k = 0; k < R::VPL; k++) {
+                    const float vv[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
+#pragma unroll
+                    for (int q = 0; q < 4; q++) {
+                        const int e = 4 * (lane + 32 * k) + q;
+                        const int nl = e / R::ROWF, rem = e - nl * R::ROWF;
+                        const int c = rem / D, p = rem - c * D;
+                        const float val = vv[q];
+                        const int r = p >= 9 ? 3 : p >= 4 ? 2 : p >= 1 ? 1 : 0;
+                        const int row = G::roff(r) + (nb + nl) * (2 * r + 1) + (p - r * r);
+                        uint8_t *chunk = bst + (size_t)((c >> 6) * SP) * G::BCHUNK;
+                        const uint32_t o = swz(row, c & 63);
+                        const __nv_bfloat16 hi = __float2bfloat16_rn(val);
+                        *reinterpret_cast<__nv_bfloat16 *>(chunk + o) = hi;
+                        if (kSplit)
+                            *reinterpret_cast<__nv_bfloat16 *>(chunk + G::BCHUNK + o) =
+                                __float2bfloat16_rn(val - __bfloat162float(hi));
+                    }
+                }
+                fence_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&b_full[sb]);
+                return true;
+            };
+            if constexpr (R::XDB) {
+                float4 va[R::VPL], vb[R::VPL];
+                load(0, va);
+                for (int64_t i = 0; i < n_local; i += 2) {
+                    load(i + 1, vb);                           // in flight while tile i is converted
+                    if (!convert(i, va)) break;
+                    if (i + 1 >= n_local) break;
+                    load(i + 2, va);
+                    if (!convert(i + 1, vb)) break;
+                }
+            } else {
+                // the next tile's rows are loaded right after this tile's operand is handed over, so
+                // they are in flight while the MMAs run
+                float4 va[R::VPL];
+                load(0, va);
+                for (int64_t i = 0; i < n_local; i++) {
+                    if (!convert(i, va)) break;
+                    load(i + 1, va);
+                }
             }
         }
     } else {
