@@ -1,10 +1,10 @@
 #!/usr/bin/env python
 """Benchmark: forward edges/s of WignerDBasis + EquivariantEdgewiseLinear
-on B200, with roofline, clocks, end-to-end and CPU baseline.
+(benchmark config 2) on B200, with roofline, clocks, end-to-end and CPU baseline.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Workload: in/out Repr(lvals=[0..4], mult=64), N = 20000
+Workload (the headline benchmark configuration): in/out Repr(lvals=[0..4], mult=64), N = 20000
 nodes uniform in a 60 A cube, 32-nearest-neighbour graph (src over the neighbours
 of dst), E = 640000, node features (N, 64, 25) ~ N(0, 1) gathered to edges by
 src, directions = dst - src, num_bins = 100 over [0, 10], float32, seed 1.
@@ -705,14 +705,14 @@ def run_train(args):
 
 
 # ---------------------------------------------------------------------------
-# EquivariantTransformerBlock forward on batched small graphs
+# benchmark config 3: EquivariantTransformerBlock forward on batched small graphs
 # ---------------------------------------------------------------------------
 BLOCK_GRAPHS, BLOCK_NODES, BLOCK_RADIUS, BLOCK_HEADS, BLOCK_SEED = 256, 30, 5.0, 8, 2
 
 
 def make_block_workload(seed, device):
     """256 molecule-like graphs of 30 nodes, coordinates N(0, 1.5^2) per axis, all directed
-    pairs within 5 A (no self loops), features (N, 64, 9) ~ N(0, 1): BASELINE config 3."""
+    pairs within 5 A (no self loops), features (N, 64, 9) ~ N(0, 1): benchmark config 3."""
     g = torch.Generator().manual_seed(seed)
     coords = torch.randn(BLOCK_GRAPHS, BLOCK_NODES, 3, generator=g) * 1.5
     x = torch.randn(BLOCK_GRAPHS * BLOCK_NODES, 64, 9, generator=g)
@@ -998,7 +998,7 @@ def block_config(n_gpus, E_total):
 
 
 # ---------------------------------------------------------------------------
-# the full 6-layer EquivariantTransformer on 4096 graphs of 50 nodes
+# benchmark config 4: the full 6-layer EquivariantTransformer on 4096 graphs of 50 nodes
 # ---------------------------------------------------------------------------
 MODEL_GRAPHS, MODEL_NODES, MODEL_K, MODEL_HEADS, MODEL_LAYERS, MODEL_SEED = 4096, 50, 16, 8, 6, 3
 # Out Repr([0], 8) stands in for the configured Repr([0], 1): the reference itself rejects 8
@@ -1009,7 +1009,7 @@ METRIC_MODEL = "edges/sec (6-layer EquivariantTransformer fwd)"
 
 def make_model_workload(seed, device, n_graphs=MODEL_GRAPHS):
     """4096 graphs of 50 nodes, coordinates N(0, 2^2) per axis, 16-NN within each graph
-    (src over the neighbours of dst), node features (N, 32, 4) ~ N(0, 1): BASELINE config 4."""
+    (src over the neighbours of dst), node features (N, 32, 4) ~ N(0, 1): benchmark config 4."""
     g = torch.Generator().manual_seed(seed)
     coords = torch.randn(n_graphs, MODEL_NODES, 3, generator=g) * 2.0
     x = torch.randn(n_graphs * MODEL_NODES, 32, 4, generator=g)
@@ -1502,10 +1502,10 @@ def main():
                     help="edge chunks per end-to-end step (output copy of one overlaps compute of the next)")
     ap.add_argument("--workload", choices=["config2", "block", "model", "train", "giant", "patch"],
                     default="config2",
-                    help="config2: the metric (default); block: BASELINE config 3 (transformer block "
-                         "forward); model: BASELINE config 4 (6-layer transformer forward on 4096 graphs); "
+                    help="config2: the metric (default); block: benchmark config 3 (transformer block "
+                         "forward); model: benchmark config 4 (6-layer transformer forward on 4096 graphs); "
                          "train: the reference's published single-layer fwd+bwd+Adam step "
-                         "(--lmax, --edges); giant: BASELINE config 5 (1 M-node graph, dst-range "
+                         "(--lmax, --edges); giant: benchmark config 5 (1 M-node graph, dst-range "
                          "partitioned across the ranks, strong scaling)")
     ap.add_argument("--edges", type=int, default=None)
     ap.add_argument("--lmax", type=int, default=4,

@@ -91,7 +91,7 @@ def knn_within(coords: torch.Tensor, batch: torch.Tensor, k: int):
 
 
 def make_model_config4(fe) -> dict:
-    """BASELINE config 4 at reduced size: EquivariantTransformer in Repr([0,1],32), hidden
+    """benchmark config 4 at reduced size: EquivariantTransformer in Repr([0,1],32), hidden
     Repr([0,1,2,3],128), 8 heads, 16-NN within each graph, coordinates N(0, 2^2), seed 3.
     Out Repr([0], 8) instead of Repr([0], 1): the reference rejects 8 heads on out mult 1
     (attention.py:233-236).  3 layers (in -> hidden, hidden -> hidden, hidden -> out) on
@@ -310,7 +310,7 @@ def main() -> int:
 
     torch.manual_seed(3)
     # out mult 4, not 1: the reference rejects num_heads that do not divide out_repr.mult
-    # (attention.py:233-234), which also rules out BASELINE config 4 as written.
+    # (attention.py:233-234), which also rules out benchmark config 4 as written.
     rin, rh, rout = fe.Repr([0, 1], mult=8), fe.Repr([0, 1, 2], mult=16), fe.Repr([0], mult=4)
     model = fe.EquivariantTransformer(rin, rh, rout, num_layers=3, num_heads=4, max_dist=10.0)
     model.eval()
