@@ -159,7 +159,7 @@ def test_radial_table_cpu_matches_reference():
 
 def test_reference_errors_preserved():
     with pytest.raises(ValueError):
-        fe.EquivariantAttention(fe.Repr([0, 1], 8), fe.Repr([0], 1), num_heads=8)   # BASELINE config 4 as written
+        fe.EquivariantAttention(fe.Repr([0, 1], 8), fe.Repr([0], 1), num_heads=8)   # benchmark config 4 as written
     with pytest.raises(ValueError):
         fe.Graph(src=torch.zeros(3, dtype=torch.long), dst=torch.zeros(2, dtype=torch.long), num_nodes=3)
     with pytest.raises(ValueError):

@@ -1,4 +1,4 @@
-"""Parity on the benched workload itself, not a small stand-in.
+"""Parity on the benched workload itself (benchmark config 2), not a small stand-in.
 
 The exact graph and inputs that ``bench.py`` times: N = 20 000 nodes uniform in a 60 A
 cube, 32-NN (E = 640 000), Repr([0..4], 64) in and out, 100 bins over [0, 10], seed 1.

@@ -1,4 +1,4 @@
-"""BASELINE config 4's layer shapes through the whole EquivariantTransformer, against the
+"""benchmark config 4's layer shapes through the whole EquivariantTransformer, against the
 reference model run on the CPU (tests/golden/model_config4.pt, made by make_golden.py).
 
 In Repr([0,1],32), hidden Repr([0,1,2,3],128), 8 heads, 16-NN within each graph; 3 layers
