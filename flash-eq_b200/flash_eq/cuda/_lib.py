@@ -135,6 +135,9 @@ SIGNATURES = {
     "feq_dense_linear_tc_workspace_bytes": (ctypes.c_size_t, [ctypes.c_int32, ctypes.c_int32, ctypes.c_int32]),
     "feq_dense_linear_tc": (ctypes.c_int, [c_vp, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, c_vp, c_vp,
                                            ctypes.c_int32, c_vp, c_vp, ctypes.c_size_t, c_vp, c_vp]),
+    "feq_radial_features": (ctypes.c_int, [c_vp, ctypes.c_int32, ctypes.c_float, ctypes.c_float, c_vp, ctypes.c_int32,
+                                           c_vp, c_vp, ctypes.c_int32, c_vp, c_vp, c_vp, c_vp, ctypes.c_int32, c_vp,
+                                           c_vp]),
     "feq_node_linear_tc_workspace_bytes": (ctypes.c_size_t, [ctypes.c_int32, ctypes.c_int32, c_i32p, ctypes.c_int32,
                                                               ctypes.c_int32]),
     "feq_node_linear_tc": (ctypes.c_int, [c_vp, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, c_i32p, ctypes.c_int32,

@@ -752,6 +752,27 @@ def node_linear(x, lvals, weight, bias, c_out, scalar_index):
     return y.view(*x.shape[:-2], cout, d)
 
 
+RADIAL_MAX_FREQS, RADIAL_MAX_HIDDEN = 64, 256     # limits of feq_radial_features
+
+
+def radial_features(bin_edges, min_val, max_val, frequencies, w1, b1, w2, b2, w3, b3):
+    """SeparableRadialNet's features at the bin edges in one launch (feq_radial_features):
+    sinusoid x envelope basis, two SiLU layers and the head, weights as nn.Linear holds them.
+    Returns (num_edges, out_dim) float32."""
+    lib = _require_cuda(bin_edges, frequencies, w1, b1, w2, b2, w3, b3)
+    edges = _f32(bin_edges, "bin_edges")
+    tensors = [_f32(t, n) for t, n in ((frequencies, "frequencies"), (w1, "w1"), (b1, "b1"), (w2, "w2"),
+                                       (b2, "b2"), (w3, "w3"), (b3, "b3"))]
+    freqs, w1, b1, w2, b2, w3, b3 = tensors
+    hidden, out_dim = w1.shape[0], w3.shape[0]
+    out = torch.empty(edges.numel(), out_dim, dtype=torch.float32, device=edges.device)
+    rc = lib.feq_radial_features(_p(edges), edges.numel(), float(min_val), float(max_val), _p(freqs), freqs.numel(),
+                                 _p(w1), _p(b1), hidden, _p(w2), _p(b2), _p(w3), _p(b3), out_dim, _p(out),
+                                 _stream(edges.device))
+    _lib.check(rc, "feq_radial_features")
+    return out
+
+
 def dense_linear_tc_supported(m, k, mix=NODE_LINEAR_MIX) -> bool:
     """Whether feq_dense_linear_tc serves y = x w^T + b with w (m, k)."""
     return _lib.load().feq_dense_linear_tc_workspace_bytes(int(m), int(k), _lib.FEQ_MIX[mix]) > 0

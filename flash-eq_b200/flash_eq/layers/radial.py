@@ -90,9 +90,26 @@ class SeparableRadialNet(nn.Module):
 
     def radial_features(self) -> torch.Tensor:
         """f_k(r_b, w) at the bin edges, (num_bins + 1, rank, weight_dim): the factor of the
-        table that depends on distance (radial.py:259-267)."""
-        f = self.head(self.trunk(self._sinusoidal_basis(self.bin_edges)))
+        table that depends on distance (radial.py:259-267).  On the GPU without autograd one
+        native launch (feq_radial_features) computes it; under autograd the PyTorch modules
+        below do, so gradients reach the radial net."""
+        if self._native_features_ok():
+            from ..cuda import ops
+            l1, l2 = self.trunk[0], self.trunk[2]
+            f = ops.radial_features(self.bin_edges, self.min_val, self.max_val, self.frequencies, l1.weight,
+                                    l1.bias, l2.weight, l2.bias, self.head.weight, self.head.bias)
+        else:
+            f = self.head(self.trunk(self._sinusoidal_basis(self.bin_edges)))
         return f.view(-1, self.rank, self.weight_dim)
+
+    def _native_features_ok(self) -> bool:
+        if torch.is_grad_enabled() or not self.bin_edges.is_cuda:
+            return False
+        from ..cuda import ops
+        l1, l2 = self.trunk[0], self.trunk[2]
+        return (self.bin_edges.dtype == torch.float32 and l1.weight.dtype == torch.float32
+                and self.frequencies.numel() <= ops.RADIAL_MAX_FREQS and l1.out_features <= ops.RADIAL_MAX_HIDDEN
+                and l2.out_features == l1.out_features)
 
     def forward(self) -> torch.Tensor:
         return torch.einsum("koi,bkw->boiw", self.channel_patterns, self.radial_features())

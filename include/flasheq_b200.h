@@ -482,6 +482,16 @@ size_t feq_dense_linear_tc_workspace_bytes(int32_t m, int32_t k, int32_t mix_mod
 int feq_dense_linear_tc(const float *x, int64_t n, int32_t m, int32_t k, const float *weight, const float *bias,
                         int32_t mix_mode, float *y, void *workspace, size_t workspace_bytes, int32_t *status,
                         feq_stream_t stream);
+/* SeparableRadialNet.radial_features (radial.py:226-267): at every bin edge r_b
+ * (num_edges of them) the sinusoid x envelope basis of x = clamp((r_b - min_val) /
+ * (max_val - min_val), 0, 1) with the given frequencies (num_freqs <= 64), then
+ * SiLU(w1 . + b1), SiLU(w2 . + b2), w3 . + b3, the weights as nn.Linear holds them (w1
+ * (hidden, 2 num_freqs), w2 (hidden, hidden), w3 (out_dim, hidden), hidden <= 256); out
+ * (num_edges, out_dim) float32.  One launch for what PyTorch runs as about twenty. */
+int feq_radial_features(const float *bin_edges, int32_t num_edges, float min_val, float max_val,
+                        const float *frequencies, int32_t num_freqs, const float *w1, const float *b1,
+                        int32_t hidden, const float *w2, const float *b2, const float *w3, const float *b3,
+                        int32_t out_dim, float *out, feq_stream_t stream);
 /* EquivariantGating's gate (gating.py:17-76): out = x * sigmoid(z)[c, irrep of the
  * position], z (N, C * n_lvals) the pre-activation. */
 int feq_node_gate(const float *x, const float *z, int64_t num_nodes, int32_t C, const int32_t *lvals,
