@@ -3,8 +3,10 @@
 ``SeparableRadialNet`` produces the binned table (num_bins + 1, Cout, Cin, W)
 consumed by the edgewise kernel:  W[b, o, i, w] = sum_k C_k[o, i] f_k(r_b, w),
 f from a sinusoid x DimeNet-envelope basis at the bin edges through a small
-SiLU MLP (radial.py:133-296).  It is O(num_bins) node-level work and stays in
-PyTorch; parameter names and shapes match the reference so state dicts load.
+SiLU MLP (radial.py:133-296).  It is O(num_bins) work: on the GPU without autograd the
+features at the bin edges come from one native launch (feq_radial_features), otherwise
+from the PyTorch modules; parameter names and shapes match the reference so state dicts
+load.
 ``RadialBasisFunctions`` / ``RadialMLP`` are kept for API completeness.
 """
 from __future__ import annotations
