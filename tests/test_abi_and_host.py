@@ -145,7 +145,8 @@ def test_reference_state_dicts_load():
 
 
 def test_radial_table_cpu_matches_reference():
-    """SeparableRadialNet is node-level PyTorch; identical to the reference table."""
+    """On the CPU SeparableRadialNet runs its PyTorch modules (the native features are a
+    GPU path): identical to the reference table."""
     rad = golden("radial.pt")
     for name, d in rad.items():
         net = fe.SeparableRadialNet(**d["kwargs"])
